@@ -1,0 +1,365 @@
+// Context, device buffers, the HBM-resident expert pool with its slot table,
+// events and the synthetic pool fill used by the benchmark.
+#include <algorithm>
+#include <chrono>
+#include <thread>
+
+#include "finch_internal.cuh"
+
+int finch_fail(finch_ctx *ctx, int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (ctx) ctx->err = buf;
+    return code;
+}
+
+extern "C" const char *finch_status_str(int s) {
+    switch (s) {
+        case FINCH_OK: return "ok";
+        case FINCH_E_ARG: return "bad argument";
+        case FINCH_E_NOSLOT: return "expert not resident";
+        case FINCH_E_CUDA: return "CUDA error";
+        case FINCH_E_NCCL: return "NCCL error";
+        case FINCH_E_TIMEOUT: return "timeout";
+        case FINCH_E_UNSUPPORTED: return "unsupported";
+        case FINCH_E_NOMEM: return "out of memory";
+    }
+    return "unknown";
+}
+
+extern "C" const char *finch_last_error(const finch_ctx *ctx) { return ctx ? ctx->err.c_str() : ""; }
+extern "C" size_t finch_expert_bytes(const finch_ctx *ctx) { return ctx ? ctx->expert_bytes : 0; }
+extern "C" uint64_t finch_launch_count(const finch_ctx *ctx) { return ctx ? ctx->launches : 0; }
+
+extern "C" int finch_ctx_create(const finch_config *cfg, finch_ctx **out) {
+    if (!cfg || !out) return FINCH_E_ARG;
+    *out = nullptr;
+    const finch_config &c = *cfg;
+    if (c.hidden <= 0 || c.hidden % 128 || c.moe_inter <= 0 || c.moe_inter % 128 || c.group_size != 64 ||
+        c.top_k < 1 || c.top_k > 8 || c.n_experts < 1 || c.n_layers < 1 || c.max_tokens < 1 ||
+        (c.expert_bits != 3) || (c.scale_dtype != FINCH_BF16 && c.scale_dtype != FINCH_FP16) ||
+        (c.act_dtype != FINCH_F32 && c.act_dtype != FINCH_BF16) || (c.shared_inter % 64) || c.hidden > 8192 ||
+        c.moe_inter > 8192)
+        return FINCH_E_ARG;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || c.device < 0 || c.device >= ndev) return FINCH_E_CUDA;
+    finch_ctx *ctx = new finch_ctx();
+    ctx->cfg = c;
+    auto bail = [&](int code) {
+        finch_ctx_destroy(ctx);
+        return code;
+    };
+    if (cudaSetDevice(c.device) != cudaSuccess) return bail(FINCH_E_CUDA);
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, c.device) != cudaSuccess) return bail(FINCH_E_CUDA);
+    ctx->sm_count = prop.multiProcessorCount;
+    if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) return bail(FINCH_E_CUDA);
+    const size_t gw = (size_t)c.moe_inter * c.hidden * 3 / 8, gs = (size_t)c.moe_inter * (c.hidden / 64) * 2;
+    const size_t dw = gw, ds = (size_t)c.hidden * (c.moe_inter / 64) * 2;
+    ctx->lay.gate_w = 0;
+    ctx->lay.gate_s = gw;
+    ctx->lay.gate_b = gw + gs;
+    ctx->lay.up_w = gw + 2 * gs;
+    ctx->lay.up_s = ctx->lay.up_w + gw;
+    ctx->lay.up_b = ctx->lay.up_s + gs;
+    ctx->lay.down_w = ctx->lay.up_b + gs;
+    ctx->lay.down_s = ctx->lay.down_w + dw;
+    ctx->lay.down_b = ctx->lay.down_s + ds;
+    ctx->expert_bytes = ctx->lay.down_b + ds;
+    const size_t pairs = (size_t)c.max_tokens * c.top_k;
+    const int sh_inter = c.shared_inter > 0 ? c.shared_inter : 64;
+    bool ok = cudaMalloc(&ctx->act, pairs * c.moe_inter * sizeof(float)) == cudaSuccess &&
+              cudaMalloc(&ctx->shared_act, (size_t)c.max_tokens * sh_inter * sizeof(float)) == cudaSuccess &&
+              cudaMalloc(&ctx->partial, (pairs + c.max_tokens) * c.hidden * sizeof(float)) == cudaSuccess &&
+              cudaMalloc(&ctx->counters, (c.hidden / 64 + 64) * sizeof(unsigned)) == cudaSuccess &&
+              cudaMalloc(&ctx->dev_status, sizeof(int)) == cudaSuccess;
+    if (!ok) return bail(FINCH_E_NOMEM);
+    cudaMemset(ctx->counters, 0, (c.hidden / 64 + 64) * sizeof(unsigned));
+    cudaMemset(ctx->dev_status, 0, sizeof(int));
+    cudaMemset(ctx->partial, 0, (pairs + c.max_tokens) * c.hidden * sizeof(float));
+    if (cudaDeviceSynchronize() != cudaSuccess) return bail(FINCH_E_CUDA);
+    *out = ctx;
+    return FINCH_OK;
+}
+
+extern "C" void finch_ctx_destroy(finch_ctx *ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->cfg.device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    cudaFree(ctx->act);
+    cudaFree(ctx->shared_act);
+    cudaFree(ctx->partial);
+    cudaFree(ctx->counters);
+    cudaFree(ctx->dev_status);
+    cudaFree(ctx->stage_dev);
+    cudaFree(ctx->pf_ws);
+    if (ctx->stage_host) cudaFreeHost(ctx->stage_host);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+
+extern "C" int finch_buf_alloc(finch_ctx *ctx, size_t bytes, void **dev) {
+    if (!ctx || !dev || bytes == 0) return FINCH_E_ARG;
+    cudaSetDevice(ctx->cfg.device);
+    if (cudaMalloc(dev, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return finch_fail(ctx, FINCH_E_NOMEM, "cudaMalloc(%zu) failed", bytes);
+    }
+    return FINCH_OK;
+}
+
+extern "C" int finch_weights_upload(finch_ctx *ctx, const void *host, size_t bytes, void **dev) {
+    if (!ctx || !host || !dev) return FINCH_E_ARG;
+    int rc = finch_buf_alloc(ctx, bytes, dev);
+    if (rc) return rc;
+    FINCH_CUDA_OK(ctx, cudaMemcpy(*dev, host, bytes, cudaMemcpyHostToDevice));
+    return FINCH_OK;
+}
+
+extern "C" int finch_buf_free(finch_ctx *ctx, void *dev) {
+    if (!ctx) return FINCH_E_ARG;
+    cudaSetDevice(ctx->cfg.device);
+    FINCH_CUDA_OK(ctx, cudaFree(dev));
+    return FINCH_OK;
+}
+
+extern "C" int finch_sync(finch_ctx *ctx) {
+    if (!ctx) return FINCH_E_ARG;
+    cudaSetDevice(ctx->cfg.device);
+    FINCH_CUDA_OK(ctx, cudaDeviceSynchronize());
+    return FINCH_OK;
+}
+
+extern "C" int finch_device_status(finch_ctx *ctx, int *status_out) {
+    if (!ctx || !status_out) return FINCH_E_ARG;
+    FINCH_CUDA_OK(ctx, cudaMemcpy(status_out, ctx->dev_status, sizeof(int), cudaMemcpyDeviceToHost));
+    return FINCH_OK;
+}
+
+// ------------------------------------------------------------------ events
+extern "C" int finch_event_create(finch_ctx *ctx, finch_event **out) {
+    if (!ctx || !out) return FINCH_E_ARG;
+    finch_event *e = new finch_event();
+    e->ctx = ctx;
+    if (cudaEventCreateWithFlags(&e->ev, cudaEventDisableTiming) != cudaSuccess) {
+        delete e;
+        return finch_fail(ctx, FINCH_E_CUDA, "cudaEventCreate failed");
+    }
+    *out = e;
+    return FINCH_OK;
+}
+extern "C" int finch_event_record(finch_event *ev, finch_stream stream) {
+    if (!ev) return FINCH_E_ARG;
+    FINCH_CUDA_OK(ev->ctx, cudaEventRecord(ev->ev, finch_pick_stream(ev->ctx, stream)));
+    return FINCH_OK;
+}
+extern "C" int finch_event_wait(finch_event *ev, int timeout_ms) {
+    if (!ev) return FINCH_E_ARG;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        cudaError_t q = cudaEventQuery(ev->ev);
+        if (q == cudaSuccess) return FINCH_OK;
+        if (q != cudaErrorNotReady) return finch_fail(ev->ctx, FINCH_E_CUDA, "cudaEventQuery: %s", cudaGetErrorString(q));
+        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+        if (timeout_ms >= 0 && ms >= timeout_ms) return finch_fail(ev->ctx, FINCH_E_TIMEOUT, "event not complete after %d ms", timeout_ms);
+        std::this_thread::yield();
+    }
+}
+extern "C" void finch_event_destroy(finch_event *ev) {
+    if (!ev) return;
+    cudaEventDestroy(ev->ev);
+    delete ev;
+}
+
+// -------------------------------------------------------------------- pool
+extern "C" int finch_pool_create(finch_ctx *ctx, int n_layers, int n_experts, int max_slots, finch_pool **out) {
+    if (!ctx || !out || n_layers < 1 || n_experts < 1 || max_slots < 0) return FINCH_E_ARG;
+    cudaSetDevice(ctx->cfg.device);
+    finch_pool *p = new finch_pool();
+    p->ctx = ctx;
+    p->n_layers = n_layers;
+    p->n_experts = n_experts;
+    const size_t total = (size_t)n_layers * n_experts;
+    p->slots = max_slots == 0 ? (int)total : (int)std::min<size_t>(max_slots, total);
+    p->slot_bytes = (ctx->expert_bytes + 255) / 256 * 256;
+    p->slot_of.assign(total, -1);
+    p->owner.assign(p->slots, -1);
+    p->last_used.assign(p->slots, 0);
+    if (cudaMalloc(&p->base, (size_t)p->slots * p->slot_bytes) != cudaSuccess ||
+        cudaMalloc(&p->slot_table_dev, total * sizeof(int32_t)) != cudaSuccess) {
+        cudaGetLastError();
+        finch_pool_destroy(p);
+        return finch_fail(ctx, FINCH_E_NOMEM, "pool of %d slots x %zu bytes does not fit", p->slots, p->slot_bytes);
+    }
+    cudaMemset(p->slot_table_dev, 0xff, total * sizeof(int32_t));
+    *out = p;
+    return FINCH_OK;
+}
+
+extern "C" void finch_pool_destroy(finch_pool *p) {
+    if (!p) return;
+    cudaSetDevice(p->ctx->cfg.device);
+    cudaDeviceSynchronize();
+    cudaFree(p->base);
+    cudaFree(p->slot_table_dev);
+    delete p;
+}
+
+static int pool_claim_slot(finch_pool *p, int key) {
+    int slot = p->slot_of[key];
+    if (slot >= 0) return slot;
+    if (p->used < p->slots) {
+        while (p->owner[p->cursor] >= 0) p->cursor = (p->cursor + 1) % p->slots;
+        slot = p->cursor;
+        p->used++;
+    } else {  // evict the least recently used entry (linear scan, as the reference does)
+        slot = 0;
+        for (int s = 1; s < p->slots; s++)
+            if (p->last_used[s] < p->last_used[slot]) slot = s;
+        const int old = p->owner[slot];
+        p->slot_of[old] = -1;
+        const int32_t neg = -1;
+        cudaMemcpy(p->slot_table_dev + old, &neg, sizeof neg, cudaMemcpyHostToDevice);
+        p->evictions++;
+    }
+    p->owner[slot] = key;
+    p->slot_of[key] = slot;
+    return slot;
+}
+
+extern "C" int finch_pool_put(finch_pool *p, int layer, int expert, const void *block) {
+    if (!p || !block || layer < 0 || layer >= p->n_layers || expert < 0 || expert >= p->n_experts) return FINCH_E_ARG;
+    finch_ctx *ctx = p->ctx;
+    cudaSetDevice(ctx->cfg.device);
+    const int key = layer * p->n_experts + expert;
+    const int slot = pool_claim_slot(p, key);
+    p->last_used[slot] = ++p->clock;
+    FINCH_CUDA_OK(ctx, cudaMemcpy(p->base + (size_t)slot * p->slot_bytes, block, ctx->expert_bytes, cudaMemcpyHostToDevice));
+    const int32_t s32 = slot;
+    FINCH_CUDA_OK(ctx, cudaMemcpy(p->slot_table_dev + key, &s32, sizeof s32, cudaMemcpyHostToDevice));
+    return FINCH_OK;
+}
+
+extern "C" int finch_pool_lookup(finch_pool *p, int layer, int expert, int *slot_out, void **dev_ptr_out) {
+    if (!p || layer < 0 || layer >= p->n_layers || expert < 0 || expert >= p->n_experts) return FINCH_E_ARG;
+    const int slot = p->slot_of[layer * p->n_experts + expert];
+    if (slot < 0) {
+        p->misses++;
+        return FINCH_E_NOSLOT;
+    }
+    p->hits++;
+    p->last_used[slot] = ++p->clock;
+    if (slot_out) *slot_out = slot;
+    if (dev_ptr_out) *dev_ptr_out = p->base + (size_t)slot * p->slot_bytes;
+    return FINCH_OK;
+}
+
+extern "C" int finch_pool_get(finch_pool *p, int layer, int expert, void *out) {
+    if (!p || !out || layer < 0 || layer >= p->n_layers || expert < 0 || expert >= p->n_experts) return FINCH_E_ARG;
+    const int slot = p->slot_of[layer * p->n_experts + expert];
+    if (slot < 0) return FINCH_E_NOSLOT;
+    cudaSetDevice(p->ctx->cfg.device);
+    FINCH_CUDA_OK(p->ctx, cudaMemcpy(out, p->base + (size_t)slot * p->slot_bytes, p->ctx->expert_bytes, cudaMemcpyDeviceToHost));
+    return FINCH_OK;
+}
+
+extern "C" int finch_pool_get_stats(const finch_pool *p, finch_pool_stats *out) {
+    if (!p || !out) return FINCH_E_ARG;
+    out->hits = p->hits;
+    out->misses = p->misses;
+    out->evictions = p->evictions;
+    out->slots = p->slots;
+    out->used = p->used;
+    out->slot_bytes = p->slot_bytes;
+    return FINCH_OK;
+}
+
+// ---- synthetic fill ------------------------------------------------------
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// One thread per 8 bytes of a block.  Code regions get random bytes; the
+// 16-bit regions get scale = |N(0, 0.01)| (Box-Muller) and bias = -4*scale
+// computed from the stored (rounded) scale.
+__global__ void pool_fill_kernel(uint8_t *base, size_t slot_bytes, size_t expert_bytes, int first_slot, uint64_t seed,
+                                 size_t gate_s, size_t up_w, size_t up_s, size_t down_w, size_t down_s,
+                                 size_t gs_bytes, size_t ds_bytes, int scale_dtype) {
+    const size_t words = expert_bytes / 8;
+    const int slot = first_slot + blockIdx.y;
+    uint8_t *blk = base + (size_t)slot * slot_bytes;
+    for (size_t w = (size_t)blockIdx.x * blockDim.x + threadIdx.x; w < words; w += (size_t)gridDim.x * blockDim.x) {
+        const size_t off = w * 8;
+        // region classification
+        int kind = 0;  // 0 codes, 1 scales, 2 biases
+        size_t sreg = 0, rel = 0, sbytes = 0;
+        if (off >= gate_s && off < up_w) { sreg = gate_s; sbytes = gs_bytes; }
+        else if (off >= up_s && off < down_w) { sreg = up_s; sbytes = gs_bytes; }
+        else if (off >= down_s) { sreg = down_s; sbytes = ds_bytes; }
+        if (sbytes) {
+            rel = off - sreg;
+            kind = rel < sbytes ? 1 : 2;
+            if (kind == 2) rel -= sbytes;
+        }
+        uint64_t out;
+        if (kind == 0) {
+            out = mix64(seed ^ ((uint64_t)slot << 32) ^ (uint64_t)w);
+        } else {
+            // the scale at element index rel/2 + j of its region; biases mirror the scale stream
+            uint16_t h[4];
+            for (int j = 0; j < 4; j++) {
+                const uint64_t r = mix64(seed ^ 0xabcdefull ^ ((uint64_t)slot << 32) ^ (uint64_t)((sreg + rel) / 2 + j));
+                const float u1 = ((r >> 40) + 1) * (1.0f / 16777217.0f), u2 = ((r >> 8) & 0xffffff) * (1.0f / 16777216.0f);
+                const float s = fabsf(0.01f * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2));
+                float sv;
+                uint16_t sb;
+                if (scale_dtype == FINCH_FP16) { sb = __half_as_ushort(__float2half_rn(s)); sv = __half2float(__ushort_as_half(sb)); }
+                else { sb = __bfloat16_as_ushort(__float2bfloat16_rn(s)); sv = __uint_as_float((uint32_t)sb << 16); }
+                if (kind == 1) h[j] = sb;
+                else h[j] = scale_dtype == FINCH_FP16 ? __half_as_ushort(__float2half_rn(-4.0f * sv))
+                                                       : __bfloat16_as_ushort(__float2bfloat16_rn(-4.0f * sv));
+            }
+            out = (uint64_t)h[0] | ((uint64_t)h[1] << 16) | ((uint64_t)h[2] << 32) | ((uint64_t)h[3] << 48);
+        }
+        *reinterpret_cast<uint64_t *>(blk + off) = out;
+    }
+}
+
+extern "C" int finch_pool_fill_synthetic(finch_pool *p, int layer0, int layer1, uint64_t seed) {
+    if (!p || layer0 < 0 || layer1 > p->n_layers || layer0 >= layer1) return FINCH_E_ARG;
+    finch_ctx *ctx = p->ctx;
+    if (p->slots != p->n_layers * p->n_experts) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "synthetic fill needs a fully resident pool");
+    cudaSetDevice(ctx->cfg.device);
+    const auto &L = ctx->lay;
+    const size_t gs = L.gate_b - L.gate_s, ds = L.down_b - L.down_s;
+    for (int l = layer0; l < layer1; l++) {
+        // identity slot assignment: slot = layer * n_experts + expert
+        for (int e = 0; e < p->n_experts; e++) {
+            const int key = l * p->n_experts + e;
+            if (p->slot_of[key] < 0) {
+                p->slot_of[key] = key;
+                p->owner[key] = key;
+                p->last_used[key] = ++p->clock;
+            } else if (p->slot_of[key] != key) {
+                return finch_fail(ctx, FINCH_E_UNSUPPORTED, "pool already holds experts in non-identity slots");
+            }
+        }
+        dim3 grid(64, p->n_experts);
+        pool_fill_kernel<<<grid, 256, 0, ctx->stream>>>(p->base, p->slot_bytes, ctx->expert_bytes, l * p->n_experts,
+                                                        seed + (uint64_t)l * 0x10001ull, L.gate_s, L.up_w, L.up_s, L.down_w,
+                                                        L.down_s, gs, ds, ctx->cfg.scale_dtype);
+        FINCH_CUDA_OK(ctx, cudaGetLastError());
+    }
+    p->used = 0;
+    for (int s = 0; s < p->slots; s++) p->used += p->owner[s] >= 0;
+    FINCH_CUDA_OK(ctx, cudaMemcpyAsync(p->slot_table_dev, p->slot_of.data(), p->slot_of.size() * sizeof(int32_t),
+                                       cudaMemcpyHostToDevice, ctx->stream));
+    FINCH_CUDA_OK(ctx, cudaStreamSynchronize(ctx->stream));
+    return FINCH_OK;
+}

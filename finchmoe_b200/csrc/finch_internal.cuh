@@ -1,0 +1,154 @@
+// Internal declarations shared by the translation units of libfinchcuda.
+// Nothing here is part of the C ABI (see include/finch_cuda.h).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "finch_cuda.h"
+
+#define FINCH_MAX_PAIRS 64  // B * K limit of the decode-shaped kernels
+
+struct finch_ctx {
+    finch_config cfg{};
+    cudaStream_t stream = nullptr;  // context-owned stream (used when the caller passes NULL)
+    int sm_count = 0;
+    // scratch shared by every call on this context (calls that overlap on the GPU race)
+    float *act = nullptr;           // [max_pairs][moe_inter]   routed SwiGLU activations
+    float *shared_act = nullptr;    // [max_tokens][shared_inter]
+    float *partial = nullptr;       // [max_pairs + max_tokens][hidden] per-pair down outputs (+ shared rows)
+    unsigned *counters = nullptr;   // [hidden / 64 + 64] arrival counters, zero between calls
+    int *dev_status = nullptr;      // sticky device status word
+    // staging for the host-pointer entry points
+    void *stage_dev = nullptr;
+    void *stage_host = nullptr;     // pinned
+    size_t stage_bytes = 0;
+    // prefill workspace (allocated on first use)
+    void *pf_ws = nullptr;
+    size_t pf_ws_bytes = 0;
+    uint64_t launches = 0;
+    std::string err;
+    size_t expert_bytes = 0;
+    struct {
+        size_t gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w, down_s, down_b;
+    } lay{};
+};
+
+struct finch_pool {
+    finch_ctx *ctx = nullptr;
+    int n_layers = 0, n_experts = 0, slots = 0, used = 0;
+    size_t slot_bytes = 0;
+    uint8_t *base = nullptr;          // device: slots * slot_bytes
+    int32_t *slot_table_dev = nullptr;  // device: [n_layers][n_experts] slot or -1
+    std::vector<int32_t> slot_of;     // host mirror
+    std::vector<int32_t> owner;       // slot -> layer * n_experts + expert, or -1
+    std::vector<uint64_t> last_used;
+    uint64_t clock = 0, hits = 0, misses = 0, evictions = 0;
+    int cursor = 0;  // next slot to probe when looking for a free one
+};
+
+struct finch_event {
+    finch_ctx *ctx = nullptr;
+    cudaEvent_t ev = nullptr;
+};
+
+int finch_fail(finch_ctx *ctx, int code, const char *fmt, ...);
+
+#define FINCH_CUDA_OK(ctx, expr)                                                                   \
+    do {                                                                                           \
+        cudaError_t e__ = (expr);                                                                  \
+        if (e__ != cudaSuccess)                                                                    \
+            return finch_fail((ctx), FINCH_E_CUDA, "%s: %s (%s:%d)", #expr, cudaGetErrorString(e__), \
+                              __FILE__, __LINE__);                                                 \
+    } while (0)
+
+static inline cudaStream_t finch_pick_stream(finch_ctx *ctx, finch_stream s) {
+    return s ? (cudaStream_t)s : ctx->stream;
+}
+
+// Implemented in moe_decode.cu / moe_prefill.cu, used by the host-pointer entry point.
+int finch_validate_wdesc(finch_ctx *ctx, const finch_wdesc *w, const char *what);
+
+// ------------------------------------------------------------------ device helpers
+#ifdef __CUDACC__
+
+__device__ __forceinline__ float finch_widen16(uint16_t h, int scale_dtype) {
+    if (scale_dtype == FINCH_FP16) return __half2float(__ushort_as_half(h));
+    return __uint_as_float(((uint32_t)h) << 16);
+}
+
+// two adjacent 16-bit values packed in one word -> floats (lo = first in memory)
+__device__ __forceinline__ void finch_widen16x2(uint32_t w, int scale_dtype, float &lo, float &hi) {
+    if (scale_dtype == FINCH_FP16) {
+        const __half2 h = *reinterpret_cast<const __half2 *>(&w);
+        const float2 f = __half22float2(h);
+        lo = f.x;
+        hi = f.y;
+    } else {
+        lo = __uint_as_float(w << 16);
+        hi = __uint_as_float(w & 0xffff0000u);
+    }
+}
+
+__device__ __forceinline__ uint32_t finch_smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier + bulk async copy (TMA, untiled form) ----
+__device__ __forceinline__ void finch_mbar_init(uint64_t *bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(finch_smem_u32(bar)), "r"(count));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void finch_mbar_expect_tx(uint64_t *bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(finch_smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+// Bounded wait: returns false when the phase did not complete within the limit.
+__device__ __forceinline__ bool finch_mbar_wait(uint64_t *bar, unsigned parity) {
+    const uint32_t a = finch_smem_u32(bar);
+    for (unsigned it = 0; it < (1u << 22); ++it) {
+        unsigned done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+// global -> shared bulk copy; src, dst 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void finch_bulk_g2s(void *dst_smem, const void *src, unsigned bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            finch_smem_u32(dst_smem)),
+        "l"(src), "r"(bytes), "r"(finch_smem_u32(bar))
+        : "memory");
+}
+
+// D = A(16x16, f16, row) * B(16x8, f16, col) + C, fp32 accumulate.
+__device__ __forceinline__ void finch_mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t finch_pack_h2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+#endif  // __CUDACC__

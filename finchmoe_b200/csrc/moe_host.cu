@@ -1,0 +1,48 @@
+// Host-pointer entry point of the MoE layer: packs the caller's CPU buffers
+// into one pinned staging block, copies it to the device in a single transfer,
+// encodes the decode or prefill path, copies the result back and waits.
+#include "finch_internal.cuh"
+
+int finch_stage_reserve(finch_ctx *ctx, size_t bytes);
+
+static inline size_t up256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+extern "C" int finch_moe_forward_host(finch_ctx *ctx, finch_pool *pool, int layer, const void *h_post,
+                                      const int32_t *expert_ids, const float *weights, const uint8_t *valid,
+                                      const finch_shared *shared, const float *shared_gate_score_host, const float *h_mid,
+                                      float *hidden_out, int T) {
+    if (!ctx || !pool || !h_post || !expert_ids || !weights || !hidden_out || T < 1) return FINCH_E_ARG;
+    if (shared && !shared_gate_score_host) return finch_fail(ctx, FINCH_E_ARG, "shared expert given without gate scores");
+    const finch_config &c = ctx->cfg;
+    const size_t elt = c.act_dtype == FINCH_BF16 ? 2 : 4;
+    const size_t n_x = (size_t)T * c.hidden * elt, n_id = (size_t)T * c.top_k * 4, n_w = n_id, n_v = valid ? (size_t)T * c.top_k : 0;
+    const size_t n_s = shared ? (size_t)T * 4 : 0, n_h = h_mid ? (size_t)T * c.hidden * 4 : 0, n_o = (size_t)T * c.hidden * 4;
+    const size_t o_x = 0, o_id = o_x + up256(n_x), o_w = o_id + up256(n_id), o_v = o_w + up256(n_w), o_s = o_v + up256(n_v),
+                 o_h = o_s + up256(n_s), o_o = o_h + up256(n_h), total = o_o + up256(n_o);
+    int rc = finch_stage_reserve(ctx, total);
+    if (rc) return rc;
+    cudaSetDevice(c.device);
+    char *hs = (char *)ctx->stage_host, *ds = (char *)ctx->stage_dev;
+    memcpy(hs + o_x, h_post, n_x);
+    memcpy(hs + o_id, expert_ids, n_id);
+    memcpy(hs + o_w, weights, n_w);
+    if (valid) memcpy(hs + o_v, valid, n_v);
+    if (shared) memcpy(hs + o_s, shared_gate_score_host, n_s);
+    if (h_mid) memcpy(hs + o_h, h_mid, n_h);
+    FINCH_CUDA_OK(ctx, cudaMemcpyAsync(ds, hs, o_o, cudaMemcpyHostToDevice, ctx->stream));
+    finch_shared sh;
+    if (shared) {
+        sh = *shared;
+        sh.gate_score = (const float *)(ds + o_s);
+    }
+    const bool small = (size_t)T * c.top_k <= FINCH_MAX_PAIRS;
+    auto fn = small ? finch_encode_moe_decode : finch_encode_moe_prefill;
+    rc = fn(ctx, ctx->stream, pool, layer, ds + o_x, (const int32_t *)(ds + o_id), (const float *)(ds + o_w),
+            valid ? (const uint8_t *)(ds + o_v) : nullptr, shared ? &sh : nullptr, h_mid ? (const float *)(ds + o_h) : nullptr,
+            (float *)(ds + o_o), T);
+    if (rc) return rc;
+    FINCH_CUDA_OK(ctx, cudaMemcpyAsync(hs + o_o, ds + o_o, n_o, cudaMemcpyDeviceToHost, ctx->stream));
+    FINCH_CUDA_OK(ctx, cudaStreamSynchronize(ctx->stream));
+    memcpy(hidden_out, hs + o_o, n_o);
+    return FINCH_OK;
+}

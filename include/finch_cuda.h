@@ -1,0 +1,220 @@
+/*
+ * finch_cuda.h -- C ABI of libfinchcuda: the quantized-expert MoE hot path of
+ * the FinchMoE engine on NVIDIA B200 (sm_100a).
+ *
+ * The reference engine (finchmoe/infer.m) has no plugin layer: its C host code
+ * builds Metal command buffers inline.  Each entry point below replaces one of
+ * the seams where that host code stops deciding what to run and starts
+ * encoding GPU work; the seam is cited as <reference file>:<lines>.  Conventions
+ * kept from the reference: plain C types, caller-owned pointers, per-expert
+ * valid[] masks instead of errors for missing experts, one calling thread per
+ * context, work made asynchronous by "encode, do not wait" (here: stream order).
+ * Changed on purpose: programmer errors return a status instead of abort().
+ *
+ * "encode" functions take DEVICE pointers and only enqueue work on `stream`;
+ * functions without "encode" take HOST pointers, copy in and out, and return
+ * when the result is in host memory.
+ */
+#ifndef FINCH_CUDA_H
+#define FINCH_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define FINCH_API
+#else
+#define FINCH_API __attribute__((visibility("default")))
+#endif
+
+/* ---- status codes -------------------------------------------------------
+ * FINCH_E_UNSUPPORTED mirrors the reference helpers that return 0 / -1 for
+ * "not handled here, caller falls back" (finchmoe/infer.m:3048-3053, 10955). */
+enum {
+    FINCH_OK = 0,
+    FINCH_E_ARG = 1,         /* shape / alignment / range */
+    FINCH_E_NOSLOT = 2,      /* expert not resident in the pool */
+    FINCH_E_CUDA = 3,
+    FINCH_E_NCCL = 4,
+    FINCH_E_TIMEOUT = 5,     /* a bounded device- or host-side wait ran out */
+    FINCH_E_UNSUPPORTED = 6,
+    FINCH_E_NOMEM = 7
+};
+
+/* 16-bit storage of scales/biases: the reference's files hold BF16
+ * (finchmoe/infer.m:1718-1719); the benchmark's synthetic tensors hold FP16. */
+enum { FINCH_BF16 = 0, FINCH_FP16 = 1, FINCH_F32 = 2 };
+
+/* `bits` convention of the reference's matvec seam (finchmoe/infer.m:1681-1701,
+ * 1249-1258): 3 / 4 / 8 = affine group-quantized, 10 = GGUF Q4_K,
+ * 11 = GGUF Q6_K, 0 = raw BF16 weights. */
+enum { FINCH_BITS_BF16 = 0, FINCH_BITS_Q4_K = 10, FINCH_BITS_Q6_K = 11 };
+
+typedef struct finch_ctx finch_ctx;
+typedef struct finch_pool finch_pool;
+typedef struct finch_event finch_event;
+typedef void *finch_stream; /* cudaStream_t; NULL = the context's own stream */
+
+/* Replaces the model #defines (finchmoe/infer.m:144-156) and the tier globals
+ * g_use_3bit etc. (infer.m:432-436). */
+typedef struct finch_config {
+    int device;       /* CUDA ordinal */
+    int hidden;       /* 2048; multiple of 128 */
+    int n_experts;    /* 256 */
+    int top_k;        /* 8 (1..8) */
+    int moe_inter;    /* 512; multiple of 128 */
+    int shared_inter; /* 512 */
+    int group_size;   /* 64 */
+    int n_layers;     /* 40 */
+    int expert_bits;  /* 3 */
+    int scale_dtype;  /* FINCH_BF16 | FINCH_FP16: storage of scales and biases */
+    int act_dtype;    /* FINCH_F32 | FINCH_BF16: element type of h_post inputs */
+    int max_tokens;   /* largest B / T any encode call will pass (scratch sizing) */
+} finch_config;
+
+/* metal_setup() / teardown, finchmoe/infer.m:2388. */
+FINCH_API int finch_ctx_create(const finch_config *cfg, finch_ctx **out);
+FINCH_API void finch_ctx_destroy(finch_ctx *ctx);
+FINCH_API const char *finch_last_error(const finch_ctx *ctx);
+FINCH_API const char *finch_status_str(int status);
+/* Bytes of one packed routed-expert block for this context
+ * ([gate W|S|B|up W|S|B|down W|S|B], finchmoe/infer.m:223-234). */
+FINCH_API size_t finch_expert_bytes(const finch_ctx *ctx);
+
+/* metal_set_weights(), finchmoe/infer.m:2813: wraps the non-expert weight file
+ * in a GPU buffer; tensors are then addressed as base + offset (2892-2894). */
+FINCH_API int finch_weights_upload(finch_ctx *ctx, const void *host, size_t bytes, void **dev);
+FINCH_API int finch_buf_alloc(finch_ctx *ctx, size_t bytes, void **dev);
+FINCH_API int finch_buf_free(finch_ctx *ctx, void *dev);
+
+/* ---- expert pool --------------------------------------------------------
+ * expert_cache_new / _lookup / _insert / _free (finchmoe/infer.m:6179-6291),
+ * the positional prefill pool (2596-2631) and the pread targets
+ * (6057-6122).  With max_slots == 0 every (layer, expert) owns a slot (all
+ * 40 x 256 3-bit experts are 14.09 GB and stay resident in HBM); with fewer
+ * slots, put() evicts the least recently used entry as the reference's LRU
+ * does (6268-6276).  The (layer, expert) -> slot table also lives on the
+ * device, so kernels resolve expert ids without a host round trip; an expert
+ * that is not resident behaves as valid[k] = 0. */
+FINCH_API int finch_pool_create(finch_ctx *ctx, int n_layers, int n_experts, int max_slots, finch_pool **out);
+FINCH_API void finch_pool_destroy(finch_pool *pool);
+/* Stores the exact on-disk block of one expert (host memory). */
+FINCH_API int finch_pool_put(finch_pool *pool, int layer, int expert, const void *packed_block);
+/* Reads a resident block back to host memory (diagnostics, parity checks). */
+FINCH_API int finch_pool_get(finch_pool *pool, int layer, int expert, void *packed_block_out);
+/* slot_out = slot index, dev_ptr_out = device address of the block.
+ * Returns FINCH_E_NOSLOT when the expert is not resident. */
+FINCH_API int finch_pool_lookup(finch_pool *pool, int layer, int expert, int *slot_out, void **dev_ptr_out);
+typedef struct finch_pool_stats {
+    uint64_t hits, misses, evictions;
+    int slots, used;
+    size_t slot_bytes;
+} finch_pool_stats;
+FINCH_API int finch_pool_get_stats(const finch_pool *pool, finch_pool_stats *out);
+/* Benchmark helper: fills layers [layer0, layer1) with seeded synthetic experts
+ * on the device (codes uniform, scale = |N(0,0.01)|, bias = -4*scale in the
+ * context's scale_dtype) and marks them resident. */
+FINCH_API int finch_pool_fill_synthetic(finch_pool *pool, int layer0, int layer1, uint64_t seed);
+
+/* ---- weight descriptor --------------------------------------------------
+ * BatchMatvecSpec, finchmoe/infer.m:3401-3411 (W / scales / biases / dims /
+ * group_size / bits).  All three pointers are device addresses.  scales and
+ * biases are NULL for bits 0, 10 and 11. */
+typedef struct finch_wdesc {
+    const void *W;
+    const void *scales;
+    const void *biases;
+    int out_dim;
+    int in_dim;
+    int group_size;
+    int bits;
+    int scale_dtype;
+} finch_wdesc;
+
+/* fast_dequant_matvec / gpu_dequant_matvec (finchmoe/infer.m:3369, 2872) and
+ * gpu_gguf_dequant_matvec (3050): out[m][r] = sum_i w[r][i] * x[m][i].
+ * x and out are HOST fp32 arrays ([M][in_dim], [M][out_dim]); synchronous. */
+FINCH_API int finch_matvec(finch_ctx *ctx, const finch_wdesc *w, const float *x_host, float *out_host, int M);
+
+/* fast_batch_matvec / gpu_encode_batch_matvec / routing_batch_fused and
+ * gpu_encode_prefill_matvec (finchmoe/infer.m:4477, 3528, 9061, 3672): n
+ * matvecs of mixed bit width sharing one input x[M][in_dim] (device, element
+ * type x_dtype), outs[i] = device fp32 [M][specs[i].out_dim]. */
+FINCH_API int finch_encode_batch_matvec(finch_ctx *ctx, finch_stream stream, const void *x, int x_dtype,
+                                        const finch_wdesc *specs, float *const *outs, int n, int M);
+
+/* cpu_softmax + cpu_topk + cpu_normalize_weights, run on the CPU by the
+ * reference after a GPU wait (finchmoe/infer.m:9285-9289, 1794-1840).
+ * logits [T][n_experts] -> ids [T][K], weights [T][K] (device).  Same
+ * selection and tie rule (earlier index wins); ids are emitted by descending
+ * probability instead of the reference's slot order. */
+FINCH_API int finch_encode_route_topk(finch_ctx *ctx, finch_stream stream, const float *logits, int n_experts,
+                                      int K, int32_t *ids, float *weights, int T);
+
+/* Shared expert and its gate: finchmoe/infer.m:9608-9629 and the
+ * sigmoid(shared_gate_score) factor of moe_combine_residual
+ * (finchmoe/shaders.metal:2196-2231). */
+typedef struct finch_shared {
+    finch_wdesc gate, up, down;   /* 4-bit affine, group 64 */
+    const float *gate_score;      /* device [B]: raw shared_expert_gate score */
+} finch_shared;
+
+/* gpu_encode_experts_batched + shared expert + moe_combine_residual
+ * (finchmoe/infer.m:4065-4381, 9603-9703): for each of B tokens
+ *   hidden_out = h_mid + sum_{k<K, valid} weights[k] * down_k(silu(gate_k x) * up_k x)
+ *                + sigmoid(gate_score) * shared(x)
+ * with k ascending.  h_post [B][hidden] in the context's act_dtype, expert_ids
+ * / weights [B][K], valid [B][K] bytes or NULL, shared or NULL, h_mid fp32
+ * [B][hidden] or NULL, hidden_out fp32 [B][hidden]; all device pointers.
+ * Experts with valid == 0, an id outside [0, n_experts) or no pool slot are
+ * skipped (never multiplied by zero).  B * K <= 64. */
+FINCH_API int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finch_pool *pool, int layer,
+                                      const void *h_post, const int32_t *expert_ids, const float *weights,
+                                      const uint8_t *valid, const finch_shared *shared, const float *h_mid,
+                                      float *hidden_out, int B);
+
+/* prefill_chunk_cmd3 / _batch_general (finchmoe/infer.m:10704-11241): the same
+ * result for a chunk of T tokens; sorts (token, k) pairs by expert and runs a
+ * grouped dequant-GEMM so every selected expert is read once. */
+FINCH_API int finch_encode_moe_prefill(finch_ctx *ctx, finch_stream stream, finch_pool *pool, int layer,
+                                       const void *h_post, const int32_t *expert_ids, const float *weights,
+                                       const uint8_t *valid, const finch_shared *shared, const float *h_mid,
+                                       float *hidden_out, int T);
+
+/* Host-pointer form of the two calls above (copies in, runs, copies out,
+ * waits): what a caller holding CPU buffers uses, as the reference's
+ * gpu_gguf_experts_forward does (finchmoe/infer.m:3153-3366). */
+FINCH_API int finch_moe_forward_host(finch_ctx *ctx, finch_pool *pool, int layer, const void *h_post,
+                                     const int32_t *expert_ids, const float *weights, const uint8_t *valid,
+                                     const finch_shared *shared, const float *shared_gate_score_host,
+                                     const float *h_mid, float *hidden_out, int T);
+
+/* [cmd commit] / waitUntilCompleted / complete_deferred_experts
+ * (finchmoe/infer.m:9741, 7437-7454). */
+FINCH_API int finch_event_create(finch_ctx *ctx, finch_event **out);
+FINCH_API int finch_event_record(finch_event *ev, finch_stream stream);
+FINCH_API int finch_event_wait(finch_event *ev, int timeout_ms); /* FINCH_E_TIMEOUT if not done in time */
+FINCH_API void finch_event_destroy(finch_event *ev);
+FINCH_API int finch_sync(finch_ctx *ctx);
+/* Sticky device-side status (bounded waits inside kernels); 0 when clean. */
+FINCH_API int finch_device_status(finch_ctx *ctx, int *status_out);
+
+/* --compare-experts (finchmoe/infer.m:9766): the bit-exactness probe.  Writes,
+ * for a weight tensor, the unpacked integer codes [out][in] (u8), the fp32
+ * dequantized weights fl32(fl32(q*s)+b) and their round-to-nearest-even 16-bit
+ * image in w16_dtype (FINCH_BF16 / FINCH_FP16).  Outputs are HOST pointers; any
+ * may be NULL. */
+FINCH_API int finch_debug_dequant(finch_ctx *ctx, const finch_wdesc *w, uint8_t *codes, float *w_f32,
+                                  uint16_t *w16, int w16_dtype);
+
+/* Count of kernels launched by this context since creation (benchmark bookkeeping). */
+FINCH_API uint64_t finch_launch_count(const finch_ctx *ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FINCH_CUDA_H */

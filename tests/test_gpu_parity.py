@@ -1,0 +1,359 @@
+"""GPU parity: the CUDA path, called through the C ABI, against the CPU oracle
+and the committed golden vectors.
+
+Bit-exact: unpacked codes, fp32 dequantized weights, their 16-bit images.
+Tolerance (fp32 accumulation): cos >= 0.99999, max rel err <= 1e-3 (parity.py).
+"""
+import os
+
+import numpy as np
+import pytest
+
+from finchmoe_b200 import lib as L
+from finchmoe_b200 import synth
+from oracle import oracle as orc
+from parity import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def api():
+    from finchmoe_b200 import api as A
+    return A
+
+
+@pytest.fixture(scope="module")
+def ctx_small(api):
+    c = api.Context(hidden=256, n_experts=16, top_k=8, moe_inter=128, shared_inter=128, n_layers=2,
+                    scale_dtype=L.BF16, act_dtype=L.F32, max_tokens=8)
+    yield c
+    c.destroy()
+
+
+def _rne16(w32, dt):
+    if dt == L.FP16:
+        return w32.astype(np.float16).view(np.uint16)
+    return synth.f32_to_bf16_rne(w32)
+
+
+# ------------------------------------------------------------------ dequant
+@pytest.mark.parametrize("bits", [3, 4, 8])
+@pytest.mark.parametrize("sd", [L.BF16, L.FP16])
+def test_dequant_affine_bit_exact(ctx_small, bits, sd):
+    t = synth.affine_tensor(synth.rng_for(2, bits, sd), 40, 512, bits, sd)
+    w = ctx_small.upload_tensor(t)
+    codes, w32, w16 = ctx_small.debug_dequant(w, L.BF16)
+    assert np.array_equal(codes, t["codes"])
+    want = orc.dequant_affine(t["W"], t["S"], t["B"], sd, 40, 512, 64, bits)
+    assert np.array_equal(w32.view(np.uint32), want.view(np.uint32))
+    assert np.array_equal(w16, _rne16(want, L.BF16))
+    _, _, h16 = ctx_small.debug_dequant(w, L.FP16)
+    assert np.array_equal(h16, _rne16(want, L.FP16))
+
+
+def test_dequant_matches_reference_golden(ctx_small, golden_dir):
+    aff = np.load(os.path.join(golden_dir, "affine_reference.npz"))
+    for tag, bits in (("rp3", 3), ("rp4", 4), ("qn4", 4), ("qn8", 8)):
+        pk = aff[tag + "_packed"]
+        o, i = pk.shape[0], pk.shape[1] * 8 // bits
+        t = dict(W=pk, S=aff[tag + "_scales"], B=aff[tag + "_biases"], out_dim=o, in_dim=i, bits=bits, scale_dtype=L.BF16)
+        _, w32, _ = ctx_small.debug_dequant(ctx_small.upload_tensor(t))
+        assert np.array_equal(w32.view(np.uint32), aff[tag + "_dequant"].view(np.uint32)), tag
+
+
+@pytest.mark.parametrize("ty,bits", [(12, 10), (14, 11)])
+def test_dequant_gguf_bit_exact(ctx_small, golden_dir, ty, bits):
+    gg = np.load(os.path.join(golden_dir, "gguf_reference.npz"))
+    name = "q4k" if ty == 12 else "q6k"
+    raw, want = gg[name + "_raw"], gg[name + "_dequant"]
+    t = dict(W=raw, S=None, B=None, out_dim=raw.shape[0], in_dim=want.shape[1], bits=bits, group=256)
+    codes, w32, _ = ctx_small.debug_dequant(ctx_small.upload_tensor(t))
+    assert np.array_equal(w32.view(np.uint32), want.view(np.uint32))
+    assert np.array_equal(codes, orc.gguf_unpack_codes(raw, raw.shape[0], want.shape[1], ty))
+    t2 = synth.gguf_tensor(synth.rng_for(4, ty), 24, 1024, ty)
+    _, w32b, _ = ctx_small.debug_dequant(ctx_small.upload_tensor(t2))
+    assert np.array_equal(w32b.view(np.uint32), orc.dequant_gguf(t2["W"], 24, 1024, ty).view(np.uint32))
+
+
+# ------------------------------------------------------------------- matvec
+@pytest.mark.parametrize("bits,o,i", [(3, 96, 2048), (4, 64, 4096), (8, 40, 512), (10, 72, 2048), (11, 72, 512), (11, 33, 2048)])
+@pytest.mark.parametrize("M", [1, 3, 9])
+def test_matvec_vs_oracle(ctx_small, bits, o, i, M):
+    rng = synth.rng_for(4, bits, M)
+    if bits in (10, 11):
+        t = synth.gguf_tensor(rng, o, i, 12 if bits == 10 else 14)
+    else:
+        t = synth.affine_tensor(rng, o, i, bits, L.FP16)
+    x = synth.activations(rng, M, i)
+    y = ctx_small.fast_dequant_matvec(ctx_small.upload_tensor(t), x)
+    want = orc.matvec(t["W"], t["S"], t["B"], L.FP16, x, o, i, t["group"], bits, orc.ACC_F64)
+    assert_close(y, want, f"matvec bits={bits} M={M}")
+
+
+def test_matvec_bf16_weights_and_bad_args(ctx_small):
+    rng = synth.rng_for(4, 99)
+    wf = synth.activations(rng, 24, 256)
+    t = dict(W=synth.f32_to_bf16_rne(wf), S=None, B=None, out_dim=24, in_dim=256, bits=0)
+    x = synth.activations(rng, 256)
+    y = ctx_small.fast_dequant_matvec(ctx_small.upload_tensor(t), x)
+    assert_close(y, wf.astype(np.float64) @ x.astype(np.float64), "bf16 matvec")
+    w = ctx_small.upload_tensor(t)
+    w.bits = 5
+    with pytest.raises(L.FinchError) as e:
+        ctx_small.fast_dequant_matvec(w, x)
+    assert e.value.status == L.E_UNSUPPORTED
+    w.bits = 4  # affine without scales
+    with pytest.raises(L.FinchError) as e:
+        ctx_small.fast_dequant_matvec(w, x)
+    assert e.value.status == L.E_ARG
+
+
+def test_batch_matvec_mixed_bits_device_pointers(ctx_small):
+    import torch
+    rng = synth.rng_for(4, 7)
+    ts = [synth.affine_tensor(rng, 256, 2048, 8, L.BF16), synth.affine_tensor(rng, 512, 2048, 4, L.BF16),
+          synth.affine_tensor(rng, 512, 2048, 4, L.BF16), synth.affine_tensor(rng, 1, 2048, 8, L.BF16)]
+    specs = [ctx_small.upload_tensor(t) for t in ts]
+    for M, xdt in ((1, L.F32), (4, L.BF16)):
+        x = synth.activations(rng, M, 2048)
+        xd = torch.from_numpy(x).cuda() if xdt == L.F32 else torch.from_numpy(x).cuda().to(torch.bfloat16)
+        outs = [torch.full((M, t["out_dim"]), float("nan"), device="cuda") for t in ts]
+        ctx_small.fast_batch_matvec(xd, xdt, specs, outs, M, stream=torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        for t, o in zip(ts, outs):
+            want = orc.matvec(t["W"], t["S"], t["B"], L.BF16, x, t["out_dim"], 2048, 64, t["bits"], orc.ACC_F64)
+            assert_close(o.cpu().numpy(), want, f"batch bits={t['bits']} M={M}")
+
+
+# -------------------------------------------------------------------- router
+def test_route_topk_vs_oracle(ctx_small):
+    import torch
+    rng = synth.rng_for(1, 5)
+    lg = synth.router_logits(rng, 37, 256)
+    lg[3, 10] = lg[3, 200] = lg[3].max() + 1.0  # exact tie at the top: lower index must rank first
+    lg[4, :] = 0.25                             # all equal: experts 0..7
+    ids_o, w_o = orc.route(lg, 8)
+    d = torch.from_numpy(lg).cuda()
+    ids = torch.empty((37, 8), dtype=torch.int32, device="cuda")
+    w = torch.empty((37, 8), dtype=torch.float32, device="cuda")
+    ctx_small.route_topk(d, 256, 8, ids, w, 37, stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    ids, w = ids.cpu().numpy(), w.cpu().numpy()
+    for t in range(37):
+        assert set(ids[t].tolist()) == set(ids_o[t].tolist()), t
+        mine = dict(zip(ids[t].tolist(), w[t].tolist()))
+        for e, wo in zip(ids_o[t].tolist(), w_o[t].tolist()):
+            assert abs(mine[e] - wo) <= 2e-6 * max(1.0, abs(wo))
+        assert np.all(np.diff(w[t]) <= 1e-7)  # emitted by descending probability
+    assert ids[3, 0] == 10 and ids[3, 1] == 200
+    assert ids[4].tolist() == list(range(8))
+
+
+# ----------------------------------------------------------------- MoE layer
+def _oracle_layer(blocks_by_expert, ids, w, valid, x, cfg, shared=None, score=None, h_mid=None, accum=orc.ACC_F64):
+    T = ids.shape[0]
+    out = np.empty((T, cfg["hidden"]), np.float32)
+    for t in range(T):
+        v = None if valid is None else valid[t]
+        blocks = [blocks_by_expert.get(int(e)) if (v is None or v[k]) else None for k, e in enumerate(ids[t])]
+        vv = np.array([1 if (b is not None and (v is None or v[k])) else 0 for k, b in enumerate(blocks)], np.uint8)
+        out[t] = orc.moe_layer(blocks, w[t], vv, x[t], bits=3, scale_dtype=cfg["sd"], hidden=cfg["hidden"],
+                               inter=cfg["inter"], h_mid=None if h_mid is None else h_mid[t], shared=shared,
+                               shared_gate_score=0.0 if score is None else float(score[t]), accum=accum)
+    return out
+
+
+def _mk_small(api, sd, ad, n_experts=16, max_tokens=8, seed=0):
+    cfg = dict(hidden=256, inter=128, sd=sd)
+    ctx = api.Context(hidden=256, n_experts=n_experts, top_k=8, moe_inter=128, shared_inter=128, n_layers=2,
+                      scale_dtype=sd, act_dtype=ad, max_tokens=max_tokens)
+    rng = synth.rng_for(1, seed)
+    pool = ctx.pool()
+    blocks = {}
+    for e in range(n_experts):
+        blocks[e] = synth.expert_block(rng, 256, 128, 64, 3, sd)
+        pool.put(1, e, blocks[e])
+    return ctx, pool, blocks, cfg, rng
+
+
+@pytest.mark.parametrize("sd", [L.BF16, L.FP16])
+@pytest.mark.parametrize("ad", [L.F32, L.BF16])
+@pytest.mark.parametrize("B", [1, 2, 3, 8])
+def test_moe_decode_small_vs_oracle(api, sd, ad, B):
+    ctx, pool, blocks, cfg, rng = _mk_small(api, sd, ad, seed=B)
+    try:
+        x = synth.activations(rng, B, 256)
+        if ad == L.F32:  # full-precision activations (not bf16-representable)
+            x = (x + rng.normal(0, 1e-3, size=x.shape)).astype(np.float32)
+        ids, w = synth.zipf_routing(rng, B, 16, 8)
+        out = ctx.moe_forward_host(pool, 1, x, ids, w)
+        want = _oracle_layer(blocks, ids, w, None, x, cfg)
+        assert_close(out, want, f"moe B={B}")
+        again = ctx.moe_forward_host(pool, 1, x, ids, w)
+        assert np.array_equal(out.view(np.uint32), again.view(np.uint32)), "not deterministic"
+        assert ctx.device_status() == 0
+    finally:
+        pool.destroy()
+        ctx.destroy()
+
+
+def test_moe_decode_shared_residual_valid_masks(api):
+    ctx, pool, blocks, cfg, rng = _mk_small(api, L.BF16, L.F32, seed=11)
+    try:
+        B = 5
+        x = rng.normal(0, 1, size=(B, 256)).astype(np.float32)
+        ids, w = synth.zipf_routing(rng, B, 16, 8)
+        valid = np.ones((B, 8), np.uint8)
+        valid[0, 2] = valid[3, 7] = 0
+        valid[4, :] = 0                  # a token with no usable expert at all
+        ids[1, 5] = 999                  # out-of-range id: skipped
+        h_mid = rng.normal(0, 1, size=(B, 256)).astype(np.float32)
+        sh = synth.shared_expert(rng, 256, 128, 64, 4, L.BF16)
+        score = rng.normal(0, 1, size=B).astype(np.float32)
+        shd = ctx.make_shared(*[ctx.upload_tensor(t) for t in sh])
+        out = ctx.moe_forward_host(pool, 1, x, ids, w, valid=valid, shared=shd, gate_score=score, h_mid=h_mid)
+        v2 = valid.copy()
+        v2[1, 5] = 0
+        ids2 = ids.copy()
+        ids2[1, 5] = 0
+        want = _oracle_layer(blocks, ids2, w, v2, x, cfg, shared=sh, score=score, h_mid=h_mid)
+        assert_close(out, want, "moe shared+residual+valid")
+        # shared expert alone (every routed expert invalid) == residual + gated shared MLP
+        allz = np.zeros((B, 8), np.uint8)
+        out0 = ctx.moe_forward_host(pool, 1, x, ids, w, valid=allz, shared=shd, gate_score=score, h_mid=h_mid)
+        want0 = _oracle_layer(blocks, ids2, w, allz, x, cfg, shared=sh, score=score, h_mid=h_mid)
+        assert_close(out0, want0, "shared only")
+        # nothing at all: output is the residual, bit for bit
+        out1 = ctx.moe_forward_host(pool, 1, x, ids, w, valid=allz, h_mid=h_mid)
+        assert np.array_equal(out1, h_mid)
+        assert ctx.device_status() == 0
+    finally:
+        pool.destroy()
+        ctx.destroy()
+
+
+def test_moe_skips_non_resident_and_poisoned_experts(api):
+    """An expert that is not in the pool behaves as valid = 0; a resident expert
+    whose block decodes to NaN is skipped (never multiplied by 0) when masked."""
+    ctx, pool, blocks, cfg, rng = _mk_small(api, L.BF16, L.F32, n_experts=16, seed=12)
+    try:
+        x = rng.normal(0, 1, size=(1, 256)).astype(np.float32)
+        ids = np.arange(8, dtype=np.int32)[None, :]
+        w = np.full((1, 8), 0.125, np.float32)
+        bad = blocks[3].copy()
+        Lo = synth.expert_layout(256, 128, 64, 3)
+        bad[Lo["gate_s"]:Lo["gate_s"] + 2] = np.array([0xC0, 0x7F], np.uint8)  # bf16 NaN scale
+        pool.put(1, 3, bad)
+        valid = np.ones((1, 8), np.uint8)
+        valid[0, 3] = 0
+        out = ctx.moe_forward_host(pool, 1, x, ids, w, valid=valid)
+        assert np.all(np.isfinite(out))
+        want = _oracle_layer(blocks, ids, w, valid, x, cfg)
+        assert_close(out, want, "masked NaN expert")
+        # layer 0 holds nothing: every expert is non-resident there
+        out_empty = ctx.moe_forward_host(pool, 0, x, ids, w)
+        assert np.array_equal(out_empty, np.zeros_like(out_empty))
+    finally:
+        pool.destroy()
+        ctx.destroy()
+
+
+@pytest.mark.parametrize("B", [1, 8])
+def test_moe_decode_full_size_vs_oracle(api, B):
+    """BASELINE shapes: hidden 2048, inter 512, 256 experts, top-8, fp16 scales, bf16 activations."""
+    ctx = api.Context(max_tokens=8, n_layers=1)
+    pool = ctx.pool(n_layers=1)
+    try:
+        rng = synth.rng_for(2, B)
+        ids, w = synth.zipf_routing(rng, B, 256, 8)
+        blocks = {}
+        for e in sorted(set(ids.ravel().tolist())):
+            blocks[e] = synth.expert_block(rng, scale_dtype=L.FP16)
+            pool.put(0, e, blocks[e])
+        x = synth.activations(rng, B, 2048)
+        sh = synth.shared_expert(rng, scale_dtype=L.FP16)
+        shd = ctx.make_shared(*[ctx.upload_tensor(t) for t in sh])
+        score = rng.normal(0, 1, size=B).astype(np.float32)
+        h_mid = synth.activations(rng, B, 2048)
+        out = ctx.moe_forward_host(pool, 0, x, ids, w, shared=shd, gate_score=score, h_mid=h_mid)
+        cfg = dict(hidden=2048, inter=512, sd=L.FP16)
+        want = _oracle_layer(blocks, ids, w, None, x, cfg, shared=sh, score=score, h_mid=h_mid)
+        assert_close(out, want, f"full-size B={B}")
+        # without residual/shared: the pure sum_k w_k * expert_k(x) of BASELINE config 1
+        out2 = ctx.moe_forward_host(pool, 0, x, ids, w)
+        want2 = _oracle_layer(blocks, ids, w, None, x, cfg)
+        assert_close(out2, want2, f"full-size routed only B={B}")
+        assert ctx.device_status() == 0
+    finally:
+        pool.destroy()
+        ctx.destroy()
+
+
+# ---------------------------------------------------------------------- pool
+def test_pool_lru_and_roundtrip(api):
+    ctx = api.Context(hidden=256, n_experts=8, top_k=8, moe_inter=128, shared_inter=128, n_layers=2, max_tokens=1)
+    pool = ctx.pool(max_slots=3)
+    try:
+        rng = synth.rng_for(3, 0)
+        blks = [synth.expert_block(rng, 256, 128, 64, 3, L.FP16) for _ in range(5)]
+        for e in range(3):
+            pool.put(0, e, blks[e])
+        assert pool.lookup(0, 0) is not None      # touch 0: now 1 is the least recently used
+        pool.put(0, 3, blks[3])                   # evicts expert 1
+        assert pool.lookup(0, 1) is None
+        assert pool.lookup(0, 0) is not None and pool.lookup(0, 3) is not None
+        assert np.array_equal(pool.get(0, 3), blks[3])
+        st = pool.stats()
+        assert st["evictions"] == 1 and st["slots"] == 3 and st["used"] == 3 and st["misses"] == 1
+        with pytest.raises(L.FinchError):
+            pool.put(5, 0, blks[0])
+    finally:
+        pool.destroy()
+        ctx.destroy()
+
+
+def test_synthetic_fill_distribution_and_property_parity(api):
+    """Device-generated pool: sample experts are read back and pushed through
+    the oracle; every scale is finite, positive and small, bias == -4*scale."""
+    ctx = api.Context(hidden=2048, n_experts=16, top_k=8, moe_inter=512, n_layers=2, max_tokens=2)
+    pool = ctx.pool()
+    try:
+        pool.fill_synthetic(0, 2, 1234)
+        Lo = synth.expert_layout()
+        blk = pool.get(1, 5)
+        s = blk[Lo["gate_s"]:Lo["gate_b"]].view(np.float16).astype(np.float32)
+        b = blk[Lo["gate_b"]:Lo["up_w"]].view(np.float16).astype(np.float32)
+        assert np.all(np.isfinite(s)) and np.all(s >= 0) and 0.004 < s.mean() < 0.012
+        assert np.array_equal(b, (-4 * s).astype(np.float16).astype(np.float32))
+        codes = orc.unpack_codes(blk[Lo["down_w"]:Lo["down_s"]], 2048, 512, 3)
+        hist = np.bincount(codes.ravel(), minlength=8) / codes.size
+        assert np.all(np.abs(hist - 0.125) < 0.01)
+        assert not np.array_equal(blk, pool.get(1, 6)) and not np.array_equal(blk, pool.get(0, 5))
+        rng = synth.rng_for(2, 77)
+        x = synth.activations(rng, 2, 2048)
+        ids, w = synth.zipf_routing(rng, 2, 16, 8)
+        out = ctx.moe_forward_host(pool, 1, x, ids, w)
+        blocks = {int(e): pool.get(1, int(e)) for e in set(ids.ravel().tolist())}
+        want = _oracle_layer(blocks, ids, w, None, x, dict(hidden=2048, inter=512, sd=L.FP16))
+        assert_close(out, want, "synthetic pool")
+    finally:
+        pool.destroy()
+        ctx.destroy()
+
+
+def test_event_wait_and_launch_count(api):
+    import ctypes as C
+    ctx = api.Context(hidden=256, n_experts=8, top_k=8, moe_inter=128, shared_inter=128, n_layers=1, max_tokens=1)
+    try:
+        ev = C.c_void_p()
+        ctx.check(ctx.lib.finch_event_create(ctx.h, C.byref(ev)))
+        ctx.check(ctx.lib.finch_event_record(ev, None))
+        ctx.check(ctx.lib.finch_event_wait(ev, 2000))
+        ctx.lib.finch_event_destroy(ev)
+        n0 = ctx.launch_count()
+        t = synth.affine_tensor(synth.rng_for(3, 3), 8, 64, 4, L.BF16)
+        ctx.fast_dequant_matvec(ctx.upload_tensor(t), np.ones(64, np.float32))
+        assert ctx.launch_count() == n0 + 1
+    finally:
+        ctx.destroy()
