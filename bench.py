@@ -1,0 +1,408 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized-expert MoE decode path.
+
+Workload at N=1: the full 40-layer expert stack, 40 x 256 three-bit experts
+(14.09 GB, resident in HBM, device-generated synthetic values), one 4-bit shared
+expert per layer, batch 8 (headline) and batch 1 (reported under "batch1"),
+per-layer top-8 ids drawn from a Zipf(1.1) popularity, hidden ~N(0,1) bf16.
+One step = one pass of the 40 layers (40 calls of the per-layer entry point).
+Metric = algorithmic HBM bytes per second: every distinct selected expert block
+(1,376,256 B) plus the shared expert (1,769,472 B) per layer, divided by the
+device time of the step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`--impl reference` times the CPU restatement of the reference's own CPU expert
+path (oracle/finch_oracle.c; the reference's Objective-C file does not compile
+here) on the host cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from finchmoe_b200 import synth  # noqa: E402
+
+HIDDEN, INTER, NEXP, TOPK, LAYERS = 2048, 512, 256, 8, 40
+EXPERT_BYTES = 1376256
+SHARED_BYTES = 3 * 589824
+GATEUP_BYTES = 2 * (393216 + 2 * 32768)  # gate + up codes, scales, biases of one expert
+SCALE_FP16, ACT_BF16 = 1, 0
+METRIC = "moe3_decode_hbm_gbs"
+
+
+def routing_sets(batch: int, n_sets: int, n_layers: int = LAYERS):
+    """[set][layer] -> (ids [B,8], weights [B,8]); Zipf(1.1) popularity per layer."""
+    out = []
+    for s in range(n_sets):
+        per_layer = []
+        for l in range(n_layers):
+            per_layer.append(synth.zipf_routing(synth.rng_for(2, l, 100 + s), batch, NEXP, TOPK))
+        out.append(per_layer)
+    return out
+
+
+def alg_bytes(ids: np.ndarray, shared: bool = True) -> int:
+    return len(set(ids.ravel().tolist())) * EXPERT_BYTES + (SHARED_BYTES if shared else 0)
+
+
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "100",
+                                       "-i", str(gpu_index)], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            pass
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.p.terminate()
+        self.p.wait()
+        self.f.flush()
+        self.f.seek(0)
+        sm, mx, reasons, pw = [], [], set(), []
+        for line in self.f.read().splitlines():
+            c = [x.strip() for x in line.split(",")]
+            if len(c) < 9:
+                continue
+            try:
+                sm.append(float(c[1]))
+                mx.append(float(c[2]))
+                pw.append(float(c[3]))
+            except ValueError:
+                continue
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), c[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        self.f.close()
+        os.unlink(self.f.name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        # "under load" = samples at or above the median power draw
+        med_p = float(np.median(pw))
+        load = [s for s, p in zip(sm, pw) if p >= med_p] or sm
+        return {"sm_mhz": float(np.median(load)), "sm_max_mhz": float(max(mx)), "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": float(max(pw))}
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+# --------------------------------------------------------------------- CPU arm
+def cpu_arm(batch: int, sample_layers: int, threads: int, steps: int = 1, warmup: int = 0, blocks_from=None):
+    """Times the oracle's CPU expert path on `sample_layers` layers of the
+    batch-`batch` workload.  Returns (GB/s by the same byte definition, seconds per pass, description)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as orc
+    orc.build()
+    rs = routing_sets(batch, 1, sample_layers)[0]
+    x = synth.activations(synth.rng_for(2, 0, 7), batch, HIDDEN)
+    layers = []
+    total_bytes = 0
+    for l, (ids, w) in enumerate(rs):
+        uniq = sorted(set(ids.ravel().tolist()))
+        if blocks_from is not None:
+            blocks = {e: blocks_from(l, e) for e in uniq}
+        else:
+            rng = synth.rng_for(2, l, 55)
+            one = synth.expert_block(rng, scale_dtype=SCALE_FP16)
+            # distinct contents per expert are irrelevant to CPU speed: rotate one block's bytes
+            blocks = {e: np.roll(one, 3 * i) if i else one for i, e in enumerate(uniq)}
+        sh = synth.shared_expert(synth.rng_for(2, l, 56), scale_dtype=SCALE_FP16)
+        layers.append((ids, w, blocks, sh))
+        total_bytes += alg_bytes(ids)
+    per_tok_threads = min(TOPK, max(1, threads))
+    tok_workers = max(1, threads // per_tok_threads)
+
+    def one_pass():
+        for ids, w, blocks, sh in layers:
+            def tok(t):
+                return orc.moe_layer([blocks[int(e)] for e in ids[t]], w[t], None, x[t], scale_dtype=SCALE_FP16,
+                                     shared=sh, shared_gate_score=0.1, accum=orc.ACC_F32, nthreads=per_tok_threads)
+            if tok_workers > 1 and batch > 1:
+                with ThreadPoolExecutor(tok_workers) as ex:
+                    list(ex.map(tok, range(batch)))
+            else:
+                for t in range(batch):
+                    tok(t)
+    for _ in range(warmup):
+        one_pass()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one_pass()
+    dt = (time.perf_counter() - t0) / steps
+    return total_bytes / dt / 1e9, dt, f"{sample_layers} of {LAYERS} layers, batch {batch}, sequential-fp32 C port"
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    # sized so warmup + steps stay within a few minutes: ~0.03 s per (token, expert) on one core
+    budget_s = 20.0
+    per_layer_s = 8 * 8 * 0.012 / min(cores, 64) + 0.02
+    sample_layers = int(max(1, min(LAYERS, budget_s / max(1, args.steps + args.warmup) / per_layer_s)))
+    gbs, dt, what = cpu_arm(8, sample_layers, cores, steps=args.steps, warmup=args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3 * LAYERS / sample_layers, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "C2: 40-layer 3-bit expert stack decode, batch 8, top-8 of 256, Zipf(1.1)", "batch": 8,
+                   "layers": LAYERS, "hidden": HIDDEN, "moe_inter": INTER, "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port", "sample": what},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line))
+
+
+# --------------------------------------------------------------------- GPU arm
+class Stack:
+    """The 40-layer expert stack resident on one GPU."""
+
+    def __init__(self, device: int, max_tokens: int, layers: int = LAYERS, seed: int = 2024):
+        import torch
+
+        from finchmoe_b200 import api, lib as L
+        self.torch, self.L = torch, L
+        torch.cuda.set_device(device)
+        self.ctx = api.Context(device=device, n_layers=layers, max_tokens=max_tokens, scale_dtype=L.FP16, act_dtype=L.BF16)
+        self.pool = self.ctx.pool()
+        self.pool.fill_synthetic(0, layers, seed)
+        self.layers = layers
+        self.shared = []
+        for l in range(layers):
+            sh = synth.shared_expert(synth.rng_for(2, l, 56), scale_dtype=SCALE_FP16)
+            self.shared.append([self.ctx.upload_tensor(t) for t in sh])
+        self.stream = torch.cuda.Stream(device=device)
+
+    def device_inputs(self, rsets, batch):
+        torch = self.torch
+        dev = []
+        for rs in rsets:
+            ids = torch.from_numpy(np.stack([r[0] for r in rs])).cuda()      # [L,B,8] int32
+            w = torch.from_numpy(np.stack([r[1] for r in rs])).cuda()        # [L,B,8] fp32
+            dev.append((ids, w))
+        x = synth.activations(synth.rng_for(2, 0, 7), batch, HIDDEN)
+        xd = torch.from_numpy(x).cuda().to(torch.bfloat16)
+        score = torch.full((batch,), 0.1, device="cuda")
+        out = torch.empty((self.layers, batch, HIDDEN), device="cuda")
+        return dev, xd, score, out, x
+
+    def encode_step(self, ids, w, xd, score, out, batch):
+        st = self.stream.cuda_stream
+        for l in range(self.layers):
+            sh = self.ctx.make_shared(*self.shared[l], gate_score=score)
+            self.ctx.encode_moe_decode(self.pool, l, xd, ids[l], w[l], None, sh, None, out[l], batch, stream=st)
+
+    def time_steps(self, rsets_dev, xd, score, out, batch, steps, warmup, barrier=None):
+        torch = self.torch
+        for i in range(warmup):
+            ids, w = rsets_dev[i % len(rsets_dev)]
+            self.encode_step(ids, w, xd, score, out, batch)
+        torch.cuda.synchronize()
+        if barrier:
+            barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        for i in range(steps):
+            ids, w = rsets_dev[(warmup + i) % len(rsets_dev)]
+            self.encode_step(ids, w, xd, score, out, batch)
+        e1.record(self.stream)
+        torch.cuda.synchronize()
+        if barrier:
+            barrier()
+        return e0.elapsed_time(e1) / 1e3  # seconds for `steps` steps
+
+    def time_e2e(self, rsets, x, batch, steps, warmup):
+        """Host buffers in and out through finch_moe_forward_host, layer by layer."""
+        torch = self.torch
+        xw = self.ctx.acts_to_wire(x)
+        score = np.full(batch, 0.1, np.float32)
+        h2d = xw.nbytes + batch * TOPK * 8 + score.nbytes
+        d2h = batch * HIDDEN * 4
+
+        def step(rs):
+            last = None
+            for l in range(self.layers):
+                sh = self.ctx.make_shared(*self.shared[l])
+                last = self.ctx.moe_forward_host(self.pool, l, xw, rs[l][0], rs[l][1], shared=sh, gate_score=score)
+            return last
+        for i in range(warmup):
+            step(rsets[i % len(rsets)])
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(steps):
+            step(rsets[(warmup + i) % len(rsets)])
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0), h2d * self.layers, d2h * self.layers
+
+
+def run_ours(args):
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    # N > 1: decode does not shard across GPUs without an exchange step; each rank runs an
+    # independent replica of the stack on its own token batch (weak scaling, no collective).
+    batch = 8
+    stack = Stack(local_rank, max_tokens=8)
+    n_sets = 4
+    rsets = [[(ids, w) for ids, w in rs] for rs in routing_sets(batch, n_sets)]
+    if world > 1:  # a different token batch per rank
+        rsets = [[synth.zipf_routing(synth.rng_for(2, l, 100 + s + 1000 * rank), batch, NEXP, TOPK) for l in range(LAYERS)]
+                 for s in range(n_sets)]
+    dev, xd, score, out, x = stack.device_inputs(rsets, batch)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    n0 = stack.ctx.launch_count()
+    secs = stack.time_steps(dev, xd, score, out, batch, args.steps, args.warmup, barrier if world > 1 else None)
+    launches = stack.ctx.launch_count() - n0
+    clocks = sampler.stop() if sampler else None
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([secs], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        secs = float(t.item())
+    step_bytes = [sum(alg_bytes(ids) for ids, _ in rs) for rs in rsets]
+    timed_bytes = sum(step_bytes[(args.warmup + i) % n_sets] for i in range(args.steps))
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([float(timed_bytes)], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        timed_bytes = float(t.item())
+    value = timed_bytes / secs / 1e9
+
+    # end to end through the host-pointer entry point
+    e2e_secs, h2d, d2h = stack.time_e2e(rsets, x, batch, args.steps, max(1, args.warmup // 2))
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([e2e_secs], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_secs = float(t.item())
+    e2e_value = timed_bytes / e2e_secs / 1e9
+
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    peaks, peak_kind = measured_peaks()
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "C2: 40-layer 3-bit expert stack decode, batch 8, top-8 of 256, Zipf(1.1)", "batch": batch,
+                   "layers": LAYERS, "hidden": HIDDEN, "moe_inter": INTER, "scale_dtype": "fp16", "act_dtype": "bf16",
+                   "pool_gb": LAYERS * NEXP * EXPERT_BYTES / 1e9, "parallelism": "1 GPU" if world == 1 else f"{world} replicas",
+                   "l2": "inputs larger than L2: every step streams >= 0.5 GB of a 14 GB pool; 4 routing sets rotate"},
+        "clocks": clocks,
+        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "hbm_frac_of_" + peak_kind: value / world / peaks["hbm_gbs"],
+    }
+
+    if world == 1:
+        # batch 1 (single-stream decode) on the same pool
+        r1 = [[(ids, w) for ids, w in rs] for rs in routing_sets(1, n_sets)]
+        dev1, xd1, score1, out1, _ = stack.device_inputs(r1, 1)
+        s1 = stack.time_steps(dev1, xd1, score1, out1, 1, args.steps, args.warmup)
+        b1 = sum(sum(alg_bytes(ids) for ids, _ in r1[(args.warmup + i) % n_sets]) for i in range(args.steps))
+        line["batch1"] = {"value": b1 / s1 / 1e9, "unit": "GB/s", "ms_per_step": s1 / args.steps * 1e3,
+                          "us_per_layer": s1 / args.steps / LAYERS * 1e6, "frac_of_" + peak_kind: b1 / s1 / 1e9 / peaks["hbm_gbs"]}
+        # per-kernel roofline of the dominant kernel (gate/up/SiLU)
+        line["roofline"] = kernel_roofline(stack, dev, rsets, xd, score, out, batch, args, peaks, peak_kind)
+        # CPU baseline: bounded sample of the same workload on the expert blocks of this pool
+        cores = os.cpu_count() or 1
+        sample_layers = 2
+        gbs, dt, what = cpu_arm(batch, sample_layers, cores, blocks_from=lambda l, e: stack.pool.get(l, e))
+        line["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port", "sample": what,
+                                "seconds": dt}
+    print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def kernel_roofline(stack, dev, rsets, xd, score, out, batch, args, peaks, peak_kind):
+    """Average duration of the gate/up/SiLU kernel over the same steps, from CUDA
+    events recorded around every launch on the launching stream (a separate pass
+    with per-kernel events, so the headline timing carries no event overhead)."""
+    import ctypes as C
+    lib = stack.ctx.lib
+    if not hasattr(lib, "finch_profile_enable"):
+        return None
+    lib.finch_profile_enable.argtypes = [C.c_void_p, C.c_int]
+    lib.finch_profile_read.argtypes = [C.c_void_p, C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(C.c_int)]
+    n_sets = len(dev)
+    lib.finch_profile_enable(stack.ctx.h, 1)
+    gate_bytes = 0
+    for i in range(args.steps):
+        ids, w = dev[(args.warmup + i) % n_sets]
+        stack.encode_step(ids, w, xd, score, out, batch)
+        gate_bytes += sum(len(set(i_.ravel().tolist())) * GATEUP_BYTES + 2 * 589824 for i_, _ in rsets[(args.warmup + i) % n_sets])
+    stack.torch.cuda.synchronize()
+    ms_a, ms_b, n = C.c_float(), C.c_float(), C.c_int()
+    lib.finch_profile_read(stack.ctx.h, C.byref(ms_a), C.byref(ms_b), C.byref(n))
+    lib.finch_profile_enable(stack.ctx.h, 0)
+    if n.value == 0:
+        return None
+    per_launch_bytes = gate_bytes / n.value
+    achieved = per_launch_bytes / (ms_a.value / n.value * 1e-3) / 1e9
+    return {"bound": "hbm", "kernel": "moe_gateup_kernel", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / peaks["hbm_gbs"], "peak_kind": peak_kind, "traffic": None,
+            "bytes_per_launch": per_launch_bytes, "us_per_launch": ms_a.value / n.value * 1e3,
+            "down_combine_us_per_launch": ms_b.value / n.value * 1e3, "launches_timed": n.value}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -36,6 +36,10 @@ struct finch_ctx {
     void *pf_ws = nullptr;
     size_t pf_ws_bytes = 0;
     uint64_t launches = 0;
+    // optional per-kernel timing of the MoE decode call (finch_profile_enable)
+    bool profile = false;
+    std::vector<cudaEvent_t> prof_events;  // triples: before gate/up, between, after down+combine
+    size_t prof_used = 0;
     std::string err;
     size_t expert_bytes = 0;
     struct {

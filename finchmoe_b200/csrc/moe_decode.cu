@@ -818,11 +818,50 @@ extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finc
     cudaStream_t st = finch_pick_stream(ctx, stream);
     const int chunks_r = c.moe_inter / A_ROWS, chunks_s = shared ? (sh_inter + S_ROWS - 1) / S_ROWS : 0;
     dim3 ga(chunks_r > chunks_s ? chunks_r : chunks_s, a.P + (shared ? 1 : 0));
+    cudaEvent_t *pe = nullptr;
+    if (ctx->profile) {
+        while (ctx->prof_events.size() < ctx->prof_used + 3) {
+            cudaEvent_t e;
+            FINCH_CUDA_OK(ctx, cudaEventCreate(&e));
+            ctx->prof_events.push_back(e);
+        }
+        pe = &ctx->prof_events[ctx->prof_used];
+        ctx->prof_used += 3;
+        FINCH_CUDA_OK(ctx, cudaEventRecord(pe[0], st));
+    }
     moe_gateup_kernel<<<ga, A_THREADS, LA.total, st>>>(a);
     FINCH_CUDA_OK(ctx, cudaGetLastError());
+    if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[1], st));
     dim3 gb(c.hidden / B_ROWS, a.P + 1);
     moe_down_combine_kernel<<<gb, B_THREADS, LB.total, st>>>(a);
     FINCH_CUDA_OK(ctx, cudaGetLastError());
+    if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[2], st));
     ctx->launches += 2;
+    return FINCH_OK;
+}
+
+extern "C" int finch_profile_enable(finch_ctx *ctx, int on) {
+    if (!ctx) return FINCH_E_ARG;
+    ctx->profile = on != 0;
+    ctx->prof_used = 0;
+    return FINCH_OK;
+}
+
+extern "C" int finch_profile_read(finch_ctx *ctx, float *ms_gateup, float *ms_down_combine, int *n_calls) {
+    if (!ctx || !ms_gateup || !ms_down_combine || !n_calls) return FINCH_E_ARG;
+    cudaSetDevice(ctx->cfg.device);
+    FINCH_CUDA_OK(ctx, cudaDeviceSynchronize());
+    float a = 0.f, b = 0.f;
+    for (size_t i = 0; i + 2 < ctx->prof_used + 0 && i + 2 < ctx->prof_events.size() + 0; i += 3) {
+        float t0 = 0.f, t1 = 0.f;
+        FINCH_CUDA_OK(ctx, cudaEventElapsedTime(&t0, ctx->prof_events[i], ctx->prof_events[i + 1]));
+        FINCH_CUDA_OK(ctx, cudaEventElapsedTime(&t1, ctx->prof_events[i + 1], ctx->prof_events[i + 2]));
+        a += t0;
+        b += t1;
+    }
+    *ms_gateup = a;
+    *ms_down_combine = b;
+    *n_calls = (int)(ctx->prof_used / 3);
+    ctx->prof_used = 0;
     return FINCH_OK;
 }

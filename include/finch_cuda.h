@@ -211,6 +211,14 @@ FINCH_API int finch_device_status(finch_ctx *ctx, int *status_out);
 FINCH_API int finch_debug_dequant(finch_ctx *ctx, const finch_wdesc *w, uint8_t *codes, float *w_f32,
                                   uint16_t *w16, int w16_dtype);
 
+/* --timing / LayerTimingAccum (finchmoe/infer.m:281-299): while enabled, every
+ * finch_encode_moe_decode call records CUDA events around its two kernels on
+ * the launching stream; read() waits, returns the summed milliseconds of the
+ * gate/up/SiLU kernels, of the down+combine kernels and the number of calls,
+ * and resets the accumulators. */
+FINCH_API int finch_profile_enable(finch_ctx *ctx, int on);
+FINCH_API int finch_profile_read(finch_ctx *ctx, float *ms_gateup, float *ms_down_combine, int *n_calls);
+
 /* Count of kernels launched by this context since creation (benchmark bookkeeping). */
 FINCH_API uint64_t finch_launch_count(const finch_ctx *ctx);
 
