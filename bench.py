@@ -41,8 +41,9 @@ SCALE_FP16, ACT_BF16 = 1, 0
 METRIC = "moe3_decode_hbm_gbs"
 
 
-def routing_sets(batch: int, n_sets: int, n_layers: int = LAYERS):
+def routing_sets(batch: int, n_sets: int, n_layers: int | None = None):
     """[set][layer] -> (ids [B,8], weights [B,8]); Zipf(1.1) popularity per layer."""
+    n_layers = LAYERS if n_layers is None else n_layers
     out = []
     for s in range(n_sets):
         per_layer = []
@@ -219,19 +220,40 @@ class Stack:
             sh = self.ctx.make_shared(*self.shared[l], gate_score=score)
             self.ctx.encode_moe_decode(self.pool, l, xd, ids[l], w[l], None, sh, None, out[l], batch, stream=st)
 
-    def time_steps(self, rsets_dev, xd, score, out, batch, steps, warmup, barrier=None):
+    def capture(self, rsets_dev, xd, score, out, batch):
+        """One CUDA graph per routing set: the 40 per-layer calls of a step, captured from the stream."""
         torch = self.torch
+        ids, w = rsets_dev[0]
+        self.encode_step(ids, w, xd, score, out, batch)  # first call sets kernel attributes: keep it out of capture
+        torch.cuda.synchronize()
+        graphs = []
+        for ids, w in rsets_dev:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self.stream):
+                self.encode_step(ids, w, xd, score, out, batch)
+            graphs.append(g)
+        return graphs
+
+    def time_steps(self, rsets_dev, xd, score, out, batch, steps, warmup, barrier=None, use_graph=True):
+        torch = self.torch
+        graphs = self.capture(rsets_dev, xd, score, out, batch) if use_graph else None
+
+        def run(i):
+            if graphs is not None:
+                with torch.cuda.stream(self.stream):
+                    graphs[i % len(graphs)].replay()
+            else:
+                ids, w = rsets_dev[i % len(rsets_dev)]
+                self.encode_step(ids, w, xd, score, out, batch)
         for i in range(warmup):
-            ids, w = rsets_dev[i % len(rsets_dev)]
-            self.encode_step(ids, w, xd, score, out, batch)
+            run(i)
         torch.cuda.synchronize()
         if barrier:
             barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(self.stream)
         for i in range(steps):
-            ids, w = rsets_dev[(warmup + i) % len(rsets_dev)]
-            self.encode_step(ids, w, xd, score, out, batch)
+            run(warmup + i)
         e1.record(self.stream)
         torch.cuda.synchronize()
         if barrier:
@@ -274,7 +296,7 @@ def run_ours(args):
     # N > 1: decode does not shard across GPUs without an exchange step; each rank runs an
     # independent replica of the stack on its own token batch (weak scaling, no collective).
     batch = 8
-    stack = Stack(local_rank, max_tokens=8)
+    stack = Stack(local_rank, max_tokens=8, layers=LAYERS)
     n_sets = 4
     rsets = [[(ids, w) for ids, w in rs] for rs in routing_sets(batch, n_sets)]
     if world > 1:  # a different token batch per rank
@@ -289,8 +311,10 @@ def run_ours(args):
 
     sampler = ClockSampler(local_rank) if rank == 0 else None
     n0 = stack.ctx.launch_count()
-    secs = stack.time_steps(dev, xd, score, out, batch, args.steps, args.warmup, barrier if world > 1 else None)
-    launches = stack.ctx.launch_count() - n0
+    secs = stack.time_steps(dev, xd, score, out, batch, args.steps, args.warmup, barrier if world > 1 else None,
+                            use_graph=not args.no_graph)
+    launches = 2 * LAYERS * args.steps  # two kernels per layer call (graph replays launch them without the host counter)
+    del n0
     clocks = sampler.stop() if sampler else None
     if world > 1:
         import torch.distributed as dist
@@ -341,7 +365,7 @@ def run_ours(args):
         # batch 1 (single-stream decode) on the same pool
         r1 = [[(ids, w) for ids, w in rs] for rs in routing_sets(1, n_sets)]
         dev1, xd1, score1, out1, _ = stack.device_inputs(r1, 1)
-        s1 = stack.time_steps(dev1, xd1, score1, out1, 1, args.steps, args.warmup)
+        s1 = stack.time_steps(dev1, xd1, score1, out1, 1, args.steps, args.warmup, use_graph=not args.no_graph)
         b1 = sum(sum(alg_bytes(ids) for ids, _ in r1[(args.warmup + i) % n_sets]) for i in range(args.steps))
         line["batch1"] = {"value": b1 / s1 / 1e9, "unit": "GB/s", "ms_per_step": s1 / args.steps * 1e3,
                           "us_per_layer": s1 / args.steps / LAYERS * 1e6, "frac_of_" + peak_kind: b1 / s1 / 1e9 / peaks["hbm_gbs"]}
@@ -392,12 +416,16 @@ def kernel_roofline(stack, dev, rsets, xd, score, out, batch, args, peaks, peak_
 
 
 def main():
+    global LAYERS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=LAYERS, help="fewer layers = a small case for profiler captures")
+    ap.add_argument("--no-graph", action="store_true", help="launch from the host every step instead of replaying CUDA graphs")
     args = ap.parse_args()
+    LAYERS = args.layers
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -42,7 +42,7 @@ extern "C" int finch_ctx_create(const finch_config *cfg, finch_ctx **out) {
         c.top_k < 1 || c.top_k > 8 || c.n_experts < 1 || c.n_layers < 1 || c.max_tokens < 1 ||
         (c.expert_bits != 3) || (c.scale_dtype != FINCH_BF16 && c.scale_dtype != FINCH_FP16) ||
         (c.act_dtype != FINCH_F32 && c.act_dtype != FINCH_BF16) || (c.shared_inter % 64) || c.hidden > 8192 ||
-        c.moe_inter > 8192)
+        c.moe_inter > 8192 || c.moe_inter > c.hidden || c.shared_inter > c.hidden || c.shared_inter < 0)
         return FINCH_E_ARG;
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || c.device < 0 || c.device >= ndev) return FINCH_E_CUDA;
@@ -74,10 +74,11 @@ extern "C" int finch_ctx_create(const finch_config *cfg, finch_ctx **out) {
     bool ok = cudaMalloc(&ctx->act, pairs * c.moe_inter * sizeof(float)) == cudaSuccess &&
               cudaMalloc(&ctx->shared_act, (size_t)c.max_tokens * sh_inter * sizeof(float)) == cudaSuccess &&
               cudaMalloc(&ctx->partial, (pairs + c.max_tokens) * c.hidden * sizeof(float)) == cudaSuccess &&
-              cudaMalloc(&ctx->counters, (c.hidden / 64 + 64) * sizeof(unsigned)) == cudaSuccess &&
-              cudaMalloc(&ctx->dev_status, sizeof(int)) == cudaSuccess;
+              cudaMalloc(&ctx->counters, (c.hidden / 64 + 128) * sizeof(unsigned)) == cudaSuccess &&
+              cudaMalloc(&ctx->dev_status, sizeof(int)) == cudaSuccess &&
+              cudaMalloc(&ctx->frag_scratch, finch_decode_scratch_bytes(c)) == cudaSuccess;
     if (!ok) return bail(FINCH_E_NOMEM);
-    cudaMemset(ctx->counters, 0, (c.hidden / 64 + 64) * sizeof(unsigned));
+    cudaMemset(ctx->counters, 0, (c.hidden / 64 + 128) * sizeof(unsigned));
     cudaMemset(ctx->dev_status, 0, sizeof(int));
     cudaMemset(ctx->partial, 0, (pairs + c.max_tokens) * c.hidden * sizeof(float));
     if (cudaDeviceSynchronize() != cudaSuccess) return bail(FINCH_E_CUDA);
@@ -94,6 +95,7 @@ extern "C" void finch_ctx_destroy(finch_ctx *ctx) {
     cudaFree(ctx->partial);
     cudaFree(ctx->counters);
     cudaFree(ctx->dev_status);
+    cudaFree(ctx->frag_scratch);
     cudaFree(ctx->stage_dev);
     cudaFree(ctx->pf_ws);
     if (ctx->stage_host) cudaFreeHost(ctx->stage_host);

@@ -26,8 +26,10 @@ struct finch_ctx {
     float *act = nullptr;           // [max_pairs][moe_inter]   routed SwiGLU activations
     float *shared_act = nullptr;    // [max_tokens][shared_inter]
     float *partial = nullptr;       // [max_pairs + max_tokens][hidden] per-pair down outputs (+ shared rows)
-    unsigned *counters = nullptr;   // [hidden / 64 + 64] arrival counters, zero between calls
+    unsigned *counters = nullptr;   // [hidden / 64 + 128] arrival counters, zero between calls
     int *dev_status = nullptr;      // sticky device status word
+    void *frag_scratch = nullptr;   // tensor-core operand fragments + expert-group table (moe_decode.cu)
+    int force_prep = -1;            // test hook: -1 auto, 0 never, 1 always run the prep kernel
     // staging for the host-pointer entry points
     void *stage_dev = nullptr;
     void *stage_host = nullptr;     // pinned
@@ -81,6 +83,7 @@ static inline cudaStream_t finch_pick_stream(finch_ctx *ctx, finch_stream s) {
 
 // Implemented in moe_decode.cu / moe_prefill.cu, used by the host-pointer entry point.
 int finch_validate_wdesc(finch_ctx *ctx, const finch_wdesc *w, const char *what);
+size_t finch_decode_scratch_bytes(const finch_config &c);
 
 // ------------------------------------------------------------------ device helpers
 #ifdef __CUDACC__

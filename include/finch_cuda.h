@@ -219,6 +219,12 @@ FINCH_API int finch_debug_dequant(finch_ctx *ctx, const finch_wdesc *w, uint8_t 
 FINCH_API int finch_profile_enable(finch_ctx *ctx, int on);
 FINCH_API int finch_profile_read(finch_ctx *ctx, float *ms_gateup, float *ms_down_combine, int *n_calls);
 
+/* Test hook for finch_encode_moe_decode: it normally decides by the batch size
+ * whether a preparation kernel builds the activation operands once per token
+ * (mode -1); 0 forces the build inside every CTA, 1 forces the preparation
+ * kernel.  Results are identical.  No counterpart in the reference. */
+FINCH_API int finch_debug_force_prep(finch_ctx *ctx, int mode);
+
 /* Count of kernels launched by this context since creation (benchmark bookkeeping). */
 FINCH_API uint64_t finch_launch_count(const finch_ctx *ctx);
 
