@@ -5,6 +5,7 @@
 #include <thread>
 
 #include "finch_internal.cuh"
+#include "tile_layout.h"
 
 int finch_fail(finch_ctx *ctx, int code, const char *fmt, ...) {
     char buf[512];
@@ -96,6 +97,7 @@ extern "C" void finch_ctx_destroy(finch_ctx *ctx) {
     cudaFree(ctx->counters);
     cudaFree(ctx->dev_status);
     cudaFree(ctx->frag_scratch);
+    for (auto &e : ctx->shared_cache) cudaFree(e.tiles);
     cudaFree(ctx->stage_dev);
     cudaFree(ctx->pf_ws);
     if (ctx->stage_host) cudaFreeHost(ctx->stage_host);
@@ -240,7 +242,9 @@ extern "C" int finch_pool_put(finch_pool *p, int layer, int expert, const void *
     const int key = layer * p->n_experts + expert;
     const int slot = pool_claim_slot(p, key);
     p->last_used[slot] = ++p->clock;
-    FINCH_CUDA_OK(ctx, cudaMemcpy(p->base + (size_t)slot * p->slot_bytes, block, ctx->expert_bytes, cudaMemcpyHostToDevice));
+    p->tmp.resize(ctx->expert_bytes);
+    finch_retile(ctx->cfg.hidden, ctx->cfg.moe_inter, (const uint8_t *)block, p->tmp.data(), 1);
+    FINCH_CUDA_OK(ctx, cudaMemcpy(p->base + (size_t)slot * p->slot_bytes, p->tmp.data(), ctx->expert_bytes, cudaMemcpyHostToDevice));
     const int32_t s32 = slot;
     FINCH_CUDA_OK(ctx, cudaMemcpy(p->slot_table_dev + key, &s32, sizeof s32, cudaMemcpyHostToDevice));
     return FINCH_OK;
@@ -265,7 +269,9 @@ extern "C" int finch_pool_get(finch_pool *p, int layer, int expert, void *out) {
     const int slot = p->slot_of[layer * p->n_experts + expert];
     if (slot < 0) return FINCH_E_NOSLOT;
     cudaSetDevice(p->ctx->cfg.device);
-    FINCH_CUDA_OK(p->ctx, cudaMemcpy(out, p->base + (size_t)slot * p->slot_bytes, p->ctx->expert_bytes, cudaMemcpyDeviceToHost));
+    p->tmp.resize(p->ctx->expert_bytes);
+    FINCH_CUDA_OK(p->ctx, cudaMemcpy(p->tmp.data(), p->base + (size_t)slot * p->slot_bytes, p->ctx->expert_bytes, cudaMemcpyDeviceToHost));
+    finch_retile(p->ctx->cfg.hidden, p->ctx->cfg.moe_inter, p->tmp.data(), (uint8_t *)out, 0);
     return FINCH_OK;
 }
 
@@ -288,49 +294,42 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
     return z ^ (z >> 31);
 }
 
-// One thread per 8 bytes of a block.  Code regions get random bytes; the
-// 16-bit regions get scale = |N(0, 0.01)| (Box-Muller) and bias = -4*scale
-// computed from the stored (rounded) scale.
-__global__ void pool_fill_kernel(uint8_t *base, size_t slot_bytes, size_t expert_bytes, int first_slot, uint64_t seed,
-                                 size_t gate_s, size_t up_w, size_t up_s, size_t down_w, size_t down_s,
-                                 size_t gs_bytes, size_t ds_bytes, int scale_dtype) {
-    const size_t words = expert_bytes / 8;
+// One thread per 32-bit word of a block (tiled layout, tile_layout.h).  Code
+// words get random bits; a scale word holds two scales = |N(0, 0.01)|
+// (Box-Muller) and the matching bias word holds -4 * the stored (rounded) scale.
+__device__ __forceinline__ uint16_t synth_scale16(uint64_t key, int scale_dtype, bool bias) {
+    const uint64_t r = mix64(key);
+    const float u1 = ((r >> 40) + 1) * (1.0f / 16777217.0f), u2 = ((r >> 8) & 0xffffff) * (1.0f / 16777216.0f);
+    const float s = fabsf(0.01f * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2));
+    if (scale_dtype == FINCH_FP16) {
+        const __half h = __float2half_rn(s);
+        return bias ? __half_as_ushort(__float2half_rn(-4.0f * __half2float(h))) : __half_as_ushort(h);
+    }
+    const __nv_bfloat16 h = __float2bfloat16_rn(s);
+    return bias ? __bfloat16_as_ushort(__float2bfloat16_rn(-4.0f * __bfloat162float(h))) : __bfloat16_as_ushort(h);
+}
+
+__global__ void pool_fill_kernel(uint8_t *base, size_t slot_bytes, int first_slot, uint64_t seed, FinchTile T, int scale_dtype) {
+    const size_t words = T.total / 4;
     const int slot = first_slot + blockIdx.y;
-    uint8_t *blk = base + (size_t)slot * slot_bytes;
+    uint32_t *blk = reinterpret_cast<uint32_t *>(base + (size_t)slot * slot_bytes);
     for (size_t w = (size_t)blockIdx.x * blockDim.x + threadIdx.x; w < words; w += (size_t)gridDim.x * blockDim.x) {
-        const size_t off = w * 8;
-        // region classification
-        int kind = 0;  // 0 codes, 1 scales, 2 biases
-        size_t sreg = 0, rel = 0, sbytes = 0;
-        if (off >= gate_s && off < up_w) { sreg = gate_s; sbytes = gs_bytes; }
-        else if (off >= up_s && off < down_w) { sreg = up_s; sbytes = gs_bytes; }
-        else if (off >= down_s) { sreg = down_s; sbytes = ds_bytes; }
-        if (sbytes) {
-            rel = off - sreg;
-            kind = rel < sbytes ? 1 : 2;
-            if (kind == 2) rel -= sbytes;
-        }
-        uint64_t out;
-        if (kind == 0) {
-            out = mix64(seed ^ ((uint64_t)slot << 32) ^ (uint64_t)w);
+        const size_t off = w * 4;
+        const bool isB = off >= T.b_base;
+        const size_t o2 = isB ? off - T.b_base : off;
+        const int tsz = isB ? T.tileB : T.tileA, sb0 = isB ? T.sbB : T.sbA;
+        const int tile = (int)(o2 / tsz), rel = (int)(o2 % tsz);
+        uint32_t out;
+        if (rel < sb0) {
+            out = (uint32_t)mix64(seed ^ ((uint64_t)slot << 32) ^ (uint64_t)w);
         } else {
-            // the scale at element index rel/2 + j of its region; biases mirror the scale stream
-            uint16_t h[4];
-            for (int j = 0; j < 4; j++) {
-                const uint64_t r = mix64(seed ^ 0xabcdefull ^ ((uint64_t)slot << 32) ^ (uint64_t)((sreg + rel) / 2 + j));
-                const float u1 = ((r >> 40) + 1) * (1.0f / 16777217.0f), u2 = ((r >> 8) & 0xffffff) * (1.0f / 16777216.0f);
-                const float s = fabsf(0.01f * sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2));
-                float sv;
-                uint16_t sb;
-                if (scale_dtype == FINCH_FP16) { sb = __half_as_ushort(__float2half_rn(s)); sv = __half2float(__ushort_as_half(sb)); }
-                else { sb = __bfloat16_as_ushort(__float2bfloat16_rn(s)); sv = __uint_as_float((uint32_t)sb << 16); }
-                if (kind == 1) h[j] = sb;
-                else h[j] = scale_dtype == FINCH_FP16 ? __half_as_ushort(__float2half_rn(-4.0f * sv))
-                                                       : __bfloat16_as_ushort(__float2bfloat16_rn(-4.0f * sv));
-            }
-            out = (uint64_t)h[0] | ((uint64_t)h[1] << 16) | ((uint64_t)h[2] << 32) | ((uint64_t)h[3] << 48);
+            const int e = (rel - sb0) / 4, field = e & 3, g = (e >> 2) & 7, u = e >> 5;
+            const bool bias = field >= 2;
+            const uint64_t id = (((((uint64_t)tile * 8 + g) * 2 + (field & 1)) * 128 + u) * 2) | ((uint64_t)isB << 40);
+            const uint64_t key = seed ^ 0xabcdefull ^ ((uint64_t)slot << 42);
+            out = (uint32_t)synth_scale16(key ^ id, scale_dtype, bias) | ((uint32_t)synth_scale16(key ^ (id + 1), scale_dtype, bias) << 16);
         }
-        *reinterpret_cast<uint64_t *>(blk + off) = out;
+        blk[w] = out;
     }
 }
 
@@ -339,8 +338,7 @@ extern "C" int finch_pool_fill_synthetic(finch_pool *p, int layer0, int layer1, 
     finch_ctx *ctx = p->ctx;
     if (p->slots != p->n_layers * p->n_experts) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "synthetic fill needs a fully resident pool");
     cudaSetDevice(ctx->cfg.device);
-    const auto &L = ctx->lay;
-    const size_t gs = L.gate_b - L.gate_s, ds = L.down_b - L.down_s;
+    const FinchTile T = finch_tile(ctx->cfg.hidden, ctx->cfg.moe_inter);
     for (int l = layer0; l < layer1; l++) {
         // identity slot assignment: slot = layer * n_experts + expert
         for (int e = 0; e < p->n_experts; e++) {
@@ -354,9 +352,8 @@ extern "C" int finch_pool_fill_synthetic(finch_pool *p, int layer0, int layer1, 
             }
         }
         dim3 grid(64, p->n_experts);
-        pool_fill_kernel<<<grid, 256, 0, ctx->stream>>>(p->base, p->slot_bytes, ctx->expert_bytes, l * p->n_experts,
-                                                        seed + (uint64_t)l * 0x10001ull, L.gate_s, L.up_w, L.up_s, L.down_w,
-                                                        L.down_s, gs, ds, ctx->cfg.scale_dtype);
+        pool_fill_kernel<<<grid, 256, 0, ctx->stream>>>(p->base, p->slot_bytes, l * p->n_experts, seed + (uint64_t)l * 0x10001ull, T,
+                                                        ctx->cfg.scale_dtype);
         FINCH_CUDA_OK(ctx, cudaGetLastError());
     }
     p->used = 0;

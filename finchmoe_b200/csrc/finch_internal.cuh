@@ -29,6 +29,12 @@ struct finch_ctx {
     unsigned *counters = nullptr;   // [hidden / 64 + 128] arrival counters, zero between calls
     int *dev_status = nullptr;      // sticky device status word
     void *frag_scratch = nullptr;   // tensor-core operand fragments + expert-group table (moe_decode.cu)
+    void *dbg = nullptr;            // finch_debug_timing buffer
+    struct SharedPrepared {
+        const void *key[3];
+        void *tiles;
+    };
+    std::vector<SharedPrepared> shared_cache;  // tiled copies of the shared experts seen so far
     int force_prep = -1;            // test hook: -1 auto, 0 never, 1 always run the prep kernel
     // staging for the host-pointer entry points
     void *stage_dev = nullptr;
@@ -60,6 +66,7 @@ struct finch_pool {
     std::vector<uint64_t> last_used;
     uint64_t clock = 0, hits = 0, misses = 0, evictions = 0;
     int cursor = 0;  // next slot to probe when looking for a free one
+    std::vector<uint8_t> tmp;  // host staging for the disk <-> tiled permutation
 };
 
 struct finch_event {

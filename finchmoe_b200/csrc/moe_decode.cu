@@ -1,15 +1,21 @@
 // MoE decode path: routed 3-bit experts (gate, up, SiLU, down), the 4-bit
-// shared expert and the router-weighted combine.
+// shared expert and the router-weighted combine, in three launches per layer.
 //
-//   prep      (only when the call has >= PREP_MIN_TOKENS tokens) groups the
-//             (token, k) pairs by expert and turns every token's activations
-//             into tensor-core operand fragments once, instead of once per CTA
-//   kernel A  gate/up/SiLU : one CTA per (expert group, 16 gate rows + the 16
-//             matching up rows); writes act[pair][inter]; the last CTA of a
-//             group turns the finished activations into fragments for kernel B
-//   kernel B  down + combine: one CTA per (expert group, 64 down rows); writes
-//             per-pair down outputs to scratch; the last CTA to arrive for a
-//             row chunk sums them in k order with the residual and the gated
+//   prep      groups the (token, k) pairs by expert, turns every token's
+//             activations into tensor-core operand records, and cuts the job
+//             lists of the two streaming kernels into one contiguous,
+//             cost-balanced range per CTA
+//   kernel A  gate/up/SiLU.  One persistent CTA per SM: a producer warp streams
+//             tiles (8 gate rows + the 8 matching up rows of one expert = one
+//             contiguous 14 KB piece of the tiled pool) through a ring of
+//             shared-memory stages with bulk async copies; twelve consumer
+//             warps each take whole tiles and run the tensor-core matvec on
+//             them, with no barrier between warps.  Writes act[pair][inter].
+//   kernel B  down + combine.  Same structure with tiles of 16 down rows.  Every
+//             CTA first turns the activations of the (few) expert groups in
+//             its range into operand records in its own shared memory.
+//             Per-pair outputs go to scratch; the CTA that completes a 64-row
+//             chunk sums them in k order with the residual and the gated
 //             shared expert (the arithmetic of moe_combine_residual,
 //             finchmoe/shaders.metal:2196-2231).
 //
@@ -29,22 +35,28 @@
 // of a quad owns period t of a 48-byte unit (128 codes = two groups); the two
 // groups of a unit are kept apart by giving them different B columns.
 #include "finch_internal.cuh"
+#include "tile_layout.h"
 
 namespace {
 
-constexpr int A_THREADS = 256;
-constexpr int A_WARPS = 8;
-constexpr int A_ROWS = 16;  // gate rows (and up rows) per CTA in the 3-bit path: two MMA tiles
-constexpr int S_ROWS = 8;   // gate rows (and up rows) per CTA in the 4-bit shared path: one MMA tile
-constexpr int B_THREADS = 128;
-constexpr int B_ROWS = 64;  // down rows per CTA: one MMA tile per warp
-constexpr int PREP_MIN_TOKENS = 3;
-constexpr int FRAG_PAD = 64;  // bytes between per-token fragment regions (keeps them on different banks)
+constexpr int TEAM_A = 4;                   // warps that split the K dimension of one gate/up tile
+constexpr int NTEAM_A = 4;
+constexpr int CW_A = TEAM_A * NTEAM_A;      // consumer warps of kernel A
+constexpr int NT_A = (CW_A + 1) * 32;       // + one producer warp
+constexpr int CW_B = 16;
+constexpr int NT_B = (CW_B + 1) * 32;
+constexpr int MAXP = FINCH_MAX_PAIRS;
+constexpr int MAXM = 8;                     // pairs per expert group (<= tokens per call)
+constexpr int MAXG = 160;                   // CTAs per streaming kernel (range table size)
+constexpr int REC_CAP = 24;                 // act records a CTA of kernel B can hold
 
-struct WRef {  // affine tensor in device memory
-    const uint8_t *W;
-    const uint16_t *S, *B;
-    int out_dim, in_dim;
+struct GroupTab {  // expert groups of one call + the job ranges of the CTAs
+    int ng;
+    int slot[MAXP];             // pool slot of the group's expert
+    unsigned char m[MAXP];      // pairs in the group
+    unsigned char pairs[MAXP][MAXM];
+    int range_a[MAXG + 1];      // CTA b of kernel A runs jobs [range_a[b], range_a[b+1])
+    int range_b[MAXG + 1];
 };
 
 struct MoeArgs {
@@ -59,36 +71,33 @@ struct MoeArgs {
     const uint8_t *valid;
     int P, K, B;
     int hidden, inter;
-    size_t gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w, down_s, down_b;
     int scale_dtype;
-    float *act;        // [P][inter]
-    float *partial;    // [P + B][hidden]
-    unsigned *counters;  // [hidden / 64] row-chunk arrivals of kernel B, then [P + 1] group arrivals of kernel A
-    unsigned *cnt_a;
+    float *act;          // [P][inter]
+    float *partial;      // [P + B][hidden]
+    unsigned *cnt_b;     // [hidden / 64] chunk arrivals of kernel B
     int *status;
     int has_shared;
-    WRef sh_gate, sh_up, sh_down;
+    const uint8_t *sh_tiles;  // prepared (tiled) copy of the shared expert
     int sh_scale_dtype, sh_inter;
-    float *shared_act;  // [B][sh_inter]
+    float *shared_act;   // [B][sh_inter]
     const float *gate_score;
     const float *h_mid;
     float *hidden_out;
-    // operand fragments in global scratch
-    int use_prep;
-    uint2 *xfrag3;  // [B][hidden/128 * 72]   (prep)
-    uint2 *xfrag4;  // [B][hidden/64 * 32]    (prep, shared expert)
-    float *xXg;     // [B][128]
-    int *xE;        // [B]
-    int2 *grp;      // [P] {m, slot}: m = 0 unless pair p is the first of its group
-    uint8_t *grp_pairs;  // [P][64]
-    int *n_groups;
-    uint2 *afrag3;  // [P][inter/128 * 72]    (written by kernel A)
-    float *aXg;     // [P][128]
-    int *aE;        // [P]
-    uint2 *sfrag4;  // [B][sh_inter/64 * 32]
-    float *sXg;     // [B][128]
-    int *sE;        // [B]
+    GroupTab *gtab;      // written by prep
+    uint8_t *xrec3;      // [B] records: 3-bit-layout operands of h_post + header
+    uint8_t *xrec4;      // [B] 4-bit-layout operand fragments of h_post (shared expert)
+    int grid_a, grid_b, stages_a, stages_b;
+    long long *dbg;      // optional per-CTA cycle counters (finch_debug_timing), or NULL
 };
+
+// ---- operand records -------------------------------------------------------
+// record = fragments (8-byte entries) followed by a header of floats:
+// hdr[0..groups) = sum of x over each group of 64, hdr[groups] = E (int bits).
+__host__ __device__ inline int frag3_bytes(int K) { return (K / 128) * 72 * 8; }
+__host__ __device__ inline int frag4_bytes(int K) { return (K / 64) * 32 * 8; }
+__host__ __device__ inline int hdr_bytes(int K) { return ((K / 64 + 1 + 15) / 16) * 64; }
+__host__ __device__ inline int rec3_bytes(int K) { return frag3_bytes(K) + hdr_bytes(K); }
+__host__ __device__ inline int rec4_bytes(int K) { return frag4_bytes(K) + hdr_bytes(K); }
 
 // slot-in-register tables of the 3-bit extraction: entry [2*e + half] for
 // extraction e (0..17) = code index inside the 32-code period (-1: empty) and
@@ -117,13 +126,17 @@ __device__ __forceinline__ void extract4(uint32_t w, uint32_t (&e)[4]) {
 }
 
 __device__ __forceinline__ float pow2_biased(int e) { return __uint_as_float((uint32_t)e << 23); }
+__device__ __forceinline__ void bar_sync(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(finch_smem_u32(bar)) : "memory");
+}
 
-// Loads one activation row into xs (fp32 shared memory) and produces the group
-// sums Xg[0..K/64) and E, the biased exponent of a power of two > max|x|
-// (clamped so that every derived scale factor is a normal float).  All NT
-// threads of the CTA take part; ends with a barrier.
+// Loads one activation row into xs (fp32 shared memory) and writes the group
+// sums hdr[0..K/64) and hdr[K/64] = E, the biased exponent of a power of two
+// > max|x| (clamped so every derived scale factor is a normal float).  Run by
+// the NT threads tid = 0..NT-1 that share named barrier `bar`; ends with it.
 template <int NT>
-__device__ void load_x(const void *src, int dtype, int K, float *xs, float *Xg, float *warp_max, int *E_out) {
+__device__ void load_x(const void *src, int dtype, int K, float *xs, float *hdr, float *warp_max, int bar) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float amax = 0.f;
     for (int base0 = 0; base0 < K; base0 += NT * 8) {
@@ -159,21 +172,21 @@ __device__ void load_x(const void *src, int dtype, int K, float *xs, float *Xg, 
         if (base < K) {
             *reinterpret_cast<float4 *>(xs + base) = make_float4(v[0], v[1], v[2], v[3]);
             *reinterpret_cast<float4 *>(xs + base + 4) = make_float4(v[4], v[5], v[6], v[7]);
-            if ((lane & 7) == 0) Xg[base >> 6] = s;
+            if ((lane & 7) == 0) hdr[base >> 6] = s;
         }
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     if (lane == 0) warp_max[warp] = amax;
-    __syncthreads();
+    bar_sync(bar, NT);
     if (tid == 0) {
         float m = 0.f;
         for (int w = 0; w < NT / 32; w++) m = fmaxf(m, warp_max[w]);
         int E = (int)(__float_as_uint(m) >> 23) + 1;
         E = E < 30 ? 30 : (E > 230 ? 230 : E);
-        *E_out = E;
+        hdr[K / 64] = __int_as_float(E);
     }
-    __syncthreads();
+    bar_sync(bar, NT);
 }
 
 // hi / lo fp16 split of four pre-scaled activations -> the two B-fragment entries of one lane.
@@ -189,12 +202,11 @@ __device__ __forceinline__ void split4(const float (&xv)[4], uint2 &hi, uint2 &l
     lo = make_uint2(finch_pack_h2(l[0], l[1]), finch_pack_h2(l[2], l[3]));
 }
 
-// B fragments of one token, 3-bit layout: frag[((u * 9 + j) * 2 + term) * 4 + t]
-// (K/128 * 72 entries of 8 bytes).  frag may be shared or global memory.
-template <int NT>
-__device__ void build_frag3(const float *xs, int K, int E, uint2 *frag) {
+// B fragments of one token, 3-bit layout: frag[((u * 9 + j) * 2 + term) * 4 + t].
+// frag may be shared or global memory.
+__device__ __forceinline__ void build_frag3_range(const float *xs, int K, int E, uint2 *frag, int first, int stride) {
     const int entries = (K / 128) * 36;
-    for (int e = threadIdx.x; e < entries; e += NT) {
+    for (int e = first; e < entries; e += stride) {
         const int u = e / 36, r = e - u * 36, j = r >> 2, t = r & 3;
         float xv[4];
 #pragma unroll
@@ -211,12 +223,15 @@ __device__ void build_frag3(const float *xs, int K, int E, uint2 *frag) {
     }
 }
 
-// B fragments of one token, 4-bit layout: frag[((gamma * 4 + j) * 2 + term) * 4 + t]
-// (K/64 * 32 entries).
 template <int NT>
-__device__ void build_frag4(const float *xs, int K, int E, uint2 *frag) {
+__device__ __forceinline__ void build_frag3(const float *xs, int K, int E, uint2 *frag) {
+    build_frag3_range(xs, K, E, frag, threadIdx.x, NT);
+}
+
+// B fragments of one token, 4-bit layout: frag[((gamma * 4 + j) * 2 + term) * 4 + t].
+__device__ __forceinline__ void build_frag4_range(const float *xs, int K, int E, uint2 *frag, int first, int stride) {
     const int entries = (K / 64) * 16;
-    for (int e = threadIdx.x; e < entries; e += NT) {
+    for (int e = first; e < entries; e += stride) {
         const int gamma = e >> 4, j = (e >> 2) & 3, t = e & 3;
         const int wbase = gamma * 64 + (2 * t + (j >> 1)) * 8 + ((j & 1) ? 2 : 0);
         // slots: (code, p) = (0,0) (4,0) (1,4) (5,4) for even j; (2,0) (6,0) (3,4) (7,4) for odd j
@@ -232,88 +247,156 @@ __device__ void build_frag4(const float *xs, int K, int E, uint2 *frag) {
         frag[o + 4] = lo;
     }
 }
+template <int NT>
+__device__ __forceinline__ void build_frag4(const float *xs, int K, int E, uint2 *frag) {
+    build_frag4_range(xs, K, E, frag, threadIdx.x, NT);
+}
+
+// One warp turns K fp32 values at src (global memory written by an earlier
+// launch) into an operand record (shared or global memory).  BITS selects the layout.
+template <int BITS>
+__device__ void warp_make_record(const float *src, int K, uint8_t *rec) {
+    const int lane = threadIdx.x & 31;
+    float *hdr = reinterpret_cast<float *>(rec + (BITS == 3 ? frag3_bytes(K) : frag4_bytes(K)));
+    float amax = 0.f;
+    for (int base = lane * 8; base < K; base += 256) {  // K is a multiple of 64, so a warp never splits a group
+        const float4 a = __ldcg(reinterpret_cast<const float4 *>(src + base));
+        const float4 b = __ldcg(reinterpret_cast<const float4 *>(src + base + 4));
+        float s = ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w));
+        amax = fmaxf(amax, fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))),
+                                 fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w)))));
+        // the eight lanes of a group are active together (K % 64 == 0)
+        const unsigned mask = __activemask();
+        s += __shfl_xor_sync(mask, s, 1);
+        s += __shfl_xor_sync(mask, s, 2);
+        s += __shfl_xor_sync(mask, s, 4);
+        if ((lane & 7) == 0) hdr[base >> 6] = s;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    int E = (int)(__float_as_uint(amax) >> 23) + 1;
+    E = E < 30 ? 30 : (E > 230 ? 230 : E);
+    if (lane == 0) hdr[K / 64] = __int_as_float(E);
+    __syncwarp();
+    // second pass: the scattered reads hit the lines the first pass just brought in
+    if (BITS == 3) build_frag3_range(src, K, E, reinterpret_cast<uint2 *>(rec), lane, 32);
+    else build_frag4_range(src, K, E, reinterpret_cast<uint2 *>(rec), lane, 32);
+    __syncwarp();
+}
 
 // ---- inner loops ---------------------------------------------------------
-// 3-bit.  NTILE MMA tiles share the B fragments of each unit.  Tile i has
-// fragment rows g -> packed row rowA[i], g + 8 -> rowB[i] (shared memory), with
-// scale rows sA[i], sB[i] (one u32 = the two groups of a unit).  Units u0,
-// u0 + ustep, ... are accumulated.  On return lane (g, t) holds in runA/runB
-// the raw sums of accumulator columns (token slot t>>1, term t&1).
-template <int NTILE>
-__device__ __forceinline__ void gemv3_units(const uint32_t *const (&rowA)[NTILE], const uint32_t *const (&rowB)[NTILE],
-                                            const uint32_t *const (&sA)[NTILE], const uint32_t *const (&sB)[NTILE],
-                                            int scale_dtype, const uint2 *frag0, const uint2 *frag1, int ntok, int units,
-                                            int u0, int ustep, float (&runA)[NTILE], float (&runB)[NTILE]) {
+// First MMA of a chain: C = 0 comes from the zero register, no accumulator initialisation needed.
+__device__ __forceinline__ void mma16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+// 3-bit tile (tile_layout.h) against up to two tokens.  tile: shared memory; frag0 / frag1 and the
+// headers h0 / h1 (group sums, E): operand records of the two tokens (any address space); zero: an
+// 8-byte zero entry in shared memory.  On return lane (g, t), t even, holds for token slot t>>1 the
+// dot products resA (fragment row g) and resB (row g + 8), bias included, over units u0, u0 + ustep, ...
+__device__ __forceinline__ void gemv3_tile(const uint8_t *tile, int units, int u0, int ustep, int scale_dtype, const uint2 *frag0,
+                                           const uint2 *frag1, const float *h0, const float *h1, const uint2 *zero, int ntok,
+                                           float &resA, float &resB) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int tokslot = g >> 2, term = (g >> 1) & 1;
     const bool bact = ((g & 1) == (t >> 1)) && tokslot < ntok;
-    const uint2 *fb = (tokslot ? frag1 : frag0) + term * 4 + t;
-#pragma unroll
-    for (int i = 0; i < NTILE; i++) runA[i] = runB[i] = 0.f;
+    // lanes whose B column is structurally zero read one shared zero entry (stride 0): no select, no moves
+    const uint2 *fb = bact ? (tokslot ? frag1 : frag0) + term * 4 + t : zero;
+    const int fstride = bact ? 8 : 0;
+    const float *h = (t >> 1) ? h1 : h0;  // token whose result this lane's accumulator columns hold
+    const uint8_t *sb = tile + units * 768;
+    float runA = 0.f, runB = 0.f, biasA = 0.f, biasB = 0.f;
     for (int u = u0; u < units; u += ustep) {
         uint2 b[9];
 #pragma unroll
-        for (int j = 0; j < 9; j++) b[j] = bact ? fb[(u * 9 + j) * 8] : make_uint2(0u, 0u);
+        for (int j = 0; j < 9; j++) b[j] = fb[(u * 9 + j) * fstride];
+        const uint2 *p = reinterpret_cast<const uint2 *>(tile + (size_t)(u * 32 + lane) * 24);
+        const uint2 q0 = p[0], q1 = p[1], q2 = p[2];
+        const uint4 s = *reinterpret_cast<const uint4 *>(sb + (size_t)(u * 8 + g) * 16);
+        const float2 xg = *reinterpret_cast<const float2 *>(h + 2 * u);
+        uint32_t ea[18], eb[18];
+        extract3(q0.x, q0.y, q1.x, ea);
+        extract3(q1.y, q2.x, q2.y, eb);
+        float acc[2][4];  // two independent accumulator chains
 #pragma unroll
-        for (int i = 0; i < NTILE; i++) {
-            const uint32_t *pa = rowA[i] + u * 12 + t * 3, *pb = rowB[i] + u * 12 + t * 3;
-            uint32_t ea[18], eb[18];
-            extract3(pa[0], pa[1], pa[2], ea);
-            extract3(pb[0], pb[1], pb[2], eb);
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int j = 0; j < 9; j++) finch_mma16816(acc, ea[2 * j], eb[2 * j], ea[2 * j + 1], eb[2 * j + 1], b[j].x, b[j].y);
-            float s0, s1;
-            finch_widen16x2(sA[i][u], scale_dtype, s0, s1);
-            runA[i] = fmaf(s0, acc[0], runA[i]);
-            runA[i] = fmaf(s1, acc[1], runA[i]);
-            finch_widen16x2(sB[i][u], scale_dtype, s0, s1);
-            runB[i] = fmaf(s0, acc[2], runB[i]);
-            runB[i] = fmaf(s1, acc[3], runB[i]);
+        for (int j = 0; j < 9; j++) {
+            if (j < 2) mma16816_z(acc[j], ea[2 * j], eb[2 * j], ea[2 * j + 1], eb[2 * j + 1], b[j].x, b[j].y);
+            else finch_mma16816(acc[j & 1], ea[2 * j], eb[2 * j], ea[2 * j + 1], eb[2 * j + 1], b[j].x, b[j].y);
         }
+        float s0, s1;
+        finch_widen16x2(s.x, scale_dtype, s0, s1);
+        runA = fmaf(s0, acc[0][0] + acc[1][0], runA);
+        runA = fmaf(s1, acc[0][1] + acc[1][1], runA);
+        finch_widen16x2(s.y, scale_dtype, s0, s1);
+        runB = fmaf(s0, acc[0][2] + acc[1][2], runB);
+        runB = fmaf(s1, acc[0][3] + acc[1][3], runB);
+        finch_widen16x2(s.z, scale_dtype, s0, s1);
+        biasA = fmaf(s0, xg.x, biasA);
+        biasA = fmaf(s1, xg.y, biasA);
+        finch_widen16x2(s.w, scale_dtype, s0, s1);
+        biasB = fmaf(s0, xg.x, biasB);
+        biasB = fmaf(s1, xg.y, biasB);
     }
+    // accumulator columns of lane t: token slot t>>1, term t&1 -> hi in even t, lo in odd t
+    const float fac = pow2_biased(__float_as_int(h[units * 2]) + 17);
+    const float oA = __shfl_xor_sync(0xffffffffu, runA, 1), oB = __shfl_xor_sync(0xffffffffu, runB, 1);
+    resA = fmaf(runA + oA * (1.0f / 2048.0f), fac, biasA);
+    resB = fmaf(runB + oB * (1.0f / 2048.0f), fac, biasB);
 }
 
-// hi (even t) + lo (odd t) columns of a 3-bit result -> value, valid in even-t lanes
-__device__ __forceinline__ float combine_hilo(float run, float fac) {
-    const float o = __shfl_xor_sync(0xffffffffu, run, 1);
-    return (run + o * (1.0f / 2048.0f)) * fac;
-}
-
-// 4-bit: one MMA tile (rows rowA / rowB), groups g0, g0 + gstep, ...; two
-// tokens per pass (columns 0..3 = token 0 hi/lo, token 1 hi/lo).  Lane (g, t)
-// with t < 2 returns the scaled sums (bias not included) of its rows for token t.
-__device__ __forceinline__ void gemv4_groups(const uint32_t *rowA, const uint32_t *rowB, const uint16_t *sA, const uint16_t *sB,
-                                             int scale_dtype, const uint2 *frag0, const uint2 *frag1, int ntok, int groups,
-                                             int g0, int gstep, float &resA, float &resB) {
+// 4-bit tile of the prepared shared expert (tile_layout.h) against up to two tokens (columns 0..3 =
+// token 0 hi/lo, token 1 hi/lo).  chunk: index of this lane's 16-byte operand chunk inside a group
+// (lane for a 16-row tile, (g&3)*4+t for a 4+4-row tile), per_group: chunks per group (32 / 16),
+// sidx / s_per_group: the same for the 8-byte scale/bias entries.  Lane (g, t) with t < 2 returns
+// the finished dot products of its two fragment rows for token t.
+__device__ __forceinline__ void gemv4_tile(const uint8_t *tile, int groups, int g0, int gstep, int chunk, int per_group, int sidx, int s_per_group,
+                                           int scale_dtype, const uint2 *frag0, const uint2 *frag1, const float *h0, const float *h1,
+                                           const uint2 *zero, int ntok, float &resA, float &resB) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int tok = g >> 1, term = g & 1;
-    const bool bact = tok < ntok;  // tok >= 2 never is
-    const uint2 *fb = ((tok & 1) ? frag1 : frag0) + term * 4 + t;
-    float runA = 0.f, runB = 0.f;
+    const bool bact = tok < ntok;  // ntok <= 2
+    const uint2 *fb = bact ? (tok ? frag1 : frag0) + term * 4 + t : zero;
+    const int fstride = bact ? 8 : 0;
+    const float *h = (t & 1) ? h1 : h0;
+    const uint8_t *sb = tile + (size_t)groups * per_group * 16;
+    float runA = 0.f, runB = 0.f, biasA = 0.f, biasB = 0.f;
     for (int gm = g0; gm < groups; gm += gstep) {
-        const uint2 wa = *reinterpret_cast<const uint2 *>(rowA + gm * 8 + t * 2);
-        const uint2 wb = *reinterpret_cast<const uint2 *>(rowB + gm * 8 + t * 2);
+        uint2 b[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) b[j] = fb[(gm * 4 + j) * fstride];
+        const uint4 w = *reinterpret_cast<const uint4 *>(tile + (size_t)(gm * per_group + chunk) * 16);
+        const uint2 s = *reinterpret_cast<const uint2 *>(sb + (size_t)(gm * s_per_group + sidx) * 8);
+        const float xg = h[gm];
         uint32_t ea[8], eb[8];
         {
             uint32_t x[4];
-            extract4(wa.x, x); ea[0] = x[0]; ea[1] = x[1]; ea[2] = x[2]; ea[3] = x[3];
-            extract4(wa.y, x); ea[4] = x[0]; ea[5] = x[1]; ea[6] = x[2]; ea[7] = x[3];
-            extract4(wb.x, x); eb[0] = x[0]; eb[1] = x[1]; eb[2] = x[2]; eb[3] = x[3];
-            extract4(wb.y, x); eb[4] = x[0]; eb[5] = x[1]; eb[6] = x[2]; eb[7] = x[3];
+            extract4(w.x, x); ea[0] = x[0]; ea[1] = x[1]; ea[2] = x[2]; ea[3] = x[3];
+            extract4(w.y, x); ea[4] = x[0]; ea[5] = x[1]; ea[6] = x[2]; ea[7] = x[3];
+            extract4(w.z, x); eb[0] = x[0]; eb[1] = x[1]; eb[2] = x[2]; eb[3] = x[3];
+            extract4(w.w, x); eb[4] = x[0]; eb[5] = x[1]; eb[6] = x[2]; eb[7] = x[3];
         }
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        float acc[2][4];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            const uint2 b = bact ? fb[(gm * 4 + j) * 8] : make_uint2(0u, 0u);
-            finch_mma16816(acc, ea[2 * j], eb[2 * j], ea[2 * j + 1], eb[2 * j + 1], b.x, b.y);
+            if (j < 2) mma16816_z(acc[j], ea[2 * j], eb[2 * j], ea[2 * j + 1], eb[2 * j + 1], b[j].x, b[j].y);
+            else finch_mma16816(acc[j & 1], ea[2 * j], eb[2 * j], ea[2 * j + 1], eb[2 * j + 1], b[j].x, b[j].y);
         }
         // accumulator columns 2t, 2t+1 = (token t, hi), (token t, lo)
-        runA = fmaf(finch_widen16(sA[gm], scale_dtype), acc[0] + acc[1] * (1.0f / 2048.0f), runA);
-        runB = fmaf(finch_widen16(sB[gm], scale_dtype), acc[2] + acc[3] * (1.0f / 2048.0f), runB);
+        float s0, s1, b0, b1;
+        finch_widen16x2(s.x, scale_dtype, s0, s1);  // scale of row A, of row B
+        finch_widen16x2(s.y, scale_dtype, b0, b1);  // bias of row A, of row B
+        runA = fmaf(s0, (acc[0][0] + acc[1][0]) + (acc[0][1] + acc[1][1]) * (1.0f / 2048.0f), runA);
+        runB = fmaf(s1, (acc[0][2] + acc[1][2]) + (acc[0][3] + acc[1][3]) * (1.0f / 2048.0f), runB);
+        biasA = fmaf(b0, xg, biasA);
+        biasB = fmaf(b1, xg, biasB);
     }
-    resA = runA;
-    resB = runB;
+    const float fac = pow2_biased(__float_as_int(h[groups]) + 17);
+    resA = fmaf(runA, fac, biasA);
+    resB = fmaf(runB, fac, biasB);
 }
 
 // ---- expert groups -------------------------------------------------------
@@ -324,541 +407,529 @@ __device__ __forceinline__ bool pair_ok(const MoeArgs &a, int p) {
     return a.slot_row[e] >= 0;
 }
 
-// Finds the pairs that share pair s's expert (no-prep path).  Returns false
-// when s is not the first pair of its group.  sm_pairs[0..m) lists the group's
-// pairs in ascending order.  Needs >= 64 threads.
-__device__ bool find_group(const MoeArgs &a, int s, int *sm_pairs, unsigned *sm_ballot, int &m) {
+// Builds the group table in shared memory.  Run by threads 0..nthreads-1
+// (nthreads >= 64) sharing named barrier `bar`.  Groups are numbered by their
+// first pair; pairs inside a group ascend.
+__device__ void build_groups(const MoeArgs &a, GroupTab *T, int *sm_ids, unsigned char *sm_first, int bar, int nthreads) {
     const int tid = threadIdx.x;
-    if (tid < 64) {
-        const bool same = tid < a.P && pair_ok(a, tid) && a.ids[tid] == a.ids[s];
-        const unsigned bal = __ballot_sync(0xffffffffu, same);
-        if ((tid & 31) == 0) sm_ballot[tid >> 5] = bal;
-    }
-    __syncthreads();
-    const unsigned long long mask = (unsigned long long)sm_ballot[0] | ((unsigned long long)sm_ballot[1] << 32);
-    if (!((mask >> s) & 1ull) || (__ffsll((long long)mask) - 1) != s) return false;
-    m = __popcll(mask);
-    if (tid < 64 && ((mask >> tid) & 1ull)) sm_pairs[__popcll(mask & ((1ull << tid) - 1ull))] = tid;
-    __syncthreads();
-    return true;
-}
-
-// Group of pair s from the prep table or by scanning the ids.  Uniform result.
-__device__ bool get_group(const MoeArgs &a, int s, int *sm_pairs, unsigned *sm_ballot, int &m, int &slot) {
-    if (a.use_prep) {
-        const int2 gi = __ldg(&a.grp[s]);
-        m = gi.x;
-        slot = gi.y;
-        if (m == 0) return false;
-        if ((int)threadIdx.x < m) sm_pairs[threadIdx.x] = a.grp_pairs[s * 64 + threadIdx.x];
-        __syncthreads();
-        return true;
-    }
-    if (!find_group(a, s, sm_pairs, sm_ballot, m)) return false;
-    slot = a.slot_row[a.ids[s]];
-    return true;
-}
-
-// sm_ids[p] = expert id of pair p, or -1 when the pair is skipped; returns the number of groups.
-__device__ int scan_pairs(const MoeArgs &a, int *sm_ids, unsigned *sm_ballot) {
-    const int tid = threadIdx.x;
-    if (tid < 64) sm_ids[tid] = (tid < a.P && pair_ok(a, tid)) ? a.ids[tid] : -1;
-    __syncthreads();
-    if (tid < 64) {
+    if (tid < MAXP) sm_ids[tid] = (tid < a.P && pair_ok(a, tid)) ? a.ids[tid] : -1;
+    bar_sync(bar, nthreads);
+    if (tid < MAXP) {
         bool first = sm_ids[tid] >= 0;
         for (int j = 0; j < tid && first; j++) first = sm_ids[j] != sm_ids[tid];
-        const unsigned bal = __ballot_sync(0xffffffffu, first);
-        if ((tid & 31) == 0) sm_ballot[tid >> 5] = bal;
+        sm_first[tid] = first;
     }
-    __syncthreads();
-    return __popc(sm_ballot[0]) + __popc(sm_ballot[1]);
+    bar_sync(bar, nthreads);
+    if (tid < MAXP) {
+        int rank = 0;
+        for (int j = 0; j < tid; j++) rank += sm_first[j];
+        if (sm_first[tid]) {
+            const int id = sm_ids[tid];
+            int m = 0;
+            for (int j = tid; j < a.P && m < MAXM; j++)
+                if (sm_ids[j] == id) T->pairs[rank][m++] = (unsigned char)j;
+            T->m[rank] = (unsigned char)m;
+            T->slot[rank] = a.slot_row[id];
+        }
+        if (tid == MAXP - 1) T->ng = rank + sm_first[tid];
+    }
+    bar_sync(bar, nthreads);
 }
 
-__host__ __device__ inline int sc_stride_words(int groups) { return groups / 2 + (((groups / 2) % 8 == 0) ? 4 : 0); }
-__host__ __device__ inline int frag3_entries(int K) { return (K / 128) * 72; }
-__host__ __device__ inline int frag4_entries(int K) { return (K / 64) * 32; }
+// ---- work distribution ---------------------------------------------------
+// Jobs (one tile against the tokens of its group) are laid out group-major:
+// job = gi * per_group + tile for the routed experts, then the shared-expert
+// tiles.  Every CTA takes one contiguous range, balanced by cost (a job of a
+// group with m pairs costs ceil(m/2) passes).  Contiguous ranges keep the
+// groups a CTA touches few: few act records to prepare, few counters to bump.
+__device__ __forceinline__ int npass_of(const GroupTab *tab, int gi) { return (tab->m[gi] + 1) >> 1; }
 
-struct SmemA {  // byte offsets inside kernel A's dynamic shared memory
-    int wg, wu, sc, xs, xg, frag, fstride, red, misc, total;
-};
-__host__ __device__ inline SmemA smem_a_layout(int hidden) {
-    const int groups = hidden / 64;
-    const int row3 = hidden * 3 / 8 + 16, row4 = hidden / 2 + 16;
-    const int w3 = A_ROWS * row3, w4 = S_ROWS * row4;
-    const int wbytes = w3 > w4 ? w3 : w4;
-    const int sc3 = 4 * A_ROWS * sc_stride_words(groups) * 4, sc4 = 4 * S_ROWS * groups * 2;
-    const int f3 = frag3_entries(hidden) * 8, f4 = frag4_entries(hidden) * 8;
-    SmemA L;
-    L.wg = 0;
-    L.wu = wbytes;
-    L.sc = 2 * wbytes;
-    L.xs = L.sc + (sc3 > sc4 ? sc3 : sc4);
-    L.xg = L.xs + hidden * 4;
-    L.frag = L.xg + 2 * 128 * 4;
-    L.fstride = (f3 > f4 ? f3 : f4) + FRAG_PAD;
-    L.red = L.frag + 2 * L.fstride;
-    L.misc = L.red + A_WARPS * 2 * 2 * 2 * 8 * 4;
-    L.total = L.misc + 512;
-    return L;
-}
-
-// group sums + E of one token / pair from global scratch into shared memory
-__device__ __forceinline__ void fetch_xg(const float *gXg, const int *gE, int idx, int groups, float *Xg, int *sm_E) {
-    for (int i = threadIdx.x; i < groups; i += blockDim.x) Xg[i] = __ldcg(gXg + (size_t)idx * 128 + i);
-    if (threadIdx.x == 0) *sm_E = __ldcg(gE + idx);
+__device__ int job_at(const GroupTab *tab, int per_group, int n_sh, int nps, long long target) {
+    long long base = 0;
+    const int ng = tab->ng;
+    for (int gi = 0; gi < ng; gi++) {
+        const int np = npass_of(tab, gi);
+        const long long gc = (long long)per_group * np;
+        if (target < base + gc) return gi * per_group + (int)((target - base + np - 1) / np);
+        base += gc;
+    }
+    if (n_sh > 0 && target < base + (long long)n_sh * nps) return ng * per_group + (int)((target - base + nps - 1) / nps);
+    return ng * per_group + n_sh;
 }
 
 // ============================ prep ========================================
-// grid: B + 1 CTAs of 256 threads.  CTA b < B: fragments of token b.  CTA B: groups.
-__global__ void __launch_bounds__(A_THREADS) moe_prep_kernel(const MoeArgs a) {
+// grid: B + 1 CTAs of 256 threads.  CTA b < B: operand records of token b.  CTA B: groups and ranges.
+__global__ void __launch_bounds__(256) moe_prep_kernel(const MoeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     float *xs = reinterpret_cast<float *>(smem);
-    float *Xg = xs + a.hidden;
-    float *warp_max = Xg + 128;
-    int *sm_E = reinterpret_cast<int *>(warp_max + 8);
-    int *sm_ids = sm_E + 4;
-    unsigned *sm_ballot = reinterpret_cast<unsigned *>(sm_ids + 64);
+    float *hdr = xs + a.hidden;              // [hidden/64 + 1]
+    float *warp_max = hdr + 144;
+    int *sm_ids = reinterpret_cast<int *>(warp_max + 8);
+    unsigned char *sm_first = reinterpret_cast<unsigned char *>(sm_ids + MAXP);
+    GroupTab *T = reinterpret_cast<GroupTab *>(sm_first + MAXP);
     const int b = blockIdx.x, tid = threadIdx.x, K = a.hidden;
     if (b < a.B) {
         const void *src = a.act_dtype == FINCH_BF16 ? (const void *)((const uint16_t *)a.h_post + (size_t)b * K)
                                                      : (const void *)((const float *)a.h_post + (size_t)b * K);
-        load_x<A_THREADS>(src, a.act_dtype, K, xs, Xg, warp_max, sm_E);
-        const int E = *sm_E;
-        build_frag3<A_THREADS>(xs, K, E, a.xfrag3 + (size_t)b * frag3_entries(K));
-        if (a.has_shared) build_frag4<A_THREADS>(xs, K, E, a.xfrag4 + (size_t)b * frag4_entries(K));
-        for (int i = tid; i < K / 64; i += A_THREADS) a.xXg[(size_t)b * 128 + i] = Xg[i];
-        if (tid == 0) a.xE[b] = E;
+        load_x<256>(src, a.act_dtype, K, xs, hdr, warp_max, 0);
+        const int E = __float_as_int(hdr[K / 64]);
+        uint8_t *rec = a.xrec3 + (size_t)b * rec3_bytes(K);
+        build_frag3<256>(xs, K, E, reinterpret_cast<uint2 *>(rec));
+        if (a.has_shared) build_frag4<256>(xs, K, E, reinterpret_cast<uint2 *>(a.xrec4 + (size_t)b * frag4_bytes(K)));
+        float *gh = reinterpret_cast<float *>(rec + frag3_bytes(K));
+        for (int i = tid; i <= K / 64; i += 256) gh[i] = hdr[i];
         return;
     }
-    const int ng = scan_pairs(a, sm_ids, sm_ballot);
-    if (tid == 0) *a.n_groups = ng;
-    if (tid < a.P) {
-        const int id = sm_ids[tid];
-        bool first = id >= 0;
-        for (int j = 0; j < tid && first; j++) first = sm_ids[j] != id;
-        int m = 0;
-        if (first)
-            for (int j = tid; j < a.P; j++)
-                if (sm_ids[j] == id) a.grp_pairs[tid * 64 + m++] = (uint8_t)j;
-        a.grp[tid] = make_int2(m, first ? a.slot_row[id] : -1);
+    build_groups(a, T, sm_ids, sm_first, 0, 256);
+    // job ranges of the two streaming kernels (thread i computes the start of CTA i)
+    const FinchTile L3 = finch_tile(a.hidden, a.inter);
+    const int nps = (a.B + 1) / 2;
+    const int n_sh_a = a.has_shared ? a.sh_inter / 4 : 0, n_sh_b = a.has_shared ? L3.nTB : 0;
+    long long Ca = (long long)n_sh_a * nps, Cb = (long long)n_sh_b * nps;
+    for (int gi = 0; gi < T->ng; gi++) {
+        Ca += (long long)L3.nTA * npass_of(T, gi);
+        Cb += (long long)L3.nTB * npass_of(T, gi);
+    }
+    for (int i = tid; i <= a.grid_a; i += 256) T->range_a[i] = job_at(T, L3.nTA, n_sh_a, nps, Ca * i / a.grid_a);
+    for (int i = tid; i <= a.grid_b; i += 256) T->range_b[i] = job_at(T, L3.nTB, n_sh_b, nps, Cb * i / a.grid_b);
+    __syncthreads();
+    const int *s = reinterpret_cast<const int *>(T);
+    int *d = reinterpret_cast<int *>(a.gtab);
+    for (int i = tid; i < (int)(sizeof(GroupTab) / 4); i += 256) d[i] = s[i];
+}
+
+// Re-tiles a shared expert from the reference tensor layout into FinchTile4 tiles (run once per
+// expert).  One thread per 16-byte operand chunk or 8-byte scale/bias entry.
+struct SharedSrc {
+    const uint32_t *gw, *uw, *dw;   // packed rows: in_dim / 8 words each
+    const uint16_t *gs, *gb, *us, *ub, *ds, *db;
+};
+__global__ void shared_retile_kernel(SharedSrc S, int hidden, int inter, uint8_t *out) {
+    const FinchTile4 T = finch_tile4(hidden, inter);
+    const size_t nA = (size_t)T.nTA * T.groupsA * 20, nB = (size_t)T.nTB * T.groupsD * 40;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nA + nB; i += (size_t)gridDim.x * blockDim.x) {
+        if (i < nA) {
+            const int ta = (int)(i / (T.groupsA * 20)), r = (int)(i % (T.groupsA * 20)), gm = r / 20, e = r % 20;
+            uint8_t *tile = out + (size_t)ta * T.tileA;
+            if (e < 16) {  // operand chunk of lane (g4, t)
+                const int g4 = e >> 2, t = e & 3;
+                const size_t row = (size_t)4 * ta + g4, wpr = hidden / 8;
+                const uint32_t *ga = S.gw + row * wpr + gm * 8 + 2 * t, *ua = S.uw + row * wpr + gm * 8 + 2 * t;
+                *reinterpret_cast<uint4 *>(tile + (size_t)(gm * 16 + e) * 16) = make_uint4(ga[0], ga[1], ua[0], ua[1]);
+            } else {
+                const int g4 = e - 16;
+                const size_t o = ((size_t)4 * ta + g4) * T.groupsA + gm;
+                *reinterpret_cast<uint2 *>(tile + T.sbA + (size_t)(gm * 4 + g4) * 8) =
+                    make_uint2((uint32_t)S.gs[o] | ((uint32_t)S.us[o] << 16), (uint32_t)S.gb[o] | ((uint32_t)S.ub[o] << 16));
+            }
+        } else {
+            const size_t k = i - nA;
+            const int tb = (int)(k / (T.groupsD * 40)), r = (int)(k % (T.groupsD * 40)), gm = r / 40, e = r % 40;
+            uint8_t *tile = out + T.b_base + (size_t)tb * T.tileB;
+            if (e < 32) {
+                const int g = e >> 2, t = e & 3;
+                const size_t r0 = (size_t)16 * tb + g, r1 = r0 + 8, wpr = inter / 8;
+                const uint32_t *pa = S.dw + r0 * wpr + gm * 8 + 2 * t, *pb = S.dw + r1 * wpr + gm * 8 + 2 * t;
+                *reinterpret_cast<uint4 *>(tile + (size_t)(gm * 32 + e) * 16) = make_uint4(pa[0], pa[1], pb[0], pb[1]);
+            } else {
+                const int g = e - 32;
+                const size_t o0 = ((size_t)16 * tb + g) * T.groupsD + gm, o1 = o0 + (size_t)8 * T.groupsD;
+                *reinterpret_cast<uint2 *>(tile + T.sbB + (size_t)(gm * 8 + g) * 8) =
+                    make_uint2((uint32_t)S.ds[o0] | ((uint32_t)S.ds[o1] << 16), (uint32_t)S.db[o0] | ((uint32_t)S.db[o1] << 16));
+            }
+        }
     }
 }
 
 // ============================ kernel A ====================================
-// grid: x = row chunk (inter / 16), y = pair slot 0..P-1, then two rows of
-// CTAs for the shared expert's gate/up (8 + 8 rows each).
-__global__ void __launch_bounds__(A_THREADS) moe_gateup_kernel(const MoeArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const SmemA L = smem_a_layout(a.hidden);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
-    float *xs = reinterpret_cast<float *>(smem + L.xs);
-    float *Xg = reinterpret_cast<float *>(smem + L.xg);
-    uint2 *frag0 = reinterpret_cast<uint2 *>(smem + L.frag);
-    uint2 *frag1 = reinterpret_cast<uint2 *>(smem + L.frag + L.fstride);
-    float *red = reinterpret_cast<float *>(smem + L.red);
-    int *sm_pairs = reinterpret_cast<int *>(smem + L.misc);                    // [64]
-    unsigned *sm_ballot = reinterpret_cast<unsigned *>(smem + L.misc + 256);   // [2]
-    float *warp_max = reinterpret_cast<float *>(smem + L.misc + 272);          // [8]
-    int *sm_E = reinterpret_cast<int *>(smem + L.misc + 304);                  // [2]
-    int *sm_last = reinterpret_cast<int *>(smem + L.misc + 312);
-    uint64_t *mbar = reinterpret_cast<uint64_t *>(smem + L.misc + 320);
-    const int s = blockIdx.y, K = a.hidden, groups = K / 64;
-
-    if (s < a.P) {
-        // ---------------- routed expert, 3-bit ----------------
-        int m = 0, slot = -1;
-        if (!get_group(a, s, sm_pairs, sm_ballot, m, slot)) return;
-        const int r0 = blockIdx.x * A_ROWS;
-        const uint8_t *blk = a.pool_base + (size_t)slot * a.slot_bytes;
-        const int rowb = K * 3 / 8, rowp = rowb + 16;  // global / padded shared row pitch
-        const unsigned fbytes = (unsigned)frag3_entries(K) * 8u;
-        if (tid == 0) finch_mbar_init(mbar, 1);
-        __syncthreads();
-        if (warp == 0) {
-            if (lane == 0) finch_mbar_expect_tx(mbar, 2u * A_ROWS * rowb + (a.use_prep ? (unsigned)min(2, m) * fbytes : 0u));
-            __syncwarp();
-            const int r = lane & 15;
-            const uint8_t *src = blk + (lane < 16 ? a.gate_w : a.up_w) + (size_t)(r0 + r) * rowb;
-            finch_bulk_g2s(smem + (lane < 16 ? L.wg : L.wu) + r * rowp, src, rowb, mbar);
-            if (a.use_prep && lane < min(2, m))
-                finch_bulk_g2s(lane ? frag1 : frag0, a.xfrag3 + (size_t)(sm_pairs[lane] / a.K) * frag3_entries(K), fbytes, mbar);
-        }
-        // scales and biases: plain loads into padded rows
-        const int scw = sc_stride_words(groups), rw = groups / 2;
-        uint32_t *sc = reinterpret_cast<uint32_t *>(smem + L.sc);
-        for (int i = tid; i < 4 * A_ROWS * rw; i += A_THREADS) {
-            const int arr = i / (A_ROWS * rw), rem = i - arr * (A_ROWS * rw), r = rem / rw, c = rem - r * rw;
-            const size_t off = arr == 0 ? a.gate_s : arr == 1 ? a.gate_b : arr == 2 ? a.up_s : a.up_b;
-            sc[(arr * A_ROWS + r) * scw + c] = __ldg(reinterpret_cast<const uint32_t *>(blk + off + (size_t)(r0 + r) * groups * 2) + c);
-        }
-        const int npass = (m + 1) / 2;
-        for (int ps = 0; ps < npass; ps++) {
-            const int ntok = min(2, m - 2 * ps);
-            if (a.use_prep) {
-                if (ps > 0 && warp == 0) {  // fragments of this pass's tokens (the previous pass is done with the buffers)
-                    if (lane == 0) finch_mbar_expect_tx(mbar, (unsigned)ntok * fbytes);
-                    __syncwarp();
-                    if (lane < ntok)
-                        finch_bulk_g2s(lane ? frag1 : frag0, a.xfrag3 + (size_t)(sm_pairs[2 * ps + lane] / a.K) * frag3_entries(K),
-                                       fbytes, mbar);
-                }
-                for (int ts = 0; ts < ntok; ts++) fetch_xg(a.xXg, a.xE, sm_pairs[2 * ps + ts] / a.K, groups, Xg + ts * 128, sm_E + ts);
-                __syncthreads();
-            } else {
-                for (int ts = 0; ts < ntok; ts++) {
-                    const int tok = sm_pairs[2 * ps + ts] / a.K;
-                    const void *src = a.act_dtype == FINCH_BF16 ? (const void *)((const uint16_t *)a.h_post + (size_t)tok * K)
-                                                                 : (const void *)((const float *)a.h_post + (size_t)tok * K);
-                    load_x<A_THREADS>(src, a.act_dtype, K, xs, Xg + ts * 128, warp_max, sm_E + ts);
-                    build_frag3<A_THREADS>(xs, K, sm_E[ts], ts ? frag1 : frag0);
-                    __syncthreads();
-                }
-            }
-            if (a.use_prep || ps == 0) {
-                if (!finch_mbar_wait(mbar, ps & 1)) {
-                    if (tid == 0) atomicExch(a.status, FINCH_E_TIMEOUT);
-                    return;
-                }
-            }
-            const uint32_t *rA[2], *rB[2], *sA[2], *sB[2];
-#pragma unroll
-            for (int tile = 0; tile < 2; tile++) {
-                const int row = tile * 8 + g;
-                rA[tile] = reinterpret_cast<const uint32_t *>(smem + L.wg + row * rowp);
-                rB[tile] = reinterpret_cast<const uint32_t *>(smem + L.wu + row * rowp);
-                sA[tile] = sc + (0 * A_ROWS + row) * scw;
-                sB[tile] = sc + (2 * A_ROWS + row) * scw;
-            }
-            float runG[2], runU[2];
-            gemv3_units<2>(rA, rB, sA, sB, a.scale_dtype, frag0, frag1, ntok, K / 128, warp, A_WARPS, runG, runU);
-            const float fac = pow2_biased(sm_E[t >> 1] + 17);
-#pragma unroll
-            for (int tile = 0; tile < 2; tile++) {
-                const float vg = combine_hilo(runG[tile], fac), vu = combine_hilo(runU[tile], fac);
-                if ((t & 1) == 0) {
-                    float *o = red + (((warp * 2 + tile) * 2 + (t >> 1)) * 2) * 8 + g;
-                    o[0] = vg;
-                    o[8] = vu;
-                }
-            }
-            __syncthreads();
-            if (tid < 64) {
-                // thread = (tile, token slot, row g, gate|up): cross-warp sum in fixed order + bias . group sums
-                const int up = tid & 1, gg = (tid >> 1) & 7, ts = (tid >> 4) & 1, tile = tid >> 5;
-                float v = 0.f;
-#pragma unroll
-                for (int w = 0; w < A_WARPS; w++) v += red[(((w * 2 + tile) * 2 + ts) * 2 + up) * 8 + gg];
-                const uint32_t *brow = sc + ((up ? 3 : 1) * A_ROWS + tile * 8 + gg) * scw;
-                const float *xg = Xg + ts * 128;
-                for (int c = 0; c < rw; c++) {
-                    float b0, b1;
-                    finch_widen16x2(brow[c], a.scale_dtype, b0, b1);
-                    v = fmaf(b0, xg[2 * c], v);
-                    v = fmaf(b1, xg[2 * c + 1], v);
-                }
-                const float other = __shfl_xor_sync(0xffffffffu, v, 1);  // gate <-> up of the same row
-                if (!up && ts < ntok) {
-                    const int pair = sm_pairs[2 * ps + ts];
-                    a.act[(size_t)pair * a.inter + r0 + tile * 8 + gg] = (v / (1.0f + expf(-v))) * other;
-                }
-            }
-            __syncthreads();
-        }
-        // ---- the last CTA of the group turns the finished activations into fragments for kernel B ----
-        __threadfence();
-        __syncthreads();
-        if (tid == 0) *sm_last = atomicAdd(&a.cnt_a[s], 1u) == (unsigned)(gridDim.x - 1);
-        __syncthreads();
-        if (!*sm_last) return;
-        __threadfence();
-        for (int i = 0; i < m; i++) {
-            const int pair = sm_pairs[i];
-            load_x<A_THREADS>(a.act + (size_t)pair * a.inter, FINCH_F32, a.inter, xs, Xg, warp_max, sm_E);
-            build_frag3<A_THREADS>(xs, a.inter, *sm_E, a.afrag3 + (size_t)pair * frag3_entries(a.inter));
-            for (int c = tid; c < a.inter / 64; c += A_THREADS) a.aXg[(size_t)pair * 128 + c] = Xg[c];
-            if (tid == 0) a.aE[pair] = *sm_E;
-            __syncthreads();
-        }
-        if (tid == 0) a.cnt_a[s] = 0u;
-        return;
-    }
-
-    // ---------------- shared expert gate/up, 4-bit ----------------
-    const int I = a.sh_inter;
-    const int r0 = ((s - a.P) * gridDim.x + blockIdx.x) * S_ROWS;
-    if (r0 >= I) return;
-    const int n_ctas = I / S_ROWS;
-    const int rowb = K / 2, rowp = rowb + 16;
-    const unsigned fbytes = (unsigned)frag4_entries(K) * 8u;
-    if (tid == 0) finch_mbar_init(mbar, 1);
-    __syncthreads();
-    if (warp == 0) {
-        if (lane == 0) finch_mbar_expect_tx(mbar, 2u * S_ROWS * rowb + (a.use_prep ? (unsigned)min(2, a.B) * fbytes : 0u));
-        __syncwarp();
-        if (lane < 2 * S_ROWS) {
-            const int r = lane & (S_ROWS - 1);
-            const uint8_t *src = (lane < S_ROWS ? a.sh_gate.W : a.sh_up.W) + (size_t)(r0 + r) * rowb;
-            finch_bulk_g2s(smem + (lane < S_ROWS ? L.wg : L.wu) + r * rowp, src, rowb, mbar);
-        }
-        if (a.use_prep && lane < min(2, a.B)) finch_bulk_g2s(lane ? frag1 : frag0, a.xfrag4 + (size_t)lane * frag4_entries(K), fbytes, mbar);
-    }
-    uint16_t *sc = reinterpret_cast<uint16_t *>(smem + L.sc);  // [4][S_ROWS][groups]: gate S, gate B, up S, up B
-    for (int i = tid; i < 4 * S_ROWS * groups; i += A_THREADS) {
-        const int arr = i / (S_ROWS * groups), rem = i - arr * (S_ROWS * groups);
-        const uint16_t *src = arr == 0 ? a.sh_gate.S : arr == 1 ? a.sh_gate.B : arr == 2 ? a.sh_up.S : a.sh_up.B;
-        sc[i] = src[(size_t)r0 * groups + rem];
-    }
-    const int npass = (a.B + 1) / 2;
-    for (int ps = 0; ps < npass; ps++) {
-        const int ntok = min(2, a.B - 2 * ps);
-        if (a.use_prep) {
-            if (ps > 0 && warp == 0) {
-                if (lane == 0) finch_mbar_expect_tx(mbar, (unsigned)ntok * fbytes);
-                __syncwarp();
-                if (lane < ntok) finch_bulk_g2s(lane ? frag1 : frag0, a.xfrag4 + (size_t)(2 * ps + lane) * frag4_entries(K), fbytes, mbar);
-            }
-            for (int ts = 0; ts < ntok; ts++) fetch_xg(a.xXg, a.xE, 2 * ps + ts, groups, Xg + ts * 128, sm_E + ts);
-            __syncthreads();
-        } else {
-            for (int ts = 0; ts < ntok; ts++) {
-                const int tok = 2 * ps + ts;
-                const void *src = a.act_dtype == FINCH_BF16 ? (const void *)((const uint16_t *)a.h_post + (size_t)tok * K)
-                                                             : (const void *)((const float *)a.h_post + (size_t)tok * K);
-                load_x<A_THREADS>(src, a.act_dtype, K, xs, Xg + ts * 128, warp_max, sm_E + ts);
-                build_frag4<A_THREADS>(xs, K, sm_E[ts], ts ? frag1 : frag0);
-                __syncthreads();
-            }
-        }
-        if (a.use_prep || ps == 0) {
-            if (!finch_mbar_wait(mbar, ps & 1)) {
-                if (tid == 0) atomicExch(a.status, FINCH_E_TIMEOUT);
-                return;
-            }
-        }
-        float rg, ru;
-        gemv4_groups(reinterpret_cast<const uint32_t *>(smem + L.wg + g * rowp), reinterpret_cast<const uint32_t *>(smem + L.wu + g * rowp),
-                     sc + (0 * S_ROWS + g) * groups, sc + (2 * S_ROWS + g) * groups, a.sh_scale_dtype, frag0, frag1, ntok, groups, warp,
-                     A_WARPS, rg, ru);
-        if (t < 2) {
-            const float fac = pow2_biased(sm_E[t] + 17);
-            red[((warp * 2 + t) * 2 + 0) * 8 + g] = rg * fac;
-            red[((warp * 2 + t) * 2 + 1) * 8 + g] = ru * fac;
-        }
-        __syncthreads();
-        if (tid < 32) {
-            const int up = tid & 1, gg = (tid >> 1) & 7, ts = tid >> 4;
-            float v = 0.f;
-#pragma unroll
-            for (int w = 0; w < A_WARPS; w++) v += red[((w * 2 + ts) * 2 + up) * 8 + gg];
-            const uint16_t *brow = sc + ((up ? 3 : 1) * S_ROWS + gg) * groups;
-            const float *xg = Xg + ts * 128;
-            for (int c = 0; c < groups; c++) v = fmaf(finch_widen16(brow[c], a.sh_scale_dtype), xg[c], v);
-            const float other = __shfl_xor_sync(0xffffffffu, v, 1);
-            if (!up && ts < ntok) a.shared_act[(size_t)(2 * ps + ts) * I + r0 + gg] = (v / (1.0f + expf(-v))) * other;
-        }
-        __syncthreads();
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) *sm_last = atomicAdd(&a.cnt_a[a.P], 1u) == (unsigned)(n_ctas - 1);
-    __syncthreads();
-    if (!*sm_last) return;
-    __threadfence();
-    for (int b = 0; b < a.B; b++) {
-        load_x<A_THREADS>(a.shared_act + (size_t)b * I, FINCH_F32, I, xs, Xg, warp_max, sm_E);
-        build_frag4<A_THREADS>(xs, I, *sm_E, a.sfrag4 + (size_t)b * frag4_entries(I));
-        for (int c = tid; c < I / 64; c += A_THREADS) a.sXg[(size_t)b * 128 + c] = Xg[c];
-        if (tid == 0) a.sE[b] = *sm_E;
-        __syncthreads();
-    }
-    if (tid == 0) a.cnt_a[a.P] = 0u;
-}
-
-struct SmemB {
-    int w, sc, xg, frag, fstride, misc, total;
+__host__ __device__ inline int up128(int x) { return (x + 127) & ~127; }
+struct SmemA {
+    int stage, stg, rec, rx3, rec4, f4s, n4, red, tab, bar, total;
 };
-__host__ __device__ inline SmemB smem_b_layout(int inter, int sh_inter) {
-    const int row3 = inter * 3 / 8 + 16, row4 = sh_inter / 2 + 16;
-    const int wb = B_ROWS * (row3 > row4 ? row3 : row4);
-    const int sc3 = 2 * B_ROWS * sc_stride_words(inter / 64) * 4, sc4 = 2 * B_ROWS * (sh_inter / 64) * 2;
-    const int f3 = frag3_entries(inter) * 8, f4 = frag4_entries(sh_inter) * 8;
-    SmemB L;
-    L.w = 0;
-    L.sc = wb;
-    L.xg = L.sc + (sc3 > sc4 ? sc3 : sc4);
-    L.frag = L.xg + 2 * 128 * 4;
-    L.fstride = (f3 > f4 ? f3 : f4) + FRAG_PAD;
-    L.misc = L.frag + 2 * L.fstride;
-    L.total = L.misc + 1024;
+__host__ __device__ inline SmemA smem_a_layout(int hidden, int inter, int sh_inter, int B, int has_shared, int stages) {
+    const FinchTile T = finch_tile(hidden, inter);
+    const FinchTile4 T4 = finch_tile4(hidden, sh_inter);
+    SmemA L;
+    L.stage = 0;
+    L.stg = up128(has_shared && T4.tileA > T.tileA ? T4.tileA : T.tileA);
+    L.rec = L.stage + stages * L.stg;         // operand records of all tokens (3-bit layout)
+    L.rx3 = rec3_bytes(hidden);
+    L.rec4 = up128(L.rec + B * L.rx3);        // 4-bit-layout fragments of the first n4 tokens (the rest stay in global memory)
+    L.f4s = frag4_bytes(hidden) + 64;
+    L.n4 = has_shared ? (B < 2 ? B : 2) : 0;
+    L.red = up128(L.rec4 + L.n4 * L.f4s);
+    L.tab = L.red + NTEAM_A * 2 * TEAM_A * 32 * 4;
+    L.bar = up128(L.tab + (int)sizeof(GroupTab));
+    L.total = L.bar + 2 * 32 * 8 + 16 + 16;
     return L;
 }
 
-// ============================ kernel B ====================================
-// grid: x = row chunk of 64 down rows, y = pair slot (0..P-1 routed; P = shared / finisher)
-__global__ void __launch_bounds__(B_THREADS) moe_down_combine_kernel(const MoeArgs a) {
+// grid: one CTA per SM (persistent); block: NTEAM_A teams of TEAM_A consumer warps + 1 producer warp.
+// A team takes whole tiles; its warps split the K dimension and one of them adds the partial sums.
+__global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const SmemB L = smem_b_layout(a.inter, a.sh_inter);
+    const long long tk0 = clock64();
+    const int S = a.stages_a;
+    const SmemA L = smem_a_layout(a.hidden, a.inter, a.sh_inter, a.B, a.has_shared, S);
+    const FinchTile T = finch_tile(a.hidden, a.inter);
+    const FinchTile4 T4 = finch_tile4(a.hidden, a.sh_inter);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
-    float *Xg = reinterpret_cast<float *>(smem + L.xg);
-    uint2 *frag0 = reinterpret_cast<uint2 *>(smem + L.frag);
-    uint2 *frag1 = reinterpret_cast<uint2 *>(smem + L.frag + L.fstride);
-    int *sm_pairs = reinterpret_cast<int *>(smem + L.misc);                   // [64]
-    int *sm_ids = reinterpret_cast<int *>(smem + L.misc + 256);               // [64]
-    unsigned *sm_ballot = reinterpret_cast<unsigned *>(smem + L.misc + 512);  // [2]
-    int *sm_E = reinterpret_cast<int *>(smem + L.misc + 528);                 // [2]
-    int *sm_last = reinterpret_cast<int *>(smem + L.misc + 540);
-    uint64_t *mbar = reinterpret_cast<uint64_t *>(smem + L.misc + 576);
-    const int s = blockIdx.y, r0 = blockIdx.x * B_ROWS;
-    const int ra = warp * 16 + g, rb = ra + 8;
+    GroupTab *tab = reinterpret_cast<GroupTab *>(smem + L.tab);
+    float *red = reinterpret_cast<float *>(smem + L.red);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar), *empty = full + 32;
+    const uint2 *zero8 = reinterpret_cast<const uint2 *>(empty + 32);
+    uint64_t *xbar = empty + 34;
+    const int K = a.hidden, groups = K / 64, I = a.sh_inter;
+    const int f4b = frag4_bytes(K);
 
-    if (s < a.P) {
-        int m = 0, slot = -1;
-        if (!get_group(a, s, sm_pairs, sm_ballot, m, slot)) return;
-        const int K = a.inter, groups = K / 64;
-        const uint8_t *blk = a.pool_base + (size_t)slot * a.slot_bytes;
-        const int rowb = K * 3 / 8, rowp = rowb + 16;
-        const unsigned fbytes = (unsigned)frag3_entries(K) * 8u;
-        if (tid == 0) finch_mbar_init(mbar, 1);
-        __syncthreads();
-        if (warp == 0) {
-            if (lane == 0) finch_mbar_expect_tx(mbar, (unsigned)B_ROWS * rowb + (unsigned)min(2, m) * fbytes);
-            __syncwarp();
-            for (int r = lane; r < B_ROWS; r += 32)
-                finch_bulk_g2s(smem + L.w + r * rowp, blk + a.down_w + (size_t)(r0 + r) * rowb, rowb, mbar);
-            if (lane < min(2, m)) finch_bulk_g2s(lane ? frag1 : frag0, a.afrag3 + (size_t)sm_pairs[lane] * frag3_entries(K), fbytes, mbar);
+    {
+        const int *s = reinterpret_cast<const int *>(a.gtab);
+        int *d = reinterpret_cast<int *>(tab);
+        for (int i = tid; i < (int)(sizeof(GroupTab) / 4); i += NT_A) d[i] = __ldcg(s + i);
+    }
+    if (tid == 0) {
+        empty[32] = 0ull;
+        for (int s = 0; s < S; s++) {
+            finch_mbar_init(full + s, 1);
+            finch_mbar_init(empty + s, TEAM_A);
         }
-        const int scw = sc_stride_words(groups), rw = groups / 2;
-        uint32_t *sc = reinterpret_cast<uint32_t *>(smem + L.sc);
-        for (int i = tid; i < 2 * B_ROWS * rw; i += B_THREADS) {
-            const int arr = i / (B_ROWS * rw), rem = i - arr * (B_ROWS * rw), r = rem / rw, c = rem - r * rw;
-            sc[(arr * B_ROWS + r) * scw + c] =
-                __ldg(reinterpret_cast<const uint32_t *>(blk + (arr ? a.down_b : a.down_s) + (size_t)(r0 + r) * groups * 2) + c);
+        finch_mbar_init(xbar, 1);
+        // operand records of the tokens: one bulk copy each, ready long before the first tile is
+        finch_mbar_expect_tx(xbar, (unsigned)(a.B * L.rx3 + L.n4 * f4b));
+        for (int b = 0; b < a.B; b++) finch_bulk_g2s(smem + L.rec + b * L.rx3, a.xrec3 + (size_t)b * L.rx3, L.rx3, xbar);
+        for (int b = 0; b < L.n4; b++) finch_bulk_g2s(smem + L.rec4 + b * L.f4s, a.xrec4 + (size_t)b * f4b, f4b, xbar);
+    }
+    __syncthreads();
+    const long long tk1 = clock64();
+    const int n_routed = tab->ng * T.nTA;
+    const int job0 = tab->range_a[blockIdx.x], job1 = tab->range_a[blockIdx.x + 1];
+
+    if (warp == CW_A) {
+        // ---------------- producer warp: one bulk copy per job ----------------
+        if (lane == 0) {
+            for (int job = job0, it = 0; job < job1; ++job, ++it) {
+                const int st = it % S, use = it / S;
+                if (use > 0 && !finch_mbar_wait(empty + st, (use - 1) & 1)) {
+                    atomicExch(a.status, FINCH_E_TIMEOUT);
+                    return;
+                }
+                uint8_t *dst = smem + L.stage + st * L.stg;
+                if (job < n_routed) {
+                    const int gi = job / T.nTA, ta = job - gi * T.nTA;
+                    finch_mbar_expect_tx(full + st, (unsigned)T.tileA);
+                    finch_bulk_g2s(dst, a.pool_base + (size_t)tab->slot[gi] * a.slot_bytes + (size_t)ta * T.tileA, T.tileA, full + st);
+                } else {
+                    finch_mbar_expect_tx(full + st, (unsigned)T4.tileA);
+                    finch_bulk_g2s(dst, a.sh_tiles + (size_t)(job - n_routed) * T4.tileA, T4.tileA, full + st);
+                }
+            }
         }
-        const int npass = (m + 1) / 2;
+        return;
+    }
+
+    // ---------------- consumer teams: team q takes the CTA's jobs q, q + NTEAM_A, ... ----------------
+    const int team = warp / TEAM_A, kw = warp % TEAM_A, bar_id = 1 + team;
+    float *tred = red + team * (2 * TEAM_A * 32);
+    if (!finch_mbar_wait(xbar, 0)) {
+        if (lane == 0) atomicExch(a.status, FINCH_E_TIMEOUT);
+        return;
+    }
+    const long long tk2 = clock64();
+    long long wait_acc = 0;
+    int njobs = 0, rbuf = 0;
+    for (int it = team; job0 + it < job1; it += NTEAM_A, ++njobs) {
+        const int job = job0 + it, st = it % S, use = it / S;
+        const long long w0 = clock64();
+        if (!finch_mbar_wait(full + st, use & 1)) {
+            if (lane == 0) atomicExch(a.status, FINCH_E_TIMEOUT);
+            return;
+        }
+        wait_acc += clock64() - w0;
+        const uint8_t *tile = smem + L.stage + st * L.stg;
+        const bool routed = job < n_routed;
+        const int gi = routed ? job / T.nTA : 0, ta = routed ? job - gi * T.nTA : job - n_routed;
+        const int m = routed ? tab->m[gi] : a.B, npass = (m + 1) / 2;
         for (int ps = 0; ps < npass; ps++) {
             const int ntok = min(2, m - 2 * ps);
-            if (ps > 0 && warp == 0) {
-                if (lane == 0) finch_mbar_expect_tx(mbar, (unsigned)ntok * fbytes);
-                __syncwarp();
-                if (lane < ntok) finch_bulk_g2s(lane ? frag1 : frag0, a.afrag3 + (size_t)sm_pairs[2 * ps + lane] * frag3_entries(K), fbytes, mbar);
+            int pair0 = 0, pair1 = 0;
+            float vA, vB;
+            if (routed) {
+                pair0 = tab->pairs[gi][2 * ps];
+                pair1 = tab->pairs[gi][2 * ps + (ntok > 1)];
+                const uint8_t *rec0 = smem + L.rec + (pair0 / a.K) * L.rx3, *rec1 = smem + L.rec + (pair1 / a.K) * L.rx3;
+                gemv3_tile(tile, T.unitsA, kw, TEAM_A, a.scale_dtype, reinterpret_cast<const uint2 *>(rec0), reinterpret_cast<const uint2 *>(rec1),
+                           reinterpret_cast<const float *>(rec0 + frag3_bytes(K)), reinterpret_cast<const float *>(rec1 + frag3_bytes(K)),
+                           zero8, ntok, vA, vB);
+            } else {
+                // shared expert gate/up tile: 4 gate rows + 4 up rows, every token, two per pass
+                const int tok0 = 2 * ps, tok1 = 2 * ps + (ntok > 1);
+                const uint2 *f0 = tok0 < L.n4 ? reinterpret_cast<const uint2 *>(smem + L.rec4 + tok0 * L.f4s)
+                                              : reinterpret_cast<const uint2 *>(a.xrec4 + (size_t)tok0 * f4b);
+                const uint2 *f1 = tok1 < L.n4 ? reinterpret_cast<const uint2 *>(smem + L.rec4 + tok1 * L.f4s)
+                                              : reinterpret_cast<const uint2 *>(a.xrec4 + (size_t)tok1 * f4b);
+                gemv4_tile(tile, groups, kw, TEAM_A, (g & 3) * 4 + t, 16, g & 3, 4, a.sh_scale_dtype, f0, f1,
+                           reinterpret_cast<const float *>(smem + L.rec + tok0 * L.rx3 + frag3_bytes(K)),
+                           reinterpret_cast<const float *>(smem + L.rec + tok1 * L.rx3 + frag3_bytes(K)), zero8, ntok, vA, vB);
             }
-            for (int ts = 0; ts < ntok; ts++) fetch_xg(a.aXg, a.aE, sm_pairs[2 * ps + ts], groups, Xg + ts * 128, sm_E + ts);
-            __syncthreads();
-            if (!finch_mbar_wait(mbar, ps & 1)) {
-                if (tid == 0) atomicExch(a.status, FINCH_E_TIMEOUT);
-                return;
-            }
-            const uint32_t *rA[1] = {reinterpret_cast<const uint32_t *>(smem + L.w + ra * rowp)};
-            const uint32_t *rB[1] = {reinterpret_cast<const uint32_t *>(smem + L.w + rb * rowp)};
-            const uint32_t *sA[1] = {sc + ra * scw}, *sB[1] = {sc + rb * scw};
-            float runA[1], runB[1];
-            gemv3_units<1>(rA, rB, sA, sB, a.scale_dtype, frag0, frag1, ntok, K / 128, 0, 1, runA, runB);
-            const float fac = pow2_biased(sm_E[t >> 1] + 17);
-            float va = combine_hilo(runA[0], fac), vb = combine_hilo(runB[0], fac);
-            if ((t & 1) == 0 && (t >> 1) < ntok) {
-                const float *xg = Xg + (t >> 1) * 128;
-                const uint32_t *ba = sc + (B_ROWS + ra) * scw, *bb = sc + (B_ROWS + rb) * scw;
-                for (int c = 0; c < rw; c++) {
-                    float b0, b1;
-                    finch_widen16x2(ba[c], a.scale_dtype, b0, b1);
-                    va = fmaf(b0, xg[2 * c], va);
-                    va = fmaf(b1, xg[2 * c + 1], va);
-                    finch_widen16x2(bb[c], a.scale_dtype, b0, b1);
-                    vb = fmaf(b0, xg[2 * c], vb);
-                    vb = fmaf(b1, xg[2 * c + 1], vb);
+            // partial sums of this warp's share of K -> team buffer [warp][token slot][row g][A|B]
+            float *mine = tred + (rbuf * TEAM_A + kw) * 32;
+            if (routed) {
+                if ((t & 1) == 0) {
+                    mine[(t >> 1) * 16 + g * 2] = vA;
+                    mine[(t >> 1) * 16 + g * 2 + 1] = vB;
                 }
-                const int pair = sm_pairs[2 * ps + (t >> 1)];
-                a.partial[(size_t)pair * a.hidden + r0 + ra] = va;
-                a.partial[(size_t)pair * a.hidden + r0 + rb] = vb;
+            } else if (t < 2) {
+                mine[t * 16 + g * 2] = vA;      // rows g >= 4 duplicate rows g - 4 and are never stored
+                mine[t * 16 + g * 2 + 1] = vB;
             }
-            __syncthreads();
-        }
-    } else if (a.has_shared) {
-        // shared expert down projection, 4-bit, all B tokens, two per pass
-        const int K = a.sh_inter, groups = K / 64;
-        const int rowb = K / 2, rowp = rowb + 16;
-        const unsigned fbytes = (unsigned)frag4_entries(K) * 8u;
-        if (tid == 0) finch_mbar_init(mbar, 1);
-        __syncthreads();
-        if (warp == 0) {
-            if (lane == 0) finch_mbar_expect_tx(mbar, (unsigned)B_ROWS * rowb + (unsigned)min(2, a.B) * fbytes);
-            __syncwarp();
-            for (int r = lane; r < B_ROWS; r += 32) finch_bulk_g2s(smem + L.w + r * rowp, a.sh_down.W + (size_t)(r0 + r) * rowb, rowb, mbar);
-            if (lane < min(2, a.B)) finch_bulk_g2s(lane ? frag1 : frag0, a.sfrag4 + (size_t)lane * frag4_entries(K), fbytes, mbar);
-        }
-        uint16_t *sc = reinterpret_cast<uint16_t *>(smem + L.sc);  // [2][B_ROWS][groups]
-        for (int i = tid; i < 2 * B_ROWS * groups; i += B_THREADS) {
-            const int arr = i / (B_ROWS * groups), rem = i - arr * (B_ROWS * groups);
-            sc[i] = (arr ? a.sh_down.B : a.sh_down.S)[(size_t)r0 * groups + rem];
-        }
-        const int npass = (a.B + 1) / 2;
-        for (int ps = 0; ps < npass; ps++) {
-            const int ntok = min(2, a.B - 2 * ps);
-            if (ps > 0 && warp == 0) {
-                if (lane == 0) finch_mbar_expect_tx(mbar, (unsigned)ntok * fbytes);
+            if (ps == npass - 1 && kw != 0) {  // this warp is done with the stage
                 __syncwarp();
-                if (lane < ntok) finch_bulk_g2s(lane ? frag1 : frag0, a.sfrag4 + (size_t)(2 * ps + lane) * frag4_entries(K), fbytes, mbar);
+                if (lane == 0) mbar_arrive(empty + st);
             }
-            for (int ts = 0; ts < ntok; ts++) fetch_xg(a.sXg, a.sE, 2 * ps + ts, groups, Xg + ts * 128, sm_E + ts);
-            __syncthreads();
-            if (!finch_mbar_wait(mbar, ps & 1)) {
-                if (tid == 0) atomicExch(a.status, FINCH_E_TIMEOUT);
-                return;
-            }
-            float va, vb;
-            gemv4_groups(reinterpret_cast<const uint32_t *>(smem + L.w + ra * rowp), reinterpret_cast<const uint32_t *>(smem + L.w + rb * rowp),
-                         sc + ra * groups, sc + rb * groups, a.sh_scale_dtype, frag0, frag1, ntok, groups, 0, 1, va, vb);
-            if (t < ntok) {
-                const float fac = pow2_biased(sm_E[t] + 17);
-                va *= fac;
-                vb *= fac;
-                const float *xg = Xg + t * 128;
-                const uint16_t *ba = sc + (B_ROWS + ra) * groups, *bb = sc + (B_ROWS + rb) * groups;
-                for (int c = 0; c < groups; c++) {
-                    va = fmaf(finch_widen16(ba[c], a.sh_scale_dtype), xg[c], va);
-                    vb = fmaf(finch_widen16(bb[c], a.sh_scale_dtype), xg[c], vb);
+            bar_sync(bar_id, TEAM_A * 32);
+            if (kw == 0) {
+                // lane = (token slot, row g, gate|up): sum of the team's partials in fixed order, then SiLU(gate) * up
+                const float *src = tred + rbuf * TEAM_A * 32 + lane;
+                float v = 0.f;
+#pragma unroll
+                for (int k = 0; k < TEAM_A; k++) v += src[k * 32];
+                const float other = __shfl_xor_sync(0xffffffffu, v, 1);
+                const int ts = lane >> 4, gg = (lane >> 1) & 7;
+                if (!(lane & 1) && ts < ntok) {
+                    const float r = (v / (1.0f + expf(-v))) * other;
+                    if (routed) a.act[(size_t)(ts ? pair1 : pair0) * a.inter + 8 * ta + gg] = r;
+                    else if (gg < 4) a.shared_act[(size_t)(2 * ps + ts) * I + 4 * ta + gg] = r;
                 }
-                float *o = a.partial + (size_t)(a.P + 2 * ps + t) * a.hidden + r0;
-                o[ra] = va;
-                o[rb] = vb;
+                if (ps == npass - 1) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(empty + st);
+                }
             }
-            __syncthreads();
+            rbuf ^= 1;
         }
     }
-    // (with no shared expert the y == P CTA only arrives, so that the combine always runs)
-
-    // ---- arrival + combine by the last CTA of this row chunk ----
-    int expected;
-    if (a.use_prep) {
-        expected = __ldcg(a.n_groups) + 1;
-    } else {
-        expected = scan_pairs(a, sm_ids, sm_ballot) + 1;
+    if (a.dbg && tid == 0) {
+        long long *d = a.dbg + (size_t)blockIdx.x * 8;
+        d[0] = tk1 - tk0;           // table + barriers
+        d[1] = tk2 - tk1;           // waiting for the token records
+        d[2] = clock64() - tk2;     // job loop of team 0
+        d[3] = wait_acc;            // ... of which waiting for a full stage
+        d[4] = 0;
+        d[5] = 0;
+        d[6] = njobs;
+        d[7] = job1 - job0;
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) *sm_last = atomicAdd(&a.counters[blockIdx.x], 1u) == (unsigned)(expected - 1);
-    __syncthreads();
-    if (!*sm_last) return;
-    __threadfence();
-    if (a.use_prep) scan_pairs(a, sm_ids, sm_ballot);
-    for (int i = tid; i < a.B * B_ROWS; i += B_THREADS) {
-        const int b = i / B_ROWS, row = r0 + (i % B_ROWS);
-        float moe = 0.f;
-        for (int k = 0; k < a.K; k++) {
-            const int p = b * a.K + k;
-            if (sm_ids[p] >= 0) moe = fmaf(a.weights[p], __ldcg(&a.partial[(size_t)p * a.hidden + row]), moe);
-        }
-        float h = a.h_mid ? a.h_mid[(size_t)b * a.hidden + row] : 0.f;
-        h += moe;
-        if (a.has_shared) {
-            const float sg = 1.0f / (1.0f + expf(-a.gate_score[b]));
-            h = fmaf(sg, __ldcg(&a.partial[(size_t)(a.P + b) * a.hidden + row]), h);
-        }
-        a.hidden_out[(size_t)b * a.hidden + row] = h;
-    }
-    if (tid == 0) a.counters[blockIdx.x] = 0u;
 }
 
+// ============================ kernel B ====================================
+struct SmemB {
+    int stage, stg, rec, srec, tab, ok, contrib, lastf, bar, total;
+};
+__host__ __device__ inline SmemB smem_b_layout(int hidden, int inter, int sh_inter, int B, int has_shared, int stages) {
+    const FinchTile T = finch_tile(hidden, inter);
+    const FinchTile4 T4 = finch_tile4(hidden, sh_inter);
+    SmemB L;
+    L.stage = 0;
+    L.stg = up128(has_shared && T4.tileB > T.tileB ? T4.tileB : T.tileB);
+    L.rec = L.stage + stages * L.stg;                        // act records of the groups in this CTA's range
+    L.srec = up128(L.rec + REC_CAP * rec3_bytes(inter));     // shared_act records
+    L.tab = up128(L.srec + (has_shared ? B * rec4_bytes(sh_inter) : 0));
+    L.ok = up128(L.tab + (int)sizeof(GroupTab));
+    L.contrib = L.ok + MAXP * 4;
+    L.lastf = L.contrib + 128 * 4;
+    L.bar = up128(L.lastf + 128);
+    L.total = L.bar + 2 * 32 * 8 + 16;
+    return L;
+}
+
+// grid: one CTA per SM (persistent); block: CW_B consumer warps + 1 producer warp.
+__global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const long long tk0 = clock64();
+    const int S = a.stages_b;
+    const SmemB L = smem_b_layout(a.hidden, a.inter, a.sh_inter, a.B, a.has_shared, S);
+    const FinchTile T = finch_tile(a.hidden, a.inter);
+    const FinchTile4 T4 = finch_tile4(a.hidden, a.sh_inter);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+    GroupTab *tab = reinterpret_cast<GroupTab *>(smem + L.tab);
+    int *sm_ok = reinterpret_cast<int *>(smem + L.ok);
+    int *contrib = reinterpret_cast<int *>(smem + L.contrib);
+    unsigned char *lastf = smem + L.lastf;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar), *empty = full + 32;
+    const uint2 *zero8 = reinterpret_cast<const uint2 *>(empty + 32);
+    const int K = a.inter, Ks = a.sh_inter, nCh = a.hidden / 64;
+    const int r3b = rec3_bytes(K), r4b = rec4_bytes(Ks);
+
+    {
+        const int *s = reinterpret_cast<const int *>(a.gtab);
+        int *d = reinterpret_cast<int *>(tab);
+        for (int i = tid; i < (int)(sizeof(GroupTab) / 4); i += NT_B) d[i] = __ldcg(s + i);
+    }
+    if (tid < 128) contrib[tid] = 0;
+    if (tid == 0) {
+        empty[32] = 0ull;
+        for (int s = 0; s < S; s++) {
+            finch_mbar_init(full + s, 1);
+            finch_mbar_init(empty + s, 1);
+        }
+    }
+    __syncthreads();
+    const long long tk1 = clock64();
+    const int ng = tab->ng, n_routed = ng * T.nTB;
+    const int job0 = tab->range_b[blockIdx.x], job1 = tab->range_b[blockIdx.x + 1];
+    const int expected = 4 * ng + (a.has_shared ? 4 : 0);  // tiles that must land in a 64-row chunk
+
+    if (warp == CW_B) {
+        if (lane == 0) {
+            for (int job = job0, it = 0; job < job1; ++job, ++it) {
+                const int st = it % S, use = it / S;
+                if (use > 0 && !finch_mbar_wait(empty + st, (use - 1) & 1)) {
+                    atomicExch(a.status, FINCH_E_TIMEOUT);
+                    return;
+                }
+                uint8_t *dst = smem + L.stage + st * L.stg;
+                if (job < n_routed) {
+                    const int gi = job / T.nTB, tb = job - gi * T.nTB;
+                    finch_mbar_expect_tx(full + st, (unsigned)T.tileB);
+                    finch_bulk_g2s(dst, a.pool_base + (size_t)tab->slot[gi] * a.slot_bytes + T.b_base + (size_t)tb * T.tileB, T.tileB, full + st);
+                } else {
+                    finch_mbar_expect_tx(full + st, (unsigned)T4.tileB);
+                    finch_bulk_g2s(dst, a.sh_tiles + T4.b_base + (size_t)(job - n_routed) * T4.tileB, T4.tileB, full + st);
+                }
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumer warps ----------------
+    // operand records of the activations this CTA needs: the pairs of the groups in its job range
+    // (and every token's shared activations if it has shared-expert jobs), one warp per record
+    const int g_lo = job0 < n_routed ? job0 / T.nTB : ng;
+    const int g_hi = job1 > job0 ? min(ng - 1, (job1 - 1) / T.nTB) : -1;   // inclusive
+    {
+        int q = 0;
+        for (int gi = g_lo; gi <= g_hi; gi++)
+            for (int i = 0; i < tab->m[gi]; i++, q++)
+                if (q % CW_B == warp && q < REC_CAP)
+                    warp_make_record<3>(a.act + (size_t)tab->pairs[gi][i] * K, K, smem + L.rec + q * r3b);
+        if (q > REC_CAP && tid == 0) atomicExch(a.status, FINCH_E_UNSUPPORTED);
+        if (a.has_shared && job1 > n_routed && job1 > job0)
+            for (int b = 0; b < a.B; b++, q++)
+                if (q % CW_B == warp) warp_make_record<4>(a.shared_act + (size_t)b * Ks, Ks, smem + L.srec + b * r4b);
+    }
+    bar_sync(1, CW_B * 32);
+    const long long tk2 = clock64();
+
+    long long wait_acc = 0;
+    int njobs = 0;
+    for (int it = warp; job0 + it < job1; it += CW_B, ++njobs) {
+        const int job = job0 + it, st = it % S, use = it / S;
+        const long long w0 = clock64();
+        if (!finch_mbar_wait(full + st, use & 1)) {
+            if (lane == 0) atomicExch(a.status, FINCH_E_TIMEOUT);
+            break;
+        }
+        wait_acc += clock64() - w0;
+        const uint8_t *tile = smem + L.stage + st * L.stg;
+        int tb;
+        if (job < n_routed) {
+            const int gi = job / T.nTB, m = tab->m[gi], npass = (m + 1) / 2;
+            tb = job - gi * T.nTB;
+            int slot0 = 0;  // first record of this group in the CTA's record area
+            for (int j = g_lo; j < gi; j++) slot0 += tab->m[j];
+            for (int ps = 0; ps < npass; ps++) {
+                const int ntok = min(2, m - 2 * ps);
+                const uint8_t *rec0 = smem + L.rec + (slot0 + 2 * ps) * r3b, *rec1 = smem + L.rec + (slot0 + 2 * ps + (ntok > 1)) * r3b;
+                float va, vb;
+                gemv3_tile(tile, T.unitsD, 0, 1, a.scale_dtype, reinterpret_cast<const uint2 *>(rec0), reinterpret_cast<const uint2 *>(rec1),
+                           reinterpret_cast<const float *>(rec0 + frag3_bytes(K)), reinterpret_cast<const float *>(rec1 + frag3_bytes(K)),
+                           zero8, ntok, va, vb);
+                if ((t & 1) == 0 && (t >> 1) < ntok) {
+                    float *o = a.partial + (size_t)tab->pairs[gi][2 * ps + (t >> 1)] * a.hidden + 16 * tb + g;
+                    o[0] = va;
+                    o[8] = vb;
+                }
+            }
+        } else {
+            tb = job - n_routed;
+            const int npass = (a.B + 1) / 2;
+            for (int ps = 0; ps < npass; ps++) {
+                const int ntok = min(2, a.B - 2 * ps);
+                const uint8_t *rec0 = smem + L.srec + (2 * ps) * r4b, *rec1 = smem + L.srec + (2 * ps + (ntok > 1)) * r4b;
+                float va, vb;
+                gemv4_tile(tile, Ks / 64, 0, 1, lane, 32, g, 8, a.sh_scale_dtype, reinterpret_cast<const uint2 *>(rec0),
+                           reinterpret_cast<const uint2 *>(rec1), reinterpret_cast<const float *>(rec0 + frag4_bytes(Ks)),
+                           reinterpret_cast<const float *>(rec1 + frag4_bytes(Ks)), zero8, ntok, va, vb);
+                if (t < ntok) {
+                    float *o = a.partial + (size_t)(a.P + 2 * ps + t) * a.hidden + 16 * tb + g;
+                    o[0] = va;
+                    o[8] = vb;
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive(empty + st);
+            atomicAdd(&contrib[tb >> 2], 1);
+        }
+    }
+
+    // ---- arrivals: the CTA that completes a 64-row chunk combines it ----
+    const long long tk3 = clock64();
+    __threadfence();
+    bar_sync(1, CW_B * 32);
+    if (tid < nCh) {
+        const int n = contrib[tid];
+        bool last = false;
+        if (n > 0) {
+            last = atomicAdd(&a.cnt_b[tid], (unsigned)n) + (unsigned)n == (unsigned)expected;
+            if (last) a.cnt_b[tid] = 0u;
+        } else if (expected == 0) {
+            last = (tid % gridDim.x) == blockIdx.x;  // nothing to wait for: spread the chunks over the CTAs
+        }
+        lastf[tid] = last;
+    }
+    bar_sync(1, CW_B * 32);
+    int any = 0;
+    for (int c = 0; c < nCh; c++) any |= lastf[c];
+    const long long tk4 = clock64();
+    if (any) {
+        if (tid < MAXP) sm_ok[tid] = tid < a.P && pair_ok(a, tid);
+        __threadfence();
+        bar_sync(1, CW_B * 32);
+        for (int c = 0; c < nCh; c++) {
+            if (!lastf[c]) continue;
+            for (int i = tid; i < a.B * 64; i += CW_B * 32) {
+                const int b = i >> 6, row = c * 64 + (i & 63);
+                float moe = 0.f;
+                for (int k = 0; k < a.K; k++) {
+                    const int p = b * a.K + k;
+                    if (sm_ok[p]) moe = fmaf(a.weights[p], __ldcg(&a.partial[(size_t)p * a.hidden + row]), moe);
+                }
+                float h = a.h_mid ? a.h_mid[(size_t)b * a.hidden + row] : 0.f;
+                h += moe;
+                if (a.has_shared) {
+                    const float sg = 1.0f / (1.0f + expf(-a.gate_score[b]));
+                    h = fmaf(sg, __ldcg(&a.partial[(size_t)(a.P + b) * a.hidden + row]), h);
+                }
+                a.hidden_out[(size_t)b * a.hidden + row] = h;
+            }
+        }
+    }
+    if (a.dbg && tid == 0) {
+        long long *d = a.dbg + (size_t)(1024 + blockIdx.x) * 8;
+        d[0] = tk1 - tk0;   // table + barriers
+        d[1] = tk2 - tk1;   // act records
+        d[2] = tk3 - tk2;   // job loop of warp 0
+        d[3] = wait_acc;    // ... of which waiting for a full stage
+        d[4] = tk4 - tk3;   // fence + arrival atomics
+        d[5] = clock64() - tk4;  // combine
+        d[6] = njobs;
+        d[7] = job1 - job0;
+    }
+}
+
+constexpr int SMEM_MAX = 227 * 1024;
 bool g_attr_set = false;
 
 int check_shared(finch_ctx *ctx, const finch_shared *sh) {
@@ -879,18 +950,47 @@ int check_shared(finch_ctx *ctx, const finch_shared *sh) {
     return FINCH_OK;
 }
 
+// Tiled copy of a shared expert, made the first time the expert is seen (keyed by its three weight
+// pointers) and kept for the life of the context.
+int prepared_shared(finch_ctx *ctx, const finch_shared *sh, cudaStream_t st, const uint8_t **out) {
+    for (auto &e : ctx->shared_cache)
+        if (e.key[0] == sh->gate.W && e.key[1] == sh->up.W && e.key[2] == sh->down.W) {
+            *out = (const uint8_t *)e.tiles;
+            return FINCH_OK;
+        }
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cap);
+    if (cap != cudaStreamCaptureStatusNone)
+        return finch_fail(ctx, FINCH_E_UNSUPPORTED, "a shared expert must be used once outside stream capture before it is captured");
+    const FinchTile4 T4 = finch_tile4(ctx->cfg.hidden, sh->gate.out_dim);
+    void *buf = nullptr;
+    if (cudaMalloc(&buf, T4.total) != cudaSuccess) {
+        cudaGetLastError();
+        return finch_fail(ctx, FINCH_E_NOMEM, "tiled copy of the shared expert (%zu bytes)", T4.total);
+    }
+    SharedSrc S{(const uint32_t *)sh->gate.W,      (const uint32_t *)sh->up.W,        (const uint32_t *)sh->down.W,
+                (const uint16_t *)sh->gate.scales, (const uint16_t *)sh->gate.biases, (const uint16_t *)sh->up.scales,
+                (const uint16_t *)sh->up.biases,   (const uint16_t *)sh->down.scales, (const uint16_t *)sh->down.biases};
+    shared_retile_kernel<<<256, 256, 0, st>>>(S, ctx->cfg.hidden, sh->gate.out_dim, (uint8_t *)buf);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        cudaFree(buf);
+        return finch_fail(ctx, FINCH_E_CUDA, "shared_retile_kernel: %s", cudaGetErrorString(e));
+    }
+    ctx->launches++;
+    ctx->shared_cache.push_back({{sh->gate.W, sh->up.W, sh->down.W}, buf});
+    *out = (const uint8_t *)buf;
+    return FINCH_OK;
+}
+
+inline size_t up256z(size_t n) { return (n + 255) & ~(size_t)255; }
+
 }  // namespace
 
-// Bytes of fragment / group scratch a context needs (allocated in finch_ctx_create).
+// Bytes of operand-record / group-table scratch a context needs (allocated in finch_ctx_create).
 size_t finch_decode_scratch_bytes(const finch_config &c) {
-    const size_t P = (size_t)c.max_tokens * c.top_k, B = c.max_tokens;
-    const int shi = c.shared_inter > 0 ? c.shared_inter : 64;
-    size_t n = 0;
-    n += B * frag3_entries(c.hidden) * 8 + B * frag4_entries(c.hidden) * 8 + B * 128 * 4 + B * 4;
-    n += P * 8 + P * 64 + 256;
-    n += P * frag3_entries(c.moe_inter) * 8 + P * 128 * 4 + P * 4;
-    n += B * frag4_entries(shi) * 8 + B * 128 * 4 + B * 4;
-    return n + 16 * 256;
+    const size_t B = c.max_tokens;
+    return up256z(sizeof(GroupTab)) + up256z(B * rec3_bytes(c.hidden)) + up256z(B * frag4_bytes(c.hidden)) + 1024;
 }
 
 extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finch_pool *pool, int layer, const void *h_post,
@@ -901,16 +1001,24 @@ extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finc
     if (pool->ctx != ctx) return finch_fail(ctx, FINCH_E_ARG, "pool belongs to another context");
     if (layer < 0 || layer >= pool->n_layers) return finch_fail(ctx, FINCH_E_ARG, "layer %d out of range", layer);
     if (B < 1 || B > c.max_tokens) return finch_fail(ctx, FINCH_E_ARG, "B=%d outside 1..max_tokens=%d", B, c.max_tokens);
-    if (B * c.top_k > FINCH_MAX_PAIRS)
-        return finch_fail(ctx, FINCH_E_UNSUPPORTED, "decode path takes at most %d (token, expert) pairs; use finch_encode_moe_prefill",
-                          FINCH_MAX_PAIRS);
+    if (B * c.top_k > FINCH_MAX_PAIRS || B > MAXM)
+        return finch_fail(ctx, FINCH_E_UNSUPPORTED, "decode path takes at most %d tokens / %d (token, expert) pairs; use finch_encode_moe_prefill",
+                          MAXM, FINCH_MAX_PAIRS);
     if (pool->n_experts != c.n_experts) return finch_fail(ctx, FINCH_E_ARG, "pool / context expert count mismatch");
+    cudaSetDevice(c.device);
+    cudaStream_t st = finch_pick_stream(ctx, stream);
+    MoeArgs a{};
+    a.sh_inter = 64;
     if (shared) {
         int rc = check_shared(ctx, shared);
         if (rc) return rc;
+        if ((rc = prepared_shared(ctx, shared, st, &a.sh_tiles))) return rc;
+        a.has_shared = 1;
+        a.sh_scale_dtype = shared->gate.scale_dtype;
+        a.shared_act = ctx->shared_act;
+        a.gate_score = shared->gate_score;
+        a.sh_inter = shared->gate.out_dim;
     }
-    cudaSetDevice(c.device);
-    MoeArgs a{};
     a.pool_base = pool->base;
     a.slot_bytes = pool->slot_bytes;
     a.slot_row = pool->slot_table_dev + (size_t)layer * pool->n_experts;
@@ -925,67 +1033,46 @@ extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finc
     a.B = B;
     a.hidden = c.hidden;
     a.inter = c.moe_inter;
-    a.gate_w = ctx->lay.gate_w; a.gate_s = ctx->lay.gate_s; a.gate_b = ctx->lay.gate_b;
-    a.up_w = ctx->lay.up_w; a.up_s = ctx->lay.up_s; a.up_b = ctx->lay.up_b;
-    a.down_w = ctx->lay.down_w; a.down_s = ctx->lay.down_s; a.down_b = ctx->lay.down_b;
     a.scale_dtype = c.scale_dtype;
     a.act = ctx->act;
     a.partial = ctx->partial;
-    a.counters = ctx->counters;
-    a.cnt_a = ctx->counters + c.hidden / 64;
+    a.cnt_b = ctx->counters;
     a.status = ctx->dev_status;
     a.h_mid = h_mid;
     a.hidden_out = hidden_out;
-    a.sh_inter = 64;
-    if (shared) {
-        a.has_shared = 1;
-        a.sh_gate = WRef{(const uint8_t *)shared->gate.W, (const uint16_t *)shared->gate.scales, (const uint16_t *)shared->gate.biases,
-                         shared->gate.out_dim, shared->gate.in_dim};
-        a.sh_up = WRef{(const uint8_t *)shared->up.W, (const uint16_t *)shared->up.scales, (const uint16_t *)shared->up.biases,
-                       shared->up.out_dim, shared->up.in_dim};
-        a.sh_down = WRef{(const uint8_t *)shared->down.W, (const uint16_t *)shared->down.scales, (const uint16_t *)shared->down.biases,
-                         shared->down.out_dim, shared->down.in_dim};
-        a.sh_scale_dtype = shared->gate.scale_dtype;
-        a.shared_act = ctx->shared_act;
-        a.gate_score = shared->gate_score;
-        a.sh_inter = shared->gate.out_dim;
-    }
-    // carve the fragment scratch (same order as finch_decode_scratch_bytes)
-    {
-        const size_t Pm = (size_t)c.max_tokens * c.top_k, Bm = c.max_tokens;
-        const int shi = c.shared_inter > 0 ? c.shared_inter : 64;
+    a.dbg = (long long *)ctx->dbg;
+    {  // carve the scratch (same order as finch_decode_scratch_bytes)
+        const size_t Bm = c.max_tokens;
         char *p = (char *)ctx->frag_scratch;
         auto take = [&](size_t bytes) {
             char *r = p;
-            p += (bytes + 255) & ~(size_t)255;
+            p += up256z(bytes);
             return r;
         };
-        a.xfrag3 = (uint2 *)take(Bm * frag3_entries(c.hidden) * 8);
-        a.xfrag4 = (uint2 *)take(Bm * frag4_entries(c.hidden) * 8);
-        a.xXg = (float *)take(Bm * 128 * 4);
-        a.xE = (int *)take(Bm * 4);
-        a.grp = (int2 *)take(Pm * 8);
-        a.grp_pairs = (uint8_t *)take(Pm * 64);
-        a.n_groups = (int *)take(256);
-        a.afrag3 = (uint2 *)take(Pm * frag3_entries(c.moe_inter) * 8);
-        a.aXg = (float *)take(Pm * 128 * 4);
-        a.aE = (int *)take(Pm * 4);
-        a.sfrag4 = (uint2 *)take(Bm * frag4_entries(shi) * 8);
-        a.sXg = (float *)take(Bm * 128 * 4);
-        a.sE = (int *)take(Bm * 4);
+        a.gtab = (GroupTab *)take(sizeof(GroupTab));
+        a.xrec3 = (uint8_t *)take(Bm * rec3_bytes(c.hidden));
+        a.xrec4 = (uint8_t *)take(Bm * frag4_bytes(c.hidden));
     }
-    a.use_prep = ctx->force_prep >= 0 ? ctx->force_prep : (B >= PREP_MIN_TOKENS ? 1 : 0);
-    const SmemA LA = smem_a_layout(c.hidden);
-    const SmemB LB = smem_b_layout(c.moe_inter, a.sh_inter);
-    const int prep_smem = c.hidden * 4 + 128 * 4 + 64 + 64 * 4 + 64;
-    if (LA.total > 227 * 1024 || LB.total > 227 * 1024) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "dims need too much shared memory");
+    const int grid = ctx->sm_count < MAXG ? ctx->sm_count : MAXG;
+    a.grid_a = a.grid_b = grid;
+    // pipeline depth: as many stages as fit
+    const SmemA A0 = smem_a_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, 0);
+    const SmemB B0 = smem_b_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, 0);
+    int sa = (SMEM_MAX - A0.total) / A0.stg, sb = (SMEM_MAX - B0.total) / B0.stg;
+    sa = sa > 32 ? 32 : sa;
+    sb = sb > 32 ? 32 : sb;
+    if (sa < 2 || sb < 2) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "dims need too much shared memory");
+    a.stages_a = sa;
+    a.stages_b = sb;
+    const SmemA LA = smem_a_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, sa);
+    const SmemB LB = smem_b_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, sb);
+    const int prep_smem = c.hidden * 4 + 144 * 4 + 32 + MAXP * 4 + MAXP + (int)sizeof(GroupTab) + 64;
     if (!g_attr_set) {
-        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_down_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
+        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_down_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
         FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
         g_attr_set = true;
     }
-    cudaStream_t st = finch_pick_stream(ctx, stream);
     cudaEvent_t *pe = nullptr;
     if (ctx->profile) {
         while (ctx->prof_events.size() < ctx->prof_used + 3) {
@@ -996,23 +1083,16 @@ extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finc
         pe = &ctx->prof_events[ctx->prof_used];
         ctx->prof_used += 3;
     }
-    if (a.use_prep) {
-        moe_prep_kernel<<<B + 1, A_THREADS, prep_smem, st>>>(a);
-        FINCH_CUDA_OK(ctx, cudaGetLastError());
-        ctx->launches++;
-    }
+    moe_prep_kernel<<<B + 1, 256, prep_smem, st>>>(a);
+    FINCH_CUDA_OK(ctx, cudaGetLastError());
     if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[0], st));
-    const int chunks_r = c.moe_inter / A_ROWS;
-    const int sh_rows_of_ctas = shared ? (a.sh_inter / S_ROWS + chunks_r - 1) / chunks_r : 0;
-    dim3 ga(chunks_r, a.P + sh_rows_of_ctas);
-    moe_gateup_kernel<<<ga, A_THREADS, LA.total, st>>>(a);
+    moe_gateup_kernel<<<grid, NT_A, LA.total, st>>>(a);
     FINCH_CUDA_OK(ctx, cudaGetLastError());
     if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[1], st));
-    dim3 gb(c.hidden / B_ROWS, a.P + 1);
-    moe_down_combine_kernel<<<gb, B_THREADS, LB.total, st>>>(a);
+    moe_down_combine_kernel<<<grid, NT_B, LB.total, st>>>(a);
     FINCH_CUDA_OK(ctx, cudaGetLastError());
     if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[2], st));
-    ctx->launches += 2;
+    ctx->launches += 3;
     return FINCH_OK;
 }
 
@@ -1042,9 +1122,17 @@ extern "C" int finch_profile_read(finch_ctx *ctx, float *ms_gateup, float *ms_do
     return FINCH_OK;
 }
 
-// Test hook: -1 = choose by batch size, 0 = never run the prep kernel, 1 = always.
+// Kept for binary compatibility of the test hook: the preparation kernel now always runs.
 extern "C" int finch_debug_force_prep(finch_ctx *ctx, int mode) {
     if (!ctx || mode < -1 || mode > 1) return FINCH_E_ARG;
     ctx->force_prep = mode;
+    return FINCH_OK;
+}
+
+// Diagnostics: when buf (device memory, 2048 x 8 int64) is non-NULL, the CTAs of the two streaming
+// kernels store the cycles they spent in each phase there.  NULL switches it off.
+extern "C" int finch_debug_timing(finch_ctx *ctx, void *buf) {
+    if (!ctx) return FINCH_E_ARG;
+    ctx->dbg = buf;
     return FINCH_OK;
 }

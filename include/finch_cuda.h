@@ -224,6 +224,11 @@ FINCH_API int finch_profile_read(finch_ctx *ctx, float *ms_gateup, float *ms_dow
  * (mode -1); 0 forces the build inside every CTA, 1 forces the preparation
  * kernel.  Results are identical.  No counterpart in the reference. */
 FINCH_API int finch_debug_force_prep(finch_ctx *ctx, int mode);
+/* Diagnostics: with a non-NULL device buffer of 8 int64 per SM, every CTA of the
+ * gate/up kernel of finch_encode_moe_decode records the clock cycles of its
+ * phases there (setup, operand records, item loop, time waiting for weights,
+ * fence, arrivals, items, records made).  NULL switches it off. */
+FINCH_API int finch_debug_timing(finch_ctx *ctx, void *device_buf);
 
 /* Count of kernels launched by this context since creation (benchmark bookkeeping). */
 FINCH_API uint64_t finch_launch_count(const finch_ctx *ctx);
