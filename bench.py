@@ -313,7 +313,7 @@ def run_ours(args):
     n0 = stack.ctx.launch_count()
     secs = stack.time_steps(dev, xd, score, out, batch, args.steps, args.warmup, barrier if world > 1 else None,
                             use_graph=not args.no_graph)
-    launches = 2 * LAYERS * args.steps  # two kernels per layer call (graph replays launch them without the host counter)
+    launches = 4 * LAYERS * args.steps  # four kernels per layer call (graph replays launch them without the host counter)
     del n0
     clocks = sampler.stop() if sampler else None
     if world > 1:

@@ -544,7 +544,7 @@ __global__ void shared_retile_kernel(SharedSrc S, int hidden, int inter, uint8_t
 // ============================ kernel A ====================================
 __host__ __device__ inline int up128(int x) { return (x + 127) & ~127; }
 struct SmemA {
-    int stage, stg, rec, rx3, rec4, f4s, n4, red, tab, bar, total;
+    int stage, stg, rec, rx3, rec4, f4s, n4, red, qcnt, tab, bar, total;
 };
 __host__ __device__ inline SmemA smem_a_layout(int hidden, int inter, int sh_inter, int B, int has_shared, int stages) {
     const FinchTile T = finch_tile(hidden, inter);
@@ -558,7 +558,8 @@ __host__ __device__ inline SmemA smem_a_layout(int hidden, int inter, int sh_int
     L.f4s = frag4_bytes(hidden) + 64;
     L.n4 = has_shared ? (B < 2 ? B : 2) : 0;
     L.red = up128(L.rec4 + L.n4 * L.f4s);
-    L.tab = L.red + NTEAM_A * 2 * TEAM_A * 32 * 4;
+    L.qcnt = L.red + stages * (MAXM / 2) * TEAM_A * 32 * 4;   // per stage: [pass][warp][32] partial sums
+    L.tab = L.qcnt + 32 * 4;
     L.bar = up128(L.tab + (int)sizeof(GroupTab));
     L.total = L.bar + 2 * 32 * 8 + 16 + 16;
     return L;
@@ -587,6 +588,7 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
         int *d = reinterpret_cast<int *>(tab);
         for (int i = tid; i < (int)(sizeof(GroupTab) / 4); i += NT_A) d[i] = __ldcg(s + i);
     }
+    if (tid < 32) reinterpret_cast<int *>(smem + L.qcnt)[tid] = 0;
     if (tid == 0) {
         empty[32] = 0ull;
         for (int s = 0; s < S; s++) {
@@ -627,16 +629,19 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
         return;
     }
 
-    // ---------------- consumer teams: team q takes the CTA's jobs q, q + NTEAM_A, ... ----------------
-    const int team = warp / TEAM_A, kw = warp % TEAM_A, bar_id = 1 + team;
-    float *tred = red + team * (2 * TEAM_A * 32);
+    // ---------------- consumer warps ----------------
+    // Warp w works on the K-quarter kw = w % 4 of the CTA's jobs w / 4, w / 4 + 4, ...  The four
+    // warps of a job never wait for each other: each leaves its partial sums in the job's slot and
+    // bumps the slot's counter; whoever comes last adds the four partials in fixed order.
+    const int team = warp / TEAM_A, kw = warp % TEAM_A;
+    int *qcnt = reinterpret_cast<int *>(smem + L.qcnt);
     if (!finch_mbar_wait(xbar, 0)) {
         if (lane == 0) atomicExch(a.status, FINCH_E_TIMEOUT);
         return;
     }
     const long long tk2 = clock64();
     long long wait_acc = 0;
-    int njobs = 0, rbuf = 0;
+    int njobs = 0;
     for (int it = team; job0 + it < job1; it += NTEAM_A, ++njobs) {
         const int job = job0 + it, st = it % S, use = it / S;
         const long long w0 = clock64();
@@ -646,20 +651,24 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
         }
         wait_acc += clock64() - w0;
         const uint8_t *tile = smem + L.stage + st * L.stg;
+        float *slot = red + st * (MAXM / 2) * TEAM_A * 32;   // [pass][warp of the job][32]
         const bool routed = job < n_routed;
         const int gi = routed ? job / T.nTA : 0, ta = routed ? job - gi * T.nTA : job - n_routed;
         const int m = routed ? tab->m[gi] : a.B, npass = (m + 1) / 2;
         for (int ps = 0; ps < npass; ps++) {
             const int ntok = min(2, m - 2 * ps);
-            int pair0 = 0, pair1 = 0;
             float vA, vB;
+            float *mine = slot + (ps * TEAM_A + kw) * 32;   // [token slot][row g][A|B]
             if (routed) {
-                pair0 = tab->pairs[gi][2 * ps];
-                pair1 = tab->pairs[gi][2 * ps + (ntok > 1)];
-                const uint8_t *rec0 = smem + L.rec + (pair0 / a.K) * L.rx3, *rec1 = smem + L.rec + (pair1 / a.K) * L.rx3;
+                const int tok0 = tab->pairs[gi][2 * ps] / a.K, tok1 = tab->pairs[gi][2 * ps + (ntok > 1)] / a.K;
+                const uint8_t *rec0 = smem + L.rec + tok0 * L.rx3, *rec1 = smem + L.rec + tok1 * L.rx3;
                 gemv3_tile(tile, T.unitsA, kw, TEAM_A, a.scale_dtype, reinterpret_cast<const uint2 *>(rec0), reinterpret_cast<const uint2 *>(rec1),
                            reinterpret_cast<const float *>(rec0 + frag3_bytes(K)), reinterpret_cast<const float *>(rec1 + frag3_bytes(K)),
                            zero8, ntok, vA, vB);
+                if ((t & 1) == 0) {
+                    mine[(t >> 1) * 16 + g * 2] = vA;
+                    mine[(t >> 1) * 16 + g * 2 + 1] = vB;
+                }
             } else {
                 // shared expert gate/up tile: 4 gate rows + 4 up rows, every token, two per pass
                 const int tok0 = 2 * ps, tok1 = 2 * ps + (ntok > 1);
@@ -670,26 +679,23 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
                 gemv4_tile(tile, groups, kw, TEAM_A, (g & 3) * 4 + t, 16, g & 3, 4, a.sh_scale_dtype, f0, f1,
                            reinterpret_cast<const float *>(smem + L.rec + tok0 * L.rx3 + frag3_bytes(K)),
                            reinterpret_cast<const float *>(smem + L.rec + tok1 * L.rx3 + frag3_bytes(K)), zero8, ntok, vA, vB);
-            }
-            // partial sums of this warp's share of K -> team buffer [warp][token slot][row g][A|B]
-            float *mine = tred + (rbuf * TEAM_A + kw) * 32;
-            if (routed) {
-                if ((t & 1) == 0) {
-                    mine[(t >> 1) * 16 + g * 2] = vA;
-                    mine[(t >> 1) * 16 + g * 2 + 1] = vB;
+                if (t < 2) {
+                    mine[t * 16 + g * 2] = vA;      // rows g >= 4 duplicate rows g - 4 and are never stored
+                    mine[t * 16 + g * 2 + 1] = vB;
                 }
-            } else if (t < 2) {
-                mine[t * 16 + g * 2] = vA;      // rows g >= 4 duplicate rows g - 4 and are never stored
-                mine[t * 16 + g * 2 + 1] = vB;
             }
-            if (ps == npass - 1 && kw != 0) {  // this warp is done with the stage
-                __syncwarp();
-                if (lane == 0) mbar_arrive(empty + st);
-            }
-            bar_sync(bar_id, TEAM_A * 32);
-            if (kw == 0) {
-                // lane = (token slot, row g, gate|up): sum of the team's partials in fixed order, then SiLU(gate) * up
-                const float *src = tred + rbuf * TEAM_A * 32 + lane;
+        }
+        __threadfence_block();
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) old = atomicAdd(&qcnt[st], 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old == TEAM_A - 1) {
+            // last of the four: lane = (token slot, row g, gate|up); sum in fixed order, then SiLU(gate) * up
+            __threadfence_block();
+            for (int ps = 0; ps < npass; ps++) {
+                const int ntok = min(2, m - 2 * ps);
+                const float *src = slot + ps * TEAM_A * 32 + lane;
                 float v = 0.f;
 #pragma unroll
                 for (int k = 0; k < TEAM_A; k++) v += src[k * 32];
@@ -697,16 +703,14 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
                 const int ts = lane >> 4, gg = (lane >> 1) & 7;
                 if (!(lane & 1) && ts < ntok) {
                     const float r = (v / (1.0f + expf(-v))) * other;
-                    if (routed) a.act[(size_t)(ts ? pair1 : pair0) * a.inter + 8 * ta + gg] = r;
+                    if (routed) a.act[(size_t)tab->pairs[gi][2 * ps + ts] * a.inter + 8 * ta + gg] = r;
                     else if (gg < 4) a.shared_act[(size_t)(2 * ps + ts) * I + 4 * ta + gg] = r;
                 }
-                if (ps == npass - 1) {
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(empty + st);
-                }
             }
-            rbuf ^= 1;
+            if (lane == 0) qcnt[st] = 0;
+            __syncwarp();
         }
+        if (lane == 0) mbar_arrive(empty + st);
     }
     if (a.dbg && tid == 0) {
         long long *d = a.dbg + (size_t)blockIdx.x * 8;
@@ -752,12 +756,9 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
     const FinchTile4 T4 = finch_tile4(a.hidden, a.sh_inter);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     GroupTab *tab = reinterpret_cast<GroupTab *>(smem + L.tab);
-    int *sm_ok = reinterpret_cast<int *>(smem + L.ok);
-    int *contrib = reinterpret_cast<int *>(smem + L.contrib);
-    unsigned char *lastf = smem + L.lastf;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar), *empty = full + 32;
     const uint2 *zero8 = reinterpret_cast<const uint2 *>(empty + 32);
-    const int K = a.inter, Ks = a.sh_inter, nCh = a.hidden / 64;
+    const int K = a.inter, Ks = a.sh_inter;
     const int r3b = rec3_bytes(K), r4b = rec4_bytes(Ks);
 
     {
@@ -765,7 +766,6 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
         int *d = reinterpret_cast<int *>(tab);
         for (int i = tid; i < (int)(sizeof(GroupTab) / 4); i += NT_B) d[i] = __ldcg(s + i);
     }
-    if (tid < 128) contrib[tid] = 0;
     if (tid == 0) {
         empty[32] = 0ull;
         for (int s = 0; s < S; s++) {
@@ -777,7 +777,6 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
     const long long tk1 = clock64();
     const int ng = tab->ng, n_routed = ng * T.nTB;
     const int job0 = tab->range_b[blockIdx.x], job1 = tab->range_b[blockIdx.x + 1];
-    const int expected = 4 * ng + (a.has_shared ? 4 : 0);  // tiles that must land in a 64-row chunk
 
     if (warp == CW_B) {
         if (lane == 0) {
@@ -868,54 +867,11 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
             }
         }
         __syncwarp();
-        if (lane == 0) {
-            mbar_arrive(empty + st);
-            atomicAdd(&contrib[tb >> 2], 1);
-        }
+        if (lane == 0) mbar_arrive(empty + st);
+        (void)tb;
     }
 
-    // ---- arrivals: the CTA that completes a 64-row chunk combines it ----
-    const long long tk3 = clock64();
-    __threadfence();
-    bar_sync(1, CW_B * 32);
-    if (tid < nCh) {
-        const int n = contrib[tid];
-        bool last = false;
-        if (n > 0) {
-            last = atomicAdd(&a.cnt_b[tid], (unsigned)n) + (unsigned)n == (unsigned)expected;
-            if (last) a.cnt_b[tid] = 0u;
-        } else if (expected == 0) {
-            last = (tid % gridDim.x) == blockIdx.x;  // nothing to wait for: spread the chunks over the CTAs
-        }
-        lastf[tid] = last;
-    }
-    bar_sync(1, CW_B * 32);
-    int any = 0;
-    for (int c = 0; c < nCh; c++) any |= lastf[c];
-    const long long tk4 = clock64();
-    if (any) {
-        if (tid < MAXP) sm_ok[tid] = tid < a.P && pair_ok(a, tid);
-        __threadfence();
-        bar_sync(1, CW_B * 32);
-        for (int c = 0; c < nCh; c++) {
-            if (!lastf[c]) continue;
-            for (int i = tid; i < a.B * 64; i += CW_B * 32) {
-                const int b = i >> 6, row = c * 64 + (i & 63);
-                float moe = 0.f;
-                for (int k = 0; k < a.K; k++) {
-                    const int p = b * a.K + k;
-                    if (sm_ok[p]) moe = fmaf(a.weights[p], __ldcg(&a.partial[(size_t)p * a.hidden + row]), moe);
-                }
-                float h = a.h_mid ? a.h_mid[(size_t)b * a.hidden + row] : 0.f;
-                h += moe;
-                if (a.has_shared) {
-                    const float sg = 1.0f / (1.0f + expf(-a.gate_score[b]));
-                    h = fmaf(sg, __ldcg(&a.partial[(size_t)(a.P + b) * a.hidden + row]), h);
-                }
-                a.hidden_out[(size_t)b * a.hidden + row] = h;
-            }
-        }
-    }
+    const long long tk3 = clock64(), tk4 = tk3;
     if (a.dbg && tid == 0) {
         long long *d = a.dbg + (size_t)(1024 + blockIdx.x) * 8;
         d[0] = tk1 - tk0;   // table + barriers
@@ -927,6 +883,31 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
         d[6] = njobs;
         d[7] = job1 - job0;
     }
+}
+
+// ============================ combine =====================================
+// hidden = h_mid + sum_{k ascending, usable} w_k * out_k + sigmoid(score) * shared_out, the arithmetic of
+// moe_combine_residual (finchmoe/shaders.metal:2196-2231).  grid: (hidden / 256, B); block 256.
+__global__ void __launch_bounds__(256) moe_combine_kernel(const MoeArgs a) {
+    __shared__ int ok[8];
+    __shared__ float wk[8];
+    const int b = blockIdx.y, row = blockIdx.x * 256 + threadIdx.x;
+    if (threadIdx.x < a.K) {
+        ok[threadIdx.x] = pair_ok(a, b * a.K + threadIdx.x);
+        wk[threadIdx.x] = a.weights[b * a.K + threadIdx.x];
+    }
+    __syncthreads();
+    if (row >= a.hidden) return;
+    float moe = 0.f;
+    for (int k = 0; k < a.K; k++)
+        if (ok[k]) moe = fmaf(wk[k], a.partial[(size_t)(b * a.K + k) * a.hidden + row], moe);
+    float h = a.h_mid ? a.h_mid[(size_t)b * a.hidden + row] : 0.f;
+    h += moe;
+    if (a.has_shared) {
+        const float sg = 1.0f / (1.0f + expf(-a.gate_score[b]));
+        h = fmaf(sg, a.partial[(size_t)(a.P + b) * a.hidden + row], h);
+    }
+    a.hidden_out[(size_t)b * a.hidden + row] = h;
 }
 
 constexpr int SMEM_MAX = 227 * 1024;
@@ -1058,7 +1039,7 @@ extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finc
     // pipeline depth: as many stages as fit
     const SmemA A0 = smem_a_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, 0);
     const SmemB B0 = smem_b_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, 0);
-    int sa = (SMEM_MAX - A0.total) / A0.stg, sb = (SMEM_MAX - B0.total) / B0.stg;
+    int sa = (SMEM_MAX - A0.total) / (A0.stg + (MAXM / 2) * TEAM_A * 32 * 4), sb = (SMEM_MAX - B0.total) / B0.stg;
     sa = sa > 32 ? 32 : sa;
     sb = sb > 32 ? 32 : sb;
     if (sa < 2 || sb < 2) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "dims need too much shared memory");
@@ -1071,6 +1052,12 @@ extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finc
         FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
         FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_down_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
         FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
+        // one shared-memory carve-out for all four kernels: an SM that has to change its L1 / shared split
+        // between consecutive launches drains first
+        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_prep_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_gateup_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_down_combine_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_combine_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
         g_attr_set = true;
     }
     cudaEvent_t *pe = nullptr;
@@ -1091,8 +1078,10 @@ extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finc
     if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[1], st));
     moe_down_combine_kernel<<<grid, NT_B, LB.total, st>>>(a);
     FINCH_CUDA_OK(ctx, cudaGetLastError());
+    moe_combine_kernel<<<dim3((c.hidden + 255) / 256, B), 256, 0, st>>>(a);
+    FINCH_CUDA_OK(ctx, cudaGetLastError());
     if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[2], st));
-    ctx->launches += 3;
+    ctx->launches += 4;
     return FINCH_OK;
 }
 

@@ -315,6 +315,38 @@ def test_moe_decode_full_size_vs_oracle(api, B):
         ctx.destroy()
 
 
+@pytest.mark.parametrize("T", [9, 23, 64])
+def test_moe_prefill_chunk_vs_oracle_and_per_token(api, T):
+    """A prefill chunk must equal the oracle within tolerance and equal, bit for bit, the rows the
+    decode entry point gives token by token (the reference's chunked == per-token claim, README.md:25)."""
+    cfg = dict(hidden=256, inter=128, sd=L.BF16)
+    ctx = api.Context(hidden=256, n_experts=16, top_k=8, moe_inter=128, shared_inter=128, n_layers=1,
+                      scale_dtype=L.BF16, act_dtype=L.F32, max_tokens=64)
+    pool = ctx.pool()
+    try:
+        rng = synth.rng_for(3, T)
+        blocks = {e: synth.expert_block(rng, 256, 128, 64, 3, L.BF16) for e in range(16)}
+        for e, blk in blocks.items():
+            pool.put(0, e, blk)
+        x = rng.normal(0, 1, size=(T, 256)).astype(np.float32)
+        ids, w = synth.zipf_routing(rng, T, 16, 8)
+        sh = synth.shared_expert(rng, 256, 128, 64, 4, L.BF16)
+        shd = ctx.make_shared(*[ctx.upload_tensor(t) for t in sh])
+        score = rng.normal(0, 1, size=T).astype(np.float32)
+        h_mid = rng.normal(0, 1, size=(T, 256)).astype(np.float32)
+        out = ctx.moe_forward_host(pool, 0, x, ids, w, shared=shd, gate_score=score, h_mid=h_mid)
+        want = _oracle_layer(blocks, ids, w, None, x, cfg, shared=sh, score=score, h_mid=h_mid)
+        assert_close(out, want, f"prefill T={T}")
+        for t in (0, T // 2, T - 1):
+            one = ctx.moe_forward_host(pool, 0, x[t:t + 1], ids[t:t + 1], w[t:t + 1], shared=shd,
+                                       gate_score=score[t:t + 1], h_mid=h_mid[t:t + 1])
+            assert np.array_equal(one[0].view(np.uint32), out[t].view(np.uint32)), f"token {t} differs from per-token decode"
+        assert ctx.device_status() == 0
+    finally:
+        pool.destroy()
+        ctx.destroy()
+
+
 # ---------------------------------------------------------------------- pool
 def test_pool_lru_and_roundtrip(api):
     ctx = api.Context(hidden=256, n_experts=8, top_k=8, moe_inter=128, shared_inter=128, n_layers=2, max_tokens=1)
