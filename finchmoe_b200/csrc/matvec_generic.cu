@@ -418,3 +418,54 @@ extern "C" int finch_debug_dequant(finch_ctx *ctx, const finch_wdesc *w, uint8_t
     if (e != cudaSuccess) return finch_fail(ctx, FINCH_E_CUDA, "debug_dequant: %s", cudaGetErrorString(e));
     return FINCH_OK;
 }
+
+// ---- allocation-free matvec ----------------------------------------------
+// Staging memory for finch_matvec_noalloc: the activations of a call are copied
+// here from the host and the results are written here before they go back.  It
+// is part of the library image, so every GPU that loads the library holds these
+// 512 KiB until the process exits.
+#define FINCH_NOALLOC_SCRATCH_BYTES (512 * 1024)
+static __device__ __align__(256) unsigned char g_noalloc_scratch[FINCH_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+void *g_noalloc_ptr[kMaxDevices] = {nullptr};  // device address of g_noalloc_scratch, per device
+std::mutex g_noalloc_mu;
+}  // namespace
+
+extern "C" int finch_matvec_noalloc(const finch_wdesc *w, const float *x_host, float *out_host, int M, finch_stream stream) {
+    if (!w || !x_host || !out_host || M < 1) return FINCH_E_ARG;
+    if (finch_validate_wdesc(nullptr, w, "matvec_noalloc")) return FINCH_E_ARG;
+    const size_t xb = (size_t)M * w->in_dim * sizeof(float), ob = (size_t)M * w->out_dim * sizeof(float);
+    const size_t x_room = (xb + 255) & ~(size_t)255;
+    if (x_room + ob > FINCH_NOALLOC_SCRATCH_BYTES) return FINCH_E_UNSUPPORTED;  // M * (in_dim + out_dim) floats must fit 512 KiB
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FINCH_E_CUDA;
+    void *base = nullptr;
+    {
+        // The array's name is only a host-side handle; the kernel needs the address it has on the
+        // current device.  Looked up once per device, on the first call made with that device current.
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void *p = nullptr;
+            if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+                cudaGetLastError();
+                return FINCH_E_CUDA;
+            }
+            g_noalloc_ptr[dev] = p;
+        }
+        base = g_noalloc_ptr[dev];
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    float *xd = (float *)base, *od = (float *)((char *)base + x_room);
+    if (cudaMemcpyAsync(xd, x_host, xb, cudaMemcpyHostToDevice, st) != cudaSuccess) return FINCH_E_CUDA;
+    SpecPack pack;
+    pack.n = 1;
+    pack.s[0] = Spec{(const uint8_t *)w->W, (const uint16_t *)w->scales, (const uint16_t *)w->biases, od, w->out_dim, w->in_dim, w->bits,
+                     w->scale_dtype};
+    batch_matvec_kernel<<<dim3((w->out_dim + 3) / 4, 1), 128, 0, st>>>(pack, xd, FINCH_F32, M);
+    if (cudaGetLastError() != cudaSuccess) return FINCH_E_CUDA;
+    if (cudaMemcpyAsync(out_host, od, ob, cudaMemcpyDeviceToHost, st) != cudaSuccess) return FINCH_E_CUDA;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return FINCH_E_CUDA;
+    return FINCH_OK;
+}

@@ -62,6 +62,7 @@ _PROTOS = {
     "finch_pool_get_stats": (_i, [_vp, C.POINTER(PoolStats)]),
     "finch_pool_fill_synthetic": (_i, [_vp, _i, _i, C.c_uint64]),
     "finch_matvec": (_i, [_vp, C.POINTER(WDesc), _vp, _vp, _i]),
+    "finch_matvec_noalloc": (_i, [C.POINTER(WDesc), _vp, _vp, _i, _vp]),
     "finch_encode_batch_matvec": (_i, [_vp, _vp, _vp, _i, C.POINTER(WDesc), C.POINTER(_vp), _i, _i]),
     "finch_encode_route_topk": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _i]),
     "finch_encode_moe_decode": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, C.POINTER(Shared), _vp, _vp, _i]),

@@ -140,6 +140,22 @@ typedef struct finch_wdesc {
  * x and out are HOST fp32 arrays ([M][in_dim], [M][out_dim]); synchronous. */
 FINCH_API int finch_matvec(finch_ctx *ctx, const finch_wdesc *w, const float *x_host, float *out_host, int M);
 
+/* The same matvec for callers that must not allocate device memory: code that
+ * runs inside somebody else's memory budget or allocator (an engine that has
+ * handed all of HBM to its own pool, a plugin host that forbids cudaMalloc in
+ * callbacks, a latency-critical thread where an allocation could block on the
+ * driver).  It needs no context.  x and out (HOST fp32, [M][in_dim] and
+ * [M][out_dim]) are staged through a fixed 512 KiB buffer that is part of the
+ * library image, so M * (in_dim + out_dim) floats must fit in it; larger calls
+ * return FINCH_E_UNSUPPORTED.  The weights are device pointers as above and
+ * must live on the current device.  The first call made on a device looks up
+ * the buffer's device address; make that first call before starting any
+ * stream capture.  All calls share the one buffer: calls that overlap on the
+ * GPU (different streams or threads) overwrite each other's data.  Nothing in
+ * the buffer has to start out zeroed.  Synchronous: returns when out is
+ * written.  This entry point has no counterpart in the reference. */
+FINCH_API int finch_matvec_noalloc(const finch_wdesc *w, const float *x_host, float *out_host, int M, finch_stream stream);
+
 /* fast_batch_matvec / gpu_encode_batch_matvec / routing_batch_fused and
  * gpu_encode_prefill_matvec (finchmoe/infer.m:4477, 3528, 9061, 3672): n
  * matvecs of mixed bit width sharing one input x[M][in_dim] (device, element
