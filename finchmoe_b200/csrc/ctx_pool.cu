@@ -2,6 +2,7 @@
 // events and the synthetic pool fill used by the benchmark.
 #include <algorithm>
 #include <chrono>
+#include <cstdlib>
 #include <thread>
 
 #include "finch_internal.cuh"
@@ -49,6 +50,7 @@ extern "C" int finch_ctx_create(const finch_config *cfg, finch_ctx **out) {
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || c.device < 0 || c.device >= ndev) return FINCH_E_CUDA;
     finch_ctx *ctx = new finch_ctx();
     ctx->cfg = c;
+    ctx->no_pdl = getenv("FINCH_NO_PDL") && getenv("FINCH_NO_PDL")[0] == '1';
     auto bail = [&](int code) {
         finch_ctx_destroy(ctx);
         return code;

@@ -30,6 +30,7 @@ struct finch_ctx {
     int *dev_status = nullptr;      // sticky device status word
     void *frag_scratch = nullptr;   // tensor-core operand fragments + expert-group table (moe_decode.cu)
     void *dbg = nullptr;            // finch_debug_timing buffer
+    bool no_pdl = false;            // FINCH_NO_PDL=1 in the environment: plain stream-ordered launches
     struct SharedPrepared {
         const void *key[3];
         void *tiles;
@@ -129,7 +130,7 @@ __device__ __forceinline__ void finch_mbar_expect_tx(uint64_t *bar, unsigned byt
 // Bounded wait: returns false when the phase did not complete within the limit.
 __device__ __forceinline__ bool finch_mbar_wait(uint64_t *bar, unsigned parity) {
     const uint32_t a = finch_smem_u32(bar);
-    for (unsigned it = 0; it < (1u << 22); ++it) {
+    for (unsigned it = 0; it < (1u << 17); ++it) {  // legitimate waits are microseconds; this bound is a fraction of a second
         unsigned done;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"

@@ -40,7 +40,7 @@
 namespace {
 
 constexpr int TEAM_A = 4;                   // warps that split the K dimension of one gate/up tile
-constexpr int NTEAM_A = 4;
+constexpr int NTEAM_A = 6;
 constexpr int CW_A = TEAM_A * NTEAM_A;      // consumer warps of kernel A
 constexpr int NT_A = (CW_A + 1) * 32;       // + one producer warp
 constexpr int CW_B = 16;
@@ -124,6 +124,15 @@ __device__ __forceinline__ void extract4(uint32_t w, uint32_t (&e)[4]) {
     e[0] = w & 0x000F000Fu; e[1] = w & 0x00F000F0u;
     e[2] = v & 0x000F000Fu; e[3] = v & 0x00F000F0u;
 }
+
+// Programmatic dependent launch: the kernels of a call are launched so that each may start while
+// its predecessor drains; nothing written by the predecessor may be read before this returns.
+__device__ __forceinline__ long long gtime() {
+    long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ float pow2_biased(int e) { return __uint_as_float((uint32_t)e << 23); }
 __device__ __forceinline__ void bar_sync(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
@@ -407,31 +416,51 @@ __device__ __forceinline__ bool pair_ok(const MoeArgs &a, int p) {
     return a.slot_row[e] >= 0;
 }
 
-// Builds the group table in shared memory.  Run by threads 0..nthreads-1
-// (nthreads >= 64) sharing named barrier `bar`.  Groups are numbered by their
-// first pair; pairs inside a group ascend.
-__device__ void build_groups(const MoeArgs &a, GroupTab *T, int *sm_ids, unsigned char *sm_first, int bar, int nthreads) {
-    const int tid = threadIdx.x;
-    if (tid < MAXP) sm_ids[tid] = (tid < a.P && pair_ok(a, tid)) ? a.ids[tid] : -1;
+// Builds the group table in shared memory.  Run by threads 0..nthreads-1 (nthreads >= 64, whole
+// warps) sharing named barrier `bar`; the first two warps hold one pair per lane.  Groups are
+// numbered by their first pair; pairs inside a group ascend.  sm_ids: MAXP + 2 ints.
+__device__ void build_groups(const MoeArgs &a, GroupTab *T, int *sm_ids, unsigned char *sm_rank, int bar, int nthreads) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int id = -1, slot = -1;
+    if (tid < a.P && (!a.valid || a.valid[tid])) {
+        const int e = a.ids[tid];
+        if (e >= 0 && e < a.n_experts) {
+            slot = a.slot_row[e];
+            if (slot >= 0) id = e;
+        }
+    }
+    if (tid < MAXP) sm_ids[tid] = id;
     bar_sync(bar, nthreads);
+    unsigned same = 0, other = 0, fb = 0;
+    bool first = false;
     if (tid < MAXP) {
-        bool first = sm_ids[tid] >= 0;
-        for (int j = 0; j < tid && first; j++) first = sm_ids[j] != sm_ids[tid];
-        sm_first[tid] = first;
+        same = __match_any_sync(0xffffffffu, id);                 // lanes of my warp with my expert
+        const int *o = sm_ids + 32 * (warp ^ 1);
+        for (int j = 0; j < 32; j++) other |= (unsigned)(o[j] == id) << j;   // lanes of the other warp
+        const unsigned lt = (1u << lane) - 1u;
+        first = id >= 0 && !(same & lt) && (warp == 0 || other == 0);
+        fb = __ballot_sync(0xffffffffu, first);
+        if (lane == 0) sm_ids[MAXP + warp] = (int)fb;
     }
     bar_sync(bar, nthreads);
     if (tid < MAXP) {
-        int rank = 0;
-        for (int j = 0; j < tid; j++) rank += sm_first[j];
-        if (sm_first[tid]) {
-            const int id = sm_ids[tid];
-            int m = 0;
-            for (int j = tid; j < a.P && m < MAXM; j++)
-                if (sm_ids[j] == id) T->pairs[rank][m++] = (unsigned char)j;
-            T->m[rank] = (unsigned char)m;
-            T->slot[rank] = a.slot_row[id];
+        const unsigned lt = (1u << lane) - 1u;
+        const int before = warp == 1 ? __popc((unsigned)sm_ids[MAXP]) : 0;
+        if (first) sm_rank[tid] = (unsigned char)(before + __popc(fb & lt));
+        if (tid == 0) T->ng = __popc((unsigned)sm_ids[MAXP]) + __popc((unsigned)sm_ids[MAXP + 1]);
+    }
+    bar_sync(bar, nthreads);
+    if (tid < MAXP && id >= 0) {
+        const unsigned lt = (1u << lane) - 1u;
+        const int fp = (warp == 1 && other) ? __ffs(other) - 1 : 32 * warp + __ffs(same) - 1;   // first pair of my group
+        const int gi = sm_rank[fp];
+        const int pos = (warp == 1 ? __popc(other) : 0) + __popc(same & lt);
+        if (pos < MAXM) T->pairs[gi][pos] = (unsigned char)tid;
+        if (first) {
+            const int m = __popc(same) + __popc(other);
+            T->m[gi] = (unsigned char)(m < MAXM ? m : MAXM);
+            T->slot[gi] = slot;
         }
-        if (tid == MAXP - 1) T->ng = rank + sm_first[tid];
     }
     bar_sync(bar, nthreads);
 }
@@ -444,17 +473,22 @@ __device__ void build_groups(const MoeArgs &a, GroupTab *T, int *sm_ids, unsigne
 // groups a CTA touches few: few act records to prepare, few counters to bump.
 __device__ __forceinline__ int npass_of(const GroupTab *tab, int gi) { return (tab->m[gi] + 1) >> 1; }
 
-__device__ int job_at(const GroupTab *tab, int per_group, int n_sh, int nps, long long target) {
-    long long base = 0;
-    const int ng = tab->ng;
-    for (int gi = 0; gi < ng; gi++) {
-        const int np = npass_of(tab, gi);
-        const long long gc = (long long)per_group * np;
-        if (target < base + gc) return gi * per_group + (int)((target - base + np - 1) / np);
-        base += gc;
+// pre[gi] = passes of the groups before gi (32-bit: at most 64 groups x 4 passes).  The job whose
+// cost interval starts at or after `target` (cost units: tile-passes).
+__device__ int job_at(const int *pre, int ng, int per_group, int n_sh, int nps, int target) {
+    const int routed_cost = pre[ng] * per_group;
+    if (target >= routed_cost) {
+        if (n_sh > 0 && target < routed_cost + n_sh * nps) return ng * per_group + (target - routed_cost + nps - 1) / nps;
+        return ng * per_group + n_sh;
     }
-    if (n_sh > 0 && target < base + (long long)n_sh * nps) return ng * per_group + (int)((target - base + nps - 1) / nps);
-    return ng * per_group + n_sh;
+    int lo = 0, hi = ng - 1;   // last group whose first job starts at or before target
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (pre[mid] * per_group <= target) lo = mid;
+        else hi = mid - 1;
+    }
+    const int gi = lo, np = pre[gi + 1] - pre[gi];
+    return gi * per_group + (target - pre[gi] * per_group + np - 1) / np;
 }
 
 // ============================ prep ========================================
@@ -465,9 +499,12 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(const MoeArgs a) {
     float *hdr = xs + a.hidden;              // [hidden/64 + 1]
     float *warp_max = hdr + 144;
     int *sm_ids = reinterpret_cast<int *>(warp_max + 8);
-    unsigned char *sm_first = reinterpret_cast<unsigned char *>(sm_ids + MAXP);
-    GroupTab *T = reinterpret_cast<GroupTab *>(sm_first + MAXP);
+    unsigned char *sm_first = reinterpret_cast<unsigned char *>(sm_ids + MAXP + 2);
+    GroupTab *T = reinterpret_cast<GroupTab *>(sm_first + MAXP + 8);
     const int b = blockIdx.x, tid = threadIdx.x, K = a.hidden;
+    const long long gt0 = gtime();
+    grid_dep_wait();
+    if (a.dbg && tid == 0) a.dbg[(size_t)(1300 + b) * 8] = gt0, a.dbg[(size_t)(1300 + b) * 8 + 1] = gtime();
     if (b < a.B) {
         const void *src = a.act_dtype == FINCH_BF16 ? (const void *)((const uint16_t *)a.h_post + (size_t)b * K)
                                                      : (const void *)((const float *)a.h_post + (size_t)b * K);
@@ -478,6 +515,7 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(const MoeArgs a) {
         if (a.has_shared) build_frag4<256>(xs, K, E, reinterpret_cast<uint2 *>(a.xrec4 + (size_t)b * frag4_bytes(K)));
         float *gh = reinterpret_cast<float *>(rec + frag3_bytes(K));
         for (int i = tid; i <= K / 64; i += 256) gh[i] = hdr[i];
+        if (a.dbg && tid == 0) a.dbg[(size_t)(1300 + b) * 8 + 2] = gtime();
         return;
     }
     build_groups(a, T, sm_ids, sm_first, 0, 256);
@@ -485,17 +523,34 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(const MoeArgs a) {
     const FinchTile L3 = finch_tile(a.hidden, a.inter);
     const int nps = (a.B + 1) / 2;
     const int n_sh_a = a.has_shared ? a.sh_inter / 4 : 0, n_sh_b = a.has_shared ? L3.nTB : 0;
-    long long Ca = (long long)n_sh_a * nps, Cb = (long long)n_sh_b * nps;
-    for (int gi = 0; gi < T->ng; gi++) {
-        Ca += (long long)L3.nTA * npass_of(T, gi);
-        Cb += (long long)L3.nTB * npass_of(T, gi);
+    int *pre = sm_ids;  // the pair ids are no longer needed: reuse as prefix sums of the groups' passes
+    const int ng = T->ng;
+    if (tid < 64) {   // exclusive scan of the per-group pass counts over two warps
+        const int lane = tid & 31, np = tid < ng ? npass_of(T, tid) : 0;
+        int inc = np;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += v;
+        }
+        if (tid == 31) pre[MAXP + 1] = inc;   // total of the first warp
+        __syncwarp();
+        pre[tid] = inc - np;
+        if (tid == 63) pre[MAXP] = inc;
     }
-    for (int i = tid; i <= a.grid_a; i += 256) T->range_a[i] = job_at(T, L3.nTA, n_sh_a, nps, Ca * i / a.grid_a);
-    for (int i = tid; i <= a.grid_b; i += 256) T->range_b[i] = job_at(T, L3.nTB, n_sh_b, nps, Cb * i / a.grid_b);
+    __syncthreads();
+    if (tid >= 32 && tid < 65) pre[tid] += pre[MAXP + 1];   // tid 64 fixes up the grand total in pre[MAXP]
+    __syncthreads();
+    const int Ca = pre[ng] * L3.nTA + n_sh_a * nps, Cb = pre[ng] * L3.nTB + n_sh_b * nps;
+    for (int i = tid; i <= a.grid_a; i += 256)
+        T->range_a[i] = job_at(pre, ng, L3.nTA, n_sh_a, nps, (int)((long long)Ca * i / a.grid_a));
+    for (int i = tid; i <= a.grid_b; i += 256)
+        T->range_b[i] = job_at(pre, ng, L3.nTB, n_sh_b, nps, (int)((long long)Cb * i / a.grid_b));
     __syncthreads();
     const int *s = reinterpret_cast<const int *>(T);
     int *d = reinterpret_cast<int *>(a.gtab);
     for (int i = tid; i < (int)(sizeof(GroupTab) / 4); i += 256) d[i] = s[i];
+    if (a.dbg && tid == 0) a.dbg[(size_t)(1300 + b) * 8 + 2] = gtime();
 }
 
 // Re-tiles a shared expert from the reference tensor layout into FinchTile4 tiles (run once per
@@ -569,9 +624,9 @@ __host__ __device__ inline SmemA smem_a_layout(int hidden, int inter, int sh_int
 // A team takes whole tiles; its warps split the K dimension and one of them adds the partial sums.
 __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const long long tk0 = clock64();
-    const int S = a.stages_a;
-    const SmemA L = smem_a_layout(a.hidden, a.inter, a.sh_inter, a.B, a.has_shared, S);
+    const long long tk0 = clock64(), gt0 = gtime();
+    const int Smax = a.stages_a;
+    const SmemA L = smem_a_layout(a.hidden, a.inter, a.sh_inter, a.B, a.has_shared, Smax);
     const FinchTile T = finch_tile(a.hidden, a.inter);
     const FinchTile4 T4 = finch_tile4(a.hidden, a.sh_inter);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
@@ -583,28 +638,37 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
     const int K = a.hidden, groups = K / 64, I = a.sh_inter;
     const int f4b = frag4_bytes(K);
 
+    if (tid < 32) reinterpret_cast<int *>(smem + L.qcnt)[tid] = 0;
+    if (tid == 0) {
+        empty[32] = 0ull;
+        for (int s = 0; s < Smax; s++) {
+            finch_mbar_init(full + s, 1);
+            finch_mbar_init(empty + s, TEAM_A);
+        }
+        finch_mbar_init(xbar, 1);
+    }
+    grid_dep_wait();  // everything above overlaps the tail of the preparation kernel
     {
         const int *s = reinterpret_cast<const int *>(a.gtab);
         int *d = reinterpret_cast<int *>(tab);
         for (int i = tid; i < (int)(sizeof(GroupTab) / 4); i += NT_A) d[i] = __ldcg(s + i);
     }
-    if (tid < 32) reinterpret_cast<int *>(smem + L.qcnt)[tid] = 0;
+    // A CTA whose range reaches into the shared-expert jobs keeps the 4-bit-layout fragments of every
+    // token in shared memory too: it gives up the last stages of its ring for them.
+    const int n_routed = __ldcg(&a.gtab->ng) * T.nTA;
+    const int job0 = __ldcg(&a.gtab->range_a[blockIdx.x]), job1 = __ldcg(&a.gtab->range_a[blockIdx.x + 1]);
+    const int n4x = (a.has_shared && job1 > n_routed && job1 > job0) ? a.B - L.n4 : 0;   // tokens beyond the fixed area
+    const int tail_off = L.stage + Smax * L.stg - n4x * L.f4s;
+    const int S = (Smax * L.stg - n4x * L.f4s) / L.stg;
     if (tid == 0) {
-        empty[32] = 0ull;
-        for (int s = 0; s < S; s++) {
-            finch_mbar_init(full + s, 1);
-            finch_mbar_init(empty + s, TEAM_A);
-        }
-        finch_mbar_init(xbar, 1);
         // operand records of the tokens: one bulk copy each, ready long before the first tile is
-        finch_mbar_expect_tx(xbar, (unsigned)(a.B * L.rx3 + L.n4 * f4b));
+        finch_mbar_expect_tx(xbar, (unsigned)(a.B * L.rx3 + (L.n4 + n4x) * f4b));
         for (int b = 0; b < a.B; b++) finch_bulk_g2s(smem + L.rec + b * L.rx3, a.xrec3 + (size_t)b * L.rx3, L.rx3, xbar);
         for (int b = 0; b < L.n4; b++) finch_bulk_g2s(smem + L.rec4 + b * L.f4s, a.xrec4 + (size_t)b * f4b, f4b, xbar);
+        for (int b = 0; b < n4x; b++) finch_bulk_g2s(smem + tail_off + b * L.f4s, a.xrec4 + (size_t)(L.n4 + b) * f4b, f4b, xbar);
     }
     __syncthreads();
     const long long tk1 = clock64();
-    const int n_routed = tab->ng * T.nTA;
-    const int job0 = tab->range_a[blockIdx.x], job1 = tab->range_a[blockIdx.x + 1];
 
     if (warp == CW_A) {
         // ---------------- producer warp: one bulk copy per job ----------------
@@ -642,7 +706,11 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
     const long long tk2 = clock64();
     long long wait_acc = 0;
     int njobs = 0;
-    for (int it = team; job0 + it < job1; it += NTEAM_A, ++njobs) {
+    // A warp may only wait for the n-th fill of a stage once the (n-1)-th has landed (a barrier that has
+    // not completed a phase yet reports the phase before it as complete).  With at least as many stages
+    // as teams that holds by construction; a CTA with fewer stages lets its surplus teams sit out.
+    const int nteam = NTEAM_A < S ? NTEAM_A : S;
+    for (int it = team; team < nteam && job0 + it < job1; it += nteam, ++njobs) {
         const int job = job0 + it, st = it % S, use = it / S;
         const long long w0 = clock64();
         if (!finch_mbar_wait(full + st, use & 1)) {
@@ -672,10 +740,8 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
             } else {
                 // shared expert gate/up tile: 4 gate rows + 4 up rows, every token, two per pass
                 const int tok0 = 2 * ps, tok1 = 2 * ps + (ntok > 1);
-                const uint2 *f0 = tok0 < L.n4 ? reinterpret_cast<const uint2 *>(smem + L.rec4 + tok0 * L.f4s)
-                                              : reinterpret_cast<const uint2 *>(a.xrec4 + (size_t)tok0 * f4b);
-                const uint2 *f1 = tok1 < L.n4 ? reinterpret_cast<const uint2 *>(smem + L.rec4 + tok1 * L.f4s)
-                                              : reinterpret_cast<const uint2 *>(a.xrec4 + (size_t)tok1 * f4b);
+                const uint2 *f0 = reinterpret_cast<const uint2 *>(smem + (tok0 < L.n4 ? L.rec4 + tok0 * L.f4s : tail_off + (tok0 - L.n4) * L.f4s));
+                const uint2 *f1 = reinterpret_cast<const uint2 *>(smem + (tok1 < L.n4 ? L.rec4 + tok1 * L.f4s : tail_off + (tok1 - L.n4) * L.f4s));
                 gemv4_tile(tile, groups, kw, TEAM_A, (g & 3) * 4 + t, 16, g & 3, 4, a.sh_scale_dtype, f0, f1,
                            reinterpret_cast<const float *>(smem + L.rec + tok0 * L.rx3 + frag3_bytes(K)),
                            reinterpret_cast<const float *>(smem + L.rec + tok1 * L.rx3 + frag3_bytes(K)), zero8, ntok, vA, vB);
@@ -718,8 +784,8 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
         d[1] = tk2 - tk1;           // waiting for the token records
         d[2] = clock64() - tk2;     // job loop of team 0
         d[3] = wait_acc;            // ... of which waiting for a full stage
-        d[4] = 0;
-        d[5] = 0;
+        d[4] = gt0;
+        d[5] = gtime();
         d[6] = njobs;
         d[7] = job1 - job0;
     }
@@ -749,7 +815,7 @@ __host__ __device__ inline SmemB smem_b_layout(int hidden, int inter, int sh_int
 // grid: one CTA per SM (persistent); block: CW_B consumer warps + 1 producer warp.
 __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const long long tk0 = clock64();
+    const long long tk0 = clock64(), gt0 = gtime();
     const int S = a.stages_b;
     const SmemB L = smem_b_layout(a.hidden, a.inter, a.sh_inter, a.B, a.has_shared, S);
     const FinchTile T = finch_tile(a.hidden, a.inter);
@@ -761,17 +827,18 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
     const int K = a.inter, Ks = a.sh_inter;
     const int r3b = rec3_bytes(K), r4b = rec4_bytes(Ks);
 
-    {
-        const int *s = reinterpret_cast<const int *>(a.gtab);
-        int *d = reinterpret_cast<int *>(tab);
-        for (int i = tid; i < (int)(sizeof(GroupTab) / 4); i += NT_B) d[i] = __ldcg(s + i);
-    }
     if (tid == 0) {
         empty[32] = 0ull;
         for (int s = 0; s < S; s++) {
             finch_mbar_init(full + s, 1);
             finch_mbar_init(empty + s, 1);
         }
+    }
+    grid_dep_wait();  // the barrier set-up overlaps the tail of the gate/up kernel
+    {
+        const int *s = reinterpret_cast<const int *>(a.gtab);
+        int *d = reinterpret_cast<int *>(tab);
+        for (int i = tid; i < (int)(sizeof(GroupTab) / 4); i += NT_B) d[i] = __ldcg(s + i);
     }
     __syncthreads();
     const long long tk1 = clock64();
@@ -878,8 +945,8 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
         d[1] = tk2 - tk1;   // act records
         d[2] = tk3 - tk2;   // job loop of warp 0
         d[3] = wait_acc;    // ... of which waiting for a full stage
-        d[4] = tk4 - tk3;   // fence + arrival atomics
-        d[5] = clock64() - tk4;  // combine
+        d[4] = gt0;
+        d[5] = gtime();
         d[6] = njobs;
         d[7] = job1 - job0;
     }
@@ -892,6 +959,8 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const MoeArgs a) {
     __shared__ int ok[8];
     __shared__ float wk[8];
     const int b = blockIdx.y, row = blockIdx.x * 256 + threadIdx.x;
+    const long long gt0 = gtime();
+    grid_dep_wait();
     if (threadIdx.x < a.K) {
         ok[threadIdx.x] = pair_ok(a, b * a.K + threadIdx.x);
         wk[threadIdx.x] = a.weights[b * a.K + threadIdx.x];
@@ -908,6 +977,11 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const MoeArgs a) {
         h = fmaf(sg, a.partial[(size_t)(a.P + b) * a.hidden + row], h);
     }
     a.hidden_out[(size_t)b * a.hidden + row] = h;
+    if (a.dbg && threadIdx.x == 0) {
+        long long *d = a.dbg + (size_t)(1400 + blockIdx.y * gridDim.x + blockIdx.x) * 8;
+        d[0] = gt0;
+        d[1] = gtime();
+    }
 }
 
 constexpr int SMEM_MAX = 227 * 1024;
@@ -1042,12 +1116,16 @@ extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finc
     int sa = (SMEM_MAX - A0.total) / (A0.stg + (MAXM / 2) * TEAM_A * 32 * 4), sb = (SMEM_MAX - B0.total) / B0.stg;
     sa = sa > 32 ? 32 : sa;
     sb = sb > 32 ? 32 : sb;
-    if (sa < 2 || sb < 2) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "dims need too much shared memory");
+    {  // CTAs that also run shared-expert jobs give some stages up for the 4-bit-layout fragments of the tokens
+        const int extra = a.has_shared ? (B - A0.n4) * A0.f4s : 0;
+        if (sa >= 2 && (sa * A0.stg - extra) / A0.stg < 2) sa = 0;
+    }
+    if (sa < 2 || sb < CW_B) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "dims need too much shared memory");
     a.stages_a = sa;
     a.stages_b = sb;
     const SmemA LA = smem_a_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, sa);
     const SmemB LB = smem_b_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, sb);
-    const int prep_smem = c.hidden * 4 + 144 * 4 + 32 + MAXP * 4 + MAXP + (int)sizeof(GroupTab) + 64;
+    const int prep_smem = c.hidden * 4 + 144 * 4 + 32 + (MAXP + 2) * 4 + MAXP + 8 + (int)sizeof(GroupTab) + 64;
     if (!g_attr_set) {
         FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
         FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_down_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
@@ -1070,16 +1148,28 @@ extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finc
         pe = &ctx->prof_events[ctx->prof_used];
         ctx->prof_used += 3;
     }
-    moe_prep_kernel<<<B + 1, 256, prep_smem, st>>>(a);
-    FINCH_CUDA_OK(ctx, cudaGetLastError());
+    // Launched with programmatic stream serialization: a kernel may be scheduled while its predecessor
+    // drains and runs its prologue up to griddepcontrol.wait, which hides most of the launch latency.
+    auto launch = [&](const void *fn, dim3 g, int threads, size_t smem_bytes) -> cudaError_t {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = g;
+        cfg.blockDim = dim3(threads);
+        cfg.dynamicSmemBytes = smem_bytes;
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = ctx->no_pdl ? 0 : 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        void *args[] = {(void *)&a};
+        return cudaLaunchKernelExC(&cfg, fn, args);
+    };
+    FINCH_CUDA_OK(ctx, launch((const void *)moe_prep_kernel, dim3(B + 1), 256, prep_smem));
     if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[0], st));
-    moe_gateup_kernel<<<grid, NT_A, LA.total, st>>>(a);
-    FINCH_CUDA_OK(ctx, cudaGetLastError());
+    FINCH_CUDA_OK(ctx, launch((const void *)moe_gateup_kernel, dim3(grid), NT_A, LA.total));
     if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[1], st));
-    moe_down_combine_kernel<<<grid, NT_B, LB.total, st>>>(a);
-    FINCH_CUDA_OK(ctx, cudaGetLastError());
-    moe_combine_kernel<<<dim3((c.hidden + 255) / 256, B), 256, 0, st>>>(a);
-    FINCH_CUDA_OK(ctx, cudaGetLastError());
+    FINCH_CUDA_OK(ctx, launch((const void *)moe_down_combine_kernel, dim3(grid), NT_B, LB.total));
+    FINCH_CUDA_OK(ctx, launch((const void *)moe_combine_kernel, dim3((c.hidden + 255) / 256, B), 256, 0));
     if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[2], st));
     ctx->launches += 4;
     return FINCH_OK;
