@@ -99,13 +99,19 @@ __host__ __device__ inline int hdr_bytes(int K) { return ((K / 64 + 1 + 15) / 16
 __host__ __device__ inline int rec3_bytes(int K) { return frag3_bytes(K) + hdr_bytes(K); }
 __host__ __device__ inline int rec4_bytes(int K) { return frag4_bytes(K) + hdr_bytes(K); }
 
-// slot-in-register tables of the 3-bit extraction: entry [2*e + half] for
-// extraction e (0..17) = code index inside the 32-code period (-1: empty) and
-// the bit position p of the code inside its half-word.
-__constant__ int8_t c_idx3[36] = {0, 6, 1, 7, 2, -1, 3, 8, 4, 9, 5, 10, 11, 16, 12, 17, 13, 18,
-                                  14, 19, 15, 20, -1, 21, 22, 27, 23, 28, -1, 29, 24, 30, 25, 31, 26, -1};
-__constant__ int8_t c_pos3[36] = {0, 2, 3, 5, 6, 0, 1, 0, 4, 3, 7, 6, 1, 0, 4, 3, 7, 6,
-                                  2, 1, 5, 4, 0, 7, 2, 1, 5, 4, 0, 7, 0, 2, 3, 5, 6, 0};
+// Slot tables of the 3-bit extraction.  Extraction e (0..17, see extract3) yields a register with one
+// code in each 16-bit half; MMA j uses extractions 2j and 2j+1, i.e. four slots 4j..4j+3.  Slot s holds
+// code number idx (0..31) of the 32-code period at bit position pos of its half, or is empty:
+//   idx: 0 6 1 7 | 2 - 3 8 | 4 9 5 10 | 11 16 12 17 | 13 18 14 19 | 15 20 - 21 | 22 27 23 28 | - 29 24 30 | 25 31 26 -
+//   pos: 0 2 3 5 | 6 0 1 0 | 4 3 7 6  | 1 0 4 3     | 7 6 2 1     | 5 4 0 7   | 2 1 5 4     | 0 7 0 2   | 3 5 6 0
+// They are packed into immediates (one byte idx | pos << 5 per slot, empty slots flagged in a bit mask) so
+// that a thread gets the four slots of its MMA without touching memory.
+__device__ __forceinline__ uint32_t slots3_of(int j) {
+    const unsigned long long w = j < 2 ? 0x082300c2a7614600ull : j < 4 ? 0x718c102bcae56984ull : j < 6 ? 0xf50094af334ed2edull
+                               : j < 8 ? 0x5e18fd009cb73b56ull : 0x0000000000dabf79ull;
+    return (uint32_t)(w >> (32 * (j & 1)));
+}
+__device__ __forceinline__ uint32_t empty3_of(int j) { return (uint32_t)(0x810400020ull >> (4 * j)) & 15u; }
 
 __device__ __forceinline__ void extract3(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t (&e)[18]) {
     const uint32_t v1 = __funnelshift_r(w0, w1, 8), v3 = __funnelshift_r(w1, w2, 8), v5 = w2 >> 8;
@@ -212,23 +218,38 @@ __device__ __forceinline__ void split4(const float (&xv)[4], uint2 &hi, uint2 &l
 }
 
 // B fragments of one token, 3-bit layout: frag[((u * 9 + j) * 2 + term) * 4 + t].
-// frag may be shared or global memory.
+// frag may be shared or global memory.  Thread `first` of `stride` (stride >= 32) cooperating threads.
+// A thread keeps one (j, t) position of the 9 x 4 entries of a unit and walks the units, so the slots
+// are decoded once per thread, not once per entry.
 __device__ __forceinline__ void build_frag3_range(const float *xs, int K, int E, uint2 *frag, int first, int stride) {
-    const int entries = (K / 128) * 36;
-    for (int e = first; e < entries; e += stride) {
-        const int u = e / 36, r = e - u * 36, j = r >> 2, t = r & 3;
-        float xv[4];
+    const int units = K / 128;
+    const int ulanes = stride >= 36 ? stride / 36 : 1;       // threads side by side along the units
+    const int rounds = stride >= 36 ? 1 : 2;                 // a single warp covers the 36 positions in two rounds
+    for (int rd = 0; rd < rounds; rd++) {
+        const int jt = stride >= 36 ? first % 36 : first + 32 * rd;
+        const int u0 = stride >= 36 ? first / 36 : 0;
+        if (jt >= 36 || u0 >= ulanes) continue;
+        const int j = jt >> 2, t = jt & 3;
+        int idx[4];
+        float mul[4];
+        const uint32_t slots = slots3_of(j), hole = empty3_of(j);
 #pragma unroll
         for (int s = 0; s < 4; s++) {
-            const int ti = (2 * j + (s >> 1)) * 2 + (s & 1);
-            const int idx = c_idx3[ti];
-            xv[s] = idx < 0 ? 0.f : xs[u * 128 + t * 32 + idx] * pow2_biased(261 - E - c_pos3[ti]);
+            const uint32_t b = (slots >> (8 * s)) & 255u;
+            idx[s] = (int)(b & 31u);
+            mul[s] = ((hole >> s) & 1u) ? 0.f : pow2_biased(261 - E - (int)(b >> 5));
         }
-        uint2 hi, lo;
-        split4(xv, hi, lo);
-        const int o = (u * 9 + j) * 8 + t;
-        frag[o] = hi;
-        frag[o + 4] = lo;
+#pragma unroll 4
+        for (int u = u0; u < units; u += ulanes) {
+            float xv[4];
+#pragma unroll
+            for (int s = 0; s < 4; s++) xv[s] = mul[s] == 0.f ? 0.f : xs[u * 128 + t * 32 + idx[s]] * mul[s];
+            uint2 hi, lo;
+            split4(xv, hi, lo);
+            const int o = (u * 9 + j) * 8 + t;
+            frag[o] = hi;
+            frag[o + 4] = lo;
+        }
     }
 }
 
@@ -263,11 +284,14 @@ __device__ __forceinline__ void build_frag4(const float *xs, int K, int E, uint2
 
 // One warp turns K fp32 values at src (global memory written by an earlier
 // launch) into an operand record (shared or global memory).  BITS selects the layout.
+// stage: K floats of shared memory private to the warp, or NULL; with it the scattered reads of the
+// second pass come from shared memory instead of paying an L2 round trip each.
 template <int BITS>
-__device__ void warp_make_record(const float *src, int K, uint8_t *rec) {
+__device__ void warp_make_record(const float *src, int K, uint8_t *rec, float *stage = nullptr) {
     const int lane = threadIdx.x & 31;
     float *hdr = reinterpret_cast<float *>(rec + (BITS == 3 ? frag3_bytes(K) : frag4_bytes(K)));
     float amax = 0.f;
+#pragma unroll 4
     for (int base = lane * 8; base < K; base += 256) {  // K is a multiple of 64, so a warp never splits a group
         const float4 a = __ldcg(reinterpret_cast<const float4 *>(src + base));
         const float4 b = __ldcg(reinterpret_cast<const float4 *>(src + base + 4));
@@ -280,6 +304,10 @@ __device__ void warp_make_record(const float *src, int K, uint8_t *rec) {
         s += __shfl_xor_sync(mask, s, 2);
         s += __shfl_xor_sync(mask, s, 4);
         if ((lane & 7) == 0) hdr[base >> 6] = s;
+        if (stage) {
+            *reinterpret_cast<float4 *>(stage + base) = a;
+            *reinterpret_cast<float4 *>(stage + base + 4) = b;
+        }
     }
     __syncwarp();
 #pragma unroll
@@ -288,9 +316,9 @@ __device__ void warp_make_record(const float *src, int K, uint8_t *rec) {
     E = E < 30 ? 30 : (E > 230 ? 230 : E);
     if (lane == 0) hdr[K / 64] = __int_as_float(E);
     __syncwarp();
-    // second pass: the scattered reads hit the lines the first pass just brought in
-    if (BITS == 3) build_frag3_range(src, K, E, reinterpret_cast<uint2 *>(rec), lane, 32);
-    else build_frag4_range(src, K, E, reinterpret_cast<uint2 *>(rec), lane, 32);
+    const float *xs = stage ? stage : src;
+    if (BITS == 3) build_frag3_range(xs, K, E, reinterpret_cast<uint2 *>(rec), lane, 32);
+    else build_frag4_range(xs, K, E, reinterpret_cast<uint2 *>(rec), lane, 32);
     __syncwarp();
 }
 
@@ -303,30 +331,58 @@ __device__ __forceinline__ void mma16816_z(float (&d)[4], uint32_t a0, uint32_t 
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
 }
 
-// 3-bit tile (tile_layout.h) against up to two tokens.  tile: shared memory; frag0 / frag1 and the
-// headers h0 / h1 (group sums, E): operand records of the two tokens (any address space); zero: an
-// 8-byte zero entry in shared memory.  On return lane (g, t), t even, holds for token slot t>>1 the
-// dot products resA (fragment row g) and resB (row g + 8), bias included, over units u0, u0 + ustep, ...
+// Shared-memory loads with a 32-bit address and an immediate offset: the inner loops keep a few running
+// addresses and spend no instructions on address arithmetic per load.
+template <int OFF>
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2+%3];" : "=r"(v.x), "=r"(v.y) : "r"(addr), "n"(OFF));
+    return v;
+}
+template <int OFF>
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4+%5];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr), "n"(OFF));
+    return v;
+}
+__device__ __forceinline__ float lds32f(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
+}
+constexpr int ZERO3_BYTES = 640;   // zeroed shared memory a lane with a structurally zero B column reads instead of a record
+
+// 3-bit tile (tile_layout.h) against up to two tokens.  Everything is in shared memory: the tile, the
+// operand records of the two tokens (frag0 / frag1 with their headers h0 / h1 = group sums, E) and
+// `zero`, ZERO3_BYTES of zeros.  On return lane (g, t), t even, holds for token slot t>>1 the dot
+// products resA (fragment row g) and resB (row g + 8), bias included, over units u0, u0 + ustep, ...
 __device__ __forceinline__ void gemv3_tile(const uint8_t *tile, int units, int u0, int ustep, int scale_dtype, const uint2 *frag0,
-                                           const uint2 *frag1, const float *h0, const float *h1, const uint2 *zero, int ntok,
+                                           const uint2 *frag1, const float *h0, const float *h1, const void *zero, int ntok,
                                            float &resA, float &resB) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int tokslot = g >> 2, term = (g >> 1) & 1;
     const bool bact = ((g & 1) == (t >> 1)) && tokslot < ntok;
-    // lanes whose B column is structurally zero read one shared zero entry (stride 0): no select, no moves
-    const uint2 *fb = bact ? (tokslot ? frag1 : frag0) + term * 4 + t : zero;
-    const int fstride = bact ? 8 : 0;
-    const float *h = (t >> 1) ? h1 : h0;  // token whose result this lane's accumulator columns hold
-    const uint8_t *sb = tile + units * 768;
+    // lanes whose B column is structurally zero walk a block of zeros with unit stride 0: no select, no moves
+    uint32_t pb = (bact ? finch_smem_u32(tokslot ? frag1 : frag0) + (uint32_t)u0 * 576u : finch_smem_u32(zero)) + (uint32_t)(term * 4 + t) * 8u;
+    const uint32_t sb_step = bact ? (uint32_t)ustep * 576u : 0u;
+    const uint32_t h32 = finch_smem_u32((t >> 1) ? h1 : h0);  // token whose result this lane's accumulator columns hold
+    const uint32_t tile32 = finch_smem_u32(tile);
+    uint32_t pw = tile32 + (uint32_t)(u0 * 32 + lane) * 24u, ps = tile32 + (uint32_t)units * 768u + (uint32_t)(u0 * 8 + g) * 16u;
+    uint32_t ph = h32 + (uint32_t)u0 * 8u;
     float runA = 0.f, runB = 0.f, biasA = 0.f, biasB = 0.f;
     for (int u = u0; u < units; u += ustep) {
         uint2 b[9];
-#pragma unroll
-        for (int j = 0; j < 9; j++) b[j] = fb[(u * 9 + j) * fstride];
-        const uint2 *p = reinterpret_cast<const uint2 *>(tile + (size_t)(u * 32 + lane) * 24);
-        const uint2 q0 = p[0], q1 = p[1], q2 = p[2];
-        const uint4 s = *reinterpret_cast<const uint4 *>(sb + (size_t)(u * 8 + g) * 16);
-        const float2 xg = *reinterpret_cast<const float2 *>(h + 2 * u);
+        b[0] = lds64<0>(pb);   b[1] = lds64<64>(pb);  b[2] = lds64<128>(pb);
+        b[3] = lds64<192>(pb); b[4] = lds64<256>(pb); b[5] = lds64<320>(pb);
+        b[6] = lds64<384>(pb); b[7] = lds64<448>(pb); b[8] = lds64<512>(pb);
+        const uint2 q0 = lds64<0>(pw), q1 = lds64<8>(pw), q2 = lds64<16>(pw);
+        const uint4 s = lds128<0>(ps);
+        const uint2 xgb = lds64<0>(ph);
+        const float2 xg = make_float2(__uint_as_float(xgb.x), __uint_as_float(xgb.y));
+        pb += sb_step;
+        pw += (uint32_t)ustep * 768u;
+        ps += (uint32_t)ustep * 128u;
+        ph += (uint32_t)ustep * 8u;
         uint32_t ea[18], eb[18];
         extract3(q0.x, q0.y, q1.x, ea);
         extract3(q1.y, q2.x, q2.y, eb);
@@ -351,7 +407,7 @@ __device__ __forceinline__ void gemv3_tile(const uint8_t *tile, int units, int u
         biasB = fmaf(s1, xg.y, biasB);
     }
     // accumulator columns of lane t: token slot t>>1, term t&1 -> hi in even t, lo in odd t
-    const float fac = pow2_biased(__float_as_int(h[units * 2]) + 17);
+    const float fac = pow2_biased(__float_as_int(lds32f(h32 + (uint32_t)units * 8u)) + 17);
     const float oA = __shfl_xor_sync(0xffffffffu, runA, 1), oB = __shfl_xor_sync(0xffffffffu, runB, 1);
     resA = fmaf(runA + oA * (1.0f / 2048.0f), fac, biasA);
     resB = fmaf(runB + oB * (1.0f / 2048.0f), fac, biasB);
@@ -599,7 +655,7 @@ __global__ void shared_retile_kernel(SharedSrc S, int hidden, int inter, uint8_t
 // ============================ kernel A ====================================
 __host__ __device__ inline int up128(int x) { return (x + 127) & ~127; }
 struct SmemA {
-    int stage, stg, rec, rx3, rec4, f4s, n4, red, qcnt, tab, bar, total;
+    int stage, stg, rec, rx3, rec4, f4s, n4, red, qcnt, tab, zero, bar, total;
 };
 __host__ __device__ inline SmemA smem_a_layout(int hidden, int inter, int sh_inter, int B, int has_shared, int stages) {
     const FinchTile T = finch_tile(hidden, inter);
@@ -615,7 +671,8 @@ __host__ __device__ inline SmemA smem_a_layout(int hidden, int inter, int sh_int
     L.red = up128(L.rec4 + L.n4 * L.f4s);
     L.qcnt = L.red + stages * (MAXM / 2) * TEAM_A * 32 * 4;   // per stage: [pass][warp][32] partial sums
     L.tab = L.qcnt + 32 * 4;
-    L.bar = up128(L.tab + (int)sizeof(GroupTab));
+    L.zero = up128(L.tab + (int)sizeof(GroupTab));
+    L.bar = L.zero + ZERO3_BYTES;
     L.total = L.bar + 2 * 32 * 8 + 16 + 16;
     return L;
 }
@@ -639,6 +696,7 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
     const int f4b = frag4_bytes(K);
 
     if (tid < 32) reinterpret_cast<int *>(smem + L.qcnt)[tid] = 0;
+    if (tid < ZERO3_BYTES / 4) reinterpret_cast<int *>(smem + L.zero)[tid] = 0;
     if (tid == 0) {
         empty[32] = 0ull;
         for (int s = 0; s < Smax; s++) {
@@ -732,7 +790,7 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
                 const uint8_t *rec0 = smem + L.rec + tok0 * L.rx3, *rec1 = smem + L.rec + tok1 * L.rx3;
                 gemv3_tile(tile, T.unitsA, kw, TEAM_A, a.scale_dtype, reinterpret_cast<const uint2 *>(rec0), reinterpret_cast<const uint2 *>(rec1),
                            reinterpret_cast<const float *>(rec0 + frag3_bytes(K)), reinterpret_cast<const float *>(rec1 + frag3_bytes(K)),
-                           zero8, ntok, vA, vB);
+                           smem + L.zero, ntok, vA, vB);
                 if ((t & 1) == 0) {
                     mine[(t >> 1) * 16 + g * 2] = vA;
                     mine[(t >> 1) * 16 + g * 2 + 1] = vB;
@@ -793,7 +851,7 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
 
 // ============================ kernel B ====================================
 struct SmemB {
-    int stage, stg, rec, srec, tab, ok, contrib, lastf, bar, total;
+    int stage, stg, rec, srec, xstage, tab, ok, contrib, lastf, zero, bar, total;
 };
 __host__ __device__ inline SmemB smem_b_layout(int hidden, int inter, int sh_inter, int B, int has_shared, int stages) {
     const FinchTile T = finch_tile(hidden, inter);
@@ -803,11 +861,13 @@ __host__ __device__ inline SmemB smem_b_layout(int hidden, int inter, int sh_int
     L.stg = up128(has_shared && T4.tileB > T.tileB ? T4.tileB : T.tileB);
     L.rec = L.stage + stages * L.stg;                        // act records of the groups in this CTA's range
     L.srec = up128(L.rec + REC_CAP * rec3_bytes(inter));     // shared_act records
-    L.tab = up128(L.srec + (has_shared ? B * rec4_bytes(sh_inter) : 0));
+    L.xstage = up128(L.srec + (has_shared ? B * rec4_bytes(sh_inter) : 0));   // one row of act per consumer warp
+    L.tab = up128(L.xstage + CW_B * 4 * (inter > sh_inter ? inter : sh_inter));
     L.ok = up128(L.tab + (int)sizeof(GroupTab));
     L.contrib = L.ok + MAXP * 4;
     L.lastf = L.contrib + 128 * 4;
-    L.bar = up128(L.lastf + 128);
+    L.zero = up128(L.lastf + 128);
+    L.bar = L.zero + ZERO3_BYTES;
     L.total = L.bar + 2 * 32 * 8 + 16;
     return L;
 }
@@ -834,6 +894,7 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
             finch_mbar_init(empty + s, 1);
         }
     }
+    if (tid < ZERO3_BYTES / 4) reinterpret_cast<int *>(smem + L.zero)[tid] = 0;
     grid_dep_wait();  // the barrier set-up overlaps the tail of the gate/up kernel
     {
         const int *s = reinterpret_cast<const int *>(a.gtab);
@@ -873,15 +934,16 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
     const int g_lo = job0 < n_routed ? job0 / T.nTB : ng;
     const int g_hi = job1 > job0 ? min(ng - 1, (job1 - 1) / T.nTB) : -1;   // inclusive
     {
+        float *xstage = reinterpret_cast<float *>(smem + L.xstage) + (size_t)warp * (K > Ks ? K : Ks);
         int q = 0;
         for (int gi = g_lo; gi <= g_hi; gi++)
             for (int i = 0; i < tab->m[gi]; i++, q++)
                 if (q % CW_B == warp && q < REC_CAP)
-                    warp_make_record<3>(a.act + (size_t)tab->pairs[gi][i] * K, K, smem + L.rec + q * r3b);
+                    warp_make_record<3>(a.act + (size_t)tab->pairs[gi][i] * K, K, smem + L.rec + q * r3b, xstage);
         if (q > REC_CAP && tid == 0) atomicExch(a.status, FINCH_E_UNSUPPORTED);
         if (a.has_shared && job1 > n_routed && job1 > job0)
             for (int b = 0; b < a.B; b++, q++)
-                if (q % CW_B == warp) warp_make_record<4>(a.shared_act + (size_t)b * Ks, Ks, smem + L.srec + b * r4b);
+                if (q % CW_B == warp) warp_make_record<4>(a.shared_act + (size_t)b * Ks, Ks, smem + L.srec + b * r4b, xstage);
     }
     bar_sync(1, CW_B * 32);
     const long long tk2 = clock64();
@@ -909,7 +971,7 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
                 float va, vb;
                 gemv3_tile(tile, T.unitsD, 0, 1, a.scale_dtype, reinterpret_cast<const uint2 *>(rec0), reinterpret_cast<const uint2 *>(rec1),
                            reinterpret_cast<const float *>(rec0 + frag3_bytes(K)), reinterpret_cast<const float *>(rec1 + frag3_bytes(K)),
-                           zero8, ntok, va, vb);
+                           smem + L.zero, ntok, va, vb);
                 if ((t & 1) == 0 && (t >> 1) < ntok) {
                     float *o = a.partial + (size_t)tab->pairs[gi][2 * ps + (t >> 1)] * a.hidden + 16 * tb + g;
                     o[0] = va;
@@ -938,7 +1000,7 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
         (void)tb;
     }
 
-    const long long tk3 = clock64(), tk4 = tk3;
+    const long long tk3 = clock64();
     if (a.dbg && tid == 0) {
         long long *d = a.dbg + (size_t)(1024 + blockIdx.x) * 8;
         d[0] = tk1 - tk0;   // table + barriers
