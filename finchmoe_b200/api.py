@@ -173,7 +173,24 @@ class Context:
                                                 w16.ctypes.data, w16_dtype))
         return codes, w32, w16
 
+    def dense_gemm(self, w: L.WDesc, x_bf16: np.ndarray) -> np.ndarray:
+        """gpu_encode_prefill_matvec (finchmoe/infer.m:3672) on the tensor cores: host x as bf16 bits
+        (uint16 [M, in]) -> host out fp32 [M, out].  torch holds the device buffers."""
+        import torch
+        x_bf16 = np.ascontiguousarray(x_bf16, np.uint16)
+        M = x_bf16.shape[0]
+        xd = torch.from_numpy(x_bf16.view(np.int16)).cuda()
+        od = torch.empty((M, w.out_dim), dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        self.check(self.lib.finch_encode_dense_gemm(self.h, None, C.byref(w), xd.data_ptr(), od.data_ptr(), M))
+        self.sync()
+        return od.cpu().numpy()
+
     # -- MoE layer
+    def set_prefill_mode(self, mode: int):
+        """0: by chunk length, 1: sub-batches through the decode kernels, 2: tensor-core grouped GEMM."""
+        self.check(self.lib.finch_set_prefill_mode(self.h, mode))
+
     def make_shared(self, gate: L.WDesc, up: L.WDesc, down: L.WDesc, gate_score=None) -> L.Shared:
         return L.Shared(gate, up, down, _ptr(gate_score))
 

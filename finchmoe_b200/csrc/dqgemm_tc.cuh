@@ -1,0 +1,431 @@
+// Dequant-GEMM on the 5th-generation tensor cores (tcgen05, accumulators in tensor memory).
+//
+//   D[128 weight rows, TN tokens] += Wdq[128, K] * X[TN, K]^T        (bf16 x bf16 -> fp32)
+//
+// One CTA owns one 128-row weight tile and up to TNMAX tokens.  Per K-block of 128 values its sixteen
+// warps read packed codes straight from HBM, dequantise them to bf16 -- RNE(fl32(fl32(q*s)+b)), the
+// value the reference's dequantised weight rounds to (quant_audit.py:245 semantics) -- and write them,
+// together with the tokens' activations, into shared memory in the 128-byte-swizzled K-major layout
+// the tensor core reads; one elected thread then issues eight tcgen05.mma (K = 16 each) and commits
+// them to an mbarrier.  Two stages: the warps dequantise block i+1 while the tensor core works on
+// block i.  The epilogue reads the accumulator with tcgen05.ld, one lane (= weight row) per thread.
+//
+// Shared by moe_prefill.cu (grouped 3-bit expert GEMMs over the pool's tiled layout) and the dense
+// 4-bit projections.  Every wait is bounded; on a time-out the CTA reports through `status`, frees
+// its tensor memory and returns.
+#pragma once
+#include "finch_internal.cuh"
+#include "tile_layout.h"
+
+namespace dqgemm {
+
+constexpr int GM = 128;       // weight rows per CTA = UMMA M
+constexpr int BK = 128;       // K values per stage = two 64-value swizzle atoms
+constexpr int NS = 2;         // stages
+constexpr int NT = 512;       // threads per CTA: four per weight row, one for each 32-value quarter of a K block
+constexpr int A_ATOM = GM * 128;   // bytes of one 64-value atom of the weight tile
+constexpr int RD = 4;         // depth of the ring of packed expert blocks (EXPERT_* modes)
+constexpr int RAW_STAGE = 8 * 768 + 8 * 128;   // one K block of eight 16-row pool tiles: operand words, then scale/bias entries
+
+enum Mode { EXPERT_GATEUP = 0, EXPERT_DOWN = 1, DENSE4 = 2 };
+
+struct Args {
+    int mode;
+    int K;                    // reduction length (multiple of 128)
+    int tn_max;               // token-tile capacity of a CTA: 16..256, multiple of 16
+    int scale_dtype;
+    // EXPERT_*: weights come from the pool (tiled layout, tile_layout.h)
+    const uint8_t *pool_base;
+    size_t slot_bytes;
+    const int32_t *slot_row;  // [n_experts] slot of each expert of this layer, < 0: absent
+    int hidden, inter;
+    const int *seg;           // [n_experts + 1] ranges of `order`
+    const int *order;         // pair ids sorted by expert
+    int top_k;
+    // DENSE4: reference tensor layout (u32 words, 16-bit scales and biases per group of 64)
+    const uint32_t *W;
+    const uint16_t *S, *B;
+    int rows;                 // output rows
+    int n_tokens;
+    // activations: bf16 rows of K values; row index = token (GATEUP, DENSE4) or pair (DOWN).  X2, when
+    // not NULL, is a second plane added to the first (value = X + X2): the low-order part of an
+    // activation kept to about 16 bits, multiplied by the same weight tile into the same accumulator.
+    const uint16_t *X, *X2;
+    // outputs
+    uint16_t *act_out;        // GATEUP: bf16 [pairs][inter] = SiLU(gate) * up, rounded to bf16 ...
+    uint16_t *act_out_lo;     // ... and bf16(value - that), or NULL
+    float *out;               // DOWN: fp32 [pairs][hidden]; DENSE4: fp32 [tokens][rows]
+    int *status;
+};
+
+__host__ __device__ inline int smem_bytes(int tn_max, int planes, int expert) {
+    return 1024 + NS * (2 * A_ATOM + planes * 2 * tn_max * 128) + (expert ? RD * RAW_STAGE : 0) + 256 + tn_max * 4;
+}
+__host__ __device__ inline int tmem_cols(int tn_max) { return tn_max <= 32 ? 32 : tn_max <= 64 ? 64 : tn_max <= 128 ? 128 : 256; }
+
+// ---- tcgen05 wrappers ----------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t smem_dst, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_dst), "r"(cols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(finch_smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tc_mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// 16 consecutive fp32 columns of this thread's lane
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+          "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+    return (uint64_t)((addr & 0x3FFFFu) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor: bf16 x bf16 -> fp32, both operands K-major, M = 128, N = tn.
+__device__ __forceinline__ uint32_t instr_desc(int tn) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(tn >> 3) << 17) | ((uint32_t)(GM >> 4) << 24);
+}
+
+// Byte offset of 16-byte chunk c (0..7) of row r inside a 64-value atom.
+__device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)); }
+
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+__device__ __forceinline__ void st_shared16(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+// 16-byte asynchronous copy global -> shared (lands while the warps dequantise)
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Dequantisation without integer-to-float conversions: a code isolated by one AND at bits [p, p+4) of a
+// 16-bit half is the fp16 subnormal q * 2^(p-24); widening it to fp32 is exact, and
+//   fma(q * 2^(p-24), s * 2^(24-p), b)  =  round_fp32(q * s + b)  =  fl32(fl32(q * s) + b)
+// because q * s is exact in fp32 (3- or 4-bit q, at most 11-bit s): the value the reference's
+// dequantised weight has (quant_audit.py:245), rounded once more to bf16 for the tile.
+struct GroupScale {
+    float sp[8];   // s * 2^(24-p), p = 0..7
+    float b;
+};
+__device__ __forceinline__ GroupScale group_scale(float s, float b) {
+    GroupScale g;
+#pragma unroll
+    for (int p = 0; p < 8; p++) g.sp[p] = s * __uint_as_float((uint32_t)(127 + 24 - p) << 23);
+    g.b = b;
+    return g;
+}
+__device__ __forceinline__ float half_lo(uint32_t r) { return __low2float(*reinterpret_cast<const __half2 *>(&r)); }
+__device__ __forceinline__ float half_hi(uint32_t r) { return __high2float(*reinterpret_cast<const __half2 *>(&r)); }
+
+// 32 three-bit codes in three words (a little-endian bit stream) -> four chunks of 8 bf16.
+// 18 masked registers hold two codes each; IDX / POS say which code and at which bit of its half.
+__device__ __forceinline__ void dq3_piece(uint32_t w0, uint32_t w1, uint32_t w2, const GroupScale &gs, uint32_t (&o)[16]) {
+    constexpr int IDX[36] = {0, 6, 1, 7, 2, -1, 3, 8, 4, 9, 5, 10, 11, 16, 12, 17, 13, 18,
+                             14, 19, 15, 20, -1, 21, 22, 27, 23, 28, -1, 29, 24, 30, 25, 31, 26, -1};
+    constexpr int POS[36] = {0, 2, 3, 5, 6, 0, 1, 0, 4, 3, 7, 6, 1, 0, 4, 3, 7, 6,
+                             2, 1, 5, 4, 0, 7, 2, 1, 5, 4, 0, 7, 0, 2, 3, 5, 6, 0};
+    const uint32_t v1 = __funnelshift_r(w0, w1, 8), v3 = __funnelshift_r(w1, w2, 8), v5 = w2 >> 8;
+    uint32_t e[18];
+    e[0] = w0 & 0x001C0007u;  e[1] = w0 & 0x00E00038u;  e[2] = w0 & 0x000001C0u;
+    e[3] = v1 & 0x0007000Eu;  e[4] = v1 & 0x00380070u;  e[5] = v1 & 0x01C00380u;
+    e[6] = w1 & 0x0007000Eu;  e[7] = w1 & 0x00380070u;  e[8] = w1 & 0x01C00380u;
+    e[9] = v3 & 0x000E001Cu;  e[10] = v3 & 0x007000E0u; e[11] = v3 & 0x03800000u;
+    e[12] = w2 & 0x000E001Cu; e[13] = w2 & 0x007000E0u; e[14] = w2 & 0x03800000u;
+    e[15] = v5 & 0x001C0007u; e[16] = v5 & 0x00E00038u; e[17] = v5 & 0x000001C0u;
+    float v[32];
+#pragma unroll
+    for (int k = 0; k < 36; k++) {
+        if (IDX[k] < 0) continue;
+        const float q = (k & 1) ? half_hi(e[k >> 1]) : half_lo(e[k >> 1]);
+        v[IDX[k]] = fmaf(q, gs.sp[POS[k]], gs.b);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; i++) o[i] = bf16x2_rn(v[2 * i], v[2 * i + 1]);
+}
+// 8 four-bit codes in one word -> one chunk of 8 bf16.
+__device__ __forceinline__ void dq4_word(uint32_t w, const GroupScale &gs, uint32_t (&o)[4]) {
+    const uint32_t x = w >> 8;
+    const uint32_t e0 = w & 0x000F000Fu, e1 = w & 0x00F000F0u, e2 = x & 0x000F000Fu, e3 = x & 0x00F000F0u;   // codes (0,4) (1,5) (2,6) (3,7)
+    float v[8];
+    v[0] = fmaf(half_lo(e0), gs.sp[0], gs.b); v[4] = fmaf(half_hi(e0), gs.sp[0], gs.b);
+    v[1] = fmaf(half_lo(e1), gs.sp[4], gs.b); v[5] = fmaf(half_hi(e1), gs.sp[4], gs.b);
+    v[2] = fmaf(half_lo(e2), gs.sp[0], gs.b); v[6] = fmaf(half_hi(e2), gs.sp[0], gs.b);
+    v[3] = fmaf(half_lo(e3), gs.sp[4], gs.b); v[7] = fmaf(half_hi(e3), gs.sp[4], gs.b);
+#pragma unroll
+    for (int i = 0; i < 4; i++) o[i] = bf16x2_rn(v[2 * i], v[2 * i + 1]);
+}
+
+// grid: x = 128-row weight tile, y = expert (EXPERT_*) or 0, z = token tile.  block: 128 threads.
+__global__ void __launch_bounds__(NT) dqgemm_tc_kernel(const Args a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tn_max = a.tn_max;
+    // ---- which tokens ----
+    int m_total, first;
+    const int *rows_of = nullptr;   // EXPERT_*: pair ids of this expert
+    if (a.mode == DENSE4) {
+        m_total = a.n_tokens;
+        first = 0;
+    } else {
+        const int e = blockIdx.y;
+        first = a.seg[e];
+        m_total = a.seg[e + 1] - first;
+        rows_of = a.order + first;
+    }
+    const int t0 = blockIdx.z * tn_max;
+    if (t0 >= m_total) return;
+    const int m = min(tn_max, m_total - t0);        // tokens of this CTA
+    const int tn = (m + 15) & ~15;                   // UMMA N
+
+    const uint32_t base = (finch_smem_u32(smem_raw) + 1023u) & ~1023u;
+    const int planes = a.X2 ? 2 : 1, plane_bytes = 2 * tn_max * 128;
+    const int stage_bytes = 2 * A_ATOM + planes * plane_bytes;
+    const bool expert = a.mode != DENSE4;
+    const uint32_t raw = base + NS * stage_bytes;     // EXPERT_*: ring of packed blocks, filled by bulk copies
+    const uint32_t ctl = raw + (expert ? RD * RAW_STAGE : 0);   // barriers, tensor-memory address, row list
+    uint8_t *ctl_p = smem_raw + (ctl - finch_smem_u32(smem_raw));
+    uint8_t *raw_p = smem_raw + (raw - finch_smem_u32(smem_raw));
+    uint64_t *done = reinterpret_cast<uint64_t *>(ctl_p);   // [NS]
+    uint64_t *full = done + NS;                              // [RD]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ctl_p + 64);
+    int *src_rows = reinterpret_cast<int *>(ctl_p + 256);   // [tn_max] activation row of each token of the tile
+
+    // zero the activation halves of the stages once: rows >= m are never written and must read as 0
+    for (int s = 0; s < NS; s++) {
+        const uint32_t bst = base + s * stage_bytes + 2 * A_ATOM;
+        for (int i = tid; i < planes * 2 * tn_max * 8; i += NT) st_shared16(bst + i * 16, 0u, 0u, 0u, 0u);
+    }
+    for (int j = tid; j < m; j += NT) {
+        int row = t0 + j;
+        if (a.mode != DENSE4) {
+            const int pair = rows_of[t0 + j];
+            row = a.mode == EXPERT_GATEUP ? pair / a.top_k : pair;
+        }
+        src_rows[j] = row;
+    }
+    if (tid == 0) {
+        for (int s = 0; s < NS; s++) finch_mbar_init(done + s, 1);
+        for (int s = 0; s < RD; s++) finch_mbar_init(full + s, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    const uint32_t ncols = (uint32_t)tmem_cols(tn_max);
+    if (warp == 0) {
+        tmem_alloc(finch_smem_u32(tmem_slot), ncols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_d = *tmem_slot;
+
+    // ---- this thread's weight row ----
+    const int r = tid & (GM - 1), kq = tid >> 7, kh = kq >> 1;   // row of the tile (= tensor-memory lane), 32-value quarter and 64-value half of a K block
+    const uint8_t *wq = nullptr;       // EXPERT_*: first operand word of (unit 0, lane g*4 + 0), row half included
+    const uint8_t *sbq = nullptr;      // EXPERT_*: scale/bias entry of (unit 0, g), row half included
+    const uint32_t *w4 = nullptr;      // DENSE4: packed row
+    const uint16_t *s4 = nullptr, *b4 = nullptr;
+    uint32_t raw_w = 0, raw_s = 0;     // EXPERT_*: this thread's words / scale inside a ring stage
+    const uint8_t *tile0 = nullptr;    // EXPERT_*: first of the CTA's eight pool tiles
+    int tile_stride = 0, sb_off = 0;
+    if (a.mode == DENSE4) {
+        const size_t row = (size_t)blockIdx.x * GM + r;
+        w4 = a.W + row * (a.K / 8);
+        s4 = a.S + row * (a.K / 64);
+        b4 = a.B + row * (a.K / 64);
+    } else {
+        const FinchTile T = finch_tile(a.hidden, a.inter);
+        const int dt = blockIdx.x * 8 + (r >> 4), fr = r & 15, g = fr & 7, half = fr >> 3;
+        const uint8_t *blk = a.pool_base + (size_t)a.slot_row[blockIdx.y] * a.slot_bytes;
+        const uint8_t *tile = a.mode == EXPERT_GATEUP ? blk + (size_t)dt * T.tileA : blk + T.b_base + (size_t)dt * T.tileB;
+        wq = tile + (size_t)g * 96 + half * 12;
+        sbq = tile + (a.mode == EXPERT_GATEUP ? T.sbA : T.sbB) + (size_t)g * 16 + half * 4;
+        raw_w = (uint32_t)((r >> 4) * 768 + (g * 4 + kq) * 24 + half * 12);
+        raw_s = (uint32_t)(8 * 768 + (r >> 4) * 128 + g * 16 + half * 4 + kh * 2);
+        tile0 = a.mode == EXPERT_GATEUP ? blk + (size_t)blockIdx.x * 8 * T.tileA : blk + T.b_base + (size_t)blockIdx.x * 8 * T.tileB;
+        tile_stride = a.mode == EXPERT_GATEUP ? T.tileA : T.tileB;
+        sb_off = a.mode == EXPERT_GATEUP ? T.sbA : T.sbB;
+    }
+    (void)wq;
+    (void)sbq;
+
+    const int nkb = a.K / BK;
+    const uint32_t idesc = instr_desc(tn);
+    bool failed = false;
+    uint32_t wreg[4];
+    uint32_t sreg = 0, breg = 0;   // low 16 bits: scale / bias of this thread's group
+    auto load_block = [&](int kb) {
+        if (a.mode == DENSE4) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(w4 + kb * 16 + kq * 4));
+            wreg[0] = v.x; wreg[1] = v.y; wreg[2] = v.z; wreg[3] = v.w;
+            sreg = __ldg(s4 + 2 * kb + kh);
+            breg = __ldg(b4 + 2 * kb + kh);
+        }
+    };
+    // EXPERT_*: one thread keeps RD - 1 K blocks of packed bytes in flight (16 bulk copies per block)
+    auto issue_raw = [&](int kb) {
+        const int slot = kb % RD;
+        uint8_t *dst = raw_p + slot * RAW_STAGE;
+        finch_mbar_expect_tx(full + slot, (unsigned)RAW_STAGE);
+        for (int d = 0; d < 8; d++) {
+            const uint8_t *t = tile0 + (size_t)d * tile_stride;
+            finch_bulk_g2s(dst + d * 768, t + (size_t)kb * 768, 768, full + slot);
+            finch_bulk_g2s(dst + 8 * 768 + d * 128, t + sb_off + (size_t)kb * 128, 128, full + slot);
+        }
+    };
+    if (expert) {
+        if (tid == 0)
+            for (int kb = 0; kb < RD - 1 && kb < nkb; kb++) issue_raw(kb);
+    } else {
+        load_block(0);
+    }
+
+    for (int kb = 0; kb < nkb; kb++) {
+        const int st = kb % NS, use = kb / NS;
+        const uint32_t ast = base + st * stage_bytes, bst = ast + 2 * A_ATOM;
+        // the tensor core must be done with this stage's previous contents
+        bool ok = true;
+        if (use > 0) ok = finch_mbar_wait(done + st, (use - 1) & 1);
+        if (expert && ok) ok = finch_mbar_wait(full + kb % RD, (kb / RD) & 1);
+        if (__syncthreads_or(!ok)) {
+            failed = true;
+            break;
+        }
+        tc_fence_after();
+        // every thread is past block kb - 1, so its ring slot can take block kb + RD - 1
+        if (expert && tid == 0 && kb + RD - 1 < nkb) issue_raw(kb + RD - 1);
+        // ---- activations: m rows of 128 values, copied asynchronously while the weights are dequantised ----
+        for (int i = tid; i < m * 16; i += NT) {
+            const int j = i >> 4, c = i & 15;
+            const size_t src = (size_t)src_rows[j] * a.K + (size_t)kb * BK + c * 8;
+            const uint32_t dst = bst + (c >> 3) * (tn_max * 128) + swz(j, c & 7);
+            cp_async16(dst, a.X + src);
+            if (a.X2) cp_async16(dst + plane_bytes, a.X2 + src);
+        }
+        // ---- weights: 32 values of row r ----
+        if (expert) {
+            const uint32_t rs = raw + (kb % RD) * RAW_STAGE;
+            asm volatile("ld.shared.u16 %0, [%1];" : "=r"(sreg) : "r"(rs + raw_s));
+            asm volatile("ld.shared.u16 %0, [%1+8];" : "=r"(breg) : "r"(rs + raw_s));
+        }
+        float s0, b0, unused;
+        finch_widen16x2(sreg, a.scale_dtype, s0, unused);
+        finch_widen16x2(breg, a.scale_dtype, b0, unused);
+        const GroupScale gs = group_scale(s0, b0);
+        uint32_t cur[4];
+        if (expert) {
+            const uint32_t rs = raw + (kb % RD) * RAW_STAGE;
+            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(cur[0]) : "r"(rs + raw_w));
+            asm volatile("ld.shared.u32 %0, [%1+4];" : "=r"(cur[1]) : "r"(rs + raw_w));
+            asm volatile("ld.shared.u32 %0, [%1+8];" : "=r"(cur[2]) : "r"(rs + raw_w));
+            cur[3] = 0;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; i++) cur[i] = wreg[i];
+            if (kb + 1 < nkb) load_block(kb + 1);   // in flight while this block is dequantised
+        }
+        const uint32_t arow = ast + kh * A_ATOM;
+        const int cbase = (kq & 1) * 4;         // first 16-byte chunk of this quarter inside its atom
+        if (a.mode == DENSE4) {
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                uint32_t o[4];
+                dq4_word(cur[c], gs, o);
+                st_shared16(arow + swz(r, cbase + c), o[0], o[1], o[2], o[3]);
+            }
+        } else {
+            uint32_t o[16];
+            dq3_piece(cur[0], cur[1], cur[2], gs, o);
+#pragma unroll
+            for (int c = 0; c < 4; c++) st_shared16(arow + swz(r, cbase + c), o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+        }
+        cp_async_wait_all();
+        proxy_fence();          // generic-proxy writes -> visible to the tensor core (async proxy)
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const uint32_t aoff = (k >> 2) * A_ATOM + (k & 3) * 32, boff = (k >> 2) * (tn_max * 128) + (k & 3) * 32;
+                tc_mma_bf16(tmem_d, smem_desc(ast + aoff), smem_desc(bst + boff), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                if (planes == 2) tc_mma_bf16(tmem_d, smem_desc(ast + aoff), smem_desc(bst + plane_bytes + boff), idesc, 1u);
+            }
+            tc_commit(done + st);
+        }
+    }
+
+    // ---- epilogue ----
+    if (!failed) {
+        const int last = nkb - 1;
+        const bool ok = finch_mbar_wait(done + last % NS, (last / NS) & 1);
+        if (__syncthreads_or(!ok)) failed = true;
+    }
+    if (!failed) {
+        tc_fence_after();
+        // warps w, w + 4, w + 8, w + 12 read the same 32 lanes and take every fourth 16-column chunk
+        const uint32_t trow = tmem_d + ((uint32_t)((warp & 3) * 32) << 16);
+        for (int c0 = (warp >> 2) * 16; c0 < tn; c0 += 64) {
+            float v[16];
+            tmem_ld16(trow + (uint32_t)c0, v);
+            if (a.mode == EXPERT_GATEUP) {
+                // lanes l and l ^ 8 hold the gate and the up row of the same index
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const float other = __shfl_xor_sync(0xffffffffu, v[j], 8);
+                    if (!(lane & 8) && c0 + j < m) {
+                        const float gv = v[j], act = (gv / (1.0f + expf(-gv))) * other;
+                        const int pair = rows_of[t0 + c0 + j];
+                        const int idx = (blockIdx.x * 8 + (r >> 4)) * 8 + (r & 7);
+                        const uint32_t hi = bf16x2_rn(act, 0.f) & 0xffffu;
+                        a.act_out[(size_t)pair * a.inter + idx] = (uint16_t)hi;
+                        if (a.act_out_lo)
+                            a.act_out_lo[(size_t)pair * a.inter + idx] = (uint16_t)(bf16x2_rn(act - __uint_as_float(hi << 16), 0.f) & 0xffffu);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    if (c0 + j < m) {
+                        if (a.mode == EXPERT_DOWN) a.out[(size_t)rows_of[t0 + c0 + j] * a.hidden + (size_t)blockIdx.x * GM + r] = v[j];
+                        else a.out[(size_t)(t0 + c0 + j) * a.rows + (size_t)blockIdx.x * GM + r] = v[j];
+                    }
+                }
+            }
+        }
+    } else if (tid == 0) {
+        atomicExch(a.status, FINCH_E_TIMEOUT);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem_d, ncols);
+}
+
+}  // namespace dqgemm

@@ -1,25 +1,303 @@
 // Chunked-prefill MoE entry point (prefill_chunk_cmd3 / _batch_general,
-// finchmoe/infer.m:10704-11241).
+// finchmoe/infer.m:10704-11241) and the dense 4-bit projection GEMM
+// (gpu_encode_prefill_matvec, infer.m:3672).
 //
-// A chunk of T tokens is cut into sub-batches of at most eight tokens and each
-// sub-batch goes through the decode kernels (moe_decode.cu), which already read
-// every expert selected inside a sub-batch once for all of its tokens.  This is
-// the reference's own scheme -- per-position dispatch of the decode kernels,
-// with the GGUF path de-duplicating experts inside a group of positions
-// (infer.m:12424-12532) -- with the group size fixed at eight.  Every output
-// row is bit-identical to what the decode entry point gives for the same token,
-// the property the reference claims for its chunked prefill (README.md:25).
-#include "finch_internal.cuh"
+// Two paths:
+//  * tensor-core path (chunks of 128 tokens and more, or on request): the (token, k) pairs are sorted by expert, the
+//    activations are rounded to bf16, and two grouped dequant-GEMMs (dqgemm_tc.cuh) run on tcgen05:
+//    gate/up with SiLU(gate)*up in the epilogue (activation stored as two bf16 planes, value and
+//    remainder, about 16 bits together), then down -- both planes against the same weight tile -- into
+//    one fp32 row per pair; the shared expert is three dense 4-bit GEMMs; a last kernel applies the router weights
+//    in ascending k, the shared gate and the residual (moe_combine_residual_prefill,
+//    finchmoe/shaders.metal:2764-2802).  Every selected expert is read from HBM once per chunk of 512.
+//  * sub-batch path (short chunks, or on request): groups of at most eight tokens go through the
+//    decode kernels (moe_decode.cu) -- the reference's own scheme, per-position dispatch of the decode
+//    kernels with expert de-duplication inside a group (infer.m:12424-12532).  Every output row is then
+//    bit-identical to the decode entry point's, the property the reference claims (README.md:25).
+//
+// The tensor-core path multiplies bf16-rounded weights by bf16-rounded activations with fp32
+// accumulation, so its results differ from the decode path's (fp32 activations, exact weights) by
+// bf16 rounding; the parity tests compare it with an oracle that rounds at the same places.
+#include "dqgemm_tc.cuh"
+
+namespace {
+
+constexpr int CHUNK = 512;   // tokens per tensor-core pass: 4096 pairs
+constexpr int TC_MIN_TOKENS = 128;   // shorter chunks are faster through the decode kernels (measured)
+
+// One CTA: pairs -> expert histogram -> ranges -> order.  Pairs that are masked, out of range or not
+// resident are left out (their rows are never produced and never combined).
+__global__ void __launch_bounds__(1024) pf_sort_kernel(const int32_t *ids, const uint8_t *valid, const int32_t *slot_row, int n_experts, int P,
+                                                       int *seg, int *order) {
+    extern __shared__ int sm[];   // [n_experts] counts, then [n_experts] cursors
+    int *cnt = sm, *cur = sm + n_experts;
+    const int tid = threadIdx.x;
+    for (int e = tid; e < n_experts; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int p = tid; p < P; p += blockDim.x) {
+        const int e = ids[p];
+        if ((valid && !valid[p]) || e < 0 || e >= n_experts || slot_row[e] < 0) continue;
+        atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int run = 0;
+        for (int e = 0; e < n_experts; e++) {
+            seg[e] = run;
+            cur[e] = run;
+            run += cnt[e];
+        }
+        seg[n_experts] = run;
+    }
+    __syncthreads();
+    // the order of the pairs inside an expert's range is arbitrary: every pair's output row is computed
+    // from its own activation row only, so the results do not depend on it
+    for (int p = tid; p < P; p += blockDim.x) {
+        const int e = ids[p];
+        if ((valid && !valid[p]) || e < 0 || e >= n_experts || slot_row[e] < 0) continue;
+        order[atomicAdd(&cur[e], 1)] = p;
+    }
+}
+
+__global__ void pf_to_bf16_kernel(const float *src, uint16_t *dst, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n / 2; i += (size_t)gridDim.x * blockDim.x)
+        reinterpret_cast<uint32_t *>(dst)[i] = dqgemm::bf16x2_rn(src[2 * i], src[2 * i + 1]);
+}
+
+// act = SiLU(g) * u, stored as two bf16 planes: the value rounded to bf16 and the remainder (shared expert)
+__global__ void pf_swiglu_kernel(const float *g, const float *u, uint16_t *act, uint16_t *act_lo, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const float gv = g[i], v = (gv / (1.0f + expf(-gv))) * u[i];
+        const uint32_t hi = dqgemm::bf16x2_rn(v, 0.f) & 0xffffu;
+        act[i] = (uint16_t)hi;
+        act_lo[i] = (uint16_t)(dqgemm::bf16x2_rn(v - __uint_as_float(hi << 16), 0.f) & 0xffffu);
+    }
+}
+
+// hidden[t] = h_mid[t] + sum_{k ascending, usable} w[t][k] * down[t*K + k] + sigmoid(score[t]) * shared[t]
+__global__ void __launch_bounds__(256) pf_combine_kernel(const int32_t *ids, const uint8_t *valid, const int32_t *slot_row, int n_experts,
+                                                         const float *weights, int K, const float *down, const float *shared_out,
+                                                         const float *gate_score, const float *h_mid, float *hidden_out, int hidden) {
+    __shared__ int ok[8];
+    __shared__ float wk[8];
+    const int t = blockIdx.y, row = blockIdx.x * 256 + threadIdx.x;
+    if (threadIdx.x < K) {
+        const int p = t * K + threadIdx.x, e = ids[p];
+        ok[threadIdx.x] = !(valid && !valid[p]) && e >= 0 && e < n_experts && slot_row[e] >= 0;
+        wk[threadIdx.x] = weights[p];
+    }
+    __syncthreads();
+    if (row >= hidden) return;
+    float moe = 0.f;
+    for (int k = 0; k < K; k++)
+        if (ok[k]) moe = fmaf(wk[k], down[(size_t)(t * K + k) * hidden + row], moe);
+    float h = h_mid ? h_mid[(size_t)t * hidden + row] : 0.f;
+    h += moe;
+    if (shared_out) {
+        const float sg = 1.0f / (1.0f + expf(-gate_score[t]));
+        h = fmaf(sg, shared_out[(size_t)t * hidden + row], h);
+    }
+    hidden_out[(size_t)t * hidden + row] = h;
+}
+
+inline size_t up256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+int tn_max_for(int tokens) {
+    int t = (tokens + 15) & ~15;
+    return t < 16 ? 16 : (t > 256 ? 256 : t);
+}
+
+bool g_gemm_attr = false;
+int launch_gemm(finch_ctx *ctx, cudaStream_t st, const dqgemm::Args &a, dim3 grid) {
+    if (!g_gemm_attr) {
+        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(dqgemm::dqgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(dqgemm::dqgemm_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        g_gemm_attr = true;
+    }
+    const int smem = dqgemm::smem_bytes(a.tn_max, a.X2 ? 2 : 1, a.mode != dqgemm::DENSE4);
+    if (smem > 227 * 1024) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "token tile %d needs %d bytes of shared memory", a.tn_max, smem);
+    dqgemm::dqgemm_tc_kernel<<<grid, dqgemm::NT, smem, st>>>(a);
+    FINCH_CUDA_OK(ctx, cudaGetLastError());
+    ctx->launches++;
+    return FINCH_OK;
+}
+
+int dense4_checked(finch_ctx *ctx, const finch_wdesc *w, const char *what) {
+    int rc = finch_validate_wdesc(ctx, w, what);
+    if (rc) return rc;
+    if (w->bits != 4 || w->group_size != 64 || w->in_dim % 128 || w->out_dim % 128)
+        return finch_fail(ctx, FINCH_E_UNSUPPORTED, "%s: the tensor-core GEMM takes 4-bit g64 tensors with dims that are multiples of 128", what);
+    return FINCH_OK;
+}
+
+// out[T][out_dim] (fp32) = X[T][in_dim] (bf16) * dequant(w)^T
+int dense4_gemm(finch_ctx *ctx, cudaStream_t st, const finch_wdesc *w, const uint16_t *xb, const uint16_t *xb_lo, float *out, int T) {
+    dqgemm::Args a{};
+    a.mode = dqgemm::DENSE4;
+    a.K = w->in_dim;
+    // token tile: small enough that the grid covers the SMs, large enough not to dequantise a tile too often
+    a.tn_max = tn_max_for((int)((long long)T * (w->out_dim / dqgemm::GM) / 148));
+    if (xb_lo && a.tn_max > 128) a.tn_max = 128;   // two activation planes per stage
+    a.X2 = xb_lo;
+    a.scale_dtype = w->scale_dtype;
+    a.W = (const uint32_t *)w->W;
+    a.S = (const uint16_t *)w->scales;
+    a.B = (const uint16_t *)w->biases;
+    a.rows = w->out_dim;
+    a.n_tokens = T;
+    a.X = xb;
+    a.out = out;
+    a.status = ctx->dev_status;
+    return launch_gemm(ctx, st, a, dim3(w->out_dim / dqgemm::GM, 1, (T + a.tn_max - 1) / a.tn_max));
+}
+
+int ensure_ws(finch_ctx *ctx, size_t bytes, cudaStream_t st) {
+    if (ctx->pf_ws_bytes >= bytes) return FINCH_OK;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cap);
+    if (cap != cudaStreamCaptureStatusNone)
+        return finch_fail(ctx, FINCH_E_UNSUPPORTED, "the prefill workspace must be sized by one call outside stream capture first");
+    if (ctx->pf_ws) {
+        cudaStreamSynchronize(st);
+        cudaFree(ctx->pf_ws);
+        ctx->pf_ws = nullptr;
+        ctx->pf_ws_bytes = 0;
+    }
+    if (cudaMalloc(&ctx->pf_ws, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return finch_fail(ctx, FINCH_E_NOMEM, "prefill workspace (%zu bytes)", bytes);
+    }
+    ctx->pf_ws_bytes = bytes;
+    return FINCH_OK;
+}
+
+int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int layer, const void *h_post, const int32_t *ids,
+                     const float *weights, const uint8_t *valid, const finch_shared *shared, const float *h_mid, float *hidden_out, int T) {
+    const finch_config &c = ctx->cfg;
+    const int P = T * c.top_k, H = c.hidden, I = c.moe_inter, Is = shared ? shared->gate.out_dim : 0;
+    const int32_t *slot_row = pool->slot_table_dev + (size_t)layer * pool->n_experts;
+    // workspace carve
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t r = off;
+        off += up256(bytes);
+        return r;
+    };
+    const size_t o_seg = take((c.n_experts + 1) * sizeof(int)), o_order = take((size_t)P * sizeof(int));
+    const size_t o_xb = take((size_t)T * H * 2), o_sg = take((size_t)T * Is * 4), o_su = take((size_t)T * Is * 4), o_sact = take((size_t)T * Is * 4);
+    int rc = ensure_ws(ctx, off, st);
+    if (rc) return rc;
+    char *ws = (char *)ctx->pf_ws;
+    int *seg = (int *)(ws + o_seg), *order = (int *)(ws + o_order);
+    uint16_t *xb = (uint16_t *)(ws + o_xb), *sact = (uint16_t *)(ws + o_sact), *sact_lo = sact + (size_t)T * Is;
+    float *sg = (float *)(ws + o_sg), *su = (float *)(ws + o_su);
+    uint16_t *act = (uint16_t *)ctx->act, *act_lo = act + (size_t)P * I;   // two bf16 planes [P][I] inside the fp32-sized buffer
+    float *down = ctx->partial, *shared_out = ctx->partial + (size_t)P * H;
+
+    pf_sort_kernel<<<1, 1024, 2 * c.n_experts * sizeof(int), st>>>(ids, valid, slot_row, c.n_experts, P, seg, order);
+    FINCH_CUDA_OK(ctx, cudaGetLastError());
+    const uint16_t *x = (const uint16_t *)h_post;
+    if (c.act_dtype != FINCH_BF16) {
+        pf_to_bf16_kernel<<<148, 256, 0, st>>>((const float *)h_post, xb, (size_t)T * H);
+        FINCH_CUDA_OK(ctx, cudaGetLastError());
+        x = xb;
+        ctx->launches++;
+    }
+    ctx->launches++;
+
+    dqgemm::Args a{};
+    a.K = H;
+    a.tn_max = tn_max_for(T < 32 ? T : 32);   // small token tiles keep two CTAs on an SM; popular experts take several
+    a.scale_dtype = c.scale_dtype;
+    a.pool_base = (const uint8_t *)pool->base;
+    a.slot_bytes = pool->slot_bytes;
+    a.slot_row = slot_row;
+    a.hidden = H;
+    a.inter = I;
+    a.seg = seg;
+    a.order = order;
+    a.top_k = c.top_k;
+    a.status = ctx->dev_status;
+    const int ztiles = (T + a.tn_max - 1) / a.tn_max;
+    a.mode = dqgemm::EXPERT_GATEUP;
+    a.X = x;
+    a.act_out = act;
+    a.act_out_lo = act_lo;
+    if ((rc = launch_gemm(ctx, st, a, dim3(I / 64, c.n_experts, ztiles)))) return rc;   // 64 gate + 64 up rows per tile
+    a.mode = dqgemm::EXPERT_DOWN;
+    a.K = I;
+    a.X = act;
+    a.X2 = act_lo;
+    a.out = down;
+    if (a.tn_max > 16) a.tn_max = 16;   // two activation planes per stage
+    if ((rc = launch_gemm(ctx, st, a, dim3(H / dqgemm::GM, c.n_experts, (T + a.tn_max - 1) / a.tn_max)))) return rc;
+
+    if (shared) {
+        if ((rc = dense4_gemm(ctx, st, &shared->gate, x, nullptr, sg, T))) return rc;
+        if ((rc = dense4_gemm(ctx, st, &shared->up, x, nullptr, su, T))) return rc;
+        pf_swiglu_kernel<<<148, 256, 0, st>>>(sg, su, sact, sact_lo, (size_t)T * Is);
+        FINCH_CUDA_OK(ctx, cudaGetLastError());
+        if ((rc = dense4_gemm(ctx, st, &shared->down, sact, sact_lo, shared_out, T))) return rc;
+        ctx->launches++;
+    }
+    pf_combine_kernel<<<dim3((H + 255) / 256, T), 256, 0, st>>>(ids, valid, slot_row, c.n_experts, weights, c.top_k, down,
+                                                                shared ? shared_out : nullptr, shared ? shared->gate_score : nullptr, h_mid,
+                                                                hidden_out, H);
+    FINCH_CUDA_OK(ctx, cudaGetLastError());
+    ctx->launches++;
+    return FINCH_OK;
+}
+
+}  // namespace
+
+extern "C" int finch_set_prefill_mode(finch_ctx *ctx, int mode) {
+    if (!ctx || mode < 0 || mode > 2) return FINCH_E_ARG;
+    ctx->prefill_mode = mode;
+    return FINCH_OK;
+}
 
 extern "C" int finch_encode_moe_prefill(finch_ctx *ctx, finch_stream stream, finch_pool *pool, int layer, const void *h_post,
                                         const int32_t *expert_ids, const float *weights, const uint8_t *valid,
                                         const finch_shared *shared, const float *h_mid, float *hidden_out, int T) {
-    if (!ctx || !h_post || !expert_ids || !weights || !hidden_out || T < 1) return FINCH_E_ARG;
+    if (!ctx || !pool || !h_post || !expert_ids || !weights || !hidden_out || T < 1) return FINCH_E_ARG;
     const finch_config &c = ctx->cfg;
+    const size_t elt = c.act_dtype == FINCH_BF16 ? 2 : 4;
+    bool tc = ctx->prefill_mode == 2 || (ctx->prefill_mode == 0 && T >= TC_MIN_TOKENS);
+    // shapes the tensor-core kernels take: whole 128-row tiles, 128-value K blocks, a 3-bit pool
+    if (c.expert_bits != 3 || c.hidden % 128 || c.moe_inter % 128 || c.top_k > 8) tc = false;
+    if (tc && shared) {
+        if (shared->gate.bits != 4 || shared->gate.out_dim % 128 || shared->gate.in_dim != c.hidden || !shared->gate_score) tc = false;
+    }
+    if (tc) {
+        if (T > c.max_tokens) return finch_fail(ctx, FINCH_E_ARG, "T=%d exceeds max_tokens=%d", T, c.max_tokens);
+        if (pool->ctx != ctx) return finch_fail(ctx, FINCH_E_ARG, "pool belongs to another context");
+        if (layer < 0 || layer >= pool->n_layers) return finch_fail(ctx, FINCH_E_ARG, "layer %d out of range", layer);
+        if (shared) {
+            int rc;
+            if ((rc = dense4_checked(ctx, &shared->gate, "shared gate")) || (rc = dense4_checked(ctx, &shared->up, "shared up")) ||
+                (rc = dense4_checked(ctx, &shared->down, "shared down")))
+                return rc;
+        }
+        cudaSetDevice(c.device);
+        cudaStream_t st = finch_pick_stream(ctx, stream);
+        for (int t0 = 0; t0 < T; t0 += CHUNK) {
+            const int n = T - t0 < CHUNK ? T - t0 : CHUNK;
+            finch_shared sh;
+            if (shared) {
+                sh = *shared;
+                sh.gate_score = shared->gate_score + t0;
+            }
+            const int rc = prefill_tc_chunk(ctx, st, pool, layer, (const char *)h_post + (size_t)t0 * c.hidden * elt,
+                                            expert_ids + (size_t)t0 * c.top_k, weights + (size_t)t0 * c.top_k,
+                                            valid ? valid + (size_t)t0 * c.top_k : nullptr, shared ? &sh : nullptr,
+                                            h_mid ? h_mid + (size_t)t0 * c.hidden : nullptr, hidden_out + (size_t)t0 * c.hidden, n);
+            if (rc) return rc;
+        }
+        return FINCH_OK;
+    }
     int sub = FINCH_MAX_PAIRS / c.top_k;
     if (sub > 8) sub = 8;
     if (sub > c.max_tokens) sub = c.max_tokens;
-    const size_t elt = c.act_dtype == FINCH_BF16 ? 2 : 4;
     for (int t0 = 0; t0 < T; t0 += sub) {
         const int n = T - t0 < sub ? T - t0 : sub;
         finch_shared sh;
@@ -34,4 +312,14 @@ extern "C" int finch_encode_moe_prefill(finch_ctx *ctx, finch_stream stream, fin
         if (rc) return rc;
     }
     return FINCH_OK;
+}
+
+// Dense 4-bit g64 projection for M tokens on the tensor cores: out fp32 [M][out_dim] = x * dequant(w)^T,
+// x bf16 [M][in_dim] on the device (gpu_encode_prefill_matvec, finchmoe/infer.m:3672, for M >= 16).
+extern "C" int finch_encode_dense_gemm(finch_ctx *ctx, finch_stream stream, const finch_wdesc *w, const void *x_bf16, float *out, int M) {
+    if (!ctx || !w || !x_bf16 || !out || M < 1) return FINCH_E_ARG;
+    int rc = dense4_checked(ctx, w, "dense GEMM");
+    if (rc) return rc;
+    cudaSetDevice(ctx->cfg.device);
+    return dense4_gemm(ctx, finch_pick_stream(ctx, stream), w, (const uint16_t *)x_bf16, nullptr, out, M);
 }

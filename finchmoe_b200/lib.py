@@ -67,6 +67,8 @@ _PROTOS = {
     "finch_encode_route_topk": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _i]),
     "finch_encode_moe_decode": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, C.POINTER(Shared), _vp, _vp, _i]),
     "finch_encode_moe_prefill": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, C.POINTER(Shared), _vp, _vp, _i]),
+    "finch_set_prefill_mode": (_i, [_vp, _i]),
+    "finch_encode_dense_gemm": (_i, [_vp, _vp, C.POINTER(WDesc), _vp, _vp, _i]),
     "finch_moe_forward_host": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, C.POINTER(Shared), _vp, _vp, _vp, _i]),
     "finch_event_create": (_i, [_vp, C.POINTER(_vp)]),
     "finch_event_record": (_i, [_vp, _vp]),

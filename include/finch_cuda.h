@@ -194,8 +194,14 @@ FINCH_API int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finch
                                       float *hidden_out, int B);
 
 /* prefill_chunk_cmd3 / _batch_general (finchmoe/infer.m:10704-11241): the same
- * result for a chunk of T tokens; sorts (token, k) pairs by expert and runs a
- * grouped dequant-GEMM so every selected expert is read once. */
+ * result for a chunk of T tokens.  Chunks of 128 tokens and more take the
+ * tensor-core path: (token, k) pairs sorted by expert, grouped dequant-GEMMs on
+ * bf16 tiles (weights RNE-rounded from the exact dequantised value, activations
+ * rounded to bf16, fp32 accumulation), every selected expert read once per 512
+ * tokens.  Shorter chunks go through the decode kernels in groups of eight
+ * tokens and are bit-identical to finch_encode_moe_decode.  T <= max_tokens on
+ * the tensor-core path; its first call sizes a workspace and must be outside
+ * stream capture. */
 FINCH_API int finch_encode_moe_prefill(finch_ctx *ctx, finch_stream stream, finch_pool *pool, int layer,
                                        const void *h_post, const int32_t *expert_ids, const float *weights,
                                        const uint8_t *valid, const finch_shared *shared, const float *h_mid,
@@ -234,6 +240,18 @@ FINCH_API int finch_debug_dequant(finch_ctx *ctx, const finch_wdesc *w, uint8_t 
  * and resets the accumulators. */
 FINCH_API int finch_profile_enable(finch_ctx *ctx, int on);
 FINCH_API int finch_profile_read(finch_ctx *ctx, float *ms_gateup, float *ms_down_combine, int *n_calls);
+
+/* Path selection of finch_encode_moe_prefill: 0 = by chunk length (default),
+ * 1 = always the sub-batch path (exact weights, fp32 activations), 2 = always
+ * the tensor-core path.  The reference has one path only (per-position CMD3). */
+FINCH_API int finch_set_prefill_mode(finch_ctx *ctx, int mode);
+
+/* gpu_encode_prefill_matvec (finchmoe/infer.m:3672) for M >= 16 positions and a
+ * 4-bit g64 tensor: out fp32 [M][out_dim] = x * dequant(w)^T on the tensor
+ * cores; x is bf16 [M][in_dim] on the device, in_dim and out_dim multiples of
+ * 128.  Weights are rounded to bf16 after the exact dequantisation. */
+FINCH_API int finch_encode_dense_gemm(finch_ctx *ctx, finch_stream stream, const finch_wdesc *w, const void *x_bf16,
+                                      float *out, int M);
 
 /* Test hook for finch_encode_moe_decode: it normally decides by the batch size
  * whether a preparation kernel builds the activation operands once per token

@@ -32,10 +32,14 @@ def max_rel_err(a, b, floor_frac=1.0):
     return float(np.max(np.abs(a - b) / np.maximum(np.abs(b), floor)))
 
 
-def assert_close(a, b, what="", cos_min=COS_MIN, rel_max=REL_MAX):
+def assert_close(a, b, what="", cos_min=COS_MIN, rel_max=REL_MAX, tight_rel=TIGHT_REL):
+    """tight_rel=None skips the extra bound: the bf16 path rounds SiLU(gate)*up to bf16, and a last-bit
+    difference in an accumulator can move that rounding by one bf16 step (0.4 % of one term), which
+    is far below REL_MAX of the rms but not below 0.5 % of an element that cancels to 1 % of the rms."""
     assert np.all(np.isfinite(np.asarray(a))), f"{what}: non-finite values"
     c, r = cos_sim(a, b), max_rel_err(a, b)
     assert c >= cos_min and r <= rel_max, f"{what}: cos={c:.8f} max_rel={r:.3e}"
-    tight = max_rel_err(a, b, 1e-2)
-    assert tight <= TIGHT_REL, f"{what}: error against 1% of rms = {tight:.3e}"
+    if tight_rel is not None:
+        tight = max_rel_err(a, b, 1e-2)
+        assert tight <= tight_rel, f"{what}: error against 1% of rms = {tight:.3e}"
     return c, r

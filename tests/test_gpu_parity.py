@@ -322,6 +322,7 @@ def test_moe_prefill_chunk_vs_oracle_and_per_token(api, T):
     cfg = dict(hidden=256, inter=128, sd=L.BF16)
     ctx = api.Context(hidden=256, n_experts=16, top_k=8, moe_inter=128, shared_inter=128, n_layers=1,
                       scale_dtype=L.BF16, act_dtype=L.F32, max_tokens=64)
+    ctx.set_prefill_mode(1)   # the sub-batch path: exact weights, fp32 activations, bit-identical to decode
     pool = ctx.pool()
     try:
         rng = synth.rng_for(3, T)
