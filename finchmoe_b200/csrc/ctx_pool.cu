@@ -311,10 +311,11 @@ __device__ __forceinline__ uint16_t synth_scale16(uint64_t key, int scale_dtype,
     return bias ? __bfloat16_as_ushort(__float2bfloat16_rn(-4.0f * __bfloat162float(h))) : __bfloat16_as_ushort(h);
 }
 
-__global__ void pool_fill_kernel(uint8_t *base, size_t slot_bytes, int first_slot, uint64_t seed, FinchTile T, int scale_dtype) {
+// The contents depend on the expert's key (layer * n_experts + expert), not on the slot that stores it.
+__global__ void pool_fill_kernel(uint8_t *base, size_t slot_bytes, int first_slot, int first_key, uint64_t seed, FinchTile T, int scale_dtype) {
     const size_t words = T.total / 4;
-    const int slot = first_slot + blockIdx.y;
-    uint32_t *blk = reinterpret_cast<uint32_t *>(base + (size_t)slot * slot_bytes);
+    const int slot = first_key + blockIdx.y;   // the name the generator mixes in
+    uint32_t *blk = reinterpret_cast<uint32_t *>(base + (size_t)(first_slot + blockIdx.y) * slot_bytes);
     for (size_t w = (size_t)blockIdx.x * blockDim.x + threadIdx.x; w < words; w += (size_t)gridDim.x * blockDim.x) {
         const size_t off = w * 4;
         const bool isB = off >= T.b_base;
@@ -354,8 +355,41 @@ extern "C" int finch_pool_fill_synthetic(finch_pool *p, int layer0, int layer1, 
             }
         }
         dim3 grid(64, p->n_experts);
-        pool_fill_kernel<<<grid, 256, 0, ctx->stream>>>(p->base, p->slot_bytes, l * p->n_experts, seed + (uint64_t)l * 0x10001ull, T,
+        pool_fill_kernel<<<grid, 256, 0, ctx->stream>>>(p->base, p->slot_bytes, l * p->n_experts, l * p->n_experts, seed + (uint64_t)l * 0x10001ull, T,
                                                         ctx->cfg.scale_dtype);
+        FINCH_CUDA_OK(ctx, cudaGetLastError());
+    }
+    p->used = 0;
+    for (int s = 0; s < p->slots; s++) p->used += p->owner[s] >= 0;
+    FINCH_CUDA_OK(ctx, cudaMemcpyAsync(p->slot_table_dev, p->slot_of.data(), p->slot_of.size() * sizeof(int32_t),
+                                       cudaMemcpyHostToDevice, ctx->stream));
+    FINCH_CUDA_OK(ctx, cudaStreamSynchronize(ctx->stream));
+    return FINCH_OK;
+}
+
+// The same generator for one shard of the experts (expert-parallel ranks): experts [e0, e1) of layers
+// [layer0, layer1) get exactly the contents finch_pool_fill_synthetic gives them in a full pool, stored in
+// slots layer * (e1 - e0) + (expert - e0).
+extern "C" int finch_pool_fill_synthetic_range(finch_pool *p, int layer0, int layer1, int e0, int e1, uint64_t seed) {
+    if (!p || layer0 < 0 || layer1 > p->n_layers || layer0 >= layer1 || e0 < 0 || e1 > p->n_experts || e0 >= e1) return FINCH_E_ARG;
+    finch_ctx *ctx = p->ctx;
+    const int per = e1 - e0;
+    if (p->slots < p->n_layers * per) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "pool has %d slots, the shard needs %d", p->slots, p->n_layers * per);
+    cudaSetDevice(ctx->cfg.device);
+    const FinchTile T = finch_tile(ctx->cfg.hidden, ctx->cfg.moe_inter);
+    for (int l = layer0; l < layer1; l++) {
+        for (int e = e0; e < e1; e++) {
+            const int key = l * p->n_experts + e, slot = l * per + (e - e0);
+            if (p->slot_of[key] < 0 && p->owner[slot] < 0) {
+                p->slot_of[key] = slot;
+                p->owner[slot] = key;
+                p->last_used[slot] = ++p->clock;
+            } else if (p->slot_of[key] != slot) {
+                return finch_fail(ctx, FINCH_E_UNSUPPORTED, "pool already holds experts in other slots");
+            }
+        }
+        pool_fill_kernel<<<dim3(64, per), 256, 0, ctx->stream>>>(p->base, p->slot_bytes, l * per, l * p->n_experts + e0,
+                                                                 seed + (uint64_t)l * 0x10001ull, T, ctx->cfg.scale_dtype);
         FINCH_CUDA_OK(ctx, cudaGetLastError());
     }
     p->used = 0;

@@ -1,0 +1,199 @@
+"""Expert-parallel MoE layer: one process per GPU, experts sharded in contiguous blocks.
+
+Rank r of G owns experts [r*E/G, (r+1)*E/G) of every layer and keeps only those in its HBM pool;
+tokens stay with the rank that owns them (each rank routes its own tokens).  One layer:
+
+  1. plan      which of my tokens go to which rank -- a token goes to a rank once, with its whole row of
+               expert ids and router weights, however many of its experts live there
+  2. counts    all-to-all of the per-destination row counts (the only host synchronisation of the layer)
+  3. dispatch  all-to-all of the packed records (activation row + ids + weights + mask)
+  4. local     the rank's ordinary MoE path over the rows it received; experts that are not in its
+               pool are skipped, so each output row is the weighted sum over the local experts
+  5. return    all-to-all of the fp32 partial rows
+  6. combine   hidden = h_mid + shared expert (computed where the token lives) + partial rows added in
+               ascending rank order, so the result does not depend on arrival order
+
+The collectives go through torch.distributed (NCCL on GPUs; gloo in the CPU tests).  `ep_layer` holds the
+protocol and is backend-agnostic: the GPU backend drives the C-ABI steps (finch_encode_ep_*), the CPU
+tests plug in a numpy backend with the same five operations.  With G = 1 the same code runs and the
+all-to-alls degenerate to copies.
+
+The reference runs on one device (finchmoe/infer.m:9597-9741 is the per-layer path this extends).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+
+def owner_of(expert: int, n_experts: int, world: int) -> int:
+    return expert // (n_experts // world)
+
+
+def plan_numpy(ids: np.ndarray, valid, n_experts: int, world: int):
+    """Host mirror of finch_encode_ep_plan: (counts[G], offs[G+1], send_tok, slot_of[T,G])."""
+    T, K = ids.shape
+    per = n_experts // world
+    ok = (ids >= 0) & (ids < n_experts)
+    if valid is not None:
+        ok &= valid.astype(bool)
+    dest = np.where(ok, ids // per, -1)
+    counts = np.zeros(world, np.int32)
+    slot_of = np.full((T, world), -1, np.int32)
+    lists = []
+    for d in range(world):
+        toks = np.nonzero((dest == d).any(axis=1))[0].astype(np.int32)
+        counts[d] = toks.size
+        slot_of[toks, d] = np.arange(toks.size, dtype=np.int32)
+        lists.append(toks)
+    offs = np.zeros(world + 1, np.int32)
+    offs[1:] = np.cumsum(counts)
+    return counts, offs, np.concatenate(lists) if lists else np.zeros(0, np.int32), slot_of
+
+
+def ep_layer(backend, dist, group, layer: int, x, ids, weights, valid, shared, h_mid, out):
+    """The protocol.  `dist` is torch.distributed (or None for a single process); tensors are whatever
+    the backend uses (torch tensors on the backend's device).  Returns `out`."""
+    with backend.stream_scope():
+        return _ep_layer(backend, dist, group, layer, x, ids, weights, valid, shared, h_mid, out)
+
+
+def _ep_layer(backend, dist, group, layer, x, ids, weights, valid, shared, h_mid, out):
+    import torch
+    world = dist.get_world_size(group) if dist is not None else 1
+    h = backend.plan(ids, valid, world)                       # -> object with .counts (int32 [G] tensor)
+    recv_counts = torch.empty_like(h.counts)
+    if world > 1:
+        dist.all_to_all_single(recv_counts, h.counts, group=group)
+    else:
+        recv_counts.copy_(h.counts)
+    c_send = h.counts.cpu().tolist()                           # host sync: split sizes must be host integers
+    c_recv = recv_counts.cpu().tolist()
+    rec = backend.record_bytes()
+    send_buf = backend.pack(h, x, ids, weights, valid, sum(c_send))            # uint8 [sum(c_send) * rec]
+    recv_buf = backend.empty_bytes(sum(c_recv) * rec)
+    if world > 1:
+        dist.all_to_all_single(recv_buf, send_buf, [c * rec for c in c_recv], [c * rec for c in c_send], group=group)
+    else:
+        recv_buf.copy_(send_buf)
+    part = backend.local_moe(layer, recv_buf, sum(c_recv))                      # fp32 [sum(c_recv), H]
+    H = backend.hidden
+    back = backend.empty_f32(sum(c_send) * H)
+    if world > 1:
+        dist.all_to_all_single(back, part.reshape(-1), [c * H for c in c_send], [c * H for c in c_recv], group=group)
+    else:
+        back.copy_(part.reshape(-1))
+    backend.base(layer, x, ids, weights, shared, h_mid, out)                    # h_mid + shared expert, no routed expert
+    backend.combine(h, out, back)
+    return out
+
+
+class _Plan:
+    pass
+
+
+class GpuBackend:
+    """Drives the C-ABI steps on one GPU.  torch holds the device buffers."""
+
+    def __init__(self, ctx, pool, max_rows: int):
+        """max_rows: the most rows this rank may receive in one layer (sum over sources)."""
+        import torch
+        self.torch, self.ctx, self.pool, self.lib = torch, ctx, pool, ctx.lib
+        self.hidden, self.K = ctx.cfg.hidden, ctx.cfg.top_k
+        self.elt = 2 if ctx.cfg.act_dtype == 0 else 4
+        self.max_rows = max_rows
+        dev = torch.device("cuda", ctx.cfg.device)
+        self.dev = dev
+        self.rx = torch.empty(max_rows * self.hidden * self.elt, dtype=torch.uint8, device=dev)
+        self.rids = torch.empty((max_rows, self.K), dtype=torch.int32, device=dev)
+        self.rw = torch.empty((max_rows, self.K), dtype=torch.float32, device=dev)
+        self.rv = torch.empty((max_rows, self.K), dtype=torch.uint8, device=dev)
+        self.rout = torch.empty((max_rows, self.hidden), dtype=torch.float32, device=dev)
+        self.zero_valid = None
+
+        self.stream = torch.cuda.Stream(device=dev)   # kernels, copies and collectives of a layer are ordered on it
+
+    def _stream(self):
+        return self.stream.cuda_stream
+
+    def stream_scope(self):
+        """Runs the layer on the backend's stream: it first waits for what the caller's stream has queued
+        (the inputs), and the caller's stream waits for it afterwards."""
+        import contextlib
+        torch = self.torch
+
+        @contextlib.contextmanager
+        def scope():
+            outer = torch.cuda.current_stream(self.dev)
+            self.stream.wait_stream(outer)
+            with torch.cuda.stream(self.stream):
+                yield
+            outer.wait_stream(self.stream)
+        return scope()
+
+    def record_bytes(self):
+        return self.lib.finch_ep_record_bytes(self.ctx.h)
+
+    def empty_bytes(self, n):
+        return self.torch.empty(n, dtype=self.torch.uint8, device=self.dev)
+
+    def empty_f32(self, n):
+        return self.torch.empty(n, dtype=self.torch.float32, device=self.dev)
+
+    def plan(self, ids, valid, world):
+        torch = self.torch
+        T = ids.shape[0]
+        p = _Plan()
+        p.T, p.world = T, world
+        p.counts = torch.empty(world, dtype=torch.int32, device=self.dev)
+        p.offs = torch.empty(world + 1, dtype=torch.int32, device=self.dev)
+        p.send_tok = torch.empty(T * world, dtype=torch.int32, device=self.dev)
+        p.slot_of = torch.empty((T, world), dtype=torch.int32, device=self.dev)
+        self.ctx.check(self.lib.finch_encode_ep_plan(self.ctx.h, self._stream(), ids.data_ptr(), valid.data_ptr() if valid is not None else None,
+                                                     T, world, p.counts.data_ptr(), p.offs.data_ptr(), p.send_tok.data_ptr(),
+                                                     p.slot_of.data_ptr()))
+        return p
+
+    def pack(self, p, x, ids, weights, valid, n_rows):
+        buf = self.empty_bytes(n_rows * self.record_bytes())
+        self.ctx.check(self.lib.finch_encode_ep_pack(self.ctx.h, self._stream(), x.data_ptr(), ids.data_ptr(), weights.data_ptr(),
+                                                     valid.data_ptr() if valid is not None else None, p.T, p.world, p.offs.data_ptr(),
+                                                     p.send_tok.data_ptr(), buf.data_ptr()))
+        return buf
+
+    def local_moe(self, layer, recv_buf, n):
+        if n > self.max_rows:
+            raise ValueError(f"received {n} rows, backend sized for {self.max_rows}")
+        st = self._stream()
+        self.ctx.check(self.lib.finch_encode_ep_unpack(self.ctx.h, st, recv_buf.data_ptr(), n, self.rx.data_ptr(), self.rids.data_ptr(),
+                                                       self.rw.data_ptr(), self.rv.data_ptr()))
+        step = self.ctx.cfg.max_tokens
+        for r0 in range(0, n, step):
+            m = min(step, n - r0)
+            self.ctx.check(self.lib.finch_encode_moe_prefill(
+                self.ctx.h, st, self.pool.h, layer, self.rx.data_ptr() + r0 * self.hidden * self.elt, self.rids[r0:].data_ptr(),
+                self.rw[r0:].data_ptr(), self.rv[r0:].data_ptr(), None, None, self.rout[r0:].data_ptr(), m))
+        return self.rout[:n]
+
+    def base(self, layer, x, ids, weights, shared, h_mid, out):
+        torch = self.torch
+        T = ids.shape[0]
+        if self.zero_valid is None or self.zero_valid.shape[0] < T:
+            self.zero_valid = torch.zeros((T, self.K), dtype=torch.uint8, device=self.dev)
+        st = self._stream()
+        step = self.ctx.cfg.max_tokens
+        for t0 in range(0, T, step):
+            m = min(step, T - t0)
+            sh = None
+            if shared is not None:
+                from . import lib as L
+                sh = L.Shared(shared.gate, shared.up, shared.down, shared.gate_score + 4 * t0)
+            self.ctx.check(self.lib.finch_encode_moe_prefill(
+                self.ctx.h, st, self.pool.h, layer, x.data_ptr() + t0 * self.hidden * self.elt, ids[t0:].data_ptr(), weights[t0:].data_ptr(),
+                self.zero_valid.data_ptr(), C.byref(sh) if sh is not None else None,
+                h_mid[t0:].data_ptr() if h_mid is not None else None, out[t0:].data_ptr(), m))
+
+    def combine(self, p, out, back):
+        self.ctx.check(self.lib.finch_encode_ep_combine(self.ctx.h, self._stream(), out.data_ptr(), back.data_ptr(), p.slot_of.data_ptr(),
+                                                        p.offs.data_ptr(), p.T, p.world))

@@ -253,6 +253,34 @@ FINCH_API int finch_set_prefill_mode(finch_ctx *ctx, int mode);
 FINCH_API int finch_encode_dense_gemm(finch_ctx *ctx, finch_stream stream, const finch_wdesc *w, const void *x_bf16,
                                       float *out, int M);
 
+/* ---- expert parallelism (no counterpart in the reference, which runs on one
+ * device; extends the per-layer CMD3 of finchmoe/infer.m:9597-9741 across GPUs).
+ * Rank r of `world` owns experts [r*E/world, (r+1)*E/world) of every layer and
+ * keeps only those in its pool; tokens stay with their owner.  The host layer
+ * (finchmoe_b200/ep.py) runs, per layer: plan -> pack -> all-to-all (NCCL) ->
+ * unpack -> finch_encode_moe_prefill on the received rows (experts that are not
+ * in the pool are skipped, so the result is the weighted sum over the local
+ * experts) -> all-to-all back -> combine.  All pointers are device pointers. */
+
+/* Bytes of one dispatch record: activation row, K ids, K weights, K mask bytes, padded to 16. */
+FINCH_API int finch_ep_record_bytes(const finch_ctx *ctx);
+/* counts[world], offs[world + 1] (exclusive prefix), send_tok[<= T * world] (tokens per
+ * destination, ascending), slot_of[T][world] (position of token t in destination d's list, or -1).
+ * A token goes to a rank once, however many of its experts live there. */
+FINCH_API int finch_encode_ep_plan(finch_ctx *ctx, finch_stream stream, const int32_t *expert_ids, const uint8_t *valid,
+                                   int T, int world, int *counts, int *offs, int *send_tok, int *slot_of);
+FINCH_API int finch_encode_ep_pack(finch_ctx *ctx, finch_stream stream, const void *h_post, const int32_t *expert_ids,
+                                   const float *weights, const uint8_t *valid, int T, int world, const int *offs,
+                                   const int *send_tok, void *records);
+FINCH_API int finch_encode_ep_unpack(finch_ctx *ctx, finch_stream stream, const void *records, int n, void *h_post,
+                                     int32_t *expert_ids, float *weights, uint8_t *valid);
+/* hidden_out[t] += sum over destinations d in ascending order of back_rows[offs[d] + slot_of[t][d]]. */
+FINCH_API int finch_encode_ep_combine(finch_ctx *ctx, finch_stream stream, float *hidden_out, const float *back_rows,
+                                      const int *slot_of, const int *offs, int T, int world);
+/* Synthetic contents for one shard: experts [e0, e1) of layers [layer0, layer1) get the bytes
+ * finch_pool_fill_synthetic gives them in a full pool; the pool needs n_layers * (e1 - e0) slots. */
+FINCH_API int finch_pool_fill_synthetic_range(finch_pool *pool, int layer0, int layer1, int e0, int e1, uint64_t seed);
+
 /* Test hook for finch_encode_moe_decode: it normally decides by the batch size
  * whether a preparation kernel builds the activation operands once per token
  * (mode -1); 0 forces the build inside every CTA, 1 forces the preparation

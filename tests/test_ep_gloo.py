@@ -1,0 +1,76 @@
+"""The expert-parallel protocol (finchmoe_b200/ep.py) on CPU: two gloo ranks, numpy backend, oracle
+arithmetic.  Checks the plan (one record per token and destination), the variable-size all-to-alls and the
+fixed-order combine against a single-process oracle run over all experts."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+
+from finchmoe_b200 import ep, synth
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def test_plan_sends_a_token_once_per_rank_and_skips_unusable_pairs():
+    ids = np.array([[0, 1, 4, 7], [5, 6, 7, 4], [2, 3, 0, 1], [9, -1, 3, 3]], np.int32)   # 8 experts, 2 ranks: 0-3 | 4-7
+    valid = np.ones_like(ids, dtype=np.uint8)
+    valid[0, 2] = 0                                  # token 0's expert 4 is masked; expert 7 still sends it to rank 1
+    counts, offs, send_tok, slot_of = ep.plan_numpy(ids, valid, 8, 2)
+    assert counts.tolist() == [3, 2]                 # rank 0: tokens 0, 2, 3; rank 1: tokens 0, 1
+    assert offs.tolist() == [0, 3, 5]
+    assert send_tok.tolist() == [0, 2, 3, 0, 1]
+    assert slot_of.tolist() == [[0, 0], [-1, 1], [1, -1], [2, -1]]
+    # a token whose pairs are all unusable goes nowhere
+    c2, _, _, s2 = ep.plan_numpy(np.array([[8, -5]], np.int32), None, 8, 2)
+    assert c2.tolist() == [0, 0] and s2.tolist() == [[-1, -1]]
+
+
+WORKER = r'''
+import os, sys
+sys.path.insert(0, sys.argv[3]); sys.path.insert(0, os.path.dirname(sys.argv[3]))
+import numpy as np, torch, torch.distributed as dist
+from finchmoe_b200 import ep, synth
+from oracle import oracle
+from ep_cpu_backend import NumpyBackend
+rank, world = int(sys.argv[1]), 2
+dist.init_process_group("gloo", init_method="tcp://127.0.0.1:" + sys.argv[2], rank=rank, world_size=world)
+cfg = dict(hidden=256, inter=128, n_experts=8, K=4, sd=oracle.SCALE_BF16)
+rng = synth.rng_for(9, 1)                          # both ranks draw the same model
+blocks = {e: synth.expert_block(rng, 256, 128, 64, 3, cfg["sd"]) for e in range(8)}
+shared = synth.shared_expert(rng, 256, 128, 64, 4, cfg["sd"])
+T = (5, 7)[rank]                                   # ragged: the ranks own different numbers of tokens
+r2 = synth.rng_for(9, 2, rank)
+x = r2.normal(0, 1, size=(T, 256)).astype(np.float32)
+ids, w = synth.zipf_routing(r2, T, 8, 4)
+valid = (r2.random((T, 4)) > 0.2).astype(np.uint8)
+if rank == 1:
+    valid[0] = 0                                   # a token with no usable expert at all
+score = r2.normal(0, 1, size=T).astype(np.float32)
+h_mid = r2.normal(0, 1, size=(T, 256)).astype(np.float32)
+per = 8 // world
+backend = NumpyBackend(cfg, {e: b for e, b in blocks.items() if e // per == rank}, shared)
+out = torch.empty((T, 256), dtype=torch.float32)
+ep.ep_layer(backend, dist, None, 0, torch.from_numpy(x), torch.from_numpy(ids), torch.from_numpy(w), torch.from_numpy(valid),
+            score, torch.from_numpy(h_mid), out)
+want = np.stack([oracle.moe_layer([blocks[int(e)] if valid[t, k] else None for k, e in enumerate(ids[t])], w[t], valid[t], x[t], bits=3,
+                                  scale_dtype=cfg["sd"], hidden=256, inter=128, h_mid=h_mid[t], shared=shared,
+                                  shared_gate_score=float(score[t])) for t in range(T)])
+err = np.abs(out.numpy() - want).max() / np.sqrt((want.astype(np.float64) ** 2).mean())
+assert err < 1e-5, err                             # same arithmetic, only the order of the fp32 additions differs
+dist.barrier()
+dist.destroy_process_group()
+print("rank", rank, "ok", err)
+'''
+
+
+def test_two_rank_layer_matches_single_process_oracle(tmp_path):
+    script = tmp_path / "ep_worker.py"
+    script.write_text(WORKER)
+    port = str(29600 + os.getpid() % 300)
+    procs = [subprocess.Popen([sys.executable, str(script), str(r), port, HERE], stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+             for r in range(2)]
+    outs = [p.communicate(timeout=240)[0] for p in procs]
+    for r, (p, o) in enumerate(zip(procs, outs)):
+        assert p.returncode == 0, f"rank {r} failed:\n{o[-3000:]}"
+        assert f"rank {r} ok" in o
