@@ -108,7 +108,7 @@ def measured_peaks():
     if os.path.exists(p):
         with open(p) as f:
             return json.load(f), "measured"
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
 # --------------------------------------------------------------------- CPU arm
@@ -185,15 +185,22 @@ def run_reference(args):
 class Stack:
     """The 40-layer expert stack resident on one GPU."""
 
-    def __init__(self, device: int, max_tokens: int, layers: int = LAYERS, seed: int = 2024):
+    def __init__(self, device: int, max_tokens: int, layers: int = LAYERS, seed: int = 2024, shard=None):
+        """shard = (rank, world): keep only this rank's contiguous block of experts (expert parallelism)."""
         import torch
 
         from finchmoe_b200 import api, lib as L
         self.torch, self.L = torch, L
         torch.cuda.set_device(device)
         self.ctx = api.Context(device=device, n_layers=layers, max_tokens=max_tokens, scale_dtype=L.FP16, act_dtype=L.BF16)
-        self.pool = self.ctx.pool()
-        self.pool.fill_synthetic(0, layers, seed)
+        if shard is None:
+            self.pool = self.ctx.pool()
+            self.pool.fill_synthetic(0, layers, seed)
+        else:
+            rank, world = shard
+            per = NEXP // world
+            self.pool = self.ctx.pool(max_slots=layers * per)
+            self.ctx.check(self.ctx.lib.finch_pool_fill_synthetic_range(self.pool.h, 0, layers, rank * per, (rank + 1) * per, seed))
         self.layers = layers
         self.shared = []
         for l in range(layers):
@@ -260,6 +267,30 @@ class Stack:
             barrier()
         return e0.elapsed_time(e1) / 1e3  # seconds for `steps` steps
 
+    def time_prefill(self, T, steps, warmup):
+        """One chunk of T tokens through finch_encode_moe_prefill on every layer; seconds per pass, distinct experts."""
+        torch = self.torch
+        rs = routing_sets(T, 1, self.layers)
+        dev, xd, score, out, _ = self.device_inputs(rs, T)
+        ids, w = dev[0]
+
+        def step():
+            st = self.stream.cuda_stream
+            for l in range(self.layers):
+                sh = self.ctx.make_shared(*self.shared[l], gate_score=score)
+                self.ctx.encode_moe_decode(self.pool, l, xd, ids[l], w[l], None, sh, None, out[l], T, stream=st, prefill=True)
+        for _ in range(max(1, warmup)):
+            step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        for _ in range(steps):
+            step()
+        e1.record(self.stream)
+        torch.cuda.synchronize()
+        uniq = sum(len(set(i_.ravel().tolist())) for i_, _ in rs[0])
+        return e0.elapsed_time(e1) / 1e3 / steps, uniq
+
     def time_e2e(self, rsets, x, batch, steps, warmup):
         """Host buffers in and out through finch_moe_forward_host, layer by layer."""
         torch = self.torch
@@ -293,10 +324,10 @@ def run_ours(args):
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
-    # N > 1: decode does not shard across GPUs without an exchange step; each rank runs an
-    # independent replica of the stack on its own token batch (weak scaling, no collective).
+    if world > 1:
+        return run_ep(args, rank, local_rank, world)
     batch = 8
-    stack = Stack(local_rank, max_tokens=8, layers=LAYERS)
+    stack = Stack(local_rank, max_tokens=512, layers=LAYERS)
     n_sets = 4
     rsets = [[(ids, w) for ids, w in rs] for rs in routing_sets(batch, n_sets)]
     if world > 1:  # a different token batch per rank
@@ -371,6 +402,17 @@ def run_ours(args):
                           "us_per_layer": s1 / args.steps / LAYERS * 1e6, "frac_of_" + peak_kind: b1 / s1 / 1e9 / peaks["hbm_gbs"]}
         # per-kernel roofline of the dominant kernel (gate/up/SiLU)
         line["roofline"] = kernel_roofline(stack, dev, rsets, xd, score, out, batch, args, peaks, peak_kind)
+        # chunked prefill: 512-token chunks through the grouped dequant-GEMM (tcgen05), the whole stack
+        T = 512
+        ps, uniq = stack.time_prefill(T, max(2, args.steps // 4), 1)
+        flops = LAYERS * (T * TOPK * 6291456 + T * 3 * 2 * 512 * HIDDEN)
+        pbytes = uniq * EXPERT_BYTES + LAYERS * SHARED_BYTES
+        ai = flops / pbytes
+        ceil_tf = min(peaks["bf16_tflops_sustained"], ai * peaks["hbm_gbs"] / 1e3)
+        line["prefill"] = {"metric": "moe3_prefill_tokens_per_s", "chunk": T, "value": T / ps, "unit": "tokens/s (40 MoE layers per token)",
+                           "ms_per_chunk": ps * 1e3, "tflops": flops / ps / 1e12, "hbm_gbs": pbytes / ps / 1e9,
+                           "roofline": {"bound": "hbm", "note": "8T/256 pairs per expert: below the tensor ridge", "ceiling_tflops": ceil_tf,
+                                        "frac": flops / ps / 1e12 / ceil_tf, "peak_kind": peak_kind}}
         # CPU baseline: bounded sample of the same workload on the expert blocks of this pool
         cores = os.cpu_count() or 1
         sample_layers = 2
@@ -382,6 +424,101 @@ def run_ours(args):
         import torch.distributed as dist
         dist.barrier()
         dist.destroy_process_group()
+
+
+
+def run_ep(args, rank, local_rank, world):
+    """N > 1: the batched-decode layer is expert parallel.  Every rank owns 8 tokens per step (weak scaling:
+    8 N tokens per step in all) and the contiguous block of 256 / N experts of every layer; per layer the
+    ranks exchange activation rows and partial outputs (finchmoe_b200/ep.py).  value = bytes of the distinct
+    local experts each rank streams per step (plus its copy of the shared expert), summed over ranks, per
+    second of the slowest rank."""
+    import torch
+    import torch.distributed as dist
+
+    from finchmoe_b200 import ep
+    batch, n_sets = 8, 4
+    stack = Stack(local_rank, max_tokens=8 * world, layers=LAYERS, shard=(rank, world))
+    per = NEXP // world
+    # every rank can regenerate every rank's routing (seeded), which is all the byte count needs
+    all_sets = [[[synth.zipf_routing(synth.rng_for(2, l, 100 + s + 1000 * r), batch, NEXP, TOPK) for l in range(LAYERS)]
+                 for s in range(n_sets)] for r in range(world)]
+    rsets = all_sets[rank]
+    dev, xd, score, out, x = stack.device_inputs(rsets, batch)
+    backend = ep.GpuBackend(stack.ctx, stack.pool, batch * world)
+    shared = [stack.ctx.make_shared(*stack.shared[l], gate_score=score) for l in range(LAYERS)]
+
+    def step(i, xin=None):
+        ids, w = dev[i % n_sets]
+        for l in range(LAYERS):
+            ep.ep_layer(backend, dist, None, l, xd if xin is None else xin, ids[l], w[l], None, shared[l], None, out[l])
+
+    def timed(n, w0, fn):
+        for i in range(w0):
+            fn(i)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(n):
+            fn(w0 + i)
+        e1.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        t = torch.tensor([e0.elapsed_time(e1) / 1e3], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    secs = timed(args.steps, args.warmup, step)
+    clocks = sampler.stop() if sampler else None
+
+    # end to end: the step's inputs come from pinned host memory and its result goes back to the host
+    xh = torch.from_numpy(stack.ctx.acts_to_wire(x).view(np.int16)).pin_memory()
+    res = torch.empty((batch, HIDDEN), dtype=torch.float32).pin_memory()
+
+    def step_e2e(i):
+        xin = xh.to("cuda", non_blocking=True).view(torch.bfloat16)
+        step(i, xin)
+        res.copy_(out[LAYERS - 1], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e2e_secs = timed(args.steps, max(1, args.warmup // 2), step_e2e)
+
+    def step_bytes(s):
+        total = 0
+        for l in range(LAYERS):
+            touched = set()
+            for r in range(world):
+                touched |= set(all_sets[r][s][l][0].ravel().tolist())
+            total += len(touched) * EXPERT_BYTES + world * SHARED_BYTES     # every rank reads its own copy of the shared expert
+        return total
+    timed_bytes = sum(step_bytes((args.warmup + i) % n_sets) for i in range(args.steps))
+    e2e_bytes = sum(step_bytes((max(1, args.warmup // 2) + i) % n_sets) for i in range(args.steps))
+    if rank == 0:
+        peaks, peak_kind = measured_peaks()
+        value = timed_bytes / secs / 1e9
+        rows_per_layer = None
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "C5: expert-parallel batched decode, 40 layers, 8 tokens per GPU per step, top-8 of 256, Zipf(1.1)",
+                       "batch": batch * world, "layers": LAYERS, "hidden": HIDDEN, "moe_inter": INTER, "scale_dtype": "fp16",
+                       "act_dtype": "bf16", "experts_per_gpu": per, "parallelism": f"ep{world}",
+                       "exchange": "3 all-to-alls per layer over NCCL (row counts, records, partial rows); one host sync per layer",
+                       "l2": "inputs larger than L2: the pool shards exceed it; 4 routing sets rotate"},
+            "clocks": clocks,
+            "e2e": {"value": e2e_bytes / e2e_secs / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(xh.numel() * 2 * world),
+                    "d2h_bytes_per_step": int(res.numel() * 4 * world)},
+            "gpu_launches": int(stack.ctx.launch_count()),
+            "tokens_per_s": batch * world * args.steps / secs,
+            "us_per_layer": secs / args.steps / LAYERS * 1e6,
+            "hbm_frac_of_" + peak_kind: value / world / peaks["hbm_gbs"],
+        }
+        del rows_per_layer
+        print(json.dumps(line))
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def kernel_roofline(stack, dev, rsets, xd, score, out, batch, args, peaks, peak_kind):
