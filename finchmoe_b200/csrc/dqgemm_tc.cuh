@@ -2,7 +2,7 @@
 //
 //   D[128 weight rows, TN tokens] += Wdq[128, K] * X[TN, K]^T        (bf16 x bf16 -> fp32)
 //
-// One CTA owns one 128-row weight tile and up to TNMAX tokens.  Per K-block of 128 values its sixteen
+// One CTA owns one 128-row weight tile and up to TNMAX tokens.  Per K-block of 128 values its eight
 // warps read packed codes straight from HBM, dequantise them to bf16 -- RNE(fl32(fl32(q*s)+b)), the
 // value the reference's dequantised weight rounds to (quant_audit.py:245 semantics) -- and write them,
 // together with the tokens' activations, into shared memory in the 128-byte-swizzled K-major layout
@@ -22,7 +22,7 @@ namespace dqgemm {
 constexpr int GM = 128;       // weight rows per CTA = UMMA M
 constexpr int BK = 128;       // K values per stage = two 64-value swizzle atoms
 constexpr int NS = 2;         // stages
-constexpr int NT = 512;       // threads per CTA: four per weight row, one for each 32-value quarter of a K block
+constexpr int NT = 256;       // threads per CTA: two per weight row, one for each 64-value half (= scale group) of a K block
 constexpr int A_ATOM = GM * 128;   // bytes of one 64-value atom of the weight tile
 constexpr int RD = 4;         // depth of the ring of packed expert blocks (EXPERT_* modes)
 constexpr int RAW_STAGE = 8 * 768 + 8 * 128;   // one K block of eight 16-row pool tiles: operand words, then scale/bias entries
@@ -41,6 +41,8 @@ struct Args {
     int hidden, inter;
     const int *seg;           // [n_experts + 1] ranges of `order`
     const int *order;         // pair ids sorted by expert
+    const int2 *items;        // (expert, first pair of the tile inside the expert's range), one per blockIdx.y
+    const int *n_items;
     int top_k;
     // DENSE4: reference tensor layout (u32 words, 16-bit scales and biases per group of 64)
     const uint32_t *W;
@@ -61,6 +63,7 @@ struct Args {
 __host__ __device__ inline int smem_bytes(int tn_max, int planes, int expert) {
     return 1024 + NS * (2 * A_ATOM + planes * 2 * tn_max * 128) + (expert ? RD * RAW_STAGE : 0) + 256 + tn_max * 4;
 }
+
 __host__ __device__ inline int tmem_cols(int tn_max) { return tn_max <= 32 ? 32 : tn_max <= 64 ? 64 : tn_max <= 128 ? 128 : 256; }
 
 // ---- tcgen05 wrappers ----------------------------------------------------
@@ -183,45 +186,60 @@ __device__ __forceinline__ void dq4_word(uint32_t w, const GroupScale &gs, uint3
     for (int i = 0; i < 4; i++) o[i] = bf16x2_rn(v[2 * i], v[2 * i + 1]);
 }
 
-// grid: x = 128-row weight tile, y = expert (EXPERT_*) or 0, z = token tile.  block: 128 threads.
+// grid: x = 128-row weight tile; EXPERT_*: y = (expert, token tile) item; DENSE4: z = token tile.  block: 256 threads.
+//
+// No CTA-wide barrier inside the K loop.  Every warp dequantises its share of block kb into stage
+// kb % NS and arrives on a_full[stage]; lane 0 of warp 0 then issues the block's MMAs and commits them
+// to done[stage], which frees the stage, while the other warps already work on block kb + 1;
+// lane 0 of warp 1 keeps the ring of packed blocks filled, waiting on raw_empty[slot] (all warps
+// have read the slot) before a refill.
 __global__ void __launch_bounds__(NT) dqgemm_tc_kernel(const Args a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tn_max = a.tn_max;
     // ---- which tokens ----
-    int m_total, first;
+    int m_total, first, t0, expert_id = 0;
     const int *rows_of = nullptr;   // EXPERT_*: pair ids of this expert
     if (a.mode == DENSE4) {
         m_total = a.n_tokens;
         first = 0;
+        t0 = blockIdx.z * tn_max;
     } else {
-        const int e = blockIdx.y;
-        first = a.seg[e];
-        m_total = a.seg[e + 1] - first;
+        if ((int)blockIdx.y >= *a.n_items) return;
+        const int2 it = a.items[blockIdx.y];
+        expert_id = it.x;
+        t0 = it.y;
+        first = a.seg[expert_id];
+        m_total = a.seg[expert_id + 1] - first;
         rows_of = a.order + first;
     }
-    const int t0 = blockIdx.z * tn_max;
     if (t0 >= m_total) return;
     const int m = min(tn_max, m_total - t0);        // tokens of this CTA
-    const int tn = (m + 15) & ~15;                   // UMMA N
+    const int tn = (m + 15) & ~15;                   // token columns of the accumulator (per plane)
 
     const uint32_t base = (finch_smem_u32(smem_raw) + 1023u) & ~1023u;
-    const int planes = a.X2 ? 2 : 1, plane_bytes = 2 * tn_max * 128;
-    const int stage_bytes = 2 * A_ATOM + planes * plane_bytes;
+    // The two activation planes sit side by side along N: rows [0, tn) of an atom are plane 0, rows
+    // [tn, 2 tn) plane 1, one MMA covers both and the epilogue adds the two halves of the accumulator.
+    const int planes = a.X2 ? 2 : 1, b_atom = planes * tn_max * 128;
+    const int stage_bytes = 2 * A_ATOM + 2 * b_atom;
     const bool expert = a.mode != DENSE4;
     const uint32_t raw = base + NS * stage_bytes;     // EXPERT_*: ring of packed blocks, filled by bulk copies
     const uint32_t ctl = raw + (expert ? RD * RAW_STAGE : 0);   // barriers, tensor-memory address, row list
     uint8_t *ctl_p = smem_raw + (ctl - finch_smem_u32(smem_raw));
     uint8_t *raw_p = smem_raw + (raw - finch_smem_u32(smem_raw));
-    uint64_t *done = reinterpret_cast<uint64_t *>(ctl_p);   // [NS]
-    uint64_t *full = done + NS;                              // [RD]
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ctl_p + 64);
+    uint64_t *done = reinterpret_cast<uint64_t *>(ctl_p);   // [NS]  MMAs of the stage finished
+    uint64_t *a_full = done + NS;                            // [NS]  all warps wrote their share of the stage
+    uint64_t *raw_full = a_full + NS;                        // [RD]  packed block landed
+    uint64_t *raw_empty = raw_full + RD;                     // [RD]  all warps read the packed block
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ctl_p + 128);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(ctl_p + 132);   // set by whoever gives up on a wait
     int *src_rows = reinterpret_cast<int *>(ctl_p + 256);   // [tn_max] activation row of each token of the tile
+    constexpr int NW = NT / 32;
 
     // zero the activation halves of the stages once: rows >= m are never written and must read as 0
     for (int s = 0; s < NS; s++) {
         const uint32_t bst = base + s * stage_bytes + 2 * A_ATOM;
-        for (int i = tid; i < planes * 2 * tn_max * 8; i += NT) st_shared16(bst + i * 16, 0u, 0u, 0u, 0u);
+        for (int i = tid; i < 2 * b_atom / 16; i += NT) st_shared16(bst + i * 16, 0u, 0u, 0u, 0u);
     }
     for (int j = tid; j < m; j += NT) {
         int row = t0 + j;
@@ -232,11 +250,18 @@ __global__ void __launch_bounds__(NT) dqgemm_tc_kernel(const Args a) {
         src_rows[j] = row;
     }
     if (tid == 0) {
-        for (int s = 0; s < NS; s++) finch_mbar_init(done + s, 1);
-        for (int s = 0; s < RD; s++) finch_mbar_init(full + s, 1);
+        *abort_flag = 0;
+        for (int s = 0; s < NS; s++) {
+            finch_mbar_init(done + s, 1);
+            finch_mbar_init(a_full + s, NW);
+        }
+        for (int s = 0; s < RD; s++) {
+            finch_mbar_init(raw_full + s, 1);
+            finch_mbar_init(raw_empty + s, NW);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    const uint32_t ncols = (uint32_t)tmem_cols(tn_max);
+    const uint32_t ncols = (uint32_t)tmem_cols(planes * tn_max);
     if (warp == 0) {
         tmem_alloc(finch_smem_u32(tmem_slot), ncols);
         tmem_relinquish();
@@ -247,9 +272,7 @@ __global__ void __launch_bounds__(NT) dqgemm_tc_kernel(const Args a) {
     const uint32_t tmem_d = *tmem_slot;
 
     // ---- this thread's weight row ----
-    const int r = tid & (GM - 1), kq = tid >> 7, kh = kq >> 1;   // row of the tile (= tensor-memory lane), 32-value quarter and 64-value half of a K block
-    const uint8_t *wq = nullptr;       // EXPERT_*: first operand word of (unit 0, lane g*4 + 0), row half included
-    const uint8_t *sbq = nullptr;      // EXPERT_*: scale/bias entry of (unit 0, g), row half included
+    const int r = tid & (GM - 1), kh = tid >> 7;   // row of the tile (= tensor-memory lane) and 64-value half of a K block
     const uint32_t *w4 = nullptr;      // DENSE4: packed row
     const uint16_t *s4 = nullptr, *b4 = nullptr;
     uint32_t raw_w = 0, raw_s = 0;     // EXPERT_*: this thread's words / scale inside a ring stage
@@ -262,139 +285,164 @@ __global__ void __launch_bounds__(NT) dqgemm_tc_kernel(const Args a) {
         b4 = a.B + row * (a.K / 64);
     } else {
         const FinchTile T = finch_tile(a.hidden, a.inter);
-        const int dt = blockIdx.x * 8 + (r >> 4), fr = r & 15, g = fr & 7, half = fr >> 3;
-        const uint8_t *blk = a.pool_base + (size_t)a.slot_row[blockIdx.y] * a.slot_bytes;
-        const uint8_t *tile = a.mode == EXPERT_GATEUP ? blk + (size_t)dt * T.tileA : blk + T.b_base + (size_t)dt * T.tileB;
-        wq = tile + (size_t)g * 96 + half * 12;
-        sbq = tile + (a.mode == EXPERT_GATEUP ? T.sbA : T.sbB) + (size_t)g * 16 + half * 4;
-        raw_w = (uint32_t)((r >> 4) * 768 + (g * 4 + kq) * 24 + half * 12);
+        const int fr = r & 15, g = fr & 7, half = fr >> 3;
+        const uint8_t *blk = a.pool_base + (size_t)a.slot_row[expert_id] * a.slot_bytes;
+        raw_w = (uint32_t)((r >> 4) * 768 + (g * 4 + 2 * kh) * 24 + half * 12);   // periods 2 kh and 2 kh + 1 (24 bytes apart)
         raw_s = (uint32_t)(8 * 768 + (r >> 4) * 128 + g * 16 + half * 4 + kh * 2);
         tile0 = a.mode == EXPERT_GATEUP ? blk + (size_t)blockIdx.x * 8 * T.tileA : blk + T.b_base + (size_t)blockIdx.x * 8 * T.tileB;
         tile_stride = a.mode == EXPERT_GATEUP ? T.tileA : T.tileB;
         sb_off = a.mode == EXPERT_GATEUP ? T.sbA : T.sbB;
     }
-    (void)wq;
-    (void)sbq;
 
     const int nkb = a.K / BK;
-    const uint32_t idesc = instr_desc(tn);
+    const uint32_t idesc = instr_desc(planes * tn);
     bool failed = false;
-    uint32_t wreg[4];
+    uint32_t wreg[8];
     uint32_t sreg = 0, breg = 0;   // low 16 bits: scale / bias of this thread's group
-    auto load_block = [&](int kb) {
-        if (a.mode == DENSE4) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(w4 + kb * 16 + kq * 4));
-            wreg[0] = v.x; wreg[1] = v.y; wreg[2] = v.z; wreg[3] = v.w;
-            sreg = __ldg(s4 + 2 * kb + kh);
-            breg = __ldg(b4 + 2 * kb + kh);
-        }
+    auto load_block = [&](int kb) {   // DENSE4: straight from global memory, one block ahead
+        const uint4 *p = reinterpret_cast<const uint4 *>(w4 + kb * 16 + kh * 8);
+        const uint4 v0 = __ldg(p), v1 = __ldg(p + 1);
+        wreg[0] = v0.x; wreg[1] = v0.y; wreg[2] = v0.z; wreg[3] = v0.w;
+        wreg[4] = v1.x; wreg[5] = v1.y; wreg[6] = v1.z; wreg[7] = v1.w;
+        sreg = __ldg(s4 + 2 * kb + kh);
+        breg = __ldg(b4 + 2 * kb + kh);
     };
-    // EXPERT_*: one thread keeps RD - 1 K blocks of packed bytes in flight (16 bulk copies per block)
+    // EXPERT_*: one thread keeps up to RD K blocks of packed bytes in flight (16 bulk copies per block)
     auto issue_raw = [&](int kb) {
         const int slot = kb % RD;
         uint8_t *dst = raw_p + slot * RAW_STAGE;
-        finch_mbar_expect_tx(full + slot, (unsigned)RAW_STAGE);
+        finch_mbar_expect_tx(raw_full + slot, (unsigned)RAW_STAGE);
         for (int d = 0; d < 8; d++) {
             const uint8_t *t = tile0 + (size_t)d * tile_stride;
-            finch_bulk_g2s(dst + d * 768, t + (size_t)kb * 768, 768, full + slot);
-            finch_bulk_g2s(dst + 8 * 768 + d * 128, t + sb_off + (size_t)kb * 128, 128, full + slot);
+            finch_bulk_g2s(dst + d * 768, t + (size_t)kb * 768, 768, raw_full + slot);
+            finch_bulk_g2s(dst + 8 * 768 + d * 128, t + sb_off + (size_t)kb * 128, 128, raw_full + slot);
         }
     };
+    // descriptors of the stages; a K step of 16 values advances the start address by 32 bytes (2 units)
+    auto issue_mma = [&](int kb) {
+        const int st = kb % NS;
+        const uint32_t ast = base + st * stage_bytes, bst = ast + 2 * A_ATOM;
+        const uint64_t ad = smem_desc(ast), bd = smem_desc(bst);
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const uint64_t aoff = (uint64_t)(((k >> 2) * A_ATOM + (k & 3) * 32) >> 4);
+            const uint64_t boff = (uint64_t)(((k >> 2) * b_atom + (k & 3) * 32) >> 4);
+            tc_mma_bf16(tmem_d, ad + aoff, bd + boff, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(done + st);
+    };
     if (expert) {
-        if (tid == 0)
-            for (int kb = 0; kb < RD - 1 && kb < nkb; kb++) issue_raw(kb);
+        if (tid == 32)
+            for (int kb = 0; kb < RD && kb < nkb; kb++) issue_raw(kb);
     } else {
         load_block(0);
     }
 
     for (int kb = 0; kb < nkb; kb++) {
-        const int st = kb % NS, use = kb / NS;
+        const int st = kb % NS, use = kb / NS, slot = kb % RD;
         const uint32_t ast = base + st * stage_bytes, bst = ast + 2 * A_ATOM;
-        // the tensor core must be done with this stage's previous contents
-        bool ok = true;
-        if (use > 0) ok = finch_mbar_wait(done + st, (use - 1) & 1);
-        if (expert && ok) ok = finch_mbar_wait(full + kb % RD, (kb / RD) & 1);
-        if (__syncthreads_or(!ok)) {
+        // the tensor core must be done with this stage's previous contents; the packed block must have landed
+        // (the decision to give up is taken per warp, so that no lane leaves its warp behind)
+        bool ok = !*abort_flag;
+        if (ok && use > 0) ok = finch_mbar_wait(done + st, (use - 1) & 1);
+        if (ok && expert) ok = finch_mbar_wait(raw_full + slot, (kb / RD) & 1);
+        if (!__all_sync(0xffffffffu, ok)) {
+            *abort_flag = 1;
             failed = true;
             break;
         }
-        tc_fence_after();
-        // every thread is past block kb - 1, so its ring slot can take block kb + RD - 1
-        if (expert && tid == 0 && kb + RD - 1 < nkb) issue_raw(kb + RD - 1);
         // ---- activations: m rows of 128 values, copied asynchronously while the weights are dequantised ----
         for (int i = tid; i < m * 16; i += NT) {
             const int j = i >> 4, c = i & 15;
             const size_t src = (size_t)src_rows[j] * a.K + (size_t)kb * BK + c * 8;
-            const uint32_t dst = bst + (c >> 3) * (tn_max * 128) + swz(j, c & 7);
+            const uint32_t dst = bst + (c >> 3) * b_atom + swz(j, c & 7);
             cp_async16(dst, a.X + src);
-            if (a.X2) cp_async16(dst + plane_bytes, a.X2 + src);
+            if (a.X2) cp_async16(bst + (c >> 3) * b_atom + swz(tn + j, c & 7), a.X2 + src);
         }
-        // ---- weights: 32 values of row r ----
+        // ---- weights: 64 values (one scale group) of row r ----
+        uint32_t cur[8];
         if (expert) {
-            const uint32_t rs = raw + (kb % RD) * RAW_STAGE;
+            const uint32_t rs = raw + slot * RAW_STAGE;
+            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(cur[0]) : "r"(rs + raw_w));
+            asm volatile("ld.shared.u32 %0, [%1+4];" : "=r"(cur[1]) : "r"(rs + raw_w));
+            asm volatile("ld.shared.u32 %0, [%1+8];" : "=r"(cur[2]) : "r"(rs + raw_w));
+            asm volatile("ld.shared.u32 %0, [%1+24];" : "=r"(cur[3]) : "r"(rs + raw_w));
+            asm volatile("ld.shared.u32 %0, [%1+28];" : "=r"(cur[4]) : "r"(rs + raw_w));
+            asm volatile("ld.shared.u32 %0, [%1+32];" : "=r"(cur[5]) : "r"(rs + raw_w));
             asm volatile("ld.shared.u16 %0, [%1];" : "=r"(sreg) : "r"(rs + raw_s));
             asm volatile("ld.shared.u16 %0, [%1+8];" : "=r"(breg) : "r"(rs + raw_s));
+            cur[6] = cur[7] = 0;
+            __syncwarp();
+            if (lane == 0) {   // this warp is done with the ring slot
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(finch_smem_u32(raw_empty + slot)) : "memory");
+            }
+            // the producer refills the slot of block kb - 1 once every warp has read it
+            if (tid == 32 && kb >= 1 && kb + RD - 1 < nkb) {
+                if (finch_mbar_wait(raw_empty + (kb - 1) % RD, ((kb - 1) / RD) & 1)) issue_raw(kb + RD - 1);
+                else *abort_flag = 1;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) cur[i] = wreg[i];
         }
         float s0, b0, unused;
         finch_widen16x2(sreg, a.scale_dtype, s0, unused);
         finch_widen16x2(breg, a.scale_dtype, b0, unused);
         const GroupScale gs = group_scale(s0, b0);
-        uint32_t cur[4];
-        if (expert) {
-            const uint32_t rs = raw + (kb % RD) * RAW_STAGE;
-            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(cur[0]) : "r"(rs + raw_w));
-            asm volatile("ld.shared.u32 %0, [%1+4];" : "=r"(cur[1]) : "r"(rs + raw_w));
-            asm volatile("ld.shared.u32 %0, [%1+8];" : "=r"(cur[2]) : "r"(rs + raw_w));
-            cur[3] = 0;
-        } else {
-#pragma unroll
-            for (int i = 0; i < 4; i++) cur[i] = wreg[i];
-            if (kb + 1 < nkb) load_block(kb + 1);   // in flight while this block is dequantised
-        }
-        const uint32_t arow = ast + kh * A_ATOM;
-        const int cbase = (kq & 1) * 4;         // first 16-byte chunk of this quarter inside its atom
+        if (!expert && kb + 1 < nkb) load_block(kb + 1);   // in flight while this block is dequantised
+        // row r of atom kh: chunk c sits at (c ^ (r & 7)) * 16 inside the row
+        const uint32_t arow = ast + kh * A_ATOM + (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+        const uint32_t rx = (uint32_t)(r & 7);
         if (a.mode == DENSE4) {
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
+            for (int c = 0; c < 8; c++) {
                 uint32_t o[4];
                 dq4_word(cur[c], gs, o);
-                st_shared16(arow + swz(r, cbase + c), o[0], o[1], o[2], o[3]);
+                st_shared16(arow + ((c ^ rx) << 4), o[0], o[1], o[2], o[3]);
             }
         } else {
-            uint32_t o[16];
-            dq3_piece(cur[0], cur[1], cur[2], gs, o);
 #pragma unroll
-            for (int c = 0; c < 4; c++) st_shared16(arow + swz(r, cbase + c), o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+            for (int t = 0; t < 2; t++) {
+                uint32_t o[16];
+                dq3_piece(cur[3 * t], cur[3 * t + 1], cur[3 * t + 2], gs, o);
+#pragma unroll
+                for (int c = 0; c < 4; c++) st_shared16(arow + (((t * 4 + c) ^ rx) << 4), o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+            }
         }
         cp_async_wait_all();
         proxy_fence();          // generic-proxy writes -> visible to the tensor core (async proxy)
-        tc_fence_before();
-        __syncthreads();
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(finch_smem_u32(a_full + st)) : "memory");
+        // one thread issues the block's MMAs as soon as every warp has written its share; the other
+        // warps are by then dequantising the next block into the other stage
         if (tid == 0) {
-            tc_fence_after();
-#pragma unroll
-            for (int k = 0; k < 8; k++) {
-                const uint32_t aoff = (k >> 2) * A_ATOM + (k & 3) * 32, boff = (k >> 2) * (tn_max * 128) + (k & 3) * 32;
-                tc_mma_bf16(tmem_d, smem_desc(ast + aoff), smem_desc(bst + boff), idesc, (kb > 0 || k > 0) ? 1u : 0u);
-                if (planes == 2) tc_mma_bf16(tmem_d, smem_desc(ast + aoff), smem_desc(bst + plane_bytes + boff), idesc, 1u);
-            }
-            tc_commit(done + st);
+            if (finch_mbar_wait(a_full + st, use & 1)) issue_mma(kb);
+            else *abort_flag = 1;
         }
     }
 
     // ---- epilogue ----
-    if (!failed) {
+    {
         const int last = nkb - 1;
-        const bool ok = finch_mbar_wait(done + last % NS, (last / NS) & 1);
+        __syncthreads();   // thread 0 has issued the last commit (or given up) before it gets here
+        bool ok = !failed && !*abort_flag;
+        if (ok) ok = finch_mbar_wait(done + last % NS, (last / NS) & 1);
         if (__syncthreads_or(!ok)) failed = true;
     }
     if (!failed) {
         tc_fence_after();
-        // warps w, w + 4, w + 8, w + 12 read the same 32 lanes and take every fourth 16-column chunk
+        // warps w and w + 4 read the same 32 lanes and take alternate 16-column chunks
         const uint32_t trow = tmem_d + ((uint32_t)((warp & 3) * 32) << 16);
-        for (int c0 = (warp >> 2) * 16; c0 < tn; c0 += 64) {
+        for (int c0 = (warp >> 2) * 16; c0 < tn; c0 += 32) {
             float v[16];
             tmem_ld16(trow + (uint32_t)c0, v);
+            if (planes == 2) {
+                float v2[16];
+                tmem_ld16(trow + (uint32_t)(tn + c0), v2);
+#pragma unroll
+                for (int j = 0; j < 16; j++) v[j] += v2[j];
+            }
             if (a.mode == EXPERT_GATEUP) {
                 // lanes l and l ^ 8 hold the gate and the up row of the same index
 #pragma unroll

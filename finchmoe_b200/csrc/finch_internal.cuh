@@ -128,17 +128,20 @@ __device__ __forceinline__ void finch_mbar_expect_tx(uint64_t *bar, unsigned byt
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(finch_smem_u32(bar)), "r"(bytes)
                  : "memory");
 }
-// Bounded wait: returns false when the phase did not complete within the limit.
+// Bounded wait: returns false when the phase did not complete within the limit.  try_wait is given a
+// suspend-time hint, so a waiting thread sleeps in hardware (and is woken when the phase completes)
+// instead of spending the SM's issue slots on polling; the hint also bounds one attempt, so the
+// attempt count bounds the total wait (about a fifth of a second; legitimate waits are microseconds).
 __device__ __forceinline__ bool finch_mbar_wait(uint64_t *bar, unsigned parity) {
     const uint32_t a = finch_smem_u32(bar);
-    for (unsigned it = 0; it < (1u << 17); ++it) {  // legitimate waits are microseconds; this bound is a fraction of a second
+    for (unsigned it = 0; it < (1u << 13); ++it) {
         unsigned done;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
             "selp.u32 %0, 1, 0, p;\n\t}"
             : "=r"(done)
-            : "r"(a), "r"(parity)
+            : "r"(a), "r"(parity), "r"(20000u)
             : "memory");
         if (done) return true;
     }

@@ -27,10 +27,13 @@ constexpr int TC_MIN_TOKENS = 128;   // shorter chunks are faster through the de
 
 // One CTA: pairs -> expert histogram -> ranges -> order.  Pairs that are masked, out of range or not
 // resident are left out (their rows are never produced and never combined).
+// It also lists the (expert, first token) tiles of the two grouped GEMMs, tn_a / tn_b tokens per tile, so
+// that their grids hold no CTA without work: items_a / items_b = [expert, first pair of the tile inside
+// the expert's range], n_items[0 / 1] = how many.
 __global__ void __launch_bounds__(1024) pf_sort_kernel(const int32_t *ids, const uint8_t *valid, const int32_t *slot_row, int n_experts, int P,
-                                                       int *seg, int *order) {
-    extern __shared__ int sm[];   // [n_experts] counts, then [n_experts] cursors
-    int *cnt = sm, *cur = sm + n_experts;
+                                                       int *seg, int *order, int tn_a, int tn_b, int2 *items_a, int2 *items_b, int *n_items) {
+    extern __shared__ int sm[];   // [n_experts] counts, cursors, first item of the expert in each list
+    int *cnt = sm, *cur = sm + n_experts, *ia = cur + n_experts, *ib = ia + n_experts;
     const int tid = threadIdx.x;
     for (int e = tid; e < n_experts; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
@@ -41,15 +44,25 @@ __global__ void __launch_bounds__(1024) pf_sort_kernel(const int32_t *ids, const
     }
     __syncthreads();
     if (tid == 0) {
-        int run = 0;
+        int run = 0, na = 0, nb = 0;
         for (int e = 0; e < n_experts; e++) {
             seg[e] = run;
             cur[e] = run;
             run += cnt[e];
+            ia[e] = na;
+            ib[e] = nb;
+            na += (cnt[e] + tn_a - 1) / tn_a;
+            nb += (cnt[e] + tn_b - 1) / tn_b;
         }
         seg[n_experts] = run;
+        n_items[0] = na;
+        n_items[1] = nb;
     }
     __syncthreads();
+    for (int e = tid; e < n_experts; e += blockDim.x) {
+        for (int i = 0, t0 = 0; t0 < cnt[e]; i++, t0 += tn_a) items_a[ia[e] + i] = make_int2(e, t0);
+        for (int i = 0, t0 = 0; t0 < cnt[e]; i++, t0 += tn_b) items_b[ib[e] + i] = make_int2(e, t0);
+    }
     // the order of the pairs inside an expert's range is arbitrary: every pair's output row is computed
     // from its own activation row only, so the results do not depend on it
     for (int p = tid; p < P; p += blockDim.x) {
@@ -137,7 +150,7 @@ int dense4_gemm(finch_ctx *ctx, cudaStream_t st, const finch_wdesc *w, const uin
     a.K = w->in_dim;
     // token tile: small enough that the grid covers the SMs, large enough not to dequantise a tile too often
     a.tn_max = tn_max_for((int)((long long)T * (w->out_dim / dqgemm::GM) / 148));
-    if (xb_lo && a.tn_max > 128) a.tn_max = 128;   // two activation planes per stage
+    if (xb_lo && a.tn_max > 128) a.tn_max = 128;   // two activation planes side by side: 2 x tokens accumulator columns
     a.X2 = xb_lo;
     a.scale_dtype = w->scale_dtype;
     a.W = (const uint32_t *)w->W;
@@ -184,17 +197,22 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
         return r;
     };
     const size_t o_seg = take((c.n_experts + 1) * sizeof(int)), o_order = take((size_t)P * sizeof(int));
+    const int max_items = P / 16 + c.n_experts + 1;   // tiles of at least 16 tokens, plus one ragged tile per expert
+    const size_t o_ia = take((size_t)max_items * sizeof(int2)), o_ib = take((size_t)max_items * sizeof(int2)), o_ni = take(2 * sizeof(int));
     const size_t o_xb = take((size_t)T * H * 2), o_sg = take((size_t)T * Is * 4), o_su = take((size_t)T * Is * 4), o_sact = take((size_t)T * Is * 4);
     int rc = ensure_ws(ctx, off, st);
     if (rc) return rc;
     char *ws = (char *)ctx->pf_ws;
-    int *seg = (int *)(ws + o_seg), *order = (int *)(ws + o_order);
+    int *seg = (int *)(ws + o_seg), *order = (int *)(ws + o_order), *n_items = (int *)(ws + o_ni);
+    int2 *items_a = (int2 *)(ws + o_ia), *items_b = (int2 *)(ws + o_ib);
     uint16_t *xb = (uint16_t *)(ws + o_xb), *sact = (uint16_t *)(ws + o_sact), *sact_lo = sact + (size_t)T * Is;
     float *sg = (float *)(ws + o_sg), *su = (float *)(ws + o_su);
     uint16_t *act = (uint16_t *)ctx->act, *act_lo = act + (size_t)P * I;   // two bf16 planes [P][I] inside the fp32-sized buffer
     float *down = ctx->partial, *shared_out = ctx->partial + (size_t)P * H;
 
-    pf_sort_kernel<<<1, 1024, 2 * c.n_experts * sizeof(int), st>>>(ids, valid, slot_row, c.n_experts, P, seg, order);
+    const int tn_a = tn_max_for(T < 32 ? T : 32), tn_b = 16;   // small token tiles keep two CTAs on an SM; popular experts take several
+    pf_sort_kernel<<<1, 1024, 4 * c.n_experts * sizeof(int), st>>>(ids, valid, slot_row, c.n_experts, P, seg, order, tn_a, tn_b, items_a, items_b,
+                                                                   n_items);
     FINCH_CUDA_OK(ctx, cudaGetLastError());
     const uint16_t *x = (const uint16_t *)h_post;
     if (c.act_dtype != FINCH_BF16) {
@@ -207,7 +225,7 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
 
     dqgemm::Args a{};
     a.K = H;
-    a.tn_max = tn_max_for(T < 32 ? T : 32);   // small token tiles keep two CTAs on an SM; popular experts take several
+    a.tn_max = tn_a;
     a.scale_dtype = c.scale_dtype;
     a.pool_base = (const uint8_t *)pool->base;
     a.slot_bytes = pool->slot_bytes;
@@ -218,19 +236,23 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
     a.order = order;
     a.top_k = c.top_k;
     a.status = ctx->dev_status;
-    const int ztiles = (T + a.tn_max - 1) / a.tn_max;
     a.mode = dqgemm::EXPERT_GATEUP;
     a.X = x;
     a.act_out = act;
     a.act_out_lo = act_lo;
-    if ((rc = launch_gemm(ctx, st, a, dim3(I / 64, c.n_experts, ztiles)))) return rc;   // 64 gate + 64 up rows per tile
+    a.items = items_a;
+    a.n_items = n_items;
+    // grid.y bounds the number of (expert, token tile) items; CTAs past the actual count return at once
+    if ((rc = launch_gemm(ctx, st, a, dim3(I / 64, P / tn_a + c.n_experts, 1)))) return rc;   // 64 gate + 64 up rows per tile
     a.mode = dqgemm::EXPERT_DOWN;
     a.K = I;
     a.X = act;
     a.X2 = act_lo;
     a.out = down;
-    if (a.tn_max > 16) a.tn_max = 16;   // two activation planes per stage
-    if ((rc = launch_gemm(ctx, st, a, dim3(H / dqgemm::GM, c.n_experts, (T + a.tn_max - 1) / a.tn_max)))) return rc;
+    a.tn_max = tn_b;   // two activation planes per stage
+    a.items = items_b;
+    a.n_items = n_items + 1;
+    if ((rc = launch_gemm(ctx, st, a, dim3(H / dqgemm::GM, P / tn_b + c.n_experts, 1)))) return rc;
 
     if (shared) {
         if ((rc = dense4_gemm(ctx, st, &shared->gate, x, nullptr, sg, T))) return rc;
