@@ -413,6 +413,7 @@ def run_ours(args):
                            "ms_per_chunk": ps * 1e3, "tflops": flops / ps / 1e12, "hbm_gbs": pbytes / ps / 1e9,
                            "roofline": {"bound": "hbm", "note": "8T/256 pairs per expert: below the tensor ridge", "ceiling_tflops": ceil_tf,
                                         "frac": flops / ps / 1e12 / ceil_tf, "peak_kind": peak_kind}}
+        line["other_rows"] = aux_rooflines(stack, peaks, peak_kind)
         # CPU baseline: bounded sample of the same workload on the expert blocks of this pool
         cores = os.cpu_count() or 1
         sample_layers = 2
@@ -521,6 +522,67 @@ def run_ep(args, rank, local_rank, world):
     dist.destroy_process_group()
 
 
+def aux_rooflines(stack, peaks, peak_kind, iters=8):
+    """The other matvec rows of the path, each timed alone with CUDA events and the L2 flushed (a 256 MB
+    write) before every timed launch: 4-bit g64 projections and GGUF Q4_K / Q6_K tensors through
+    finch_encode_batch_matvec at 1 / 8 (/ 90) positions, and the 4-bit projections at 64 / 512 positions
+    through the tensor-core GEMM.  bytes = packed weights + scales (+ activations); flops = 2 T out in."""
+    import ctypes as C
+
+    import torch
+    ctx, L = stack.ctx, stack.L
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    rng = synth.rng_for(4, 0, 99)
+    st = stack.stream
+    rows = []
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(iters):
+            with torch.cuda.stream(st):
+                flush.fill_(1)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                fn()
+                e1.record(st)
+            torch.cuda.synchronize()
+            tot += e0.elapsed_time(e1)
+        return tot / iters * 1e-3
+
+    def wbytes(t):
+        return int(t["W"].nbytes + (t["S"].nbytes if t.get("S") is not None else 0) + (t["B"].nbytes if t.get("B") is not None else 0))
+
+    cases = [("4bit_g64", synth.affine_tensor(rng, 8192, 2048, 4, SCALE_FP16), (1, 8)),
+             ("4bit_g64", synth.affine_tensor(rng, 2048, 4096, 4, SCALE_FP16), (1, 8)),
+             ("q4_k", synth.gguf_tensor(rng, 8192, 2048, 12), (1, 8, 90)),
+             ("q6_k", synth.gguf_tensor(rng, 8192, 2048, 14), (1, 8, 90)),
+             ("q4_k", synth.gguf_tensor(rng, 2048, 512, 12), (1, 8)),
+             ("q6_k", synth.gguf_tensor(rng, 512, 2048, 14), (1, 8))]
+    for name, t, Ts in cases:
+        w = ctx.upload_tensor(t)
+        for T in Ts:
+            x = torch.from_numpy(synth.activations(rng, T, t["in_dim"])).cuda().to(torch.bfloat16)
+            out = torch.empty((T, t["out_dim"]), dtype=torch.float32, device="cuda")
+            secs = timed(lambda: ctx.fast_batch_matvec(x, L.BF16, [w], [out], M=T, stream=st.cuda_stream))
+            b = wbytes(t) + T * t["in_dim"] * 2 + T * t["out_dim"] * 4
+            rows.append({"op": f"matvec_{name}", "shape": [t["out_dim"], t["in_dim"]], "T": T, "us": secs * 1e6, "gbs": b / secs / 1e9,
+                         "frac_hbm_" + peak_kind: b / secs / 1e9 / peaks["hbm_gbs"]})
+    for shape in ((8192, 2048), (2048, 4096)):
+        t = synth.affine_tensor(rng, shape[0], shape[1], 4, SCALE_FP16)
+        w = ctx.upload_tensor(t)
+        for T in (64, 512):
+            x = torch.from_numpy(synth.activations(rng, T, shape[1])).cuda().to(torch.bfloat16)
+            out = torch.empty((T, shape[0]), dtype=torch.float32, device="cuda")
+            secs = timed(lambda: ctx.check(ctx.lib.finch_encode_dense_gemm(ctx.h, st.cuda_stream, C.byref(w), x.data_ptr(), out.data_ptr(), T)))
+            fl, b = 2.0 * T * shape[0] * shape[1], wbytes(t) + T * shape[1] * 2 + T * shape[0] * 4
+            ceil = min(peaks["bf16_tflops"], fl / b * peaks["hbm_gbs"] / 1e3)
+            rows.append({"op": "dense_gemm_4bit_g64_tcgen05", "shape": list(shape), "T": T, "us": secs * 1e6, "tflops": fl / secs / 1e12,
+                         "gbs": b / secs / 1e9, "ceiling_tflops": ceil, "frac_" + peak_kind: fl / secs / 1e12 / ceil})
+    return rows
+
+
 def kernel_roofline(stack, dev, rsets, xd, score, out, batch, args, peaks, peak_kind):
     """Average duration of the gate/up/SiLU kernel over the same steps, from CUDA
     events recorded around every launch on the launching stream (a separate pass
@@ -547,7 +609,10 @@ def kernel_roofline(stack, dev, rsets, xd, score, out, batch, args, peaks, peak_
     per_launch_bytes = gate_bytes / n.value
     achieved = per_launch_bytes / (ms_a.value / n.value * 1e-3) / 1e9
     return {"bound": "hbm", "kernel": "moe_gateup_kernel", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": achieved / peaks["hbm_gbs"], "peak_kind": peak_kind, "traffic": None,
+            "frac": achieved / peaks["hbm_gbs"], "peak_kind": peak_kind,
+            # dram__bytes_read + write of one launch with 38 distinct experts (36,044,800 algorithmic bytes):
+            # 38,070,528 B (profiles/moe_decode_batch8_gateup_down_full.md), scaled to this run's average launch
+            "traffic": per_launch_bytes * (38070528 / 36044800), "traffic_source": "ncu, 38-expert launch, scaled by bytes",
             "bytes_per_launch": per_launch_bytes, "us_per_launch": ms_a.value / n.value * 1e3,
             "down_combine_us_per_launch": ms_b.value / n.value * 1e3, "launches_timed": n.value}
 
@@ -561,9 +626,15 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS, help="fewer layers = a small case for profiler captures")
     ap.add_argument("--no-graph", action="store_true", help="launch from the host every step instead of replaying CUDA graphs")
+    ap.add_argument("--only", default="", choices=["", "prefill"], help="prefill: just the 512-token chunk on --layers layers (profiler captures)")
     args = ap.parse_args()
     LAYERS = args.layers
-    if args.impl == "reference":
+    if args.only == "prefill":
+        stack = Stack(0, max_tokens=512, layers=LAYERS)
+        ps, uniq = stack.time_prefill(512, max(1, args.steps), max(1, args.warmup))
+        print(json.dumps({"only": "prefill", "chunk": 512, "layers": LAYERS, "ms_per_chunk": ps * 1e3, "tokens_per_s": 512 / ps,
+                          "distinct_experts": uniq, "status": stack.ctx.device_status()}))
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
