@@ -8,6 +8,8 @@
 // (moe_decode.cu).
 #include "finch_internal.cuh"
 
+int finch_try_fast_matvec(finch_ctx *ctx, cudaStream_t st, const void *x, int x_dtype, const finch_wdesc *specs, float *const *outs, int n, int M);
+
 namespace {
 
 // ---- decoders: eight weights starting at element i0 (multiple of 8) of one row ----
@@ -349,6 +351,10 @@ extern "C" int finch_encode_batch_matvec(finch_ctx *ctx, finch_stream stream, co
         max_out = max_out > specs[i].out_dim ? max_out : specs[i].out_dim;
     }
     cudaSetDevice(ctx->cfg.device);
+    {   // 1..8 positions of a 3-bit / 4-bit / Q4_K tensor: the streaming kernel (matvec_fast.cu)
+        const int rc = finch_try_fast_matvec(ctx, finch_pick_stream(ctx, stream), x, x_dtype, specs, outs, n, M);
+        if (rc >= 0) return rc;
+    }
     dim3 grid((max_out + 3) / 4, n);
     batch_matvec_kernel<<<grid, 128, 0, finch_pick_stream(ctx, stream)>>>(pack, x, x_dtype, M);
     ctx->launches++;

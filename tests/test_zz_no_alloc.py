@@ -37,9 +37,9 @@ def test_matvec_noalloc_matches_regular_entry_point_twice():
                 got = np.full((M, t["out_dim"]), np.nan, np.float32)
                 rc = so.finch_matvec_noalloc(C.byref(w), x.ctypes.data, got.ctypes.data, M, None)
                 assert rc == L.OK, rc
-                # same kernel, same inputs: the two entry points must agree bit for bit
-                assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"rep {rep} bits={t['bits']}"
-                assert_close(got, want, "noalloc vs regular")
+                # the regular entry point may pick a different kernel for the same tensor (streaming kernel for
+                # few positions), so the two agree to the path's tolerance, not bit for bit
+                assert_close(got, want, f"noalloc vs regular, rep {rep} bits={t['bits']}")
         # a call that does not fit the fixed buffer is refused, not truncated
         big = synth.affine_tensor(rng, 64, 4096, 4, L.BF16)
         wb = ctx.upload_tensor(big)
