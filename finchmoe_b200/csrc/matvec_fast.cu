@@ -198,6 +198,29 @@ __global__ void __launch_bounds__(FNT, 1) fast_matvec_kernel(FPack pack, const v
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int Kp = (K + 1023) & ~1023, nchunk = K / 32;
     float *xs = fsm, *sx = fsm + (size_t)M * Kp, *sx16 = sx + (size_t)M * (Kp / 32);   // sums per 32 and per 16 values
+    // ---- rows: two per warp and step; the packed words are loaded PD steps ahead, the first ones before the staging ----
+    const int ncb = Kp / 1024, warps = FNT / 32;
+    const int first_pair = blockIdx.x * warps + warp, pair_step = gridDim.x * warps;
+    const int npairs = (sp.out_dim + 1) / 2;
+    const int my_pairs = first_pair < npairs ? (npairs - first_pair + pair_step - 1) / pair_step : 0;
+    const int nit = my_pairs * ncb;
+    auto row_of = [&](int it) { return (first_pair + (it / ncb) * pair_step) * 2; };
+    auto chunk_of = [&](int it) { return (it % ncb) * 32 + lane; };
+    constexpr int PD = Depth<BITS>::value;
+    Raw<BITS> n0[PD], n1[PD];
+    auto fetch = [&](int it, Raw<BITS> &a, Raw<BITS> &b) {
+        if (it < nit && chunk_of(it) < nchunk) {
+            const int rn = row_of(it);
+            a = load_raw<BITS>(sp, (size_t)rn, K, chunk_of(it));
+            if (rn + 1 < sp.out_dim) b = load_raw<BITS>(sp, (size_t)rn + 1, K, chunk_of(it));
+        }
+    };
+#pragma unroll
+    for (int d = 0; d < PD; d++) {
+        n0[d] = Raw<BITS>{};
+        n1[d] = Raw<BITS>{};
+        fetch(d, n0[d], n1[d]);
+    }
     // ---- stage the activations: a thread takes eight consecutive values (16-byte loads), four threads a chunk ----
     const int oct_per_row = Kp / 8;
 #pragma unroll 4
@@ -236,29 +259,6 @@ __global__ void __launch_bounds__(FNT, 1) fast_matvec_kernel(FPack pack, const v
     }
     __syncthreads();
     const float4 *xs4 = reinterpret_cast<const float4 *>(xs);
-    // ---- rows: two per warp and step; the packed words of the next step are loaded before this one is computed ----
-    const int ncb = Kp / 1024, warps = FNT / 32;
-    const int first_pair = blockIdx.x * warps + warp, pair_step = gridDim.x * warps;
-    const int npairs = (sp.out_dim + 1) / 2;
-    const int my_pairs = first_pair < npairs ? (npairs - first_pair + pair_step - 1) / pair_step : 0;
-    const int nit = my_pairs * ncb;
-    auto row_of = [&](int it) { return (first_pair + (it / ncb) * pair_step) * 2; };
-    auto chunk_of = [&](int it) { return (it % ncb) * 32 + lane; };
-    constexpr int PD = Depth<BITS>::value;
-    Raw<BITS> n0[PD], n1[PD];
-    auto fetch = [&](int it, Raw<BITS> &a, Raw<BITS> &b) {
-        if (it < nit && chunk_of(it) < nchunk) {
-            const int rn = row_of(it);
-            a = load_raw<BITS>(sp, (size_t)rn, K, chunk_of(it));
-            if (rn + 1 < sp.out_dim) b = load_raw<BITS>(sp, (size_t)rn + 1, K, chunk_of(it));
-        }
-    };
-#pragma unroll
-    for (int d = 0; d < PD; d++) {
-        n0[d] = Raw<BITS>{};
-        n1[d] = Raw<BITS>{};
-        fetch(d, n0[d], n1[d]);
-    }
     float acc[2][MT];
     for (int it0 = 0; it0 < nit; it0 += PD) {
 #pragma unroll

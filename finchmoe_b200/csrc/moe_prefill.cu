@@ -43,20 +43,47 @@ __global__ void __launch_bounds__(1024) pf_sort_kernel(const int32_t *ids, const
         atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
-    if (tid == 0) {
-        int run = 0, na = 0, nb = 0;
-        for (int e = 0; e < n_experts; e++) {
-            seg[e] = run;
-            cur[e] = run;
-            run += cnt[e];
-            ia[e] = na;
-            ib[e] = nb;
-            na += (cnt[e] + tn_a - 1) / tn_a;
-            nb += (cnt[e] + tn_b - 1) / tn_b;
+    // exclusive scans over the experts (one thread each, n_experts <= 1024): pairs, tiles of each GEMM
+    {
+        __shared__ int wsum[3][32];
+        const int lane = tid & 31, wid = tid >> 5;
+        const int c0 = tid < n_experts ? cnt[tid] : 0;
+        int v[3] = {c0, (c0 + tn_a - 1) / tn_a, (c0 + tn_b - 1) / tn_b}, inc[3];
+#pragma unroll
+        for (int q = 0; q < 3; q++) {
+            inc[q] = v[q];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, inc[q], o);
+                if (lane >= o) inc[q] += t;
+            }
+            if (lane == 31) wsum[q][wid] = inc[q];
         }
-        seg[n_experts] = run;
-        n_items[0] = na;
-        n_items[1] = nb;
+        __syncthreads();
+        if (wid == 0) {
+#pragma unroll
+            for (int q = 0; q < 3; q++) {
+                const int w = wsum[q][lane];
+                int acc = w;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int t = __shfl_up_sync(0xffffffffu, acc, o);
+                    if (lane >= o) acc += t;
+                }
+                wsum[q][lane] = acc - w;   // exclusive prefix of the warp totals
+                if (lane == 31) {
+                    if (q == 0) seg[n_experts] = acc;
+                    else n_items[q - 1] = acc;
+                }
+            }
+        }
+        __syncthreads();
+        if (tid < n_experts) {
+            const int e = tid;
+            seg[e] = cur[e] = wsum[0][wid] + inc[0] - v[0];
+            ia[e] = wsum[1][wid] + inc[1] - v[1];
+            ib[e] = wsum[2][wid] + inc[2] - v[2];
+        }
     }
     __syncthreads();
     for (int e = tid; e < n_experts; e += blockDim.x) {
@@ -286,7 +313,7 @@ extern "C" int finch_encode_moe_prefill(finch_ctx *ctx, finch_stream stream, fin
     const size_t elt = c.act_dtype == FINCH_BF16 ? 2 : 4;
     bool tc = ctx->prefill_mode == 2 || (ctx->prefill_mode == 0 && T >= TC_MIN_TOKENS);
     // shapes the tensor-core kernels take: whole 128-row tiles, 128-value K blocks, a 3-bit pool
-    if (c.expert_bits != 3 || c.hidden % 128 || c.moe_inter % 128 || c.top_k > 8) tc = false;
+    if (c.expert_bits != 3 || c.hidden % 128 || c.moe_inter % 128 || c.top_k > 8 || c.n_experts > 1024) tc = false;
     if (tc && shared) {
         if (shared->gate.bits != 4 || shared->gate.out_dim % 128 || shared->gate.in_dim != c.hidden || !shared->gate_score) tc = false;
     }

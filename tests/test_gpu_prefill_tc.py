@@ -153,3 +153,36 @@ def test_prefill_tensor_core_full_size_vs_oracle(api):
     finally:
         pool.destroy()
         ctx.destroy()
+
+
+def test_prefill_512_tokens_full_size_sampled_oracle_and_exact_path(api):
+    """BASELINE's largest chunk (512 tokens, hidden 2048, 256 experts, Zipf top-8) through the tensor-core path: every
+    row finite, 24 sampled rows against the oracle, and all rows close to the exact sub-batch path (bf16 rounding only)."""
+    T = 512
+    ctx = api.Context(max_tokens=T, n_layers=1, scale_dtype=L.FP16, act_dtype=L.BF16)
+    pool = ctx.pool(n_layers=1)
+    try:
+        pool.fill_synthetic(0, 1, 77)
+        rng = synth.rng_for(8, T)
+        ids, w = synth.zipf_routing(rng, T, 256, 8)
+        x = synth.activations(rng, T, 2048)
+        sh = synth.shared_expert(rng, scale_dtype=L.FP16)
+        shd = ctx.make_shared(*[ctx.upload_tensor(t) for t in sh])
+        score = rng.normal(0, 1, size=T).astype(np.float32)
+        h_mid = synth.activations(rng, T, 2048)
+        ctx.set_prefill_mode(2)
+        out = ctx.moe_forward_host(pool, 0, x, ids, w, shared=shd, gate_score=score, h_mid=h_mid)
+        assert np.all(np.isfinite(out))
+        sample = rng.choice(T, size=24, replace=False)
+        blocks = {int(e): pool.get(0, int(e)) for e in set(ids[sample].ravel().tolist())}
+        want = _oracle_prefill(blocks, ids[sample], w[sample], None, x[sample], dict(hidden=2048, inter=512, sd=L.FP16), shared=sh,
+                               score=score[sample], h_mid=h_mid[sample])
+        assert_close(out[sample], want, "512-token chunk, sampled rows", tight_rel=None)
+        ctx.set_prefill_mode(1)
+        exact = ctx.moe_forward_host(pool, 0, x, ids, w, shared=shd, gate_score=score, h_mid=h_mid)
+        rel = np.abs(out - exact).max() / np.sqrt((exact.astype(np.float64) ** 2).mean())
+        assert rel < 3e-2, rel
+        assert ctx.device_status() == 0
+    finally:
+        pool.destroy()
+        ctx.destroy()
