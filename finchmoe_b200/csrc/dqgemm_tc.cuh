@@ -22,7 +22,8 @@ namespace dqgemm {
 constexpr int GM = 128;       // weight rows per CTA = UMMA M
 constexpr int BK = 128;       // K values per stage = two 64-value swizzle atoms
 constexpr int NS = 2;         // stages
-constexpr int NT = 256;       // threads per CTA: two per weight row, one for each 64-value half (= scale group) of a K block
+constexpr int NT = 256;       // dequantising threads per CTA: two per weight row, one for each 64-value half (= scale group) of a K block
+constexpr int NTB = NT + 32;  // + one control warp: its lane 0 issues the MMAs and the bulk copies of the packed blocks
 constexpr int A_ATOM = GM * 128;   // bytes of one 64-value atom of the weight tile
 constexpr int RD = 4;         // depth of the ring of packed expert blocks (EXPERT_* modes)
 constexpr int RAW_STAGE = 8 * 768 + 8 * 128;   // one K block of eight 16-row pool tiles: operand words, then scale/bias entries
@@ -186,14 +187,14 @@ __device__ __forceinline__ void dq4_word(uint32_t w, const GroupScale &gs, uint3
     for (int i = 0; i < 4; i++) o[i] = bf16x2_rn(v[2 * i], v[2 * i + 1]);
 }
 
-// grid: x = 128-row weight tile; EXPERT_*: y = (expert, token tile) item; DENSE4: z = token tile.  block: 256 threads.
+// grid: x = 128-row weight tile; EXPERT_*: y = (expert, token tile) item; DENSE4: z = token tile.  block: 288 threads.
 //
-// No CTA-wide barrier inside the K loop.  Every warp dequantises its share of block kb into stage
-// kb % NS and arrives on a_full[stage]; lane 0 of warp 0 then issues the block's MMAs and commits them
-// to done[stage], which frees the stage, while the other warps already work on block kb + 1;
-// lane 0 of warp 1 keeps the ring of packed blocks filled, waiting on raw_empty[slot] (all warps
-// have read the slot) before a refill.
-__global__ void __launch_bounds__(NT) dqgemm_tc_kernel(const Args a) {
+// No CTA-wide barrier inside the K loop.  Each of the eight dequantising warps writes its share of block
+// kb into stage kb % NS and arrives on a_full[stage]; lane 0 of the ninth (control) warp then issues the
+// block's MMAs and commits them to done[stage], which frees the stage, while the other warps already
+// work on block kb + 1; the same thread keeps the ring of packed blocks filled, refilling a slot once
+// raw_empty[slot] says that every dequantising warp has read it.
+__global__ void __launch_bounds__(NTB) dqgemm_tc_kernel(const Args a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tn_max = a.tn_max;
@@ -234,14 +235,15 @@ __global__ void __launch_bounds__(NT) dqgemm_tc_kernel(const Args a) {
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ctl_p + 128);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(ctl_p + 132);   // set by whoever gives up on a wait
     int *src_rows = reinterpret_cast<int *>(ctl_p + 256);   // [tn_max] activation row of each token of the tile
-    constexpr int NW = NT / 32;
+    constexpr int NW = NT / 32;   // dequantising warps
+    const bool control = warp == NW;
 
     // zero the activation halves of the stages once: rows >= m are never written and must read as 0
     for (int s = 0; s < NS; s++) {
         const uint32_t bst = base + s * stage_bytes + 2 * A_ATOM;
-        for (int i = tid; i < 2 * b_atom / 16; i += NT) st_shared16(bst + i * 16, 0u, 0u, 0u, 0u);
+        for (int i = tid; i < 2 * b_atom / 16 && !control; i += NT) st_shared16(bst + i * 16, 0u, 0u, 0u, 0u);
     }
-    for (int j = tid; j < m; j += NT) {
+    for (int j = tid; j < m && !control; j += NT) {
         int row = t0 + j;
         if (a.mode != DENSE4) {
             const int pair = rows_of[t0 + j];
@@ -333,12 +335,29 @@ __global__ void __launch_bounds__(NT) dqgemm_tc_kernel(const Args a) {
         tc_commit(done + st);
     };
     if (expert) {
-        if (tid == 32)
+        if (control && lane == 0)
             for (int kb = 0; kb < RD && kb < nkb; kb++) issue_raw(kb);
-    } else {
+    } else if (!control) {
         load_block(0);
     }
 
+    if (control) {
+        if (lane == 0) {
+            for (int kb = 0; kb < nkb; kb++) {
+                const int st = kb % NS, use = kb / NS;
+                if (*abort_flag || !finch_mbar_wait(a_full + st, use & 1)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                issue_mma(kb);
+                // every dequantising warp read block kb's ring slot before it arrived on a_full: refill it
+                if (expert && kb + RD < nkb) {
+                    if (finch_mbar_wait(raw_empty + kb % RD, (kb / RD) & 1)) issue_raw(kb + RD);
+                    else *abort_flag = 1;
+                }
+            }
+        }
+    } else
     for (int kb = 0; kb < nkb; kb++) {
         const int st = kb % NS, use = kb / NS, slot = kb % RD;
         const uint32_t ast = base + st * stage_bytes, bst = ast + 2 * A_ATOM;
@@ -377,11 +396,6 @@ __global__ void __launch_bounds__(NT) dqgemm_tc_kernel(const Args a) {
             if (lane == 0) {   // this warp is done with the ring slot
                 asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(finch_smem_u32(raw_empty + slot)) : "memory");
             }
-            // the producer refills the slot of block kb - 1 once every warp has read it
-            if (tid == 32 && kb >= 1 && kb + RD - 1 < nkb) {
-                if (finch_mbar_wait(raw_empty + (kb - 1) % RD, ((kb - 1) / RD) & 1)) issue_raw(kb + RD - 1);
-                else *abort_flag = 1;
-            }
         } else {
 #pragma unroll
             for (int i = 0; i < 8; i++) cur[i] = wreg[i];
@@ -414,12 +428,6 @@ __global__ void __launch_bounds__(NT) dqgemm_tc_kernel(const Args a) {
         proxy_fence();          // generic-proxy writes -> visible to the tensor core (async proxy)
         __syncwarp();
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(finch_smem_u32(a_full + st)) : "memory");
-        // one thread issues the block's MMAs as soon as every warp has written its share; the other
-        // warps are by then dequantising the next block into the other stage
-        if (tid == 0) {
-            if (finch_mbar_wait(a_full + st, use & 1)) issue_mma(kb);
-            else *abort_flag = 1;
-        }
     }
 
     // ---- epilogue ----
@@ -430,7 +438,7 @@ __global__ void __launch_bounds__(NT) dqgemm_tc_kernel(const Args a) {
         if (ok) ok = finch_mbar_wait(done + last % NS, (last / NS) & 1);
         if (__syncthreads_or(!ok)) failed = true;
     }
-    if (!failed) {
+    if (!failed && !control) {
         tc_fence_after();
         // warps w and w + 4 read the same 32 lanes and take alternate 16-column chunks
         const uint32_t trow = tmem_d + ((uint32_t)((warp & 3) * 32) << 16);
@@ -468,7 +476,7 @@ __global__ void __launch_bounds__(NT) dqgemm_tc_kernel(const Args a) {
                 }
             }
         }
-    } else if (tid == 0) {
+    } else if (failed && tid == 0) {
         atomicExch(a.status, FINCH_E_TIMEOUT);
     }
     tc_fence_before();

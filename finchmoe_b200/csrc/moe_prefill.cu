@@ -156,7 +156,7 @@ int launch_gemm(finch_ctx *ctx, cudaStream_t st, const dqgemm::Args &a, dim3 gri
     }
     const int smem = dqgemm::smem_bytes(a.tn_max, a.X2 ? 2 : 1, a.mode != dqgemm::DENSE4);
     if (smem > 227 * 1024) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "token tile %d needs %d bytes of shared memory", a.tn_max, smem);
-    dqgemm::dqgemm_tc_kernel<<<grid, dqgemm::NT, smem, st>>>(a);
+    dqgemm::dqgemm_tc_kernel<<<grid, dqgemm::NTB, smem, st>>>(a);
     FINCH_CUDA_OK(ctx, cudaGetLastError());
     ctx->launches++;
     return FINCH_OK;
