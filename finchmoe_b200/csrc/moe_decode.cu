@@ -1,23 +1,24 @@
 // MoE decode path: routed 3-bit experts (gate, up, SiLU, down), the 4-bit
-// shared expert and the router-weighted combine, in three launches per layer.
+// shared expert and the router-weighted combine, in four launches per layer chained
+// with programmatic dependent launch.
 //
 //   prep      groups the (token, k) pairs by expert, turns every token's
 //             activations into tensor-core operand records, and cuts the job
 //             lists of the two streaming kernels into one contiguous,
 //             cost-balanced range per CTA
-//   kernel A  gate/up/SiLU.  One persistent CTA per SM: a producer warp streams
-//             tiles (8 gate rows + the 8 matching up rows of one expert = one
-//             contiguous 14 KB piece of the tiled pool) through a ring of
-//             shared-memory stages with bulk async copies; twelve consumer
-//             warps each take whole tiles and run the tensor-core matvec on
-//             them, with no barrier between warps.  Writes act[pair][inter].
-//   kernel B  down + combine.  Same structure with tiles of 16 down rows.  Every
-//             CTA first turns the activations of the (few) expert groups in
-//             its range into operand records in its own shared memory.
-//             Per-pair outputs go to scratch; the CTA that completes a 64-row
-//             chunk sums them in k order with the residual and the gated
-//             shared expert (the arithmetic of moe_combine_residual,
-//             finchmoe/shaders.metal:2196-2231).
+//   gate/up   (moe_gateup_kernel) gate, up and SiLU.  One persistent CTA per SM: a
+//             producer warp streams tiles (8 gate rows + the 8 matching up rows of
+//             one expert = one contiguous 14 KB piece of the tiled pool) through a
+//             ring of shared-memory stages with bulk async copies; six teams of
+//             four consumer warps take whole tiles, the warps of a team split K and
+//             whichever finishes last adds the partial sums.  Writes act[pair][inter].
+//   down      (moe_down_combine_kernel) same structure with tiles of 16 down rows
+//             and sixteen independent consumer warps.  Every CTA first turns the
+//             activations of the (few) expert groups in its range into operand
+//             records in its own shared memory.  Writes one fp32 row per pair.
+//   combine   (moe_combine_kernel) sums the rows of a token in k order with the
+//             residual and the gated shared expert (the arithmetic of
+//             moe_combine_residual, finchmoe/shaders.metal:2196-2231).
 //
 // "Expert group" = the (token, k) pairs of this call that selected the same
 // expert: its weights are read from HBM once for all of them.
@@ -74,7 +75,6 @@ struct MoeArgs {
     int scale_dtype;
     float *act;          // [P][inter]
     float *partial;      // [P + B][hidden]
-    unsigned *cnt_b;     // [hidden / 64] chunk arrivals of kernel B
     int *status;
     int has_shared;
     const uint8_t *sh_tiles;  // prepared (tiled) copy of the shared expert
@@ -139,6 +139,10 @@ __device__ __forceinline__ long long gtime() {
     return t;
 }
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel of the chain be scheduled as soon as SMs free up instead of when this grid has
+// drained: its CTAs run their prologue (and whatever does not depend on this grid's output) and then
+// block in griddepcontrol.wait until this grid has completed and its writes are visible.
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ float pow2_biased(int e) { return __uint_as_float((uint32_t)e << 23); }
 __device__ __forceinline__ void bar_sync(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
@@ -559,6 +563,7 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(const MoeArgs a) {
     GroupTab *T = reinterpret_cast<GroupTab *>(sm_first + MAXP + 8);
     const int b = blockIdx.x, tid = threadIdx.x, K = a.hidden;
     const long long gt0 = gtime();
+    grid_dep_launch();
     grid_dep_wait();
     if (a.dbg && tid == 0) a.dbg[(size_t)(1300 + b) * 8] = gt0, a.dbg[(size_t)(1300 + b) * 8 + 1] = gtime();
     if (b < a.B) {
@@ -705,6 +710,7 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
         }
         finch_mbar_init(xbar, 1);
     }
+    grid_dep_launch();
     grid_dep_wait();  // everything above overlaps the tail of the preparation kernel
     {
         const int *s = reinterpret_cast<const int *>(a.gtab);
@@ -851,7 +857,7 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
 
 // ============================ kernel B ====================================
 struct SmemB {
-    int stage, stg, rec, srec, xstage, tab, ok, contrib, lastf, zero, bar, total;
+    int stage, stg, rec, srec, xstage, tab, zero, bar, total;
 };
 __host__ __device__ inline SmemB smem_b_layout(int hidden, int inter, int sh_inter, int B, int has_shared, int stages) {
     const FinchTile T = finch_tile(hidden, inter);
@@ -863,10 +869,7 @@ __host__ __device__ inline SmemB smem_b_layout(int hidden, int inter, int sh_int
     L.srec = up128(L.rec + REC_CAP * rec3_bytes(inter));     // shared_act records
     L.xstage = up128(L.srec + (has_shared ? B * rec4_bytes(sh_inter) : 0));   // one row of act per consumer warp
     L.tab = up128(L.xstage + CW_B * 4 * (inter > sh_inter ? inter : sh_inter));
-    L.ok = up128(L.tab + (int)sizeof(GroupTab));
-    L.contrib = L.ok + MAXP * 4;
-    L.lastf = L.contrib + 128 * 4;
-    L.zero = up128(L.lastf + 128);
+    L.zero = up128(L.tab + (int)sizeof(GroupTab));
     L.bar = L.zero + ZERO3_BYTES;
     L.total = L.bar + 2 * 32 * 8 + 16;
     return L;
@@ -895,7 +898,10 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
         }
     }
     if (tid < ZERO3_BYTES / 4) reinterpret_cast<int *>(smem + L.zero)[tid] = 0;
-    grid_dep_wait();  // the barrier set-up overlaps the tail of the gate/up kernel
+    grid_dep_launch();
+    // The group table and the job ranges are the preparation kernel's output: that grid completed before the
+    // gate/up kernel started, so they can be read, and the weight tiles streamed, while the gate/up kernel
+    // is still finishing on other SMs.  Only the activations (its output) have to wait.
     {
         const int *s = reinterpret_cast<const int *>(a.gtab);
         int *d = reinterpret_cast<int *>(tab);
@@ -929,6 +935,7 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
     }
 
     // ---------------- consumer warps ----------------
+    grid_dep_wait();   // the gate/up kernel has completed: act / shared_act are final
     // operand records of the activations this CTA needs: the pairs of the groups in its job range
     // (and every token's shared activations if it has shared-expert jobs), one warp per record
     const int g_lo = job0 < n_routed ? job0 / T.nTB : ng;
@@ -1022,6 +1029,7 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const MoeArgs a) {
     __shared__ float wk[8];
     const int b = blockIdx.y, row = blockIdx.x * 256 + threadIdx.x;
     const long long gt0 = gtime();
+    grid_dep_launch();
     grid_dep_wait();
     if (threadIdx.x < a.K) {
         ok[threadIdx.x] = pair_ok(a, b * a.K + threadIdx.x);
@@ -1153,7 +1161,6 @@ extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finc
     a.scale_dtype = c.scale_dtype;
     a.act = ctx->act;
     a.partial = ctx->partial;
-    a.cnt_b = ctx->counters;
     a.status = ctx->dev_status;
     a.h_mid = h_mid;
     a.hidden_out = hidden_out;
