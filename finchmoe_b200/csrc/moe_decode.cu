@@ -710,8 +710,10 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
         }
         finch_mbar_init(xbar, 1);
     }
-    grid_dep_launch();
     grid_dep_wait();  // everything above overlaps the tail of the preparation kernel
+    // only now may the down kernel be scheduled: it reads the preparation kernel's tables before its own wait,
+    // and every CTA of this grid gets here only after the preparation kernel has completed
+    grid_dep_launch();
     {
         const int *s = reinterpret_cast<const int *>(a.gtab);
         int *d = reinterpret_cast<int *>(tab);
