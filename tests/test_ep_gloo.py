@@ -43,6 +43,8 @@ T = (5, 7)[rank]                                   # ragged: the ranks own diffe
 r2 = synth.rng_for(9, 2, rank)
 x = r2.normal(0, 1, size=(T, 256)).astype(np.float32)
 ids, w = synth.zipf_routing(r2, T, 8, 4)
+if sys.argv[4] == "one_sided":                     # every token picks rank 0's experts only: rank 1 receives nothing
+    ids = np.stack([r2.permutation(4) for _ in range(T)]).astype(np.int32)
 valid = (r2.random((T, 4)) > 0.2).astype(np.uint8)
 if rank == 1:
     valid[0] = 0                                   # a token with no usable expert at all
@@ -64,11 +66,15 @@ print("rank", rank, "ok", err)
 '''
 
 
-def test_two_rank_layer_matches_single_process_oracle(tmp_path):
+import pytest
+
+
+@pytest.mark.parametrize("mode", ["mixed", "one_sided"])
+def test_two_rank_layer_matches_single_process_oracle(tmp_path, mode):
     script = tmp_path / "ep_worker.py"
     script.write_text(WORKER)
-    port = str(29600 + os.getpid() % 300)
-    procs = [subprocess.Popen([sys.executable, str(script), str(r), port, HERE], stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+    port = str(29600 + (os.getpid() + (7 if mode == "mixed" else 13)) % 300)
+    procs = [subprocess.Popen([sys.executable, str(script), str(r), port, HERE, mode], stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
              for r in range(2)]
     outs = [p.communicate(timeout=240)[0] for p in procs]
     for r, (p, o) in enumerate(zip(procs, outs)):
