@@ -201,6 +201,11 @@ class Context:
         self.check(fn(self.h, stream, pool.h, layer, _ptr(h_post), _ptr(ids), _ptr(weights), _ptr(valid),
                       C.byref(shared) if shared is not None else None, _ptr(h_mid), _ptr(hidden_out), B))
 
+    def encode_moe_gguf(self, experts: L.GgufExperts, h_post, ids, weights, valid, h_mid, hidden_out, B: int, stream=None):
+        """gpu_gguf_experts_forward (finchmoe/infer.m:3153): device pointers, enqueues only."""
+        self.check(self.lib.finch_encode_moe_gguf(self.h, stream, C.byref(experts), _ptr(h_post), _ptr(ids), _ptr(weights), _ptr(valid),
+                                                  _ptr(h_mid), _ptr(hidden_out), B))
+
     def moe_forward_host(self, pool: Pool, layer: int, h_post: np.ndarray, ids: np.ndarray, weights: np.ndarray,
                          valid=None, shared: L.Shared | None = None, gate_score=None, h_mid=None) -> np.ndarray:
         """Host buffers in, host buffer out (one H2D, the kernels, one D2H, wait)."""

@@ -21,9 +21,16 @@ struct FSpec {
     const uint16_t *S, *B;
     float *out;
     int out_dim, scale_dtype;
+    // stacked expert slabs (GGUF ffn_*_exps): the tensor starts at W + slab * ids[id_index] and the spec is
+    // skipped when that id is negative, out of range or masked; eid == NULL: W as given
+    const int32_t *eid;
+    const uint8_t *evalid;
+    int id_index, n_ids;
+    size_t slab;
+    size_t x_off;   // first activation element of this spec inside x (specs of one launch may have different inputs)
 };
 struct FPack {
-    FSpec s[8];
+    FSpec s[16];
     int n;
 };
 
@@ -194,7 +201,13 @@ struct Depth {
 template <int BITS, int MT>
 __global__ void __launch_bounds__(FNT, 1) fast_matvec_kernel(FPack pack, const void *x, int x_dtype, int M, int K) {
     extern __shared__ __align__(16) float fsm[];
-    const FSpec &sp = pack.s[blockIdx.y];
+    FSpec sp = pack.s[blockIdx.y];
+    if (sp.eid) {
+        const int e = sp.eid[sp.id_index];
+        if (e < 0 || e >= sp.n_ids || (sp.evalid && !sp.evalid[sp.id_index])) return;   // whole CTA: uniform
+        sp.W += sp.slab * (size_t)e;
+    }
+    x = x_dtype == FINCH_BF16 ? (const void *)((const uint16_t *)x + sp.x_off) : (const void *)((const float *)x + sp.x_off);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int Kp = (K + 1023) & ~1023, nchunk = K / 32;
     float *xs = fsm, *sx = fsm + (size_t)M * Kp, *sx16 = sx + (size_t)M * (Kp / 32);   // sums per 32 and per 16 values
@@ -378,7 +391,7 @@ int finch_try_fast_matvec(finch_ctx *ctx, cudaStream_t st, const void *x, int x_
         pack.n = n;
         for (int i = 0; i < n; i++)
             pack.s[i] = FSpec{(const uint8_t *)specs[i].W, (const uint16_t *)specs[i].scales, (const uint16_t *)specs[i].biases,
-                              outs[i] + (size_t)m0 * specs[i].out_dim, specs[i].out_dim, specs[i].scale_dtype};
+                              outs[i] + (size_t)m0 * specs[i].out_dim, specs[i].out_dim, specs[i].scale_dtype, nullptr, nullptr, 0, 0, 0, 0};
         const void *xm = (const char *)x + (size_t)m0 * K * xelt;
         int rc;
         if (bits == 4) rc = launch_fast<4>(ctx, st, pack, xm, x_dtype, mt, K, max_out, 0);
@@ -386,6 +399,139 @@ int finch_try_fast_matvec(finch_ctx *ctx, cudaStream_t st, const void *x, int x_
         else if (bits == 10) rc = launch_fast<10>(ctx, st, pack, xm, x_dtype, mt, K, max_out, 2);
         else rc = launch_fast<11>(ctx, st, pack, xm, x_dtype, mt, K, max_out, 3);
         if (rc) return rc;
+    }
+    return FINCH_OK;
+}
+
+// ---------------------------------------------------------------------------------------------------
+// GGUF expert MLP for decode (gpu_gguf_experts_forward, finchmoe/infer.m:3153-3366): the K selected experts
+// of a token straight from the stacked ffn_{gate,up,down}_exps slabs -- gate and up of all K experts in one
+// launch (they share the token's activations), SiLU(gate) * up, the K down projections in one launch (each
+// with its own input), then the reference's combine: moe_out = sum_k w_k * out_k over the experts whose
+// output energy is finite and below 1e20, divided by the accepted weight if that is in (0, 0.99)
+// (infer.m:3334-3347).
+namespace {
+
+__global__ void gguf_swiglu_kernel(const float *g, const float *u, float *act, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float gv = g[i];
+        act[i] = (gv / (1.0f + expf(-gv))) * u[i];
+    }
+}
+
+// one CTA of 256 threads per token
+__global__ void __launch_bounds__(256) gguf_combine_kernel(const float *outs, const int32_t *ids, const float *weights, const uint8_t *valid, int K,
+                                                           int n_experts, int hidden, const float *h_mid, float *hidden_out) {
+    __shared__ float red[8];
+    __shared__ float wk[8];
+    __shared__ float total;
+    const int tid = threadIdx.x;
+    if (tid == 0) total = 0.f;
+    for (int k = 0; k < K; k++) {
+        const int e = ids[k];
+        const bool usable = e >= 0 && e < n_experts && (!valid || valid[k]);
+        float er = 0.f;
+        if (usable)
+            for (int j = tid; j < hidden; j += 256) {
+                const float v = outs[(size_t)k * hidden + j];
+                er += v * v;
+            }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) er += __shfl_xor_sync(0xffffffffu, er, o);
+        if ((tid & 31) == 0) red[tid >> 5] = er;
+        __syncthreads();
+        if (tid == 0) {
+            float s = 0.f;
+            for (int w = 0; w < 8; w++) s += red[w];
+            const bool ok = usable && isfinite(s) && s < 1e20f;
+            wk[k] = ok ? weights[k] : 0.f;
+            if (ok) total += weights[k];
+        }
+        __syncthreads();
+    }
+    const float tw = total, inv = (tw > 0.f && tw < 0.99f) ? 1.0f / tw : 1.0f;
+    for (int j = tid; j < hidden; j += 256) {
+        float m = 0.f;
+        for (int k = 0; k < K; k++)
+            if (wk[k] != 0.f) m = fmaf(wk[k], outs[(size_t)k * hidden + j], m);
+        hidden_out[j] = (h_mid ? h_mid[j] : 0.f) + m * inv;
+    }
+}
+
+int launch_gguf(finch_ctx *ctx, cudaStream_t st, int type, const FPack &pack, const void *x, int x_dtype, int K, int max_out) {
+    if (type == 10) return launch_fast<10>(ctx, st, pack, x, x_dtype, 1, K, max_out, 2);
+    return launch_fast<11>(ctx, st, pack, x, x_dtype, 1, K, max_out, 3);
+}
+
+}  // namespace
+
+extern "C" int finch_encode_moe_gguf(finch_ctx *ctx, finch_stream stream, const finch_gguf_experts *ex, const void *h_post, const int32_t *expert_ids,
+                                     const float *weights, const uint8_t *valid, const float *h_mid, float *hidden_out, int B) {
+    if (!ctx || !ex || !h_post || !expert_ids || !weights || !hidden_out || B < 1) return FINCH_E_ARG;
+    const finch_config &c = ctx->cfg;
+    const int H = c.hidden, I = c.moe_inter, K = c.top_k;
+    for (int t : {ex->gate_type, ex->up_type, ex->down_type})
+        if (t != 10 && t != 11) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "GGUF expert tensors must be Q4_K (10) or Q6_K (11)");
+    if (H % 256 || I % 256 || K > 8) return finch_fail(ctx, FINCH_E_ARG, "GGUF experts: hidden and inter must be whole 256-value blocks, top_k <= 8");
+    if (!ex->gate || !ex->up || !ex->down) return finch_fail(ctx, FINCH_E_ARG, "GGUF experts: null slab");
+    cudaSetDevice(c.device);
+    cudaStream_t st = finch_pick_stream(ctx, stream);
+    const size_t need = (size_t)K * (3 * I + H) * sizeof(float);
+    if (ctx->gguf_ws_bytes < need) {
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        cudaStreamIsCapturing(st, &cap);
+        if (cap != cudaStreamCaptureStatusNone) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "first GGUF call must be outside stream capture");
+        if (ctx->gguf_ws) cudaFree(ctx->gguf_ws);
+        ctx->gguf_ws = nullptr;
+        ctx->gguf_ws_bytes = 0;
+        if (cudaMalloc(&ctx->gguf_ws, need) != cudaSuccess) {
+            cudaGetLastError();
+            return finch_fail(ctx, FINCH_E_NOMEM, "GGUF expert scratch (%zu bytes)", need);
+        }
+        ctx->gguf_ws_bytes = need;
+    }
+    float *g = (float *)ctx->gguf_ws, *u = g + (size_t)K * I, *act = u + (size_t)K * I, *outs = act + (size_t)K * I;
+    const int x_dtype = c.act_dtype;
+    for (int b = 0; b < B; b++) {
+        const int32_t *ids = expert_ids + (size_t)b * K;
+        const uint8_t *vb = valid ? valid + (size_t)b * K : nullptr;
+        const void *xb = x_dtype == FINCH_BF16 ? (const void *)((const uint16_t *)h_post + (size_t)b * H) : (const void *)((const float *)h_post + (size_t)b * H);
+        // a masked or absent expert leaves its rows untouched: clear them so the combine's energy test reads zeros, not stale data
+        FINCH_CUDA_OK(ctx, cudaMemsetAsync(outs, 0, (size_t)K * H * sizeof(float), st));
+        FINCH_CUDA_OK(ctx, cudaMemsetAsync(g, 0, (size_t)2 * K * I * sizeof(float), st));
+        int rc;
+        if (ex->gate_type == ex->up_type) {
+            FPack p;
+            p.n = 2 * K;
+            for (int k = 0; k < K; k++) {
+                p.s[k] = FSpec{(const uint8_t *)ex->gate, nullptr, nullptr, g + (size_t)k * I, I, FINCH_FP16, ids, vb, k, c.n_experts, ex->gate_slab, 0};
+                p.s[K + k] = FSpec{(const uint8_t *)ex->up, nullptr, nullptr, u + (size_t)k * I, I, FINCH_FP16, ids, vb, k, c.n_experts, ex->up_slab, 0};
+            }
+            if ((rc = launch_gguf(ctx, st, ex->gate_type, p, xb, x_dtype, H, I))) return rc;
+        } else {
+            for (int which = 0; which < 2; which++) {
+                FPack p;
+                p.n = K;
+                for (int k = 0; k < K; k++)
+                    p.s[k] = FSpec{(const uint8_t *)(which ? ex->up : ex->gate), nullptr, nullptr, (which ? u : g) + (size_t)k * I, I, FINCH_FP16, ids, vb, k,
+                                   c.n_experts, which ? ex->up_slab : ex->gate_slab, 0};
+                if ((rc = launch_gguf(ctx, st, which ? ex->up_type : ex->gate_type, p, xb, x_dtype, H, I))) return rc;
+            }
+        }
+        gguf_swiglu_kernel<<<(K * I + 255) / 256, 256, 0, st>>>(g, u, act, K * I);
+        FINCH_CUDA_OK(ctx, cudaGetLastError());
+        {
+            FPack p;
+            p.n = K;
+            for (int k = 0; k < K; k++)
+                p.s[k] = FSpec{(const uint8_t *)ex->down, nullptr, nullptr, outs + (size_t)k * H, H, FINCH_FP16, ids, vb, k, c.n_experts, ex->down_slab,
+                               (size_t)k * I};
+            if ((rc = launch_gguf(ctx, st, ex->down_type, p, act, FINCH_F32, I, H))) return rc;
+        }
+        gguf_combine_kernel<<<1, 256, 0, st>>>(outs, ids, weights + (size_t)b * K, vb, K, c.n_experts, H, h_mid ? h_mid + (size_t)b * H : nullptr,
+                                               hidden_out + (size_t)b * H);
+        FINCH_CUDA_OK(ctx, cudaGetLastError());
+        ctx->launches += 2;
     }
     return FINCH_OK;
 }

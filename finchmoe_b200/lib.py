@@ -39,6 +39,11 @@ class Shared(C.Structure):
     _fields_ = [("gate", WDesc), ("up", WDesc), ("down", WDesc), ("gate_score", C.c_void_p)]
 
 
+class GgufExperts(C.Structure):
+    _fields_ = [("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p), ("gate_slab", C.c_size_t), ("up_slab", C.c_size_t),
+                ("down_slab", C.c_size_t), ("gate_type", C.c_int), ("up_type", C.c_int), ("down_type", C.c_int)]
+
+
 class PoolStats(C.Structure):
     _fields_ = [("hits", C.c_uint64), ("misses", C.c_uint64), ("evictions", C.c_uint64), ("slots", C.c_int),
                 ("used", C.c_int), ("slot_bytes", C.c_size_t)]
@@ -75,6 +80,7 @@ _PROTOS = {
     "finch_encode_ep_unpack": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp]),
     "finch_encode_ep_combine": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i]),
     "finch_pool_fill_synthetic_range": (_i, [_vp, _i, _i, _i, _i, C.c_uint64]),
+    "finch_encode_moe_gguf": (_i, [_vp, _vp, C.POINTER(GgufExperts), _vp, _vp, _vp, _vp, _vp, _vp, _i]),
     "finch_moe_forward_host": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, C.POINTER(Shared), _vp, _vp, _vp, _i]),
     "finch_event_create": (_i, [_vp, C.POINTER(_vp)]),
     "finch_event_record": (_i, [_vp, _vp]),

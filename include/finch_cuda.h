@@ -253,6 +253,21 @@ FINCH_API int finch_set_prefill_mode(finch_ctx *ctx, int mode);
 FINCH_API int finch_encode_dense_gemm(finch_ctx *ctx, finch_stream stream, const finch_wdesc *w, const void *x_bf16,
                                       float *out, int M);
 
+/* gpu_gguf_experts_forward (finchmoe/infer.m:3153-3366; GgufExpertInfo 1017-1021): the K selected experts
+ * of each of B tokens straight from the stacked GGUF slabs ffn_{gate,up,down}_exps (device copies; expert e of a
+ * tensor starts at base + e * slab), types FINCH_BITS_Q4_K / FINCH_BITS_Q6_K.  hidden_out[b] = h_mid[b] (or 0) +
+ * sum_k w_k * out_k over the experts whose output energy is finite and < 1e20, renormalised by the accepted
+ * weight when that lies in (0, 0.99) -- the reference's guarded combine (infer.m:3334-3347).  No shared expert
+ * here: the reference's GGUF path adds it in the caller.  The first call allocates scratch (outside capture). */
+typedef struct finch_gguf_experts {
+    const void *gate, *up, *down;
+    size_t gate_slab, up_slab, down_slab;
+    int gate_type, up_type, down_type;
+} finch_gguf_experts;
+FINCH_API int finch_encode_moe_gguf(finch_ctx *ctx, finch_stream stream, const finch_gguf_experts *experts, const void *h_post,
+                                    const int32_t *expert_ids, const float *weights, const uint8_t *valid, const float *h_mid,
+                                    float *hidden_out, int B);
+
 /* ---- expert parallelism (no counterpart in the reference, which runs on one
  * device; extends the per-layer CMD3 of finchmoe/infer.m:9597-9741 across GPUs).
  * Rank r of `world` owns experts [r*E/world, (r+1)*E/world) of every layer and

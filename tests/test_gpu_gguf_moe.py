@@ -1,0 +1,65 @@
+"""GGUF expert MLP for decode (finch_encode_moe_gguf) against the oracle: Q4_K gate / up, Q6_K down (the Q4_K_M
+mix), stacked slabs, the reference's guarded combine (finite-energy test and renormalisation)."""
+import numpy as np
+import pytest
+
+from finchmoe_b200 import lib as L
+from finchmoe_b200 import synth
+from oracle import oracle
+from parity import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _expert_out(gate, up, down, x):
+    g = oracle.matvec(gate["W"], None, None, 1, x, gate["out_dim"], gate["in_dim"], 256, gate["bits"])
+    u = oracle.matvec(up["W"], None, None, 1, x, up["out_dim"], up["in_dim"], 256, up["bits"])
+    act = oracle.swiglu(g, u)
+    return oracle.matvec(down["W"], None, None, 1, act, down["out_dim"], down["in_dim"], 256, down["bits"])
+
+
+@pytest.mark.parametrize("types", [(12, 12, 14), (12, 14, 12), (14, 14, 14)])
+@pytest.mark.parametrize("B", [1, 3])
+def test_gguf_expert_moe_vs_oracle(types, B):
+    import torch
+    from finchmoe_b200 import api
+    H, I, NE, K = 512, 256, 6, 4
+    ctx = api.Context(hidden=H, n_experts=NE, top_k=K, moe_inter=I, shared_inter=256, n_layers=1, act_dtype=L.F32, max_tokens=4)
+    try:
+        rng = synth.rng_for(14, B, types[1])
+        ex = [(synth.gguf_tensor(rng, I, H, types[0]), synth.gguf_tensor(rng, I, H, types[1]), synth.gguf_tensor(rng, H, I, types[2]))
+              for _ in range(NE)]
+        slabs = [np.stack([e[i]["W"] for e in ex]) for i in range(3)]          # [NE, rows, row_bytes]
+        dev = [torch.from_numpy(s).cuda() for s in slabs]
+        ge = L.GgufExperts(dev[0].data_ptr(), dev[1].data_ptr(), dev[2].data_ptr(), slabs[0][0].nbytes, slabs[1][0].nbytes, slabs[2][0].nbytes,
+                           ex[0][0]["bits"], ex[0][1]["bits"], ex[0][2]["bits"])
+        x = rng.normal(0, 1, size=(B, H)).astype(np.float32)
+        ids = np.stack([rng.permutation(NE)[:K] for _ in range(B)]).astype(np.int32)
+        w = rng.random((B, K)).astype(np.float32)
+        w /= w.sum(axis=1, keepdims=True)
+        valid = np.ones((B, K), np.uint8)
+        valid[0, 1] = 0                       # a masked expert: the accepted weight drops below 0.99 -> renormalised
+        if B > 1:
+            ids[1, 2] = -1                    # an absent expert
+        h_mid = rng.normal(0, 1, size=(B, H)).astype(np.float32)
+        d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        out = torch.empty((B, H), dtype=torch.float32, device="cuda")
+        xd, idd, wd, vd, hd = d(x), d(ids), d(w), d(valid), d(h_mid)
+        torch.cuda.synchronize()
+        for rep in range(2):
+            ctx.encode_moe_gguf(ge, xd, idd, wd, vd, hd, out, B)
+        ctx.sync()
+        got = out.cpu().numpy()
+        for b in range(B):
+            outs = np.zeros((K, H), np.float32)
+            ok = np.zeros(K, np.uint8)
+            for k in range(K):
+                e = int(ids[b, k])
+                if valid[b, k] and 0 <= e < NE:
+                    outs[k] = _expert_out(*ex[e], x[b])
+                    ok[k] = 1
+            want = oracle.combine(h_mid[b], outs, w[b], ok, np.zeros(H, np.float32), 0.0, guard=1)
+            assert_close(got[b], want, f"GGUF MoE types={types} token {b}")
+        assert ctx.device_status() == 0
+    finally:
+        ctx.destroy()
