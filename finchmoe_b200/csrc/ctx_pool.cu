@@ -103,6 +103,7 @@ extern "C" void finch_ctx_destroy(finch_ctx *ctx) {
     cudaFree(ctx->stage_dev);
     cudaFree(ctx->pf_ws);
     cudaFree(ctx->gguf_ws);
+    cudaFree(ctx->logits);
     if (ctx->stage_host) cudaFreeHost(ctx->stage_host);
     for (cudaEvent_t e : ctx->prof_events) cudaEventDestroy(e);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);

@@ -475,3 +475,30 @@ extern "C" int finch_matvec_noalloc(const finch_wdesc *w, const float *x_host, f
     if (cudaStreamSynchronize(st) != cudaSuccess) return FINCH_E_CUDA;
     return FINCH_OK;
 }
+
+// Router front end of a layer (routing_batch_fused / the gemv_bf16 fallback + cpu_softmax / cpu_topk /
+// cpu_normalize_weights, finchmoe/infer.m:9061-9105, 9285-9289): logits = gate * h_post, the shared expert's gate
+// score = shared_gate * h_post, then softmax / top-K / renormalise on the device -- no host round trip.
+extern "C" int finch_encode_router(finch_ctx *ctx, finch_stream stream, const finch_wdesc *gate, const finch_wdesc *shared_gate, const void *h_post,
+                                   int32_t *ids, float *weights, float *shared_score, int T) {
+    if (!ctx || !gate || !h_post || !ids || !weights || T < 1) return FINCH_E_ARG;
+    const finch_config &c = ctx->cfg;
+    if (gate->out_dim != c.n_experts || gate->in_dim != c.hidden) return finch_fail(ctx, FINCH_E_ARG, "router gate must be [n_experts x hidden]");
+    if (shared_gate && (!shared_score || shared_gate->out_dim != 1 || shared_gate->in_dim != c.hidden))
+        return finch_fail(ctx, FINCH_E_ARG, "shared gate must be [1 x hidden] with a score output");
+    if (T > c.max_tokens) return finch_fail(ctx, FINCH_E_ARG, "T=%d exceeds max_tokens=%d", T, c.max_tokens);
+    if (!ctx->logits) {
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        cudaStreamIsCapturing(finch_pick_stream(ctx, stream), &cap);
+        if (cap != cudaStreamCaptureStatusNone) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "first router call must be outside stream capture");
+        if (cudaMalloc(&ctx->logits, (size_t)c.max_tokens * c.n_experts * sizeof(float)) != cudaSuccess) {
+            cudaGetLastError();
+            return finch_fail(ctx, FINCH_E_NOMEM, "router logits");
+        }
+    }
+    finch_wdesc specs[2] = {*gate, shared_gate ? *shared_gate : *gate};
+    float *outs[2] = {ctx->logits, shared_score};
+    int rc = finch_encode_batch_matvec(ctx, stream, h_post, c.act_dtype, specs, outs, shared_gate ? 2 : 1, T);
+    if (rc) return rc;
+    return finch_encode_route_topk(ctx, stream, ctx->logits, c.n_experts, c.top_k, ids, weights, T);
+}

@@ -171,6 +171,14 @@ FINCH_API int finch_encode_batch_matvec(finch_ctx *ctx, finch_stream stream, con
 FINCH_API int finch_encode_route_topk(finch_ctx *ctx, finch_stream stream, const float *logits, int n_experts,
                                       int K, int32_t *ids, float *weights, int T);
 
+/* Router front end of a layer without the host round trip the reference pays (finchmoe/infer.m:9061-9105 runs
+ * the gate matvecs on the GPU, waits, then cpu_softmax / cpu_topk / cpu_normalize_weights, 9285-9289): logits =
+ * gate [n_experts x hidden] * h_post, shared_score = shared_gate [1 x hidden] * h_post (or NULL), then
+ * finch_encode_route_topk.  gate / shared_gate are any matvec tier (BF16 rows with the default quantizer,
+ * finchmoe/quantize_non_experts.py:103-105).  h_post [T][hidden] in the context's act dtype; all device. */
+FINCH_API int finch_encode_router(finch_ctx *ctx, finch_stream stream, const finch_wdesc *gate, const finch_wdesc *shared_gate,
+                                  const void *h_post, int32_t *ids, float *weights, float *shared_score, int T);
+
 /* Shared expert and its gate: finchmoe/infer.m:9608-9629 and the
  * sigmoid(shared_gate_score) factor of moe_combine_residual
  * (finchmoe/shaders.metal:2196-2231). */

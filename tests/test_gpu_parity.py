@@ -416,3 +416,39 @@ def test_event_wait_and_launch_count(api):
         assert ctx.launch_count() == n0 + 1
     finally:
         ctx.destroy()
+
+
+@pytest.mark.parametrize("T", [1, 8, 20])
+def test_router_front_end_vs_oracle(api, T):
+    """gate (BF16 rows, the default quantizer's choice) x h_post -> softmax / top-8 / renormalise, plus the shared
+    expert's gate score, all on the device (finch_encode_router) against the oracle's matvec + route."""
+    import torch
+    ctx = api.Context(hidden=512, n_experts=64, top_k=8, moe_inter=128, shared_inter=128, n_layers=1, act_dtype=L.BF16, max_tokens=32)
+    try:
+        rng = synth.rng_for(16, T)
+        gate = synth.f32_to_bf16_rne(rng.normal(0, 0.2, size=(64, 512)).astype(np.float32))
+        sgate = synth.f32_to_bf16_rne(rng.normal(0, 0.2, size=(1, 512)).astype(np.float32))
+        wg = ctx.upload_tensor(dict(W=gate, S=None, B=None, out_dim=64, in_dim=512, bits=0, scale_dtype=L.BF16))
+        ws = ctx.upload_tensor(dict(W=sgate, S=None, B=None, out_dim=1, in_dim=512, bits=0, scale_dtype=L.BF16))
+        x = synth.activations(rng, T, 512)
+        xd = torch.from_numpy(x).cuda().to(torch.bfloat16)
+        ids = torch.empty((T, 8), dtype=torch.int32, device="cuda")
+        w = torch.empty((T, 8), dtype=torch.float32, device="cuda")
+        score = torch.empty(T, dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        import ctypes as C
+        ctx.check(ctx.lib.finch_encode_router(ctx.h, None, C.byref(wg), C.byref(ws), xd.data_ptr(), ids.data_ptr(), w.data_ptr(),
+                                              score.data_ptr(), T))
+        ctx.sync()
+        g64 = synth.bf16_to_f32(gate).astype(np.float64)
+        for t in range(T):
+            logits = (g64 @ x[t].astype(np.float64)).astype(np.float32)
+            want_ids, want_w = orc.route(logits, 8)
+            got_ids, got_w = ids[t].cpu().numpy(), w[t].cpu().numpy()
+            assert sorted(got_ids.tolist()) == sorted(want_ids.tolist()), f"token {t}"
+            order = {int(e): i for i, e in enumerate(want_ids)}
+            assert np.allclose(got_w, want_w[[order[int(e)] for e in got_ids]], rtol=1e-4, atol=1e-6)
+        want_s = synth.bf16_to_f32(sgate).astype(np.float64)[0] @ x.astype(np.float64).T
+        assert np.allclose(score.cpu().numpy(), want_s, rtol=1e-4, atol=1e-5)
+    finally:
+        ctx.destroy()
