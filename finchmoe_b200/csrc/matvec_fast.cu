@@ -1,4 +1,4 @@
-// Streaming quantized matvec for 1..8 positions: 3-bit and 4-bit affine g64 and GGUF Q4_K / Q6_K tensors in the
+// Streaming quantized matvec for 1..8 positions: 3-, 4- and 8-bit affine g64 and GGUF Q4_K / Q6_K tensors in the
 // reference's own layouts (dequant_matvec_3bit / _4bit_v3 / dequant_matvec_qk, finchmoe/shaders.metal:
 // 544-612, 374-463, 3216-3299; cpu twins finchmoe/infer.m:1660-1763).
 //
@@ -46,7 +46,7 @@ __device__ __forceinline__ float h_hi(uint32_t r) { return __high2float(*reinter
 // Packed words of one 32-code chunk of a row (loaded one iteration ahead of their use).
 template <int BITS>
 struct Raw {
-    uint32_t w[BITS == 4 ? 4 : BITS == 3 ? 3 : BITS == 10 ? 8 : 16];
+    uint32_t w[BITS == 4 ? 4 : BITS == 3 ? 3 : (BITS == 10 || BITS == 8) ? 8 : 16];
 };
 template <int BITS>
 __device__ __forceinline__ Raw<BITS> load_raw(const FSpec &sp, size_t row, int K, int c);
@@ -106,6 +106,27 @@ __device__ __forceinline__ void decode_chunk<3>(const FSpec &sp, size_t row, int
     for (int k = 0; k < 36; k++) {
         if (IDX[k] < 0) continue;
         qf[IDX[k]] = (k & 1) ? h_hi(e[k >> 1]) : h_lo(e[k >> 1]);
+    }
+    const size_t g = row * (size_t)(K / 64) + (c >> 1);
+    s = finch_widen16(__ldg(sp.S + g), sp.scale_dtype);
+    b = finch_widen16(__ldg(sp.B + g), sp.scale_dtype);
+}
+
+template <>
+__device__ __forceinline__ Raw<8> load_raw<8>(const FSpec &sp, size_t row, int K, int c) {
+    const uint4 *q = reinterpret_cast<const uint4 *>(sp.W + row * (size_t)K) + 2 * c;
+    const uint4 a = __ldg(q), bb = __ldg(q + 1);
+    return Raw<8>{{a.x, a.y, a.z, a.w, bb.x, bb.y, bb.z, bb.w}};
+}
+// 8-bit affine g64 (dequant_matvec_8bit, finchmoe/shaders.metal:473-533): a byte at bits [0, 8) of a half is the fp16
+// subnormal q * 2^-24 as well.
+template <>
+__device__ __forceinline__ void decode_chunk<8>(const FSpec &sp, size_t row, int K, int c, const Raw<8> &raw, float (&qf)[32], float &s, float &b) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint32_t e0 = raw.w[i] & 0x00FF00FFu, e1 = (raw.w[i] >> 8) & 0x00FF00FFu;   // bytes (0, 2) and (1, 3)
+        qf[4 * i + 0] = h_lo(e0); qf[4 * i + 2] = h_hi(e0);
+        qf[4 * i + 1] = h_lo(e1); qf[4 * i + 3] = h_hi(e1);
     }
     const size_t g = row * (size_t)(K / 64) + (c >> 1);
     s = finch_widen16(__ldg(sp.S + g), sp.scale_dtype);
@@ -346,7 +367,7 @@ __global__ void __launch_bounds__(FNT, 1) fast_matvec_kernel(FPack pack, const v
     }
 }
 
-bool g_fast_attr[8] = {false, false, false, false, false, false, false, false};
+bool g_fast_attr[10] = {false, false, false, false, false, false, false, false, false, false};
 
 template <int BITS>
 int launch_fast(finch_ctx *ctx, cudaStream_t st, const FPack &pack, const void *x, int x_dtype, int M, int K, int max_out, int slot) {
@@ -375,7 +396,7 @@ int launch_fast(finch_ctx *ctx, cudaStream_t st, const FPack &pack, const void *
 int finch_try_fast_matvec(finch_ctx *ctx, cudaStream_t st, const void *x, int x_dtype, const finch_wdesc *specs, float *const *outs, int n, int M) {
     if (M > 16 * FM || n > 8) return -1;
     const int bits = specs[0].bits, K = specs[0].in_dim;
-    if (bits != 3 && bits != 4 && bits != 10 && bits != 11) return -1;
+    if (bits != 3 && bits != 4 && bits != 8 && bits != 10 && bits != 11) return -1;
     if (K % 32 || (bits >= 10 && K % 256)) return -1;
     const int Kp = (K + 1023) & ~1023, Mmax = M < FM ? M : FM;
     if (((size_t)Mmax * Kp + (size_t)Mmax * (Kp / 32) + (size_t)Mmax * (Kp / 16)) * sizeof(float) > 200 * 1024) return -1;
@@ -396,6 +417,7 @@ int finch_try_fast_matvec(finch_ctx *ctx, cudaStream_t st, const void *x, int x_
         int rc;
         if (bits == 4) rc = launch_fast<4>(ctx, st, pack, xm, x_dtype, mt, K, max_out, 0);
         else if (bits == 3) rc = launch_fast<3>(ctx, st, pack, xm, x_dtype, mt, K, max_out, 1);
+        else if (bits == 8) rc = launch_fast<8>(ctx, st, pack, xm, x_dtype, mt, K, max_out, 4);
         else if (bits == 10) rc = launch_fast<10>(ctx, st, pack, xm, x_dtype, mt, K, max_out, 2);
         else rc = launch_fast<11>(ctx, st, pack, xm, x_dtype, mt, K, max_out, 3);
         if (rc) return rc;

@@ -78,7 +78,7 @@ def test_dequant_gguf_bit_exact(ctx_small, golden_dir, ty, bits):
 
 # ------------------------------------------------------------------- matvec
 @pytest.mark.parametrize("bits,o,i", [(3, 96, 2048), (4, 64, 4096), (8, 40, 512), (10, 72, 2048), (11, 72, 512), (11, 33, 2048),
-                                      (3, 33, 512), (4, 45, 1536), (10, 41, 512), (4, 2048, 4096)])
+                                      (3, 33, 512), (4, 45, 1536), (10, 41, 512), (4, 2048, 4096), (8, 1000, 2048)])
 @pytest.mark.parametrize("M", [1, 3, 9])
 def test_matvec_vs_oracle(ctx_small, bits, o, i, M):
     rng = synth.rng_for(4, bits, M)
