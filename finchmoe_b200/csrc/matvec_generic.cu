@@ -502,3 +502,46 @@ extern "C" int finch_encode_router(finch_ctx *ctx, finch_stream stream, const fi
     if (rc) return rc;
     return finch_encode_route_topk(ctx, stream, ctx->logits, c.n_experts, c.top_k, ids, weights, T);
 }
+
+// Residual add + RMS norm either side of the MoE layer (residual_norm_fused, finchmoe/shaders.metal:1232-1263;
+// rms_norm_sum_sq + rms_norm_apply_bf16 after the combine, finchmoe/infer.m:9705-9737): h = resid + oproj,
+// h_post = h / sqrt(mean(h^2) + eps) * w.  One CTA of 256 threads per token.
+namespace {
+__global__ void __launch_bounds__(256) residual_norm_kernel(const float *resid, const float *oproj, const uint16_t *norm_w, int dim, float eps,
+                                                            float *h_mid_out, void *h_post_out, int out_dtype) {
+    __shared__ float red[8];
+    const int t = blockIdx.x, tid = threadIdx.x;
+    const float *r = resid + (size_t)t * dim, *o = oproj ? oproj + (size_t)t * dim : nullptr;
+    float s = 0.f;
+    for (int i = tid; i < dim; i += 256) {
+        const float h = o ? r[i] + o[i] : r[i];
+        if (h_mid_out) h_mid_out[(size_t)t * dim + i] = h;
+        s = fmaf(h, h, s);
+    }
+#pragma unroll
+    for (int k = 16; k; k >>= 1) s += __shfl_xor_sync(0xffffffffu, s, k);
+    if ((tid & 31) == 0) red[tid >> 5] = s;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; w++) tot += red[w];
+    const float inv = 1.0f / sqrtf(tot / (float)dim + eps);
+    for (int i = tid; i < dim; i += 256) {
+        const float h = o ? r[i] + o[i] : r[i];
+        const float v = h * inv * __uint_as_float((uint32_t)norm_w[i] << 16);
+        if (out_dtype == FINCH_BF16) ((__nv_bfloat16 *)h_post_out)[(size_t)t * dim + i] = __float2bfloat16_rn(v);
+        else ((float *)h_post_out)[(size_t)t * dim + i] = v;
+    }
+}
+}  // namespace
+
+extern "C" int finch_encode_residual_norm(finch_ctx *ctx, finch_stream stream, const float *resid, const float *oproj, const uint16_t *norm_w_bf16,
+                                          float eps, float *h_mid_out, void *h_post_out, int T) {
+    if (!ctx || !resid || !norm_w_bf16 || !h_post_out || T < 1) return FINCH_E_ARG;
+    cudaSetDevice(ctx->cfg.device);
+    residual_norm_kernel<<<T, 256, 0, finch_pick_stream(ctx, stream)>>>(resid, oproj, norm_w_bf16, ctx->cfg.hidden, eps, h_mid_out, h_post_out,
+                                                                        ctx->cfg.act_dtype);
+    ctx->launches++;
+    FINCH_CUDA_OK(ctx, cudaGetLastError());
+    return FINCH_OK;
+}

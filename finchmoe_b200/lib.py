@@ -80,6 +80,7 @@ _PROTOS = {
     "finch_encode_ep_unpack": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp]),
     "finch_encode_ep_combine": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i]),
     "finch_pool_fill_synthetic_range": (_i, [_vp, _i, _i, _i, _i, C.c_uint64]),
+    "finch_encode_residual_norm": (_i, [_vp, _vp, _vp, _vp, _vp, C.c_float, _vp, _vp, _i]),
     "finch_encode_router": (_i, [_vp, _vp, C.POINTER(WDesc), C.POINTER(WDesc), _vp, _vp, _vp, _vp, _i]),
     "finch_encode_moe_gguf": (_i, [_vp, _vp, C.POINTER(GgufExperts), _vp, _vp, _vp, _vp, _vp, _vp, _i]),
     "finch_moe_forward_host": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, C.POINTER(Shared), _vp, _vp, _vp, _i]),

@@ -179,6 +179,13 @@ FINCH_API int finch_encode_route_topk(finch_ctx *ctx, finch_stream stream, const
 FINCH_API int finch_encode_router(finch_ctx *ctx, finch_stream stream, const finch_wdesc *gate, const finch_wdesc *shared_gate,
                                   const void *h_post, int32_t *ids, float *weights, float *shared_score, int T);
 
+/* residual_norm_fused (finchmoe/shaders.metal:1232-1263) before the layer, and the RMS norm of the next
+ * layer's input after the combine (finchmoe/infer.m:9705-9737) with oproj = NULL: h = resid + oproj,
+ * h_mid_out = h (or NULL), h_post_out = h / sqrt(mean(h^2) + eps) * norm_w, written in the context's act dtype.
+ * resid / oproj / h_mid_out fp32 [T][hidden], norm_w bf16 [hidden]; device pointers. */
+FINCH_API int finch_encode_residual_norm(finch_ctx *ctx, finch_stream stream, const float *resid, const float *oproj,
+                                         const uint16_t *norm_w_bf16, float eps, float *h_mid_out, void *h_post_out, int T);
+
 /* Shared expert and its gate: finchmoe/infer.m:9608-9629 and the
  * sigmoid(shared_gate_score) factor of moe_combine_residual
  * (finchmoe/shaders.metal:2196-2231). */

@@ -573,6 +573,24 @@ FO_API void fo_moe_layer(const uint8_t *const *blocks, const float *w, const uin
 /* Exhaustive self-check helper: the reference's magic-number fp16 widening
  * (finchmoe/infer.m:1579-1593) restated with explicit steps, so the test can
  * confirm the field-based fo_fp16_to_f32 above agrees on all 65536 inputs. */
+/* Residual add + RMS norm (residual_norm_fused, finchmoe/shaders.metal:1232-1263; cpu_rms_norm,
+ * finchmoe/infer.m:1766-1777): h = resid + oproj (oproj may be NULL), h_mid_out = h (may be NULL),
+ * h_post_out = h * (1 / sqrt(mean(h^2) + eps)) * bf16(w), fp32, sequential sum like the CPU form. */
+FO_API void fo_residual_norm(const float *resid, const float *oproj, const uint16_t *norm_w, int dim, float eps,
+                             float *h_mid_out, float *h_post_out) {
+    float sum_sq = 0.0f;
+    for (int i = 0; i < dim; i++) {
+        const float h = oproj ? resid[i] + oproj[i] : resid[i];
+        if (h_mid_out) h_mid_out[i] = h;
+        sum_sq += h * h;
+    }
+    const float inv_rms = 1.0f / sqrtf(sum_sq / (float)dim + eps);
+    for (int i = 0; i < dim; i++) {
+        const float h = oproj ? resid[i] + oproj[i] : resid[i];
+        h_post_out[i] = h * inv_rms * fo_bf16_to_f32(norm_w[i]);
+    }
+}
+
 FO_API float fo_fp16_to_f32_magic(uint16_t h) {
     const uint32_t w = (uint32_t)h << 16, sign = w & 0x80000000u, two_w = w + w;
     uint32_t nb = (two_w >> 4) + (0xE0u << 23), db = (two_w >> 17) | (126u << 23), rb;

@@ -156,6 +156,14 @@ def swiglu(g, u):
     return out
 
 
+def residual_norm(resid, oproj, norm_w_bf16, eps):
+    """(h_mid, h_post) of residual_norm_fused; oproj may be None."""
+    resid, oproj, w = _c(resid, np.float32), _c(oproj, np.float32), _c(norm_w_bf16, np.uint16)
+    h_mid, h_post = np.empty_like(resid), np.empty_like(resid)
+    lib().fo_residual_norm(_p(resid), _p(oproj), _p(w), resid.size, C.c_float(eps), _p(h_mid), _p(h_post))
+    return h_mid, h_post
+
+
 def route(logits, K):
     """softmax -> top-K (reference tie rule, slot order) -> renormalise."""
     logits = _c(logits, np.float32)

@@ -452,3 +452,33 @@ def test_router_front_end_vs_oracle(api, T):
         assert np.allclose(score.cpu().numpy(), want_s, rtol=1e-4, atol=1e-5)
     finally:
         ctx.destroy()
+
+
+@pytest.mark.parametrize("ad", [L.F32, L.BF16])
+def test_residual_norm_vs_oracle(api, ad):
+    import ctypes as C
+
+    import torch
+    ctx = api.Context(hidden=2048, n_layers=1, act_dtype=ad, max_tokens=4)
+    try:
+        rng = synth.rng_for(17, ad)
+        T = 3
+        resid, oproj = rng.normal(0, 1, (T, 2048)).astype(np.float32), rng.normal(0, 1, (T, 2048)).astype(np.float32)
+        w = synth.f32_to_bf16_rne(rng.normal(1, 0.1, 2048).astype(np.float32))
+        d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        rd, od, wd = d(resid), d(oproj), d(w.view(np.int16))
+        h_mid = torch.empty((T, 2048), dtype=torch.float32, device="cuda")
+        h_post = torch.empty((T, 2048), dtype=torch.float32 if ad == L.F32 else torch.bfloat16, device="cuda")
+        torch.cuda.synchronize()
+        for op in (od, None):
+            ctx.check(ctx.lib.finch_encode_residual_norm(ctx.h, None, rd.data_ptr(), op.data_ptr() if op is not None else None, wd.data_ptr(),
+                                                         C.c_float(1e-6), h_mid.data_ptr(), h_post.data_ptr(), T))
+            ctx.sync()
+            for t in range(T):
+                want_mid, want_post = orc.residual_norm(resid[t], oproj[t] if op is not None else None, w, 1e-6)
+                assert np.array_equal(h_mid[t].cpu().numpy(), want_mid)
+                got = h_post[t].float().cpu().numpy()
+                tol = 2e-6 if ad == L.F32 else 2 ** -8
+                assert np.allclose(got, want_post, rtol=tol, atol=1e-6)
+    finally:
+        ctx.destroy()

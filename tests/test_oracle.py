@@ -166,3 +166,18 @@ def test_moe_layer_f32_order_vs_f64_spread():
     c = orc.moe_layer(blocks, w[0], None, x, scale_dtype=0, hidden=hid, inter=inter, accum=orc.ACC_F64, nthreads=8)
     assert np.array_equal(b, c)
     assert_close(a, b, "f32-order vs f64")
+
+
+def test_residual_norm_restatement_against_numpy():
+    """fo_residual_norm follows residual_norm_fused / cpu_rms_norm; pinned here against a float64 numpy form."""
+    rng = np.random.default_rng(5)
+    resid, oproj = rng.normal(0, 1, 2048).astype(np.float32), rng.normal(0, 1, 2048).astype(np.float32)
+    w = synth.f32_to_bf16_rne(rng.normal(1, 0.1, 2048).astype(np.float32))
+    h_mid, h_post = orc.residual_norm(resid, oproj, w, 1e-6)
+    h = resid.astype(np.float64) + oproj
+    want = h / np.sqrt((h * h).mean() + 1e-6) * synth.bf16_to_f32(w)
+    assert np.array_equal(h_mid, resid + oproj)
+    assert np.allclose(h_post, want, rtol=2e-6, atol=1e-7)
+    _, plain = orc.residual_norm(resid, None, w, 1e-6)
+    r = resid.astype(np.float64)
+    assert np.allclose(plain, r / np.sqrt((r * r).mean() + 1e-6) * synth.bf16_to_f32(w), rtol=2e-6, atol=1e-7)
