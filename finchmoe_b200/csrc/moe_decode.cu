@@ -859,7 +859,7 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
 
 // ============================ kernel B ====================================
 struct SmemB {
-    int stage, stg, rec, srec, xstage, tab, zero, bar, total;
+    int stage, stg, rec, srec, xstage, umax, tab, zero, bar, total;
 };
 __host__ __device__ inline SmemB smem_b_layout(int hidden, int inter, int sh_inter, int B, int has_shared, int stages) {
     const FinchTile T = finch_tile(hidden, inter);
@@ -869,8 +869,9 @@ __host__ __device__ inline SmemB smem_b_layout(int hidden, int inter, int sh_int
     L.stg = up128(has_shared && T4.tileB > T.tileB ? T4.tileB : T.tileB);
     L.rec = L.stage + stages * L.stg;                        // act records of the groups in this CTA's range
     L.srec = up128(L.rec + REC_CAP * rec3_bytes(inter));     // shared_act records
-    L.xstage = up128(L.srec + (has_shared ? B * rec4_bytes(sh_inter) : 0));   // one row of act per consumer warp
-    L.tab = up128(L.xstage + CW_B * 4 * (inter > sh_inter ? inter : sh_inter));
+    L.xstage = up128(L.srec + (has_shared ? B * rec4_bytes(sh_inter) : 0));   // the act rows behind the records, staged as fp32
+    L.umax = up128(L.xstage + REC_CAP * 4 * inter);                            // max |act| per (record, 128-value unit)
+    L.tab = up128(L.umax + REC_CAP * (inter / 128) * 4);
     L.zero = up128(L.tab + (int)sizeof(GroupTab));
     L.bar = L.zero + ZERO3_BYTES;
     L.total = L.bar + 2 * 32 * 8 + 16;
@@ -939,20 +940,51 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
     // ---------------- consumer warps ----------------
     grid_dep_wait();   // the gate/up kernel has completed: act / shared_act are final
     // operand records of the activations this CTA needs: the pairs of the groups in its job range
-    // (and every token's shared activations if it has shared-expert jobs), one warp per record
+    // (and every token's shared activations if it has shared-expert jobs)
     const int g_lo = job0 < n_routed ? job0 / T.nTB : ng;
     const int g_hi = job1 > job0 ? min(ng - 1, (job1 - 1) / T.nTB) : -1;   // inclusive
     {
-        float *xstage = reinterpret_cast<float *>(smem + L.xstage) + (size_t)warp * (K > Ks ? K : Ks);
-        int q = 0;
-        for (int gi = g_lo; gi <= g_hi; gi++)
-            for (int i = 0; i < tab->m[gi]; i++, q++)
-                if (q % CW_B == warp && q < REC_CAP)
-                    warp_make_record<3>(a.act + (size_t)tab->pairs[gi][i] * K, K, smem + L.rec + q * r3b, xstage);
-        if (q > REC_CAP && tid == 0) atomicExch(a.status, FINCH_E_UNSUPPORTED);
+        // One warp per (record, 128-value unit): first the unit's values are staged, its two group sums written and its
+        // largest magnitude noted; after a barrier every unit knows its record's exponent and builds its fragments.
+        float *xstage = reinterpret_cast<float *>(smem + L.xstage), *umax = reinterpret_cast<float *>(smem + L.umax);
+        const int units = K / 128;
+        int nrec = 0;
+        for (int gi = g_lo; gi <= g_hi; gi++) nrec += tab->m[gi];
+        if (nrec > REC_CAP) {
+            if (tid == 0) atomicExch(a.status, FINCH_E_UNSUPPORTED);
+            nrec = REC_CAP;
+        }
+        auto pair_of = [&](int q) {   // q-th record of the CTA -> its (token, k) pair
+            int gi = g_lo;
+            while (q >= tab->m[gi]) q -= tab->m[gi++];
+            return (int)tab->pairs[gi][q];
+        };
+        for (int it = warp; it < nrec * units; it += CW_B) {
+            const int q = it / units, u = it - q * units;
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(a.act + (size_t)pair_of(q) * K + u * 128) + lane);
+            *reinterpret_cast<float4 *>(xstage + q * K + u * 128 + lane * 4) = v;
+            float sum = (v.x + v.y) + (v.z + v.w), mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            float *hdr = reinterpret_cast<float *>(smem + L.rec + q * r3b + frag3_bytes(K));
+            if ((lane & 15) == 0) hdr[2 * u + (lane >> 4)] = sum;
+            if (lane == 0) umax[it] = mx;
+        }
+        bar_sync(1, CW_B * 32);
+        for (int it = warp; it < nrec * units; it += CW_B) {
+            const int q = it / units, u = it - q * units;
+            float m = 0.f;
+            for (int j = 0; j < units; j++) m = fmaxf(m, umax[q * units + j]);
+            int E = (int)(__float_as_uint(m) >> 23) + 1;
+            E = E < 30 ? 30 : (E > 230 ? 230 : E);
+            uint8_t *rec = smem + L.rec + q * r3b;
+            if (u == 0 && lane == 0) reinterpret_cast<float *>(rec + frag3_bytes(K))[K / 64] = __int_as_float(E);
+            build_frag3_range(xstage + q * K + u * 128, 128, E, reinterpret_cast<uint2 *>(rec) + u * 72, lane, 32);
+        }
         if (a.has_shared && job1 > n_routed && job1 > job0)
-            for (int b = 0; b < a.B; b++, q++)
-                if (q % CW_B == warp) warp_make_record<4>(a.shared_act + (size_t)b * Ks, Ks, smem + L.srec + b * r4b, xstage);
+            for (int b = warp; b < a.B; b += CW_B) warp_make_record<4>(a.shared_act + (size_t)b * Ks, Ks, smem + L.srec + b * r4b);
     }
     bar_sync(1, CW_B * 32);
     const long long tk2 = clock64();
