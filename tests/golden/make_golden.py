@@ -12,14 +12,16 @@ Sources of truth executed here:
   * gguf-py (the ``gguf`` package of llama.cpp, version recorded in the file)
     for the Q4_K / Q6_K block decoders: gguf.quants.dequantize.
 
-Usage: python tests/golden/make_golden.py [/path/to/reference]
+Usage: python tests/golden/make_golden.py /path/to/reference/checkout
 """
 import os
 import sys
 
 import numpy as np
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+if len(sys.argv) < 2:
+    sys.exit(__doc__)
+REF = sys.argv[1]
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(REF, "finchmoe"))
 sys.path.insert(0, os.path.join(REF, "finchmoe", "finchTool", "tools"))
