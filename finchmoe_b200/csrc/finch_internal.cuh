@@ -36,7 +36,6 @@ struct finch_ctx {
         void *tiles;
     };
     std::vector<SharedPrepared> shared_cache;  // tiled copies of the shared experts seen so far
-    int force_prep = -1;            // test hook: -1 auto, 0 never, 1 always run the prep kernel
     // staging for the host-pointer entry points
     void *stage_dev = nullptr;
     void *stage_host = nullptr;     // pinned

@@ -1305,14 +1305,6 @@ extern "C" int finch_profile_read(finch_ctx *ctx, float *ms_gateup, float *ms_do
 }
 
 // Kept for binary compatibility of the test hook: the preparation kernel now always runs.
-extern "C" int finch_debug_force_prep(finch_ctx *ctx, int mode) {
-    if (!ctx || mode < -1 || mode > 1) return FINCH_E_ARG;
-    ctx->force_prep = mode;
-    return FINCH_OK;
-}
-
-// Diagnostics: when buf (device memory, 2048 x 8 int64) is non-NULL, the CTAs of the two streaming
-// kernels store the cycles they spent in each phase there.  NULL switches it off.
 extern "C" int finch_debug_timing(finch_ctx *ctx, void *buf) {
     if (!ctx) return FINCH_E_ARG;
     ctx->dbg = buf;

@@ -92,7 +92,6 @@ _PROTOS = {
     "finch_device_status": (_i, [_vp, C.POINTER(_i)]),
     "finch_debug_dequant": (_i, [_vp, C.POINTER(WDesc), _vp, _vp, _vp, _i]),
     "finch_launch_count": (C.c_uint64, [_vp]),
-    "finch_debug_force_prep": (_i, [_vp, _i]),
     "finch_debug_timing": (_i, [_vp, _vp]),
     "finch_profile_enable": (_i, [_vp, _i]),
     "finch_profile_read": (_i, [_vp, C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(_i)]),

@@ -311,15 +311,10 @@ FINCH_API int finch_encode_ep_combine(finch_ctx *ctx, finch_stream stream, float
  * finch_pool_fill_synthetic gives them in a full pool; the pool needs n_layers * (e1 - e0) slots. */
 FINCH_API int finch_pool_fill_synthetic_range(finch_pool *pool, int layer0, int layer1, int e0, int e1, uint64_t seed);
 
-/* Test hook for finch_encode_moe_decode: it normally decides by the batch size
- * whether a preparation kernel builds the activation operands once per token
- * (mode -1); 0 forces the build inside every CTA, 1 forces the preparation
- * kernel.  Results are identical.  No counterpart in the reference. */
-FINCH_API int finch_debug_force_prep(finch_ctx *ctx, int mode);
-/* Diagnostics: with a non-NULL device buffer of 8 int64 per SM, every CTA of the
- * gate/up kernel of finch_encode_moe_decode records the clock cycles of its
- * phases there (setup, operand records, item loop, time waiting for weights,
- * fence, arrivals, items, records made).  NULL switches it off. */
+/* Diagnostics: with a non-NULL device buffer of 2048 rows of 8 int64, the kernels of
+ * finch_encode_moe_decode record per-CTA clock-cycle and global-timer stamps of their phases
+ * there (rows 0.. gate/up, 1024.. down, 1300.. preparation, 1400.. combine).  NULL switches it
+ * off.  No counterpart in the reference. */
 FINCH_API int finch_debug_timing(finch_ctx *ctx, void *device_buf);
 
 /* Count of kernels launched by this context since creation (benchmark bookkeeping). */

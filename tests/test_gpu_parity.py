@@ -200,9 +200,8 @@ def test_moe_decode_small_vs_oracle(api, sd, ad, B):
 
 
 @pytest.mark.parametrize("B", [1, 2, 5, 8])
-def test_moe_decode_prep_and_inline_paths_agree(api, B):
-    """The operand fragments are built either inside every CTA or once by the
-    preparation kernel; the two must give bit-identical outputs, and both match the oracle."""
+def test_moe_decode_is_deterministic_run_to_run(api, B):
+    """No atomics on floats and fixed summation orders: repeated calls give bit-identical outputs, and they match the oracle."""
     ctx, pool, blocks, cfg, rng = _mk_small(api, L.FP16, L.BF16, seed=40 + B)
     try:
         x = synth.activations(rng, B, 256)
@@ -210,14 +209,11 @@ def test_moe_decode_prep_and_inline_paths_agree(api, B):
         sh = synth.shared_expert(rng, 256, 128, 64, 4, L.FP16)
         shd = ctx.make_shared(*[ctx.upload_tensor(t) for t in sh])
         score = rng.normal(0, 1, size=B).astype(np.float32)
-        outs = []
-        for mode in (0, 1, -1):
-            ctx.check(ctx.lib.finch_debug_force_prep(ctx.h, mode))
-            outs.append(ctx.moe_forward_host(pool, 1, x, ids, w, shared=shd, gate_score=score))
+        outs = [ctx.moe_forward_host(pool, 1, x, ids, w, shared=shd, gate_score=score) for _ in range(3)]
         assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
         assert np.array_equal(outs[0].view(np.uint32), outs[2].view(np.uint32))
         want = _oracle_layer(blocks, ids, w, None, x, cfg, shared=sh, score=score)
-        assert_close(outs[0], want, f"prep/inline B={B}")
+        assert_close(outs[0], want, f"repeat B={B}")
         assert ctx.device_status() == 0
     finally:
         pool.destroy()
