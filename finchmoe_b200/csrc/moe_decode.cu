@@ -123,6 +123,16 @@ __device__ __forceinline__ void extract3(uint32_t w0, uint32_t w1, uint32_t w2, 
     e[15] = v5 & 0x001C0007u; e[16] = v5 & 0x00E00038u; e[17] = v5 & 0x000001C0u;
 }
 
+// The same extraction, one register at a time (k = 0..17, compile-time): lets the matvec loop form the four A
+// registers of an MMA right before issuing it, which keeps few of them alive at once.
+template <int k>
+__device__ __forceinline__ uint32_t extract3_one(uint32_t w0, uint32_t v1, uint32_t w1, uint32_t v3, uint32_t w2, uint32_t v5) {
+    constexpr uint32_t M0[3] = {0x001C0007u, 0x00E00038u, 0x000001C0u}, M1[3] = {0x0007000Eu, 0x00380070u, 0x01C00380u},
+                       M2[3] = {0x000E001Cu, 0x007000E0u, 0x03800000u};
+    constexpr int grp = k / 3, i = k % 3;
+    return grp == 0 ? (w0 & M0[i]) : grp == 1 ? (v1 & M1[i]) : grp == 2 ? (w1 & M1[i]) : grp == 3 ? (v3 & M2[i]) : grp == 4 ? (w2 & M2[i]) : (v5 & M0[i]);
+}
+
 // One u32 of eight nibbles -> four registers: (0,4) (1,5) at p = 0 / 4 of the
 // word itself, (2,6) (3,7) at p = 0 / 4 of the word shifted right by 8.
 __device__ __forceinline__ void extract4(uint32_t w, uint32_t (&e)[4]) {
@@ -387,15 +397,21 @@ __device__ __forceinline__ void gemv3_tile(const uint8_t *tile, int units, int u
         pw += (uint32_t)ustep * 768u;
         ps += (uint32_t)ustep * 128u;
         ph += (uint32_t)ustep * 8u;
-        uint32_t ea[18], eb[18];
-        extract3(q0.x, q0.y, q1.x, ea);
-        extract3(q1.y, q2.x, q2.y, eb);
+        // row A words q0.x q0.y q1.x, row B words q1.y q2.x q2.y; the shifted views of extract3
+        const uint32_t av1 = __funnelshift_r(q0.x, q0.y, 8), av3 = __funnelshift_r(q0.y, q1.x, 8), av5 = q1.x >> 8;
+        const uint32_t bv1 = __funnelshift_r(q1.y, q2.x, 8), bv3 = __funnelshift_r(q2.x, q2.y, 8), bv5 = q2.y >> 8;
         float acc[2][4];  // two independent accumulator chains
-#pragma unroll
-        for (int j = 0; j < 9; j++) {
-            if (j < 2) mma16816_z(acc[j], ea[2 * j], eb[2 * j], ea[2 * j + 1], eb[2 * j + 1], b[j].x, b[j].y);
-            else finch_mma16816(acc[j & 1], ea[2 * j], eb[2 * j], ea[2 * j + 1], eb[2 * j + 1], b[j].x, b[j].y);
-        }
+#define FINCH_MMA3(j)                                                                                                     \
+    {                                                                                                                     \
+        const uint32_t a0 = extract3_one<2 * (j)>(q0.x, av1, q0.y, av3, q1.x, av5);                                       \
+        const uint32_t a1 = extract3_one<2 * (j)>(q1.y, bv1, q2.x, bv3, q2.y, bv5);                                       \
+        const uint32_t a2 = extract3_one<2 * (j) + 1>(q0.x, av1, q0.y, av3, q1.x, av5);                                   \
+        const uint32_t a3 = extract3_one<2 * (j) + 1>(q1.y, bv1, q2.x, bv3, q2.y, bv5);                                   \
+        if ((j) < 2) mma16816_z(acc[(j) & 1], a0, a1, a2, a3, b[j].x, b[j].y);                                            \
+        else finch_mma16816(acc[(j) & 1], a0, a1, a2, a3, b[j].x, b[j].y);                                                \
+    }
+        FINCH_MMA3(0) FINCH_MMA3(1) FINCH_MMA3(2) FINCH_MMA3(3) FINCH_MMA3(4) FINCH_MMA3(5) FINCH_MMA3(6) FINCH_MMA3(7) FINCH_MMA3(8)
+#undef FINCH_MMA3
         float s0, s1;
         finch_widen16x2(s.x, scale_dtype, s0, s1);
         runA = fmaf(s0, acc[0][0] + acc[1][0], runA);
