@@ -330,52 +330,21 @@ def run_ours(args):
     stack = Stack(local_rank, max_tokens=512, layers=LAYERS)
     n_sets = 4
     rsets = [[(ids, w) for ids, w in rs] for rs in routing_sets(batch, n_sets)]
-    if world > 1:  # a different token batch per rank
-        rsets = [[synth.zipf_routing(synth.rng_for(2, l, 100 + s + 1000 * rank), batch, NEXP, TOPK) for l in range(LAYERS)]
-                 for s in range(n_sets)]
     dev, xd, score, out, x = stack.device_inputs(rsets, batch)
 
-    def barrier():
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
-
-    sampler = ClockSampler(local_rank) if rank == 0 else None
-    n0 = stack.ctx.launch_count()
-    secs = stack.time_steps(dev, xd, score, out, batch, args.steps, args.warmup, barrier if world > 1 else None,
-                            use_graph=not args.no_graph)
+    sampler = ClockSampler(local_rank)
+    secs = stack.time_steps(dev, xd, score, out, batch, args.steps, args.warmup, None, use_graph=not args.no_graph)
     launches = 4 * LAYERS * args.steps  # four kernels per layer call (graph replays launch them without the host counter)
-    del n0
-    clocks = sampler.stop() if sampler else None
-    if world > 1:
-        import torch.distributed as dist
-        t = torch.tensor([secs], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        secs = float(t.item())
+    clocks = sampler.stop()
     step_bytes = [sum(alg_bytes(ids) for ids, _ in rs) for rs in rsets]
     timed_bytes = sum(step_bytes[(args.warmup + i) % n_sets] for i in range(args.steps))
-    if world > 1:
-        import torch.distributed as dist
-        t = torch.tensor([float(timed_bytes)], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        timed_bytes = float(t.item())
     value = timed_bytes / secs / 1e9
 
     # end to end through the host-pointer entry point
-    e2e_secs, h2d, d2h = stack.time_e2e(rsets, x, batch, args.steps, max(1, args.warmup // 2))
-    if world > 1:
-        import torch.distributed as dist
-        t = torch.tensor([e2e_secs], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_secs = float(t.item())
-    e2e_value = timed_bytes / e2e_secs / 1e9
-
-    if rank != 0:
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
-            dist.destroy_process_group()
-        return
+    e2e_warm = max(1, args.warmup // 2)
+    e2e_secs, h2d, d2h = stack.time_e2e(rsets, x, batch, args.steps, e2e_warm)
+    e2e_bytes = sum(step_bytes[(e2e_warm + i) % n_sets] for i in range(args.steps))   # the routing sets its timed steps used
+    e2e_value = e2e_bytes / e2e_secs / 1e9
 
     peaks, peak_kind = measured_peaks()
     line = {
@@ -384,7 +353,7 @@ def run_ours(args):
         "dtype": "f32", "data": "synthetic",
         "config": {"workload": "C2: 40-layer 3-bit expert stack decode, batch 8, top-8 of 256, Zipf(1.1)", "batch": batch,
                    "layers": LAYERS, "hidden": HIDDEN, "moe_inter": INTER, "scale_dtype": "fp16", "act_dtype": "bf16",
-                   "pool_gb": LAYERS * NEXP * EXPERT_BYTES / 1e9, "parallelism": "1 GPU" if world == 1 else f"{world} replicas",
+                   "pool_gb": LAYERS * NEXP * EXPERT_BYTES / 1e9, "parallelism": "1 GPU",
                    "l2": "inputs larger than L2: every step streams >= 0.5 GB of a 14 GB pool; 4 routing sets rotate"},
         "clocks": clocks,
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -421,10 +390,6 @@ def run_ours(args):
         line["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port", "sample": what,
                                 "seconds": dt}
     print(json.dumps(line))
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-        dist.destroy_process_group()
 
 
 
