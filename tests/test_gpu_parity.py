@@ -478,3 +478,36 @@ def test_residual_norm_vs_oracle(api, ad):
                 assert np.allclose(got, want_post, rtol=tol, atol=1e-6)
     finally:
         ctx.destroy()
+
+
+@pytest.mark.parametrize("shape", ["all_same", "all_distinct", "one_hot_expert"])
+def test_moe_decode_extreme_routings_full_size(api, shape):
+    """Group sizes at their extremes, BASELINE shapes, batch 8: every token picks the same eight experts (eight groups of
+    eight pairs), all 64 pairs distinct (64 groups of one), and one expert shared by all tokens next to distinct ones."""
+    B = 8
+    ctx = api.Context(max_tokens=8, n_layers=1)
+    pool = ctx.pool(n_layers=1)
+    try:
+        rng = synth.rng_for(18, len(shape))
+        if shape == "all_same":
+            ids = np.tile(rng.permutation(256)[:8].astype(np.int32), (B, 1))
+        elif shape == "all_distinct":
+            ids = rng.permutation(256)[:64].astype(np.int32).reshape(B, 8)
+        else:
+            ids = rng.permutation(256)[:64].astype(np.int32).reshape(B, 8)
+            ids[:, 3] = ids[0, 3]
+        lg = rng.normal(0, 1, size=(B, 8))
+        w = np.exp(lg - lg.max(axis=1, keepdims=True))
+        w = (w / w.sum(axis=1, keepdims=True)).astype(np.float32)
+        blocks = {}
+        for e in sorted(set(ids.ravel().tolist())):
+            blocks[e] = synth.expert_block(rng, scale_dtype=L.FP16)
+            pool.put(0, e, blocks[e])
+        x = synth.activations(rng, B, 2048)
+        out = ctx.moe_forward_host(pool, 0, x, ids, w)
+        want = _oracle_layer(blocks, ids, w, None, x, dict(hidden=2048, inter=512, sd=L.FP16))
+        assert_close(out, want, f"routing {shape}")
+        assert ctx.device_status() == 0
+    finally:
+        pool.destroy()
+        ctx.destroy()
