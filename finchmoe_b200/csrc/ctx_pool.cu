@@ -77,11 +77,9 @@ extern "C" int finch_ctx_create(const finch_config *cfg, finch_ctx **out) {
     bool ok = cudaMalloc(&ctx->act, pairs * c.moe_inter * sizeof(float)) == cudaSuccess &&
               cudaMalloc(&ctx->shared_act, (size_t)c.max_tokens * sh_inter * sizeof(float)) == cudaSuccess &&
               cudaMalloc(&ctx->partial, (pairs + c.max_tokens) * c.hidden * sizeof(float)) == cudaSuccess &&
-              cudaMalloc(&ctx->counters, (c.hidden / 64 + 128) * sizeof(unsigned)) == cudaSuccess &&
               cudaMalloc(&ctx->dev_status, sizeof(int)) == cudaSuccess &&
               cudaMalloc(&ctx->frag_scratch, finch_decode_scratch_bytes(c)) == cudaSuccess;
     if (!ok) return bail(FINCH_E_NOMEM);
-    cudaMemset(ctx->counters, 0, (c.hidden / 64 + 128) * sizeof(unsigned));
     cudaMemset(ctx->dev_status, 0, sizeof(int));
     cudaMemset(ctx->partial, 0, (pairs + c.max_tokens) * c.hidden * sizeof(float));
     if (cudaDeviceSynchronize() != cudaSuccess) return bail(FINCH_E_CUDA);
@@ -96,7 +94,6 @@ extern "C" void finch_ctx_destroy(finch_ctx *ctx) {
     cudaFree(ctx->act);
     cudaFree(ctx->shared_act);
     cudaFree(ctx->partial);
-    cudaFree(ctx->counters);
     cudaFree(ctx->dev_status);
     cudaFree(ctx->frag_scratch);
     for (auto &e : ctx->shared_cache) cudaFree(e.tiles);

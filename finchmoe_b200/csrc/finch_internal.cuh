@@ -26,7 +26,6 @@ struct finch_ctx {
     float *act = nullptr;           // [max_pairs][moe_inter]   routed SwiGLU activations
     float *shared_act = nullptr;    // [max_tokens][shared_inter]
     float *partial = nullptr;       // [max_pairs + max_tokens][hidden] per-pair down outputs (+ shared rows)
-    unsigned *counters = nullptr;   // [hidden / 64 + 128] arrival counters, zero between calls
     int *dev_status = nullptr;      // sticky device status word
     void *frag_scratch = nullptr;   // tensor-core operand fragments + expert-group table (moe_decode.cu)
     void *dbg = nullptr;            // finch_debug_timing buffer

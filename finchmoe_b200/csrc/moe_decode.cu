@@ -546,7 +546,7 @@ __device__ void build_groups(const MoeArgs &a, GroupTab *T, int *sm_ids, unsigne
 // job = gi * per_group + tile for the routed experts, then the shared-expert
 // tiles.  Every CTA takes one contiguous range, balanced by cost (a job of a
 // group with m pairs costs ceil(m/2) passes).  Contiguous ranges keep the
-// groups a CTA touches few: few act records to prepare, few counters to bump.
+// groups a CTA touches few: few act records to prepare.
 __device__ __forceinline__ int npass_of(const GroupTab *tab, int gi) { return (tab->m[gi] + 1) >> 1; }
 
 // pre[gi] = passes of the groups before gi (32-bit: at most 64 groups x 4 passes).  The job whose
