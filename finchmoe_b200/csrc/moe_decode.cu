@@ -932,9 +932,13 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
     const int job0 = tab->range_b[blockIdx.x], job1 = tab->range_b[blockIdx.x + 1];
 
     if (warp == CW_B) {
-        if (lane == 0) {
-            for (int job = job0, it = 0; job < job1; ++job, ++it) {
-                const int st = it % S, use = it / S;
+        // Producer warp: lane s owns stage s and issues that stage's fills in order (a single thread cannot issue
+        // a 3.5 KB tile as fast as sixteen consumer warps use them up).  Per stage the order of fills and waits is
+        // the serial one, so a wait never sees a barrier more than one phase behind.
+        if (lane < S) {
+            const int st = lane;
+            for (int it = lane, use = 0; job0 + it < job1; it += S, ++use) {
+                const int job = job0 + it;
                 if (use > 0 && !finch_mbar_wait(empty + st, (use - 1) & 1)) {
                     atomicExch(a.status, FINCH_E_TIMEOUT);
                     return;
