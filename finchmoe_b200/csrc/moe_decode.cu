@@ -675,6 +675,21 @@ __global__ void shared_retile_kernel(SharedSrc S, int hidden, int inter, uint8_t
 
 // ============================ kernel A ====================================
 __host__ __device__ inline int up128(int x) { return (x + 127) & ~127; }
+// Stage s of a ring is used by whichever consumer the job order assigns, and the producer lanes of different
+// stages run independently, so a consumer can be ready for the n-th fill of a stage while the job of its
+// (n-1)-th fill is still in progress (or that fill has not even been issued).  An mbarrier cannot tell these
+// apart: a barrier one phase behind reports the awaited phase's parity as complete.  So every stage carries a
+// count of the jobs consumed from it, and a consumer waits for the barrier only once that count says the
+// previous fill has been used up.  Bounded like every other wait here.
+__device__ __forceinline__ bool wait_consumed(const int *cnt, int want) {
+    const volatile int *c = cnt;
+    for (unsigned i = 0; i < (1u << 22); ++i) {
+        if (*c >= want) return true;
+        __nanosleep(40);
+    }
+    return false;
+}
+
 struct SmemA {
     int stage, stg, rec, rx3, rec4, f4s, n4, red, qcnt, tab, zero, bar, total;
 };
@@ -691,7 +706,7 @@ __host__ __device__ inline SmemA smem_a_layout(int hidden, int inter, int sh_int
     L.n4 = has_shared ? (B < 2 ? B : 2) : 0;
     L.red = up128(L.rec4 + L.n4 * L.f4s);
     L.qcnt = L.red + stages * (MAXM / 2) * TEAM_A * 32 * 4;   // per stage: [pass][warp][32] partial sums
-    L.tab = L.qcnt + 32 * 4;
+    L.tab = L.qcnt + 64 * 4;                                  // + jobs consumed per stage
     L.zero = up128(L.tab + (int)sizeof(GroupTab));
     L.bar = L.zero + ZERO3_BYTES;
     L.total = L.bar + 2 * 32 * 8 + 16 + 16;
@@ -716,7 +731,7 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
     const int K = a.hidden, groups = K / 64, I = a.sh_inter;
     const int f4b = frag4_bytes(K);
 
-    if (tid < 32) reinterpret_cast<int *>(smem + L.qcnt)[tid] = 0;
+    if (tid < 64) reinterpret_cast<int *>(smem + L.qcnt)[tid] = 0;
     if (tid < ZERO3_BYTES / 4) reinterpret_cast<int *>(smem + L.zero)[tid] = 0;
     if (tid == 0) {
         empty[32] = 0ull;
@@ -753,7 +768,7 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
     const long long tk1 = clock64();
 
     if (warp == CW_A) {
-        // ---------------- producer warp: one bulk copy per job ----------------
+        // ---------------- producer warp: one bulk copy per job, issued in job order ----------------
         if (lane == 0) {
             for (int job = job0, it = 0; job < job1; ++job, ++it) {
                 const int st = it % S, use = it / S;
@@ -788,14 +803,13 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
     const long long tk2 = clock64();
     long long wait_acc = 0;
     int njobs = 0;
-    // A warp may only wait for the n-th fill of a stage once the (n-1)-th has landed (a barrier that has
-    // not completed a phase yet reports the phase before it as complete).  With at least as many stages
-    // as teams that holds by construction; a CTA with fewer stages lets its surplus teams sit out.
+    // a CTA with fewer stages than teams lets its surplus teams sit out
     const int nteam = NTEAM_A < S ? NTEAM_A : S;
+    int *cons = qcnt + 32;
     for (int it = team; team < nteam && job0 + it < job1; it += nteam, ++njobs) {
         const int job = job0 + it, st = it % S, use = it / S;
         const long long w0 = clock64();
-        if (!finch_mbar_wait(full + st, use & 1)) {
+        if (!wait_consumed(cons + st, use) || !finch_mbar_wait(full + st, use & 1)) {
             if (lane == 0) atomicExch(a.status, FINCH_E_TIMEOUT);
             return;
         }
@@ -855,11 +869,16 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
                     else if (gg < 4) a.shared_act[(size_t)(2 * ps + ts) * I + 4 * ta + gg] = r;
                 }
             }
-            if (lane == 0) qcnt[st] = 0;
+            if (lane == 0) {
+                qcnt[st] = 0;
+                __threadfence_block();
+                *reinterpret_cast<volatile int *>(cons + st) = use + 1;
+            }
             __syncwarp();
         }
         if (lane == 0) mbar_arrive(empty + st);
     }
+    if (a.dbg && lane == 0) atomicMax(reinterpret_cast<unsigned long long *>(a.dbg + (size_t)blockIdx.x * 8 + 5), (unsigned long long)gtime());
     if (a.dbg && tid == 0) {
         long long *d = a.dbg + (size_t)blockIdx.x * 8;
         d[0] = tk1 - tk0;           // table + barriers
@@ -867,7 +886,6 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
         d[2] = clock64() - tk2;     // job loop of team 0
         d[3] = wait_acc;            // ... of which waiting for a full stage
         d[4] = gt0;
-        d[5] = gtime();
         d[6] = njobs;
         d[7] = job1 - job0;
     }
@@ -890,7 +908,7 @@ __host__ __device__ inline SmemB smem_b_layout(int hidden, int inter, int sh_int
     L.tab = up128(L.umax + REC_CAP * (inter / 128) * 4);
     L.zero = up128(L.tab + (int)sizeof(GroupTab));
     L.bar = L.zero + ZERO3_BYTES;
-    L.total = L.bar + 2 * 32 * 8 + 16;
+    L.total = L.bar + 2 * 32 * 8 + 16 + 32 * 4;              // barriers, 16 zero bytes, jobs consumed per stage
     return L;
 }
 
@@ -917,6 +935,8 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
         }
     }
     if (tid < ZERO3_BYTES / 4) reinterpret_cast<int *>(smem + L.zero)[tid] = 0;
+    int *cons = reinterpret_cast<int *>(smem + L.bar + 2 * 32 * 8 + 16);
+    if (tid < 32) cons[tid] = 0;
     grid_dep_launch();
     // The group table and the job ranges are the preparation kernel's output: that grid completed before the
     // gate/up kernel started, so they can be read, and the weight tiles streamed, while the gate/up kernel
@@ -934,7 +954,7 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
     if (warp == CW_B) {
         // Producer warp: lane s owns stage s and issues that stage's fills in order (a single thread cannot issue
         // a 3.5 KB tile as fast as sixteen consumer warps use them up).  Per stage the order of fills and waits is
-        // the serial one, so a wait never sees a barrier more than one phase behind.
+        // the serial one, so the producer's waits never see a barrier more than one phase behind.
         if (lane < S) {
             const int st = lane;
             for (int it = lane, use = 0; job0 + it < job1; it += S, ++use) {
@@ -959,6 +979,7 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
 
     // ---------------- consumer warps ----------------
     grid_dep_wait();   // the gate/up kernel has completed: act / shared_act are final
+    const long long tkw = clock64();
     // operand records of the activations this CTA needs: the pairs of the groups in its job range
     // (and every token's shared activations if it has shared-expert jobs)
     const int g_lo = job0 < n_routed ? job0 / T.nTB : ng;
@@ -1014,7 +1035,7 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
     for (int it = warp; job0 + it < job1; it += CW_B, ++njobs) {
         const int job = job0 + it, st = it % S, use = it / S;
         const long long w0 = clock64();
-        if (!finch_mbar_wait(full + st, use & 1)) {
+        if (!wait_consumed(cons + st, use) || !finch_mbar_wait(full + st, use & 1)) {
             if (lane == 0) atomicExch(a.status, FINCH_E_TIMEOUT);
             break;
         }
@@ -1057,20 +1078,23 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty + st);
+        if (lane == 0) {
+            *reinterpret_cast<volatile int *>(cons + st) = use + 1;
+            mbar_arrive(empty + st);
+        }
         (void)tb;
     }
 
     const long long tk3 = clock64();
+    if (a.dbg && lane == 0) atomicMax(reinterpret_cast<unsigned long long *>(a.dbg + (size_t)(1024 + blockIdx.x) * 8 + 5), (unsigned long long)gtime());
     if (a.dbg && tid == 0) {
         long long *d = a.dbg + (size_t)(1024 + blockIdx.x) * 8;
         d[0] = tk1 - tk0;   // table + barriers
-        d[1] = tk2 - tk1;   // act records
+        d[1] = tk2 - tkw;   // act records
         d[2] = tk3 - tk2;   // job loop of warp 0
         d[3] = wait_acc;    // ... of which waiting for a full stage
         d[4] = gt0;
-        d[5] = gtime();
-        d[6] = njobs;
+        d[6] = tkw - tk1;   // waiting for the gate/up kernel
         d[7] = job1 - job0;
     }
 }
