@@ -414,10 +414,48 @@ def run_ep(args, rank, local_rank, world):
     backend = ep.GpuBackend(stack.ctx, stack.pool, batch * world)
     shared = [stack.ctx.make_shared(*stack.shared[l], gate_score=score) for l in range(LAYERS)]
 
-    def step(i, xin=None):
-        ids, w = dev[i % n_sets]
+    # Decode batches are small and the same size on every rank: the fixed-capacity exchange (every token to
+    # every rank, known message sizes) needs no row counts and no host synchronisation, so a whole step is a
+    # fixed sequence of launches and all-to-alls, recorded once per routing set into a CUDA graph.
+    def layers_of(s):
+        ids, w = dev[s]
         for l in range(LAYERS):
-            ep.ep_layer(backend, dist, None, l, xd if xin is None else xin, ids[l], w[l], None, shared[l], None, out[l])
+            ep.ep_layer_static(backend, dist, None, l, xd, ids[l], w[l], None, shared[l], None, out[l], in_scope=True)
+
+    def step_eager(i):
+        with backend.stream_scope():
+            layers_of(i % n_sets)
+
+    graphs, graph_note = None, "launched from the host every step"
+    if not args.no_graph:
+        try:
+            for s in range(n_sets):          # communicators, lazily made buffers and tables exist before capture
+                step_eager(s)
+            torch.cuda.synchronize()
+            dist.barrier()
+            graphs = []
+            for s in range(n_sets):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=backend.stream, capture_error_mode="thread_local"):
+                    layers_of(s)
+                graphs.append(g)
+            torch.cuda.synchronize()
+            graph_note = "one CUDA graph per routing set (kernels and all-to-alls)"
+        except Exception as e:               # capture of the collectives unavailable: keep launching from the host
+            graphs = None
+            graph_note = "launched from the host every step (graph capture failed: %s)" % (str(e).splitlines()[0][:120] if str(e) else type(e).__name__)
+            torch.cuda.synchronize()
+    # every rank must take the same path: a rank that replays graphs cannot pair with one that launches eagerly
+    flag = torch.tensor([1 if graphs is not None else 0], device="cuda")
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    if int(flag.item()) == 0:
+        graphs = None
+
+    def step(i):
+        if graphs is not None:
+            graphs[i % n_sets].replay()
+        else:
+            step_eager(i)
 
     def timed(n, w0, fn):
         for i in range(w0):
@@ -444,8 +482,8 @@ def run_ep(args, rank, local_rank, world):
     res = torch.empty((batch, HIDDEN), dtype=torch.float32).pin_memory()
 
     def step_e2e(i):
-        xin = xh.to("cuda", non_blocking=True).view(torch.bfloat16)
-        step(i, xin)
+        xd.view(torch.int16).copy_(xh, non_blocking=True)
+        step(i)
         res.copy_(out[LAYERS - 1], non_blocking=True)
         torch.cuda.current_stream().synchronize()
     e2e_secs = timed(args.steps, max(1, args.warmup // 2), step_e2e)
@@ -463,7 +501,6 @@ def run_ep(args, rank, local_rank, world):
     if rank == 0:
         peaks, peak_kind = measured_peaks()
         value = timed_bytes / secs / 1e9
-        rows_per_layer = None
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -471,7 +508,8 @@ def run_ep(args, rank, local_rank, world):
             "config": {"workload": "C5: expert-parallel batched decode, 40 layers, 8 tokens per GPU per step, top-8 of 256, Zipf(1.1)",
                        "batch": batch * world, "layers": LAYERS, "hidden": HIDDEN, "moe_inter": INTER, "scale_dtype": "fp16",
                        "act_dtype": "bf16", "experts_per_gpu": per, "parallelism": f"ep{world}",
-                       "exchange": "3 all-to-alls per layer over NCCL (row counts, records, partial rows); one host sync per layer",
+                       "exchange": "fixed capacity: 2 all-to-alls per layer over NCCL (records, partial rows), no host synchronisation",
+                       "launch": graph_note,
                        "l2": "inputs larger than L2: the pool shards exceed it; 4 routing sets rotate"},
             "clocks": clocks,
             "e2e": {"value": e2e_bytes / e2e_secs / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(xh.numel() * 2 * world),
@@ -481,10 +519,16 @@ def run_ep(args, rank, local_rank, world):
             "us_per_layer": secs / args.steps / LAYERS * 1e6,
             "hbm_frac_of_" + peak_kind: value / world / peaks["hbm_gbs"],
         }
-        del rows_per_layer
-        print(json.dumps(line))
+        print(json.dumps(line), flush=True)
+    # The graphs hold the recorded all-to-alls: they go before the communicator does, and the process then
+    # leaves without tearing NCCL down (a communicator destroyed after graphs had captured its collectives did
+    # not return on this stack).
+    graphs = None
+    torch.cuda.synchronize()
     dist.barrier()
-    dist.destroy_process_group()
+    sys.stdout.flush()
+    sys.stderr.flush()
+    os._exit(0)
 
 
 def aux_rooflines(stack, peaks, peak_kind, iters=8):

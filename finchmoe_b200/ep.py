@@ -89,6 +89,53 @@ def _ep_layer(backend, dist, group, layer, x, ids, weights, valid, shared, h_mid
     return out
 
 
+def static_plan_numpy(T: int, world: int):
+    """The plan of the fixed-capacity exchange: every token goes to every rank, in token order.  Same
+    four arrays as plan_numpy."""
+    counts = np.full(world, T, np.int32)
+    offs = (np.arange(world + 1, dtype=np.int32) * T).astype(np.int32)
+    send_tok = np.tile(np.arange(T, dtype=np.int32), world)
+    slot_of = np.repeat(np.arange(T, dtype=np.int32)[:, None], world, axis=1)
+    return counts, offs, send_tok, slot_of
+
+
+def ep_layer_static(backend, dist, group, layer: int, x, ids, weights, valid, shared, h_mid, out, in_scope=False):
+    """The same layer with a fixed-capacity exchange: every rank owns the same number of tokens T and sends
+    each of them to every rank, so all message sizes are known beforehand.  No row counts are exchanged and
+    the host never waits for the device: the whole layer is a fixed sequence of launches and two
+    all-to-alls with equal splits, which can also be recorded into a CUDA graph (in_scope=True: the caller
+    has already made the backend's stream current, as a graph capture does).  A rank skips the experts
+    it does not hold, so rows that have no expert there cost it no weight traffic and come back as zeros.
+    Meant for decode-sized batches, where the rows are few and latency is what matters; the planned
+    exchange (ep_layer) sends less when batches are large."""
+    if in_scope:
+        return _ep_layer_static(backend, dist, group, layer, x, ids, weights, valid, shared, h_mid, out)
+    with backend.stream_scope():
+        return _ep_layer_static(backend, dist, group, layer, x, ids, weights, valid, shared, h_mid, out)
+
+
+def _ep_layer_static(backend, dist, group, layer, x, ids, weights, valid, shared, h_mid, out):
+    world = dist.get_world_size(group) if dist is not None else 1
+    T = ids.shape[0]
+    h = backend.static_plan(T, world)
+    rec, H, n = backend.record_bytes(), backend.hidden, T * world
+    send_buf = backend.pack(h, x, ids, weights, valid, n)
+    if world > 1:
+        recv_buf = backend.empty_bytes(n * rec)
+        dist.all_to_all_single(recv_buf, send_buf, group=group)       # equal splits: T records per peer
+    else:
+        recv_buf = send_buf
+    part = backend.local_moe(layer, recv_buf, n)                       # fp32 [n, H], source-major
+    if world > 1:
+        back = backend.empty_f32(n * H)
+        dist.all_to_all_single(back, part.reshape(-1), group=group)
+    else:
+        back = part.reshape(-1)
+    backend.base(layer, x, ids, weights, shared, h_mid, out)
+    backend.combine(h, out, back)
+    return out
+
+
 class _Plan:
     pass
 
@@ -111,6 +158,7 @@ class GpuBackend:
         self.rv = torch.empty((max_rows, self.K), dtype=torch.uint8, device=dev)
         self.rout = torch.empty((max_rows, self.hidden), dtype=torch.float32, device=dev)
         self.zero_valid = None
+        self._static = {}
 
         self.stream = torch.cuda.Stream(device=dev)   # kernels, copies and collectives of a layer are ordered on it
 
@@ -154,6 +202,21 @@ class GpuBackend:
                                                      T, world, p.counts.data_ptr(), p.offs.data_ptr(), p.send_tok.data_ptr(),
                                                      p.slot_of.data_ptr()))
         return p
+
+    def static_plan(self, T, world):
+        """Device copy of static_plan_numpy, made once per (T, world)."""
+        torch = self.torch
+        key = (T, world)
+        if key not in self._static:
+            counts, offs, send_tok, slot_of = static_plan_numpy(T, world)
+            p = _Plan()
+            p.T, p.world = T, world
+            p.counts = torch.from_numpy(counts).to(self.dev)
+            p.offs = torch.from_numpy(offs).to(self.dev)
+            p.send_tok = torch.from_numpy(send_tok).to(self.dev)
+            p.slot_of = torch.from_numpy(np.ascontiguousarray(slot_of)).to(self.dev)
+            self._static[key] = p
+        return self._static[key]
 
     def pack(self, p, x, ids, weights, valid, n_rows):
         buf = self.empty_bytes(n_rows * self.record_bytes())

@@ -38,6 +38,13 @@ class NumpyBackend:
         p.counts, p.offs, p.send_tok, p.slot_of = torch.from_numpy(counts), offs, send_tok, slot_of
         return p
 
+    def static_plan(self, T, world):
+        p = _Plan()
+        p.world = world
+        counts, p.offs, p.send_tok, p.slot_of = ep.static_plan_numpy(T, world)
+        p.counts = torch.from_numpy(counts)
+        return p
+
     def pack(self, p, x, ids, weights, valid, n_rows):
         rec, H, K = self.record_bytes(), self.hidden, self.K
         buf = np.zeros((n_rows, rec), np.uint8)

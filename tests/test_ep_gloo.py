@@ -40,6 +40,8 @@ rng = synth.rng_for(9, 1)                          # both ranks draw the same mo
 blocks = {e: synth.expert_block(rng, 256, 128, 64, 3, cfg["sd"]) for e in range(8)}
 shared = synth.shared_expert(rng, 256, 128, 64, 4, cfg["sd"])
 T = (5, 7)[rank]                                   # ragged: the ranks own different numbers of tokens
+if sys.argv[4] == "static":
+    T = 6                                          # the fixed-capacity exchange wants the same count everywhere
 r2 = synth.rng_for(9, 2, rank)
 x = r2.normal(0, 1, size=(T, 256)).astype(np.float32)
 ids, w = synth.zipf_routing(r2, T, 8, 4)
@@ -53,8 +55,9 @@ h_mid = r2.normal(0, 1, size=(T, 256)).astype(np.float32)
 per = 8 // world
 backend = NumpyBackend(cfg, {e: b for e, b in blocks.items() if e // per == rank}, shared)
 out = torch.empty((T, 256), dtype=torch.float32)
-ep.ep_layer(backend, dist, None, 0, torch.from_numpy(x), torch.from_numpy(ids), torch.from_numpy(w), torch.from_numpy(valid),
-            score, torch.from_numpy(h_mid), out)
+layer_fn = ep.ep_layer_static if sys.argv[4] == "static" else ep.ep_layer
+layer_fn(backend, dist, None, 0, torch.from_numpy(x), torch.from_numpy(ids), torch.from_numpy(w), torch.from_numpy(valid),
+         score, torch.from_numpy(h_mid), out)
 want = np.stack([oracle.moe_layer([blocks[int(e)] if valid[t, k] else None for k, e in enumerate(ids[t])], w[t], valid[t], x[t], bits=3,
                                   scale_dtype=cfg["sd"], hidden=256, inter=128, h_mid=h_mid[t], shared=shared,
                                   shared_gate_score=float(score[t])) for t in range(T)])
@@ -69,11 +72,11 @@ print("rank", rank, "ok", err)
 import pytest
 
 
-@pytest.mark.parametrize("mode", ["mixed", "one_sided"])
+@pytest.mark.parametrize("mode", ["mixed", "one_sided", "static"])
 def test_two_rank_layer_matches_single_process_oracle(tmp_path, mode):
     script = tmp_path / "ep_worker.py"
     script.write_text(WORKER)
-    port = str(29600 + (os.getpid() + (7 if mode == "mixed" else 13)) % 300)
+    port = str(29600 + (os.getpid() + {"mixed": 7, "one_sided": 13, "static": 19}[mode]) % 300)
     procs = [subprocess.Popen([sys.executable, str(script), str(r), port, HERE, mode], stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
              for r in range(2)]
     outs = [p.communicate(timeout=240)[0] for p in procs]

@@ -45,7 +45,8 @@ def test_device_plan_matches_host_mirror(world):
 
 
 @pytest.mark.parametrize("T", [5, 40, 200])
-def test_single_rank_protocol_matches_plain_layer(T):
+@pytest.mark.parametrize("static", [False, True])
+def test_single_rank_protocol_matches_plain_layer(T, static):
     import torch
     from finchmoe_b200 import api
     ctx = _ctx(api, max_tokens=256)
@@ -66,9 +67,9 @@ def test_single_rank_protocol_matches_plain_layer(T):
         want = ctx.moe_forward_host(pool, 0, x, ids, w, valid=valid, shared=shd, gate_score=score, h_mid=h_mid)
         be = ep.GpuBackend(ctx, pool, T)
         out = torch.empty((T, 256), dtype=torch.float32, device="cuda")
-        ep.ep_layer(be, None, None, 0, d(x), d(ids), d(w), d(valid), shd, d(h_mid), out)
+        (ep.ep_layer_static if static else ep.ep_layer)(be, None, None, 0, d(x), d(ids), d(w), d(valid), shd, d(h_mid), out)
         torch.cuda.synchronize()
-        assert_close(out.cpu().numpy(), want, f"single-rank protocol T={T}")
+        assert_close(out.cpu().numpy(), want, f"single-rank protocol T={T} static={static}")
         assert ctx.device_status() == 0
     finally:
         pool.destroy()
@@ -114,10 +115,28 @@ want = np.stack([oracle.moe_layer([blocks[int(e)] if valid[t, k] else None for k
                                   scale_dtype=oracle.SCALE_BF16, hidden=H, inter=I, h_mid=h_mid[t], shared=sh,
                                   shared_gate_score=float(score[t])) for t in range(T)])
 assert_close(out.cpu().numpy(), want, f"rank {rank}")
-assert ctx.device_status() == 0
+# fixed-capacity exchange (same token count on every rank), launched from the host and replayed from a CUDA graph
+Ts = 32
+args = (d(x[:Ts]), d(ids[:Ts]), d(w[:Ts]), d(valid[:Ts]), shd, d(h_mid[:Ts]), torch.zeros((Ts, H), dtype=torch.float32, device="cuda"))
+ep.ep_layer_static(be, dist, None, 0, *args)
+torch.cuda.synchronize()
+assert_close(args[-1].cpu().numpy(), want[:Ts], f"rank {rank} fixed capacity")
+args[-1].zero_()
+torch.cuda.synchronize()
 dist.barrier()
-dist.destroy_process_group()
-print("rank", rank, "ok")
+g = torch.cuda.CUDAGraph()
+with torch.cuda.graph(g, stream=be.stream, capture_error_mode="thread_local"):
+    ep.ep_layer_static(be, dist, None, 0, *args, in_scope=True)
+for rep in range(2):
+    g.replay()
+torch.cuda.synchronize()
+assert_close(args[-1].cpu().numpy(), want[:Ts], f"rank {rank} fixed capacity, graph replay")
+assert ctx.device_status() == 0
+del g                                   # the graph holds the recorded all-to-alls: it goes before the communicator
+torch.cuda.synchronize()
+dist.barrier()
+print("rank", rank, "ok", flush=True)
+os._exit(0)                             # leave without tearing NCCL down after a capture
 '''
 
 
