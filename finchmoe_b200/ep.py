@@ -89,13 +89,16 @@ def _ep_layer(backend, dist, group, layer, x, ids, weights, valid, shared, h_mid
     return out
 
 
-def static_plan_numpy(T: int, world: int):
+def static_plan_numpy(T: int, world: int, skip: int = -1):
     """The plan of the fixed-capacity exchange: every token goes to every rank, in token order.  Same
-    four arrays as plan_numpy."""
+    four arrays as plan_numpy.  skip: a rank whose returned rows the combine step leaves out (the home
+    rank, when it adds its own experts' share to the output directly)."""
     counts = np.full(world, T, np.int32)
     offs = (np.arange(world + 1, dtype=np.int32) * T).astype(np.int32)
     send_tok = np.tile(np.arange(T, dtype=np.int32), world)
     slot_of = np.repeat(np.arange(T, dtype=np.int32)[:, None], world, axis=1)
+    if skip >= 0:
+        slot_of[:, skip] = -1
     return counts, offs, send_tok, slot_of
 
 
@@ -116,22 +119,31 @@ def ep_layer_static(backend, dist, group, layer: int, x, ids, weights, valid, sh
 
 def _ep_layer_static(backend, dist, group, layer, x, ids, weights, valid, shared, h_mid, out):
     world = dist.get_world_size(group) if dist is not None else 1
+    rank = dist.get_rank(group) if dist is not None else 0
     T = ids.shape[0]
-    h = backend.static_plan(T, world)
+    # A backend that can run the home rank's own tokens straight from their buffers does so while the records
+    # are in flight: one pass gives h_mid + shared expert + the experts this rank holds, and the rows the rank
+    # would have sent to itself are neither processed a second time nor added again.
+    direct = world > 1 and getattr(backend, "home_direct", False)
+    h = backend.static_plan(T, world, rank if direct else -1)
     rec, H, n = backend.record_bytes(), backend.hidden, T * world
     send_buf = backend.pack(h, x, ids, weights, valid, n)
     if world > 1:
         recv_buf = backend.empty_bytes(n * rec)
-        dist.all_to_all_single(recv_buf, send_buf, group=group)       # equal splits: T records per peer
+        work = dist.all_to_all_single(recv_buf, send_buf, group=group, async_op=True)    # equal splits: T records per peer
+        if direct:
+            backend.home(layer, x, ids, weights, valid, shared, h_mid, out)
+        work.wait()
     else:
         recv_buf = send_buf
-    part = backend.local_moe(layer, recv_buf, n)                       # fp32 [n, H], source-major
+    part = backend.local_moe(layer, recv_buf, n, (rank * T, T) if direct else None)   # fp32 [n, H], source-major
     if world > 1:
         back = backend.empty_f32(n * H)
         dist.all_to_all_single(back, part.reshape(-1), group=group)
     else:
         back = part.reshape(-1)
-    backend.base(layer, x, ids, weights, shared, h_mid, out)
+    if not direct:
+        backend.base(layer, x, ids, weights, shared, h_mid, out)
     backend.combine(h, out, back)
     return out
 
@@ -203,12 +215,14 @@ class GpuBackend:
                                                      p.slot_of.data_ptr()))
         return p
 
-    def static_plan(self, T, world):
-        """Device copy of static_plan_numpy, made once per (T, world)."""
+    home_direct = True
+
+    def static_plan(self, T, world, skip=-1):
+        """Device copy of static_plan_numpy, made once per (T, world, skip)."""
         torch = self.torch
-        key = (T, world)
+        key = (T, world, skip)
         if key not in self._static:
-            counts, offs, send_tok, slot_of = static_plan_numpy(T, world)
+            counts, offs, send_tok, slot_of = static_plan_numpy(T, world, skip)
             p = _Plan()
             p.T, p.world = T, world
             p.counts = torch.from_numpy(counts).to(self.dev)
@@ -225,15 +239,32 @@ class GpuBackend:
                                                      p.send_tok.data_ptr(), buf.data_ptr()))
         return buf
 
-    def local_moe(self, layer, recv_buf, n):
+    def home(self, layer, x, ids, weights, valid, shared, h_mid, out):
+        """out = h_mid + shared expert + the experts of this rank's pool, for the rank's own tokens."""
+        T = ids.shape[0]
+        st = self._stream()
+        step = self.ctx.cfg.max_tokens
+        for t0 in range(0, T, step):
+            m = min(step, T - t0)
+            sh = None
+            if shared is not None:
+                from . import lib as L
+                sh = L.Shared(shared.gate, shared.up, shared.down, shared.gate_score + 4 * t0)
+            self.ctx.check(self.lib.finch_encode_moe_prefill(
+                self.ctx.h, st, self.pool.h, layer, x.data_ptr() + t0 * self.hidden * self.elt, ids[t0:].data_ptr(), weights[t0:].data_ptr(),
+                valid[t0:].data_ptr() if valid is not None else None, C.byref(sh) if sh is not None else None,
+                h_mid[t0:].data_ptr() if h_mid is not None else None, out[t0:].data_ptr(), m))
+
+    def local_moe(self, layer, recv_buf, n, skip=None):
+        """skip = (first row, rows): a block of received rows that is left out (its output rows are not written)."""
         if n > self.max_rows:
             raise ValueError(f"received {n} rows, backend sized for {self.max_rows}")
         st = self._stream()
         self.ctx.check(self.lib.finch_encode_ep_unpack(self.ctx.h, st, recv_buf.data_ptr(), n, self.rx.data_ptr(), self.rids.data_ptr(),
                                                        self.rw.data_ptr(), self.rv.data_ptr()))
         step = self.ctx.cfg.max_tokens
-        for r0 in range(0, n, step):
-            m = min(step, n - r0)
+        blocks = [(0, n)] if skip is None else [(0, skip[0]), (skip[0] + skip[1], n)]
+        for r0, m in ((r, min(step, hi - r)) for lo, hi in blocks for r in range(lo, hi, step)):
             self.ctx.check(self.lib.finch_encode_moe_prefill(
                 self.ctx.h, st, self.pool.h, layer, self.rx.data_ptr() + r0 * self.hidden * self.elt, self.rids[r0:].data_ptr(),
                 self.rw[r0:].data_ptr(), self.rv[r0:].data_ptr(), None, None, self.rout[r0:].data_ptr(), m))

@@ -38,10 +38,10 @@ class NumpyBackend:
         p.counts, p.offs, p.send_tok, p.slot_of = torch.from_numpy(counts), offs, send_tok, slot_of
         return p
 
-    def static_plan(self, T, world):
+    def static_plan(self, T, world, skip=-1):
         p = _Plan()
         p.world = world
-        counts, p.offs, p.send_tok, p.slot_of = ep.static_plan_numpy(T, world)
+        counts, p.offs, p.send_tok, p.slot_of = ep.static_plan_numpy(T, world, skip)
         p.counts = torch.from_numpy(counts)
         return p
 
@@ -57,7 +57,7 @@ class NumpyBackend:
             buf[i, H * 4 + 8 * K:H * 4 + 9 * K] = vn[t]
         return torch.from_numpy(buf.reshape(-1))
 
-    def local_moe(self, layer, recv_buf, n):
+    def local_moe(self, layer, recv_buf, n, skip=None):
         rec, H, K, c = self.record_bytes(), self.hidden, self.K, self.cfg
         buf = recv_buf.numpy().reshape(n, rec)
         out = np.zeros((n, H), np.float32)
