@@ -33,13 +33,13 @@ import numpy as np, torch, torch.distributed as dist
 from finchmoe_b200 import ep, synth
 from oracle import oracle
 from ep_cpu_backend import NumpyBackend
-rank, world = int(sys.argv[1]), 2
+rank, world = int(sys.argv[1]), int(sys.argv[5])
 dist.init_process_group("gloo", init_method="tcp://127.0.0.1:" + sys.argv[2], rank=rank, world_size=world)
 cfg = dict(hidden=256, inter=128, n_experts=8, K=4, sd=oracle.SCALE_BF16)
 rng = synth.rng_for(9, 1)                          # both ranks draw the same model
 blocks = {e: synth.expert_block(rng, 256, 128, 64, 3, cfg["sd"]) for e in range(8)}
 shared = synth.shared_expert(rng, 256, 128, 64, 4, cfg["sd"])
-T = (5, 7)[rank]                                   # ragged: the ranks own different numbers of tokens
+T = (5, 7, 3, 6)[rank]                             # ragged: the ranks own different numbers of tokens
 if sys.argv[4] == "static":
     T = 6                                          # the fixed-capacity exchange wants the same count everywhere
 r2 = synth.rng_for(9, 2, rank)
@@ -72,13 +72,13 @@ print("rank", rank, "ok", err)
 import pytest
 
 
-@pytest.mark.parametrize("mode", ["mixed", "one_sided", "static"])
-def test_two_rank_layer_matches_single_process_oracle(tmp_path, mode):
+@pytest.mark.parametrize("mode,world", [("mixed", 2), ("one_sided", 2), ("static", 2), ("mixed", 4), ("static", 4)])
+def test_ranks_match_single_process_oracle(tmp_path, mode, world):
     script = tmp_path / "ep_worker.py"
     script.write_text(WORKER)
-    port = str(29600 + (os.getpid() + {"mixed": 7, "one_sided": 13, "static": 19}[mode]) % 300)
-    procs = [subprocess.Popen([sys.executable, str(script), str(r), port, HERE, mode], stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
-             for r in range(2)]
+    port = str(29600 + (os.getpid() + {"mixed": 7, "one_sided": 13, "static": 19}[mode] + 31 * world) % 300)
+    procs = [subprocess.Popen([sys.executable, str(script), str(r), port, HERE, mode, str(world)], stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+                              text=True) for r in range(world)]
     outs = [p.communicate(timeout=240)[0] for p in procs]
     for r, (p, o) in enumerate(zip(procs, outs)):
         assert p.returncode == 0, f"rank {r} failed:\n{o[-3000:]}"
