@@ -299,11 +299,12 @@ class Stack:
         h2d = xw.nbytes + batch * TOPK * 8 + score.nbytes
         d2h = batch * HIDDEN * 4
 
+        shs = [self.ctx.make_shared(*self.shared[l]) for l in range(self.layers)]
+
         def step(rs):
             last = None
             for l in range(self.layers):
-                sh = self.ctx.make_shared(*self.shared[l])
-                last = self.ctx.moe_forward_host(self.pool, l, xw, rs[l][0], rs[l][1], shared=sh, gate_score=score)
+                last = self.ctx.moe_forward_host(self.pool, l, xw, rs[l][0], rs[l][1], shared=shs[l], gate_score=score)
             return last
         for i in range(warmup):
             step(rsets[i % len(rsets)])
@@ -341,7 +342,7 @@ def run_ours(args):
     value = timed_bytes / secs / 1e9
 
     # end to end through the host-pointer entry point
-    e2e_warm = max(1, args.warmup // 2)
+    e2e_warm = max(3, args.warmup)
     e2e_secs, h2d, d2h = stack.time_e2e(rsets, x, batch, args.steps, e2e_warm)
     e2e_bytes = sum(step_bytes[(e2e_warm + i) % n_sets] for i in range(args.steps))   # the routing sets its timed steps used
     e2e_value = e2e_bytes / e2e_secs / 1e9
@@ -486,7 +487,7 @@ def run_ep(args, rank, local_rank, world):
         step(i)
         res.copy_(out[LAYERS - 1], non_blocking=True)
         torch.cuda.current_stream().synchronize()
-    e2e_secs = timed(args.steps, max(1, args.warmup // 2), step_e2e)
+    e2e_secs = timed(args.steps, max(3, args.warmup), step_e2e)
 
     def step_bytes(s):
         total = 0
@@ -497,7 +498,7 @@ def run_ep(args, rank, local_rank, world):
             total += len(touched) * EXPERT_BYTES + world * SHARED_BYTES     # every rank reads its own copy of the shared expert
         return total
     timed_bytes = sum(step_bytes((args.warmup + i) % n_sets) for i in range(args.steps))
-    e2e_bytes = sum(step_bytes((max(1, args.warmup // 2) + i) % n_sets) for i in range(args.steps))
+    e2e_bytes = sum(step_bytes((max(3, args.warmup) + i) % n_sets) for i in range(args.steps))
     if rank == 0:
         peaks, peak_kind = measured_peaks()
         value = timed_bytes / secs / 1e9
