@@ -727,7 +727,7 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
     float *red = reinterpret_cast<float *>(smem + L.red);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar), *empty = full + 32;
     const uint2 *zero8 = reinterpret_cast<const uint2 *>(empty + 32);
-    uint64_t *xbar = empty + 34;
+    uint64_t *xbar = empty + 34, *xbar2 = empty + 35;
     const int K = a.hidden, groups = K / 64, I = a.sh_inter;
     const int f4b = frag4_bytes(K);
 
@@ -740,11 +740,18 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
             finch_mbar_init(empty + s, TEAM_A);
         }
         finch_mbar_init(xbar, 1);
+        finch_mbar_init(xbar2, 1);
     }
     grid_dep_wait();  // everything above overlaps the tail of the preparation kernel
     // only now may the down kernel be scheduled: it reads the preparation kernel's tables before its own wait,
     // and every CTA of this grid gets here only after the preparation kernel has completed
     grid_dep_launch();
+    if (tid == 0) {
+        // operand records of the tokens: one bulk copy each, under way while the group table is read
+        finch_mbar_expect_tx(xbar, (unsigned)(a.B * L.rx3 + L.n4 * f4b));
+        for (int b = 0; b < a.B; b++) finch_bulk_g2s(smem + L.rec + b * L.rx3, a.xrec3 + (size_t)b * L.rx3, L.rx3, xbar);
+        for (int b = 0; b < L.n4; b++) finch_bulk_g2s(smem + L.rec4 + b * L.f4s, a.xrec4 + (size_t)b * f4b, f4b, xbar);
+    }
     {
         const int *s = reinterpret_cast<const int *>(a.gtab);
         int *d = reinterpret_cast<int *>(tab);
@@ -757,12 +764,10 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
     const int n4x = (a.has_shared && job1 > n_routed && job1 > job0) ? a.B - L.n4 : 0;   // tokens beyond the fixed area
     const int tail_off = L.stage + Smax * L.stg - n4x * L.f4s;
     const int S = (Smax * L.stg - n4x * L.f4s) / L.stg;
-    if (tid == 0) {
-        // operand records of the tokens: one bulk copy each, ready long before the first tile is
-        finch_mbar_expect_tx(xbar, (unsigned)(a.B * L.rx3 + (L.n4 + n4x) * f4b));
-        for (int b = 0; b < a.B; b++) finch_bulk_g2s(smem + L.rec + b * L.rx3, a.xrec3 + (size_t)b * L.rx3, L.rx3, xbar);
-        for (int b = 0; b < L.n4; b++) finch_bulk_g2s(smem + L.rec4 + b * L.f4s, a.xrec4 + (size_t)b * f4b, f4b, xbar);
-        for (int b = 0; b < n4x; b++) finch_bulk_g2s(smem + tail_off + b * L.f4s, a.xrec4 + (size_t)(L.n4 + b) * f4b, f4b, xbar);
+    if (tid == 0 && n4x > 0) {
+        // the other tokens' 4-bit-layout fragments, only in CTAs with shared-expert jobs
+        finch_mbar_expect_tx(xbar2, (unsigned)(n4x * f4b));
+        for (int b = 0; b < n4x; b++) finch_bulk_g2s(smem + tail_off + b * L.f4s, a.xrec4 + (size_t)(L.n4 + b) * f4b, f4b, xbar2);
     }
     __syncthreads();
     const long long tk1 = clock64();
@@ -796,7 +801,7 @@ __global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
     // bumps the slot's counter; whoever comes last adds the four partials in fixed order.
     const int team = warp / TEAM_A, kw = warp % TEAM_A;
     int *qcnt = reinterpret_cast<int *>(smem + L.qcnt);
-    if (!finch_mbar_wait(xbar, 0)) {
+    if (!finch_mbar_wait(xbar, 0) || (n4x > 0 && !finch_mbar_wait(xbar2, 0))) {
         if (lane == 0) atomicExch(a.status, FINCH_E_TIMEOUT);
         return;
     }
@@ -1108,22 +1113,26 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const MoeArgs a) {
     const int b = blockIdx.y, row = blockIdx.x * 256 + threadIdx.x;
     const long long gt0 = gtime();
     grid_dep_launch();
-    grid_dep_wait();
+    // Routing, router weights, gate scores and h_mid are inputs of the whole call: final since the preparation
+    // kernel (the first of the chain) passed its own wait, and this kernel only starts once the down kernel has,
+    // which started after the gate/up kernel's wait, i.e. after the preparation kernel completed.  Only the
+    // partial rows (the down kernel's output) have to wait; the dependent loads of the routing (mask -> id ->
+    // slot) are out of the way by then.
     if (threadIdx.x < a.K) {
         ok[threadIdx.x] = pair_ok(a, b * a.K + threadIdx.x);
         wk[threadIdx.x] = a.weights[b * a.K + threadIdx.x];
     }
+    const bool live = row < a.hidden;
+    float h = live && a.h_mid ? a.h_mid[(size_t)b * a.hidden + row] : 0.f;
+    const float sg = a.has_shared ? 1.0f / (1.0f + expf(-a.gate_score[b])) : 0.f;
     __syncthreads();
-    if (row >= a.hidden) return;
+    grid_dep_wait();
+    if (!live) return;
     float moe = 0.f;
     for (int k = 0; k < a.K; k++)
         if (ok[k]) moe = fmaf(wk[k], a.partial[(size_t)(b * a.K + k) * a.hidden + row], moe);
-    float h = a.h_mid ? a.h_mid[(size_t)b * a.hidden + row] : 0.f;
     h += moe;
-    if (a.has_shared) {
-        const float sg = 1.0f / (1.0f + expf(-a.gate_score[b]));
-        h = fmaf(sg, a.partial[(size_t)(a.P + b) * a.hidden + row], h);
-    }
+    if (a.has_shared) h = fmaf(sg, a.partial[(size_t)(a.P + b) * a.hidden + row], h);
     a.hidden_out[(size_t)b * a.hidden + row] = h;
     if (a.dbg && threadIdx.x == 0) {
         long long *d = a.dbg + (size_t)(1400 + blockIdx.y * gridDim.x + blockIdx.x) * 8;
