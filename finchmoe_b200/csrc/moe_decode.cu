@@ -1018,6 +1018,14 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
             if ((lane & 15) == 0) hdr[2 * u + (lane >> 4)] = sum;
             if (lane == 0) umax[it] = mx;
         }
+        // the shared expert's records, from the last warp down (the first warps have the routed records), before the
+        // barrier so that they overlap the loads above
+        if (a.has_shared && job1 > n_routed && job1 > job0)
+            for (int b = CW_B - 1 - warp; b >= 0 && b < a.B; b += CW_B) {
+                // staged in the rows of the staging area that the routed records leave free, when there are enough
+                float *stg = (Ks <= K && nrec + a.B <= REC_CAP) ? xstage + (size_t)(REC_CAP - 1 - b) * K : nullptr;
+                warp_make_record<4>(a.shared_act + (size_t)b * Ks, Ks, smem + L.srec + b * r4b, stg);
+            }
         bar_sync(1, CW_B * 32);
         for (int it = warp; it < nrec * units; it += CW_B) {
             const int q = it / units, u = it - q * units;
@@ -1029,8 +1037,6 @@ __global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs
             if (u == 0 && lane == 0) reinterpret_cast<float *>(rec + frag3_bytes(K))[K / 64] = __int_as_float(E);
             build_frag3_range(xstage + q * K + u * 128, 128, E, reinterpret_cast<uint2 *>(rec) + u * 72, lane, 32);
         }
-        if (a.has_shared && job1 > n_routed && job1 > job0)
-            for (int b = warp; b < a.B; b += CW_B) warp_make_record<4>(a.shared_act + (size_t)b * Ks, Ks, smem + L.srec + b * r4b);
     }
     bar_sync(1, CW_B * 32);
     const long long tk2 = clock64();
