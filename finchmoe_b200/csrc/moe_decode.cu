@@ -498,9 +498,11 @@ __device__ __forceinline__ bool pair_ok(const MoeArgs &a, int p) {
 __device__ void build_groups(const MoeArgs &a, GroupTab *T, int *sm_ids, unsigned char *sm_rank, int bar, int nthreads) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     int id = -1, slot = -1;
-    if (tid < a.P && (!a.valid || a.valid[tid])) {
+    if (tid < a.P) {
+        // mask and id are loaded side by side (one memory round trip instead of two on the layer's critical path)
         const int e = a.ids[tid];
-        if (e >= 0 && e < a.n_experts) {
+        const bool on = !a.valid || a.valid[tid];
+        if (on && e >= 0 && e < a.n_experts) {
             slot = a.slot_row[e];
             if (slot >= 0) id = e;
         }
