@@ -569,6 +569,29 @@ __device__ int job_at(const int *pre, int ng, int per_group, int n_sh, int nps, 
     return gi * per_group + (target - pre[gi] * per_group + np - 1) / np;
 }
 
+// How many CTAs at the end of the grid take the shared expert's jobs (`units` jobs each).  A CTA whose range
+// crosses from routed to shared-expert jobs would finish last: its consumer units (teams or warps, `units` of
+// them, one job at a time each) are dealt its jobs round robin, and a shared-expert job - every token, so
+// several passes - lands on a unit that already has its share of routed ones.  So with three tokens or more
+// (two passes per shared job) the boundary is put on a CTA boundary and every shared CTA gets one job per
+// unit.  Returns -1 where that does not apply (no shared expert, one pass per job, a grid too small to split):
+// ranges are proportional to cost then.
+__device__ __forceinline__ int shared_ctas(int grid, int units, int n_sh, int nps) {
+    if (n_sh == 0 || nps < 2) return -1;
+    const int gs = (n_sh + units - 1) / units;
+    return gs < grid ? gs : -1;
+}
+
+// start of CTA i's range under that split
+__device__ int range_start(const int *pre, int ng, int per_group, int n_sh, int nps, int grid, int gs, int per, int i) {
+    const int routed_cost = pre[ng] * per_group, n_routed = ng * per_group;
+    if (gs < 0) return job_at(pre, ng, per_group, n_sh, nps, (int)((long long)(routed_cost + n_sh * nps) * i / grid));
+    const int gr = grid - gs;
+    if (i <= gr) return job_at(pre, ng, per_group, 0, 1, (int)((long long)routed_cost * i / gr));
+    const int j = (i - gr) * per;
+    return n_routed + (j < n_sh ? j : n_sh);
+}
+
 // ============================ prep ========================================
 // grid: B + 1 CTAs of 256 threads.  CTA b < B: operand records of token b.  CTA B: groups and ranges.
 __global__ void __launch_bounds__(256) moe_prep_kernel(const MoeArgs a) {
@@ -620,11 +643,9 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(const MoeArgs a) {
     __syncthreads();
     if (tid >= 32 && tid < 65) pre[tid] += pre[MAXP + 1];   // tid 64 fixes up the grand total in pre[MAXP]
     __syncthreads();
-    const int Ca = pre[ng] * L3.nTA + n_sh_a * nps, Cb = pre[ng] * L3.nTB + n_sh_b * nps;
-    for (int i = tid; i <= a.grid_a; i += 256)
-        T->range_a[i] = job_at(pre, ng, L3.nTA, n_sh_a, nps, (int)((long long)Ca * i / a.grid_a));
-    for (int i = tid; i <= a.grid_b; i += 256)
-        T->range_b[i] = job_at(pre, ng, L3.nTB, n_sh_b, nps, (int)((long long)Cb * i / a.grid_b));
+    const int gs_a = shared_ctas(a.grid_a, NTEAM_A, n_sh_a, nps), gs_b = shared_ctas(a.grid_b, CW_B, n_sh_b, nps);
+    for (int i = tid; i <= a.grid_a; i += 256) T->range_a[i] = range_start(pre, ng, L3.nTA, n_sh_a, nps, a.grid_a, gs_a, NTEAM_A, i);
+    for (int i = tid; i <= a.grid_b; i += 256) T->range_b[i] = range_start(pre, ng, L3.nTB, n_sh_b, nps, a.grid_b, gs_b, CW_B, i);
     __syncthreads();
     const int *s = reinterpret_cast<const int *>(T);
     int *d = reinterpret_cast<int *>(a.gtab);
