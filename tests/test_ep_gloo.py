@@ -26,6 +26,15 @@ def test_plan_sends_a_token_once_per_rank_and_skips_unusable_pairs():
     assert c2.tolist() == [0, 0] and s2.tolist() == [[-1, -1]]
 
 
+def test_static_plan_sends_every_token_to_every_rank():
+    counts, offs, send_tok, slot_of = ep.static_plan_numpy(3, 4)
+    assert counts.tolist() == [3, 3, 3, 3] and offs.tolist() == [0, 3, 6, 9, 12]
+    assert send_tok.tolist() == [0, 1, 2] * 4
+    assert slot_of.tolist() == [[0] * 4, [1] * 4, [2] * 4]
+    # the home rank's column is left out of the combine step when it adds its own share directly
+    assert ep.static_plan_numpy(3, 4, skip=2)[3].tolist() == [[0, 0, -1, 0], [1, 1, -1, 1], [2, 2, -1, 2]]
+
+
 WORKER = r'''
 import os, sys
 sys.path.insert(0, sys.argv[3]); sys.path.insert(0, os.path.dirname(sys.argv[3]))
