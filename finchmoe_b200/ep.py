@@ -18,6 +18,10 @@ protocol and is backend-agnostic: the GPU backend drives the C-ABI steps (finch_
 tests plug in a numpy backend with the same five operations.  With G = 1 the same code runs and the
 all-to-alls degenerate to copies.
 
+`ep_layer_static` is the same layer for decode-sized batches of equal size on every rank: the plan is fixed
+(every token to every rank), so steps 1 and 2 and the host synchronisation disappear, the home rank works on its
+own tokens while the records travel, and the layer can be recorded into a CUDA graph.
+
 The reference runs on one device (finchmoe/infer.m:9597-9741 is the per-layer path this extends).
 """
 from __future__ import annotations
