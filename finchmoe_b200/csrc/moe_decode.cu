@@ -5,7 +5,8 @@
 //   prep      groups the (token, k) pairs by expert, turns every token's
 //             activations into tensor-core operand records, and cuts the job
 //             lists of the two streaming kernels into one contiguous,
-//             cost-balanced range per CTA
+//             cost-balanced range per CTA (the shared expert's jobs get CTAs
+//             of their own when they take several passes)
 //   gate/up   (moe_gateup_kernel) gate, up and SiLU.  One persistent CTA per SM: a
 //             producer warp streams tiles (8 gate rows + the 8 matching up rows of
 //             one expert = one contiguous 14 KB piece of the tiled pool) through a
@@ -13,7 +14,8 @@
 //             four consumer warps take whole tiles, the warps of a team split K and
 //             whichever finishes last adds the partial sums.  Writes act[pair][inter].
 //   down      (moe_down_combine_kernel) same structure with tiles of 16 down rows
-//             and sixteen independent consumer warps.  Every CTA first turns the
+//             and sixteen independent consumer warps; the tiles are small, so one
+//             producer lane per stage issues the copies.  Every CTA first turns the
 //             activations of the (few) expert groups in its range into operand
 //             records in its own shared memory.  Writes one fp32 row per pair.
 //   combine   (moe_combine_kernel) sums the rows of a token in k order with the
