@@ -281,7 +281,7 @@ def test_moe_skips_non_resident_and_poisoned_experts(api):
         ctx.destroy()
 
 
-@pytest.mark.parametrize("B", [1, 8])
+@pytest.mark.parametrize("B", [1, 3, 5, 8])
 def test_moe_decode_full_size_vs_oracle(api, B):
     """BASELINE shapes: hidden 2048, inter 512, 256 experts, top-8, fp16 scales, bf16 activations."""
     ctx = api.Context(max_tokens=8, n_layers=1)
