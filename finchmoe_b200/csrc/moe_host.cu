@@ -1,6 +1,7 @@
 // Host-pointer entry point of the MoE layer: packs the caller's CPU buffers
-// into one pinned staging block, copies it to the device in a single transfer,
-// encodes the decode or prefill path, copies the result back and waits.
+// into one pinned staging block, encodes the decode or prefill path on it
+// (decode-sized calls: the kernels work on the pinned block in place; larger
+// ones: one transfer to the device, one back) and waits.
 #include "finch_internal.cuh"
 
 int finch_stage_reserve(finch_ctx *ctx, size_t bytes);
@@ -29,19 +30,37 @@ extern "C" int finch_moe_forward_host(finch_ctx *ctx, finch_pool *pool, int laye
     if (valid) memcpy(hs + o_v, valid, n_v);
     if (shared) memcpy(hs + o_s, shared_gate_score_host, n_s);
     if (h_mid) memcpy(hs + o_h, h_mid, n_h);
-    FINCH_CUDA_OK(ctx, cudaMemcpyAsync(ds, hs, o_o, cudaMemcpyHostToDevice, ctx->stream));
+    const bool small = (size_t)T * c.top_k <= FINCH_MAX_PAIRS;
+    // Where the kernels find the staged inputs and leave the result.  A decode-sized call moves a few tens of KB:
+    // its kernels read the pinned staging block in place over the bus and the combine kernel writes the result
+    // rows straight into it, which saves the two copy operations and their stream dependencies (each costs more
+    // than moving the bytes).  Larger calls copy to and from device memory.  FINCH_HOST_PATH=0 forces copies.
+    static const int host_path = [] {
+        const char *e = getenv("FINCH_HOST_PATH");
+        return e ? atoi(e) : 2;
+    }();
+    char *in = ds, *out = ds;
+    if (small && host_path >= 1) {
+        void *m = nullptr;
+        if (cudaHostGetDevicePointer(&m, hs, 0) == cudaSuccess && m) {
+            in = (char *)m;
+            if (host_path >= 2) out = (char *)m;
+        } else {
+            cudaGetLastError();
+        }
+    }
+    if (in == ds) FINCH_CUDA_OK(ctx, cudaMemcpyAsync(ds, hs, o_o, cudaMemcpyHostToDevice, ctx->stream));
     finch_shared sh;
     if (shared) {
         sh = *shared;
-        sh.gate_score = (const float *)(ds + o_s);
+        sh.gate_score = (const float *)(in + o_s);
     }
-    const bool small = (size_t)T * c.top_k <= FINCH_MAX_PAIRS;
     auto fn = small ? finch_encode_moe_decode : finch_encode_moe_prefill;
-    rc = fn(ctx, ctx->stream, pool, layer, ds + o_x, (const int32_t *)(ds + o_id), (const float *)(ds + o_w),
-            valid ? (const uint8_t *)(ds + o_v) : nullptr, shared ? &sh : nullptr, h_mid ? (const float *)(ds + o_h) : nullptr,
-            (float *)(ds + o_o), T);
+    rc = fn(ctx, ctx->stream, pool, layer, in + o_x, (const int32_t *)(in + o_id), (const float *)(in + o_w),
+            valid ? (const uint8_t *)(in + o_v) : nullptr, shared ? &sh : nullptr, h_mid ? (const float *)(in + o_h) : nullptr,
+            (float *)(out + o_o), T);
     if (rc) return rc;
-    FINCH_CUDA_OK(ctx, cudaMemcpyAsync(hs + o_o, ds + o_o, n_o, cudaMemcpyDeviceToHost, ctx->stream));
+    if (out == ds) FINCH_CUDA_OK(ctx, cudaMemcpyAsync(hs + o_o, ds + o_o, n_o, cudaMemcpyDeviceToHost, ctx->stream));
     FINCH_CUDA_OK(ctx, cudaStreamSynchronize(ctx->stream));
     memcpy(hidden_out, hs + o_o, n_o);
     return FINCH_OK;

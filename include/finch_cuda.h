@@ -224,7 +224,11 @@ FINCH_API int finch_encode_moe_prefill(finch_ctx *ctx, finch_stream stream, finc
 
 /* Host-pointer form of the two calls above (copies in, runs, copies out,
  * waits): what a caller holding CPU buffers uses, as the reference's
- * gpu_gguf_experts_forward does (finchmoe/infer.m:3153-3366). */
+ * gpu_gguf_experts_forward does (finchmoe/infer.m:3153-3366).  A decode-sized
+ * call (T * top_k <= FINCH_MAX_PAIRS) stages the caller's buffers in pinned
+ * memory that the kernels read and write in place (no copy operations on the
+ * stream); larger calls copy through device memory.  FINCH_HOST_PATH=0 in the
+ * environment forces the copies. */
 FINCH_API int finch_moe_forward_host(finch_ctx *ctx, finch_pool *pool, int layer, const void *h_post,
                                      const int32_t *expert_ids, const float *weights, const uint8_t *valid,
                                      const finch_shared *shared, const float *shared_gate_score_host,
