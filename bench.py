@@ -292,7 +292,9 @@ class Stack:
         return e0.elapsed_time(e1) / 1e3 / steps, uniq
 
     def time_e2e(self, rsets, x, batch, steps, warmup):
-        """Host buffers in and out through finch_moe_forward_host, layer by layer."""
+        """Host buffers in and out through finch_moe_forward_host, layer by layer.  Every call stages its inputs in
+        pinned host memory and the bytes cross the bus inside the timed region, both ways: for decode-sized calls as
+        reads and writes of the layer's kernels on the pinned block, otherwise as one copy in and one copy out."""
         torch = self.torch
         xw = self.ctx.acts_to_wire(x)
         score = np.full(batch, 0.1, np.float32)
