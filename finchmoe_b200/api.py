@@ -114,6 +114,13 @@ class Context:
         self.check(self.lib.finch_device_status(self.h, C.byref(s)))
         return s.value
 
+    def device_status_clear(self):
+        self.check(self.lib.finch_device_status_clear(self.h))
+
+    def debug_fault(self, kind: int):
+        """Failure injection for the tests of the bounded device-side waits (finch_debug_fault)."""
+        self.check(self.lib.finch_debug_fault(self.h, kind))
+
     def launch_count(self) -> int:
         return int(self.lib.finch_launch_count(self.h))
 

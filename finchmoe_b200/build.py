@@ -11,7 +11,7 @@ CSRC = os.path.join(PKG, "csrc")
 SO = os.path.join(PKG, "libfinchcuda.so")
 SOURCES = ["ctx_pool.cu", "matvec_generic.cu", "moe_decode.cu", "moe_prefill.cu", "moe_host.cu", "ep_exchange.cu", "matvec_fast.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
-FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17", "--use_fast_math=false",
+FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
          "-Xcompiler", "-fPIC,-fvisibility=hidden", "-I", os.path.join(ROOT, "include"), "-I", CSRC]
 
 
@@ -26,7 +26,7 @@ def _stale() -> bool:
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale():
         return SO
-    flags = [f for f in FLAGS if f != "--use_fast_math=false"]
+    flags = FLAGS + os.environ.get("FINCH_NVCC_FLAGS", "").split()   # e.g. -DFINCH_STAMPS for the phase-timing build
     objs = []
     os.makedirs(os.path.join(PKG, "build"), exist_ok=True)
     procs = []

@@ -77,8 +77,7 @@ extern "C" int finch_ctx_create(const finch_config *cfg, finch_ctx **out) {
     bool ok = cudaMalloc(&ctx->act, pairs * c.moe_inter * sizeof(float)) == cudaSuccess &&
               cudaMalloc(&ctx->shared_act, (size_t)c.max_tokens * sh_inter * sizeof(float)) == cudaSuccess &&
               cudaMalloc(&ctx->partial, (pairs + c.max_tokens) * c.hidden * sizeof(float)) == cudaSuccess &&
-              cudaMalloc(&ctx->dev_status, sizeof(int)) == cudaSuccess &&
-              cudaMalloc(&ctx->frag_scratch, finch_decode_scratch_bytes(c)) == cudaSuccess;
+              cudaMalloc(&ctx->dev_status, sizeof(int)) == cudaSuccess;
     if (!ok) return bail(FINCH_E_NOMEM);
     cudaMemset(ctx->dev_status, 0, sizeof(int));
     cudaMemset(ctx->partial, 0, (pairs + c.max_tokens) * c.hidden * sizeof(float));
@@ -95,7 +94,6 @@ extern "C" void finch_ctx_destroy(finch_ctx *ctx) {
     cudaFree(ctx->shared_act);
     cudaFree(ctx->partial);
     cudaFree(ctx->dev_status);
-    cudaFree(ctx->frag_scratch);
     for (auto &e : ctx->shared_cache) cudaFree(e.tiles);
     cudaFree(ctx->stage_dev);
     cudaFree(ctx->pf_ws);
@@ -142,6 +140,14 @@ extern "C" int finch_sync(finch_ctx *ctx) {
 extern "C" int finch_device_status(finch_ctx *ctx, int *status_out) {
     if (!ctx || !status_out) return FINCH_E_ARG;
     FINCH_CUDA_OK(ctx, cudaMemcpy(status_out, ctx->dev_status, sizeof(int), cudaMemcpyDeviceToHost));
+    return FINCH_OK;
+}
+
+extern "C" int finch_device_status_clear(finch_ctx *ctx) {
+    if (!ctx) return FINCH_E_ARG;
+    cudaSetDevice(ctx->cfg.device);
+    FINCH_CUDA_OK(ctx, cudaDeviceSynchronize());
+    FINCH_CUDA_OK(ctx, cudaMemset(ctx->dev_status, 0, sizeof(int)));
     return FINCH_OK;
 }
 

@@ -27,8 +27,7 @@ struct finch_ctx {
     float *shared_act = nullptr;    // [max_tokens][shared_inter]
     float *partial = nullptr;       // [max_pairs + max_tokens][hidden] per-pair down outputs (+ shared rows)
     int *dev_status = nullptr;      // sticky device status word
-    void *frag_scratch = nullptr;   // tensor-core operand fragments + expert-group table (moe_decode.cu)
-    void *dbg = nullptr;            // finch_debug_timing buffer
+    int fault = 0;                  // finch_debug_fault: failure injected into the next decode calls
     bool no_pdl = false;            // FINCH_NO_PDL=1 in the environment: plain stream-ordered launches
     struct SharedPrepared {
         const void *key[3];
@@ -93,7 +92,6 @@ static inline cudaStream_t finch_pick_stream(finch_ctx *ctx, finch_stream s) {
 
 // Implemented in moe_decode.cu / moe_prefill.cu, used by the host-pointer entry point.
 int finch_validate_wdesc(finch_ctx *ctx, const finch_wdesc *w, const char *what);
-size_t finch_decode_scratch_bytes(const finch_config &c);
 
 // ------------------------------------------------------------------ device helpers
 #ifdef __CUDACC__

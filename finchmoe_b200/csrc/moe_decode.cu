@@ -1,26 +1,29 @@
 // MoE decode path: routed 3-bit experts (gate, up, SiLU, down), the 4-bit
-// shared expert and the router-weighted combine, in four launches per layer chained
-// with programmatic dependent launch.
+// shared expert and the router-weighted combine, in three launches per layer
+// chained with programmatic dependent launch.
 //
-//   prep      groups the (token, k) pairs by expert, turns every token's
-//             activations into tensor-core operand records, and cuts the job
-//             lists of the two streaming kernels into one contiguous,
-//             cost-balanced range per CTA (the shared expert's jobs get CTAs
-//             of their own when they take several passes)
-//   gate/up   (moe_gateup_kernel) gate, up and SiLU.  One persistent CTA per SM: a
-//             producer warp streams tiles (8 gate rows + the 8 matching up rows of
-//             one expert = one contiguous 14 KB piece of the tiled pool) through a
-//             ring of shared-memory stages with bulk async copies; six teams of
-//             four consumer warps take whole tiles, the warps of a team split K and
-//             whichever finishes last adds the partial sums.  Writes act[pair][inter].
-//   down      (moe_down_combine_kernel) same structure with tiles of 16 down rows
-//             and sixteen independent consumer warps; the tiles are small, so one
-//             producer lane per stage issues the copies.  Every CTA first turns the
-//             activations of the (few) expert groups in its range into operand
-//             records in its own shared memory.  Writes one fp32 row per pair.
+//   gate/up   (moe_gateup_kernel) gate, up and SiLU.  One persistent CTA per SM.  Every CTA
+//             prepares for itself (no preparation launch): two warps group the (token, k)
+//             pairs of the call by expert while the others turn the tokens' activations
+//             (brought in by bulk copies, a few tens of KB from L2) into tensor-core operand
+//             records in shared memory.  The work is cut into tiles (8 gate rows + the 8
+//             matching up rows of one expert); a team of four warps takes a contiguous,
+//             cost-balanced range of tiles, each warp one quarter of K: it fetches its own
+//             piece (3.5 KB of the tiled pool) with bulk async copies into two private
+//             stages, so there is no producer warp, no ring shared between warps and no
+//             empty-barrier traffic.  The team adds its four partial sums in fixed order
+//             behind a named barrier, applies SiLU(gate) * up and writes act[pair][inter].
+//   down      (moe_down_kernel) same structure with tiles of 16 down rows = one piece, one
+//             warp per tile.  A CTA takes a contiguous, cost-balanced range of the
+//             group-major job list, so it needs the activations of one or two expert groups
+//             only; it turns those into operand records after its dependency wait (its first
+//             weight pieces are already on their way by then).  Writes one fp32 row per pair.
 //   combine   (moe_combine_kernel) sums the rows of a token in k order with the
 //             residual and the gated shared expert (the arithmetic of
 //             moe_combine_residual, finchmoe/shaders.metal:2196-2231).
+//
+// The shared expert's tiles go to CTAs of their own at the end of each grid (their number
+// follows the expected share of the work), which keep the 4-bit-layout records instead.
 //
 // "Expert group" = the (token, k) pairs of this call that selected the same
 // expert: its weights are read from HBM once for all of them.
@@ -30,36 +33,41 @@
 // p <= 7, is -- after a single AND -- the fp16 *subnormal* q * 2^(p-24); that
 // register goes straight into the A operand of mma.sync.m16n8k16 (f16 inputs,
 // fp32 accumulate).  The B operand holds the activations, pre-scaled per
-// k-slot by 2^(7-p) / norm (norm = power of two > max|x|) and split into an
-// fp16 "hi" and a "lo * 2^11" column so that no mantissa bit of an fp32 x is
-// lost.  Every product is exact in fp32; the per-group scale and bias are
-// applied to the fp32 group sums:  out = sum_g s_g * (sum_i q_i x_i) + b_g *
-// (sum_i x_i).  A 96-bit period (32 codes) needs 18 ANDs + 3 shifts.  Lane t
-// of a quad owns period t of a 48-byte unit (128 codes = two groups); the two
-// groups of a unit are kept apart by giving them different B columns.
+// k-slot by 2^(7-p) / norm (norm = power of two > max|x|).  An fp32 activation is
+// split into an fp16 "hi" and a "lo * 2^11" column so that none of its mantissa bits
+// is lost; a bf16 activation (8 significant bits) is its own "hi" and needs no second
+// column: it is exact unless it lies below 2^-17 of the row's largest magnitude, where
+// it is rounded to a multiple of 2^-24 * norm (a change of less than 2^-25 * norm in
+// one term, below the rounding noise of the fp32 accumulation).  Every product is exact
+// in fp32; the per-group scale and bias are applied to the fp32 group sums:
+// out = sum_g s_g * (sum_i q_i x_i) + b_g * (sum_i x_i).  A 96-bit period (32 codes)
+// needs 18 ANDs + 3 shifts.  Lane t of a quad owns period t of a 48-byte unit
+// (128 codes = two groups); the two groups of a unit are kept apart by giving them
+// different B columns, so the eight columns of an MMA are four "virtual columns"
+// (token, or token x {hi, lo}) times two groups: one pass over a tile serves four
+// bf16 tokens or two fp32 tokens.
+#include <algorithm>
+
 #include "finch_internal.cuh"
 #include "tile_layout.h"
 
 namespace {
 
-constexpr int TEAM_A = 4;                   // warps that split the K dimension of one gate/up tile
-constexpr int NTEAM_A = 6;
-constexpr int CW_A = TEAM_A * NTEAM_A;      // consumer warps of kernel A
-constexpr int NT_A = (CW_A + 1) * 32;       // + one producer warp
-constexpr int CW_B = 16;
-constexpr int NT_B = (CW_B + 1) * 32;
+constexpr int TEAM = 4;                     // warps that split the K dimension of one gate/up tile
 constexpr int MAXP = FINCH_MAX_PAIRS;
 constexpr int MAXM = 8;                     // pairs per expert group (<= tokens per call)
-constexpr int MAXG = 160;                   // CTAs per streaming kernel (range table size)
-constexpr int REC_CAP = 24;                 // act records a CTA of kernel B can hold
+constexpr int NW_MAX = 24;                  // consumer warps per CTA
+constexpr int REC_CAP = 24;                 // act records a CTA of the down kernel can hold
+constexpr int UB = 288;                     // bytes of one 128-value unit in one section of a 3-bit operand record
+constexpr int GB4 = 128;                    // bytes of one 64-value group in one section of a 4-bit operand record
+constexpr int MMA_A3 = 9, MMA_A4 = 4;       // MMAs per 3-bit unit / per 4-bit group (cost model of the work split)
 
-struct GroupTab {  // expert groups of one call + the job ranges of the CTAs
+struct GroupTab {  // expert groups of one call
     int ng;
     int slot[MAXP];             // pool slot of the group's expert
     unsigned char m[MAXP];      // pairs in the group
     unsigned char pairs[MAXP][MAXM];
-    int range_a[MAXG + 1];      // CTA b of kernel A runs jobs [range_a[b], range_a[b+1])
-    int range_b[MAXG + 1];
+    int pre[MAXP + 2];          // pre[gi] = passes of the groups before gi; pre[ng] = total
 };
 
 struct MoeArgs {
@@ -74,59 +82,33 @@ struct MoeArgs {
     const uint8_t *valid;
     int P, K, B;
     int hidden, inter;
-    int scale_dtype;
     float *act;          // [P][inter]
     float *partial;      // [P + B][hidden]
     int *status;
     int has_shared;
     const uint8_t *sh_tiles;  // prepared (tiled) copy of the shared expert
-    int sh_scale_dtype, sh_inter;
+    int sh_inter, sh_fp16;    // shared expert: intermediate size, scales / biases are fp16 (else bf16)
     float *shared_act;   // [B][sh_inter]
     const float *gate_score;
     const float *h_mid;
     float *hidden_out;
-    GroupTab *gtab;      // written by prep
-    uint8_t *xrec3;      // [B] records: 3-bit-layout operands of h_post + header
-    uint8_t *xrec4;      // [B] 4-bit-layout operand fragments of h_post (shared expert)
-    int grid_a, grid_b, stages_a, stages_b;
-    long long *dbg;      // optional per-CTA cycle counters (finch_debug_timing), or NULL
+    int gs_a, gs_b;      // CTAs at the end of the gate/up / down grid that take the shared expert's tiles
+    int fault;           // finch_debug_fault: 1 = one warp of the gate/up kernel withholds its first fetch
 };
 
 // ---- operand records -------------------------------------------------------
-// record = fragments (8-byte entries) followed by a header of floats:
+// record = one or two sections of B fragments (hi; hi + lo) followed by a header of floats:
 // hdr[0..groups) = sum of x over each group of 64, hdr[groups] = E (int bits).
-__host__ __device__ inline int frag3_bytes(int K) { return (K / 128) * 72 * 8; }
-__host__ __device__ inline int frag4_bytes(int K) { return (K / 64) * 32 * 8; }
+// 3-bit section: per unit UB bytes = MMA pairs (0,1) (2,3) (4,5) (6,7) as [pair][t][16 B], then MMA 8 as [t][8 B].
+// 4-bit section: per group GB4 bytes = MMA pairs (0,1) (2,3) as [pair][t][16 B].
+__host__ __device__ inline int up128(int x) { return (x + 127) & ~127; }
+__host__ __device__ inline int sec3_bytes(int K) { return (K / 128) * UB; }
+__host__ __device__ inline int sec4_bytes(int K) { return (K / 64) * GB4; }
 __host__ __device__ inline int hdr_bytes(int K) { return ((K / 64 + 1 + 15) / 16) * 64; }
-__host__ __device__ inline int rec3_bytes(int K) { return frag3_bytes(K) + hdr_bytes(K); }
-__host__ __device__ inline int rec4_bytes(int K) { return frag4_bytes(K) + hdr_bytes(K); }
+__host__ __device__ inline int rec3_bytes(int K, int hilo) { return up128(sec3_bytes(K) * (1 + hilo) + hdr_bytes(K)); }
+__host__ __device__ inline int rec4_bytes(int K, int hilo) { return up128(sec4_bytes(K) * (1 + hilo) + hdr_bytes(K)); }
 
-// Slot tables of the 3-bit extraction.  Extraction e (0..17, see extract3) yields a register with one
-// code in each 16-bit half; MMA j uses extractions 2j and 2j+1, i.e. four slots 4j..4j+3.  Slot s holds
-// code number idx (0..31) of the 32-code period at bit position pos of its half, or is empty:
-//   idx: 0 6 1 7 | 2 - 3 8 | 4 9 5 10 | 11 16 12 17 | 13 18 14 19 | 15 20 - 21 | 22 27 23 28 | - 29 24 30 | 25 31 26 -
-//   pos: 0 2 3 5 | 6 0 1 0 | 4 3 7 6  | 1 0 4 3     | 7 6 2 1     | 5 4 0 7   | 2 1 5 4     | 0 7 0 2   | 3 5 6 0
-// They are packed into immediates (one byte idx | pos << 5 per slot, empty slots flagged in a bit mask) so
-// that a thread gets the four slots of its MMA without touching memory.
-__device__ __forceinline__ uint32_t slots3_of(int j) {
-    const unsigned long long w = j < 2 ? 0x082300c2a7614600ull : j < 4 ? 0x718c102bcae56984ull : j < 6 ? 0xf50094af334ed2edull
-                               : j < 8 ? 0x5e18fd009cb73b56ull : 0x0000000000dabf79ull;
-    return (uint32_t)(w >> (32 * (j & 1)));
-}
-__device__ __forceinline__ uint32_t empty3_of(int j) { return (uint32_t)(0x810400020ull >> (4 * j)) & 15u; }
-
-__device__ __forceinline__ void extract3(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t (&e)[18]) {
-    const uint32_t v1 = __funnelshift_r(w0, w1, 8), v3 = __funnelshift_r(w1, w2, 8), v5 = w2 >> 8;
-    e[0] = w0 & 0x001C0007u;  e[1] = w0 & 0x00E00038u;  e[2] = w0 & 0x000001C0u;
-    e[3] = v1 & 0x0007000Eu;  e[4] = v1 & 0x00380070u;  e[5] = v1 & 0x01C00380u;
-    e[6] = w1 & 0x0007000Eu;  e[7] = w1 & 0x00380070u;  e[8] = w1 & 0x01C00380u;
-    e[9] = v3 & 0x000E001Cu;  e[10] = v3 & 0x007000E0u; e[11] = v3 & 0x03800000u;
-    e[12] = w2 & 0x000E001Cu; e[13] = w2 & 0x007000E0u; e[14] = w2 & 0x03800000u;
-    e[15] = v5 & 0x001C0007u; e[16] = v5 & 0x00E00038u; e[17] = v5 & 0x000001C0u;
-}
-
-// The same extraction, one register at a time (k = 0..17, compile-time): lets the matvec loop form the four A
-// registers of an MMA right before issuing it, which keeps few of them alive at once.
+// Extraction k (0..17, compile-time) of a 96-bit period given as its words w0 w1 w2 and the views shifted by a byte.
 template <int k>
 __device__ __forceinline__ uint32_t extract3_one(uint32_t w0, uint32_t v1, uint32_t w1, uint32_t v3, uint32_t w2, uint32_t v5) {
     constexpr uint32_t M0[3] = {0x001C0007u, 0x00E00038u, 0x000001C0u}, M1[3] = {0x0007000Eu, 0x00380070u, 0x01C00380u},
@@ -144,12 +126,7 @@ __device__ __forceinline__ void extract4(uint32_t w, uint32_t (&e)[4]) {
 }
 
 // Programmatic dependent launch: the kernels of a call are launched so that each may start while
-// its predecessor drains; nothing written by the predecessor may be read before this returns.
-__device__ __forceinline__ long long gtime() {
-    long long t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
+// its predecessor drains; nothing written by the predecessor may be read before the wait returns.
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // Lets the next kernel of the chain be scheduled as soon as SMs free up instead of when this grid has
 // drained: its CTAs run their prologue (and whatever does not depend on this grid's output) and then
@@ -157,68 +134,61 @@ __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.w
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ float pow2_biased(int e) { return __uint_as_float((uint32_t)e << 23); }
-__device__ __forceinline__ void bar_sync(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(finch_smem_u32(bar)) : "memory");
+
+__device__ __forceinline__ bool mbar_wait_lim(uint64_t *bar, unsigned parity, unsigned tries) {
+    const uint32_t a = finch_smem_u32(bar);
+    for (unsigned it = 0; it < tries; ++it) {
+        unsigned done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity), "r"(20000u)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
 }
 
-// Loads one activation row into xs (fp32 shared memory) and writes the group
-// sums hdr[0..K/64) and hdr[K/64] = E, the biased exponent of a power of two
-// > max|x| (clamped so every derived scale factor is a normal float).  Run by
-// the NT threads tid = 0..NT-1 that share named barrier `bar`; ends with it.
-template <int NT>
-__device__ void load_x(const void *src, int dtype, int K, float *xs, float *hdr, float *warp_max, int bar) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float amax = 0.f;
-    for (int base0 = 0; base0 < K; base0 += NT * 8) {
-        const int base = base0 + tid * 8;
-        float v[8];
-        if (base < K) {
-            if (dtype == FINCH_BF16) {
-                const uint4 r = __ldcg(reinterpret_cast<const uint4 *>((const uint16_t *)src + base));
-                const uint32_t u[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    v[2 * j] = __uint_as_float(u[j] << 16);
-                    v[2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
-                }
-            } else {
-                const float4 a = __ldcg(reinterpret_cast<const float4 *>((const float *)src + base));
-                const float4 b = __ldcg(reinterpret_cast<const float4 *>((const float *)src + base + 4));
-                v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; j++) v[j] = 0.f;
-        }
-        float s = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            s += v[j];
-            amax = fmaxf(amax, fabsf(v[j]));
-        }
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        s += __shfl_xor_sync(0xffffffffu, s, 4);
-        if (base < K) {
-            *reinterpret_cast<float4 *>(xs + base) = make_float4(v[0], v[1], v[2], v[3]);
-            *reinterpret_cast<float4 *>(xs + base + 4) = make_float4(v[4], v[5], v[6], v[7]);
-            if ((lane & 7) == 0) hdr[base >> 6] = s;
-        }
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if (lane == 0) warp_max[warp] = amax;
-    bar_sync(bar, NT);
-    if (tid == 0) {
-        float m = 0.f;
-        for (int w = 0; w < NT / 32; w++) m = fmaxf(m, warp_max[w]);
-        int E = (int)(__float_as_uint(m) >> 23) + 1;
-        E = E < 30 ? 30 : (E > 230 ? 230 : E);
-        hdr[K / 64] = __int_as_float(E);
-    }
-    bar_sync(bar, NT);
+// A warp that gives up records the timeout and, before it returns, lets the one fetch it may still have in
+// flight land (a CTA's shared memory must not be released under a copy).
+__device__ __forceinline__ void give_up(int *status, uint64_t *pending, unsigned parity) {
+    if ((threadIdx.x & 31) == 0) atomicExch(status, FINCH_E_TIMEOUT);
+    if (pending) mbar_wait_lim(pending, parity, 1u << 13);
 }
+
+// Orders this thread's earlier generic-proxy accesses to shared memory before later async-proxy (bulk copy) ones.
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Pulls the 128-byte lines of [p, p + bytes) into L2 (no data is consumed: allowed ahead of the dependency wait).
+__device__ __forceinline__ void prefetch_l2(const void *p, int bytes, int first, int stride) {
+    for (int o = first * 128; o < bytes; o += stride * 128) asm volatile("prefetch.global.L2 [%0];" ::"l"((const char *)p + o));
+}
+// Release / acquire on shared-memory words (CTA scope): a team's hand-over of its partial sums.
+__device__ __forceinline__ int atom_add_acq_rel(int *p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(finch_smem_u32(p)), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ void st_release(int *p, int v) {
+    asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(finch_smem_u32(p)), "r"(v) : "memory");
+}
+// Bounded wait for a shared-memory word to reach a value (a teammate publishes it).
+__device__ __forceinline__ bool wait_ge(const int *p, int want, unsigned limit) {
+    const uint32_t a = finch_smem_u32(p);
+    for (unsigned i = 0; i < limit; ++i) {
+        int v;
+        asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
+        if (v >= want) return true;
+        __nanosleep(32);
+    }
+    return false;
+}
+
+// Named barrier `id` (1..15; 0 is __syncthreads) over `threads` threads.
+__device__ __forceinline__ void named_sync(int id, int threads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory"); }
+constexpr int BAR_GROUPS = 7, BAR_RECORDS = 8;   // ids 1..6 belong to the teams of the gate/up kernel
 
 // hi / lo fp16 split of four pre-scaled activations -> the two B-fragment entries of one lane.
 __device__ __forceinline__ void split4(const float (&xv)[4], uint2 &hi, uint2 &lo) {
@@ -233,231 +203,340 @@ __device__ __forceinline__ void split4(const float (&xv)[4], uint2 &hi, uint2 &l
     lo = make_uint2(finch_pack_h2(l[0], l[1]), finch_pack_h2(l[2], l[3]));
 }
 
-// B fragments of one token, 3-bit layout: frag[((u * 9 + j) * 2 + term) * 4 + t].
-// frag may be shared or global memory.  Thread `first` of `stride` (stride >= 32) cooperating threads.
-// A thread keeps one (j, t) position of the 9 x 4 entries of a unit and walks the units, so the slots
-// are decoded once per thread, not once per entry.
-__device__ __forceinline__ void build_frag3_range(const float *xs, int K, int E, uint2 *frag, int first, int stride) {
-    const int units = K / 128;
-    const int ulanes = stride >= 36 ? stride / 36 : 1;       // threads side by side along the units
-    const int rounds = stride >= 36 ? 1 : 2;                 // a single warp covers the 36 positions in two rounds
-    for (int rd = 0; rd < rounds; rd++) {
-        const int jt = stride >= 36 ? first % 36 : first + 32 * rd;
-        const int u0 = stride >= 36 ? first / 36 : 0;
-        if (jt >= 36 || u0 >= ulanes) continue;
-        const int j = jt >> 2, t = jt & 3;
-        int idx[4];
-        float mul[4];
-        const uint32_t slots = slots3_of(j), hole = empty3_of(j);
+// B fragments of `units` 128-value units of one row, 3-bit layout.  xs: the unit's values (fp32, shared memory);
+// sec: first byte of the hi section at unit 0; lo_off: distance of the lo section (HILO only).  Thread `first`
+// of `stride` (stride >= 32) cooperating threads.  A thread keeps one (j, t) position of the 9 x 4 entries
+// of a unit and walks the units, so the slots are decoded once per thread, not once per entry.
+// Values base .. base + N - 1 of a staged row (bf16 or fp32 in shared memory, 16-byte aligned) as floats.
+template <bool SRC_BF16, int N>
+__device__ __forceinline__ void row_vals(const uint8_t *row, int base, float (&x)[N]) {
+    if (SRC_BF16) {
 #pragma unroll
-        for (int s = 0; s < 4; s++) {
-            const uint32_t b = (slots >> (8 * s)) & 255u;
-            idx[s] = (int)(b & 31u);
-            mul[s] = ((hole >> s) & 1u) ? 0.f : pow2_biased(261 - E - (int)(b >> 5));
+        for (int i = 0; i < N / 8; i++) {
+            const uint4 r = *reinterpret_cast<const uint4 *>(row + (size_t)(base + 8 * i) * 2);
+            const uint32_t u[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                x[8 * i + 2 * j] = __uint_as_float(u[j] << 16);
+                x[8 * i + 2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
+            }
         }
-#pragma unroll 4
-        for (int u = u0; u < units; u += ulanes) {
-            float xv[4];
+    } else {
 #pragma unroll
-            for (int s = 0; s < 4; s++) xv[s] = mul[s] == 0.f ? 0.f : xs[u * 128 + t * 32 + idx[s]] * mul[s];
-            uint2 hi, lo;
-            split4(xv, hi, lo);
-            const int o = (u * 9 + j) * 8 + t;
-            frag[o] = hi;
-            frag[o + 4] = lo;
+        for (int i = 0; i < N / 4; i++) {
+            const float4 r = *reinterpret_cast<const float4 *>(row + (size_t)(base + 4 * i) * 4);
+            x[4 * i] = r.x; x[4 * i + 1] = r.y; x[4 * i + 2] = r.z; x[4 * i + 3] = r.w;
         }
     }
 }
 
-template <int NT>
-__device__ __forceinline__ void build_frag3(const float *xs, int K, int E, uint2 *frag) {
-    build_frag3_range(xs, K, E, frag, threadIdx.x, NT);
+// Eight pre-scaled values = the entries of two consecutive MMAs of one lane -> 16 bytes of the hi section (and of the lo one).
+template <bool HILO>
+__device__ __forceinline__ void store_pair(const float (&v)[8], uint8_t *o, int lo_off) {
+    if (HILO) {
+        const float a[4] = {v[0], v[1], v[2], v[3]}, b[4] = {v[4], v[5], v[6], v[7]};
+        uint2 h0, l0, h1, l1;
+        split4(a, h0, l0);
+        split4(b, h1, l1);
+        *reinterpret_cast<uint4 *>(o) = make_uint4(h0.x, h0.y, h1.x, h1.y);
+        *reinterpret_cast<uint4 *>(o + lo_off) = make_uint4(l0.x, l0.y, l1.x, l1.y);
+    } else {
+        *reinterpret_cast<uint4 *>(o) = make_uint4(finch_pack_h2(v[0], v[1]), finch_pack_h2(v[2], v[3]), finch_pack_h2(v[4], v[5]), finch_pack_h2(v[6], v[7]));
+    }
 }
 
-// B fragments of one token, 4-bit layout: frag[((gamma * 4 + j) * 2 + term) * 4 + t].
-__device__ __forceinline__ void build_frag4_range(const float *xs, int K, int E, uint2 *frag, int first, int stride) {
-    const int entries = (K / 64) * 16;
-    for (int e = first; e < entries; e += stride) {
-        const int gamma = e >> 4, j = (e >> 2) & 3, t = e & 3;
-        const int wbase = gamma * 64 + (2 * t + (j >> 1)) * 8 + ((j & 1) ? 2 : 0);
-        // slots: (code, p) = (0,0) (4,0) (1,4) (5,4) for even j; (2,0) (6,0) (3,4) (7,4) for odd j
-        float xv[4];
-        xv[0] = xs[wbase + 0] * pow2_biased(261 - E);
-        xv[1] = xs[wbase + 4] * pow2_biased(261 - E);
-        xv[2] = xs[wbase + 1] * pow2_biased(257 - E);
-        xv[3] = xs[wbase + 5] * pow2_biased(257 - E);
+// B entries of period t of unit u of one row, 3-bit layout: the period's 32 values against the slot table
+// (code number and bit position of every k-slot of the nine MMAs; -1 = empty slot), which follows from the
+// masks of extract3_one.  sec: the hi section of the row's record; lo_off: distance of the lo section.
+template <bool HILO, bool SRC_BF16>
+__device__ __forceinline__ void build_frag3_item(const uint8_t *row, int u, int t, int E, uint8_t *sec, int lo_off) {
+    constexpr int IDX[36] = {0, 6, 1, 7, 2, -1, 3, 8, 4, 9, 5, 10, 11, 16, 12, 17, 13, 18, 14, 19, 15, 20, -1, 21, 22, 27, 23, 28, -1, 29, 24, 30, 25, 31, 26, -1};
+    constexpr int POS[36] = {0, 2, 3, 5, 6, 0, 1, 0, 4, 3, 7, 6, 1, 0, 4, 3, 7, 6, 2, 1, 5, 4, 0, 7, 2, 1, 5, 4, 0, 7, 0, 2, 3, 5, 6, 0};
+    float x[32], c[8];
+    row_vals<SRC_BF16, 32>(row, u * 128 + t * 32, x);
+#pragma unroll
+    for (int p = 0; p < 8; p++) c[p] = pow2_biased(261 - E - p);
+    uint8_t *o = sec + u * UB + t * 16;
+#pragma unroll
+    for (int jp = 0; jp < 4; jp++) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = IDX[jp * 8 + k] < 0 ? 0.f : x[IDX[jp * 8 + k] < 0 ? 0 : IDX[jp * 8 + k]] * c[POS[jp * 8 + k]];
+        store_pair<HILO>(v, o + jp * 64, lo_off);
+    }
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) v[k] = IDX[32 + k] < 0 ? 0.f : x[IDX[32 + k] < 0 ? 0 : IDX[32 + k]] * c[POS[32 + k]];
+    uint8_t *o8 = sec + u * UB + 256 + t * 8;
+    if (HILO) {
         uint2 hi, lo;
-        split4(xv, hi, lo);
-        const int o = (gamma * 4 + j) * 8 + t;
-        frag[o] = hi;
-        frag[o + 4] = lo;
+        split4(v, hi, lo);
+        *reinterpret_cast<uint2 *>(o8) = hi;
+        *reinterpret_cast<uint2 *>(o8 + lo_off) = lo;
+    } else {
+        *reinterpret_cast<uint2 *>(o8) = make_uint2(finch_pack_h2(v[0], v[1]), finch_pack_h2(v[2], v[3]));
     }
-}
-template <int NT>
-__device__ __forceinline__ void build_frag4(const float *xs, int K, int E, uint2 *frag) {
-    build_frag4_range(xs, K, E, frag, threadIdx.x, NT);
 }
 
-// One warp turns K fp32 values at src (global memory written by an earlier
-// launch) into an operand record (shared or global memory).  BITS selects the layout.
-// stage: K floats of shared memory private to the warp, or NULL; with it the scattered reads of the
-// second pass come from shared memory instead of paying an L2 round trip each.
-template <int BITS>
-__device__ void warp_make_record(const float *src, int K, uint8_t *rec, float *stage = nullptr) {
-    const int lane = threadIdx.x & 31;
-    float *hdr = reinterpret_cast<float *>(rec + (BITS == 3 ? frag3_bytes(K) : frag4_bytes(K)));
-    float amax = 0.f;
-#pragma unroll 4
-    for (int base = lane * 8; base < K; base += 256) {  // K is a multiple of 64, so a warp never splits a group
-        const float4 a = __ldcg(reinterpret_cast<const float4 *>(src + base));
-        const float4 b = __ldcg(reinterpret_cast<const float4 *>(src + base + 4));
-        float s = ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w));
-        amax = fmaxf(amax, fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))),
-                                 fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w)))));
-        // the eight lanes of a group are active together (K % 64 == 0)
-        const unsigned mask = __activemask();
-        s += __shfl_xor_sync(mask, s, 1);
-        s += __shfl_xor_sync(mask, s, 2);
-        s += __shfl_xor_sync(mask, s, 4);
-        if ((lane & 7) == 0) hdr[base >> 6] = s;
-        if (stage) {
-            *reinterpret_cast<float4 *>(stage + base) = a;
-            *reinterpret_cast<float4 *>(stage + base + 4) = b;
-        }
-    }
-    __syncwarp();
+// B entries of quad lane t of group gamma of one row, 4-bit layout: words 2t, 2t + 1 of the group (16 values).
+// MMA j takes codes (0,4,1,5) of word 2t (j = 0), (2,6,3,7) (j = 1), then the same of word 2t + 1; codes in the low
+// half of a byte sit at p = 0, in the high half at p = 4.
+template <bool HILO, bool SRC_BF16>
+__device__ __forceinline__ void build_frag4_item(const uint8_t *row, int gamma, int t, int E, uint8_t *sec, int lo_off) {
+    float x[16];
+    row_vals<SRC_BF16, 16>(row, gamma * 64 + t * 16, x);
+    const float c0 = pow2_biased(261 - E), c4 = pow2_biased(257 - E);
+    uint8_t *o = sec + gamma * GB4 + t * 16;
 #pragma unroll
-    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    int E = (int)(__float_as_uint(amax) >> 23) + 1;
-    E = E < 30 ? 30 : (E > 230 ? 230 : E);
-    if (lane == 0) hdr[K / 64] = __int_as_float(E);
-    __syncwarp();
-    const float *xs = stage ? stage : src;
-    if (BITS == 3) build_frag3_range(xs, K, E, reinterpret_cast<uint2 *>(rec), lane, 32);
-    else build_frag4_range(xs, K, E, reinterpret_cast<uint2 *>(rec), lane, 32);
-    __syncwarp();
+    for (int jp = 0; jp < 2; jp++) {
+        const int b = jp * 8;
+        const float v[8] = {x[b] * c0, x[b + 4] * c0, x[b + 1] * c4, x[b + 5] * c4, x[b + 2] * c0, x[b + 6] * c0, x[b + 3] * c4, x[b + 7] * c4};
+        store_pair<HILO>(v, o + jp * 64, lo_off);
+    }
+}
+
+// Phase stamps for working out where a launch spends its time: compiled in with -DFINCH_STAMPS only.
+#ifdef FINCH_STAMPS
+__device__ long long g_stamps[2 * 160 * 32 * 16];
+__device__ __forceinline__ long long gtime() {
+    long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+#define STAMP(i) do { if ((threadIdx.x & 31) == 0) g_stamps[((size_t)blockIdx.x * 32 + (threadIdx.x >> 5)) * 16 + (i)] = gtime(); } while (0)
+#define STAMP_ADD(i, v) do { if ((threadIdx.x & 31) == 0) g_stamps[((size_t)blockIdx.x * 32 + (threadIdx.x >> 5)) * 16 + (i)] += (v); } while (0)
+#define STAMPB(i) do { if ((threadIdx.x & 31) == 0) g_stamps[(160 * 32 + (size_t)blockIdx.x * 32 + (threadIdx.x >> 5)) * 16 + (i)] = gtime(); } while (0)
+#define STAMP_CLK() clock64()
+#else
+#define STAMPB(i) do {} while (0)
+#define STAMP(i) do {} while (0)
+#define STAMP_ADD(i, v) do {} while (0)
+#define STAMP_CLK() 0ll
+#endif
+
+// Operand records are built from rows staged in shared memory in two steps, by the nthr threads tid0 .. tid0 + nthr - 1
+// of the CTA (whole warps).  BITS selects the layout.  rows: nb staged rows of K values (bf16 or fp32), records
+// r0 .. r0 + nb - 1.  umax: one float per (staged row, 256-value slab).
+// Step 1: the group sums of every row into its header, the largest magnitude of every slab into umax.
+template <int BITS, bool HILO, bool SRC_BF16>
+__device__ void records_sums(int nb, int r0, int K, uint8_t *recs, int rec_stride, const uint8_t *xs, float *umax, int tid0, int nthr) {
+    const int tid = threadIdx.x - tid0, lane = tid & 31, warp = tid >> 5, nwarp = nthr >> 5;
+    const int rowb = K * (SRC_BF16 ? 2 : 4), nsl = (K + 255) / 256;
+    const int hdr_off = (BITS == 3 ? sec3_bytes(K) : sec4_bytes(K)) * (HILO ? 2 : 1);
+    for (int it = warp; it < nb * nsl; it += nwarp) {
+        const int bl = it / nsl, sl = it - bl * nsl, base = sl * 256 + lane * 8;
+        float v[8];
+        const bool live = base < K;
+        if (live) row_vals<SRC_BF16, 8>(xs + (size_t)bl * rowb, base, v);
+        else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = 0.f;
+        }
+        float s = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7])), amax = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) amax = fmaxf(amax, fabsf(v[j]));
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        s += __shfl_xor_sync(0xffffffffu, s, 4);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (live && (lane & 7) == 0) reinterpret_cast<float *>(recs + (size_t)(r0 + bl) * rec_stride + hdr_off)[base >> 6] = s;
+        if (lane == 0) umax[it] = amax;
+    }
+}
+// Step 2 (after a barrier): the B fragments; one (row, unit, period) or (row, group, quad lane) item per thread and turn.
+template <int BITS, bool HILO, bool SRC_BF16>
+__device__ void records_frags(int nb, int r0, int K, uint8_t *recs, int rec_stride, const uint8_t *xs, const float *umax, int tid0, int nthr) {
+    const int tid = threadIdx.x - tid0;
+    const int rowb = K * (SRC_BF16 ? 2 : 4), nsl = (K + 255) / 256;
+    const int secb = BITS == 3 ? sec3_bytes(K) : sec4_bytes(K), hdr_off = secb * (HILO ? 2 : 1);
+    const int per_row = BITS == 3 ? (K / 128) * 4 : (K / 64) * 4;
+    for (int it = tid; it < nb * per_row; it += nthr) {
+        const int bl = it / per_row, q = it - bl * per_row;
+        float m = 0.f;
+        for (int j = 0; j < nsl; j++) m = fmaxf(m, umax[bl * nsl + j]);
+        int E = (int)(__float_as_uint(m) >> 23) + 1;
+        E = E < 30 ? 30 : (E > 230 ? 230 : E);
+        uint8_t *rec = recs + (size_t)(r0 + bl) * rec_stride;
+        if (q == 0) reinterpret_cast<float *>(rec + hdr_off)[K / 64] = __int_as_float(E);
+        if (BITS == 3) build_frag3_item<HILO, SRC_BF16>(xs + (size_t)bl * rowb, q >> 2, q & 3, E, rec, secb);
+        else build_frag4_item<HILO, SRC_BF16>(xs + (size_t)bl * rowb, q >> 2, q & 3, E, rec, secb);
+    }
+}
+// Brings rows r0 .. r0 + nb - 1 into the staging area: one bulk copy each, issued by the calling thread and
+// signalled on xbar (an mbarrier of count 1 that nothing else uses).  row_ptr(r): global address of row r (16-byte aligned).
+template <class RowPtr>
+__device__ __forceinline__ void records_fetch_rows(int nb, int r0, int rowb, uint8_t *xs, uint64_t *xbar, RowPtr row_ptr) {
+    fence_async_smem();
+    finch_mbar_expect_tx(xbar, (unsigned)(nb * rowb));
+    for (int i = 0; i < nb; i++) finch_bulk_g2s(xs + (size_t)i * rowb, row_ptr(r0 + i), (unsigned)rowb, xbar);
+}
+
+// Turns `nrec` rows of K values into operand records in shared memory, xs_rows rows at a time.  Run by the nthr threads
+// tid0 .. tid0 + nthr - 1, which share named barrier `bar`; the first of them brings the rows in.  xs_rows * nsl must
+// not exceed the floats of umax.
+template <int BITS, bool HILO, bool SRC_BF16, class RowPtr>
+__device__ void build_records(int nrec, int K, uint8_t *recs, int rec_stride, uint8_t *xs, int xs_rows, float *umax, uint64_t *xbar, int tid0,
+                              int nthr, int bar, unsigned tries, int *status, RowPtr row_ptr) {
+    const int tid = threadIdx.x - tid0;
+    const int rowb = K * (SRC_BF16 ? 2 : 4);
+    int round = 0;
+    for (int r0 = 0; r0 < nrec; r0 += xs_rows, ++round) {
+        const int nb = min(xs_rows, nrec - r0);
+        if (tid == 0) records_fetch_rows(nb, r0, rowb, xs, xbar, row_ptr);
+        if (!mbar_wait_lim(xbar, round & 1, tries) && (tid & 31) == 0) atomicExch(status, FINCH_E_TIMEOUT);
+        records_sums<BITS, HILO, SRC_BF16>(nb, r0, K, recs, rec_stride, xs, umax, tid0, nthr);
+        named_sync(bar, nthr);
+        records_frags<BITS, HILO, SRC_BF16>(nb, r0, K, recs, rec_stride, xs, umax, tid0, nthr);
+        named_sync(bar, nthr);
+    }
 }
 
 // ---- inner loops ---------------------------------------------------------
+// D = A(16x16, f16, row) * B(16x8, f16, col) + C.  Not volatile: a pure function of its operands.
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 // First MMA of a chain: C = 0 comes from the zero register, no accumulator initialisation needed.
 __device__ __forceinline__ void mma16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
         : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
 }
 
-// Shared-memory loads with a 32-bit address and an immediate offset: the inner loops keep a few running
-// addresses and spend no instructions on address arithmetic per load.
-template <int OFF>
+// Shared-memory loads by 32-bit address.  Volatile: they must stay behind the barrier wait that makes the stage
+// readable; constant offsets added by the caller are folded into the instruction's immediate.
 __device__ __forceinline__ uint2 lds64(uint32_t addr) {
     uint2 v;
-    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2+%3];" : "=r"(v.x), "=r"(v.y) : "r"(addr), "n"(OFF));
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
     return v;
 }
-template <int OFF>
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
     uint4 v;
-    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4+%5];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr), "n"(OFF));
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
     return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ void sts64f(uint32_t addr, float x, float y) {
+    asm volatile("st.shared.v2.f32 [%0], {%1,%2};" ::"r"(addr), "f"(x), "f"(y) : "memory");
+}
+// global -> shared bulk copy to a 32-bit shared address; src, dst 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void finch_bulk_g2s_a(uint32_t dst, const void *src, unsigned bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst), "l"(src), "r"(bytes),
+                 "r"(finch_smem_u32(bar))
+                 : "memory");
 }
 __device__ __forceinline__ float lds32f(uint32_t addr) {
     float v;
     asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
     return v;
 }
-constexpr int ZERO3_BYTES = 640;   // zeroed shared memory a lane with a structurally zero B column reads instead of a record
 
-// 3-bit tile (tile_layout.h) against up to two tokens.  Everything is in shared memory: the tile, the
-// operand records of the two tokens (frag0 / frag1 with their headers h0 / h1 = group sums, E) and
-// `zero`, ZERO3_BYTES of zeros.  On return lane (g, t), t even, holds for token slot t>>1 the dot
-// products resA (fragment row g) and resB (row g + 8), bias included, over units u0, u0 + ustep, ...
-__device__ __forceinline__ void gemv3_tile(const uint8_t *tile, int units, int u0, int ustep, int scale_dtype, const uint2 *frag0,
-                                           const uint2 *frag1, const float *h0, const float *h1, const void *zero, int ntok,
-                                           float &resA, float &resB) {
-    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int tokslot = g >> 2, term = (g >> 1) & 1;
-    const bool bact = ((g & 1) == (t >> 1)) && tokslot < ntok;
-    // lanes whose B column is structurally zero walk a block of zeros with unit stride 0: no select, no moves
-    uint32_t pb = (bact ? finch_smem_u32(tokslot ? frag1 : frag0) + (uint32_t)u0 * 576u : finch_smem_u32(zero)) + (uint32_t)(term * 4 + t) * 8u;
-    const uint32_t sb_step = bact ? (uint32_t)ustep * 576u : 0u;
-    const uint32_t h32 = finch_smem_u32((t >> 1) ? h1 : h0);  // token whose result this lane's accumulator columns hold
-    const uint32_t tile32 = finch_smem_u32(tile);
-    uint32_t pw = tile32 + (uint32_t)(u0 * 32 + lane) * 24u, ps = tile32 + (uint32_t)units * 768u + (uint32_t)(u0 * 8 + g) * 16u;
-    uint32_t ph = h32 + (uint32_t)u0 * 8u;
-    float runA = 0.f, runB = 0.f, biasA = 0.f, biasB = 0.f;
-    for (int u = u0; u < units; u += ustep) {
-        uint2 b[9];
-        b[0] = lds64<0>(pb);   b[1] = lds64<64>(pb);  b[2] = lds64<128>(pb);
-        b[3] = lds64<192>(pb); b[4] = lds64<256>(pb); b[5] = lds64<320>(pb);
-        b[6] = lds64<384>(pb); b[7] = lds64<448>(pb); b[8] = lds64<512>(pb);
-        const uint2 q0 = lds64<0>(pw), q1 = lds64<8>(pw), q2 = lds64<16>(pw);
-        const uint4 s = lds128<0>(ps);
-        const uint2 xgb = lds64<0>(ph);
-        const float2 xg = make_float2(__uint_as_float(xgb.x), __uint_as_float(xgb.y));
-        pb += sb_step;
-        pw += (uint32_t)ustep * 768u;
-        ps += (uint32_t)ustep * 128u;
-        ph += (uint32_t)ustep * 8u;
-        // row A words q0.x q0.y q1.x, row B words q1.y q2.x q2.y; the shifted views of extract3
-        const uint32_t av1 = __funnelshift_r(q0.x, q0.y, 8), av3 = __funnelshift_r(q0.y, q1.x, 8), av5 = q1.x >> 8;
-        const uint32_t bv1 = __funnelshift_r(q1.y, q2.x, 8), bv3 = __funnelshift_r(q2.x, q2.y, 8), bv5 = q2.y >> 8;
-        float acc[2][4];  // two independent accumulator chains
-#define FINCH_MMA3(j)                                                                                                     \
+template <bool FP16S>
+__device__ __forceinline__ void widen2(uint32_t w, float &lo, float &hi) {
+    if (FP16S) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w));
+        lo = f.x;
+        hi = f.y;
+    } else {
+        lo = __uint_as_float(w << 16);
+        hi = __uint_as_float(w & 0xffff0000u);
+    }
+}
+
+// One 128-code unit of a 3-bit piece against the four virtual columns of a pass.
+//   pw   this lane's 24 bytes of the unit's weights (3 words of fragment row g, 3 of row g + 8)
+//   ps   the 16-byte scale / bias entry of rows g, g + 8
+//   pb   this lane's B entries: the unit's section of the record of virtual column g >> 1 (or of the zero
+//        record when the lane's k-slots belong to the other group or the column is unused), + t * 16
+//   pb8  the same + 256 + t * 8 (the ninth MMA's entry)
+//   ph   the two group sums of the unit in the header of the token whose result this lane's accumulator
+//        columns (virtual column t) hold
+// run / bias accumulate sum_g s_g * (sum q x') and sum_g b_g * (sum x) for rows g (A) and g + 8 (B).
+template <bool FP16S>
+__device__ __forceinline__ void gemv3_unit(uint32_t pw, uint32_t ps, uint32_t pb, uint32_t pb8, uint32_t ph, float &runA, float &runB,
+                                           float &biasA, float &biasB) {
+    const uint4 b01 = lds128(pb), b23 = lds128(pb + 64), b45 = lds128(pb + 128), b67 = lds128(pb + 192);
+    const uint2 b8 = lds64(pb8);
+    const uint2 q0 = lds64(pw), q1 = lds64(pw + 8), q2 = lds64(pw + 16);
+    const uint4 s = lds128(ps);
+    const uint2 xgb = lds64(ph);
+    // row A words q0.x q0.y q1.x, row B words q1.y q2.x q2.y; the shifted views of the extraction
+    const uint32_t av1 = __funnelshift_r(q0.x, q0.y, 8), av3 = __funnelshift_r(q0.y, q1.x, 8), av5 = q1.x >> 8;
+    const uint32_t bv1 = __funnelshift_r(q1.y, q2.x, 8), bv3 = __funnelshift_r(q2.x, q2.y, 8), bv5 = q2.y >> 8;
+    float acc[4];
+#define FINCH_MMA3(j, B0, B1)                                                                                             \
     {                                                                                                                     \
         const uint32_t a0 = extract3_one<2 * (j)>(q0.x, av1, q0.y, av3, q1.x, av5);                                       \
         const uint32_t a1 = extract3_one<2 * (j)>(q1.y, bv1, q2.x, bv3, q2.y, bv5);                                       \
         const uint32_t a2 = extract3_one<2 * (j) + 1>(q0.x, av1, q0.y, av3, q1.x, av5);                                   \
         const uint32_t a3 = extract3_one<2 * (j) + 1>(q1.y, bv1, q2.x, bv3, q2.y, bv5);                                   \
-        if ((j) < 2) mma16816_z(acc[(j) & 1], a0, a1, a2, a3, b[j].x, b[j].y);                                            \
-        else finch_mma16816(acc[(j) & 1], a0, a1, a2, a3, b[j].x, b[j].y);                                                \
+        if ((j) == 0) mma16816_z(acc, a0, a1, a2, a3, B0, B1);                                                            \
+        else mma16816(acc, a0, a1, a2, a3, B0, B1);                                                                       \
     }
-        FINCH_MMA3(0) FINCH_MMA3(1) FINCH_MMA3(2) FINCH_MMA3(3) FINCH_MMA3(4) FINCH_MMA3(5) FINCH_MMA3(6) FINCH_MMA3(7) FINCH_MMA3(8)
+    FINCH_MMA3(0, b01.x, b01.y) FINCH_MMA3(1, b01.z, b01.w) FINCH_MMA3(2, b23.x, b23.y) FINCH_MMA3(3, b23.z, b23.w)
+    FINCH_MMA3(4, b45.x, b45.y) FINCH_MMA3(5, b45.z, b45.w) FINCH_MMA3(6, b67.x, b67.y) FINCH_MMA3(7, b67.z, b67.w)
+    FINCH_MMA3(8, b8.x, b8.y)
 #undef FINCH_MMA3
-        float s0, s1;
-        finch_widen16x2(s.x, scale_dtype, s0, s1);
-        runA = fmaf(s0, acc[0][0] + acc[1][0], runA);
-        runA = fmaf(s1, acc[0][1] + acc[1][1], runA);
-        finch_widen16x2(s.y, scale_dtype, s0, s1);
-        runB = fmaf(s0, acc[0][2] + acc[1][2], runB);
-        runB = fmaf(s1, acc[0][3] + acc[1][3], runB);
-        finch_widen16x2(s.z, scale_dtype, s0, s1);
-        biasA = fmaf(s0, xg.x, biasA);
-        biasA = fmaf(s1, xg.y, biasA);
-        finch_widen16x2(s.w, scale_dtype, s0, s1);
-        biasB = fmaf(s0, xg.x, biasB);
-        biasB = fmaf(s1, xg.y, biasB);
-    }
-    // accumulator columns of lane t: token slot t>>1, term t&1 -> hi in even t, lo in odd t
-    const float fac = pow2_biased(__float_as_int(lds32f(h32 + (uint32_t)units * 8u)) + 17);
-    const float oA = __shfl_xor_sync(0xffffffffu, runA, 1), oB = __shfl_xor_sync(0xffffffffu, runB, 1);
-    resA = fmaf(runA + oA * (1.0f / 2048.0f), fac, biasA);
-    resB = fmaf(runB + oB * (1.0f / 2048.0f), fac, biasB);
+    const float x0 = __uint_as_float(xgb.x), x1 = __uint_as_float(xgb.y);
+    float s0, s1;
+    widen2<FP16S>(s.x, s0, s1);
+    runA = fmaf(s0, acc[0], runA);
+    runA = fmaf(s1, acc[1], runA);
+    widen2<FP16S>(s.y, s0, s1);
+    runB = fmaf(s0, acc[2], runB);
+    runB = fmaf(s1, acc[3], runB);
+    widen2<FP16S>(s.z, s0, s1);
+    biasA = fmaf(s0, x0, biasA);
+    biasA = fmaf(s1, x1, biasA);
+    widen2<FP16S>(s.w, s0, s1);
+    biasB = fmaf(s0, x0, biasB);
+    biasB = fmaf(s1, x1, biasB);
 }
 
-// 4-bit tile of the prepared shared expert (tile_layout.h) against up to two tokens (columns 0..3 =
-// token 0 hi/lo, token 1 hi/lo).  chunk: index of this lane's 16-byte operand chunk inside a group
-// (lane for a 16-row tile, (g&3)*4+t for a 4+4-row tile), per_group: chunks per group (32 / 16),
-// sidx / s_per_group: the same for the 8-byte scale/bias entries.  Lane (g, t) with t < 2 returns
-// the finished dot products of its two fragment rows for token t.
-__device__ __forceinline__ void gemv4_tile(const uint8_t *tile, int groups, int g0, int gstep, int chunk, int per_group, int sidx, int s_per_group,
-                                           int scale_dtype, const uint2 *frag0, const uint2 *frag1, const float *h0, const float *h1,
-                                           const uint2 *zero, int ntok, float &resA, float &resB) {
-    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int tok = g >> 1, term = g & 1;
-    const bool bact = tok < ntok;  // ntok <= 2
-    const uint2 *fb = bact ? (tok ? frag1 : frag0) + term * 4 + t : zero;
-    const int fstride = bact ? 8 : 0;
-    const float *h = (t & 1) ? h1 : h0;
-    const uint8_t *sb = tile + (size_t)groups * per_group * 16;
-    float runA = 0.f, runB = 0.f, biasA = 0.f, biasB = 0.f;
-    for (int gm = g0; gm < groups; gm += gstep) {
-        uint2 b[4];
+// nu consecutive units of a piece: weights [nu][32][24 B], scale / bias entries [nu][8][16 B].  pw, ps: this lane's
+// words of the first unit (+ lane * 24, + g * 16); pb: the section of its B column at the first unit.
+template <bool FP16S>
+__device__ __forceinline__ void gemv3_piece(uint32_t pw, uint32_t ps, int nu, uint32_t pb, uint32_t ph, float &runA, float &runB, float &biasA,
+                                            float &biasB) {
+    const int t = threadIdx.x & 3;
+    const uint32_t pb16 = pb + t * 16, pb8 = pb + 256 + t * 8;
+    runA = runB = biasA = biasB = 0.f;
+    if (nu == 4) {
 #pragma unroll
-        for (int j = 0; j < 4; j++) b[j] = fb[(gm * 4 + j) * fstride];
-        const uint4 w = *reinterpret_cast<const uint4 *>(tile + (size_t)(gm * per_group + chunk) * 16);
-        const uint2 s = *reinterpret_cast<const uint2 *>(sb + (size_t)(gm * s_per_group + sidx) * 8);
-        const float xg = h[gm];
+        for (int u = 0; u < 4; u++) gemv3_unit<FP16S>(pw + u * 768, ps + u * 128, pb16 + u * UB, pb8 + u * UB, ph + u * 8, runA, runB, biasA, biasB);
+    } else {
+        for (int u = 0; u < nu; u++) gemv3_unit<FP16S>(pw + u * 768, ps + u * 128, pb16 + u * UB, pb8 + u * UB, ph + u * 8, runA, runB, biasA, biasB);
+    }
+}
+
+// ngr 64-code groups of a 4-bit piece against the eight columns of a pass.
+//   pw / wstep   this lane's 16-byte chunk of the first group, bytes per group
+//   ps / sstep   the 8-byte scale / bias entry (scale row A, scale row B, bias row A, bias row B as u16)
+//   pb / bstep   this lane's B entries (record section of column g, + t * 16), bytes per group (0 for the zero block)
+//   ph0, ph1     the group sums in the headers of the tokens of accumulator columns 2t and 2t + 1
+// r[0..3] / bias[0..3]: (row A, col 2t) (row A, col 2t+1) (row B, col 2t) (row B, col 2t+1).
+template <bool FP16S>
+__device__ __forceinline__ void gemv4_piece(uint32_t pw, int wstep, uint32_t ps, int sstep, int ngr, uint32_t pb, int bstep, uint32_t ph0,
+                                            uint32_t ph1, float (&r)[4], float (&bias)[4]) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) r[i] = bias[i] = 0.f;
+    for (int gm = 0; gm < ngr; gm++) {
+        const uint4 b01 = lds128(pb), b23 = lds128(pb + 64);
+        const uint4 w = lds128(pw);
+        const uint2 s = lds64(ps);
+        const float x0 = lds32f(ph0), x1 = lds32f(ph1);
+        pb += bstep;
+        pw += wstep;
+        ps += sstep;
+        ph0 += 4;
+        ph1 += 4;
         uint32_t ea[8], eb[8];
         {
             uint32_t x[4];
@@ -466,24 +545,23 @@ __device__ __forceinline__ void gemv4_tile(const uint8_t *tile, int groups, int 
             extract4(w.z, x); eb[0] = x[0]; eb[1] = x[1]; eb[2] = x[2]; eb[3] = x[3];
             extract4(w.w, x); eb[4] = x[0]; eb[5] = x[1]; eb[6] = x[2]; eb[7] = x[3];
         }
-        float acc[2][4];
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            if (j < 2) mma16816_z(acc[j], ea[2 * j], eb[2 * j], ea[2 * j + 1], eb[2 * j + 1], b[j].x, b[j].y);
-            else finch_mma16816(acc[j & 1], ea[2 * j], eb[2 * j], ea[2 * j + 1], eb[2 * j + 1], b[j].x, b[j].y);
-        }
-        // accumulator columns 2t, 2t+1 = (token t, hi), (token t, lo)
+        float acc[4];
+        mma16816_z(acc, ea[0], eb[0], ea[1], eb[1], b01.x, b01.y);
+        mma16816(acc, ea[2], eb[2], ea[3], eb[3], b01.z, b01.w);
+        mma16816(acc, ea[4], eb[4], ea[5], eb[5], b23.x, b23.y);
+        mma16816(acc, ea[6], eb[6], ea[7], eb[7], b23.z, b23.w);
         float s0, s1, b0, b1;
-        finch_widen16x2(s.x, scale_dtype, s0, s1);  // scale of row A, of row B
-        finch_widen16x2(s.y, scale_dtype, b0, b1);  // bias of row A, of row B
-        runA = fmaf(s0, (acc[0][0] + acc[1][0]) + (acc[0][1] + acc[1][1]) * (1.0f / 2048.0f), runA);
-        runB = fmaf(s1, (acc[0][2] + acc[1][2]) + (acc[0][3] + acc[1][3]) * (1.0f / 2048.0f), runB);
-        biasA = fmaf(b0, xg, biasA);
-        biasB = fmaf(b1, xg, biasB);
+        widen2<FP16S>(s.x, s0, s1);  // scale of row A, of row B
+        widen2<FP16S>(s.y, b0, b1);  // bias of row A, of row B
+        r[0] = fmaf(s0, acc[0], r[0]);
+        r[1] = fmaf(s0, acc[1], r[1]);
+        r[2] = fmaf(s1, acc[2], r[2]);
+        r[3] = fmaf(s1, acc[3], r[3]);
+        bias[0] = fmaf(b0, x0, bias[0]);
+        bias[1] = fmaf(b0, x1, bias[1]);
+        bias[2] = fmaf(b1, x0, bias[2]);
+        bias[3] = fmaf(b1, x1, bias[3]);
     }
-    const float fac = pow2_biased(__float_as_int(h[groups]) + 17);
-    resA = fmaf(runA, fac, biasA);
-    resB = fmaf(runB, fac, biasB);
 }
 
 // ---- expert groups -------------------------------------------------------
@@ -494,10 +572,31 @@ __device__ __forceinline__ bool pair_ok(const MoeArgs &a, int p) {
     return a.slot_row[e] >= 0;
 }
 
-// Builds the group table in shared memory.  Run by threads 0..nthreads-1 (nthreads >= 64, whole
-// warps) sharing named barrier `bar`; the first two warps hold one pair per lane.  Groups are
-// numbered by their first pair; pairs inside a group ascend.  sm_ids: MAXP + 2 ints.
-__device__ void build_groups(const MoeArgs &a, GroupTab *T, int *sm_ids, unsigned char *sm_rank, int bar, int nthreads) {
+// Jobs of the down kernel are laid out group-major: job = gi * per_group + tile.  Every routed CTA takes one
+// contiguous range, balanced by cost (a job of a group costs its pass count).  The job whose cost interval
+// starts at or after `target`.
+__device__ int job_at(const int *pre, int ng, int per_group, int target) {
+    if (target >= pre[ng] * per_group) return ng * per_group;
+    int lo = 0, hi = ng - 1;   // last group whose first job starts at or before target
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (pre[mid] * per_group <= target) lo = mid;
+        else hi = mid - 1;
+    }
+    const int gi = lo, np = pre[gi + 1] - pre[gi];
+    return gi * per_group + (target - pre[gi] * per_group + np - 1) / np;
+}
+
+// Builds the group table in shared memory.  Run by the first two warps of the CTA (one pair per lane), which
+// share named barrier BAR_GROUPS.  Groups are numbered by their first pair; pairs inside a group ascend.
+// per_pass: pairs a pass serves (2 or 4); T->pre gets the prefix sums of the groups' pass counts.
+// col (optional, [MAXP][MAXM]): shared address of the operand record of the token of every (group, pair of
+// the group), rec32 + token * rstride, or 0 where the group has no such pair.
+// sm_ids: MAXP + 2 ints, sm_rank: MAXP bytes of scratch.
+// bound (optional, nbound + 1 ints): boundaries of nbound cost-balanced contiguous ranges of the group-major tile list
+// (per_group tiles per group) for the teams first_team .. first_team + nbound - 1 of n_teams.
+__device__ void build_groups(const MoeArgs &a, GroupTab *T, int *sm_ids, unsigned char *sm_rank, int per_pass, uint32_t *col, uint32_t rec32,
+                             int rstride, int *bound = nullptr, int nbound = 0, int first_team = 0, int n_teams = 1, int per_group = 1) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     int id = -1, slot = -1;
     if (tid < a.P) {
@@ -509,150 +608,60 @@ __device__ void build_groups(const MoeArgs &a, GroupTab *T, int *sm_ids, unsigne
             if (slot >= 0) id = e;
         }
     }
-    if (tid < MAXP) sm_ids[tid] = id;
-    bar_sync(bar, nthreads);
+    sm_ids[tid] = id;
+    if (col)
+        for (int i = tid; i < MAXP * MAXM; i += 64) col[i] = 0u;
+    named_sync(BAR_GROUPS, 64);
     unsigned same = 0, other = 0, fb = 0;
     bool first = false;
-    if (tid < MAXP) {
-        same = __match_any_sync(0xffffffffu, id);                 // lanes of my warp with my expert
-        const int *o = sm_ids + 32 * (warp ^ 1);
-        for (int j = 0; j < 32; j++) other |= (unsigned)(o[j] == id) << j;   // lanes of the other warp
-        const unsigned lt = (1u << lane) - 1u;
-        first = id >= 0 && !(same & lt) && (warp == 0 || other == 0);
-        fb = __ballot_sync(0xffffffffu, first);
-        if (lane == 0) sm_ids[MAXP + warp] = (int)fb;
-    }
-    bar_sync(bar, nthreads);
-    if (tid < MAXP) {
-        const unsigned lt = (1u << lane) - 1u;
-        const int before = warp == 1 ? __popc((unsigned)sm_ids[MAXP]) : 0;
-        if (first) sm_rank[tid] = (unsigned char)(before + __popc(fb & lt));
-        if (tid == 0) T->ng = __popc((unsigned)sm_ids[MAXP]) + __popc((unsigned)sm_ids[MAXP + 1]);
-    }
-    bar_sync(bar, nthreads);
-    if (tid < MAXP && id >= 0) {
-        const unsigned lt = (1u << lane) - 1u;
+    same = __match_any_sync(0xffffffffu, id);                 // lanes of my warp with my expert
+    const int *o = sm_ids + 32 * (warp ^ 1);
+    for (int j = 0; j < 32; j++) other |= (unsigned)(o[j] == id) << j;   // lanes of the other warp
+    const unsigned lt = (1u << lane) - 1u;
+    first = id >= 0 && !(same & lt) && (warp == 0 || other == 0);
+    fb = __ballot_sync(0xffffffffu, first);
+    if (lane == 0) sm_ids[MAXP + warp] = (int)fb;
+    named_sync(BAR_GROUPS, 64);
+    const int before = warp == 1 ? __popc((unsigned)sm_ids[MAXP]) : 0;
+    if (first) sm_rank[tid] = (unsigned char)(before + __popc(fb & lt));
+    const int ng = __popc((unsigned)sm_ids[MAXP]) + __popc((unsigned)sm_ids[MAXP + 1]);
+    if (tid == 0) T->ng = ng;
+    named_sync(BAR_GROUPS, 64);
+    int np = 0;   // passes of group `tid`
+    if (id >= 0) {
         const int fp = (warp == 1 && other) ? __ffs(other) - 1 : 32 * warp + __ffs(same) - 1;   // first pair of my group
         const int gi = sm_rank[fp];
         const int pos = (warp == 1 ? __popc(other) : 0) + __popc(same & lt);
-        if (pos < MAXM) T->pairs[gi][pos] = (unsigned char)tid;
+        if (pos < MAXM) {
+            T->pairs[gi][pos] = (unsigned char)tid;
+            if (col) col[gi * MAXM + pos] = rec32 + (uint32_t)((tid / a.K) * rstride);
+        }
         if (first) {
             const int m = __popc(same) + __popc(other);
             T->m[gi] = (unsigned char)(m < MAXM ? m : MAXM);
             T->slot[gi] = slot;
         }
     }
-    bar_sync(bar, nthreads);
-}
-
-// ---- work distribution ---------------------------------------------------
-// Jobs (one tile against the tokens of its group) are laid out group-major:
-// job = gi * per_group + tile for the routed experts, then the shared-expert
-// tiles.  Every CTA takes one contiguous range, balanced by cost (a job of a
-// group with m pairs costs ceil(m/2) passes).  Contiguous ranges keep the
-// groups a CTA touches few: few act records to prepare.
-__device__ __forceinline__ int npass_of(const GroupTab *tab, int gi) { return (tab->m[gi] + 1) >> 1; }
-
-// pre[gi] = passes of the groups before gi (32-bit: at most 64 groups x 4 passes).  The job whose
-// cost interval starts at or after `target` (cost units: tile-passes).
-__device__ int job_at(const int *pre, int ng, int per_group, int n_sh, int nps, int target) {
-    const int routed_cost = pre[ng] * per_group;
-    if (target >= routed_cost) {
-        if (n_sh > 0 && target < routed_cost + n_sh * nps) return ng * per_group + (target - routed_cost + nps - 1) / nps;
-        return ng * per_group + n_sh;
-    }
-    int lo = 0, hi = ng - 1;   // last group whose first job starts at or before target
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (pre[mid] * per_group <= target) lo = mid;
-        else hi = mid - 1;
-    }
-    const int gi = lo, np = pre[gi + 1] - pre[gi];
-    return gi * per_group + (target - pre[gi] * per_group + np - 1) / np;
-}
-
-// How many CTAs at the end of the grid take the shared expert's jobs (`units` jobs each).  A CTA whose range
-// crosses from routed to shared-expert jobs would finish last: its consumer units (teams or warps, `units` of
-// them, one job at a time each) are dealt its jobs round robin, and a shared-expert job - every token, so
-// several passes - lands on a unit that already has its share of routed ones.  So with three tokens or more
-// (two passes per shared job) the boundary is put on a CTA boundary and every shared CTA gets one job per
-// unit.  Returns -1 where that does not apply (no shared expert, one pass per job, a grid too small to split):
-// ranges are proportional to cost then.
-__device__ __forceinline__ int shared_ctas(int grid, int units, int n_sh, int nps) {
-    if (n_sh == 0 || nps < 2) return -1;
-    const int gs = (n_sh + units - 1) / units;
-    return gs < grid ? gs : -1;
-}
-
-// start of CTA i's range under that split
-__device__ int range_start(const int *pre, int ng, int per_group, int n_sh, int nps, int grid, int gs, int per, int i) {
-    const int routed_cost = pre[ng] * per_group, n_routed = ng * per_group;
-    if (gs < 0) return job_at(pre, ng, per_group, n_sh, nps, (int)((long long)(routed_cost + n_sh * nps) * i / grid));
-    const int gr = grid - gs;
-    if (i <= gr) return job_at(pre, ng, per_group, 0, 1, (int)((long long)routed_cost * i / gr));
-    const int j = (i - gr) * per;
-    return n_routed + (j < n_sh ? j : n_sh);
-}
-
-// ============================ prep ========================================
-// grid: B + 1 CTAs of 256 threads.  CTA b < B: operand records of token b.  CTA B: groups and ranges.
-__global__ void __launch_bounds__(256) moe_prep_kernel(const MoeArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    float *xs = reinterpret_cast<float *>(smem);
-    float *hdr = xs + a.hidden;              // [hidden/64 + 1]
-    float *warp_max = hdr + 144;
-    int *sm_ids = reinterpret_cast<int *>(warp_max + 8);
-    unsigned char *sm_first = reinterpret_cast<unsigned char *>(sm_ids + MAXP + 2);
-    GroupTab *T = reinterpret_cast<GroupTab *>(sm_first + MAXP + 8);
-    const int b = blockIdx.x, tid = threadIdx.x, K = a.hidden;
-    const long long gt0 = gtime();
-    grid_dep_launch();
-    grid_dep_wait();
-    if (a.dbg && tid == 0) a.dbg[(size_t)(1300 + b) * 8] = gt0, a.dbg[(size_t)(1300 + b) * 8 + 1] = gtime();
-    if (b < a.B) {
-        const void *src = a.act_dtype == FINCH_BF16 ? (const void *)((const uint16_t *)a.h_post + (size_t)b * K)
-                                                     : (const void *)((const float *)a.h_post + (size_t)b * K);
-        load_x<256>(src, a.act_dtype, K, xs, hdr, warp_max, 0);
-        const int E = __float_as_int(hdr[K / 64]);
-        uint8_t *rec = a.xrec3 + (size_t)b * rec3_bytes(K);
-        build_frag3<256>(xs, K, E, reinterpret_cast<uint2 *>(rec));
-        if (a.has_shared) build_frag4<256>(xs, K, E, reinterpret_cast<uint2 *>(a.xrec4 + (size_t)b * frag4_bytes(K)));
-        float *gh = reinterpret_cast<float *>(rec + frag3_bytes(K));
-        for (int i = tid; i <= K / 64; i += 256) gh[i] = hdr[i];
-        if (a.dbg && tid == 0) a.dbg[(size_t)(1300 + b) * 8 + 2] = gtime();
-        return;
-    }
-    build_groups(a, T, sm_ids, sm_first, 0, 256);
-    // job ranges of the two streaming kernels (thread i computes the start of CTA i)
-    const FinchTile L3 = finch_tile(a.hidden, a.inter);
-    const int nps = (a.B + 1) / 2;
-    const int n_sh_a = a.has_shared ? a.sh_inter / 4 : 0, n_sh_b = a.has_shared ? L3.nTB : 0;
-    int *pre = sm_ids;  // the pair ids are no longer needed: reuse as prefix sums of the groups' passes
-    const int ng = T->ng;
-    if (tid < 64) {   // exclusive scan of the per-group pass counts over two warps
-        const int lane = tid & 31, np = tid < ng ? npass_of(T, tid) : 0;
-        int inc = np;
+    named_sync(BAR_GROUPS, 64);
+    // exclusive scan of the per-group pass counts over the two warps
+    np = tid < ng ? (T->m[tid] + per_pass - 1) / per_pass : 0;
+    int inc = np;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int v = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc += v;
-        }
-        if (tid == 31) pre[MAXP + 1] = inc;   // total of the first warp
-        __syncwarp();
-        pre[tid] = inc - np;
-        if (tid == 63) pre[MAXP] = inc;
+    for (int d = 1; d < 32; d <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, inc, d);
+        if (lane >= d) inc += v;
     }
-    __syncthreads();
-    if (tid >= 32 && tid < 65) pre[tid] += pre[MAXP + 1];   // tid 64 fixes up the grand total in pre[MAXP]
-    __syncthreads();
-    const int gs_a = shared_ctas(a.grid_a, NTEAM_A, n_sh_a, nps), gs_b = shared_ctas(a.grid_b, CW_B, n_sh_b, nps);
-    for (int i = tid; i <= a.grid_a; i += 256) T->range_a[i] = range_start(pre, ng, L3.nTA, n_sh_a, nps, a.grid_a, gs_a, NTEAM_A, i);
-    for (int i = tid; i <= a.grid_b; i += 256) T->range_b[i] = range_start(pre, ng, L3.nTB, n_sh_b, nps, a.grid_b, gs_b, CW_B, i);
-    __syncthreads();
-    const int *s = reinterpret_cast<const int *>(T);
-    int *d = reinterpret_cast<int *>(a.gtab);
-    for (int i = tid; i < (int)(sizeof(GroupTab) / 4); i += 256) d[i] = s[i];
-    if (a.dbg && tid == 0) a.dbg[(size_t)(1300 + b) * 8 + 2] = gtime();
+    if (tid == 31) sm_ids[0] = inc;   // total of the first warp
+    named_sync(BAR_GROUPS, 64);
+    const int add = warp == 1 ? sm_ids[0] : 0;
+    T->pre[tid] = inc - np + add;
+    if (tid == 63) T->pre[64] = inc + add;
+    named_sync(BAR_GROUPS, 64);
+    if (bound && tid <= nbound) {
+        // total <= 64 groups * 4 passes * tiles per group and the team count is a few thousand: the products fit 32 bits
+        const unsigned total = (unsigned)(T->pre[ng] * per_group);
+        bound[tid] = job_at(T->pre, ng, per_group, (int)(total * (unsigned)(first_team + tid) / (unsigned)n_teams));
+    }
 }
 
 // Re-tiles a shared expert from the reference tensor layout into FinchTile4 tiles (run once per
@@ -698,440 +707,532 @@ __global__ void shared_retile_kernel(SharedSrc S, int hidden, int inter, uint8_t
     }
 }
 
-// ============================ kernel A ====================================
-__host__ __device__ inline int up128(int x) { return (x + 127) & ~127; }
-// Stage s of a ring is used by whichever consumer the job order assigns, and the producer lanes of different
-// stages run independently, so a consumer can be ready for the n-th fill of a stage while the job of its
-// (n-1)-th fill is still in progress (or that fill has not even been issued).  An mbarrier cannot tell these
-// apart: a barrier one phase behind reports the awaited phase's parity as complete.  So every stage carries a
-// count of the jobs consumed from it, and a consumer waits for the barrier only once that count says the
-// previous fill has been used up.  Bounded like every other wait here.
-__device__ __forceinline__ bool wait_consumed(const int *cnt, int want) {
-    const volatile int *c = cnt;
-    for (unsigned i = 0; i < (1u << 22); ++i) {
-        if (*c >= want) return true;
-        __nanosleep(40);
-    }
-    return false;
-}
-
+// ============================ gate / up ===================================
+// Shared memory of a gate/up CTA.  stage: [2][warps][stg]; while the records are built the second half
+// (every warp's stage 1) is the staging area of the rows.
 struct SmemA {
-    int stage, stg, rec, rx3, rec4, f4s, n4, red, qcnt, tab, zero, bar, total;
+    int stage, stg, rec, rstride, zero, red, umax, tab, col, ids, rank, sync, bar, total;
 };
-__host__ __device__ inline SmemA smem_a_layout(int hidden, int inter, int sh_inter, int B, int has_shared, int stages) {
+__host__ __device__ inline SmemA smem_a_layout(int hidden, int inter, int sh_inter, int B, int has_shared, int hilo, int nwarps) {
     const FinchTile T = finch_tile(hidden, inter);
-    const FinchTile4 T4 = finch_tile4(hidden, sh_inter);
+    const int upq = (T.unitsA + TEAM - 1) / TEAM, gq = (hidden / 64 + TEAM - 1) / TEAM;
+    (void)sh_inter;
     SmemA L;
     L.stage = 0;
-    L.stg = up128(has_shared && T4.tileA > T.tileA ? T4.tileA : T.tileA);
-    L.rec = L.stage + stages * L.stg;         // operand records of all tokens (3-bit layout)
-    L.rx3 = rec3_bytes(hidden);
-    L.rec4 = up128(L.rec + B * L.rx3);        // 4-bit-layout fragments of the first n4 tokens (the rest stay in global memory)
-    L.f4s = frag4_bytes(hidden) + 64;
-    L.n4 = has_shared ? (B < 2 ? B : 2) : 0;
-    L.red = up128(L.rec4 + L.n4 * L.f4s);
-    L.qcnt = L.red + stages * (MAXM / 2) * TEAM_A * 32 * 4;   // per stage: [pass][warp][32] partial sums
-    L.tab = L.qcnt + 64 * 4;                                  // + jobs consumed per stage
-    L.zero = up128(L.tab + (int)sizeof(GroupTab));
-    L.bar = L.zero + ZERO3_BYTES;
-    L.total = L.bar + 2 * 32 * 8 + 16 + 16;
+    L.stg = up128(upq * 896 > (has_shared ? gq * 288 : 0) ? upq * 896 : gq * 288);
+    L.rec = L.stage + 2 * nwarps * L.stg;
+    const int r3 = rec3_bytes(hidden, hilo), r4 = has_shared ? rec4_bytes(hidden, hilo) : 0;
+    L.rstride = r3 > r4 ? r3 : r4;
+    // the zero record sits 64 bytes off the records' 128-byte grid: a lane reading zeros and a lane reading the
+    // same offset of a record then never share a bank
+    L.zero = L.rec + B * L.rstride + 64;
+    L.red = L.zero + sec3_bytes(hidden) + 64;
+    L.umax = L.red + (nwarps / TEAM) * TEAM * MAXM * 64;      // per team: [4 K-quarters][8 tokens][8 g][gate | up] floats
+    L.tab = L.umax + 8 * ((hidden + 255) / 256) * 4;
+    L.col = L.tab + (((int)sizeof(GroupTab) + 15) & ~15);     // [group][pair of the group]: shared address of the token's record, or 0
+    L.ids = L.col + MAXP * MAXM * 4;
+    L.rank = L.ids + (MAXP + 2) * 4;
+    L.sync = (L.rank + MAXP + 7) & ~7;                        // per team: partial sums written, reductions done
+    L.bar = L.sync + 4 * (NW_MAX / TEAM) * 4;                 // + the boundaries of the teams' tile ranges
+    L.total = L.bar + (2 * NW_MAX + 1) * 8;
     return L;
 }
 
-// grid: one CTA per SM (persistent); block: NTEAM_A teams of TEAM_A consumer warps + 1 producer warp.
-// A team takes whole tiles; its warps split the K dimension and one of them adds the partial sums.
-__global__ void __launch_bounds__(NT_A, 1) moe_gateup_kernel(const MoeArgs a) {
+// What a warp of the gate/up kernel works on: its K-quarter of every tile of its team's range.
+struct WarpJobA {
+    int u0, nu, nkw;   // first unit / units of the quarter (groups for the shared expert), quarters that exist
+    int j0, j1, step;  // tiles j0, j0 + step, ... < j1
+};
+// bound: the routed teams' range boundaries left by build_groups.
+__device__ __forceinline__ WarpJobA warp_job_a(bool routed, int units, int n_tiles_shared, int cta, int Gr, int gs, int nteam, int w, const int *bound) {
+    WarpJobA J;
+    const int team = w / TEAM, kw = w % TEAM, upq = (units + TEAM - 1) / TEAM;
+    J.u0 = kw * upq;
+    J.nu = min(upq, units - J.u0);
+    J.nkw = (units + upq - 1) / upq;
+    if (routed) {
+        J.j0 = bound[team];
+        J.j1 = bound[team + 1];
+        J.step = 1;
+    } else {
+        J.j0 = (cta - Gr) * nteam + team;
+        J.j1 = n_tiles_shared;
+        J.step = gs * nteam;
+    }
+    return J;
+}
+
+// grid: one CTA per SM (persistent); block: nteam teams of TEAM warps.
+template <bool HILO, bool FP16S>
+__global__ void __launch_bounds__(NW_MAX * 32, 1) moe_gateup_kernel(const MoeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const long long tk0 = clock64(), gt0 = gtime();
-    const int Smax = a.stages_a;
-    const SmemA L = smem_a_layout(a.hidden, a.inter, a.sh_inter, a.B, a.has_shared, Smax);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+    const int nwarps = blockDim.x >> 5, nteam = nwarps / TEAM;
+    const SmemA L = smem_a_layout(a.hidden, a.inter, a.sh_inter, a.B, a.has_shared, HILO, nwarps);
     const FinchTile T = finch_tile(a.hidden, a.inter);
     const FinchTile4 T4 = finch_tile4(a.hidden, a.sh_inter);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     GroupTab *tab = reinterpret_cast<GroupTab *>(smem + L.tab);
-    float *red = reinterpret_cast<float *>(smem + L.red);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar), *empty = full + 32;
-    const uint2 *zero8 = reinterpret_cast<const uint2 *>(empty + 32);
-    uint64_t *xbar = empty + 34, *xbar2 = empty + 35;
-    const int K = a.hidden, groups = K / 64, I = a.sh_inter;
-    const int f4b = frag4_bytes(K);
+    int *sm_ids = reinterpret_cast<int *>(smem + L.ids);
+    unsigned char *sm_rank = smem + L.rank;
+    uint32_t *col = reinterpret_cast<uint32_t *>(smem + L.col);
+    int *arrived = reinterpret_cast<int *>(smem + L.sync), *reduced = arrived + NW_MAX / TEAM, *trange = reduced + NW_MAX / TEAM;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar);
+    uint64_t *full = bars + 2 * warp;   // this warp's two stages
+    uint64_t *xbar = bars + 2 * NW_MAX;
+    const int K = a.hidden;
+    const unsigned tries = a.fault ? 4u : (1u << 13);
+    const unsigned spins = a.fault ? 64u : (1u << 22);
+    constexpr int PER_PASS = HILO ? 2 : 4;
+    const int Gr = gridDim.x - a.gs_a;
+    const bool routed = (int)blockIdx.x < Gr;
+    const uint32_t rec32 = finch_smem_u32(smem + L.rec), zero32 = finch_smem_u32(smem + L.zero), col32 = finch_smem_u32(col);
+    const uint32_t stage32 = finch_smem_u32(smem + L.stage), stdelta = (uint32_t)(nwarps * L.stg);   // stage s of warp w at stage32 + w * stg + s * stdelta
+    const int rowb = K * (HILO ? 4 : 2);
 
-    if (tid < 64) reinterpret_cast<int *>(smem + L.qcnt)[tid] = 0;
-    if (tid < ZERO3_BYTES / 4) reinterpret_cast<int *>(smem + L.zero)[tid] = 0;
-    if (tid == 0) {
-        empty[32] = 0ull;
-        for (int s = 0; s < Smax; s++) {
-            finch_mbar_init(full + s, 1);
-            finch_mbar_init(empty + s, TEAM_A);
-        }
-        finch_mbar_init(xbar, 1);
-        finch_mbar_init(xbar2, 1);
+    if (lane == 0) {
+        finch_mbar_init(full, 1);
+        finch_mbar_init(full + 1, 1);
+        if (warp == 0) finch_mbar_init(xbar, 1);
     }
-    grid_dep_wait();  // everything above overlaps the tail of the preparation kernel
-    // only now may the down kernel be scheduled: it reads the preparation kernel's tables before its own wait,
-    // and every CTA of this grid gets here only after the preparation kernel has completed
-    grid_dep_launch();
-    if (tid == 0) {
-        // operand records of the tokens: one bulk copy each, under way while the group table is read
-        finch_mbar_expect_tx(xbar, (unsigned)(a.B * L.rx3 + L.n4 * f4b));
-        for (int b = 0; b < a.B; b++) finch_bulk_g2s(smem + L.rec + b * L.rx3, a.xrec3 + (size_t)b * L.rx3, L.rx3, xbar);
-        for (int b = 0; b < L.n4; b++) finch_bulk_g2s(smem + L.rec4 + b * L.f4s, a.xrec4 + (size_t)b * f4b, f4b, xbar);
-    }
-    {
-        const int *s = reinterpret_cast<const int *>(a.gtab);
-        int *d = reinterpret_cast<int *>(tab);
-        for (int i = tid; i < (int)(sizeof(GroupTab) / 4); i += NT_A) d[i] = __ldcg(s + i);
-    }
-    // A CTA whose range reaches into the shared-expert jobs keeps the 4-bit-layout fragments of every
-    // token in shared memory too: it gives up the last stages of its ring for them.
-    const int n_routed = __ldcg(&a.gtab->ng) * T.nTA;
-    const int job0 = __ldcg(&a.gtab->range_a[blockIdx.x]), job1 = __ldcg(&a.gtab->range_a[blockIdx.x + 1]);
-    const int n4x = (a.has_shared && job1 > n_routed && job1 > job0) ? a.B - L.n4 : 0;   // tokens beyond the fixed area
-    const int tail_off = L.stage + Smax * L.stg - n4x * L.f4s;
-    const int S = (Smax * L.stg - n4x * L.f4s) / L.stg;
-    if (tid == 0 && n4x > 0) {
-        // the other tokens' 4-bit-layout fragments, only in CTAs with shared-expert jobs
-        finch_mbar_expect_tx(xbar2, (unsigned)(n4x * f4b));
-        for (int b = 0; b < n4x; b++) finch_bulk_g2s(smem + tail_off + b * L.f4s, a.xrec4 + (size_t)(L.n4 + b) * f4b, f4b, xbar2);
+    if (tid < 4 * (NW_MAX / TEAM)) arrived[tid] = 0;
+    for (int i = tid; i < sec3_bytes(K) / 4; i += blockDim.x) reinterpret_cast<int *>(smem + L.zero)[i] = 0;
+    // the call's inputs on their way into L2 while the previous kernel of the stream drains
+    if (warp == 0) {
+        prefetch_l2(a.ids, a.P * 4, lane, 32);
+        prefetch_l2(a.slot_row, a.n_experts * 4, lane, 32);
+        if (a.valid) prefetch_l2(a.valid, a.P, lane, 32);
+    } else {
+        prefetch_l2(a.h_post, a.B * rowb, tid - 32, blockDim.x - 32);
     }
     __syncthreads();
-    const long long tk1 = clock64();
-
-    if (warp == CW_A) {
-        // ---------------- producer warp: one bulk copy per job, issued in job order ----------------
-        if (lane == 0) {
-            for (int job = job0, it = 0; job < job1; ++job, ++it) {
-                const int st = it % S, use = it / S;
-                if (use > 0 && !finch_mbar_wait(empty + st, (use - 1) & 1)) {
-                    atomicExch(a.status, FINCH_E_TIMEOUT);
-                    return;
-                }
-                uint8_t *dst = smem + L.stage + st * L.stg;
-                if (job < n_routed) {
-                    const int gi = job / T.nTA, ta = job - gi * T.nTA;
-                    finch_mbar_expect_tx(full + st, (unsigned)T.tileA);
-                    finch_bulk_g2s(dst, a.pool_base + (size_t)tab->slot[gi] * a.slot_bytes + (size_t)ta * T.tileA, T.tileA, full + st);
-                } else {
-                    finch_mbar_expect_tx(full + st, (unsigned)T4.tileA);
-                    finch_bulk_g2s(dst, a.sh_tiles + (size_t)(job - n_routed) * T4.tileA, T4.tileA, full + st);
-                }
-            }
+    STAMP(0);
+    grid_dep_wait();  // everything above overlaps the tail of the previous kernel in the stream
+    STAMP(1);
+    // only now may the down kernel be scheduled: it reads this call's inputs before its own wait, and every
+    // CTA of this grid gets here only after whatever produced those inputs has completed
+    grid_dep_launch();
+    const int units = routed ? T.unitsA : T4.groupsA, unit_w = routed ? 768 : 256, unit_s = routed ? 128 : 32;
+    // Fetch of tile j of warp job J into shared address dst (lane 0).
+    auto fetch = [&](const WarpJobA &J, int j, uint32_t dst, uint64_t *bar) {
+        const uint8_t *src;
+        int sb;
+        if (routed) {
+            const int gi = j / T.nTA, ta = j - gi * T.nTA;
+            src = a.pool_base + (size_t)tab->slot[gi] * a.slot_bytes + (size_t)ta * T.tileA;
+            sb = T.sbA;
+        } else {
+            src = a.sh_tiles + (size_t)j * T4.tileA;
+            sb = T4.sbA;
         }
-        return;
+        finch_mbar_expect_tx(bar, (unsigned)(J.nu * (unit_w + unit_s)));
+        finch_bulk_g2s_a(dst, src + (size_t)J.u0 * unit_w, (unsigned)(J.nu * unit_w), bar);
+        finch_bulk_g2s_a(dst + J.nu * unit_w, src + sb + (size_t)J.u0 * unit_s, (unsigned)(J.nu * unit_s), bar);
+    };
+    // Two warps sort out the routing (and the teams' tile ranges) while the others bring the activation rows in
+    // and take their group sums.  Once both are done every warp requests its first piece, and the rows are turned
+    // into operand records while that piece is on its way.
+    uint8_t *xs = smem + L.stage + nwarps * L.stg;
+    float *umax = reinterpret_cast<float *>(smem + L.umax);
+    int xs_rows = (nwarps * L.stg) / rowb;
+    xs_rows = xs_rows > 8 ? 8 : xs_rows;
+    auto row_ptr = [&](int b) { return (const void *)((const uint8_t *)a.h_post + (size_t)b * rowb); };
+    const bool one_round = a.B <= xs_rows;   // else: the records are built round by round before anything is fetched
+    if (warp < 2) {
+        build_groups(a, tab, sm_ids, sm_rank, PER_PASS, routed ? col : nullptr, rec32, L.rstride, trange, routed ? nteam : 0, blockIdx.x * nteam, Gr * nteam, T.nTA);
+        STAMP(2);
+    } else if (one_round) {
+        if (tid == 64) records_fetch_rows(a.B, 0, rowb, xs, xbar, row_ptr);
+        if (!mbar_wait_lim(xbar, 0, tries) && lane == 0) atomicExch(a.status, FINCH_E_TIMEOUT);
+        if (routed) records_sums<3, HILO, !HILO>(a.B, 0, K, smem + L.rec, L.rstride, xs, umax, 64, blockDim.x - 64);
+        else records_sums<4, HILO, !HILO>(a.B, 0, K, smem + L.rec, L.rstride, xs, umax, 64, blockDim.x - 64);
+        STAMP(12);
+    } else {
+        xs_rows = xs_rows > nwarps - 2 ? nwarps - 2 : xs_rows;
+        if (routed) build_records<3, HILO, !HILO>(a.B, K, smem + L.rec, L.rstride, xs, xs_rows, umax, xbar, 64, blockDim.x - 64, BAR_RECORDS, tries, a.status, row_ptr);
+        else build_records<4, HILO, !HILO>(a.B, K, smem + L.rec, L.rstride, xs, xs_rows, umax, xbar, 64, blockDim.x - 64, BAR_RECORDS, tries, a.status, row_ptr);
     }
-
-    // ---------------- consumer warps ----------------
-    // Warp w works on the K-quarter kw = w % 4 of the CTA's jobs w / 4, w / 4 + 4, ...  The four
-    // warps of a job never wait for each other: each leaves its partial sums in the job's slot and
-    // bumps the slot's counter; whoever comes last adds the four partials in fixed order.
-    const int team = warp / TEAM_A, kw = warp % TEAM_A;
-    int *qcnt = reinterpret_cast<int *>(smem + L.qcnt);
-    if (!finch_mbar_wait(xbar, 0) || (n4x > 0 && !finch_mbar_wait(xbar2, 0))) {
-        if (lane == 0) atomicExch(a.status, FINCH_E_TIMEOUT);
-        return;
+    __syncthreads();
+    STAMP(13);
+    const WarpJobA J = warp_job_a(routed, units, T4.nTA, blockIdx.x, Gr, a.gs_a, nteam, warp, trange);
+    const bool withhold = a.fault == 1 && routed && J.j0 == 0 && warp % TEAM == 0;   // the warp that owns the first quarter of tile 0
+    if (lane == 0 && J.nu > 0 && J.j0 < J.j1 && !withhold) fetch(J, J.j0, stage32 + (uint32_t)(warp * L.stg), full);
+    if (one_round) {
+        if (routed) records_frags<3, HILO, !HILO>(a.B, 0, K, smem + L.rec, L.rstride, xs, umax, 0, blockDim.x);
+        else records_frags<4, HILO, !HILO>(a.B, 0, K, smem + L.rec, L.rstride, xs, umax, 0, blockDim.x);
+        STAMP(3);
+        __syncthreads();
     }
-    const long long tk2 = clock64();
-    long long wait_acc = 0;
-    int njobs = 0;
-    // a CTA with fewer stages than teams lets its surplus teams sit out
-    const int nteam = NTEAM_A < S ? NTEAM_A : S;
-    int *cons = qcnt + 32;
-    for (int it = team; team < nteam && job0 + it < job1; it += nteam, ++njobs) {
-        const int job = job0 + it, st = it % S, use = it / S;
-        const long long w0 = clock64();
-        if (!wait_consumed(cons + st, use) || !finch_mbar_wait(full + st, use & 1)) {
-            if (lane == 0) atomicExch(a.status, FINCH_E_TIMEOUT);
-            return;
-        }
-        wait_acc += clock64() - w0;
-        const uint8_t *tile = smem + L.stage + st * L.stg;
-        float *slot = red + st * (MAXM / 2) * TEAM_A * 32;   // [pass][warp of the job][32]
-        const bool routed = job < n_routed;
-        const int gi = routed ? job / T.nTA : 0, ta = routed ? job - gi * T.nTA : job - n_routed;
-        const int m = routed ? tab->m[gi] : a.B, npass = (m + 1) / 2;
-        for (int ps = 0; ps < npass; ps++) {
-            const int ntok = min(2, m - 2 * ps);
-            float vA, vB;
-            float *mine = slot + (ps * TEAM_A + kw) * 32;   // [token slot][row g][A|B]
-            if (routed) {
-                const int tok0 = tab->pairs[gi][2 * ps] / a.K, tok1 = tab->pairs[gi][2 * ps + (ntok > 1)] / a.K;
-                const uint8_t *rec0 = smem + L.rec + tok0 * L.rx3, *rec1 = smem + L.rec + tok1 * L.rx3;
-                gemv3_tile(tile, T.unitsA, kw, TEAM_A, a.scale_dtype, reinterpret_cast<const uint2 *>(rec0), reinterpret_cast<const uint2 *>(rec1),
-                           reinterpret_cast<const float *>(rec0 + frag3_bytes(K)), reinterpret_cast<const float *>(rec1 + frag3_bytes(K)),
-                           smem + L.zero, ntok, vA, vB);
-                if ((t & 1) == 0) {
-                    mine[(t >> 1) * 16 + g * 2] = vA;
-                    mine[(t >> 1) * 16 + g * 2 + 1] = vB;
-                }
-            } else {
-                // shared expert gate/up tile: 4 gate rows + 4 up rows, every token, two per pass
-                const int tok0 = 2 * ps, tok1 = 2 * ps + (ntok > 1);
-                const uint2 *f0 = reinterpret_cast<const uint2 *>(smem + (tok0 < L.n4 ? L.rec4 + tok0 * L.f4s : tail_off + (tok0 - L.n4) * L.f4s));
-                const uint2 *f1 = reinterpret_cast<const uint2 *>(smem + (tok1 < L.n4 ? L.rec4 + tok1 * L.f4s : tail_off + (tok1 - L.n4) * L.f4s));
-                gemv4_tile(tile, groups, kw, TEAM_A, (g & 3) * 4 + t, 16, g & 3, 4, a.sh_scale_dtype, f0, f1,
-                           reinterpret_cast<const float *>(smem + L.rec + tok0 * L.rx3 + frag3_bytes(K)),
-                           reinterpret_cast<const float *>(smem + L.rec + tok1 * L.rx3 + frag3_bytes(K)), zero8, ntok, vA, vB);
-                if (t < 2) {
-                    mine[t * 16 + g * 2] = vA;      // rows g >= 4 duplicate rows g - 4 and are never stored
-                    mine[t * 16 + g * 2 + 1] = vB;
-                }
-            }
-        }
-        __threadfence_block();
-        __syncwarp();
+    STAMP(7);
+#ifdef FINCH_STAMPS
+    if (lane == 0)
+        for (int i = 8; i < 12; i++) g_stamps[((size_t)blockIdx.x * 32 + warp) * 16 + i] = 0;
+#endif
+    if (J.nu <= 0) return;
+    const int team = warp / TEAM, kw = warp % TEAM, nkw = J.nkw, u0 = J.u0, nu = J.nu;
+    const uint32_t st32 = stage32 + (uint32_t)(warp * L.stg);
+    float *slot = reinterpret_cast<float *>(smem + L.red) + team * (TEAM * MAXM * 16);   // [kw][ti][g][gate | up]
+    const uint32_t slot32 = finch_smem_u32(slot);
+    bool dead = false;   // a wait ran out: the warp keeps its team's protocol going and does nothing else
+    // second piece (the second stages were the staging area of the rows until the barrier above)
+    int fj = J.j0 + J.step;
+    if (lane == 0) {
+        fence_async_smem();
+        if (fj < J.j1) fetch(J, fj, st32 + stdelta, full + 1);
+    }
+    fj += J.step;
+
+    // One tile's partial sums are in the team's slot: the warp that arrives last adds the K-quarters in fixed
+    // order and applies SiLU(gate) * up.  `store(ti, gg, v)` takes the value of (token ti of the tile, row gg).
+    auto finish = [&](int n, int nti, auto store) {
+        __syncwarp();   // the lanes' partial sums are ordered before lane 0's release
         int old = 0;
-        if (lane == 0) old = atomicAdd(&qcnt[st], 1);
+        if (lane == 0) old = atom_add_acq_rel(arrived + team, 1);
         old = __shfl_sync(0xffffffffu, old, 0);
-        if (old == TEAM_A - 1) {
-            // last of the four: lane = (token slot, row g, gate|up); sum in fixed order, then SiLU(gate) * up
-            __threadfence_block();
-            for (int ps = 0; ps < npass; ps++) {
-                const int ntok = min(2, m - 2 * ps);
-                const float *src = slot + ps * TEAM_A * 32 + lane;
-                float v = 0.f;
+        if (old != nkw * (n + 1) - 1) return;
+        __syncwarp();   // ... and lane 0's acquire before the lanes' reads
+        for (int item = lane; item < nti * 8; item += 32) {
+            const int ti = item >> 3, gg = item & 7;
+            float va = 0.f, vb = 0.f;
+            for (int k = 0; k < nkw; k++) {
+                const float2 v = *reinterpret_cast<const float2 *>(slot + ((k * MAXM + ti) * 8 + gg) * 2);
+                va += v.x;
+                vb += v.y;
+            }
+            store(ti, gg, __fdividef(va, 1.0f + __expf(-va)) * vb);
+        }
+        __syncwarp();
+        if (lane == 0) st_release(reduced + team, n + 1);
+    };
+
+    if (routed) {
+        // ---------------- routed experts: 3-bit tiles ----------------
+        const int sec = sec3_bytes(K), hdr_off = sec * (HILO ? 2 : 1);
+        const bool mine = (g & 1) == (t >> 1);   // this lane's k-slots belong to the group of its B column
+        // lane constants: which pair of a pass this lane's B column / accumulator columns belong to
+        const int pos_b = HILO ? (g >> 2) : (g >> 1), pos_o = HILO ? (t >> 1) : t;
+        const uint32_t sec_b = HILO ? (uint32_t)(((g >> 1) & 1) * sec) : 0u;
+        const uint32_t lane_w = (uint32_t)lane * 24u, lane_s = (uint32_t)(nu * 768 + g * 16), boff = (uint32_t)(u0 * UB);
+        const uint32_t my_slot = slot32 + (uint32_t)(((kw * MAXM) * 8 + g) * 8);
+        int gi = J.j0 / T.nTA, ta = J.j0 - gi * T.nTA;
+        STAMP(14);
+        for (int j = J.j0, n = 0; j < J.j1; ++j, ++n) {
+            const int st = n & 1;
+            const int m = tab->m[gi], npass = (m + PER_PASS - 1) / PER_PASS;
+            const long long c0 = STAMP_CLK();
+            if (!dead && !mbar_wait_lim(full + st, (n >> 1) & 1, tries)) {
+                give_up(a.status, j + 1 < J.j1 ? full + ((n + 1) & 1) : nullptr, ((n + 1) >> 1) & 1);
+                dead = true;
+            }
+            const long long c1 = STAMP_CLK();
+            STAMP_ADD(8, c1 - c0);
+            if (n == 0) STAMP(4);
+            const uint32_t w32 = st32 + (uint32_t)st * stdelta;
+            float resA[HILO ? 4 : 2], resB[HILO ? 4 : 2];
+            if (!dead) {
 #pragma unroll
-                for (int k = 0; k < TEAM_A; k++) v += src[k * 32];
-                const float other = __shfl_xor_sync(0xffffffffu, v, 1);
-                const int ts = lane >> 4, gg = (lane >> 1) & 7;
-                if (!(lane & 1) && ts < ntok) {
-                    const float r = (v / (1.0f + expf(-v))) * other;
-                    if (routed) a.act[(size_t)tab->pairs[gi][2 * ps + ts] * a.inter + 8 * ta + gg] = r;
-                    else if (gg < 4) a.shared_act[(size_t)(2 * ps + ts) * I + 4 * ta + gg] = r;
+                for (int ps = 0; ps < (HILO ? 4 : 2); ps++) {
+                    if (ps < npass) {
+                        const uint32_t cb = lds32(col32 + (uint32_t)((gi * MAXM + ps * PER_PASS + pos_b) * 4));
+                        const uint32_t co = lds32(col32 + (uint32_t)((gi * MAXM + ps * PER_PASS + pos_o) * 4));
+                        const uint32_t pb = ((mine && cb) ? cb + sec_b : zero32) + boff;
+                        const uint32_t ph = (co ? co : rec32) + hdr_off;
+                        float runA, runB, biasA, biasB;
+                        gemv3_piece<FP16S>(w32 + lane_w, w32 + lane_s, nu, pb, ph + u0 * 8, runA, runB, biasA, biasB);
+                        const float fac = pow2_biased(__float_as_int(lds32f(ph + (K / 64) * 4)) + 17);
+                        if (HILO) {
+                            const float oA = __shfl_xor_sync(0xffffffffu, runA, 1), oB = __shfl_xor_sync(0xffffffffu, runB, 1);
+                            runA += oA * (1.0f / 2048.0f);
+                            runB += oB * (1.0f / 2048.0f);
+                        }
+                        resA[ps] = fmaf(runA, fac, biasA);
+                        resB[ps] = fmaf(runB, fac, biasB);
+                    }
+                }
+                __syncwarp();   // every lane is done with the stage
+                if (lane == 0 && fj < J.j1) fetch(J, fj, w32, full + st);
+            }
+            fj += J.step;
+            const long long c2 = STAMP_CLK();
+            STAMP_ADD(9, c2 - c1);
+            if (n == 0) STAMP(5);
+            // the previous tile's partial sums have been read before this tile's overwrite them
+            if (nkw > 1 && n > 0 && !dead && !wait_ge(reduced + team, n, spins)) {
+                give_up(a.status, j + 1 < J.j1 ? full + ((n + 1) & 1) : nullptr, ((n + 1) >> 1) & 1);
+                dead = true;
+            }
+            if (!dead) {
+#pragma unroll
+                for (int ps = 0; ps < (HILO ? 4 : 2); ps++) {
+                    const int pio = ps * PER_PASS + pos_o;
+                    if (ps < npass && pio < m && (!HILO || !(t & 1))) sts64f(my_slot + (uint32_t)(pio * 64), resA[ps], resB[ps]);
                 }
             }
-            if (lane == 0) {
-                qcnt[st] = 0;
-                __threadfence_block();
-                *reinterpret_cast<volatile int *>(cons + st) = use + 1;
-            }
-            __syncwarp();
+            finish(n, m, [&](int ti, int gg, float v) { a.act[(size_t)tab->pairs[gi][ti] * a.inter + 8 * ta + gg] = v; });
+            STAMP_ADD(10, STAMP_CLK() - c2);
+            STAMP_ADD(11, 1);
+            if (++ta == T.nTA) ta = 0, ++gi;
         }
-        if (lane == 0) mbar_arrive(empty + st);
-    }
-    if (a.dbg && lane == 0) atomicMax(reinterpret_cast<unsigned long long *>(a.dbg + (size_t)blockIdx.x * 8 + 5), (unsigned long long)gtime());
-    if (a.dbg && tid == 0) {
-        long long *d = a.dbg + (size_t)blockIdx.x * 8;
-        d[0] = tk1 - tk0;           // table + barriers
-        d[1] = tk2 - tk1;           // waiting for the token records
-        d[2] = clock64() - tk2;     // job loop of team 0
-        d[3] = wait_acc;            // ... of which waiting for a full stage
-        d[4] = gt0;
-        d[6] = njobs;
-        d[7] = job1 - job0;
+        STAMP(6);
+    } else {
+        // ---------------- shared expert: 4-bit tiles of 4 gate rows + the 4 matching up rows ----------------
+        const int g0 = u0, ngr = nu;
+        const int nps = HILO ? (a.B + 3) / 4 : (a.B + 7) / 8;   // passes of a tile (every token): four (hi + lo) or eight tokens each
+        const int sec = sec4_bytes(K), hdr_off = sec * (HILO ? 2 : 1);
+        const int I = a.sh_inter;
+        int n = 0;
+        for (int tile = J.j0; tile < J.j1; tile += J.step, ++n) {
+            const int st = n & 1;
+            if (!dead && !mbar_wait_lim(full + st, (n >> 1) & 1, tries)) {
+                give_up(a.status, tile + J.step < J.j1 ? full + ((n + 1) & 1) : nullptr, ((n + 1) >> 1) & 1);
+                dead = true;
+            }
+            const uint32_t w32 = st32 + (uint32_t)st * stdelta, s32 = w32 + ngr * 256;
+            if (nkw > 1 && n > 0 && !dead && !wait_ge(reduced + team, n, spins)) {
+                give_up(a.status, tile + J.step < J.j1 ? full + ((n + 1) & 1) : nullptr, ((n + 1) >> 1) & 1);
+                dead = true;
+            }
+            if (!dead) {
+                for (int ps = 0; ps < nps; ps++) {
+                    // column g of the pass: HILO: token 4 ps + (g >> 1), term g & 1; else token 8 ps + g
+                    const int tokb = HILO ? 4 * ps + (g >> 1) : 8 * ps + g;
+                    const int tok0 = HILO ? 4 * ps + t : 8 * ps + 2 * t, tok1 = HILO ? tok0 : tok0 + 1;   // accumulator columns 2t, 2t + 1
+                    const bool bact = tokb < a.B;
+                    const uint32_t pb = (bact ? rec32 + tokb * L.rstride + (HILO ? (g & 1) * sec : 0) + g0 * GB4 : zero32) + t * 16;
+                    const uint32_t ph0 = rec32 + (tok0 < a.B ? tok0 : 0) * L.rstride + hdr_off, ph1 = rec32 + (tok1 < a.B ? tok1 : 0) * L.rstride + hdr_off;
+                    float r[4], bias[4];
+                    if (a.sh_fp16) gemv4_piece<true>(w32 + ((g & 3) * 4 + t) * 16, 256, s32 + (g & 3) * 8, 32, ngr, pb, bact ? GB4 : 0, ph0 + g0 * 4, ph1 + g0 * 4, r, bias);
+                    else gemv4_piece<false>(w32 + ((g & 3) * 4 + t) * 16, 256, s32 + (g & 3) * 8, 32, ngr, pb, bact ? GB4 : 0, ph0 + g0 * 4, ph1 + g0 * 4, r, bias);
+                    const float f0 = pow2_biased(__float_as_int(lds32f(ph0 + (K / 64) * 4)) + 17);
+                    const float f1 = pow2_biased(__float_as_int(lds32f(ph1 + (K / 64) * 4)) + 17);
+                    if (g < 4) {   // rows g >= 4 duplicate rows g - 4
+                        if (HILO) {
+                            if (tok0 < a.B)
+                                *reinterpret_cast<float2 *>(slot + ((kw * MAXM + tok0) * 8 + g) * 2) =
+                                    make_float2(fmaf(r[0] + r[1] * (1.0f / 2048.0f), f0, bias[0]), fmaf(r[2] + r[3] * (1.0f / 2048.0f), f0, bias[2]));
+                        } else {
+                            if (tok0 < a.B)
+                                *reinterpret_cast<float2 *>(slot + ((kw * MAXM + tok0) * 8 + g) * 2) = make_float2(fmaf(r[0], f0, bias[0]), fmaf(r[2], f0, bias[2]));
+                            if (tok1 < a.B)
+                                *reinterpret_cast<float2 *>(slot + ((kw * MAXM + tok1) * 8 + g) * 2) = make_float2(fmaf(r[1], f1, bias[1]), fmaf(r[3], f1, bias[3]));
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0 && fj < J.j1) fetch(J, fj, w32, full + st);
+            }
+            fj += J.step;
+            finish(n, a.B, [&](int ti, int gg, float v) {
+                if (gg < 4) a.shared_act[(size_t)ti * I + 4 * tile + gg] = v;
+            });
+            if (n == 0) STAMP(5);
+            STAMP_ADD(11, 1);
+        }
+        STAMP(6);
     }
 }
 
-// ============================ kernel B ====================================
+// ============================ down ========================================
+// stage: [2][warps][stg] as in the gate/up kernel (the second half doubles as the staging area of the rows).
 struct SmemB {
-    int stage, stg, rec, srec, xstage, umax, tab, zero, bar, total;
+    int stage, stg, rec, rstride, zero, umax, tab, col, ids, rank, bar, total;
 };
-__host__ __device__ inline SmemB smem_b_layout(int hidden, int inter, int sh_inter, int B, int has_shared, int stages) {
+__host__ __device__ inline SmemB smem_b_layout(int hidden, int inter, int sh_inter, int B, int has_shared, int nwarps) {
     const FinchTile T = finch_tile(hidden, inter);
     const FinchTile4 T4 = finch_tile4(hidden, sh_inter);
     SmemB L;
     L.stage = 0;
     L.stg = up128(has_shared && T4.tileB > T.tileB ? T4.tileB : T.tileB);
-    L.rec = L.stage + stages * L.stg;                        // act records of the groups in this CTA's range
-    L.srec = up128(L.rec + REC_CAP * rec3_bytes(inter));     // shared_act records
-    L.xstage = up128(L.srec + (has_shared ? B * rec4_bytes(sh_inter) : 0));   // the act rows behind the records, staged as fp32
-    L.umax = up128(L.xstage + REC_CAP * 4 * inter);                            // max |act| per (record, 128-value unit)
-    L.tab = up128(L.umax + REC_CAP * (inter / 128) * 4);
-    L.zero = up128(L.tab + (int)sizeof(GroupTab));
-    L.bar = L.zero + ZERO3_BYTES;
-    L.total = L.bar + 2 * 32 * 8 + 16 + 32 * 4;              // barriers, 16 zero bytes, jobs consumed per stage
+    L.rec = L.stage + 2 * nwarps * L.stg;
+    L.rstride = rec3_bytes(inter, 1);
+    const int routed = REC_CAP * L.rstride, shared = has_shared ? B * rec4_bytes(sh_inter, 1) : 0;
+    L.zero = L.rec + (routed > shared ? routed : shared) + 64;
+    L.umax = L.zero + sec3_bytes(inter) + 64;
+    L.tab = L.umax + REC_CAP * (((inter > sh_inter ? inter : sh_inter) + 255) / 256) * 4;
+    L.col = L.tab + (((int)sizeof(GroupTab) + 15) & ~15);
+    L.ids = L.col + MAXP * MAXM * 4;
+    L.rank = L.ids + (MAXP + 2) * 4;
+    L.bar = (L.rank + MAXP + 7) & ~7;
+    L.total = L.bar + (2 * NW_MAX + 1) * 8;
     return L;
 }
 
-// grid: one CTA per SM (persistent); block: CW_B consumer warps + 1 producer warp.
-__global__ void __launch_bounds__(NT_B, 1) moe_down_combine_kernel(const MoeArgs a) {
+// grid: one CTA per SM (persistent); block: nwarps warps, each takes whole tiles.
+template <bool FP16S>
+__global__ void __launch_bounds__(NW_MAX * 32, 1) moe_down_kernel(const MoeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const long long tk0 = clock64(), gt0 = gtime();
-    const int S = a.stages_b;
-    const SmemB L = smem_b_layout(a.hidden, a.inter, a.sh_inter, a.B, a.has_shared, S);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+    const int nwarps = blockDim.x >> 5;
+    const SmemB L = smem_b_layout(a.hidden, a.inter, a.sh_inter, a.B, a.has_shared, nwarps);
     const FinchTile T = finch_tile(a.hidden, a.inter);
     const FinchTile4 T4 = finch_tile4(a.hidden, a.sh_inter);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     GroupTab *tab = reinterpret_cast<GroupTab *>(smem + L.tab);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar), *empty = full + 32;
-    const uint2 *zero8 = reinterpret_cast<const uint2 *>(empty + 32);
+    int *sm_ids = reinterpret_cast<int *>(smem + L.ids);
+    unsigned char *sm_rank = smem + L.rank;
+    uint32_t *col = reinterpret_cast<uint32_t *>(smem + L.col);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar) + 2 * warp;
+    uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + L.bar) + 2 * NW_MAX;
     const int K = a.inter, Ks = a.sh_inter;
-    const int r3b = rec3_bytes(K), r4b = rec4_bytes(Ks);
+    const unsigned tries = a.fault ? 4u : (1u << 13);
+    const int Gr = gridDim.x - a.gs_b;
+    const bool routed = (int)blockIdx.x < Gr;
 
-    if (tid == 0) {
-        empty[32] = 0ull;
-        for (int s = 0; s < S; s++) {
-            finch_mbar_init(full + s, 1);
-            finch_mbar_init(empty + s, 1);
-        }
+    if (lane == 0) {
+        finch_mbar_init(full, 1);
+        finch_mbar_init(full + 1, 1);
+        if (warp == 0) finch_mbar_init(xbar, 1);
     }
-    if (tid < ZERO3_BYTES / 4) reinterpret_cast<int *>(smem + L.zero)[tid] = 0;
-    int *cons = reinterpret_cast<int *>(smem + L.bar + 2 * 32 * 8 + 16);
-    if (tid < 32) cons[tid] = 0;
+    for (int i = tid; i < sec3_bytes(K) / 4; i += blockDim.x) reinterpret_cast<int *>(smem + L.zero)[i] = 0;
+    STAMPB(0);
     grid_dep_launch();
-    // The group table and the job ranges are the preparation kernel's output: that grid completed before the
-    // gate/up kernel started, so they can be read, and the weight tiles streamed, while the gate/up kernel
-    // is still finishing on other SMs.  Only the activations (its output) have to wait.
-    {
-        const int *s = reinterpret_cast<const int *>(a.gtab);
-        int *d = reinterpret_cast<int *>(tab);
-        for (int i = tid; i < (int)(sizeof(GroupTab) / 4); i += NT_B) d[i] = __ldcg(s + i);
-    }
+    // The routing is an input of the whole call, final since the gate/up kernel passed its own wait (this grid
+    // is scheduled only after that): groups, ranges and the first weight pieces do not wait for the gate/up
+    // kernel to finish.  Only the activations (its output) do.
+    if (routed && warp < 2) build_groups(a, tab, sm_ids, sm_rank, 2, nullptr, 0u, 0);
     __syncthreads();
-    const long long tk1 = clock64();
-    const int ng = tab->ng, n_routed = ng * T.nTB;
-    const int job0 = tab->range_b[blockIdx.x], job1 = tab->range_b[blockIdx.x + 1];
+    STAMPB(1);
+    const uint32_t st32 = finch_smem_u32(smem + L.stage + warp * L.stg), stdelta = (uint32_t)(nwarps * L.stg);
+    uint8_t *xs = smem + L.stage + nwarps * L.stg;
+    float *umax = reinterpret_cast<float *>(smem + L.umax);
+    const uint32_t zero32 = finch_smem_u32(smem + L.zero), rec32 = finch_smem_u32(smem + L.rec), col32 = finch_smem_u32(col);
 
-    if (warp == CW_B) {
-        // Producer warp: lane s owns stage s and issues that stage's fills in order (a single thread cannot issue
-        // a 3.5 KB tile as fast as sixteen consumer warps use them up).  Per stage the order of fills and waits is
-        // the serial one, so the producer's waits never see a barrier more than one phase behind.
-        if (lane < S) {
-            const int st = lane;
-            for (int it = lane, use = 0; job0 + it < job1; it += S, ++use) {
-                const int job = job0 + it;
-                if (use > 0 && !finch_mbar_wait(empty + st, (use - 1) & 1)) {
-                    atomicExch(a.status, FINCH_E_TIMEOUT);
-                    return;
-                }
-                uint8_t *dst = smem + L.stage + st * L.stg;
-                if (job < n_routed) {
-                    const int gi = job / T.nTB, tb = job - gi * T.nTB;
-                    finch_mbar_expect_tx(full + st, (unsigned)T.tileB);
-                    finch_bulk_g2s(dst, a.pool_base + (size_t)tab->slot[gi] * a.slot_bytes + T.b_base + (size_t)tb * T.tileB, T.tileB, full + st);
-                } else {
-                    finch_mbar_expect_tx(full + st, (unsigned)T4.tileB);
-                    finch_bulk_g2s(dst, a.sh_tiles + T4.b_base + (size_t)(job - n_routed) * T4.tileB, T4.tileB, full + st);
-                }
-            }
-        }
-        return;
-    }
-
-    // ---------------- consumer warps ----------------
-    grid_dep_wait();   // the gate/up kernel has completed: act / shared_act are final
-    const long long tkw = clock64();
-    // operand records of the activations this CTA needs: the pairs of the groups in its job range
-    // (and every token's shared activations if it has shared-expert jobs)
-    const int g_lo = job0 < n_routed ? job0 / T.nTB : ng;
-    const int g_hi = job1 > job0 ? min(ng - 1, (job1 - 1) / T.nTB) : -1;   // inclusive
-    {
-        // One warp per (record, 128-value unit): first the unit's values are staged, its two group sums written and its
-        // largest magnitude noted; after a barrier every unit knows its record's exponent and builds its fragments.
-        float *xstage = reinterpret_cast<float *>(smem + L.xstage), *umax = reinterpret_cast<float *>(smem + L.umax);
-        const int units = K / 128;
-        int nrec = 0;
-        for (int gi = g_lo; gi <= g_hi; gi++) nrec += tab->m[gi];
-        if (nrec > REC_CAP) {
-            if (tid == 0) atomicExch(a.status, FINCH_E_UNSUPPORTED);
-            nrec = REC_CAP;
-        }
-        auto pair_of = [&](int q) {   // q-th record of the CTA -> its (token, k) pair
-            int gi = g_lo;
-            while (q >= tab->m[gi]) q -= tab->m[gi++];
-            return (int)tab->pairs[gi][q];
+    if (routed) {
+        const int ng = tab->ng;
+        const int total = tab->pre[ng] * T.nTB;
+        const int job0 = job_at(tab->pre, ng, T.nTB, (int)((unsigned)total * blockIdx.x / (unsigned)Gr));
+        const int job1 = job_at(tab->pre, ng, T.nTB, (int)((unsigned)total * (blockIdx.x + 1) / (unsigned)Gr));
+        auto fetch = [&](int gi, int tb, uint32_t dst, uint64_t *bar) {   // lane 0
+            finch_mbar_expect_tx(bar, (unsigned)T.tileB);
+            finch_bulk_g2s_a(dst, a.pool_base + (size_t)tab->slot[gi] * a.slot_bytes + T.b_base + (size_t)tb * T.tileB, (unsigned)T.tileB, bar);
         };
-        for (int it = warp; it < nrec * units; it += CW_B) {
-            const int q = it / units, u = it - q * units;
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(a.act + (size_t)pair_of(q) * K + u * 128) + lane);
-            *reinterpret_cast<float4 *>(xstage + q * K + u * 128 + lane * 4) = v;
-            float sum = (v.x + v.y) + (v.z + v.w), mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-#pragma unroll
-            for (int o = 1; o < 16; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-#pragma unroll
-            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            float *hdr = reinterpret_cast<float *>(smem + L.rec + q * r3b + frag3_bytes(K));
-            if ((lane & 15) == 0) hdr[2 * u + (lane >> 4)] = sum;
-            if (lane == 0) umax[it] = mx;
+        const int dgi = nwarps / T.nTB, dtb = nwarps - dgi * T.nTB;
+        auto advance = [&](int &G, int &A) {
+            G += dgi;
+            A += dtb;
+            if (A >= T.nTB) A -= T.nTB, ++G;
+        };
+        const int first = job0 + warp;
+        int gi = first / T.nTB, tb = first - gi * T.nTB, fgi = gi, ftb = tb, fjob = first;
+        if (lane == 0 && fjob < job1) fetch(fgi, ftb, st32, full);
+        fjob += nwarps;
+        advance(fgi, ftb);
+        // operand records of the activations this CTA needs: the pairs of the groups in its job range
+        const int g_lo = job0 < job1 ? job0 / T.nTB : 0;
+        const int g_hi = job0 < job1 ? (job1 - 1) / T.nTB : -1;   // inclusive
+        int nrec = 0;
+        for (int j = g_lo; j <= g_hi; j++) nrec += tab->m[j];
+        for (int i = tid; i < MAXP * MAXM; i += blockDim.x) {
+            const int j = i / MAXM, pos = i % MAXM;
+            int r0 = 0;   // first record of group j in the CTA's record area
+            for (int q = g_lo; q < j && q <= g_hi; q++) r0 += tab->m[q];
+            col[i] = (j >= g_lo && j <= g_hi && pos < tab->m[j] && r0 + pos < REC_CAP) ? rec32 + (r0 + pos) * L.rstride : 0u;
         }
-        // the shared expert's records, from the last warp down (the first warps have the routed records), before the
-        // barrier so that they overlap the loads above
-        if (a.has_shared && job1 > n_routed && job1 > job0)
-            for (int b = CW_B - 1 - warp; b >= 0 && b < a.B; b += CW_B) {
-                // staged in the rows of the staging area that the routed records leave free, when there are enough
-                float *stg = (Ks <= K && nrec + a.B <= REC_CAP) ? xstage + (size_t)(REC_CAP - 1 - b) * K : nullptr;
-                warp_make_record<4>(a.shared_act + (size_t)b * Ks, Ks, smem + L.srec + b * r4b, stg);
-            }
-        bar_sync(1, CW_B * 32);
-        for (int it = warp; it < nrec * units; it += CW_B) {
-            const int q = it / units, u = it - q * units;
-            float m = 0.f;
-            for (int j = 0; j < units; j++) m = fmaxf(m, umax[q * units + j]);
-            int E = (int)(__float_as_uint(m) >> 23) + 1;
-            E = E < 30 ? 30 : (E > 230 ? 230 : E);
-            uint8_t *rec = smem + L.rec + q * r3b;
-            if (u == 0 && lane == 0) reinterpret_cast<float *>(rec + frag3_bytes(K))[K / 64] = __int_as_float(E);
-            build_frag3_range(xstage + q * K + u * 128, 128, E, reinterpret_cast<uint2 *>(rec) + u * 72, lane, 32);
+        STAMPB(2);
+        grid_dep_wait();   // the gate/up kernel has completed: act is final
+        STAMPB(3);
+        if (nrec > REC_CAP) {   // cannot happen with a grid of a hundred CTAs or more; refuse instead of clipping
+            if (tid == 0) atomicExch(a.status, FINCH_E_UNSUPPORTED);
+            if (first < job1) mbar_wait_lim(full, 0, 1u << 13);   // the fetch under way
+            return;
         }
-    }
-    bar_sync(1, CW_B * 32);
-    const long long tk2 = clock64();
-
-    long long wait_acc = 0;
-    int njobs = 0;
-    for (int it = warp; job0 + it < job1; it += CW_B, ++njobs) {
-        const int job = job0 + it, st = it % S, use = it / S;
-        const long long w0 = clock64();
-        if (!wait_consumed(cons + st, use) || !finch_mbar_wait(full + st, use & 1)) {
-            if (lane == 0) atomicExch(a.status, FINCH_E_TIMEOUT);
-            break;
-        }
-        wait_acc += clock64() - w0;
-        const uint8_t *tile = smem + L.stage + st * L.stg;
-        int tb;
-        if (job < n_routed) {
-            const int gi = job / T.nTB, m = tab->m[gi], npass = (m + 1) / 2;
-            tb = job - gi * T.nTB;
-            int slot0 = 0;  // first record of this group in the CTA's record area
-            for (int j = g_lo; j < gi; j++) slot0 += tab->m[j];
-            for (int ps = 0; ps < npass; ps++) {
-                const int ntok = min(2, m - 2 * ps);
-                const uint8_t *rec0 = smem + L.rec + (slot0 + 2 * ps) * r3b, *rec1 = smem + L.rec + (slot0 + 2 * ps + (ntok > 1)) * r3b;
-                float va, vb;
-                gemv3_tile(tile, T.unitsD, 0, 1, a.scale_dtype, reinterpret_cast<const uint2 *>(rec0), reinterpret_cast<const uint2 *>(rec1),
-                           reinterpret_cast<const float *>(rec0 + frag3_bytes(K)), reinterpret_cast<const float *>(rec1 + frag3_bytes(K)),
-                           smem + L.zero, ntok, va, vb);
-                if ((t & 1) == 0 && (t >> 1) < ntok) {
-                    float *o = a.partial + (size_t)tab->pairs[gi][2 * ps + (t >> 1)] * a.hidden + 16 * tb + g;
-                    o[0] = va;
-                    o[8] = vb;
-                }
-            }
-        } else {
-            tb = job - n_routed;
-            const int npass = (a.B + 1) / 2;
-            for (int ps = 0; ps < npass; ps++) {
-                const int ntok = min(2, a.B - 2 * ps);
-                const uint8_t *rec0 = smem + L.srec + (2 * ps) * r4b, *rec1 = smem + L.srec + (2 * ps + (ntok > 1)) * r4b;
-                float va, vb;
-                gemv4_tile(tile, Ks / 64, 0, 1, lane, 32, g, 8, a.sh_scale_dtype, reinterpret_cast<const uint2 *>(rec0),
-                           reinterpret_cast<const uint2 *>(rec1), reinterpret_cast<const float *>(rec0 + frag4_bytes(Ks)),
-                           reinterpret_cast<const float *>(rec1 + frag4_bytes(Ks)), zero8, ntok, va, vb);
-                if (t < ntok) {
-                    float *o = a.partial + (size_t)(a.P + 2 * ps + t) * a.hidden + 16 * tb + g;
-                    o[0] = va;
-                    o[8] = vb;
-                }
-            }
-        }
-        __syncwarp();
+        int xs_rows = (nwarps * L.stg) / (K * 4);
+        xs_rows = xs_rows > nwarps ? nwarps : xs_rows;
+        auto row_ptr = [&](int q) {   // q-th record of the CTA -> the activations of its (token, k) pair
+            int j = g_lo;
+            while (q >= tab->m[j]) q -= tab->m[j++];
+            return (const void *)(a.act + (size_t)tab->pairs[j][q] * K);
+        };
+        build_records<3, true, false>(nrec, K, smem + L.rec, L.rstride, xs, xs_rows, umax, xbar, 0, blockDim.x, BAR_RECORDS, tries, a.status, row_ptr);
+        STAMPB(4);
         if (lane == 0) {
-            *reinterpret_cast<volatile int *>(cons + st) = use + 1;
-            mbar_arrive(empty + st);
+            fence_async_smem();
+            if (fjob < job1) fetch(fgi, ftb, st32 + stdelta, full + 1);
         }
-        (void)tb;
-    }
-
-    const long long tk3 = clock64();
-    if (a.dbg && lane == 0) atomicMax(reinterpret_cast<unsigned long long *>(a.dbg + (size_t)(1024 + blockIdx.x) * 8 + 5), (unsigned long long)gtime());
-    if (a.dbg && tid == 0) {
-        long long *d = a.dbg + (size_t)(1024 + blockIdx.x) * 8;
-        d[0] = tk1 - tk0;   // table + barriers
-        d[1] = tk2 - tkw;   // act records
-        d[2] = tk3 - tk2;   // job loop of warp 0
-        d[3] = wait_acc;    // ... of which waiting for a full stage
-        d[4] = gt0;
-        d[6] = tkw - tk1;   // waiting for the gate/up kernel
-        d[7] = job1 - job0;
+        fjob += nwarps;
+        advance(fgi, ftb);
+        const int sec = sec3_bytes(K), hdr_off = 2 * sec;
+        const bool mine = (g & 1) == (t >> 1);
+        const int pos_b = g >> 2, pos_o = t >> 1;
+        const uint32_t sec_b = (uint32_t)(((g >> 1) & 1) * sec);
+        const uint32_t lane_w = (uint32_t)lane * 24u, lane_s = (uint32_t)(T.sbB + g * 16);
+        int n = 0;
+        for (int job = first; job < job1; job += nwarps, ++n, advance(gi, tb)) {
+            const int st = n & 1;
+            if (!mbar_wait_lim(full + st, (n >> 1) & 1, tries)) {
+                give_up(a.status, job + nwarps < job1 ? full + ((n + 1) & 1) : nullptr, ((n + 1) >> 1) & 1);
+                return;
+            }
+            const int m = tab->m[gi], npass = (m + 1) / 2;
+            const uint32_t w32 = st32 + (uint32_t)st * stdelta;
+            if (n == 0) STAMPB(5);
+            for (int ps = 0; ps < npass; ps++) {
+                const uint32_t cb = lds32(col32 + (uint32_t)((gi * MAXM + 2 * ps + pos_b) * 4));
+                const uint32_t co = lds32(col32 + (uint32_t)((gi * MAXM + 2 * ps + pos_o) * 4));
+                const uint32_t pb = (mine && cb) ? cb + sec_b : zero32;
+                const uint32_t ph = (co ? co : rec32) + hdr_off;
+                float runA, runB, biasA, biasB;
+                gemv3_piece<FP16S>(w32 + lane_w, w32 + lane_s, T.unitsD, pb, ph, runA, runB, biasA, biasB);
+                const float fac = pow2_biased(__float_as_int(lds32f(ph + (K / 64) * 4)) + 17);
+                const float oA = __shfl_xor_sync(0xffffffffu, runA, 1), oB = __shfl_xor_sync(0xffffffffu, runB, 1);
+                if (!(t & 1) && co) {
+                    float *o = a.partial + (size_t)tab->pairs[gi][2 * ps + pos_o] * a.hidden + 16 * tb + g;
+                    o[0] = fmaf(runA + oA * (1.0f / 2048.0f), fac, biasA);
+                    o[8] = fmaf(runB + oB * (1.0f / 2048.0f), fac, biasB);
+                }
+            }
+            __syncwarp();
+            if (lane == 0 && fjob < job1) fetch(fgi, ftb, w32, full + st);
+            fjob += nwarps;
+            advance(fgi, ftb);
+            if (n == 0) STAMPB(6);
+        }
+        STAMPB(7);
+    } else {
+        // ---------------- shared expert: 4-bit tiles of 16 down rows ----------------
+        const int nps = (a.B + 3) / 4;   // passes of a tile: four tokens (hi + lo columns) each
+        const int n_tiles = T4.nTB, stride = a.gs_b * nwarps;
+        const int tile0 = (blockIdx.x - Gr) * nwarps + warp;
+        auto fetch = [&](int tile, uint32_t dst, uint64_t *bar) {   // lane 0
+            finch_mbar_expect_tx(bar, (unsigned)T4.tileB);
+            finch_bulk_g2s_a(dst, a.sh_tiles + T4.b_base + (size_t)tile * T4.tileB, (unsigned)T4.tileB, bar);
+        };
+        if (lane == 0 && tile0 < n_tiles) fetch(tile0, st32, full);
+        grid_dep_wait();   // shared_act is final
+        int xs_rows = (nwarps * L.stg) / (Ks * 4);
+        xs_rows = xs_rows > 8 ? 8 : xs_rows;
+        const int r4 = rec4_bytes(Ks, 1);
+        auto row_ptr = [&](int b) { return (const void *)(a.shared_act + (size_t)b * Ks); };
+        build_records<4, true, false>(a.B, Ks, smem + L.rec, r4, xs, xs_rows, umax, xbar, 0, blockDim.x, BAR_RECORDS, tries, a.status, row_ptr);
+        if (lane == 0) {
+            fence_async_smem();
+            if (tile0 + stride < n_tiles) fetch(tile0 + stride, st32 + stdelta, full + 1);
+        }
+        const int sec = sec4_bytes(Ks), hdr_off = 2 * sec;
+        int n = 0;
+        for (int tile = tile0; tile < n_tiles; tile += stride, ++n) {
+            const int st = n & 1;
+            if (!mbar_wait_lim(full + st, (n >> 1) & 1, tries)) {
+                give_up(a.status, tile + stride < n_tiles ? full + ((n + 1) & 1) : nullptr, ((n + 1) >> 1) & 1);
+                return;
+            }
+            const uint32_t w32 = st32 + (uint32_t)st * stdelta, s32 = w32 + T4.sbB;
+            for (int ps = 0; ps < nps; ps++) {
+                const int tokb = 4 * ps + (g >> 1), tok = 4 * ps + t;   // column g: (token, term g & 1); accumulator columns 2t, 2t + 1: token t, hi | lo
+                const bool bact = tokb < a.B;
+                const uint32_t pb = (bact ? rec32 + tokb * r4 + (g & 1) * sec : zero32) + t * 16;
+                const uint32_t ph = rec32 + (tok < a.B ? tok : 0) * r4 + hdr_off;
+                float r[4], bias[4];
+                if (a.sh_fp16) gemv4_piece<true>(w32 + lane * 16, 512, s32 + g * 8, 64, T4.groupsD, pb, bact ? GB4 : 0, ph, ph, r, bias);
+                else gemv4_piece<false>(w32 + lane * 16, 512, s32 + g * 8, 64, T4.groupsD, pb, bact ? GB4 : 0, ph, ph, r, bias);
+                const float fac = pow2_biased(__float_as_int(lds32f(ph + (Ks / 64) * 4)) + 17);
+                if (tok < a.B) {
+                    float *o = a.partial + (size_t)(a.P + tok) * a.hidden + 16 * tile + g;
+                    o[0] = fmaf(r[0] + r[1] * (1.0f / 2048.0f), fac, bias[0]);
+                    o[8] = fmaf(r[2] + r[3] * (1.0f / 2048.0f), fac, bias[2]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0 && tile + 2 * stride < n_tiles) fetch(tile + 2 * stride, w32, full + st);
+        }
     }
 }
 
@@ -1142,13 +1243,11 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const MoeArgs a) {
     __shared__ int ok[8];
     __shared__ float wk[8];
     const int b = blockIdx.y, row = blockIdx.x * 256 + threadIdx.x;
-    const long long gt0 = gtime();
     grid_dep_launch();
-    // Routing, router weights, gate scores and h_mid are inputs of the whole call: final since the preparation
-    // kernel (the first of the chain) passed its own wait, and this kernel only starts once the down kernel has,
-    // which started after the gate/up kernel's wait, i.e. after the preparation kernel completed.  Only the
-    // partial rows (the down kernel's output) have to wait; the dependent loads of the routing (mask -> id ->
-    // slot) are out of the way by then.
+    // Routing, router weights, gate scores and h_mid are inputs of the whole call: final since the gate/up
+    // kernel (the first of the chain) passed its own wait, and this kernel only starts once the down kernel has
+    // started, which was after that.  Only the partial rows (the down kernel's output) have to wait; the
+    // dependent loads of the routing (mask -> id -> slot) are out of the way by then.
     if (threadIdx.x < a.K) {
         ok[threadIdx.x] = pair_ok(a, b * a.K + threadIdx.x);
         wk[threadIdx.x] = a.weights[b * a.K + threadIdx.x];
@@ -1161,19 +1260,13 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const MoeArgs a) {
     if (!live) return;
     float moe = 0.f;
     for (int k = 0; k < a.K; k++)
-        if (ok[k]) moe = fmaf(wk[k], a.partial[(size_t)(b * a.K + k) * a.hidden + row], moe);
+        if (ok[k]) moe = fmaf(wk[k], __ldcg(a.partial + (size_t)(b * a.K + k) * a.hidden + row), moe);
     h += moe;
-    if (a.has_shared) h = fmaf(sg, a.partial[(size_t)(a.P + b) * a.hidden + row], h);
+    if (a.has_shared) h = fmaf(sg, __ldcg(a.partial + (size_t)(a.P + b) * a.hidden + row), h);
     a.hidden_out[(size_t)b * a.hidden + row] = h;
-    if (a.dbg && threadIdx.x == 0) {
-        long long *d = a.dbg + (size_t)(1400 + blockIdx.y * gridDim.x + blockIdx.x) * 8;
-        d[0] = gt0;
-        d[1] = gtime();
-    }
 }
 
 constexpr int SMEM_MAX = 227 * 1024;
-bool g_attr_set = false;
 
 int check_shared(finch_ctx *ctx, const finch_shared *sh) {
     const finch_wdesc *w[3] = {&sh->gate, &sh->up, &sh->down};
@@ -1226,15 +1319,29 @@ int prepared_shared(finch_ctx *ctx, const finch_shared *sh, cudaStream_t st, con
     return FINCH_OK;
 }
 
-inline size_t up256z(size_t n) { return (n + 255) & ~(size_t)255; }
+// The kernels' opt-in to 227 KB of shared memory is a per-device function attribute: set once per device.
+int set_attrs_once(finch_ctx *ctx) {
+    static std::mutex mu;
+    static std::vector<int> done;
+    std::lock_guard<std::mutex> lk(mu);
+    const int dev = ctx->cfg.device;
+    for (int d : done)
+        if (d == dev) return FINCH_OK;
+    const void *big[] = {(const void *)moe_gateup_kernel<false, false>, (const void *)moe_gateup_kernel<false, true>,
+                         (const void *)moe_gateup_kernel<true, false>,  (const void *)moe_gateup_kernel<true, true>,
+                         (const void *)moe_down_kernel<false>,          (const void *)moe_down_kernel<true>};
+    for (const void *f : big) {
+        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
+        // one shared-memory carve-out for all kernels of the chain: an SM that has to change its L1 / shared
+        // split between consecutive launches drains first
+        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    }
+    FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_combine_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    done.push_back(dev);
+    return FINCH_OK;
+}
 
 }  // namespace
-
-// Bytes of operand-record / group-table scratch a context needs (allocated in finch_ctx_create).
-size_t finch_decode_scratch_bytes(const finch_config &c) {
-    const size_t B = c.max_tokens;
-    return up256z(sizeof(GroupTab)) + up256z(B * rec3_bytes(c.hidden)) + up256z(B * frag4_bytes(c.hidden)) + 1024;
-}
 
 extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finch_pool *pool, int layer, const void *h_post,
                                        const int32_t *expert_ids, const float *weights, const uint8_t *valid,
@@ -1257,10 +1364,10 @@ extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finc
         if (rc) return rc;
         if ((rc = prepared_shared(ctx, shared, st, &a.sh_tiles))) return rc;
         a.has_shared = 1;
-        a.sh_scale_dtype = shared->gate.scale_dtype;
         a.shared_act = ctx->shared_act;
         a.gate_score = shared->gate_score;
         a.sh_inter = shared->gate.out_dim;
+        a.sh_fp16 = shared->gate.scale_dtype == FINCH_FP16;
     }
     a.pool_base = pool->base;
     a.slot_bytes = pool->slot_bytes;
@@ -1276,54 +1383,49 @@ extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finc
     a.B = B;
     a.hidden = c.hidden;
     a.inter = c.moe_inter;
-    a.scale_dtype = c.scale_dtype;
     a.act = ctx->act;
     a.partial = ctx->partial;
     a.status = ctx->dev_status;
     a.h_mid = h_mid;
     a.hidden_out = hidden_out;
-    a.dbg = (long long *)ctx->dbg;
-    {  // carve the scratch (same order as finch_decode_scratch_bytes)
-        const size_t Bm = c.max_tokens;
-        char *p = (char *)ctx->frag_scratch;
-        auto take = [&](size_t bytes) {
-            char *r = p;
-            p += up256z(bytes);
-            return r;
+    a.fault = ctx->fault;
+    if ((uintptr_t)h_post & 15) return finch_fail(ctx, FINCH_E_ARG, "h_post must be 16-byte aligned");
+    const int hilo = c.act_dtype == FINCH_BF16 ? 0 : 1;
+    const bool fp16s = c.scale_dtype == FINCH_FP16;
+    const int grid = ctx->sm_count;
+    if (shared) {
+        // CTAs that take the shared expert's tiles: its expected share of the MMAs of each kernel.  The routing is
+        // not known on the host: the distinct experts of a call are estimated from the batch (a token's K experts
+        // are distinct; tokens overlap more as the batch grows) and so are the passes of a popular expert's tiles.
+        const FinchTile T = finch_tile(c.hidden, c.moe_inter);
+        const FinchTile4 T4 = finch_tile4(c.hidden, a.sh_inter);
+        const double U = B == 1 ? c.top_k : std::max((double)c.top_k, a.P * (1.0 - 0.04 * (B - 1)));
+        const int ppa = hilo ? 2 : 4;
+        const double fa = 1.0 + (B > ppa ? 0.1 : 0.0) + (hilo && B > 2 ? 0.35 * (B - 2) / 6.0 : 0.0), fb = B > 2 ? 1.0 + 0.45 * (B - 2) / 6.0 : 1.0;
+        const int npa = hilo ? (B + 3) / 4 : (B + 7) / 8, npb = (B + 3) / 4;
+        auto split = [&](double routed, double sh) {
+            int gs = (int)(grid * sh / (routed + sh) + 0.5);
+            return gs < 1 ? 1 : (gs > grid / 2 ? grid / 2 : gs);
         };
-        a.gtab = (GroupTab *)take(sizeof(GroupTab));
-        a.xrec3 = (uint8_t *)take(Bm * rec3_bytes(c.hidden));
-        a.xrec4 = (uint8_t *)take(Bm * frag4_bytes(c.hidden));
+        // a gate/up tile of the shared expert carries 4 + 4 rows (half of the MMA's rows are duplicates) and its
+        // group loop is not unrolled: per MMA it costs about 2.3 times a routed tile's (measured)
+        a.gs_a = split(U * T.nTA * T.unitsA * MMA_A3 * fa, 2.3 * npa * T4.nTA * T4.groupsA * MMA_A4);
+        a.gs_b = split(U * T.nTB * T.unitsD * MMA_A3 * fb, (double)npb * T4.nTB * T4.groupsD * MMA_A4);
     }
-    const int grid = ctx->sm_count < MAXG ? ctx->sm_count : MAXG;
-    a.grid_a = a.grid_b = grid;
-    // pipeline depth: as many stages as fit
-    const SmemA A0 = smem_a_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, 0);
-    const SmemB B0 = smem_b_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, 0);
-    int sa = (SMEM_MAX - A0.total) / (A0.stg + (MAXM / 2) * TEAM_A * 32 * 4), sb = (SMEM_MAX - B0.total) / B0.stg;
-    sa = sa > 32 ? 32 : sa;
-    sb = sb > 32 ? 32 : sb;
-    {  // CTAs that also run shared-expert jobs give some stages up for the 4-bit-layout fragments of the tokens
-        const int extra = a.has_shared ? (B - A0.n4) * A0.f4s : 0;
-        if (sa >= 2 && (sa * A0.stg - extra) / A0.stg < 2) sa = 0;
-    }
-    if (sa < 2 || sb < CW_B) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "dims need too much shared memory");
-    a.stages_a = sa;
-    a.stages_b = sb;
-    const SmemA LA = smem_a_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, sa);
-    const SmemB LB = smem_b_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, sb);
-    const int prep_smem = c.hidden * 4 + 144 * 4 + 32 + (MAXP + 2) * 4 + MAXP + 8 + (int)sizeof(GroupTab) + 64;
-    if (!g_attr_set) {
-        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
-        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_down_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
-        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
-        // one shared-memory carve-out for all four kernels: an SM that has to change its L1 / shared split
-        // between consecutive launches drains first
-        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_prep_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_gateup_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_down_combine_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(moe_combine_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-        g_attr_set = true;
+    // as many teams / warps as their stages leave room for
+    int nteam = NW_MAX / TEAM;
+    while (nteam > 0 && smem_a_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, hilo, nteam * TEAM).total > SMEM_MAX) --nteam;
+    int nwb = NW_MAX;
+    while (nwb > 0 && smem_b_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, nwb).total > SMEM_MAX) nwb -= 2;
+    // the staging area (every warp's second stage) has to hold one row, and a row gets at least a warp
+    if (nteam < 2 || nwb < 4 || nteam * TEAM * smem_a_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, hilo, nteam * TEAM).stg < c.hidden * 4 ||
+        nwb * smem_b_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, nwb).stg < (c.moe_inter > a.sh_inter ? c.moe_inter : a.sh_inter) * 4)
+        return finch_fail(ctx, FINCH_E_UNSUPPORTED, "dims need too much shared memory");
+    const SmemA LA = smem_a_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, hilo, nteam * TEAM);
+    const SmemB LB = smem_b_layout(c.hidden, c.moe_inter, a.sh_inter, B, a.has_shared, nwb);
+    {
+        int rc = set_attrs_once(ctx);
+        if (rc) return rc;
     }
     cudaEvent_t *pe = nullptr;
     if (ctx->profile) {
@@ -1351,14 +1453,16 @@ extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finc
         void *args[] = {(void *)&a};
         return cudaLaunchKernelExC(&cfg, fn, args);
     };
-    FINCH_CUDA_OK(ctx, launch((const void *)moe_prep_kernel, dim3(B + 1), 256, prep_smem));
+    const void *ka = hilo ? (fp16s ? (const void *)moe_gateup_kernel<true, true> : (const void *)moe_gateup_kernel<true, false>)
+                          : (fp16s ? (const void *)moe_gateup_kernel<false, true> : (const void *)moe_gateup_kernel<false, false>);
+    const void *kb = fp16s ? (const void *)moe_down_kernel<true> : (const void *)moe_down_kernel<false>;
     if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[0], st));
-    FINCH_CUDA_OK(ctx, launch((const void *)moe_gateup_kernel, dim3(grid), NT_A, LA.total));
+    FINCH_CUDA_OK(ctx, launch(ka, dim3(grid), nteam * TEAM * 32, LA.total));
     if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[1], st));
-    FINCH_CUDA_OK(ctx, launch((const void *)moe_down_combine_kernel, dim3(grid), NT_B, LB.total));
+    FINCH_CUDA_OK(ctx, launch(kb, dim3(grid), nwb * 32, LB.total));
     FINCH_CUDA_OK(ctx, launch((const void *)moe_combine_kernel, dim3((c.hidden + 255) / 256, B), 256, 0));
     if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[2], st));
-    ctx->launches += 4;
+    ctx->launches += 3;
     return FINCH_OK;
 }
 
@@ -1388,9 +1492,14 @@ extern "C" int finch_profile_read(finch_ctx *ctx, float *ms_gateup, float *ms_do
     return FINCH_OK;
 }
 
-// Kept for binary compatibility of the test hook: the preparation kernel now always runs.
-extern "C" int finch_debug_timing(finch_ctx *ctx, void *buf) {
-    if (!ctx) return FINCH_E_ARG;
-    ctx->dbg = buf;
+#ifdef FINCH_STAMPS
+extern "C" __attribute__((visibility("default"))) int finch_stamps_read(long long *host, int n) {
+    return cudaMemcpyFromSymbol(host, g_stamps, (size_t)n * sizeof(long long)) == cudaSuccess ? 0 : 1;
+}
+#endif
+
+extern "C" int finch_debug_fault(finch_ctx *ctx, int kind) {
+    if (!ctx || kind < 0 || kind > 1) return FINCH_E_ARG;
+    ctx->fault = kind;
     return FINCH_OK;
 }

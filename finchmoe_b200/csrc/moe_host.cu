@@ -1,7 +1,7 @@
 // Host-pointer entry point of the MoE layer: packs the caller's CPU buffers
-// into one pinned staging block, encodes the decode or prefill path on it
-// (decode-sized calls: the kernels work on the pinned block in place; larger
-// ones: one transfer to the device, one back) and waits.
+// into one pinned staging block, moves it to the device in one transfer, encodes
+// the decode or prefill path (decode-sized calls write their result rows straight
+// into the pinned block; larger ones copy them back) and waits.
 #include "finch_internal.cuh"
 
 int finch_stage_reserve(finch_ctx *ctx, size_t bytes);
@@ -19,7 +19,7 @@ extern "C" int finch_moe_forward_host(finch_ctx *ctx, finch_pool *pool, int laye
     const size_t n_x = (size_t)T * c.hidden * elt, n_id = (size_t)T * c.top_k * 4, n_w = n_id, n_v = valid ? (size_t)T * c.top_k : 0;
     const size_t n_s = shared ? (size_t)T * 4 : 0, n_h = h_mid ? (size_t)T * c.hidden * 4 : 0, n_o = (size_t)T * c.hidden * 4;
     const size_t o_x = 0, o_id = o_x + up256(n_x), o_w = o_id + up256(n_id), o_v = o_w + up256(n_w), o_s = o_v + up256(n_v),
-                 o_h = o_s + up256(n_s), o_o = o_h + up256(n_h), total = o_o + up256(n_o);
+                 o_h = o_s + up256(n_s), o_o = o_h + up256(n_h), o_st = o_o + up256(n_o), total = o_st + 256;
     int rc = finch_stage_reserve(ctx, total);
     if (rc) return rc;
     cudaSetDevice(c.device);
@@ -30,26 +30,23 @@ extern "C" int finch_moe_forward_host(finch_ctx *ctx, finch_pool *pool, int laye
     if (valid) memcpy(hs + o_v, valid, n_v);
     if (shared) memcpy(hs + o_s, shared_gate_score_host, n_s);
     if (h_mid) memcpy(hs + o_h, h_mid, n_h);
-    const bool small = (size_t)T * c.top_k <= FINCH_MAX_PAIRS;
-    // Where the kernels find the staged inputs and leave the result.  A decode-sized call moves a few tens of KB:
-    // its kernels read the pinned staging block in place over the bus and the combine kernel writes the result
-    // rows straight into it, which saves the two copy operations and their stream dependencies (each costs more
-    // than moving the bytes).  Larger calls copy to and from device memory.  FINCH_HOST_PATH=0 forces copies.
+    // what finch_encode_moe_decode accepts; everything else goes through the prefill entry (which splits)
+    const bool small = T <= 8 && T <= c.max_tokens && (size_t)T * c.top_k <= FINCH_MAX_PAIRS;
+    // The inputs cross the bus in one copy into device memory: every CTA of the gate/up kernel reads the
+    // activations and the routing.  The result of a decode-sized call is a few tens of KB: the combine kernel
+    // writes its rows straight into the pinned staging block, which saves the copy back and its stream
+    // dependency (it costs more than moving the bytes).  FINCH_HOST_PATH=0 forces a copy back as well.
     static const int host_path = [] {
         const char *e = getenv("FINCH_HOST_PATH");
-        return e ? atoi(e) : 2;
+        return e ? atoi(e) : 1;
     }();
     char *in = ds, *out = ds;
     if (small && host_path >= 1) {
         void *m = nullptr;
-        if (cudaHostGetDevicePointer(&m, hs, 0) == cudaSuccess && m) {
-            in = (char *)m;
-            if (host_path >= 2) out = (char *)m;
-        } else {
-            cudaGetLastError();
-        }
+        if (cudaHostGetDevicePointer(&m, hs, 0) == cudaSuccess && m) out = (char *)m;
+        else cudaGetLastError();
     }
-    if (in == ds) FINCH_CUDA_OK(ctx, cudaMemcpyAsync(ds, hs, o_o, cudaMemcpyHostToDevice, ctx->stream));
+    FINCH_CUDA_OK(ctx, cudaMemcpyAsync(ds, hs, o_o, cudaMemcpyHostToDevice, ctx->stream));
     finch_shared sh;
     if (shared) {
         sh = *shared;
@@ -61,7 +58,11 @@ extern "C" int finch_moe_forward_host(finch_ctx *ctx, finch_pool *pool, int laye
             (float *)(out + o_o), T);
     if (rc) return rc;
     if (out == ds) FINCH_CUDA_OK(ctx, cudaMemcpyAsync(hs + o_o, ds + o_o, n_o, cudaMemcpyDeviceToHost, ctx->stream));
+    // the device status word rides along (a bounded wait that ran out leaves the output undefined)
+    FINCH_CUDA_OK(ctx, cudaMemcpyAsync(hs + o_st, ctx->dev_status, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
     FINCH_CUDA_OK(ctx, cudaStreamSynchronize(ctx->stream));
     memcpy(hidden_out, hs + o_o, n_o);
+    const int dev_rc = *(const int *)(hs + o_st);
+    if (dev_rc != FINCH_OK) return finch_fail(ctx, dev_rc, "device status %d after the MoE layer", dev_rc);
     return FINCH_OK;
 }

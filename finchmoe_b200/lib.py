@@ -11,6 +11,7 @@ import re
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 SO_PATH = os.path.join(PKG, "libfinchcuda.so")
+SO_PATH = os.environ.get("FINCH_CUDA_SO", SO_PATH)   # another build of the same sources (e.g. one with phase stamps)
 HEADER = os.path.join(os.path.dirname(PKG), "include", "finch_cuda.h")
 
 OK, E_ARG, E_NOSLOT, E_CUDA, E_NCCL, E_TIMEOUT, E_UNSUPPORTED, E_NOMEM = range(8)
@@ -90,9 +91,10 @@ _PROTOS = {
     "finch_event_destroy": (None, [_vp]),
     "finch_sync": (_i, [_vp]),
     "finch_device_status": (_i, [_vp, C.POINTER(_i)]),
+    "finch_device_status_clear": (_i, [_vp]),
     "finch_debug_dequant": (_i, [_vp, C.POINTER(WDesc), _vp, _vp, _vp, _i]),
     "finch_launch_count": (C.c_uint64, [_vp]),
-    "finch_debug_timing": (_i, [_vp, _vp]),
+    "finch_debug_fault": (_i, [_vp, _i]),
     "finch_profile_enable": (_i, [_vp, _i]),
     "finch_profile_read": (_i, [_vp, C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(_i)]),
 }

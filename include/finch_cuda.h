@@ -241,8 +241,11 @@ FINCH_API int finch_event_record(finch_event *ev, finch_stream stream);
 FINCH_API int finch_event_wait(finch_event *ev, int timeout_ms); /* FINCH_E_TIMEOUT if not done in time */
 FINCH_API void finch_event_destroy(finch_event *ev);
 FINCH_API int finch_sync(finch_ctx *ctx);
-/* Sticky device-side status (bounded waits inside kernels); 0 when clean. */
+/* Sticky device-side status (bounded waits inside kernels); 0 when clean.  Synchronises with the
+ * work already queued.  finch_device_status_clear puts it back to 0 after the caller has dealt
+ * with a failure (the reference's analogue is discard_deferred_experts, finchmoe/infer.m:7448-7454). */
 FINCH_API int finch_device_status(finch_ctx *ctx, int *status_out);
+FINCH_API int finch_device_status_clear(finch_ctx *ctx);
 
 /* --compare-experts (finchmoe/infer.m:9766): the bit-exactness probe.  Writes,
  * for a weight tensor, the unpacked integer codes [out][in] (u8), the fp32
@@ -315,11 +318,15 @@ FINCH_API int finch_encode_ep_combine(finch_ctx *ctx, finch_stream stream, float
  * finch_pool_fill_synthetic gives them in a full pool; the pool needs n_layers * (e1 - e0) slots. */
 FINCH_API int finch_pool_fill_synthetic_range(finch_pool *pool, int layer0, int layer1, int e0, int e1, uint64_t seed);
 
-/* Diagnostics: with a non-NULL device buffer of 2048 rows of 8 int64, the kernels of
- * finch_encode_moe_decode record per-CTA clock-cycle and global-timer stamps of their phases
- * there (rows 0.. gate/up, 1024.. down, 1300.. preparation, 1400.. combine).  NULL switches it
- * off.  No counterpart in the reference. */
-FINCH_API int finch_debug_timing(finch_ctx *ctx, void *device_buf);
+/* Failure injection for tests of the bounded device-side waits (no counterpart in the reference;
+ * its waits are Metal's waitUntilCompleted, finchmoe/infer.m:7437-7454).  kind 1: in the following
+ * finch_encode_moe_decode calls the warp of the gate/up kernel that owns the first piece of the
+ * first tile withholds its first weight fetch
+ * and every wait of that kernel gives up after microseconds instead of a fraction of a second.
+ * The warps that wait in vain record FINCH_E_TIMEOUT in the device status word
+ * (finch_device_status) and return; nothing faults, spins for long or is left in flight, and the
+ * call's output is undefined.  kind 0 switches it off. */
+FINCH_API int finch_debug_fault(finch_ctx *ctx, int kind);
 
 /* Count of kernels launched by this context since creation (benchmark bookkeeping). */
 FINCH_API uint64_t finch_launch_count(const finch_ctx *ctx);

@@ -511,3 +511,50 @@ def test_moe_decode_extreme_routings_full_size(api, shape):
     finally:
         pool.destroy()
         ctx.destroy()
+
+
+def test_bounded_wait_runs_out_and_reports_timeout(api):
+    """A warp of the gate/up kernel withholds its weight fetch (finch_debug_fault): the warps that wait for it give up
+    after their (shortened) limit, the device status word reads FINCH_E_TIMEOUT, the host entry point returns that
+    code, nothing hangs or faults, and after clearing the status the same context computes correct results again."""
+    ctx, pool, blocks, cfg, rng = _mk_small(api, L.FP16, L.BF16, seed=77)
+    try:
+        x = synth.activations(rng, 4, 256)
+        ids, w = synth.zipf_routing(rng, 4, 16, 8)
+        good = ctx.moe_forward_host(pool, 1, x, ids, w)
+        ctx.debug_fault(1)
+        with pytest.raises(L.FinchError) as e:
+            ctx.moe_forward_host(pool, 1, x, ids, w)
+        assert e.value.status == L.E_TIMEOUT
+        assert ctx.device_status() == L.E_TIMEOUT
+        ctx.debug_fault(0)
+        ctx.device_status_clear()
+        assert ctx.device_status() == 0
+        again = ctx.moe_forward_host(pool, 1, x, ids, w)
+        assert np.array_equal(good.view(np.uint32), again.view(np.uint32))
+        assert_close(again, _oracle_layer(blocks, ids, w, None, x, cfg), "after a timeout")
+    finally:
+        pool.destroy()
+        ctx.destroy()
+
+
+def test_host_path_top_k_4_more_than_8_tokens(api):
+    """T = 12 with top_k = 4 is 48 pairs (fewer than 64) but more tokens than the decode entry takes: the host
+    entry point must route it through the chunked path."""
+    ctx = api.Context(hidden=256, n_experts=16, top_k=4, moe_inter=128, shared_inter=128, n_layers=1,
+                      scale_dtype=L.FP16, act_dtype=L.BF16, max_tokens=16)
+    rng = synth.rng_for(1, 512)
+    pool = ctx.pool()
+    try:
+        blocks = {}
+        for e in range(16):
+            blocks[e] = synth.expert_block(rng, 256, 128, 64, 3, L.FP16)
+            pool.put(0, e, blocks[e])
+        x = synth.activations(rng, 12, 256)
+        ids, w = synth.zipf_routing(rng, 12, 16, 4)
+        out = ctx.moe_forward_host(pool, 0, x, ids, w)
+        want = _oracle_layer(blocks, ids, w, None, x, dict(hidden=256, inter=128, sd=L.FP16))
+        assert_close(out, want, "top_k=4, T=12")
+    finally:
+        pool.destroy()
+        ctx.destroy()
