@@ -508,12 +508,15 @@ __device__ __forceinline__ void gemv3_piece(uint32_t pw, uint32_t ps, int nu, ui
     const int t = threadIdx.x & 3;
     const uint32_t pb16 = pb + t * 16, pb8 = pb + 256 + t * 8;
     runA = runB = biasA = biasB = 0.f;
+#ifndef FINCH_ROLLED_UNITS
     if (nu == 4) {
 #pragma unroll
         for (int u = 0; u < 4; u++) gemv3_unit<FP16S>(pw + u * 768, ps + u * 128, pb16 + u * UB, pb8 + u * UB, ph + u * 8, runA, runB, biasA, biasB);
-    } else {
-        for (int u = 0; u < nu; u++) gemv3_unit<FP16S>(pw + u * 768, ps + u * 128, pb16 + u * UB, pb8 + u * UB, ph + u * 8, runA, runB, biasA, biasB);
+        return;
     }
+#endif
+#pragma unroll 1
+    for (int u = 0; u < nu; u++) gemv3_unit<FP16S>(pw + u * 768, ps + u * 128, pb16 + u * UB, pb8 + u * UB, ph + u * 8, runA, runB, biasA, biasB);
 }
 
 // ngr 64-code groups of a 4-bit piece against the eight columns of a pass.
@@ -927,48 +930,43 @@ __global__ void __launch_bounds__(NW_MAX * 32, 1) moe_gateup_kernel(const MoeArg
             STAMP_ADD(8, c1 - c0);
             if (n == 0) STAMP(4);
             const uint32_t w32 = st32 + (uint32_t)st * stdelta;
-            float resA[HILO ? 4 : 2], resB[HILO ? 4 : 2];
-            if (!dead) {
-#pragma unroll
-                for (int ps = 0; ps < (HILO ? 4 : 2); ps++) {
-                    if (ps < npass) {
-                        const uint32_t cb = lds32(col32 + (uint32_t)((gi * MAXM + ps * PER_PASS + pos_b) * 4));
-                        const uint32_t co = lds32(col32 + (uint32_t)((gi * MAXM + ps * PER_PASS + pos_o) * 4));
-                        const uint32_t pb = ((mine && cb) ? cb + sec_b : zero32) + boff;
-                        const uint32_t ph = (co ? co : rec32) + hdr_off;
-                        float runA, runB, biasA, biasB;
-                        gemv3_piece<FP16S>(w32 + lane_w, w32 + lane_s, nu, pb, ph + u0 * 8, runA, runB, biasA, biasB);
-                        const float fac = pow2_biased(__float_as_int(lds32f(ph + (K / 64) * 4)) + 17);
-                        if (HILO) {
-                            const float oA = __shfl_xor_sync(0xffffffffu, runA, 1), oB = __shfl_xor_sync(0xffffffffu, runB, 1);
-                            runA += oA * (1.0f / 2048.0f);
-                            runB += oB * (1.0f / 2048.0f);
-                        }
-                        resA[ps] = fmaf(runA, fac, biasA);
-                        resB[ps] = fmaf(runB, fac, biasB);
-                    }
+            for (int ps = 0; ps < npass && !dead; ps++) {
+                const uint32_t cb = lds32(col32 + (uint32_t)((gi * MAXM + ps * PER_PASS + pos_b) * 4));
+                const uint32_t co = lds32(col32 + (uint32_t)((gi * MAXM + ps * PER_PASS + pos_o) * 4));
+                const uint32_t pb = ((mine && cb) ? cb + sec_b : zero32) + boff;
+                const uint32_t ph = (co ? co : rec32) + hdr_off;
+                float runA, runB, biasA, biasB;
+                gemv3_piece<FP16S>(w32 + lane_w, w32 + lane_s, nu, pb, ph + u0 * 8, runA, runB, biasA, biasB);
+                const float fac = pow2_biased(__float_as_int(lds32f(ph + (K / 64) * 4)) + 17);
+                if (HILO) {
+                    const float oA = __shfl_xor_sync(0xffffffffu, runA, 1), oB = __shfl_xor_sync(0xffffffffu, runB, 1);
+                    runA += oA * (1.0f / 2048.0f);
+                    runB += oB * (1.0f / 2048.0f);
                 }
+                if (ps == 0) {
+                    if (npass == 1) {   // the stage is free before the hand-over: the next fetch goes out first
+                        __syncwarp();
+                        if (lane == 0 && fj < J.j1) fetch(J, fj, w32, full + st);
+                    }
+                    const long long c2 = STAMP_CLK();
+                    STAMP_ADD(9, c2 - c1);
+                    // the previous tile's partial sums have been read before this tile's overwrite them
+                    if (nkw > 1 && n > 0 && !wait_ge(reduced + team, n, spins)) {
+                        give_up(a.status, j + 1 < J.j1 ? full + ((n + 1) & 1) : nullptr, ((n + 1) >> 1) & 1);
+                        dead = true;
+                        break;
+                    }
+                    STAMP_ADD(10, STAMP_CLK() - c2);
+                }
+                if (co && (!HILO || !(t & 1))) sts64f(my_slot + (uint32_t)((ps * PER_PASS + pos_o) * 64), fmaf(runA, fac, biasA), fmaf(runB, fac, biasB));
+            }
+            if (npass > 1 && !dead) {
                 __syncwarp();   // every lane is done with the stage
                 if (lane == 0 && fj < J.j1) fetch(J, fj, w32, full + st);
             }
             fj += J.step;
-            const long long c2 = STAMP_CLK();
-            STAMP_ADD(9, c2 - c1);
             if (n == 0) STAMP(5);
-            // the previous tile's partial sums have been read before this tile's overwrite them
-            if (nkw > 1 && n > 0 && !dead && !wait_ge(reduced + team, n, spins)) {
-                give_up(a.status, j + 1 < J.j1 ? full + ((n + 1) & 1) : nullptr, ((n + 1) >> 1) & 1);
-                dead = true;
-            }
-            if (!dead) {
-#pragma unroll
-                for (int ps = 0; ps < (HILO ? 4 : 2); ps++) {
-                    const int pio = ps * PER_PASS + pos_o;
-                    if (ps < npass && pio < m && (!HILO || !(t & 1))) sts64f(my_slot + (uint32_t)(pio * 64), resA[ps], resB[ps]);
-                }
-            }
             finish(n, m, [&](int ti, int gg, float v) { a.act[(size_t)tab->pairs[gi][ti] * a.inter + 8 * ta + gg] = v; });
-            STAMP_ADD(10, STAMP_CLK() - c2);
             STAMP_ADD(11, 1);
             if (++ta == T.nTA) ta = 0, ++gi;
         }
