@@ -33,6 +33,52 @@ def build(force: bool = False) -> str:
     return _SO
 
 
+_REF_SO = os.path.join(_HERE, "_ref", "libfinch_ref.so")
+_ref_lib = None
+
+
+def build_ref(ref_root: str = "/root/reference") -> str | None:
+    """Compile the reference's own CPU math (``make ref``: its pure-C region, from a reference checkout)
+    into ``oracle/_ref/``.  Returns the library's path, the path of an earlier build when the checkout is
+    absent (the build travels with the tree), or None."""
+    src = os.path.join(ref_root, "finchmoe", "infer.m")
+    if os.path.exists(src):
+        subprocess.check_call(["make", "-C", _HERE, "-s", "ref", f"REF={ref_root}"])
+    return _REF_SO if os.path.exists(_REF_SO) else None
+
+
+def ref_lib():
+    """ctypes handle of oracle/_ref/libfinch_ref.so (the reference's CPU functions), or None if it cannot be had."""
+    global _ref_lib
+    if _ref_lib is None:
+        so = build_ref()
+        if so is None:
+            return None
+        R = C.CDLL(so)
+        f32p, u16p, i32p = C.POINTER(C.c_float), C.POINTER(C.c_uint16), C.POINTER(C.c_int)
+        R.ref_bf16_to_f32.restype = C.c_float
+        R.ref_bf16_to_f32.argtypes = [C.c_uint16]
+        R.ref_f32_to_bf16.restype = C.c_uint16
+        R.ref_f32_to_bf16.argtypes = [C.c_float]
+        R.ref_fp16_to_f32.restype = C.c_float
+        R.ref_fp16_to_f32.argtypes = [C.c_uint16]
+        R.ref_cpu_sigmoid.restype = C.c_float
+        R.ref_cpu_sigmoid.argtypes = [C.c_float]
+        R.ref_gguf_dequant_row.argtypes = [C.c_void_p, f32p, C.c_int, C.c_int]
+        R.ref_cpu_dequant_matvec.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, f32p, f32p, C.c_int, C.c_int, C.c_int, C.c_int]
+        R.ref_cpu_rms_norm.argtypes = [f32p, u16p, f32p, C.c_int, C.c_float]
+        R.ref_cpu_swiglu.argtypes = [f32p, f32p, f32p, C.c_int]
+        R.ref_cpu_softmax.argtypes = [f32p, C.c_int]
+        R.ref_cpu_topk.argtypes = [f32p, C.c_int, C.c_int, i32p, f32p]
+        R.ref_cpu_normalize_weights.argtypes = [f32p, C.c_int]
+        R.ref_cpu_vec_madd.argtypes = [f32p, f32p, C.c_float, C.c_int]
+        for n in ("ref_gguf_dequant_row", "ref_cpu_dequant_matvec", "ref_cpu_rms_norm", "ref_cpu_swiglu", "ref_cpu_softmax",
+                  "ref_cpu_topk", "ref_cpu_normalize_weights", "ref_cpu_vec_madd"):
+            getattr(R, n).restype = None
+        _ref_lib = R
+    return _ref_lib
+
+
 class _WDesc(C.Structure):
     _fields_ = [("W", C.c_void_p), ("S", C.c_void_p), ("B", C.c_void_p), ("out_dim", C.c_int),
                 ("in_dim", C.c_int), ("group", C.c_int), ("bits", C.c_int), ("scale_dtype", C.c_int)]
