@@ -2,13 +2,16 @@
 //
 //   D[128 weight rows, TN tokens] += Wdq[128, K] * X[TN, K]^T        (bf16 x bf16 -> fp32)
 //
-// One CTA owns one 128-row weight tile and up to TNMAX tokens.  Per K-block of 128 values its eight
-// warps read packed codes straight from HBM, dequantise them to bf16 -- RNE(fl32(fl32(q*s)+b)), the
-// value the reference's dequantised weight rounds to (quant_audit.py:245 semantics) -- and write them,
-// together with the tokens' activations, into shared memory in the 128-byte-swizzled K-major layout
-// the tensor core reads; one elected thread then issues eight tcgen05.mma (K = 16 each) and commits
-// them to an mbarrier.  Two stages: the warps dequantise block i+1 while the tensor core works on
-// block i.  The epilogue reads the accumulator with tcgen05.ld, one lane (= weight row) per thread.
+// One CTA owns one 128-row weight tile and up to tn_max tokens.  Per K block of 128 values its eight
+// dequantising warps turn packed codes (EXPERT_*: brought into a ring of shared-memory slots by bulk copies;
+// DENSE4: loaded from global memory one block ahead) into the weight fl32(fl32(q*s)+b) -- the value the
+// reference's dequantised weight has (quant_audit.py:245 semantics) -- and write it as TWO bf16 planes, the
+// value rounded to bf16 and the bf16-rounded remainder (16 significant bits together), into shared memory in
+// the 128-byte-swizzled K-major layout the tensor core reads; the tokens' activations arrive by cp.async
+// (one bf16 plane, or two when the caller passes the remainder plane of fp32 activations).  Lane 0 of a ninth,
+// control warp issues the block's tcgen05.mma (K = 16 each, both weight planes into the same accumulator)
+// and commits them to an mbarrier.  Two stages: the warps dequantise block i+1 while the tensor core works
+// on block i.  The epilogue reads the accumulator with tcgen05.ld, one lane (= weight row) per thread.
 //
 // Shared by moe_prefill.cu (grouped 3-bit expert GEMMs over the pool's tiled layout) and the dense
 // 4-bit projections.  Every wait is bounded; on a time-out the CTA reports through `status`, frees
@@ -62,7 +65,7 @@ struct Args {
 };
 
 __host__ __device__ inline int smem_bytes(int tn_max, int planes, int expert) {
-    return 1024 + NS * (2 * A_ATOM + planes * 2 * tn_max * 128) + (expert ? RD * RAW_STAGE : 0) + 256 + tn_max * 4;
+    return 1024 + NS * (4 * A_ATOM + planes * 2 * tn_max * 128) + (expert ? RD * RAW_STAGE : 0) + 256 + tn_max * 4;
 }
 
 __host__ __device__ inline int tmem_cols(int tn_max) { return tn_max <= 32 ? 32 : tn_max <= 64 ? 64 : tn_max <= 128 ? 128 : 256; }
@@ -120,6 +123,11 @@ __device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     return r;
 }
+// two fp32 values -> their bf16 images (packed) and the bf16 images of the remainders
+__device__ __forceinline__ void bf16x2_split(float lo, float hi, uint32_t &h, uint32_t &r) {
+    h = bf16x2_rn(lo, hi);
+    r = bf16x2_rn(lo - __uint_as_float(h << 16), hi - __uint_as_float(h & 0xffff0000u));
+}
 __device__ __forceinline__ void st_shared16(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
@@ -134,7 +142,7 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // 16-bit half is the fp16 subnormal q * 2^(p-24); widening it to fp32 is exact, and
 //   fma(q * 2^(p-24), s * 2^(24-p), b)  =  round_fp32(q * s + b)  =  fl32(fl32(q * s) + b)
 // because q * s is exact in fp32 (3- or 4-bit q, at most 11-bit s): the value the reference's
-// dequantised weight has (quant_audit.py:245), rounded once more to bf16 for the tile.
+// dequantised weight has (quant_audit.py:245), written to the tile as a bf16 value and a bf16 remainder.
 struct GroupScale {
     float sp[8];   // s * 2^(24-p), p = 0..7
     float b;
@@ -149,9 +157,9 @@ __device__ __forceinline__ GroupScale group_scale(float s, float b) {
 __device__ __forceinline__ float half_lo(uint32_t r) { return __low2float(*reinterpret_cast<const __half2 *>(&r)); }
 __device__ __forceinline__ float half_hi(uint32_t r) { return __high2float(*reinterpret_cast<const __half2 *>(&r)); }
 
-// 32 three-bit codes in three words (a little-endian bit stream) -> four chunks of 8 bf16.
+// 32 three-bit codes in three words (a little-endian bit stream) -> four chunks of 8 bf16 (value plane o, remainder plane ol).
 // 18 masked registers hold two codes each; IDX / POS say which code and at which bit of its half.
-__device__ __forceinline__ void dq3_piece(uint32_t w0, uint32_t w1, uint32_t w2, const GroupScale &gs, uint32_t (&o)[16]) {
+__device__ __forceinline__ void dq3_piece(uint32_t w0, uint32_t w1, uint32_t w2, const GroupScale &gs, uint32_t (&o)[16], uint32_t (&ol)[16]) {
     constexpr int IDX[36] = {0, 6, 1, 7, 2, -1, 3, 8, 4, 9, 5, 10, 11, 16, 12, 17, 13, 18,
                              14, 19, 15, 20, -1, 21, 22, 27, 23, 28, -1, 29, 24, 30, 25, 31, 26, -1};
     constexpr int POS[36] = {0, 2, 3, 5, 6, 0, 1, 0, 4, 3, 7, 6, 1, 0, 4, 3, 7, 6,
@@ -172,10 +180,10 @@ __device__ __forceinline__ void dq3_piece(uint32_t w0, uint32_t w1, uint32_t w2,
         v[IDX[k]] = fmaf(q, gs.sp[POS[k]], gs.b);
     }
 #pragma unroll
-    for (int i = 0; i < 16; i++) o[i] = bf16x2_rn(v[2 * i], v[2 * i + 1]);
+    for (int i = 0; i < 16; i++) bf16x2_split(v[2 * i], v[2 * i + 1], o[i], ol[i]);
 }
-// 8 four-bit codes in one word -> one chunk of 8 bf16.
-__device__ __forceinline__ void dq4_word(uint32_t w, const GroupScale &gs, uint32_t (&o)[4]) {
+// 8 four-bit codes in one word -> one chunk of 8 bf16 (value plane and remainder plane).
+__device__ __forceinline__ void dq4_word(uint32_t w, const GroupScale &gs, uint32_t (&o)[4], uint32_t (&ol)[4]) {
     const uint32_t x = w >> 8;
     const uint32_t e0 = w & 0x000F000Fu, e1 = w & 0x00F000F0u, e2 = x & 0x000F000Fu, e3 = x & 0x00F000F0u;   // codes (0,4) (1,5) (2,6) (3,7)
     float v[8];
@@ -184,7 +192,7 @@ __device__ __forceinline__ void dq4_word(uint32_t w, const GroupScale &gs, uint3
     v[2] = fmaf(half_lo(e2), gs.sp[0], gs.b); v[6] = fmaf(half_hi(e2), gs.sp[0], gs.b);
     v[3] = fmaf(half_lo(e3), gs.sp[4], gs.b); v[7] = fmaf(half_hi(e3), gs.sp[4], gs.b);
 #pragma unroll
-    for (int i = 0; i < 4; i++) o[i] = bf16x2_rn(v[2 * i], v[2 * i + 1]);
+    for (int i = 0; i < 4; i++) bf16x2_split(v[2 * i], v[2 * i + 1], o[i], ol[i]);
 }
 
 // grid: x = 128-row weight tile; EXPERT_*: y = (expert, token tile) item; DENSE4: z = token tile.  block: 288 threads.
@@ -222,7 +230,7 @@ __global__ void __launch_bounds__(NTB) dqgemm_tc_kernel(const Args a) {
     // The two activation planes sit side by side along N: rows [0, tn) of an atom are plane 0, rows
     // [tn, 2 tn) plane 1, one MMA covers both and the epilogue adds the two halves of the accumulator.
     const int planes = a.X2 ? 2 : 1, b_atom = planes * tn_max * 128;
-    const int stage_bytes = 2 * A_ATOM + 2 * b_atom;
+    const int stage_bytes = 4 * A_ATOM + 2 * b_atom;   // weights: [value | remainder plane][K half] atoms, then the activations' atoms
     const bool expert = a.mode != DENSE4;
     const uint32_t raw = base + NS * stage_bytes;     // EXPERT_*: ring of packed blocks, filled by bulk copies
     const uint32_t ctl = raw + (expert ? RD * RAW_STAGE : 0);   // barriers, tensor-memory address, row list
@@ -240,7 +248,7 @@ __global__ void __launch_bounds__(NTB) dqgemm_tc_kernel(const Args a) {
 
     // zero the activation halves of the stages once: rows >= m are never written and must read as 0
     for (int s = 0; s < NS; s++) {
-        const uint32_t bst = base + s * stage_bytes + 2 * A_ATOM;
+        const uint32_t bst = base + s * stage_bytes + 4 * A_ATOM;
         for (int i = tid; i < 2 * b_atom / 16 && !control; i += NT) st_shared16(bst + i * 16, 0u, 0u, 0u, 0u);
     }
     for (int j = tid; j < m && !control; j += NT) {
@@ -323,7 +331,7 @@ __global__ void __launch_bounds__(NTB) dqgemm_tc_kernel(const Args a) {
     // descriptors of the stages; a K step of 16 values advances the start address by 32 bytes (2 units)
     auto issue_mma = [&](int kb) {
         const int st = kb % NS;
-        const uint32_t ast = base + st * stage_bytes, bst = ast + 2 * A_ATOM;
+        const uint32_t ast = base + st * stage_bytes, bst = ast + 4 * A_ATOM;
         const uint64_t ad = smem_desc(ast), bd = smem_desc(bst);
         tc_fence_after();
 #pragma unroll
@@ -331,6 +339,7 @@ __global__ void __launch_bounds__(NTB) dqgemm_tc_kernel(const Args a) {
             const uint64_t aoff = (uint64_t)(((k >> 2) * A_ATOM + (k & 3) * 32) >> 4);
             const uint64_t boff = (uint64_t)(((k >> 2) * b_atom + (k & 3) * 32) >> 4);
             tc_mma_bf16(tmem_d, ad + aoff, bd + boff, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            tc_mma_bf16(tmem_d, ad + aoff + (uint64_t)((2 * A_ATOM) >> 4), bd + boff, idesc, 1u);   // the remainder plane of the weights
         }
         tc_commit(done + st);
     };
@@ -360,7 +369,7 @@ __global__ void __launch_bounds__(NTB) dqgemm_tc_kernel(const Args a) {
     } else
     for (int kb = 0; kb < nkb; kb++) {
         const int st = kb % NS, use = kb / NS, slot = kb % RD;
-        const uint32_t ast = base + st * stage_bytes, bst = ast + 2 * A_ATOM;
+        const uint32_t ast = base + st * stage_bytes, bst = ast + 4 * A_ATOM;
         // the tensor core must be done with this stage's previous contents; the packed block must have landed
         // (the decision to give up is taken per warp, so that no lane leaves its warp behind)
         bool ok = !*abort_flag;
@@ -411,17 +420,21 @@ __global__ void __launch_bounds__(NTB) dqgemm_tc_kernel(const Args a) {
         if (a.mode == DENSE4) {
 #pragma unroll
             for (int c = 0; c < 8; c++) {
-                uint32_t o[4];
-                dq4_word(cur[c], gs, o);
+                uint32_t o[4], ol[4];
+                dq4_word(cur[c], gs, o, ol);
                 st_shared16(arow + ((c ^ rx) << 4), o[0], o[1], o[2], o[3]);
+                st_shared16(arow + 2 * A_ATOM + ((c ^ rx) << 4), ol[0], ol[1], ol[2], ol[3]);
             }
         } else {
 #pragma unroll
             for (int t = 0; t < 2; t++) {
-                uint32_t o[16];
-                dq3_piece(cur[3 * t], cur[3 * t + 1], cur[3 * t + 2], gs, o);
+                uint32_t o[16], ol[16];
+                dq3_piece(cur[3 * t], cur[3 * t + 1], cur[3 * t + 2], gs, o, ol);
 #pragma unroll
-                for (int c = 0; c < 4; c++) st_shared16(arow + (((t * 4 + c) ^ rx) << 4), o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                for (int c = 0; c < 4; c++) {
+                    st_shared16(arow + (((t * 4 + c) ^ rx) << 4), o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                    st_shared16(arow + 2 * A_ATOM + (((t * 4 + c) ^ rx) << 4), ol[4 * c], ol[4 * c + 1], ol[4 * c + 2], ol[4 * c + 3]);
+                }
             }
         }
         cp_async_wait_all();

@@ -3,8 +3,8 @@
 // (gpu_encode_prefill_matvec, infer.m:3672).
 //
 // Two paths:
-//  * tensor-core path (chunks of 128 tokens and more, or on request): the (token, k) pairs are sorted by expert, the
-//    activations are rounded to bf16, and two grouped dequant-GEMMs (dqgemm_tc.cuh) run on tcgen05:
+//  * tensor-core path (chunks of 128 tokens and more, or on request): the (token, k) pairs are sorted by expert
+//    and two grouped dequant-GEMMs (dqgemm_tc.cuh) run on tcgen05:
 //    gate/up with SiLU(gate)*up in the epilogue (activation stored as two bf16 planes, value and
 //    remainder, about 16 bits together), then down -- both planes against the same weight tile -- into
 //    one fp32 row per pair; the shared expert is three dense 4-bit GEMMs; a last kernel applies the router weights
@@ -15,9 +15,10 @@
 //    kernels with expert de-duplication inside a group (infer.m:12424-12532).  Every output row is then
 //    bit-identical to the decode entry point's, the property the reference claims (README.md:25).
 //
-// The tensor-core path multiplies bf16-rounded weights by bf16-rounded activations with fp32
-// accumulation, so its results differ from the decode path's (fp32 activations, exact weights) by
-// bf16 rounding; the parity tests compare it with an oracle that rounds at the same places.
+// The tensor-core path carries every operand as a bf16 value plus a bf16 remainder (16 significant bits:
+// the dequantised weights, fp32 activations, SiLU(gate)*up; bf16 activations are exact as they are) and
+// accumulates in fp32, so it agrees with the reference's arithmetic (exact fp32 weights and activations)
+// to about 1e-5 of an output's scale; the parity tests hold it to the same bar as the decode path.
 #include "dqgemm_tc.cuh"
 
 namespace {
@@ -99,9 +100,14 @@ __global__ void __launch_bounds__(1024) pf_sort_kernel(const int32_t *ids, const
     }
 }
 
-__global__ void pf_to_bf16_kernel(const float *src, uint16_t *dst, size_t n) {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n / 2; i += (size_t)gridDim.x * blockDim.x)
-        reinterpret_cast<uint32_t *>(dst)[i] = dqgemm::bf16x2_rn(src[2 * i], src[2 * i + 1]);
+// fp32 activations -> two bf16 planes: the value rounded to bf16 and the bf16-rounded remainder
+__global__ void pf_to_bf16_kernel(const float *src, uint16_t *dst, uint16_t *dst_lo, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n / 2; i += (size_t)gridDim.x * blockDim.x) {
+        uint32_t h, r;
+        dqgemm::bf16x2_split(src[2 * i], src[2 * i + 1], h, r);
+        reinterpret_cast<uint32_t *>(dst)[i] = h;
+        reinterpret_cast<uint32_t *>(dst_lo)[i] = r;
+    }
 }
 
 // act = SiLU(g) * u, stored as two bf16 planes: the value rounded to bf16 and the remainder (shared expert)
@@ -147,12 +153,22 @@ int tn_max_for(int tokens) {
     return t < 16 ? 16 : (t > 256 ? 256 : t);
 }
 
-bool g_gemm_attr = false;
+// The kernel's opt-in to 227 KB of shared memory is a per-device function attribute: set once per device.
+int gemm_attr_once(finch_ctx *ctx) {
+    static std::mutex mu;
+    static std::vector<int> done;
+    std::lock_guard<std::mutex> lk(mu);
+    for (int d : done)
+        if (d == ctx->cfg.device) return FINCH_OK;
+    FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(dqgemm::dqgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(dqgemm::dqgemm_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    done.push_back(ctx->cfg.device);
+    return FINCH_OK;
+}
 int launch_gemm(finch_ctx *ctx, cudaStream_t st, const dqgemm::Args &a, dim3 grid) {
-    if (!g_gemm_attr) {
-        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(dqgemm::dqgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(dqgemm::dqgemm_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-        g_gemm_attr = true;
+    {
+        const int rc = gemm_attr_once(ctx);
+        if (rc) return rc;
     }
     const int smem = dqgemm::smem_bytes(a.tn_max, a.X2 ? 2 : 1, a.mode != dqgemm::DENSE4);
     if (smem > 227 * 1024) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "token tile %d needs %d bytes of shared memory", a.tn_max, smem);
@@ -177,7 +193,9 @@ int dense4_gemm(finch_ctx *ctx, cudaStream_t st, const finch_wdesc *w, const uin
     a.K = w->in_dim;
     // token tile: small enough that the grid covers the SMs, large enough not to dequantise a tile too often
     a.tn_max = tn_max_for((int)((long long)T * (w->out_dim / dqgemm::GM) / 148));
-    if (xb_lo && a.tn_max > 128) a.tn_max = 128;   // two activation planes side by side: 2 x tokens accumulator columns
+    // two stages of [two weight planes + the activation planes] have to fit 227 KB of shared memory
+    if (a.tn_max > 128) a.tn_max = 128;
+    if (xb_lo && a.tn_max > 64) a.tn_max = 64;
     a.X2 = xb_lo;
     a.scale_dtype = w->scale_dtype;
     a.W = (const uint32_t *)w->W;
@@ -226,13 +244,13 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
     const size_t o_seg = take((c.n_experts + 1) * sizeof(int)), o_order = take((size_t)P * sizeof(int));
     const int max_items = P / 16 + c.n_experts + 1;   // tiles of at least 16 tokens, plus one ragged tile per expert
     const size_t o_ia = take((size_t)max_items * sizeof(int2)), o_ib = take((size_t)max_items * sizeof(int2)), o_ni = take(2 * sizeof(int));
-    const size_t o_xb = take((size_t)T * H * 2), o_sg = take((size_t)T * Is * 4), o_su = take((size_t)T * Is * 4), o_sact = take((size_t)T * Is * 4);
+    const size_t o_xb = take((size_t)T * H * 2), o_xl = take((size_t)T * H * 2), o_sg = take((size_t)T * Is * 4), o_su = take((size_t)T * Is * 4), o_sact = take((size_t)T * Is * 4);
     int rc = ensure_ws(ctx, off, st);
     if (rc) return rc;
     char *ws = (char *)ctx->pf_ws;
     int *seg = (int *)(ws + o_seg), *order = (int *)(ws + o_order), *n_items = (int *)(ws + o_ni);
     int2 *items_a = (int2 *)(ws + o_ia), *items_b = (int2 *)(ws + o_ib);
-    uint16_t *xb = (uint16_t *)(ws + o_xb), *sact = (uint16_t *)(ws + o_sact), *sact_lo = sact + (size_t)T * Is;
+    uint16_t *xb = (uint16_t *)(ws + o_xb), *xl = (uint16_t *)(ws + o_xl), *sact = (uint16_t *)(ws + o_sact), *sact_lo = sact + (size_t)T * Is;
     float *sg = (float *)(ws + o_sg), *su = (float *)(ws + o_su);
     uint16_t *act = (uint16_t *)ctx->act, *act_lo = act + (size_t)P * I;   // two bf16 planes [P][I] inside the fp32-sized buffer
     float *down = ctx->partial, *shared_out = ctx->partial + (size_t)P * H;
@@ -241,11 +259,12 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
     pf_sort_kernel<<<1, 1024, 4 * c.n_experts * sizeof(int), st>>>(ids, valid, slot_row, c.n_experts, P, seg, order, tn_a, tn_b, items_a, items_b,
                                                                    n_items);
     FINCH_CUDA_OK(ctx, cudaGetLastError());
-    const uint16_t *x = (const uint16_t *)h_post;
+    const uint16_t *x = (const uint16_t *)h_post, *x_lo = nullptr;
     if (c.act_dtype != FINCH_BF16) {
-        pf_to_bf16_kernel<<<148, 256, 0, st>>>((const float *)h_post, xb, (size_t)T * H);
+        pf_to_bf16_kernel<<<148, 256, 0, st>>>((const float *)h_post, xb, xl, (size_t)T * H);
         FINCH_CUDA_OK(ctx, cudaGetLastError());
         x = xb;
+        x_lo = xl;
         ctx->launches++;
     }
     ctx->launches++;
@@ -265,6 +284,7 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
     a.status = ctx->dev_status;
     a.mode = dqgemm::EXPERT_GATEUP;
     a.X = x;
+    a.X2 = x_lo;
     a.act_out = act;
     a.act_out_lo = act_lo;
     a.items = items_a;
@@ -282,8 +302,8 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
     if ((rc = launch_gemm(ctx, st, a, dim3(H / dqgemm::GM, P / tn_b + c.n_experts, 1)))) return rc;
 
     if (shared) {
-        if ((rc = dense4_gemm(ctx, st, &shared->gate, x, nullptr, sg, T))) return rc;
-        if ((rc = dense4_gemm(ctx, st, &shared->up, x, nullptr, su, T))) return rc;
+        if ((rc = dense4_gemm(ctx, st, &shared->gate, x, x_lo, sg, T))) return rc;
+        if ((rc = dense4_gemm(ctx, st, &shared->up, x, x_lo, su, T))) return rc;
         pf_swiglu_kernel<<<148, 256, 0, st>>>(sg, su, sact, sact_lo, (size_t)T * Is);
         FINCH_CUDA_OK(ctx, cudaGetLastError());
         if ((rc = dense4_gemm(ctx, st, &shared->down, sact, sact_lo, shared_out, T))) return rc;

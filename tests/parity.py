@@ -43,3 +43,20 @@ def assert_close(a, b, what="", cos_min=COS_MIN, rel_max=REL_MAX, tight_rel=TIGH
         tight = max_rel_err(a, b, 1e-2)
         assert tight <= tight_rel, f"{what}: error against 1% of rms = {tight:.3e}"
     return c, r
+
+
+def oracle_layer(blocks_by_expert, ids, w, valid, x, cfg, shared=None, score=None, h_mid=None, accum=None):
+    """The MoE layer of T tokens on the CPU oracle (fp64 accumulation unless told otherwise): experts that are
+    masked or missing from blocks_by_expert are skipped, as the library skips them."""
+    from oracle import oracle as orc
+    accum = orc.ACC_F64 if accum is None else accum
+    T = ids.shape[0]
+    out = np.empty((T, cfg["hidden"]), np.float32)
+    for t in range(T):
+        v = None if valid is None else valid[t]
+        blocks = [blocks_by_expert.get(int(e)) if (v is None or v[k]) else None for k, e in enumerate(ids[t])]
+        vv = np.array([1 if (b is not None and (v is None or v[k])) else 0 for k, b in enumerate(blocks)], np.uint8)
+        out[t] = orc.moe_layer(blocks, w[t], vv, x[t], bits=3, scale_dtype=cfg["sd"], hidden=cfg["hidden"],
+                               inter=cfg["inter"], h_mid=None if h_mid is None else h_mid[t], shared=shared,
+                               shared_gate_score=0.0 if score is None else float(score[t]), accum=accum)
+    return out

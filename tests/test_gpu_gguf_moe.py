@@ -63,3 +63,41 @@ def test_gguf_expert_moe_vs_oracle(types, B):
         assert ctx.device_status() == 0
     finally:
         ctx.destroy()
+
+
+def test_gguf_expert_moe_full_size_vs_oracle():
+    """The model's own dimensions: hidden 2048, expert intermediate 512, 256 experts, top-8; Q4_K gate / up and Q6_K
+    down slabs.  Only the experts that are routed to carry data (the other slabs stay zero)."""
+    import torch
+    from finchmoe_b200 import api
+    H, I, NE, K, B = 2048, 512, 256, 8, 2
+    ctx = api.Context(hidden=H, n_experts=NE, top_k=K, moe_inter=I, shared_inter=512, n_layers=1, act_dtype=L.F32, max_tokens=4)
+    try:
+        rng = synth.rng_for(14, 2048)
+        ids, w = synth.zipf_routing(rng, B, NE, K)
+        used = sorted(set(ids.ravel().tolist()))
+        ex = {e: (synth.gguf_tensor(rng, I, H, 12), synth.gguf_tensor(rng, I, H, 12), synth.gguf_tensor(rng, H, I, 14)) for e in used}
+        proto = ex[used[0]]
+        slabs = [np.zeros((NE,) + proto[i]["W"].shape, np.uint8) for i in range(3)]
+        for e in used:
+            for i in range(3):
+                slabs[i][e] = ex[e][i]["W"]
+        dev = [torch.from_numpy(s).cuda() for s in slabs]
+        ge = L.GgufExperts(dev[0].data_ptr(), dev[1].data_ptr(), dev[2].data_ptr(), slabs[0][0].nbytes, slabs[1][0].nbytes, slabs[2][0].nbytes,
+                           proto[0]["bits"], proto[1]["bits"], proto[2]["bits"])
+        x = (synth.activations(rng, B, H) + rng.normal(0, 1e-3, size=(B, H))).astype(np.float32)
+        h_mid = synth.activations(rng, B, H)
+        d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        out = torch.empty((B, H), dtype=torch.float32, device="cuda")
+        xd, idd, wd, hd = d(x), d(ids), d(w), d(h_mid)
+        torch.cuda.synchronize()
+        ctx.encode_moe_gguf(ge, xd, idd, wd, None, hd, out, B)
+        ctx.sync()
+        got = out.cpu().numpy()
+        for b in range(B):
+            outs = np.stack([_expert_out(*ex[int(e)], x[b]) for e in ids[b]])
+            want = oracle.combine(h_mid[b], outs, w[b], np.ones(K, np.uint8), np.zeros(H, np.float32), 0.0, guard=1)
+            assert_close(got[b], want, f"GGUF MoE at model size, token {b}")
+        assert ctx.device_status() == 0
+    finally:
+        ctx.destroy()

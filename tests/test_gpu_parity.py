@@ -12,7 +12,7 @@ import pytest
 from finchmoe_b200 import lib as L
 from finchmoe_b200 import synth
 from oracle import oracle as orc
-from parity import assert_close
+from parity import assert_close, oracle_layer
 
 pytestmark = pytest.mark.gpu
 
@@ -92,6 +92,23 @@ def test_matvec_vs_oracle(ctx_small, bits, o, i, M):
     assert_close(y, want, f"matvec bits={bits} M={M}")
 
 
+@pytest.mark.parametrize("ty,bits", [(12, 10), (14, 11)])
+@pytest.mark.parametrize("o,i", [(512, 2048), (2048, 512), (8192, 2048)])
+@pytest.mark.parametrize("T", [1, 8, 90])
+def test_gguf_matvec_benchmark_shapes_vs_oracle(ctx_small, ty, bits, o, i, T):
+    """Q4_K / Q6_K at the shapes and token counts of the GGUF benchmark rows ([512 x 2048], [2048 x 512], [8192 x 2048]
+    at 1, 8 and 90 positions; 90 positions run as several passes of the streaming kernel).  The oracle takes a sample
+    of the positions of the large cases."""
+    rng = synth.rng_for(4, ty, o + T)
+    t = synth.gguf_tensor(rng, o, i, ty)
+    x = synth.activations(rng, T, i)
+    y = ctx_small.fast_dequant_matvec(ctx_small.upload_tensor(t), x)
+    assert y.shape == (T, o) and np.all(np.isfinite(y))
+    rows = np.arange(T) if o * i * T <= 2 ** 27 else np.sort(rng.choice(T, size=8, replace=False))
+    want = orc.matvec(t["W"], None, None, L.FP16, x[rows], o, i, 256, bits, orc.ACC_F64)
+    assert_close(y[rows], want, f"GGUF type {ty} [{o} x {i}] T={T}")
+
+
 def test_matvec_bf16_weights_and_bad_args(ctx_small):
     rng = synth.rng_for(4, 99)
     wf = synth.activations(rng, 24, 256)
@@ -152,17 +169,7 @@ def test_route_topk_vs_oracle(ctx_small):
 
 
 # ----------------------------------------------------------------- MoE layer
-def _oracle_layer(blocks_by_expert, ids, w, valid, x, cfg, shared=None, score=None, h_mid=None, accum=orc.ACC_F64):
-    T = ids.shape[0]
-    out = np.empty((T, cfg["hidden"]), np.float32)
-    for t in range(T):
-        v = None if valid is None else valid[t]
-        blocks = [blocks_by_expert.get(int(e)) if (v is None or v[k]) else None for k, e in enumerate(ids[t])]
-        vv = np.array([1 if (b is not None and (v is None or v[k])) else 0 for k, b in enumerate(blocks)], np.uint8)
-        out[t] = orc.moe_layer(blocks, w[t], vv, x[t], bits=3, scale_dtype=cfg["sd"], hidden=cfg["hidden"],
-                               inter=cfg["inter"], h_mid=None if h_mid is None else h_mid[t], shared=shared,
-                               shared_gate_score=0.0 if score is None else float(score[t]), accum=accum)
-    return out
+_oracle_layer = oracle_layer
 
 
 def _mk_small(api, sd, ad, n_experts=16, max_tokens=8, seed=0):

@@ -6,7 +6,8 @@ callback that runs under a "no allocation" rule, a thread that must not block
 on the driver.  For them the library carries a fixed staging buffer inside its
 own image and this entry point uses only that.  The test calls it through the C
 ABI twice in a row (the second call reuses the buffer with the first call's
-contents still in it) and checks each result against the regular entry point.
+contents still in it) and checks each result against the regular entry point
+and against the CPU oracle.
 It is collected last so that a failure here cannot hide any other test.
 """
 import ctypes as C
@@ -16,6 +17,7 @@ import pytest
 
 from finchmoe_b200 import lib as L
 from finchmoe_b200 import synth
+from oracle import oracle as orc
 from parity import assert_close
 
 pytestmark = pytest.mark.gpu
@@ -40,6 +42,10 @@ def test_matvec_noalloc_matches_regular_entry_point_twice():
                 # the regular entry point may pick a different kernel for the same tensor (streaming kernel for
                 # few positions), so the two agree to the path's tolerance, not bit for bit
                 assert_close(got, want, f"noalloc vs regular, rep {rep} bits={t['bits']}")
+                # and, directly, against the CPU oracle
+                ref = orc.matvec(t["W"], t.get("S"), t.get("B"), t.get("scale_dtype", L.FP16), x, t["out_dim"], t["in_dim"], t["group"],
+                                 t["bits"], orc.ACC_F64)
+                assert_close(got, ref, f"noalloc vs oracle, rep {rep} bits={t['bits']}")
         # a call that does not fit the fixed buffer is refused, not truncated
         big = synth.affine_tensor(rng, 64, 4096, 4, L.BF16)
         wb = ctx.upload_tensor(big)
