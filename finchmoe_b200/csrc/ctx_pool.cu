@@ -247,6 +247,12 @@ extern "C" int finch_pool_put(finch_pool *p, int layer, int expert, const void *
     finch_ctx *ctx = p->ctx;
     cudaSetDevice(ctx->cfg.device);
     const int key = layer * p->n_experts + expert;
+    // A put may overwrite a slot (a full pool evicts) and edits the slot table that queued kernels resolve ids
+    // with.  The copies below are synchronous on the legacy stream, which does not order them against the
+    // context's non-blocking stream or a caller's stream: wait for what is queued on this device first, so that no
+    // kernel in flight reads a slot or a table entry while it changes.  (With every expert resident, the
+    // intended mode here, puts happen before the first layer call and this costs nothing.)
+    if (p->slot_of[key] >= 0 || p->used >= p->slots) FINCH_CUDA_OK(ctx, cudaDeviceSynchronize());
     const int slot = pool_claim_slot(p, key);
     p->last_used[slot] = ++p->clock;
     p->tmp.resize(ctx->expert_bytes);

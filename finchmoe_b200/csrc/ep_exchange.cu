@@ -149,8 +149,9 @@ extern "C" int finch_encode_ep_pack(finch_ctx *ctx, finch_stream stream, const v
 
 extern "C" int finch_encode_ep_unpack(finch_ctx *ctx, finch_stream stream, const void *records, int n, void *h_post, int32_t *expert_ids, float *weights,
                                       uint8_t *valid) {
-    if (!ctx || !records || !h_post || !expert_ids || !weights || !valid || n < 0) return FINCH_E_ARG;
-    if (n == 0) return FINCH_OK;
+    if (!ctx || n < 0) return FINCH_E_ARG;
+    if (n == 0) return FINCH_OK;   // a rank that received nothing (its buffers may be NULL)
+    if (!records || !h_post || !expert_ids || !weights || !valid) return FINCH_E_ARG;
     const finch_config &c = ctx->cfg;
     const int elt = c.act_dtype == FINCH_BF16 ? 2 : 4;
     cudaSetDevice(c.device);

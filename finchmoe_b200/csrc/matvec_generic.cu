@@ -9,6 +9,7 @@
 #include "finch_internal.cuh"
 
 int finch_try_fast_matvec(finch_ctx *ctx, cudaStream_t st, const void *x, int x_dtype, const finch_wdesc *specs, float *const *outs, int n, int M);
+int finch_try_stream_matvec(finch_ctx *ctx, cudaStream_t st, const void *x, int x_dtype, const finch_wdesc *specs, float *const *outs, int n, int M);
 
 namespace {
 
@@ -351,6 +352,10 @@ extern "C" int finch_encode_batch_matvec(finch_ctx *ctx, finch_stream stream, co
         max_out = max_out > specs[i].out_dim ? max_out : specs[i].out_dim;
     }
     cudaSetDevice(ctx->cfg.device);
+    {   // a large 4- or 8-bit tensor (lm_head, the big projections) at a few positions: the tensor-core streaming kernel (matvec_stream.cu)
+        const int rc = finch_try_stream_matvec(ctx, finch_pick_stream(ctx, stream), x, x_dtype, specs, outs, n, M);
+        if (rc >= 0) return rc;
+    }
     {   // 1..8 positions of a 3-bit / 4-bit / Q4_K tensor: the streaming kernel (matvec_fast.cu)
         const int rc = finch_try_fast_matvec(ctx, finch_pick_stream(ctx, stream), x, x_dtype, specs, outs, n, M);
         if (rc >= 0) return rc;
@@ -441,7 +446,7 @@ std::mutex g_noalloc_mu;
 
 extern "C" int finch_matvec_noalloc(const finch_wdesc *w, const float *x_host, float *out_host, int M, finch_stream stream) {
     if (!w || !x_host || !out_host || M < 1) return FINCH_E_ARG;
-    if (finch_validate_wdesc(nullptr, w, "matvec_noalloc")) return FINCH_E_ARG;
+    if (const int rc = finch_validate_wdesc(nullptr, w, "matvec_noalloc")) return rc;   // the code finch_matvec gives for the same tensor
     const size_t xb = (size_t)M * w->in_dim * sizeof(float), ob = (size_t)M * w->out_dim * sizeof(float);
     const size_t x_room = (xb + 255) & ~(size_t)255;
     if (x_room + ob > FINCH_NOALLOC_SCRATCH_BYTES) return FINCH_E_UNSUPPORTED;  // M * (in_dim + out_dim) floats must fit 512 KiB
@@ -450,7 +455,8 @@ extern "C" int finch_matvec_noalloc(const finch_wdesc *w, const float *x_host, f
     void *base = nullptr;
     {
         // The array's name is only a host-side handle; the kernel needs the address it has on the
-        // current device.  Looked up once per device, on the first call made with that device current.
+        // current device.  Looked up once per device, on the first call made with that device current
+        // (the address does not outlive a cudaDeviceReset: the entry point is not to be used across one).
         std::lock_guard<std::mutex> lock(g_noalloc_mu);
         if (!g_noalloc_ptr[dev]) {
             void *p = nullptr;

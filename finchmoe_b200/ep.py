@@ -238,6 +238,8 @@ class GpuBackend:
 
     def pack(self, p, x, ids, weights, valid, n_rows):
         buf = self.empty_bytes(n_rows * self.record_bytes())
+        if n_rows == 0:   # nothing leaves this rank (no token picked an expert elsewhere, or every pair is masked)
+            return buf
         self.ctx.check(self.lib.finch_encode_ep_pack(self.ctx.h, self._stream(), x.data_ptr(), ids.data_ptr(), weights.data_ptr(),
                                                      valid.data_ptr() if valid is not None else None, p.T, p.world, p.offs.data_ptr(),
                                                      p.send_tok.data_ptr(), buf.data_ptr()))
@@ -263,6 +265,8 @@ class GpuBackend:
         """skip = (first row, rows): a block of received rows that is left out (its output rows are not written)."""
         if n > self.max_rows:
             raise ValueError(f"received {n} rows, backend sized for {self.max_rows}")
+        if n == 0:
+            return self.rout[:0]
         st = self._stream()
         self.ctx.check(self.lib.finch_encode_ep_unpack(self.ctx.h, st, recv_buf.data_ptr(), n, self.rx.data_ptr(), self.rids.data_ptr(),
                                                        self.rw.data_ptr(), self.rv.data_ptr()))
@@ -293,5 +297,7 @@ class GpuBackend:
                 h_mid[t0:].data_ptr() if h_mid is not None else None, out[t0:].data_ptr(), m))
 
     def combine(self, p, out, back):
+        if back.numel() == 0:   # no row left this rank: nothing comes back
+            return
         self.ctx.check(self.lib.finch_encode_ep_combine(self.ctx.h, self._stream(), out.data_ptr(), back.data_ptr(), p.slot_of.data_ptr(),
                                                         p.offs.data_ptr(), p.T, p.world))

@@ -102,7 +102,10 @@ FINCH_API int finch_buf_free(finch_ctx *ctx, void *dev);
  * that is not resident behaves as valid[k] = 0. */
 FINCH_API int finch_pool_create(finch_ctx *ctx, int n_layers, int n_experts, int max_slots, finch_pool **out);
 FINCH_API void finch_pool_destroy(finch_pool *pool);
-/* Stores the exact on-disk block of one expert (host memory). */
+/* Stores the exact on-disk block of one expert (host memory).  A put that replaces a resident expert or
+ * evicts one first waits for the work already queued on the device (a kernel in flight may be reading that
+ * slot or the slot table); a put into a free slot does not wait.  The LRU clock is advanced by put() and
+ * lookup(), as the reference's access_counter is (finchmoe/infer.m:6216-6276). */
 FINCH_API int finch_pool_put(finch_pool *pool, int layer, int expert, const void *packed_block);
 /* Reads a resident block back to host memory (diagnostics, parity checks). */
 FINCH_API int finch_pool_get(finch_pool *pool, int layer, int expert, void *packed_block_out);

@@ -76,6 +76,38 @@ def test_single_rank_protocol_matches_plain_layer(T, static):
         ctx.destroy()
 
 
+def test_single_rank_protocol_with_nothing_to_send():
+    """Every pair masked: the plan sends no row anywhere, pack and unpack see zero rows (and NULL-sized buffers), and
+    the layer is h_mid + the gated shared expert."""
+    import torch
+    from finchmoe_b200 import api
+    T = 6
+    ctx = _ctx(api, max_tokens=8)
+    pool = ctx.pool()
+    try:
+        rng = synth.rng_for(12, 999)
+        for e in range(16):
+            pool.put(0, e, synth.expert_block(rng, 256, 128, 64, 3, L.BF16))
+        x = synth.activations(rng, T, 256)
+        ids, w = synth.zipf_routing(rng, T, 16, 8)
+        valid = np.zeros((T, 8), np.uint8)
+        sh = synth.shared_expert(rng, 256, 128, 64, 4, L.BF16)
+        score = rng.normal(0, 1, size=T).astype(np.float32)
+        h_mid = rng.normal(0, 1, size=(T, 256)).astype(np.float32)
+        d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        shd = ctx.make_shared(*[ctx.upload_tensor(t) for t in sh], gate_score=d(score))
+        want = ctx.moe_forward_host(pool, 0, x, ids, w, valid=valid, shared=shd, gate_score=score, h_mid=h_mid)
+        be = ep.GpuBackend(ctx, pool, T)
+        out = torch.empty((T, 256), dtype=torch.float32, device="cuda")
+        ep.ep_layer(be, None, None, 0, d(x), d(ids), d(w), d(valid), shd, d(h_mid), out)
+        torch.cuda.synchronize()
+        assert_close(out.cpu().numpy(), want, "nothing to send")
+        assert ctx.device_status() == 0
+    finally:
+        pool.destroy()
+        ctx.destroy()
+
+
 WORKER = r'''
 import os, sys
 sys.path.insert(0, sys.argv[3]); sys.path.insert(0, os.path.dirname(sys.argv[3]))

@@ -109,6 +109,54 @@ def test_gguf_matvec_benchmark_shapes_vs_oracle(ctx_small, ty, bits, o, i, T):
     assert_close(y[rows], want, f"GGUF type {ty} [{o} x {i}] T={T}")
 
 
+@pytest.mark.parametrize("bits,o,i", [(8, 4100, 2048), (4, 8192, 2048), (4, 4099, 4096), (8, 5000, 512)])
+@pytest.mark.parametrize("M", [1, 3, 9])
+@pytest.mark.parametrize("xdt", [L.F32, L.BF16])
+def test_large_affine_matvec_streaming_kernel_vs_oracle(ctx_small, bits, o, i, M, xdt):
+    """Large row-major 4- / 8-bit tensors (4096 rows and more) take the tensor-core streaming kernel, straight from
+    the reference tensor layout; row counts that are not multiples of 16, fp32 and bf16 activations, several passes."""
+    import torch
+    rng = synth.rng_for(4, bits, o + M)
+    t = synth.affine_tensor(rng, o, i, bits, L.FP16 if (o + M) % 2 else L.BF16)
+    x = synth.activations(rng, M, i)
+    if xdt == L.F32:
+        x = (x + rng.normal(0, 1e-3, size=x.shape)).astype(np.float32)
+        xd = torch.from_numpy(x).cuda()
+    else:
+        xd = torch.from_numpy(synth.f32_to_bf16_rne(x)).cuda().view(torch.bfloat16)
+    out = torch.empty((M, o), dtype=torch.float32, device="cuda")
+    ctx_small.fast_batch_matvec(xd, xdt, [ctx_small.upload_tensor(t)], [out], M=M)
+    ctx_small.sync()
+    want = orc.matvec(t["W"], t["S"], t["B"], t["scale_dtype"], x, o, i, 64, bits, orc.ACC_F64)
+    assert_close(out.cpu().numpy(), want, f"streaming matvec bits={bits} [{o} x {i}] M={M}")
+
+
+def test_lm_head_tier_row_slices_vs_oracle(ctx_small):
+    """The lm_head / embedding tier (finchmoe/infer.m:5728-5815): 8-bit g64 [248,320 x 2048] at one position;
+    three slices of rows against the oracle."""
+    import torch
+    OUT, K = 248320, 2048
+    rng = synth.rng_for(4, 8, 248320)
+    base = synth.affine_tensor(rng, 8192, K, 8, L.FP16)
+    reps = OUT // 8192 + 1
+    perm = rng.permutation(8192)
+    t = dict(base, out_dim=OUT)
+    for k in ("W", "S", "B"):   # rows of the small tensor, repeated in a shuffled order
+        t[k] = np.ascontiguousarray(np.concatenate([base[k][np.roll(perm, r)] for r in range(reps)])[:OUT])
+    x = synth.activations(rng, 1, K)
+    xd = torch.from_numpy(synth.f32_to_bf16_rne(x)).cuda().view(torch.bfloat16)
+    out = torch.empty((1, OUT), dtype=torch.float32, device="cuda")
+    w = ctx_small.upload_tensor(t)
+    ctx_small.fast_batch_matvec(xd, L.BF16, [w], [out], M=1)
+    ctx_small.sync()
+    got = out.cpu().numpy()[0]
+    assert np.all(np.isfinite(got))
+    for r0 in (0, 123456, OUT - 700):
+        sl = slice(r0, r0 + 700)
+        want = orc.matvec(t["W"][sl], t["S"][sl], t["B"][sl], L.FP16, x[0], 700, K, 64, 8, orc.ACC_F64)
+        assert_close(got[sl], want, f"lm_head rows {r0}..")
+
+
 def test_matvec_bf16_weights_and_bad_args(ctx_small):
     rng = synth.rng_for(4, 99)
     wf = synth.activations(rng, 24, 256)
@@ -562,6 +610,41 @@ def test_host_path_top_k_4_more_than_8_tokens(api):
         out = ctx.moe_forward_host(pool, 0, x, ids, w)
         want = _oracle_layer(blocks, ids, w, None, x, dict(hidden=256, inter=128, sd=L.FP16))
         assert_close(out, want, "top_k=4, T=12")
+    finally:
+        pool.destroy()
+        ctx.destroy()
+
+
+def test_pool_put_between_decode_calls_with_fewer_slots_than_experts(api):
+    """LRU mode (fewer slots than experts): puts that evict are interleaved with decode calls without any host
+    synchronisation by the caller; every call must see the experts it was given."""
+    import torch
+    ctx = api.Context(hidden=256, n_experts=16, top_k=4, moe_inter=128, shared_inter=128, n_layers=1, scale_dtype=L.FP16,
+                      act_dtype=L.BF16, max_tokens=2)
+    pool = ctx.pool(max_slots=10)   # a call needs up to eight experts at once
+    try:
+        rng = synth.rng_for(1, 4242)
+        blocks = {e: synth.expert_block(rng, 256, 128, 64, 3, L.FP16) for e in range(16)}
+        cfg = dict(hidden=256, inter=128, sd=L.FP16)
+        d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        outs, wants = [], []
+        for step in range(6):
+            ids = np.stack([rng.permutation(16)[:4] for _ in range(2)]).astype(np.int32)
+            w = rng.random((2, 4)).astype(np.float32)
+            x = synth.activations(rng, 2, 256)
+            for e in sorted(set(ids.ravel().tolist())):
+                if pool.lookup(0, int(e)) is None:
+                    pool.put(0, int(e), blocks[int(e)])     # evicts once the ten slots are taken
+            out = torch.empty((2, 256), dtype=torch.float32, device="cuda")
+            xd = d(synth.f32_to_bf16_rne(x)).view(torch.bfloat16)
+            ctx.encode_moe_decode(pool, 0, xd, d(ids), d(w), None, None, None, out, 2)   # enqueued only
+            outs.append((out, xd))
+            resident = {e: blocks[e] for e in range(16)}
+            wants.append(oracle_layer(resident, ids, w, None, x, cfg))
+        ctx.sync()
+        for step, ((out, _), want) in enumerate(zip(outs, wants)):
+            assert_close(out.cpu().numpy(), want, f"step {step}")
+        assert ctx.device_status() == 0 and pool.stats()["evictions"] > 0
     finally:
         pool.destroy()
         ctx.destroy()
