@@ -2,16 +2,18 @@
 //
 //   D[128 weight rows, TN tokens] += Wdq[128, K] * X[TN, K]^T        (bf16 x bf16 -> fp32)
 //
-// One CTA owns one 128-row weight tile and up to tn_max tokens.  Per K block of 128 values its eight
-// dequantising warps turn packed codes (EXPERT_*: brought into a ring of shared-memory slots by bulk copies;
+// One CTA owns one 128-row weight tile and up to tn_max tokens.  Per K block of 64 values (one scale group) its
+// eight dequantising warps turn packed codes (EXPERT_*: brought into a ring of shared-memory slots by bulk copies;
 // DENSE4: loaded from global memory one block ahead) into the weight fl32(fl32(q*s)+b) -- the value the
 // reference's dequantised weight has (quant_audit.py:245 semantics) -- and write it as TWO bf16 planes, the
 // value rounded to bf16 and the bf16-rounded remainder (16 significant bits together), into shared memory in
 // the 128-byte-swizzled K-major layout the tensor core reads; the tokens' activations arrive by cp.async
 // (one bf16 plane, or two when the caller passes the remainder plane of fp32 activations).  Lane 0 of a ninth,
 // control warp issues the block's tcgen05.mma (K = 16 each, both weight planes into the same accumulator)
-// and commits them to an mbarrier.  Two stages: the warps dequantise block i+1 while the tensor core works
-// on block i.  The epilogue reads the accumulator with tcgen05.ld, one lane (= weight row) per thread.
+// and commits them to an mbarrier.  Two weight stages and three activation stages: the warps dequantise block
+// i+1 while the tensor core works on block i, and the activations of block i+1 are requested before block i is
+// dequantised, so no block waits for a load it has just issued.  Two CTAs fit an SM.  The epilogue reads the
+// accumulator with tcgen05.ld, one lane (= weight row) per thread.
 //
 // Shared by moe_prefill.cu (grouped 3-bit expert GEMMs over the pool's tiled layout) and the dense
 // 4-bit projections.  Every wait is bounded; on a time-out the CTA reports through `status`, frees
@@ -23,13 +25,14 @@
 namespace dqgemm {
 
 constexpr int GM = 128;       // weight rows per CTA = UMMA M
-constexpr int BK = 128;       // K values per stage = two 64-value swizzle atoms
-constexpr int NS = 2;         // stages
-constexpr int NT = 256;       // dequantising threads per CTA: two per weight row, one for each 64-value half (= scale group) of a K block
+constexpr int BK = 64;        // K values per stage = one 64-value swizzle atom = one scale group
+constexpr int NS = 2;         // weight stages
+constexpr int NB = 3;         // activation stages
+constexpr int NT = 256;       // dequantising threads per CTA: two per weight row, one for each 32-value half of a K block
 constexpr int NTB = NT + 32;  // + one control warp: its lane 0 issues the MMAs and the bulk copies of the packed blocks
 constexpr int A_ATOM = GM * 128;   // bytes of one 64-value atom of the weight tile
-constexpr int RD = 4;         // depth of the ring of packed expert blocks (EXPERT_* modes)
-constexpr int RAW_STAGE = 8 * 768 + 8 * 128;   // one K block of eight 16-row pool tiles: operand words, then scale/bias entries
+constexpr int RD = 3;         // depth of the ring of packed expert blocks (EXPERT_* modes)
+constexpr int RAW_STAGE = 8 * 768 + 8 * 128;   // one 128-value unit (two K blocks) of eight 16-row pool tiles: operand words, then scale/bias entries
 
 enum Mode { EXPERT_GATEUP = 0, EXPERT_DOWN = 1, DENSE4 = 2 };
 
@@ -65,7 +68,7 @@ struct Args {
 };
 
 __host__ __device__ inline int smem_bytes(int tn_max, int planes, int expert) {
-    return 1024 + NS * (4 * A_ATOM + planes * 2 * tn_max * 128) + (expert ? RD * RAW_STAGE : 0) + 256 + tn_max * 4;
+    return 1024 + NS * 2 * A_ATOM + NB * planes * tn_max * 128 + (expert ? RD * RAW_STAGE : 0) + 256 + tn_max * 4;
 }
 
 __host__ __device__ inline int tmem_cols(int tn_max) { return tn_max <= 32 ? 32 : tn_max <= 64 ? 64 : tn_max <= 128 ? 128 : 256; }
@@ -198,11 +201,11 @@ __device__ __forceinline__ void dq4_word(uint32_t w, const GroupScale &gs, uint3
 // grid: x = 128-row weight tile; EXPERT_*: y = (expert, token tile) item; DENSE4: z = token tile.  block: 288 threads.
 //
 // No CTA-wide barrier inside the K loop.  Each of the eight dequantising warps writes its share of block
-// kb into stage kb % NS and arrives on a_full[stage]; lane 0 of the ninth (control) warp then issues the
-// block's MMAs and commits them to done[stage], which frees the stage, while the other warps already
-// work on block kb + 1; the same thread keeps the ring of packed blocks filled, refilling a slot once
-// raw_empty[slot] says that every dequantising warp has read it.
-__global__ void __launch_bounds__(NTB) dqgemm_tc_kernel(const Args a) {
+// kb into weight stage kb % NS and arrives on a_full[stage]; lane 0 of the ninth (control) warp then issues the
+// block's MMAs and commits them to done[stage], which frees the stage (and the activation stage of the same
+// block), while the other warps already work on block kb + 1; the same thread keeps the ring of packed units
+// filled, refilling a slot once raw_empty[slot] says that every dequantising warp has read both of its groups.
+__global__ void __launch_bounds__(NTB, 2) dqgemm_tc_kernel(const Args a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tn_max = a.tn_max;
@@ -230,27 +233,25 @@ __global__ void __launch_bounds__(NTB) dqgemm_tc_kernel(const Args a) {
     // The two activation planes sit side by side along N: rows [0, tn) of an atom are plane 0, rows
     // [tn, 2 tn) plane 1, one MMA covers both and the epilogue adds the two halves of the accumulator.
     const int planes = a.X2 ? 2 : 1, b_atom = planes * tn_max * 128;
-    const int stage_bytes = 4 * A_ATOM + 2 * b_atom;   // weights: [value | remainder plane][K half] atoms, then the activations' atoms
+    const int a_stage = 2 * A_ATOM;                    // weights of one K block: value plane, remainder plane
     const bool expert = a.mode != DENSE4;
-    const uint32_t raw = base + NS * stage_bytes;     // EXPERT_*: ring of packed blocks, filled by bulk copies
+    const uint32_t bbase = base + NS * a_stage;        // NB activation stages of b_atom bytes
+    const uint32_t raw = bbase + NB * b_atom;          // EXPERT_*: ring of packed units, filled by bulk copies
     const uint32_t ctl = raw + (expert ? RD * RAW_STAGE : 0);   // barriers, tensor-memory address, row list
     uint8_t *ctl_p = smem_raw + (ctl - finch_smem_u32(smem_raw));
     uint8_t *raw_p = smem_raw + (raw - finch_smem_u32(smem_raw));
-    uint64_t *done = reinterpret_cast<uint64_t *>(ctl_p);   // [NS]  MMAs of the stage finished
+    uint64_t *done = reinterpret_cast<uint64_t *>(ctl_p);   // [NS]  MMAs of the block in this weight stage finished
     uint64_t *a_full = done + NS;                            // [NS]  all warps wrote their share of the stage
-    uint64_t *raw_full = a_full + NS;                        // [RD]  packed block landed
-    uint64_t *raw_empty = raw_full + RD;                     // [RD]  all warps read the packed block
+    uint64_t *raw_full = a_full + NS;                        // [RD]  packed unit landed
+    uint64_t *raw_empty = raw_full + RD;                     // [RD]  all warps read the packed unit
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ctl_p + 128);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(ctl_p + 132);   // set by whoever gives up on a wait
     int *src_rows = reinterpret_cast<int *>(ctl_p + 256);   // [tn_max] activation row of each token of the tile
     constexpr int NW = NT / 32;   // dequantising warps
     const bool control = warp == NW;
 
-    // zero the activation halves of the stages once: rows >= m are never written and must read as 0
-    for (int s = 0; s < NS; s++) {
-        const uint32_t bst = base + s * stage_bytes + 4 * A_ATOM;
-        for (int i = tid; i < 2 * b_atom / 16 && !control; i += NT) st_shared16(bst + i * 16, 0u, 0u, 0u, 0u);
-    }
+    // zero the activation stages once: rows >= m are never written and must read as 0
+    for (int i = tid; i < NB * b_atom / 16 && !control; i += NT) st_shared16(bbase + i * 16, 0u, 0u, 0u, 0u);
     for (int j = tid; j < m && !control; j += NT) {
         int row = t0 + j;
         if (a.mode != DENSE4) {
@@ -282,10 +283,10 @@ __global__ void __launch_bounds__(NTB) dqgemm_tc_kernel(const Args a) {
     const uint32_t tmem_d = *tmem_slot;
 
     // ---- this thread's weight row ----
-    const int r = tid & (GM - 1), kh = tid >> 7;   // row of the tile (= tensor-memory lane) and 64-value half of a K block
+    const int r = tid & (GM - 1), kh = tid >> 7;   // row of the tile (= tensor-memory lane) and 32-value half of a K block
     const uint32_t *w4 = nullptr;      // DENSE4: packed row
     const uint16_t *s4 = nullptr, *b4 = nullptr;
-    uint32_t raw_w = 0, raw_s = 0;     // EXPERT_*: this thread's words / scale inside a ring stage
+    uint32_t raw_w = 0, raw_s = 0;     // EXPERT_*: this thread's words / scale inside a ring slot (first group of the unit)
     const uint8_t *tile0 = nullptr;    // EXPERT_*: first of the CTA's eight pool tiles
     int tile_stride = 0, sb_off = 0;
     if (a.mode == DENSE4) {
@@ -297,55 +298,62 @@ __global__ void __launch_bounds__(NTB) dqgemm_tc_kernel(const Args a) {
         const FinchTile T = finch_tile(a.hidden, a.inter);
         const int fr = r & 15, g = fr & 7, half = fr >> 3;
         const uint8_t *blk = a.pool_base + (size_t)a.slot_row[expert_id] * a.slot_bytes;
-        raw_w = (uint32_t)((r >> 4) * 768 + (g * 4 + 2 * kh) * 24 + half * 12);   // periods 2 kh and 2 kh + 1 (24 bytes apart)
-        raw_s = (uint32_t)(8 * 768 + (r >> 4) * 128 + g * 16 + half * 4 + kh * 2);
+        raw_w = (uint32_t)((r >> 4) * 768 + (g * 4 + kh) * 24 + half * 12);   // period kh of the unit's first group; the second group is 48 bytes on
+        raw_s = (uint32_t)(8 * 768 + (r >> 4) * 128 + g * 16 + half * 4);     // + 2 for the second group, + 8 for the bias
         tile0 = a.mode == EXPERT_GATEUP ? blk + (size_t)blockIdx.x * 8 * T.tileA : blk + T.b_base + (size_t)blockIdx.x * 8 * T.tileB;
         tile_stride = a.mode == EXPERT_GATEUP ? T.tileA : T.tileB;
         sb_off = a.mode == EXPERT_GATEUP ? T.sbA : T.sbB;
     }
 
-    const int nkb = a.K / BK;
+    const int nkb = a.K / BK, nunits = a.K / 128;
     const uint32_t idesc = instr_desc(planes * tn);
     bool failed = false;
-    uint32_t wreg[8];
+    uint32_t wreg[4];
     uint32_t sreg = 0, breg = 0;   // low 16 bits: scale / bias of this thread's group
     auto load_block = [&](int kb) {   // DENSE4: straight from global memory, one block ahead
-        const uint4 *p = reinterpret_cast<const uint4 *>(w4 + kb * 16 + kh * 8);
-        const uint4 v0 = __ldg(p), v1 = __ldg(p + 1);
+        const uint4 v0 = __ldg(reinterpret_cast<const uint4 *>(w4 + kb * 8 + kh * 4));
         wreg[0] = v0.x; wreg[1] = v0.y; wreg[2] = v0.z; wreg[3] = v0.w;
-        wreg[4] = v1.x; wreg[5] = v1.y; wreg[6] = v1.z; wreg[7] = v1.w;
-        sreg = __ldg(s4 + 2 * kb + kh);
-        breg = __ldg(b4 + 2 * kb + kh);
+        sreg = __ldg(s4 + kb);
+        breg = __ldg(b4 + kb);
     };
-    // EXPERT_*: one thread keeps up to RD K blocks of packed bytes in flight (16 bulk copies per block)
-    auto issue_raw = [&](int kb) {
-        const int slot = kb % RD;
+    // EXPERT_*: one thread keeps up to RD units of packed bytes in flight (16 bulk copies per unit)
+    auto issue_raw = [&](int u) {
+        const int slot = u % RD;
         uint8_t *dst = raw_p + slot * RAW_STAGE;
         finch_mbar_expect_tx(raw_full + slot, (unsigned)RAW_STAGE);
         for (int d = 0; d < 8; d++) {
             const uint8_t *t = tile0 + (size_t)d * tile_stride;
-            finch_bulk_g2s(dst + d * 768, t + (size_t)kb * 768, 768, raw_full + slot);
-            finch_bulk_g2s(dst + 8 * 768 + d * 128, t + sb_off + (size_t)kb * 128, 128, raw_full + slot);
+            finch_bulk_g2s(dst + d * 768, t + (size_t)u * 768, 768, raw_full + slot);
+            finch_bulk_g2s(dst + 8 * 768 + d * 128, t + sb_off + (size_t)u * 128, 128, raw_full + slot);
         }
     };
     // descriptors of the stages; a K step of 16 values advances the start address by 32 bytes (2 units)
     auto issue_mma = [&](int kb) {
-        const int st = kb % NS;
-        const uint32_t ast = base + st * stage_bytes, bst = ast + 4 * A_ATOM;
+        const uint32_t ast = base + (kb % NS) * a_stage, bst = bbase + (kb % NB) * b_atom;
         const uint64_t ad = smem_desc(ast), bd = smem_desc(bst);
         tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const uint64_t aoff = (uint64_t)(((k >> 2) * A_ATOM + (k & 3) * 32) >> 4);
-            const uint64_t boff = (uint64_t)(((k >> 2) * b_atom + (k & 3) * 32) >> 4);
-            tc_mma_bf16(tmem_d, ad + aoff, bd + boff, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-            tc_mma_bf16(tmem_d, ad + aoff + (uint64_t)((2 * A_ATOM) >> 4), bd + boff, idesc, 1u);   // the remainder plane of the weights
+        for (int k = 0; k < 4; k++) {
+            const uint64_t off = (uint64_t)((k * 32) >> 4);
+            tc_mma_bf16(tmem_d, ad + off, bd + off, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            tc_mma_bf16(tmem_d, ad + off + (uint64_t)(A_ATOM >> 4), bd + off, idesc, 1u);   // the remainder plane of the weights
         }
-        tc_commit(done + st);
+        tc_commit(done + kb % NS);
+    };
+    // the activations of block kb: m rows of 64 values, copied asynchronously into activation stage kb % NB
+    auto issue_acts = [&](int kb) {
+        const uint32_t bst = bbase + (kb % NB) * b_atom;
+        for (int i = tid; i < m * 8; i += NT) {
+            const int j = i >> 3, c = i & 7;
+            const size_t src = (size_t)src_rows[j] * a.K + (size_t)kb * BK + c * 8;
+            cp_async16(bst + swz(j, c), a.X + src);
+            if (a.X2) cp_async16(bst + swz(tn + j, c), a.X2 + src);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
     };
     if (expert) {
         if (control && lane == 0)
-            for (int kb = 0; kb < RD && kb < nkb; kb++) issue_raw(kb);
+            for (int u = 0; u < RD && u < nunits; u++) issue_raw(u);
     } else if (!control) {
         load_block(0);
     }
@@ -359,88 +367,81 @@ __global__ void __launch_bounds__(NTB) dqgemm_tc_kernel(const Args a) {
                     break;
                 }
                 issue_mma(kb);
-                // every dequantising warp read block kb's ring slot before it arrived on a_full: refill it
-                if (expert && kb + RD < nkb) {
-                    if (finch_mbar_wait(raw_empty + kb % RD, (kb / RD) & 1)) issue_raw(kb + RD);
+                // every dequantising warp read the unit's ring slot before it arrived on a_full for its second block: refill it
+                if (expert && (kb & 1) && (kb >> 1) + RD < nunits) {
+                    const int u = kb >> 1;
+                    if (finch_mbar_wait(raw_empty + u % RD, (u / RD) & 1)) issue_raw(u + RD);
                     else *abort_flag = 1;
                 }
             }
         }
-    } else
-    for (int kb = 0; kb < nkb; kb++) {
-        const int st = kb % NS, use = kb / NS, slot = kb % RD;
-        const uint32_t ast = base + st * stage_bytes, bst = ast + 4 * A_ATOM;
-        // the tensor core must be done with this stage's previous contents; the packed block must have landed
-        // (the decision to give up is taken per warp, so that no lane leaves its warp behind)
-        bool ok = !*abort_flag;
-        if (ok && use > 0) ok = finch_mbar_wait(done + st, (use - 1) & 1);
-        if (ok && expert) ok = finch_mbar_wait(raw_full + slot, (kb / RD) & 1);
-        if (!__all_sync(0xffffffffu, ok)) {
-            *abort_flag = 1;
-            failed = true;
-            break;
-        }
-        // ---- activations: m rows of 128 values, copied asynchronously while the weights are dequantised ----
-        for (int i = tid; i < m * 16; i += NT) {
-            const int j = i >> 4, c = i & 15;
-            const size_t src = (size_t)src_rows[j] * a.K + (size_t)kb * BK + c * 8;
-            const uint32_t dst = bst + (c >> 3) * b_atom + swz(j, c & 7);
-            cp_async16(dst, a.X + src);
-            if (a.X2) cp_async16(bst + (c >> 3) * b_atom + swz(tn + j, c & 7), a.X2 + src);
-        }
-        // ---- weights: 64 values (one scale group) of row r ----
-        uint32_t cur[8];
-        if (expert) {
-            const uint32_t rs = raw + slot * RAW_STAGE;
-            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(cur[0]) : "r"(rs + raw_w));
-            asm volatile("ld.shared.u32 %0, [%1+4];" : "=r"(cur[1]) : "r"(rs + raw_w));
-            asm volatile("ld.shared.u32 %0, [%1+8];" : "=r"(cur[2]) : "r"(rs + raw_w));
-            asm volatile("ld.shared.u32 %0, [%1+24];" : "=r"(cur[3]) : "r"(rs + raw_w));
-            asm volatile("ld.shared.u32 %0, [%1+28];" : "=r"(cur[4]) : "r"(rs + raw_w));
-            asm volatile("ld.shared.u32 %0, [%1+32];" : "=r"(cur[5]) : "r"(rs + raw_w));
-            asm volatile("ld.shared.u16 %0, [%1];" : "=r"(sreg) : "r"(rs + raw_s));
-            asm volatile("ld.shared.u16 %0, [%1+8];" : "=r"(breg) : "r"(rs + raw_s));
-            cur[6] = cur[7] = 0;
-            __syncwarp();
-            if (lane == 0) {   // this warp is done with the ring slot
-                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(finch_smem_u32(raw_empty + slot)) : "memory");
+    } else {
+        issue_acts(0);
+        for (int kb = 0; kb < nkb; kb++) {
+            const int st = kb % NS, u = kb >> 1, slot = u % RD;
+            const uint32_t ast = base + st * a_stage;
+            // Block kb - 2 used this weight stage and the activation stage block kb + 1 goes into: the tensor core must be
+            // done with it.  The packed unit must have landed.  (The decision to give up is taken per warp, so that no
+            // lane leaves its warp behind.)
+            bool ok = !*abort_flag;
+            if (ok && kb >= NS) ok = finch_mbar_wait(done + st, ((kb - NS) / NS) & 1);
+            if (ok && expert && !(kb & 1)) ok = finch_mbar_wait(raw_full + slot, (u / RD) & 1);
+            if (!__all_sync(0xffffffffu, ok)) {
+                *abort_flag = 1;
+                failed = true;
+                break;
             }
-        } else {
+            if (kb + 1 < nkb) issue_acts(kb + 1);   // lands while this block is dequantised
+            // ---- weights: 32 values of row r, group kb ----
+            uint32_t cur[4];
+            if (expert) {
+                const uint32_t rs = raw + slot * RAW_STAGE, wo = rs + raw_w + (uint32_t)((kb & 1) * 48), so = rs + raw_s + (uint32_t)((kb & 1) * 2);
+                asm volatile("ld.shared.u32 %0, [%1];" : "=r"(cur[0]) : "r"(wo));
+                asm volatile("ld.shared.u32 %0, [%1+4];" : "=r"(cur[1]) : "r"(wo));
+                asm volatile("ld.shared.u32 %0, [%1+8];" : "=r"(cur[2]) : "r"(wo));
+                asm volatile("ld.shared.u16 %0, [%1];" : "=r"(sreg) : "r"(so));
+                asm volatile("ld.shared.u16 %0, [%1+8];" : "=r"(breg) : "r"(so));
+                cur[3] = 0;
+                __syncwarp();
+                if ((kb & 1) && lane == 0) {   // this warp is done with the ring slot
+                    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(finch_smem_u32(raw_empty + slot)) : "memory");
+                }
+            } else {
 #pragma unroll
-            for (int i = 0; i < 8; i++) cur[i] = wreg[i];
-        }
-        float s0, b0, unused;
-        finch_widen16x2(sreg, a.scale_dtype, s0, unused);
-        finch_widen16x2(breg, a.scale_dtype, b0, unused);
-        const GroupScale gs = group_scale(s0, b0);
-        if (!expert && kb + 1 < nkb) load_block(kb + 1);   // in flight while this block is dequantised
-        // row r of atom kh: chunk c sits at (c ^ (r & 7)) * 16 inside the row
-        const uint32_t arow = ast + kh * A_ATOM + (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
-        const uint32_t rx = (uint32_t)(r & 7);
-        if (a.mode == DENSE4) {
-#pragma unroll
-            for (int c = 0; c < 8; c++) {
-                uint32_t o[4], ol[4];
-                dq4_word(cur[c], gs, o, ol);
-                st_shared16(arow + ((c ^ rx) << 4), o[0], o[1], o[2], o[3]);
-                st_shared16(arow + 2 * A_ATOM + ((c ^ rx) << 4), ol[0], ol[1], ol[2], ol[3]);
+                for (int i = 0; i < 4; i++) cur[i] = wreg[i];
             }
-        } else {
-#pragma unroll
-            for (int t = 0; t < 2; t++) {
-                uint32_t o[16], ol[16];
-                dq3_piece(cur[3 * t], cur[3 * t + 1], cur[3 * t + 2], gs, o, ol);
+            float s0, b0, unused;
+            finch_widen16x2(sreg, a.scale_dtype, s0, unused);
+            finch_widen16x2(breg, a.scale_dtype, b0, unused);
+            const GroupScale gs = group_scale(s0, b0);
+            if (!expert && kb + 1 < nkb) load_block(kb + 1);   // in flight while this block is dequantised
+            // row r of the atom: chunk c sits at (c ^ (r & 7)) * 16 inside the row; this thread owns chunks 4 kh .. 4 kh + 3
+            const uint32_t arow = ast + (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+            const uint32_t rx = (uint32_t)(r & 7);
+            if (a.mode == DENSE4) {
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
-                    st_shared16(arow + (((t * 4 + c) ^ rx) << 4), o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-                    st_shared16(arow + 2 * A_ATOM + (((t * 4 + c) ^ rx) << 4), ol[4 * c], ol[4 * c + 1], ol[4 * c + 2], ol[4 * c + 3]);
+                    uint32_t o[4], ol[4];
+                    dq4_word(cur[c], gs, o, ol);
+                    st_shared16(arow + (((kh * 4 + c) ^ rx) << 4), o[0], o[1], o[2], o[3]);
+                    st_shared16(arow + A_ATOM + (((kh * 4 + c) ^ rx) << 4), ol[0], ol[1], ol[2], ol[3]);
+                }
+            } else {
+                uint32_t o[16], ol[16];
+                dq3_piece(cur[0], cur[1], cur[2], gs, o, ol);
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    st_shared16(arow + (((kh * 4 + c) ^ rx) << 4), o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+                    st_shared16(arow + A_ATOM + (((kh * 4 + c) ^ rx) << 4), ol[4 * c], ol[4 * c + 1], ol[4 * c + 2], ol[4 * c + 3]);
                 }
             }
+            // the activations of this block have landed (those of the next one may still be on their way)
+            if (kb + 1 < nkb) asm volatile("cp.async.wait_group 1;" ::: "memory");
+            else asm volatile("cp.async.wait_group 0;" ::: "memory");
+            proxy_fence();          // generic-proxy writes -> visible to the tensor core (async proxy)
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(finch_smem_u32(a_full + st)) : "memory");
         }
-        cp_async_wait_all();
-        proxy_fence();          // generic-proxy writes -> visible to the tensor core (async proxy)
-        __syncwarp();
-        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(finch_smem_u32(a_full + st)) : "memory");
     }
 
     // ---- epilogue ----

@@ -193,9 +193,7 @@ int dense4_gemm(finch_ctx *ctx, cudaStream_t st, const finch_wdesc *w, const uin
     a.K = w->in_dim;
     // token tile: small enough that the grid covers the SMs, large enough not to dequantise a tile too often
     a.tn_max = tn_max_for((int)((long long)T * (w->out_dim / dqgemm::GM) / 148));
-    // two stages of [two weight planes + the activation planes] have to fit 227 KB of shared memory
-    if (a.tn_max > 128) a.tn_max = 128;
-    if (xb_lo && a.tn_max > 64) a.tn_max = 64;
+    if (xb_lo && a.tn_max > 128) a.tn_max = 128;   // two activation planes side by side: 2 x tokens accumulator columns (an MMA takes 256)
     a.X2 = xb_lo;
     a.scale_dtype = w->scale_dtype;
     a.W = (const uint32_t *)w->W;
@@ -255,12 +253,14 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
     uint16_t *act = (uint16_t *)ctx->act, *act_lo = act + (size_t)P * I;   // two bf16 planes [P][I] inside the fp32-sized buffer
     float *down = ctx->partial, *shared_out = ctx->partial + (size_t)P * H;
 
-    const int tn_a = tn_max_for(T < 32 ? T : 32), tn_b = 16;   // small token tiles keep two CTAs on an SM; popular experts take several
+    // token tiles: as many tokens as still let two CTAs share an SM (an expert's tile is dequantised once per token tile)
+    const bool x_lo_needed = c.act_dtype != FINCH_BF16;   // fp32 activations travel as two bf16 planes
+    const int tn_a = tn_max_for(T < 64 ? T : (x_lo_needed ? 32 : 64)), tn_b = 32;
     pf_sort_kernel<<<1, 1024, 4 * c.n_experts * sizeof(int), st>>>(ids, valid, slot_row, c.n_experts, P, seg, order, tn_a, tn_b, items_a, items_b,
                                                                    n_items);
     FINCH_CUDA_OK(ctx, cudaGetLastError());
     const uint16_t *x = (const uint16_t *)h_post, *x_lo = nullptr;
-    if (c.act_dtype != FINCH_BF16) {
+    if (x_lo_needed) {
         pf_to_bf16_kernel<<<148, 256, 0, st>>>((const float *)h_post, xb, xl, (size_t)T * H);
         FINCH_CUDA_OK(ctx, cudaGetLastError());
         x = xb;
