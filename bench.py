@@ -1,26 +1,30 @@
 #!/usr/bin/env python
-"""Benchmark of the quantized-expert MoE decode path.
+"""Benchmark of the quantized-expert MoE path: the 40-layer 3-bit expert stack.
 
-Workload at N=1: the full 40-layer expert stack, 40 x 256 three-bit experts
-(14.09 GB, resident in HBM, device-generated synthetic values), one 4-bit shared
-expert per layer, batch 8 (headline) and batch 1 (reported under "batch1"),
-per-layer top-8 ids drawn from a Zipf(1.1) popularity, hidden ~N(0,1) bf16.
-One step = one pass of the 40 layers (40 calls of the per-layer entry point).
-Metric = algorithmic HBM bytes per second: every distinct selected expert block
-(1,376,256 B) plus the shared expert (1,769,472 B) per layer, divided by the
-device time of the step.
+N = 1.  The full stack, 40 x 256 three-bit experts (14.09 GB resident in HBM, device-generated synthetic
+values), one 4-bit shared expert per layer, batch 8 (headline) and batch 1, top-8 ids per layer drawn from a
+Zipf(1.1) popularity that all tokens of a layer share, hidden ~N(0,1) bf16.  One step = one pass of the 40
+layers (40 calls of the per-layer entry point).  Metric = algorithmic HBM bytes per second: every distinct
+selected expert block (1,376,256 B) plus the shared expert (1,769,472 B) per layer, over the device time of
+the step.  The same line carries the 512-token chunked prefill, the expert-parallel layer run by one rank,
+the other matvec tiers and the CPU baseline.
+
+N > 1 (under torchrun).  The expert-parallel layer: every rank holds 256 / N experts of every layer and owns
+8 tokens per decode step and 512 tokens per prefill chunk (64 and 4096 in all at N = 8).  The line carries
+tokens/s of both, the parity of what was timed, and the all-to-all's share of the time.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-`--impl reference` times the CPU restatement of the reference's own CPU expert
-path (oracle/finch_oracle.c; the reference's Objective-C file does not compile
-here) on the host cores, on a bounded sample of the same workload.
+`--impl reference` times the reference's own CPU expert path on the host cores (its C functions compiled into
+oracle/_ref when that build is present, else the restatement in oracle/finch_oracle.c).
 """
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
+import re
 import subprocess
 import sys
 import tempfile
@@ -39,22 +43,40 @@ SHARED_BYTES = 3 * 589824
 GATEUP_BYTES = 2 * (393216 + 2 * 32768)  # gate + up codes, scales, biases of one expert
 SCALE_FP16, ACT_BF16 = 1, 0
 METRIC = "moe3_decode_hbm_gbs"
+PREFILL_CHUNK = 512
+KERNELS_PER_LAYER = 3            # gate/up/SiLU, down, combine
 
 
-def routing_sets(batch: int, n_sets: int, n_layers: int | None = None):
-    """[set][layer] -> (ids [B,8], weights [B,8]); Zipf(1.1) popularity per layer."""
+def layer_popularity(layer: int) -> np.ndarray:
+    return synth.zipf_popularity(synth.rng_for(2, layer, 7), NEXP)
+
+
+def routing_sets(batch: int, n_sets: int, n_layers: int | None = None, rank: int = 0):
+    """[set][layer] -> (ids [B,8], weights [B,8]).  A layer's Zipf(1.1) popularity is the same for every token,
+    set and rank; the draws differ."""
     n_layers = LAYERS if n_layers is None else n_layers
-    out = []
-    for s in range(n_sets):
-        per_layer = []
-        for l in range(n_layers):
-            per_layer.append(synth.zipf_routing(synth.rng_for(2, l, 100 + s), batch, NEXP, TOPK))
-        out.append(per_layer)
-    return out
+    perms = [layer_popularity(l) for l in range(n_layers)]
+    return [[synth.zipf_routing_shared(synth.rng_for(2, l, 100 + s + 1000 * rank), batch, perms[l], TOPK) for l in range(n_layers)]
+            for s in range(n_sets)]
 
 
 def alg_bytes(ids: np.ndarray, shared: bool = True) -> int:
     return len(set(ids.ravel().tolist())) * EXPERT_BYTES + (SHARED_BYTES if shared else 0)
+
+
+def spread(ms) -> dict:
+    a = np.asarray(ms, np.float64)
+    return {"median": float(np.median(a)), "p10": float(np.percentile(a, 10)), "p90": float(np.percentile(a, 90)),
+            "min": float(a.min()), "max": float(a.max()), "n": int(a.size)}
+
+
+def cos_and_rel(got, want) -> dict:
+    """cos and max |a - b| / max(|b|, rms(b)): the parity tests' two figures."""
+    a, b = np.asarray(got, np.float64).ravel(), np.asarray(want, np.float64).ravel()
+    na, nb = np.linalg.norm(a), np.linalg.norm(b)
+    cos = 1.0 if na == 0 and nb == 0 else float(a @ b / (na * nb + 1e-300))
+    floor = np.sqrt(np.mean(b * b)) + 1e-30
+    return {"cos": cos, "max_rel": float(np.max(np.abs(a - b) / np.maximum(np.abs(b), floor))), "finite": bool(np.all(np.isfinite(a)))}
 
 
 class ClockSampler:
@@ -111,51 +133,110 @@ def measured_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
+def profiled_traffic_ratio():
+    """DRAM bytes per algorithmic byte of the gate/up kernel, from the committed profiler summary
+    (a line `traffic_ratio: dram_bytes / algorithmic_bytes`); None when the summary carries none."""
+    p = os.path.join(ROOT, "profiles", "moe_gateup_kernel_batch8.md")
+    try:
+        m = re.search(r"^traffic_ratio:\s*([0-9]+)\s*/\s*([0-9]+)", open(p).read(), re.M)
+    except OSError:
+        return None, None
+    if not m:
+        return None, None
+    return int(m.group(1)) / int(m.group(2)), os.path.relpath(p, ROOT)
+
+
 # --------------------------------------------------------------------- CPU arm
-def cpu_arm(batch: int, sample_layers: int, threads: int, steps: int = 1, warmup: int = 0, blocks_from=None):
-    """Times the oracle's CPU expert path on `sample_layers` layers of the
-    batch-`batch` workload.  Returns (GB/s by the same byte definition, seconds per pass, description)."""
-    from concurrent.futures import ThreadPoolExecutor
+class CpuExpertPath:
+    """The reference's CPU expert path (serial over a token's experts, finchmoe/infer.m:10109-10204: gate and up
+    matvec, SwiGLU, down matvec, weighted add), on expert blocks of the bench's shapes.  kind "reference" drives
+    the reference's own functions (oracle/_ref); "port" the restatement."""
 
-    from oracle import oracle as orc
-    orc.build()
-    rs = routing_sets(batch, 1, sample_layers)[0]
-    x = synth.activations(synth.rng_for(2, 0, 7), batch, HIDDEN)
-    layers = []
-    total_bytes = 0
-    for l, (ids, w) in enumerate(rs):
-        uniq = sorted(set(ids.ravel().tolist()))
-        if blocks_from is not None:
-            blocks = {e: blocks_from(l, e) for e in uniq}
+    def __init__(self):
+        from oracle import oracle as orc
+        self.orc = orc
+        orc.build()
+        self.ref = orc.ref_lib()
+        self.kind = "reference" if self.ref is not None else "port"
+        rng = synth.rng_for(2, 0, 55)
+        self.blocks = [synth.expert_block(rng, scale_dtype=SCALE_FP16) for _ in range(8)]
+        self.block = self.blocks[0]
+        self.lay = synth.expert_layout()
+        self.x = synth.activations(synth.rng_for(2, 0, 7), 8, HIDDEN)
+
+    def blocks_for(self, uniq):
+        # which values an expert holds is irrelevant to CPU speed: eight generated blocks take turns
+        return {e: self.blocks[i % len(self.blocks)] for i, e in enumerate(uniq)}
+
+    def pair(self, blk, x, w, acc):
+        """acc += w * expert(x) for one (token, expert) pair."""
+        if self.ref is None:
+            acc += w * self.orc.expert_forward(blk, 3, SCALE_FP16, HIDDEN, INTER, 64, x, accum=self.orc.ACC_F32)
+            return
+        import ctypes as C
+        R, L = self.ref, self.lay
+        f32p = C.POINTER(C.c_float)
+        base = blk.ctypes.data
+        g, u, a, d = (np.empty(n, np.float32) for n in (INTER, INTER, INTER, HIDDEN))
+        xp = x.ctypes.data_as(f32p)
+        # the reference's function reads the 16-bit scale words as bf16; the arithmetic per weight is the same
+        R.ref_cpu_dequant_matvec(base + L["gate_w"], base + L["gate_s"], base + L["gate_b"], xp, g.ctypes.data_as(f32p), INTER, HIDDEN, 64, 3)
+        R.ref_cpu_dequant_matvec(base + L["up_w"], base + L["up_s"], base + L["up_b"], xp, u.ctypes.data_as(f32p), INTER, HIDDEN, 64, 3)
+        R.ref_cpu_swiglu(g.ctypes.data_as(f32p), u.ctypes.data_as(f32p), a.ctypes.data_as(f32p), INTER)
+        R.ref_cpu_dequant_matvec(base + L["down_w"], base + L["down_s"], base + L["down_b"], a.ctypes.data_as(f32p), d.ctypes.data_as(f32p),
+                                 HIDDEN, INTER, 64, 3)
+        R.ref_cpu_vec_madd(acc.ctypes.data_as(f32p), d.ctypes.data_as(f32p), float(w), HIDDEN)
+
+    def time_layers(self, rs, batch, threads):
+        """One pass over the layers of routing set rs ([layer] -> (ids, w)); returns (seconds, algorithmic bytes).
+        The routed experts only, as the reference's CPU fallback runs them; threads > 1 = one pair per thread."""
+        from concurrent.futures import ThreadPoolExecutor
+        x = np.ascontiguousarray(self.x[:batch])
+        jobs, nbytes = [], 0
+        for ids, w in rs:
+            blocks = self.blocks_for(sorted(set(ids.ravel().tolist())))
+            accs = [np.zeros(HIDDEN, np.float32) for _ in range(batch)]
+            jobs.append([(blocks[int(ids[t, k])], x[t], float(w[t, k]), accs[t], t) for t in range(batch) for k in range(TOPK)])
+            nbytes += alg_bytes(ids, shared=False)
+        t0 = time.perf_counter()
+        if threads <= 1:
+            for layer in jobs:
+                for blk, xt, wk, acc, _ in layer:
+                    self.pair(blk, xt, wk, acc)
         else:
-            rng = synth.rng_for(2, l, 55)
-            one = synth.expert_block(rng, scale_dtype=SCALE_FP16)
-            # distinct contents per expert are irrelevant to CPU speed: rotate one block's bytes
-            blocks = {e: np.roll(one, 3 * i) if i else one for i, e in enumerate(uniq)}
-        sh = synth.shared_expert(synth.rng_for(2, l, 56), scale_dtype=SCALE_FP16)
-        layers.append((ids, w, blocks, sh))
-        total_bytes += alg_bytes(ids)
-    per_tok_threads = min(TOPK, max(1, threads))
-    tok_workers = max(1, threads // per_tok_threads)
+            with ThreadPoolExecutor(threads) as ex:
+                for layer in jobs:
+                    # pairs of one token go to one worker in order (its accumulator is not shared)
+                    per_tok = {}
+                    for j in layer:
+                        per_tok.setdefault(j[4], []).append(j)
+                    chunks = []
+                    for lst in per_tok.values():
+                        n = max(1, min(len(lst), threads // max(1, len(per_tok))))
+                        chunks += [lst[i::n] for i in range(n)]
 
-    def one_pass():
-        for ids, w, blocks, sh in layers:
-            def tok(t):
-                return orc.moe_layer([blocks[int(e)] for e in ids[t]], w[t], None, x[t], scale_dtype=SCALE_FP16,
-                                     shared=sh, shared_gate_score=0.1, accum=orc.ACC_F32, nthreads=per_tok_threads)
-            if tok_workers > 1 and batch > 1:
-                with ThreadPoolExecutor(tok_workers) as ex:
-                    list(ex.map(tok, range(batch)))
-            else:
-                for t in range(batch):
-                    tok(t)
-    for _ in range(warmup):
-        one_pass()
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        one_pass()
-    dt = (time.perf_counter() - t0) / steps
-    return total_bytes / dt / 1e9, dt, f"{sample_layers} of {LAYERS} layers, batch {batch}, sequential-fp32 C port"
+                    def run(chunk):
+                        part = np.zeros(HIDDEN, np.float32)
+                        for blk, xt, wk, _, _ in chunk:
+                            self.pair(blk, xt, wk, part)
+                        return chunk[0][3], part
+                    for acc, part in list(ex.map(run, chunks)):
+                        acc += part
+        return time.perf_counter() - t0, nbytes
+
+    def numpy_row(self, rs, batch):
+        """numpy: dequantise the tile (codes * scale + bias), then W @ x (BLAS threads as configured)."""
+        x = self.x[:batch]
+        n_pairs = sum(ids.size for ids, _ in rs)
+        t0 = time.perf_counter()
+        reps = min(n_pairs, 16)
+        for _ in range(reps):
+            for which in ("gate", "up", "down"):
+                tt = synth.block_tensor(self.block, which, scale_dtype=SCALE_FP16)
+                W = self.orc.np_dequant_affine(tt["W"], tt["S"], tt["B"], SCALE_FP16, tt["out_dim"], tt["in_dim"], 64, 3)
+                _ = W @ (x[0] if which != "down" else np.zeros(INTER, np.float32))
+        dt = (time.perf_counter() - t0) / reps
+        return dt   # seconds per (token, expert) pair
 
 
 def run_reference(args):
@@ -163,18 +244,51 @@ def run_reference(args):
     if rank != 0:
         return
     cores = os.cpu_count() or 1
-    # sized so warmup + steps stay within a few minutes: ~0.03 s per (token, expert) on one core
-    budget_s = 20.0
-    per_layer_s = 8 * 8 * 0.012 / min(cores, 64) + 0.02
-    sample_layers = int(max(1, min(LAYERS, budget_s / max(1, args.steps + args.warmup) / per_layer_s)))
-    gbs, dt, what = cpu_arm(8, sample_layers, cores, steps=args.steps, warmup=args.warmup)
+    cpu = CpuExpertPath()
+    rs_all = routing_sets(8, 1)[0]
+    # one probe pair sizes the step: all 40 layers when warm-up + steps fit in about two minutes, else fewer layers
+    acc = np.zeros(HIDDEN, np.float32)
+    cpu.pair(cpu.block, cpu.x[0], 1.0, acc)
+    t0 = time.perf_counter()
+    cpu.pair(cpu.block, cpu.x[0], 1.0, acc)
+    pair_s = time.perf_counter() - t0
+    threads = min(cores, 64)
+    est_layer = 64 * pair_s / min(threads, 64) * 1.3 + 0.005
+    n_layers = int(max(1, min(LAYERS, 120.0 / max(1, args.steps + args.warmup) / est_layer)))
+    rs = rs_all[:n_layers]
+    for _ in range(args.warmup):
+        cpu.time_layers(rs, 8, threads)
+    secs, nbytes = [], 0
+    for _ in range(args.steps):
+        dt, b = cpu.time_layers(rs, 8, threads)
+        secs.append(dt)
+        nbytes += b
+    total = float(sum(secs))
+    gbs = nbytes / total / 1e9
+    # rows beside it, on one layer: the single-thread loop the reference's fallback runs, 8 threads, numpy
+    one = rs_all[:1]
+    dt1, b1 = cpu.time_layers(one, 8, 1)
+    dt8, _ = cpu.time_layers(one, 8, 8)
+    np_pair = cpu.numpy_row(one, 8)
+    what = (f"{n_layers} of {LAYERS} layers per step, batch 8, routed experts, {threads} threads (one (token, expert) pair per task), "
+            + ("the reference's C functions (finchmoe/infer.m:1676-1763, 1780-1786, 1849-1851) compiled with gcc -O2"
+               if cpu.kind == "reference" else "sequential-fp32 C restatement"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     line = {
         "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": dt * 1e3 * LAYERS / sample_layers, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "C2: 40-layer 3-bit expert stack decode, batch 8, top-8 of 256, Zipf(1.1)", "batch": 8,
-                   "layers": LAYERS, "hidden": HIDDEN, "moe_inter": INTER, "l2": "n/a (CPU)"},
-        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port", "sample": what},
+        "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3, "step_ms": spread([s * 1e3 for s in secs]),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "C2: 40-layer 3-bit expert stack decode, batch 8, top-8 of 256, Zipf(1.1)"
+                   + ("" if world == 1 else f" (the one-process CPU path; it stands in for C5, the expert-parallel layer on {world} GPUs, which has no CPU form)"),
+                   "batch": 8, "layers": LAYERS, "layers_per_step": n_layers, "hidden": HIDDEN, "moe_inter": INTER, "scale_dtype": "fp16",
+                   "act_dtype": "f32", "pool_gb": LAYERS * NEXP * EXPERT_BYTES / 1e9, "parallelism": f"{threads} host threads",
+                   "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": cpu.kind, "sample": what},
+        "cpu_rows": {"single_thread": {"value": b1 / dt1 / 1e9, "unit": "GB/s", "ms_per_layer": dt1 * 1e3, "cores": 1,
+                                       "note": "the reference's --cpu-experts loop is serial over experts (finchmoe/infer.m:10109-10204)"},
+                     "threads_8": {"value": b1 / dt8 / 1e9, "unit": "GB/s", "ms_per_layer": dt8 * 1e3, "cores": 8},
+                     "numpy": {"ms_per_pair": np_pair * 1e3, "note": "dequantise three tiles with numpy, then W @ x"}},
+        "tokens_per_s": 8 * n_layers / LAYERS * args.steps / total,
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
@@ -192,8 +306,9 @@ class Stack:
         from finchmoe_b200 import api, lib as L
         self.torch, self.L = torch, L
         torch.cuda.set_device(device)
+        self.seed = seed
         self.ctx = api.Context(device=device, n_layers=layers, max_tokens=max_tokens, scale_dtype=L.FP16, act_dtype=L.BF16)
-        if shard is None:
+        if shard is None or shard[1] == 1:
             self.pool = self.ctx.pool()
             self.pool.fill_synthetic(0, layers, seed)
         else:
@@ -241,7 +356,9 @@ class Stack:
             graphs.append(g)
         return graphs
 
-    def time_steps(self, rsets_dev, xd, score, out, batch, steps, warmup, barrier=None, use_graph=True):
+    def time_steps(self, rsets_dev, xd, score, out, batch, steps, warmup, use_graph=True):
+        """Returns (seconds for `steps` steps, [ms of every step]) from CUDA events on the launching stream: one
+        event before the first step and one after each."""
         torch = self.torch
         graphs = self.capture(rsets_dev, xd, score, out, batch) if use_graph else None
 
@@ -255,17 +372,13 @@ class Stack:
         for i in range(warmup):
             run(i)
         torch.cuda.synchronize()
-        if barrier:
-            barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(self.stream)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+        ev[0].record(self.stream)
         for i in range(steps):
             run(warmup + i)
-        e1.record(self.stream)
+            ev[i + 1].record(self.stream)
         torch.cuda.synchronize()
-        if barrier:
-            barrier()
-        return e0.elapsed_time(e1) / 1e3  # seconds for `steps` steps
+        return ev[0].elapsed_time(ev[steps]) / 1e3, [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
 
     def time_prefill(self, T, steps, warmup):
         """One chunk of T tokens through finch_encode_moe_prefill on every layer; seconds per pass, distinct experts."""
@@ -293,8 +406,9 @@ class Stack:
 
     def time_e2e(self, rsets, x, batch, steps, warmup):
         """Host buffers in and out through finch_moe_forward_host, layer by layer.  Every call stages its inputs in
-        pinned host memory and the bytes cross the bus inside the timed region, both ways: for decode-sized calls as
-        reads and writes of the layer's kernels on the pinned block, otherwise as one copy in and one copy out."""
+        pinned host memory and the bytes cross the bus inside the timed region, both ways: the inputs as one copy
+        to the device, the result as the combine kernel's writes to the pinned block (decode-sized calls) or one
+        copy back."""
         torch = self.torch
         xw = self.ctx.acts_to_wire(x)
         score = np.full(batch, 0.1, np.float32)
@@ -318,6 +432,285 @@ class Stack:
         return (time.perf_counter() - t0), h2d * self.layers, d2h * self.layers
 
 
+# ------------------------------------------------------- expert-parallel layer
+class EpBench:
+    """The expert-parallel layer at any number of ranks (one rank: the same protocol, its exchanges are copies).
+    Decode: 8 tokens per rank per step through ep_layer_static, one CUDA graph per routing set.  Prefill: 512
+    tokens per rank per chunk through ep_layer (planned exchange)."""
+
+    BATCH, N_SETS = 8, 4
+
+    def __init__(self, stack, dist, rank, world, args):
+        import torch
+
+        from finchmoe_b200 import ep
+        self.torch, self.ep, self.stack, self.dist, self.rank, self.world, self.args = torch, ep, stack, dist, rank, world, args
+        self.backend = ep.GpuBackend(stack.ctx, stack.pool, max(self.BATCH, PREFILL_CHUNK) * world)
+        self.score_val = 0.1
+        self.graphs = None
+
+    # ---- helpers
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
+
+    def max_over_ranks(self, v: float) -> float:
+        if self.dist is None:
+            return v
+        t = self.torch.tensor([v], device="cuda", dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(self, v: float) -> float:
+        if self.dist is None:
+            return v
+        t = self.torch.tensor([v], device="cuda", dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def gather_ints(self, v: int):
+        if self.dist is None:
+            return [int(v)]
+        t = self.torch.zeros(self.world, device="cuda", dtype=self.torch.int64)
+        t[self.rank] = int(v)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        return [int(a) for a in t.cpu().tolist()]
+
+    def timed(self, n, w0, fn):
+        """w0 warm-up calls, then n timed: barrier and synchronize on both sides, one event per step, the total as
+        the maximum over ranks.  Returns (seconds, [ms per step on this rank])."""
+        torch = self.torch
+        for i in range(w0):
+            fn(i)
+        torch.cuda.synchronize()
+        self.barrier()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(n + 1)]
+        ev[0].record()
+        for i in range(n):
+            fn(w0 + i)
+            ev[i + 1].record()
+        torch.cuda.synchronize()
+        self.barrier()
+        return self.max_over_ranks(ev[0].elapsed_time(ev[n]) / 1e3), [ev[i].elapsed_time(ev[i + 1]) for i in range(n)]
+
+    # ---- decode
+    def setup_decode(self):
+        st, world, rank = self.stack, self.world, self.rank
+        # every rank can regenerate every rank's routing (seeded), which is all the byte count needs
+        self.all_sets = [routing_sets(self.BATCH, self.N_SETS, LAYERS, r) for r in range(world)]
+        self.dev, self.xd, self.score, self.out, self.x = st.device_inputs(self.all_sets[rank], self.BATCH)
+        self.shared = [st.ctx.make_shared(*st.shared[l], gate_score=self.score) for l in range(LAYERS)]
+
+    def decode_layers(self, s):
+        ids, w = self.dev[s]
+        for l in range(LAYERS):
+            self.ep.ep_layer_static(self.backend, self.dist, None, l, self.xd, ids[l], w[l], None, self.shared[l], None, self.out[l], in_scope=True)
+
+    def decode_eager(self, i):
+        with self.backend.stream_scope():
+            self.decode_layers(i % self.N_SETS)
+
+    def capture_decode(self):
+        """One CUDA graph per routing set (kernels and all-to-alls).  Every rank must take the same path: a rank
+        that replays graphs cannot pair with one that launches from the host."""
+        torch = self.torch
+        note = "launched from the host every step"
+        graphs = None
+        if not self.args.no_graph:
+            try:
+                for s in range(self.N_SETS):      # communicators, lazily made buffers and tables exist before capture
+                    self.decode_eager(s)
+                torch.cuda.synchronize()
+                self.barrier()
+                graphs = []
+                for s in range(self.N_SETS):
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=self.backend.stream, capture_error_mode="thread_local"):
+                        self.decode_layers(s)
+                    graphs.append(g)
+                    del g
+                torch.cuda.synchronize()
+                note = "one CUDA graph per routing set (kernels and all-to-alls)"
+            except Exception as e:                # capture of the collectives unavailable: keep launching from the host
+                graphs = None
+                note = "launched from the host every step (graph capture failed: %s)" % (str(e).splitlines()[0][:120] if str(e) else type(e).__name__)
+                torch.cuda.synchronize()
+        ok = 1 if graphs is not None else 0
+        if self.dist is not None:
+            flag = torch.tensor([ok], device="cuda")
+            self.dist.all_reduce(flag, op=self.dist.ReduceOp.MIN)
+            ok = int(flag.item())
+        self.graphs = graphs if ok else None
+        return note
+
+    def decode_step(self, i):
+        if self.graphs is not None:
+            self.graphs[i % self.N_SETS].replay()
+        else:
+            self.decode_eager(i)
+
+    def decode_step_bytes(self, s):
+        """Distinct experts touched by all ranks' tokens (each lives on one rank), plus every rank's copy of the
+        shared expert."""
+        total = 0
+        for l in range(LAYERS):
+            touched = set()
+            for r in range(self.world):
+                touched |= set(self.all_sets[r][s][l][0].ravel().tolist())
+            total += len(touched) * EXPERT_BYTES + self.world * SHARED_BYTES
+        return total
+
+    def run_decode(self):
+        args, torch = self.args, self.torch
+        self.setup_decode()
+        c0 = int(self.stack.ctx.launch_count())
+        self.decode_eager(0)
+        torch.cuda.synchronize()
+        launches_per_step = int(self.stack.ctx.launch_count()) - c0      # graph replays do not pass the host counter
+        note = self.capture_decode()
+        secs, per_step = self.timed(args.steps, args.warmup, self.decode_step)
+        # end to end: the step's inputs come from pinned host memory and its result goes back to the host
+        xh = torch.from_numpy(self.stack.ctx.acts_to_wire(self.x).view(np.int16)).pin_memory()
+        res = torch.empty((self.BATCH, HIDDEN), dtype=torch.float32).pin_memory()
+
+        def step_e2e(i):
+            self.xd.view(torch.int16).copy_(xh, non_blocking=True)
+            self.decode_step(i)
+            res.copy_(self.out[LAYERS - 1], non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+        e2e_w = max(3, args.warmup)
+        e2e_secs, _ = self.timed(args.steps, e2e_w, step_e2e)
+        timed_bytes = sum(self.decode_step_bytes((args.warmup + i) % self.N_SETS) for i in range(args.steps))
+        e2e_bytes = sum(self.decode_step_bytes((e2e_w + i) % self.N_SETS) for i in range(args.steps))
+        rec = self.backend.record_bytes()
+        link_bytes = (self.world - 1) * self.BATCH * (rec + HIDDEN * 4) * LAYERS       # sent by one rank per step (it receives as much)
+        return {"launches_per_step": launches_per_step, "secs": secs, "per_step": per_step, "e2e_secs": e2e_secs, "bytes": timed_bytes, "e2e_bytes": e2e_bytes, "note": note,
+                "h2d": int(xh.numel() * 2 * self.world), "d2h": int(res.numel() * 4 * self.world),
+                "tokens_per_s": self.BATCH * self.world * args.steps / secs, "us_per_layer": secs / args.steps / LAYERS * 1e6,
+                "nvlink_gbs_per_gpu_per_direction": link_bytes * args.steps / secs / 1e9 if self.world > 1 else 0.0,
+                "link_bytes_per_gpu_per_step": link_bytes if self.world > 1 else 0}
+
+    # ---- prefill
+    def run_prefill(self, steps, warmup):
+        torch, st, T = self.torch, self.stack, PREFILL_CHUNK
+        rs = routing_sets(T, 1, LAYERS, self.rank)[0]
+        ids = torch.from_numpy(np.stack([r[0] for r in rs])).cuda()
+        w = torch.from_numpy(np.stack([r[1] for r in rs])).cuda()
+        x = synth.activations(synth.rng_for(2, 0, 9 + 1000 * self.rank), T, HIDDEN)
+        xd = torch.from_numpy(x).cuda().to(torch.bfloat16)
+        score = torch.full((T,), self.score_val, device="cuda")
+        out = torch.empty((2, T, HIDDEN), device="cuda")
+        shared = [st.ctx.make_shared(*st.shared[l], gate_score=score) for l in range(LAYERS)]
+        self.pf = (rs, ids, w, x, xd, score, shared)
+        self.backend.stats = []
+
+        def step(_):
+            for l in range(LAYERS):
+                self.ep.ep_layer(self.backend, self.dist, None, l, xd, ids[l], w[l], None, shared[l], None, out[l & 1])
+        secs, per_step = self.timed(steps, warmup, step)
+        stats, self.backend.stats = self.backend.stats, None
+        per_call = stats[-LAYERS:]                                       # the last step's layers
+        rows_sent = sum(sum(c for d, c in enumerate(cs) if d != self.rank) for cs, _ in per_call)
+        rows_recv = sum(sum(cr) for _, cr in per_call)
+        rec = self.backend.record_bytes()
+        pairs_local = sum(int(((r[0] // (NEXP // self.world)) == self.rank).sum()) for r in rs)   # of this rank's own tokens
+        link = rows_sent * (rec + HIDDEN * 4)
+        return {"chunk_tokens_per_gpu": T, "tokens_per_step": T * self.world, "steps": steps, "ms_per_step": secs / steps * 1e3,
+                "step_ms": spread(per_step), "tokens_per_s": T * self.world * steps / secs,
+                "rows_received_per_gpu_per_step": self.gather_ints(rows_recv),
+                "rows_sent_per_gpu_per_step": self.gather_ints(rows_sent),
+                "nvlink_gbs_per_gpu_per_direction": self.max_over_ranks(link * steps / secs / 1e9) if self.world > 1 else 0.0,
+                "own_pairs_on_own_experts": self.gather_ints(pairs_local)}
+
+    # ---- parity of what was timed
+    def parity(self):
+        """Layer 0 of routing set 0 (decode) and of the prefill chunk, as the expert-parallel layer computed them
+        for this rank's tokens, against the one-GPU entry point on a pool that holds all 256 experts of that
+        layer (the same synthetic contents).  The worst figures over the ranks are reported."""
+        torch, st, ctx = self.torch, self.stack, self.stack.ctx
+        full = ctx.pool(n_layers=1)
+        full.fill_synthetic(0, 1, st.seed)
+        res = {}
+        try:
+            ids, w = self.dev[0]
+            with self.backend.stream_scope():
+                self.ep.ep_layer_static(self.backend, self.dist, None, 0, self.xd, ids[0], w[0], None, self.shared[0], None, self.out[0], in_scope=True)
+            torch.cuda.synchronize()
+            got = self.out[0].cpu().numpy()
+            want_d = torch.empty_like(self.out[0])
+            ctx.encode_moe_decode(full, 0, self.xd, ids[0], w[0], None, self.shared[0], None, want_d, self.BATCH)
+            torch.cuda.synchronize()
+            res["decode"] = cos_and_rel(got, want_d.cpu().numpy())
+            rs, pids, pw, x, xd, score, shared = self.pf
+            T = PREFILL_CHUNK
+            out = torch.empty((T, HIDDEN), device="cuda")
+            self.ep.ep_layer(self.backend, self.dist, None, 0, xd, pids[0], pw[0], None, shared[0], None, out)
+            torch.cuda.synchronize()
+            want_p = torch.empty_like(out)
+            ctx.set_prefill_mode(1)            # the exact sub-batch path: the decode kernels, 8 tokens at a time
+            ctx.encode_moe_decode(full, 0, xd, pids[0], pw[0], None, shared[0], None, want_p, T, prefill=True)
+            ctx.set_prefill_mode(0)
+            torch.cuda.synchronize()
+            res["prefill"] = cos_and_rel(out.cpu().numpy(), want_p.cpu().numpy())
+        finally:
+            full.destroy()
+        status = int(ctx.device_status())
+        worst = {}
+        for k, v in res.items():
+            worst[k] = {"cos": -self.max_over_ranks(-v["cos"]), "max_rel": self.max_over_ranks(v["max_rel"]),
+                        "finite": self.max_over_ranks(0.0 if v["finite"] else 1.0) == 0.0}
+        worst["device_status"] = int(self.max_over_ranks(float(abs(status))))
+        worst["against"] = "finch_encode_moe_decode on a rank-local pool holding all 256 experts of layer 0 (prefill rows: its sub-batch path)"
+        worst["ok"] = bool(worst["device_status"] == 0 and all(worst[k]["finite"] and worst[k]["cos"] >= 0.99999 and worst[k]["max_rel"] <= 1e-3
+                                                                for k in ("decode", "prefill")))
+        return worst
+
+    # ---- the exchanges alone
+    def time_exchanges(self, reps=5):
+        """The two all-to-alls of a decode layer with nothing between them, 40 pairs per CUDA graph: what the
+        exchange alone costs per layer."""
+        if self.world == 1:
+            return None
+        torch, dist = self.torch, self.dist
+        n = self.BATCH * self.world
+        a = torch.zeros(n * self.backend.record_bytes(), dtype=torch.uint8, device="cuda")
+        b = torch.empty_like(a)
+        c = torch.zeros(n * HIDDEN, dtype=torch.float32, device="cuda")
+        d = torch.empty_like(c)
+
+        def pairs():
+            for _ in range(LAYERS):
+                dist.all_to_all_single(b, a)
+                dist.all_to_all_single(d, c)
+        run = None
+        if self.graphs is not None:
+            try:
+                with self.backend.stream_scope():
+                    pairs()
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=self.backend.stream, capture_error_mode="thread_local"):
+                    pairs()
+                self.graphs.append(g)      # released with the others
+                run = g.replay
+                del g
+            except Exception:
+                run = None
+        ok = 1 if run is not None else 0
+        flag = torch.tensor([ok], device="cuda")
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if int(flag.item()) == 0:
+            def run():
+                with self.backend.stream_scope():
+                    pairs()
+        secs, _ = self.timed(reps, 2, lambda i: run())
+        return {"us_per_layer": secs / reps / LAYERS * 1e6, "what": "two all_to_all_single per layer (records out, fp32 rows back), nothing else"}
+
+    def release(self):
+        self.graphs = None
+        gc.collect()
+
+
 def run_ours(args):
     import torch
     rank = int(os.environ.get("RANK", "0"))
@@ -327,17 +720,16 @@ def run_ours(args):
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
-    if world > 1:
-        return run_ep(args, rank, local_rank, world)
+        return run_ep(args, rank, local_rank, world, dist)
     batch = 8
-    stack = Stack(local_rank, max_tokens=512, layers=LAYERS)
+    stack = Stack(local_rank, max_tokens=PREFILL_CHUNK, layers=LAYERS)
     n_sets = 4
-    rsets = [[(ids, w) for ids, w in rs] for rs in routing_sets(batch, n_sets)]
+    rsets = routing_sets(batch, n_sets)
     dev, xd, score, out, x = stack.device_inputs(rsets, batch)
 
     sampler = ClockSampler(local_rank)
-    secs = stack.time_steps(dev, xd, score, out, batch, args.steps, args.warmup, None, use_graph=not args.no_graph)
-    launches = 4 * LAYERS * args.steps  # four kernels per layer call (graph replays launch them without the host counter)
+    secs, per_step = stack.time_steps(dev, xd, score, out, batch, args.steps, args.warmup, use_graph=not args.no_graph)
+    launches = KERNELS_PER_LAYER * LAYERS * args.steps  # graph replays launch them without passing the host counter
     clocks = sampler.stop()
     step_bytes = [sum(alg_bytes(ids) for ids, _ in rs) for rs in rsets]
     timed_bytes = sum(step_bytes[(args.warmup + i) % n_sets] for i in range(args.steps))
@@ -352,181 +744,110 @@ def run_ours(args):
     peaks, peak_kind = measured_peaks()
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": secs / args.steps * 1e3, "step_ms": spread(per_step), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
         "config": {"workload": "C2: 40-layer 3-bit expert stack decode, batch 8, top-8 of 256, Zipf(1.1)", "batch": batch,
-                   "layers": LAYERS, "hidden": HIDDEN, "moe_inter": INTER, "scale_dtype": "fp16", "act_dtype": "bf16",
+                   "layers": LAYERS, "layers_per_step": LAYERS, "hidden": HIDDEN, "moe_inter": INTER, "scale_dtype": "fp16", "act_dtype": "bf16",
                    "pool_gb": LAYERS * NEXP * EXPERT_BYTES / 1e9, "parallelism": "1 GPU",
                    "l2": "inputs larger than L2: every step streams >= 0.5 GB of a 14 GB pool; 4 routing sets rotate"},
         "clocks": clocks,
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
-        "hbm_frac_of_" + peak_kind: value / world / peaks["hbm_gbs"],
+        "tokens_per_s": batch * args.steps / secs,
+        "us_per_layer": secs / args.steps / LAYERS * 1e6,
+        "hbm_frac_of_" + peak_kind: value / peaks["hbm_gbs"],
     }
 
-    if world == 1:
-        # batch 1 (single-stream decode) on the same pool
-        r1 = [[(ids, w) for ids, w in rs] for rs in routing_sets(1, n_sets)]
-        dev1, xd1, score1, out1, _ = stack.device_inputs(r1, 1)
-        s1 = stack.time_steps(dev1, xd1, score1, out1, 1, args.steps, args.warmup, use_graph=not args.no_graph)
-        b1 = sum(sum(alg_bytes(ids) for ids, _ in r1[(args.warmup + i) % n_sets]) for i in range(args.steps))
-        line["batch1"] = {"value": b1 / s1 / 1e9, "unit": "GB/s", "ms_per_step": s1 / args.steps * 1e3,
-                          "us_per_layer": s1 / args.steps / LAYERS * 1e6, "frac_of_" + peak_kind: b1 / s1 / 1e9 / peaks["hbm_gbs"]}
-        # per-kernel roofline of the dominant kernel (gate/up/SiLU)
-        line["roofline"] = kernel_roofline(stack, dev, rsets, xd, score, out, batch, args, peaks, peak_kind)
-        # chunked prefill: 512-token chunks through the grouped dequant-GEMM (tcgen05), the whole stack
-        T = 512
-        ps, uniq = stack.time_prefill(T, max(2, args.steps // 4), 1)
-        flops = LAYERS * (T * TOPK * 6291456 + T * 3 * 2 * 512 * HIDDEN)
-        pbytes = uniq * EXPERT_BYTES + LAYERS * SHARED_BYTES
-        ai = flops / pbytes
-        ceil_tf = min(peaks["bf16_tflops_sustained"], ai * peaks["hbm_gbs"] / 1e3)
-        line["prefill"] = {"metric": "moe3_prefill_tokens_per_s", "chunk": T, "value": T / ps, "unit": "tokens/s (40 MoE layers per token)",
-                           "ms_per_chunk": ps * 1e3, "tflops": flops / ps / 1e12, "hbm_gbs": pbytes / ps / 1e9,
-                           "roofline": {"bound": "hbm", "note": "8T/256 pairs per expert: below the tensor ridge", "ceiling_tflops": ceil_tf,
-                                        "frac": flops / ps / 1e12 / ceil_tf, "peak_kind": peak_kind}}
-        line["other_rows"] = aux_rooflines(stack, peaks, peak_kind)
-        # CPU baseline: bounded sample of the same workload on the expert blocks of this pool
-        cores = os.cpu_count() or 1
-        sample_layers = 2
-        gbs, dt, what = cpu_arm(batch, sample_layers, cores, blocks_from=lambda l, e: stack.pool.get(l, e))
-        line["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port", "sample": what,
-                                "seconds": dt}
+    # batch 1 (single-stream decode) on the same pool
+    r1 = routing_sets(1, n_sets)
+    dev1, xd1, score1, out1, _ = stack.device_inputs(r1, 1)
+    s1, per1 = stack.time_steps(dev1, xd1, score1, out1, 1, args.steps, args.warmup, use_graph=not args.no_graph)
+    b1 = sum(sum(alg_bytes(ids) for ids, _ in r1[(args.warmup + i) % n_sets]) for i in range(args.steps))
+    line["batch1"] = {"value": b1 / s1 / 1e9, "unit": "GB/s", "ms_per_step": s1 / args.steps * 1e3, "step_ms": spread(per1),
+                      "us_per_layer": s1 / args.steps / LAYERS * 1e6, "tokens_per_s": args.steps / s1,
+                      "frac_of_" + peak_kind: b1 / s1 / 1e9 / peaks["hbm_gbs"]}
+    # per-kernel roofline of the dominant kernel (gate/up/SiLU)
+    line["roofline"] = kernel_roofline(stack, dev, rsets, xd, score, out, batch, args, peaks, peak_kind)
+    # chunked prefill: 512-token chunks through the grouped dequant-GEMM (tcgen05), the whole stack
+    T = PREFILL_CHUNK
+    pf_steps = max(3, args.steps // 8)
+    ps, uniq = stack.time_prefill(T, pf_steps, 2)
+    flops = LAYERS * (T * TOPK * 6291456 + T * 3 * 2 * 512 * HIDDEN)
+    pbytes = uniq * EXPERT_BYTES + LAYERS * SHARED_BYTES
+    ai = flops / pbytes
+    ceil_tf = min(peaks["bf16_tflops_sustained"], ai * peaks["hbm_gbs"] / 1e3)
+    line["prefill"] = {"metric": "moe3_prefill_tokens_per_s", "chunk": T, "value": T / ps, "unit": "tokens/s (40 MoE layers per token)",
+                       "ms_per_chunk": ps * 1e3, "tflops": flops / ps / 1e12, "hbm_gbs": pbytes / ps / 1e9,
+                       "roofline": {"bound": "hbm", "note": "8T/256 pairs per expert: below the tensor ridge", "ceiling_tflops": ceil_tf,
+                                    "frac": flops / ps / 1e12 / ceil_tf, "peak_kind": peak_kind}}
+    # the expert-parallel layer run by one rank: the code path of --gpus N with its exchanges as copies
+    epb = EpBench(stack, None, 0, 1, args)
+    d = epb.run_decode()
+    p = epb.run_prefill(pf_steps, 2)
+    line["ep"] = {"n_gpus": 1, "decode": {"tokens_per_step": epb.BATCH, "tokens_per_s": d["tokens_per_s"], "us_per_layer": d["us_per_layer"],
+                                          "step_ms": spread(d["per_step"]), "launch": d["note"]},
+                  "prefill": p, "ep_parity": epb.parity()}
+    epb.release()
+    line["other_rows"] = aux_rooflines(stack, peaks, peak_kind)
+    # CPU baseline: a bounded sample of the same workload, all host threads
+    cores = os.cpu_count() or 1
+    cpu = CpuExpertPath()
+    sample = rsets[0][:2]
+    dt, nb = cpu.time_layers(sample, batch, min(cores, 64))
+    line["cpu_baseline"] = {"value": nb / dt / 1e9, "unit": "GB/s", "cores": min(cores, 64), "kind": cpu.kind,
+                            "sample": f"2 of {LAYERS} layers, batch {batch}, routed experts, one (token, expert) pair per task", "seconds": dt}
     print(json.dumps(line))
 
 
-
-def run_ep(args, rank, local_rank, world):
-    """N > 1: the batched-decode layer is expert parallel.  Every rank owns 8 tokens per step (weak scaling:
-    8 N tokens per step in all) and the contiguous block of 256 / N experts of every layer; per layer the
-    ranks exchange activation rows and partial outputs (finchmoe_b200/ep.py).  value = bytes of the distinct
-    local experts each rank streams per step (plus its copy of the shared expert), summed over ranks, per
-    second of the slowest rank."""
+def run_ep(args, rank, local_rank, world, dist):
+    """N > 1: the layer is expert parallel.  Every rank owns 8 tokens per decode step and 512 tokens per prefill
+    chunk (weak scaling) and the contiguous block of 256 / N experts of every layer; per layer the ranks exchange
+    activation rows and partial outputs (finchmoe_b200/ep.py).  value = bytes of the distinct experts the ranks
+    stream per decode step (plus every rank's copy of the shared expert) per second of the slowest rank."""
     import torch
-    import torch.distributed as dist
-
-    from finchmoe_b200 import ep
-    batch, n_sets = 8, 4
-    stack = Stack(local_rank, max_tokens=8 * world, layers=LAYERS, shard=(rank, world))
-    per = NEXP // world
-    # every rank can regenerate every rank's routing (seeded), which is all the byte count needs
-    all_sets = [[[synth.zipf_routing(synth.rng_for(2, l, 100 + s + 1000 * r), batch, NEXP, TOPK) for l in range(LAYERS)]
-                 for s in range(n_sets)] for r in range(world)]
-    rsets = all_sets[rank]
-    dev, xd, score, out, x = stack.device_inputs(rsets, batch)
-    backend = ep.GpuBackend(stack.ctx, stack.pool, batch * world)
-    shared = [stack.ctx.make_shared(*stack.shared[l], gate_score=score) for l in range(LAYERS)]
-
-    # Decode batches are small and the same size on every rank: the fixed-capacity exchange (every token to
-    # every rank, known message sizes) needs no row counts and no host synchronisation, so a whole step is a
-    # fixed sequence of launches and all-to-alls, recorded once per routing set into a CUDA graph.
-    def layers_of(s):
-        ids, w = dev[s]
-        for l in range(LAYERS):
-            ep.ep_layer_static(backend, dist, None, l, xd, ids[l], w[l], None, shared[l], None, out[l], in_scope=True)
-
-    def step_eager(i):
-        with backend.stream_scope():
-            layers_of(i % n_sets)
-
-    graphs, graph_note = None, "launched from the host every step"
-    if not args.no_graph:
-        try:
-            for s in range(n_sets):          # communicators, lazily made buffers and tables exist before capture
-                step_eager(s)
-            torch.cuda.synchronize()
-            dist.barrier()
-            graphs = []
-            for s in range(n_sets):
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=backend.stream, capture_error_mode="thread_local"):
-                    layers_of(s)
-                graphs.append(g)
-            torch.cuda.synchronize()
-            graph_note = "one CUDA graph per routing set (kernels and all-to-alls)"
-        except Exception as e:               # capture of the collectives unavailable: keep launching from the host
-            graphs = None
-            graph_note = "launched from the host every step (graph capture failed: %s)" % (str(e).splitlines()[0][:120] if str(e) else type(e).__name__)
-            torch.cuda.synchronize()
-    # every rank must take the same path: a rank that replays graphs cannot pair with one that launches eagerly
-    flag = torch.tensor([1 if graphs is not None else 0], device="cuda")
-    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
-    if int(flag.item()) == 0:
-        graphs = None
-
-    def step(i):
-        if graphs is not None:
-            graphs[i % n_sets].replay()
-        else:
-            step_eager(i)
-
-    def timed(n, w0, fn):
-        for i in range(w0):
-            fn(i)
-        torch.cuda.synchronize()
-        dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for i in range(n):
-            fn(w0 + i)
-        e1.record()
-        torch.cuda.synchronize()
-        dist.barrier()
-        t = torch.tensor([e0.elapsed_time(e1) / 1e3], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
+    stack = Stack(local_rank, max_tokens=PREFILL_CHUNK * world, layers=LAYERS, shard=(rank, world))
+    epb = EpBench(stack, dist, rank, world, args)
     sampler = ClockSampler(local_rank) if rank == 0 else None
-    secs = timed(args.steps, args.warmup, step)
+    d = epb.run_decode()
     clocks = sampler.stop() if sampler else None
-
-    # end to end: the step's inputs come from pinned host memory and its result goes back to the host
-    xh = torch.from_numpy(stack.ctx.acts_to_wire(x).view(np.int16)).pin_memory()
-    res = torch.empty((batch, HIDDEN), dtype=torch.float32).pin_memory()
-
-    def step_e2e(i):
-        xd.view(torch.int16).copy_(xh, non_blocking=True)
-        step(i)
-        res.copy_(out[LAYERS - 1], non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-    e2e_secs = timed(args.steps, max(3, args.warmup), step_e2e)
-
-    def step_bytes(s):
-        total = 0
-        for l in range(LAYERS):
-            touched = set()
-            for r in range(world):
-                touched |= set(all_sets[r][s][l][0].ravel().tolist())
-            total += len(touched) * EXPERT_BYTES + world * SHARED_BYTES     # every rank reads its own copy of the shared expert
-        return total
-    timed_bytes = sum(step_bytes((args.warmup + i) % n_sets) for i in range(args.steps))
-    e2e_bytes = sum(step_bytes((max(3, args.warmup) + i) % n_sets) for i in range(args.steps))
+    p = epb.run_prefill(max(3, args.steps // 8), 2)
+    parity = epb.parity()
+    exch = epb.time_exchanges()
+    status = int(stack.ctx.device_status())
     if rank == 0:
         peaks, peak_kind = measured_peaks()
-        value = timed_bytes / secs / 1e9
+        secs = d["secs"]
+        value = d["bytes"] / secs / 1e9
+        per = NEXP // world
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "C5: expert-parallel batched decode, 40 layers, 8 tokens per GPU per step, top-8 of 256, Zipf(1.1)",
-                       "batch": batch * world, "layers": LAYERS, "hidden": HIDDEN, "moe_inter": INTER, "scale_dtype": "fp16",
-                       "act_dtype": "bf16", "experts_per_gpu": per, "parallelism": f"ep{world}",
+            "ms_per_step": secs / args.steps * 1e3, "step_ms": spread(d["per_step"]), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "C5: expert-parallel batched decode, 40 layers, 8 tokens per GPU per step, top-8 of 256, Zipf(1.1) (one popularity per layer for all ranks)",
+                       "batch": epb.BATCH * world, "layers": LAYERS, "layers_per_step": LAYERS, "hidden": HIDDEN, "moe_inter": INTER,
+                       "scale_dtype": "fp16", "act_dtype": "bf16", "pool_gb": LAYERS * NEXP * EXPERT_BYTES / 1e9, "experts_per_gpu": per,
+                       "parallelism": f"ep{world}",
                        "exchange": "fixed capacity: 2 all-to-alls per layer over NCCL (records, partial rows), no host synchronisation",
-                       "launch": graph_note,
+                       "launch": d["note"],
                        "l2": "inputs larger than L2: the pool shards exceed it; 4 routing sets rotate"},
             "clocks": clocks,
-            "e2e": {"value": e2e_bytes / e2e_secs / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(xh.numel() * 2 * world),
-                    "d2h_bytes_per_step": int(res.numel() * 4 * world)},
-            "gpu_launches": int(stack.ctx.launch_count()),
-            "tokens_per_s": batch * world * args.steps / secs,
-            "us_per_layer": secs / args.steps / LAYERS * 1e6,
+            "e2e": {"value": d["e2e_bytes"] / d["e2e_secs"] / 1e9, "unit": "GB/s", "h2d_bytes_per_step": d["h2d"], "d2h_bytes_per_step": d["d2h"]},
+            "gpu_launches": d["launches_per_step"] * args.steps * world,
+            "tokens_per_s": d["tokens_per_s"],
+            "us_per_layer": d["us_per_layer"],
+            "decode": {"tokens_per_step": epb.BATCH * world, "tokens_per_gpu_per_step": epb.BATCH, "tokens_per_s": d["tokens_per_s"],
+                       "us_per_layer": d["us_per_layer"], "nvlink_gbs_per_gpu_per_direction": d["nvlink_gbs_per_gpu_per_direction"],
+                       "link_bytes_per_gpu_per_step": d["link_bytes_per_gpu_per_step"], "exchange_alone": exch},
+            "prefill": dict(p, metric="moe3_prefill_tokens_per_s", value=p["tokens_per_s"], unit="tokens/s (40 MoE layers per token)"),
+            "ep_parity": parity,
+            "device_status": status,
             "hbm_frac_of_" + peak_kind: value / world / peaks["hbm_gbs"],
         }
         print(json.dumps(line), flush=True)
-    # The graphs hold the recorded all-to-alls: they go before the communicator does, and the process then
-    # leaves without tearing NCCL down (a communicator destroyed after graphs had captured its collectives did
-    # not return on this stack).
-    graphs = None
+    # The graphs hold the recorded all-to-alls.  NCCL keeps a communicator alive while a graph that captured its
+    # collectives exists (destroying it waits for those graphs to be released), so the graphs go first and no name
+    # may still hold one; the process then leaves without tearing the process group down.
+    epb.release()
     torch.cuda.synchronize()
     dist.barrier()
     sys.stdout.flush()
@@ -537,8 +858,10 @@ def run_ep(args, rank, local_rank, world):
 def aux_rooflines(stack, peaks, peak_kind, iters=8):
     """The other matvec rows of the path, each timed alone with CUDA events and the L2 flushed (a 256 MB
     write) before every timed launch: 4-bit g64 projections and GGUF Q4_K / Q6_K tensors through
-    finch_encode_batch_matvec at 1 / 8 (/ 90) positions, and the 4-bit projections at 64 / 512 positions
-    through the tensor-core GEMM.  bytes = packed weights + scales (+ activations); flops = 2 T out in."""
+    finch_encode_batch_matvec at 1 / 8 (/ 90) positions, the 4-bit projections at 64 / 512 positions
+    through the tensor-core GEMM, and the 248,320-row output projection in 8 and 4 bits (larger than L2 by
+    itself: no flush, which would leave dirty lines to be written back under the timed launch).
+    bytes = packed weights + scales (+ activations); flops = 2 T out in."""
     import ctypes as C
 
     import torch
@@ -548,13 +871,14 @@ def aux_rooflines(stack, peaks, peak_kind, iters=8):
     st = stack.stream
     rows = []
 
-    def timed(fn):
+    def timed(fn, do_flush=True):
         fn()
         torch.cuda.synchronize()
         tot = 0.0
         for _ in range(iters):
             with torch.cuda.stream(st):
-                flush.fill_(1)
+                if do_flush:
+                    flush.fill_(1)
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(st)
                 fn()
@@ -592,6 +916,20 @@ def aux_rooflines(stack, peaks, peak_kind, iters=8):
             ceil = min(peaks["bf16_tflops"], fl / b * peaks["hbm_gbs"] / 1e3)
             rows.append({"op": "dense_gemm_4bit_g64_tcgen05", "shape": list(shape), "T": T, "us": secs * 1e6, "tflops": fl / secs / 1e12,
                          "gbs": b / secs / 1e9, "ceiling_tflops": ceil, "frac_" + peak_kind: fl / secs / 1e12 / ceil})
+    # the output projection (lm_head tier): 248,320 rows of 2048, device-generated bytes
+    rows_out, in_dim = 248320, 2048
+    for bits in (8, 4):
+        Wd = torch.randint(0, 256, (rows_out, in_dim * bits // 8), dtype=torch.uint8, device="cuda")
+        Sd = (torch.rand((rows_out, in_dim // 64), device="cuda") * 0.01 + 1e-4).to(torch.float16)
+        Bd = (Sd.float() * -(128.0 if bits == 8 else 8.0)).to(torch.float16)
+        w = L.WDesc(Wd.data_ptr(), Sd.data_ptr(), Bd.data_ptr(), rows_out, in_dim, 64, bits, L.FP16)
+        x = torch.from_numpy(synth.activations(rng, 1, in_dim)).cuda().to(torch.bfloat16)
+        out = torch.empty((1, rows_out), dtype=torch.float32, device="cuda")
+        secs = timed(lambda: ctx.fast_batch_matvec(x, L.BF16, [w], [out], M=1, stream=st.cuda_stream), do_flush=False)
+        b = Wd.numel() + Sd.numel() * 2 + Bd.numel() * 2 + in_dim * 2 + rows_out * 4
+        rows.append({"op": f"lm_head_matvec_{bits}bit_g64", "shape": [rows_out, in_dim], "T": 1, "us": secs * 1e6, "gbs": b / secs / 1e9,
+                     "frac_hbm_" + peak_kind: b / secs / 1e9 / peaks["hbm_gbs"]})
+        del Wd, Sd, Bd
     return rows
 
 
@@ -620,11 +958,11 @@ def kernel_roofline(stack, dev, rsets, xd, score, out, batch, args, peaks, peak_
         return None
     per_launch_bytes = gate_bytes / n.value
     achieved = per_launch_bytes / (ms_a.value / n.value * 1e-3) / 1e9
+    ratio, src = profiled_traffic_ratio()
     return {"bound": "hbm", "kernel": "moe_gateup_kernel", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": achieved / peaks["hbm_gbs"], "peak_kind": peak_kind,
-            # dram__bytes_read + write of one launch with 38 distinct experts (36,044,800 algorithmic bytes):
-            # 38,070,528 B (profiles/moe_decode_batch8_gateup_down_full.md), scaled to this run's average launch
-            "traffic": per_launch_bytes * (38070528 / 36044800), "traffic_source": "ncu, 38-expert launch, scaled by bytes",
+            # DRAM bytes of one profiled launch over its algorithmic bytes, applied to this run's average launch
+            "traffic": per_launch_bytes * ratio if ratio else None, "traffic_source": src,
             "bytes_per_launch": per_launch_bytes, "us_per_launch": ms_a.value / n.value * 1e3,
             "down_combine_us_per_launch": ms_b.value / n.value * 1e3, "launches_timed": n.value}
 
@@ -633,19 +971,26 @@ def main():
     global LAYERS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS, help="fewer layers = a small case for profiler captures")
     ap.add_argument("--no-graph", action="store_true", help="launch from the host every step instead of replaying CUDA graphs")
-    ap.add_argument("--only", default="", choices=["", "prefill"], help="prefill: just the 512-token chunk on --layers layers (profiler captures)")
+    ap.add_argument("--only", default="", choices=["", "prefill", "decode"], help="just the 512-token chunk, or just the batch-8 decode steps, on --layers layers (profiler captures)")
     args = ap.parse_args()
     LAYERS = args.layers
     if args.only == "prefill":
-        stack = Stack(0, max_tokens=512, layers=LAYERS)
-        ps, uniq = stack.time_prefill(512, max(1, args.steps), max(1, args.warmup))
-        print(json.dumps({"only": "prefill", "chunk": 512, "layers": LAYERS, "ms_per_chunk": ps * 1e3, "tokens_per_s": 512 / ps,
+        stack = Stack(0, max_tokens=PREFILL_CHUNK, layers=LAYERS)
+        ps, uniq = stack.time_prefill(PREFILL_CHUNK, max(1, args.steps), max(1, args.warmup))
+        print(json.dumps({"only": "prefill", "chunk": PREFILL_CHUNK, "layers": LAYERS, "ms_per_chunk": ps * 1e3, "tokens_per_s": PREFILL_CHUNK / ps,
                           "distinct_experts": uniq, "status": stack.ctx.device_status()}))
+    elif args.only == "decode":
+        stack = Stack(0, max_tokens=8, layers=LAYERS)
+        rsets = routing_sets(8, 4)
+        dev, xd, score, out, _ = stack.device_inputs(rsets, 8)
+        secs, per_step = stack.time_steps(dev, xd, score, out, 8, args.steps, args.warmup, use_graph=not args.no_graph)
+        print(json.dumps({"only": "decode", "layers": LAYERS, "ms_per_step": secs / args.steps * 1e3, "step_ms": spread(per_step),
+                          "status": stack.ctx.device_status()}))
     elif args.impl == "reference":
         run_reference(args)
     else:

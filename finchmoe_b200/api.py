@@ -197,6 +197,12 @@ class Context:
     def set_prefill_mode(self, mode: int):
         """0: by chunk length, 1: sub-batches through the decode kernels, 2: tensor-core grouped GEMM."""
         self.check(self.lib.finch_set_prefill_mode(self.h, mode))
+        self.prefill_mode = mode
+
+    def set_prefill_chunk(self, tokens: int):
+        """Tokens per pass of the tensor-core prefill path (0 = the default 512; at most max_tokens)."""
+        self.check(self.lib.finch_set_prefill_chunk(self.h, tokens))
+        self.prefill_chunk = tokens
 
     def make_shared(self, gate: L.WDesc, up: L.WDesc, down: L.WDesc, gate_score=None) -> L.Shared:
         return L.Shared(gate, up, down, _ptr(gate_score))

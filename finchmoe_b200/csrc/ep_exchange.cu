@@ -20,9 +20,10 @@ namespace {
 __host__ __device__ inline int rec_bytes_of(int hidden, int elt, int K) { return (hidden * elt + 9 * K + 15) & ~15; }
 
 // One CTA of 1024 threads.  counts[d], offs[d] (exclusive prefix, offs[G] = total), send_tok[offs[d] + p] =
-// p-th token (ascending) that has a usable expert on rank d, slot_of[t * G + d] = p or -1.
-__global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t *ids, const uint8_t *valid, int T, int K, int n_experts, int G, int *counts,
-                                                       int *offs, int *send_tok, int *slot_of) {
+// p-th token (ascending) that has a usable expert on rank d, slot_of[t * G + d] = p or -1.  Nothing goes to rank
+// `skip` (the home rank, when it computes its own experts' share of its own tokens in place).
+__global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t *ids, const uint8_t *valid, int T, int K, int n_experts, int G, int skip,
+                                                       int *counts, int *offs, int *send_tok, int *slot_of) {
     __shared__ int warp_sum[32];
     __shared__ int run;        // tokens placed so far in the current destination's list
     __shared__ int base;       // offs[d]
@@ -36,7 +37,7 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t *ids, const
         for (int t0 = 0; t0 < T; t0 += 1024) {
             const int t = t0 + tid;
             bool go = false;
-            if (t < T)
+            if (t < T && d != skip)
                 for (int k = 0; k < K; k++) {
                     const int e = ids[t * K + k];
                     if ((!valid || valid[t * K + k]) && e >= 0 && e < n_experts && e / per == d) go = true;
@@ -122,12 +123,12 @@ extern "C" int finch_ep_record_bytes(const finch_ctx *ctx) {
 }
 
 extern "C" int finch_encode_ep_plan(finch_ctx *ctx, finch_stream stream, const int32_t *expert_ids, const uint8_t *valid, int T, int world,
-                                    int *counts, int *offs, int *send_tok, int *slot_of) {
+                                    int skip_rank, int *counts, int *offs, int *send_tok, int *slot_of) {
     if (!ctx || !expert_ids || !counts || !offs || !send_tok || !slot_of || T < 1 || world < 1) return FINCH_E_ARG;
     if (ctx->cfg.n_experts % world) return finch_fail(ctx, FINCH_E_ARG, "%d experts do not split over %d ranks", ctx->cfg.n_experts, world);
     cudaSetDevice(ctx->cfg.device);
-    ep_plan_kernel<<<1, 1024, 0, finch_pick_stream(ctx, stream)>>>(expert_ids, valid, T, ctx->cfg.top_k, ctx->cfg.n_experts, world, counts, offs, send_tok,
-                                                                    slot_of);
+    ep_plan_kernel<<<1, 1024, 0, finch_pick_stream(ctx, stream)>>>(expert_ids, valid, T, ctx->cfg.top_k, ctx->cfg.n_experts, world, skip_rank, counts, offs,
+                                                                    send_tok, slot_of);
     FINCH_CUDA_OK(ctx, cudaGetLastError());
     ctx->launches++;
     return FINCH_OK;

@@ -44,6 +44,7 @@ struct finch_ctx {
     float *logits = nullptr;        // [max_tokens][n_experts] router logits (finch_encode_router, allocated on first use)
     void *gguf_ws = nullptr;        // scratch of finch_encode_moe_gguf (allocated on first use)
     size_t gguf_ws_bytes = 0;
+    int prefill_chunk = 0;          // finch_set_prefill_chunk: tokens per tensor-core pass, 0 = 512
     int prefill_mode = 0;           // finch_set_prefill_mode: 0 by chunk length, 1 sub-batches through decode, 2 tensor cores
     uint64_t launches = 0;
     // optional per-kernel timing of the MoE decode call (finch_profile_enable)

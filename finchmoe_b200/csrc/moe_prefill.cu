@@ -23,7 +23,7 @@
 
 namespace {
 
-constexpr int CHUNK = 512;   // tokens per tensor-core pass: 4096 pairs
+constexpr int CHUNK = 512;   // default tokens per tensor-core pass: 4096 pairs (finch_set_prefill_chunk changes it)
 constexpr int TC_MIN_TOKENS = 128;   // shorter chunks are faster through the decode kernels (measured)
 
 // One CTA: pairs -> expert histogram -> ranges -> order.  Pairs that are masked, out of range or not
@@ -31,8 +31,12 @@ constexpr int TC_MIN_TOKENS = 128;   // shorter chunks are faster through the de
 // It also lists the (expert, first token) tiles of the two grouped GEMMs, tn_a / tn_b tokens per tile, so
 // that their grids hold no CTA without work: items_a / items_b = [expert, first pair of the tile inside
 // the expert's range], n_items[0 / 1] = how many.
+// cap_a / cap_b: the most tiles the two GEMM grids were sized for (pairs / tile + experts resident when the call
+// was encoded); more than that -- experts added to the pool between encode and execution -- is reported
+// through status and the lists are cut there.
 __global__ void __launch_bounds__(1024) pf_sort_kernel(const int32_t *ids, const uint8_t *valid, const int32_t *slot_row, int n_experts, int P,
-                                                       int *seg, int *order, int tn_a, int tn_b, int2 *items_a, int2 *items_b, int *n_items) {
+                                                       int *seg, int *order, int tn_a, int tn_b, int2 *items_a, int2 *items_b, int *n_items,
+                                                       int cap_a, int cap_b, int *status) {
     extern __shared__ int sm[];   // [n_experts] counts, cursors, first item of the expert in each list
     int *cnt = sm, *cur = sm + n_experts, *ia = cur + n_experts, *ib = ia + n_experts;
     const int tid = threadIdx.x;
@@ -74,7 +78,11 @@ __global__ void __launch_bounds__(1024) pf_sort_kernel(const int32_t *ids, const
                 wsum[q][lane] = acc - w;   // exclusive prefix of the warp totals
                 if (lane == 31) {
                     if (q == 0) seg[n_experts] = acc;
-                    else n_items[q - 1] = acc;
+                    else {
+                        const int cap = q == 1 ? cap_a : cap_b;
+                        if (acc > cap) atomicCAS(status, 0, FINCH_E_UNSUPPORTED);
+                        n_items[q - 1] = acc < cap ? acc : cap;
+                    }
                 }
             }
         }
@@ -88,8 +96,10 @@ __global__ void __launch_bounds__(1024) pf_sort_kernel(const int32_t *ids, const
     }
     __syncthreads();
     for (int e = tid; e < n_experts; e += blockDim.x) {
-        for (int i = 0, t0 = 0; t0 < cnt[e]; i++, t0 += tn_a) items_a[ia[e] + i] = make_int2(e, t0);
-        for (int i = 0, t0 = 0; t0 < cnt[e]; i++, t0 += tn_b) items_b[ib[e] + i] = make_int2(e, t0);
+        for (int i = 0, t0 = 0; t0 < cnt[e]; i++, t0 += tn_a)
+            if (ia[e] + i < cap_a) items_a[ia[e] + i] = make_int2(e, t0);
+        for (int i = 0, t0 = 0; t0 < cnt[e]; i++, t0 += tn_b)
+            if (ib[e] + i < cap_b) items_b[ib[e] + i] = make_int2(e, t0);
     }
     // the order of the pairs inside an expert's range is arbitrary: every pair's output row is computed
     // from its own activation row only, so the results do not depend on it
@@ -256,8 +266,13 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
     // token tiles: as many tokens as still let two CTAs share an SM (an expert's tile is dequantised once per token tile)
     const bool x_lo_needed = c.act_dtype != FINCH_BF16;   // fp32 activations travel as two bf16 planes
     const int tn_a = tn_max_for(T < 64 ? T : (x_lo_needed ? 32 : 64)), tn_b = 32;
+    // the grids of the two grouped GEMMs hold one CTA row per possible (expert, token tile): at most one ragged tile
+    // per expert that is resident now, plus the full tiles
+    int resident = 0;
+    for (int e = 0; e < pool->n_experts; e++) resident += pool->slot_of[(size_t)layer * pool->n_experts + e] >= 0;
+    const int cap_a = P / tn_a + resident + 1, cap_b = P / tn_b + resident + 1;
     pf_sort_kernel<<<1, 1024, 4 * c.n_experts * sizeof(int), st>>>(ids, valid, slot_row, c.n_experts, P, seg, order, tn_a, tn_b, items_a, items_b,
-                                                                   n_items);
+                                                                   n_items, cap_a, cap_b, ctx->dev_status);
     FINCH_CUDA_OK(ctx, cudaGetLastError());
     const uint16_t *x = (const uint16_t *)h_post, *x_lo = nullptr;
     if (x_lo_needed) {
@@ -290,7 +305,7 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
     a.items = items_a;
     a.n_items = n_items;
     // grid.y bounds the number of (expert, token tile) items; CTAs past the actual count return at once
-    if ((rc = launch_gemm(ctx, st, a, dim3(I / 64, P / tn_a + c.n_experts, 1)))) return rc;   // 64 gate + 64 up rows per tile
+    if ((rc = launch_gemm(ctx, st, a, dim3(I / 64, cap_a, 1)))) return rc;   // 64 gate + 64 up rows per tile
     a.mode = dqgemm::EXPERT_DOWN;
     a.K = I;
     a.X = act;
@@ -299,7 +314,7 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
     a.tn_max = tn_b;   // two activation planes per stage
     a.items = items_b;
     a.n_items = n_items + 1;
-    if ((rc = launch_gemm(ctx, st, a, dim3(H / dqgemm::GM, P / tn_b + c.n_experts, 1)))) return rc;
+    if ((rc = launch_gemm(ctx, st, a, dim3(H / dqgemm::GM, cap_b, 1)))) return rc;
 
     if (shared) {
         if ((rc = dense4_gemm(ctx, st, &shared->gate, x, x_lo, sg, T))) return rc;
@@ -322,6 +337,13 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
 extern "C" int finch_set_prefill_mode(finch_ctx *ctx, int mode) {
     if (!ctx || mode < 0 || mode > 2) return FINCH_E_ARG;
     ctx->prefill_mode = mode;
+    return FINCH_OK;
+}
+
+extern "C" int finch_set_prefill_chunk(finch_ctx *ctx, int tokens) {
+    if (!ctx || tokens < 0) return FINCH_E_ARG;
+    if (tokens > ctx->cfg.max_tokens) return finch_fail(ctx, FINCH_E_ARG, "chunk of %d tokens exceeds max_tokens=%d", tokens, ctx->cfg.max_tokens);
+    ctx->prefill_chunk = tokens;
     return FINCH_OK;
 }
 
@@ -349,8 +371,9 @@ extern "C" int finch_encode_moe_prefill(finch_ctx *ctx, finch_stream stream, fin
         }
         cudaSetDevice(c.device);
         cudaStream_t st = finch_pick_stream(ctx, stream);
-        for (int t0 = 0; t0 < T; t0 += CHUNK) {
-            const int n = T - t0 < CHUNK ? T - t0 : CHUNK;
+        const int chunk = ctx->prefill_chunk > 0 ? ctx->prefill_chunk : CHUNK;
+        for (int t0 = 0; t0 < T; t0 += chunk) {
+            const int n = T - t0 < chunk ? T - t0 : chunk;
             finch_shared sh;
             if (shared) {
                 sh = *shared;

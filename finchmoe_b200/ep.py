@@ -35,8 +35,8 @@ def owner_of(expert: int, n_experts: int, world: int) -> int:
     return expert // (n_experts // world)
 
 
-def plan_numpy(ids: np.ndarray, valid, n_experts: int, world: int):
-    """Host mirror of finch_encode_ep_plan: (counts[G], offs[G+1], send_tok, slot_of[T,G])."""
+def plan_numpy(ids: np.ndarray, valid, n_experts: int, world: int, skip: int = -1):
+    """Host mirror of finch_encode_ep_plan: (counts[G], offs[G+1], send_tok, slot_of[T,G]).  Nothing goes to rank `skip`."""
     T, K = ids.shape
     per = n_experts // world
     ok = (ids >= 0) & (ids < n_experts)
@@ -47,7 +47,7 @@ def plan_numpy(ids: np.ndarray, valid, n_experts: int, world: int):
     slot_of = np.full((T, world), -1, np.int32)
     lists = []
     for d in range(world):
-        toks = np.nonzero((dest == d).any(axis=1))[0].astype(np.int32)
+        toks = np.nonzero((dest == d).any(axis=1))[0].astype(np.int32) if d != skip else np.zeros(0, np.int32)
         counts[d] = toks.size
         slot_of[toks, d] = np.arange(toks.size, dtype=np.int32)
         lists.append(toks)
@@ -66,7 +66,11 @@ def ep_layer(backend, dist, group, layer: int, x, ids, weights, valid, shared, h
 def _ep_layer(backend, dist, group, layer, x, ids, weights, valid, shared, h_mid, out):
     import torch
     world = dist.get_world_size(group) if dist is not None else 1
-    h = backend.plan(ids, valid, world)                       # -> object with .counts (int32 [G] tensor)
+    rank = dist.get_rank(group) if dist is not None else 0
+    # A backend that can run the home rank's own tokens straight from their buffers sends nothing to itself:
+    # one pass over its tokens gives h_mid + shared expert + the experts this rank holds, while the records travel.
+    direct = getattr(backend, "home_direct", False)
+    h = backend.plan(ids, valid, world, rank) if direct else backend.plan(ids, valid, world)   # .counts: int32 [G] tensor
     recv_counts = torch.empty_like(h.counts)
     if world > 1:
         dist.all_to_all_single(recv_counts, h.counts, group=group)
@@ -74,13 +78,20 @@ def _ep_layer(backend, dist, group, layer, x, ids, weights, valid, shared, h_mid
         recv_counts.copy_(h.counts)
     c_send = h.counts.cpu().tolist()                           # host sync: split sizes must be host integers
     c_recv = recv_counts.cpu().tolist()
+    if getattr(backend, "stats", None) is not None:            # rows that left for / arrived from every rank, this layer
+        backend.stats.append((c_send, c_recv))
     rec = backend.record_bytes()
     send_buf = backend.pack(h, x, ids, weights, valid, sum(c_send))            # uint8 [sum(c_send) * rec]
     recv_buf = backend.empty_bytes(sum(c_recv) * rec)
+    work = None
     if world > 1:
-        dist.all_to_all_single(recv_buf, send_buf, [c * rec for c in c_recv], [c * rec for c in c_send], group=group)
+        work = dist.all_to_all_single(recv_buf, send_buf, [c * rec for c in c_recv], [c * rec for c in c_send], group=group, async_op=direct)
     else:
         recv_buf.copy_(send_buf)
+    if direct:
+        backend.home(layer, x, ids, weights, valid, shared, h_mid, out)
+        if work is not None:
+            work.wait()
     part = backend.local_moe(layer, recv_buf, sum(c_recv))                      # fp32 [sum(c_recv), H]
     H = backend.hidden
     back = backend.empty_f32(sum(c_send) * H)
@@ -88,7 +99,8 @@ def _ep_layer(backend, dist, group, layer, x, ids, weights, valid, shared, h_mid
         dist.all_to_all_single(back, part.reshape(-1), [c * H for c in c_send], [c * H for c in c_recv], group=group)
     else:
         back.copy_(part.reshape(-1))
-    backend.base(layer, x, ids, weights, shared, h_mid, out)                    # h_mid + shared expert, no routed expert
+    if not direct:
+        backend.base(layer, x, ids, weights, shared, h_mid, out)                # h_mid + shared expert, no routed expert
     backend.combine(h, out, back)
     return out
 
@@ -128,7 +140,10 @@ def _ep_layer_static(backend, dist, group, layer, x, ids, weights, valid, shared
     # A backend that can run the home rank's own tokens straight from their buffers does so while the records
     # are in flight: one pass gives h_mid + shared expert + the experts this rank holds, and the rows the rank
     # would have sent to itself are neither processed a second time nor added again.
-    direct = world > 1 and getattr(backend, "home_direct", False)
+    direct = getattr(backend, "home_direct", False)
+    if direct and world == 1:      # every expert is here: the rank's ordinary pass over its own tokens is the layer
+        backend.home(layer, x, ids, weights, valid, shared, h_mid, out)
+        return out
     h = backend.static_plan(T, world, rank if direct else -1)
     rec, H, n = backend.record_bytes(), backend.hidden, T * world
     send_buf = backend.pack(h, x, ids, weights, valid, n)
@@ -175,6 +190,12 @@ class GpuBackend:
         self.rout = torch.empty((max_rows, self.hidden), dtype=torch.float32, device=dev)
         self.zero_valid = None
         self._static = {}
+        self.stats = None            # a list makes ep_layer append (rows sent per rank, rows received per rank) per layer
+        # Received rows select few local experts each.  More than one decode-sized batch of them goes through the
+        # tensor-core path in passes of `tc_chunk` rows (one sort and one pair of grouped GEMMs per pass) instead of
+        # one decode pass per 8 rows.
+        self.tc_rows_min = 9
+        self.tc_chunk = min(ctx.cfg.max_tokens, max_rows, 4096)
 
         self.stream = torch.cuda.Stream(device=dev)   # kernels, copies and collectives of a layer are ordered on it
 
@@ -205,7 +226,7 @@ class GpuBackend:
     def empty_f32(self, n):
         return self.torch.empty(n, dtype=self.torch.float32, device=self.dev)
 
-    def plan(self, ids, valid, world):
+    def plan(self, ids, valid, world, skip=-1):
         torch = self.torch
         T = ids.shape[0]
         p = _Plan()
@@ -215,7 +236,7 @@ class GpuBackend:
         p.send_tok = torch.empty(T * world, dtype=torch.int32, device=self.dev)
         p.slot_of = torch.empty((T, world), dtype=torch.int32, device=self.dev)
         self.ctx.check(self.lib.finch_encode_ep_plan(self.ctx.h, self._stream(), ids.data_ptr(), valid.data_ptr() if valid is not None else None,
-                                                     T, world, p.counts.data_ptr(), p.offs.data_ptr(), p.send_tok.data_ptr(),
+                                                     T, world, skip, p.counts.data_ptr(), p.offs.data_ptr(), p.send_tok.data_ptr(),
                                                      p.slot_of.data_ptr()))
         return p
 
@@ -272,10 +293,23 @@ class GpuBackend:
                                                        self.rw.data_ptr(), self.rv.data_ptr()))
         step = self.ctx.cfg.max_tokens
         blocks = [(0, n)] if skip is None else [(0, skip[0]), (skip[0] + skip[1], n)]
-        for r0, m in ((r, min(step, hi - r)) for lo, hi in blocks for r in range(lo, hi, step)):
-            self.ctx.check(self.lib.finch_encode_moe_prefill(
-                self.ctx.h, st, self.pool.h, layer, self.rx.data_ptr() + r0 * self.hidden * self.elt, self.rids[r0:].data_ptr(),
-                self.rw[r0:].data_ptr(), self.rv[r0:].data_ptr(), None, None, self.rout[r0:].data_ptr(), m))
+        rows = sum(hi - lo for lo, hi in blocks)
+        tc = rows >= self.tc_rows_min and step >= 16
+        if tc:
+            self.ctx.check(self.lib.finch_set_prefill_mode(self.ctx.h, 2))
+            self.ctx.check(self.lib.finch_set_prefill_chunk(self.ctx.h, min(self.tc_chunk, step)))
+            if skip is not None:     # one pass over all rows; the block that is left out selects nothing
+                self.rv[skip[0]:skip[0] + skip[1]].zero_()
+                blocks = [(0, n)]
+        try:
+            for r0, m in ((r, min(step, hi - r)) for lo, hi in blocks for r in range(lo, hi, step)):
+                self.ctx.check(self.lib.finch_encode_moe_prefill(
+                    self.ctx.h, st, self.pool.h, layer, self.rx.data_ptr() + r0 * self.hidden * self.elt, self.rids[r0:].data_ptr(),
+                    self.rw[r0:].data_ptr(), self.rv[r0:].data_ptr(), None, None, self.rout[r0:].data_ptr(), m))
+        finally:
+            if tc:
+                self.ctx.check(self.lib.finch_set_prefill_mode(self.ctx.h, getattr(self.ctx, "prefill_mode", 0)))
+                self.ctx.check(self.lib.finch_set_prefill_chunk(self.ctx.h, getattr(self.ctx, "prefill_chunk", 0)))
         return self.rout[:n]
 
     def base(self, layer, x, ids, weights, shared, h_mid, out):

@@ -74,9 +74,10 @@ _PROTOS = {
     "finch_encode_moe_decode": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, C.POINTER(Shared), _vp, _vp, _i]),
     "finch_encode_moe_prefill": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, C.POINTER(Shared), _vp, _vp, _i]),
     "finch_set_prefill_mode": (_i, [_vp, _i]),
+    "finch_set_prefill_chunk": (_i, [_vp, _i]),
     "finch_encode_dense_gemm": (_i, [_vp, _vp, C.POINTER(WDesc), _vp, _vp, _i]),
     "finch_ep_record_bytes": (_i, [_vp]),
-    "finch_encode_ep_plan": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp]),
+    "finch_encode_ep_plan": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "finch_encode_ep_pack": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp, _vp]),
     "finch_encode_ep_unpack": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp]),
     "finch_encode_ep_combine": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i]),

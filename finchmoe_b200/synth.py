@@ -163,5 +163,25 @@ def zipf_routing(rng, T, n_experts=256, K=8, s=1.1):
     return ids, w
 
 
+def zipf_popularity(rng, n_experts=256):
+    """A seeded order of popularity: expert perm[i] has Zipf rank i + 1."""
+    return rng.permutation(n_experts)
+
+
+def zipf_routing_shared(rng, T, perm, K=8, s=1.1):
+    """zipf_routing for tokens that share one order of popularity `perm` (a layer's, whichever rank owns the
+    token).  K distinct experts per token, drawn without replacement from the Zipf(s) popularity: the K largest
+    of log p + Gumbel noise, which is the same distribution as drawing them one after another."""
+    n = perm.shape[0]
+    logp = -s * np.log(np.arange(1, n + 1, dtype=np.float64))
+    keys = logp[None, :] + rng.gumbel(size=(T, n))
+    top = np.argsort(-keys, axis=1)[:, :K]
+    ids = perm[top].astype(np.int32)
+    lg = rng.normal(0.0, 1.0, size=(T, K))
+    w = np.exp(lg - lg.max(axis=1, keepdims=True))
+    w = (w / w.sum(axis=1, keepdims=True)).astype(np.float32)
+    return ids, w
+
+
 def router_logits(rng, T, n_experts=256) -> np.ndarray:
     return rng.normal(0.0, 1.0, size=(T, n_experts)).astype(np.float32)

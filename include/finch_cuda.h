@@ -271,6 +271,14 @@ FINCH_API int finch_profile_read(finch_ctx *ctx, float *ms_gateup, float *ms_dow
  * the tensor-core path.  The reference has one path only (per-position CMD3). */
 FINCH_API int finch_set_prefill_mode(finch_ctx *ctx, int mode);
 
+/* Tokens per pass of the tensor-core path of finch_encode_moe_prefill (the
+ * reference's chunk length, PREFILL_CHUNK in finchmoe/infer.m:12892-12902, is the
+ * caller's T; this bounds how many of them share one sort and one pair of
+ * grouped GEMMs).  0 = the default 512; at most max_tokens.  An expert-parallel
+ * rank, whose rows each select few local experts, raises it so that a pass
+ * still carries a few thousand (token, expert) pairs. */
+FINCH_API int finch_set_prefill_chunk(finch_ctx *ctx, int tokens);
+
 /* gpu_encode_prefill_matvec (finchmoe/infer.m:3672) for M >= 16 positions and a
  * 4-bit g64 tensor: out fp32 [M][out_dim] = x * dequant(w)^T on the tensor
  * cores; x is bf16 [M][in_dim] on the device, in_dim and out_dim multiples of
@@ -306,9 +314,11 @@ FINCH_API int finch_encode_moe_gguf(finch_ctx *ctx, finch_stream stream, const f
 FINCH_API int finch_ep_record_bytes(const finch_ctx *ctx);
 /* counts[world], offs[world + 1] (exclusive prefix), send_tok[<= T * world] (tokens per
  * destination, ascending), slot_of[T][world] (position of token t in destination d's list, or -1).
- * A token goes to a rank once, however many of its experts live there. */
+ * A token goes to a rank once, however many of its experts live there.  Nothing goes to skip_rank
+ * (its counts entry is 0, its slot_of column -1): the calling rank's own index when it runs its own
+ * experts on its own tokens in place (finch_encode_moe_prefill on its pool), else -1. */
 FINCH_API int finch_encode_ep_plan(finch_ctx *ctx, finch_stream stream, const int32_t *expert_ids, const uint8_t *valid,
-                                   int T, int world, int *counts, int *offs, int *send_tok, int *slot_of);
+                                   int T, int world, int skip_rank, int *counts, int *offs, int *send_tok, int *slot_of);
 FINCH_API int finch_encode_ep_pack(finch_ctx *ctx, finch_stream stream, const void *h_post, const int32_t *expert_ids,
                                    const float *weights, const uint8_t *valid, int T, int world, const int *offs,
                                    const int *send_tok, void *records);

@@ -26,6 +26,19 @@ def test_plan_sends_a_token_once_per_rank_and_skips_unusable_pairs():
     assert c2.tolist() == [0, 0] and s2.tolist() == [[-1, -1]]
 
 
+def test_plan_leaves_out_the_home_rank_when_asked():
+    rng = synth.rng_for(21, 3)
+    ids = rng.integers(0, 16, size=(50, 8)).astype(np.int32)
+    full = ep.plan_numpy(ids, None, 16, 4)
+    cut = ep.plan_numpy(ids, None, 16, 4, skip=2)
+    assert cut[0][2] == 0 and np.all(cut[3][:, 2] == -1)
+    for d in (0, 1, 3):                                   # the other destinations keep their lists
+        assert cut[0][d] == full[0][d]
+        assert np.array_equal(cut[3][:, d], full[3][:, d])
+        assert cut[2][cut[1][d]:cut[1][d + 1]].tolist() == full[2][full[1][d]:full[1][d + 1]].tolist()
+    assert cut[1][-1] == full[1][-1] - full[0][2]
+
+
 def test_static_plan_sends_every_token_to_every_rank():
     counts, offs, send_tok, slot_of = ep.static_plan_numpy(3, 4)
     assert counts.tolist() == [3, 3, 3, 3] and offs.tolist() == [0, 3, 6, 9, 12]

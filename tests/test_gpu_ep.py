@@ -39,6 +39,16 @@ def test_device_plan_matches_host_mirror(world):
                 assert p.offs.cpu().numpy().tolist() == offs.tolist()
                 assert p.send_tok.cpu().numpy()[:offs[-1]].tolist() == send_tok.tolist()
                 assert np.array_equal(p.slot_of.cpu().numpy(), slot_of)
+            # nothing goes to the rank that is left out (the home rank, when it works on its own tokens in place)
+            skip = world - 1
+            p = be.plan(torch.from_numpy(ids).cuda(), torch.from_numpy(valid).cuda(), world, skip)
+            torch.cuda.synchronize()
+            counts, offs, send_tok, slot_of = ep.plan_numpy(ids, valid, 16, world, skip)
+            assert counts[skip] == 0 and np.all(slot_of[:, skip] == -1)
+            assert p.counts.cpu().numpy().tolist() == counts.tolist()
+            assert p.offs.cpu().numpy().tolist() == offs.tolist()
+            assert p.send_tok.cpu().numpy()[:offs[-1]].tolist() == send_tok.tolist()
+            assert np.array_equal(p.slot_of.cpu().numpy(), slot_of)
             be.pool.destroy()
     finally:
         ctx.destroy()
@@ -46,7 +56,8 @@ def test_device_plan_matches_host_mirror(world):
 
 @pytest.mark.parametrize("T", [5, 40, 200])
 @pytest.mark.parametrize("static", [False, True])
-def test_single_rank_protocol_matches_plain_layer(T, static):
+@pytest.mark.parametrize("direct", [False, True])
+def test_single_rank_protocol_matches_plain_layer(T, static, direct):
     import torch
     from finchmoe_b200 import api
     ctx = _ctx(api, max_tokens=256)
@@ -66,10 +77,11 @@ def test_single_rank_protocol_matches_plain_layer(T, static):
         shd = ctx.make_shared(*[ctx.upload_tensor(t) for t in sh], gate_score=score_d)
         want = ctx.moe_forward_host(pool, 0, x, ids, w, valid=valid, shared=shd, gate_score=score, h_mid=h_mid)
         be = ep.GpuBackend(ctx, pool, T)
+        be.home_direct = direct      # False: the rank's own rows also go through pack / unpack / combine
         out = torch.empty((T, 256), dtype=torch.float32, device="cuda")
         (ep.ep_layer_static if static else ep.ep_layer)(be, None, None, 0, d(x), d(ids), d(w), d(valid), shd, d(h_mid), out)
         torch.cuda.synchronize()
-        assert_close(out.cpu().numpy(), want, f"single-rank protocol T={T} static={static}")
+        assert_close(out.cpu().numpy(), want, f"single-rank protocol T={T} static={static} direct={direct}")
         assert ctx.device_status() == 0
     finally:
         pool.destroy()
