@@ -448,6 +448,16 @@ class EpBench:
         self.backend = ep.GpuBackend(stack.ctx, stack.pool, max(self.BATCH, PREFILL_CHUNK) * world)
         self.score_val = 0.1
         self.graphs = None
+        # decode: the exchange goes through the ranks' own kernels over peer memory unless told (or forced) otherwise
+        self.exchange = "none (one rank)"
+        if world > 1:
+            self.exchange = "2 all-to-alls per layer over NCCL (records, partial rows)"
+            if args.exchange == "peer":
+                self.backend.peer = ep.PeerExchange.connect(stack.ctx, dist, None, self.BATCH)
+                if self.backend.peer is not None:
+                    self.exchange = "the ranks' own kernels over NVLink peer memory: stores into the peers' receive areas, one flag per slot, bounded waits"
+                else:
+                    self.exchange += " (the peer areas could not be mapped)"
 
     # ---- helpers
     def barrier(self):
@@ -667,21 +677,35 @@ class EpBench:
 
     # ---- the exchanges alone
     def time_exchanges(self, reps=5):
-        """The two all-to-alls of a decode layer with nothing between them, 40 pairs per CUDA graph: what the
-        exchange alone costs per layer."""
+        """The exchange of a decode layer with nothing between its steps, 40 layers per CUDA graph: what it costs alone.
+        Through peer memory: dispatch, receive, return, combine; over NCCL: the two all-to-alls."""
         if self.world == 1:
             return None
         torch, dist = self.torch, self.dist
         n = self.BATCH * self.world
-        a = torch.zeros(n * self.backend.record_bytes(), dtype=torch.uint8, device="cuda")
-        b = torch.empty_like(a)
-        c = torch.zeros(n * HIDDEN, dtype=torch.float32, device="cuda")
-        d = torch.empty_like(c)
+        be = self.backend
+        if be.peer is not None:
+            ids, w = self.dev[0]
+            what = "dispatch, receive, return and combine kernels of every layer, nothing else"
 
-        def pairs():
-            for _ in range(LAYERS):
-                dist.all_to_all_single(b, a)
-                dist.all_to_all_single(d, c)
+            def pairs():
+                for _ in range(LAYERS):
+                    be.peer_dispatch(self.xd, ids[0], w[0], None)
+                    be.ctx.check(be.lib.finch_encode_ep_peer_receive(be.ctx.h, be._stream(), be.peer.h, be.rx.data_ptr(), be.rids.data_ptr(),
+                                                                     be.rw.data_ptr(), be.rv.data_ptr()))
+                    be.peer_return(be.rout)
+                    be.peer_combine(self.out[0])
+        else:
+            a = torch.zeros(n * self.backend.record_bytes(), dtype=torch.uint8, device="cuda")
+            b = torch.empty_like(a)
+            c = torch.zeros(n * HIDDEN, dtype=torch.float32, device="cuda")
+            d = torch.empty_like(c)
+            what = "two all_to_all_single per layer (records out, fp32 rows back), nothing else"
+
+            def pairs():
+                for _ in range(LAYERS):
+                    dist.all_to_all_single(b, a)
+                    dist.all_to_all_single(d, c)
         run = None
         if self.graphs is not None:
             try:
@@ -704,7 +728,7 @@ class EpBench:
                 with self.backend.stream_scope():
                     pairs()
         secs, _ = self.timed(reps, 2, lambda i: run())
-        return {"us_per_layer": secs / reps / LAYERS * 1e6, "what": "two all_to_all_single per layer (records out, fp32 rows back), nothing else"}
+        return {"us_per_layer": secs / reps / LAYERS * 1e6, "what": what}
 
     def release(self):
         self.graphs = None
@@ -827,7 +851,7 @@ def run_ep(args, rank, local_rank, world, dist):
                        "batch": epb.BATCH * world, "layers": LAYERS, "layers_per_step": LAYERS, "hidden": HIDDEN, "moe_inter": INTER,
                        "scale_dtype": "fp16", "act_dtype": "bf16", "pool_gb": LAYERS * NEXP * EXPERT_BYTES / 1e9, "experts_per_gpu": per,
                        "parallelism": f"ep{world}",
-                       "exchange": "fixed capacity: 2 all-to-alls per layer over NCCL (records, partial rows), no host synchronisation",
+                       "exchange": "fixed capacity, no host synchronisation: " + epb.exchange,
                        "launch": d["note"],
                        "l2": "inputs larger than L2: the pool shards exceed it; 4 routing sets rotate"},
             "clocks": clocks,
@@ -976,6 +1000,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS, help="fewer layers = a small case for profiler captures")
     ap.add_argument("--no-graph", action="store_true", help="launch from the host every step instead of replaying CUDA graphs")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"], help="N > 1, decode: the ranks' own kernels over peer memory, or NCCL all-to-alls")
     ap.add_argument("--only", default="", choices=["", "prefill", "decode"], help="just the 512-token chunk, or just the batch-8 decode steps, on --layers layers (profiler captures)")
     args = ap.parse_args()
     LAYERS = args.layers

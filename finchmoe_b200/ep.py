@@ -67,9 +67,14 @@ def _ep_layer(backend, dist, group, layer, x, ids, weights, valid, shared, h_mid
     import torch
     world = dist.get_world_size(group) if dist is not None else 1
     rank = dist.get_rank(group) if dist is not None else 0
-    # A backend that can run the home rank's own tokens straight from their buffers sends nothing to itself:
-    # one pass over its tokens gives h_mid + shared expert + the experts this rank holds, while the records travel.
-    direct = getattr(backend, "home_direct", False)
+    # Two ways to treat the tokens' experts that live on the home rank.  planned_direct: nothing is sent to the home
+    # rank itself; one pass over its tokens gives h_mid + shared expert + the experts this rank holds while the
+    # records travel, and a second pass serves the received rows.  Otherwise (the default) the rank's own rows take
+    # the same route as everybody else's (a local copy inside the all-to-all) and ONE pass serves all rows of the
+    # rank's experts -- the grouped GEMMs dequantise an expert's tile once per pass, so one fuller pass beats
+    # two -- while h_mid + shared expert is computed during the exchange.
+    direct = getattr(backend, "planned_direct", False) or (world == 1 and getattr(backend, "home_direct", False))
+    overlap = hasattr(backend, "home")             # the GPU backend: collectives run beside its stream
     h = backend.plan(ids, valid, world, rank) if direct else backend.plan(ids, valid, world)   # .counts: int32 [G] tensor
     recv_counts = torch.empty_like(h.counts)
     if world > 1:
@@ -85,13 +90,15 @@ def _ep_layer(backend, dist, group, layer, x, ids, weights, valid, shared, h_mid
     recv_buf = backend.empty_bytes(sum(c_recv) * rec)
     work = None
     if world > 1:
-        work = dist.all_to_all_single(recv_buf, send_buf, [c * rec for c in c_recv], [c * rec for c in c_send], group=group, async_op=direct)
+        work = dist.all_to_all_single(recv_buf, send_buf, [c * rec for c in c_recv], [c * rec for c in c_send], group=group, async_op=overlap)
     else:
         recv_buf.copy_(send_buf)
     if direct:
         backend.home(layer, x, ids, weights, valid, shared, h_mid, out)
-        if work is not None:
-            work.wait()
+    elif overlap:
+        backend.base(layer, x, ids, weights, shared, h_mid, out)                # h_mid + shared expert, no routed expert
+    if work is not None:
+        work.wait()
     part = backend.local_moe(layer, recv_buf, sum(c_recv))                      # fp32 [sum(c_recv), H]
     H = backend.hidden
     back = backend.empty_f32(sum(c_send) * H)
@@ -99,8 +106,8 @@ def _ep_layer(backend, dist, group, layer, x, ids, weights, valid, shared, h_mid
         dist.all_to_all_single(back, part.reshape(-1), [c * H for c in c_send], [c * H for c in c_recv], group=group)
     else:
         back.copy_(part.reshape(-1))
-    if not direct:
-        backend.base(layer, x, ids, weights, shared, h_mid, out)                # h_mid + shared expert, no routed expert
+    if not direct and not overlap:
+        backend.base(layer, x, ids, weights, shared, h_mid, out)
     backend.combine(h, out, back)
     return out
 
@@ -144,6 +151,16 @@ def _ep_layer_static(backend, dist, group, layer, x, ids, weights, valid, shared
     if direct and world == 1:      # every expert is here: the rank's ordinary pass over its own tokens is the layer
         backend.home(layer, x, ids, weights, valid, shared, h_mid, out)
         return out
+    peer = getattr(backend, "peer", None)
+    if peer is not None and direct and peer.world == world and peer.T == T:
+        # The ranks' own kernels move the records and the partial rows through each other's memory (NVLink), each
+        # slot with its flag: no collective and no host step, the whole layer is launches on the backend's stream.
+        backend.peer_dispatch(x, ids, weights, valid)
+        backend.home(layer, x, ids, weights, valid, shared, h_mid, out)          # while the peers' records arrive
+        part = backend.peer_local_moe(layer, T * world, (rank * T, T))
+        backend.peer_return(part)
+        backend.peer_combine(out)
+        return out
     h = backend.static_plan(T, world, rank if direct else -1)
     rec, H, n = backend.record_bytes(), backend.hidden, T * world
     send_buf = backend.pack(h, x, ids, weights, valid, n)
@@ -171,6 +188,72 @@ class _Plan:
     pass
 
 
+class PeerExchange:
+    """This rank's receive area for the fixed-capacity layer and the other ranks' areas mapped into this process
+    (finch_ep_peer_*): T tokens per rank, `world` ranks on one node."""
+
+    def __init__(self, ctx, rank: int, world: int, T: int):
+        self.ctx, self.rank, self.world, self.T = ctx, rank, world, T
+        self.h = C.c_void_p()
+        ctx.check(ctx.lib.finch_ep_peer_create(ctx.h, rank, world, T, C.byref(self.h)))
+
+    def export(self) -> bytes:
+        buf = C.create_string_buffer(64)
+        self.ctx.check(self.ctx.lib.finch_ep_peer_export(self.h, buf))
+        return buf.raw
+
+    def import_handle(self, src_rank: int, handle: bytes):
+        self.ctx.check(self.ctx.lib.finch_ep_peer_import(self.h, src_rank, C.create_string_buffer(handle, 64)))
+
+    def area(self) -> int:
+        return self.ctx.lib.finch_ep_peer_area(self.h)
+
+    def attach(self, src_rank: int, area: int):
+        self.ctx.check(self.ctx.lib.finch_ep_peer_attach(self.h, src_rank, C.c_void_p(area)))
+
+    def set_wait_limit(self, polls: int):
+        self.ctx.check(self.ctx.lib.finch_ep_peer_set_wait_limit(self.h, polls))
+
+    def reset(self):
+        self.ctx.check(self.ctx.lib.finch_ep_peer_reset(self.h))
+
+    def destroy(self):
+        if self.h:
+            self.ctx.lib.finch_ep_peer_destroy(self.h)
+            self.h = None
+
+    @classmethod
+    def connect(cls, ctx, dist, group, T: int):
+        """Collective over the group: every rank creates its area and maps the others'.  Returns None on every rank
+        when any rank could not (no peer access between the devices, handles that cannot cross the processes)."""
+        import torch
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        px, payload = None, None
+        try:
+            px = cls(ctx, rank, world, T)
+            payload = px.export()
+        except Exception:
+            payload = None
+        handles = [None] * world
+        dist.all_gather_object(handles, payload, group=group)      # every rank takes part, whatever happened above
+        ok = 1 if all(hd is not None for hd in handles) else 0
+        if ok:
+            try:
+                for r, hd in enumerate(handles):
+                    if r != rank:
+                        px.import_handle(r, hd)
+            except Exception:
+                ok = 0
+        flag = torch.tensor([ok], device=torch.device("cuda", ctx.cfg.device))
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+        if int(flag.item()) == 0:
+            if px is not None and px.h:
+                px.destroy()
+            return None
+        dist.barrier(group)
+        return px
+
+
 class GpuBackend:
     """Drives the C-ABI steps on one GPU.  torch holds the device buffers."""
 
@@ -190,6 +273,7 @@ class GpuBackend:
         self.rout = torch.empty((max_rows, self.hidden), dtype=torch.float32, device=dev)
         self.zero_valid = None
         self._static = {}
+        self.peer = None             # a connected PeerExchange routes the fixed-capacity layer through peer memory
         self.stats = None            # a list makes ep_layer append (rows sent per rank, rows received per rank) per layer
         # Received rows select few local experts each.  More than one decode-sized batch of them goes through the
         # tensor-core path in passes of `tc_chunk` rows (one sort and one pair of grouped GEMMs per pass) instead of
@@ -240,7 +324,8 @@ class GpuBackend:
                                                      p.slot_of.data_ptr()))
         return p
 
-    home_direct = True
+    home_direct = True        # fixed-capacity layer: the rank's own tokens in one in-place pass
+    planned_direct = False    # planned layer: see _ep_layer
 
     def static_plan(self, T, world, skip=-1):
         """Device copy of static_plan_numpy, made once per (T, world, skip)."""
@@ -291,6 +376,11 @@ class GpuBackend:
         st = self._stream()
         self.ctx.check(self.lib.finch_encode_ep_unpack(self.ctx.h, st, recv_buf.data_ptr(), n, self.rx.data_ptr(), self.rids.data_ptr(),
                                                        self.rw.data_ptr(), self.rv.data_ptr()))
+        return self._moe_rows(layer, n, skip)
+
+    def _moe_rows(self, layer, n, skip=None):
+        """The rank's MoE path over rows [0, n) of rx / rids / rw / rv -> rout."""
+        st = self._stream()
         step = self.ctx.cfg.max_tokens
         blocks = [(0, n)] if skip is None else [(0, skip[0]), (skip[0] + skip[1], n)]
         rows = sum(hi - lo for lo, hi in blocks)
@@ -311,6 +401,24 @@ class GpuBackend:
                 self.ctx.check(self.lib.finch_set_prefill_mode(self.ctx.h, getattr(self.ctx, "prefill_mode", 0)))
                 self.ctx.check(self.lib.finch_set_prefill_chunk(self.ctx.h, getattr(self.ctx, "prefill_chunk", 0)))
         return self.rout[:n]
+
+    # -- the exchange through peer memory (PeerExchange)
+    def peer_dispatch(self, x, ids, weights, valid):
+        self.ctx.check(self.lib.finch_encode_ep_peer_dispatch(self.ctx.h, self._stream(), self.peer.h, x.data_ptr(), ids.data_ptr(), weights.data_ptr(),
+                                                              valid.data_ptr() if valid is not None else None))
+
+    def peer_local_moe(self, layer, n, skip):
+        if n > self.max_rows:
+            raise ValueError(f"{n} rows, backend sized for {self.max_rows}")
+        self.ctx.check(self.lib.finch_encode_ep_peer_receive(self.ctx.h, self._stream(), self.peer.h, self.rx.data_ptr(), self.rids.data_ptr(),
+                                                             self.rw.data_ptr(), self.rv.data_ptr()))
+        return self._moe_rows(layer, n, skip)
+
+    def peer_return(self, part):
+        self.ctx.check(self.lib.finch_encode_ep_peer_return(self.ctx.h, self._stream(), self.peer.h, part.data_ptr()))
+
+    def peer_combine(self, out):
+        self.ctx.check(self.lib.finch_encode_ep_peer_combine(self.ctx.h, self._stream(), self.peer.h, out.data_ptr()))
 
     def base(self, layer, x, ids, weights, shared, h_mid, out):
         torch = self.torch

@@ -81,6 +81,18 @@ _PROTOS = {
     "finch_encode_ep_pack": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp, _vp]),
     "finch_encode_ep_unpack": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp]),
     "finch_encode_ep_combine": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i]),
+    "finch_ep_peer_create": (_i, [_vp, _i, _i, _i, C.POINTER(_vp)]),
+    "finch_ep_peer_export": (_i, [_vp, _vp]),
+    "finch_ep_peer_import": (_i, [_vp, _i, _vp]),
+    "finch_ep_peer_area": (_vp, [_vp]),
+    "finch_ep_peer_attach": (_i, [_vp, _i, _vp]),
+    "finch_ep_peer_set_wait_limit": (_i, [_vp, C.c_longlong]),
+    "finch_ep_peer_reset": (_i, [_vp]),
+    "finch_ep_peer_destroy": (_i, [_vp]),
+    "finch_encode_ep_peer_dispatch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "finch_encode_ep_peer_receive": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "finch_encode_ep_peer_return": (_i, [_vp, _vp, _vp, _vp]),
+    "finch_encode_ep_peer_combine": (_i, [_vp, _vp, _vp, _vp]),
     "finch_pool_fill_synthetic_range": (_i, [_vp, _i, _i, _i, _i, C.c_uint64]),
     "finch_encode_residual_norm": (_i, [_vp, _vp, _vp, _vp, _vp, C.c_float, _vp, _vp, _i]),
     "finch_encode_router": (_i, [_vp, _vp, C.POINTER(WDesc), C.POINTER(WDesc), _vp, _vp, _vp, _vp, _i]),

@@ -327,6 +327,36 @@ FINCH_API int finch_encode_ep_unpack(finch_ctx *ctx, finch_stream stream, const 
 /* hidden_out[t] += sum over destinations d in ascending order of back_rows[offs[d] + slot_of[t][d]]. */
 FINCH_API int finch_encode_ep_combine(finch_ctx *ctx, finch_stream stream, float *hidden_out, const float *back_rows,
                                       const int *slot_of, const int *offs, int T, int world);
+/* ---- the fixed-capacity exchange over NVLink peer memory (decode-sized batches: every rank owns
+ * tokens_per_rank tokens and sends each to every rank).  The ranks' kernels store records and partial
+ * rows into each other's receive areas and wait on one flag per slot: no collective call and no host
+ * step per layer, so a layer is a fixed sequence of launches that a CUDA graph can hold.  Setup, once:
+ * every rank creates its area, exports a 64-byte handle, receives the other ranks' handles by whatever
+ * channel the host has (the MPI / NCCL bootstrap, a file) and imports them.  Per layer, every rank, in
+ * this order: dispatch -> (finch_encode_moe_decode on its own tokens) -> receive ->
+ * finch_encode_moe_prefill on the world * tokens_per_rank received rows -> return -> combine.
+ * Every device-side wait is bounded: a flag that does not arrive records FINCH_E_TIMEOUT in the
+ * device status word, the slot counts as empty and later waits no longer spin; the host then calls
+ * finch_ep_peer_reset on every rank (after a barrier) or falls back to the all-to-all steps above. */
+typedef struct finch_ep_peer finch_ep_peer;
+FINCH_API int finch_ep_peer_create(finch_ctx *ctx, int rank, int world, int tokens_per_rank, finch_ep_peer **out);
+FINCH_API int finch_ep_peer_export(finch_ep_peer *peer, void *handle64);                        /* this rank's area, for the others */
+FINCH_API int finch_ep_peer_import(finch_ep_peer *peer, int src_rank, const void *handle64);    /* another process's area */
+FINCH_API void *finch_ep_peer_area(finch_ep_peer *peer);                                        /* device pointer of this rank's area */
+FINCH_API int finch_ep_peer_attach(finch_ep_peer *peer, int src_rank, void *area);              /* an area of the same process */
+FINCH_API int finch_ep_peer_set_wait_limit(finch_ep_peer *peer, long long polls);               /* ~100 ns each; default 4,000,000 */
+FINCH_API int finch_ep_peer_reset(finch_ep_peer *peer);                                         /* waits for the device, clears all flags */
+FINCH_API int finch_ep_peer_destroy(finch_ep_peer *peer);
+FINCH_API int finch_encode_ep_peer_dispatch(finch_ctx *ctx, finch_stream stream, finch_ep_peer *peer, const void *h_post,
+                                            const int32_t *expert_ids, const float *weights, const uint8_t *valid);
+/* Rows [world * tokens_per_rank] in source-rank order; the block of this rank's own tokens gets an all-zero mask. */
+FINCH_API int finch_encode_ep_peer_receive(finch_ctx *ctx, finch_stream stream, finch_ep_peer *peer, void *h_post,
+                                           int32_t *expert_ids, float *weights, uint8_t *valid);
+/* rows: fp32 [world * tokens_per_rank][hidden], block s = the partial sums of rank s's tokens. */
+FINCH_API int finch_encode_ep_peer_return(finch_ctx *ctx, finch_stream stream, finch_ep_peer *peer, const float *rows);
+/* hidden_out[t] += the other ranks' partial rows of token t, in ascending rank order. */
+FINCH_API int finch_encode_ep_peer_combine(finch_ctx *ctx, finch_stream stream, finch_ep_peer *peer, float *hidden_out);
+
 /* Synthetic contents for one shard: experts [e0, e1) of layers [layer0, layer1) get the bytes
  * finch_pool_fill_synthetic gives them in a full pool; the pool needs n_layers * (e1 - e0) slots. */
 FINCH_API int finch_pool_fill_synthetic_range(finch_pool *pool, int layer0, int layer1, int e0, int e1, uint64_t seed);

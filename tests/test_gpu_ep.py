@@ -77,7 +77,7 @@ def test_single_rank_protocol_matches_plain_layer(T, static, direct):
         shd = ctx.make_shared(*[ctx.upload_tensor(t) for t in sh], gate_score=score_d)
         want = ctx.moe_forward_host(pool, 0, x, ids, w, valid=valid, shared=shd, gate_score=score, h_mid=h_mid)
         be = ep.GpuBackend(ctx, pool, T)
-        be.home_direct = direct      # False: the rank's own rows also go through pack / unpack / combine
+        be.home_direct = be.planned_direct = direct      # False: the rank's own rows also go through pack / unpack / combine
         out = torch.empty((T, 256), dtype=torch.float32, device="cuda")
         (ep.ep_layer_static if static else ep.ep_layer)(be, None, None, 0, d(x), d(ids), d(w), d(valid), shd, d(h_mid), out)
         torch.cuda.synchronize()
@@ -118,6 +118,114 @@ def test_single_rank_protocol_with_nothing_to_send():
     finally:
         pool.destroy()
         ctx.destroy()
+
+
+def _two_ranks_one_process(api, T=8):
+    """Two ranks' contexts, sharded pools and connected peer areas on one GPU, plus a full pool for the yardstick."""
+    NE, H, I = 16, 256, 128
+    rng = synth.rng_for(14, 1)
+    blocks = {e: synth.expert_block(rng, H, I, 64, 3, L.BF16) for e in range(NE - 1)}      # expert 15 is nowhere
+    sh = synth.shared_expert(rng, H, I, 64, 4, L.BF16)
+    ranks = []
+    for r in range(2):
+        ctx = _ctx(api, max_tokens=2 * T)
+        pool = ctx.pool(max_slots=8)
+        for e in range(r * 8, r * 8 + 8):
+            if e in blocks:
+                pool.put(0, e, blocks[e])
+        be = ep.GpuBackend(ctx, pool, 2 * T)
+        be.peer = ep.PeerExchange(ctx, r, 2, T)
+        ranks.append((ctx, pool, be))
+    ranks[0][2].peer.attach(1, ranks[1][2].peer.area())
+    ranks[1][2].peer.attach(0, ranks[0][2].peer.area())
+    return blocks, sh, ranks
+
+
+def test_peer_exchange_two_ranks_in_one_process_match_oracle():
+    """The exchange through peer memory (dispatch / receive / return / combine with one flag per slot), its two
+    ranks run from one process on one GPU: each step of both ranks is launched before the step that waits for it, so
+    no kernel ever waits for one that has not run.  Twice, so that the cleared flags are exercised."""
+    import torch
+    from finchmoe_b200 import api
+    from oracle import oracle
+    T, H, I, K = 8, 256, 128, 8
+    blocks, sh, ranks = _two_ranks_one_process(api, T)
+    try:
+        d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        for rep in range(2):
+            inputs, outs = [], []
+            for r in range(2):
+                r2 = synth.rng_for(14, 2 + rep, r)
+                x = synth.activations(r2, T, H)
+                ids, w = synth.zipf_routing(r2, T, 16, K)
+                valid = (r2.random((T, K)) > 0.1).astype(np.uint8)
+                score = r2.normal(0, 1, size=T).astype(np.float32)
+                h_mid = r2.normal(0, 1, size=(T, H)).astype(np.float32)
+                ctx = ranks[r][0]
+                score_d = d(score)
+                shd = ctx.make_shared(*[ctx.upload_tensor(t) for t in sh], gate_score=score_d)
+                inputs.append((x, ids, w, valid, score, h_mid, d(x), d(ids), d(w), d(valid), shd, d(h_mid), score_d))
+                outs.append(torch.zeros((T, H), dtype=torch.float32, device="cuda"))
+            for r, (ctx, pool, be) in enumerate(ranks):
+                with be.stream_scope():
+                    be.peer_dispatch(*inputs[r][6:10])
+            torch.cuda.synchronize()
+            for r, (ctx, pool, be) in enumerate(ranks):
+                with be.stream_scope():
+                    be.home(0, *inputs[r][6:10], inputs[r][10], inputs[r][11], outs[r])
+                    part = be.peer_local_moe(0, 2 * T, (r * T, T))
+                    be.peer_return(part)
+            torch.cuda.synchronize()
+            for r, (ctx, pool, be) in enumerate(ranks):
+                with be.stream_scope():
+                    be.peer_combine(outs[r])
+            torch.cuda.synchronize()
+            for r, (ctx, pool, be) in enumerate(ranks):
+                x, ids, w, valid, score, h_mid = inputs[r][:6]
+                want = np.stack([oracle.moe_layer([blocks.get(int(e)) if valid[t, k] else None for k, e in enumerate(ids[t])], w[t],
+                                                  np.array([1 if (valid[t, k] and int(e) in blocks) else 0 for k, e in enumerate(ids[t])], np.uint8),
+                                                  x[t], bits=3, scale_dtype=oracle.SCALE_BF16, hidden=H, inter=I, h_mid=h_mid[t], shared=sh,
+                                                  shared_gate_score=float(score[t])) for t in range(T)])
+                assert_close(outs[r].cpu().numpy(), want, f"peer exchange, rank {r}, pass {rep}")
+                assert ctx.device_status() == 0
+    finally:
+        for ctx, pool, be in ranks:
+            be.peer.destroy()
+            pool.destroy()
+            ctx.destroy()
+
+
+def test_peer_receive_wait_runs_out_and_reports_timeout():
+    """Nobody dispatches: the receive kernel's bounded wait gives up after a fraction of a millisecond, records
+    FINCH_E_TIMEOUT in the device status word, masks the rows it did not get and returns; the context stays usable
+    (the same exchange then works after a reset)."""
+    import torch
+    from finchmoe_b200 import api
+    T = 8
+    blocks, sh, ranks = _two_ranks_one_process(api, T)
+    try:
+        ctx, pool, be = ranks[0]
+        be.peer.set_wait_limit(2000)
+        be.rv.fill_(1)
+        with be.stream_scope():
+            be.ctx.check(be.lib.finch_encode_ep_peer_receive(ctx.h, be._stream(), be.peer.h, be.rx.data_ptr(), be.rids.data_ptr(),
+                                                             be.rw.data_ptr(), be.rv.data_ptr()))
+        torch.cuda.synchronize()
+        assert ctx.device_status() == L.E_TIMEOUT
+        assert int(be.rv[:2 * T].sum().item()) == 0            # nothing arrived: every row is masked
+        out = torch.zeros((T, 256), dtype=torch.float32, device="cuda")
+        with be.stream_scope():
+            be.peer_combine(out)                               # the status word is set: this wait does not spin
+        torch.cuda.synchronize()
+        assert float(out.abs().sum().item()) == 0.0
+        ctx.device_status_clear()
+        be.peer.reset()
+        assert ctx.device_status() == 0
+    finally:
+        for ctx, pool, be in ranks:
+            be.peer.destroy()
+            pool.destroy()
+            ctx.destroy()
 
 
 WORKER = r'''
@@ -176,6 +284,25 @@ for rep in range(2):
 torch.cuda.synchronize()
 assert_close(args[-1].cpu().numpy(), want[:Ts], f"rank {rank} fixed capacity, graph replay")
 assert ctx.device_status() == 0
+# the same layer with the exchange through peer memory instead of the all-to-alls: from the host, then from a graph
+be.peer = ep.PeerExchange.connect(ctx, dist, None, Ts)
+assert be.peer is not None, "the ranks could not map each other's receive areas"
+args[-1].zero_()
+ep.ep_layer_static(be, dist, None, 0, *args)
+torch.cuda.synchronize()
+assert_close(args[-1].cpu().numpy(), want[:Ts], f"rank {rank} peer exchange")
+dist.barrier()
+g2 = torch.cuda.CUDAGraph()
+with torch.cuda.graph(g2, stream=be.stream, capture_error_mode="thread_local"):
+    ep.ep_layer_static(be, dist, None, 0, *args, in_scope=True)
+for rep in range(3):
+    args[-1].zero_()
+    g2.replay()
+torch.cuda.synchronize()
+assert_close(args[-1].cpu().numpy(), want[:Ts], f"rank {rank} peer exchange, graph replay")
+assert ctx.device_status() == 0
+dist.barrier()
+del g2
 del g                                   # the graph holds the recorded all-to-alls: it goes before the communicator
 torch.cuda.synchronize()
 dist.barrier()
