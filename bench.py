@@ -691,8 +691,7 @@ class EpBench:
             def pairs():
                 for _ in range(LAYERS):
                     be.peer_dispatch(self.xd, ids[0], w[0], None)
-                    be.ctx.check(be.lib.finch_encode_ep_peer_receive(be.ctx.h, be._stream(), be.peer.h, be.rx.data_ptr(), be.rids.data_ptr(),
-                                                                     be.rw.data_ptr(), be.rv.data_ptr()))
+                    be.peer_receive(False)
                     be.peer_return(be.rout)
                     be.peer_combine(self.out[0])
         else:

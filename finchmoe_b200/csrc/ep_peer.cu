@@ -3,9 +3,9 @@
 // the receiving kernels wait for the flags.  No collective library call and no host step per layer, so a
 // decode layer is a fixed sequence of launches on one stream (and can sit in a CUDA graph).
 //
-//   dispatch   every token's record -> slot [my rank][t] of every other rank's area, then its flag
-//   receive    wait for the (world - 1) * T records addressed to me, spread them into the row arrays the
-//              MoE entry points take, clear their flags; the block of my own tokens is masked out
+//   dispatch   every token's record -> slot [my rank][t] of every rank's area (my own included), then its flag
+//   receive    wait for the world * T records addressed to me, spread them into the row arrays the MoE entry
+//              points take, clear their flags; on request the block of my own tokens is masked out
 //   return     the partial rows of source s's tokens -> slot [my rank][t] of rank s's area, then its flag
 //   combine    wait for every other rank's partial rows of my tokens, add them to the layer output in
 //              ascending rank order, clear their flags
@@ -65,8 +65,7 @@ __device__ bool wait_flag(const uint32_t *flag, int *status, long long limit) {
 // grid (T, world), 128 threads: record of token t -> rank d's area
 __global__ void __launch_bounds__(128) peer_dispatch_kernel(Areas areas, int rank, int T, const uint8_t *x, const int32_t *ids, const float *weights,
                                                             const uint8_t *valid, int row_bytes, int K, int rec_bytes, size_t off_rflag) {
-    const int t = blockIdx.x, d = blockIdx.y;
-    if (d == rank) return;
+    const int t = blockIdx.x, d = blockIdx.y;   // d == rank: my own area (the rank's tokens take the same route)
     uint8_t *area = areas.p[d];
     uint8_t *rec = area + (size_t)(rank * T + t) * rec_bytes;
     const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)t * row_bytes);
@@ -87,13 +86,10 @@ __global__ void __launch_bounds__(128) peer_dispatch_kernel(Areas areas, int ran
 
 // grid world * T, 128 threads: slot i = [source][t] of my area -> row i of the arrays
 __global__ void __launch_bounds__(128) peer_receive_kernel(uint8_t *area, int rank, int T, int row_bytes, int K, int rec_bytes, size_t off_rflag, uint8_t *x,
-                                                           int32_t *ids, float *weights, uint8_t *valid, int *status, long long limit) {
+                                                           int32_t *ids, float *weights, uint8_t *valid, int *status, long long limit, int mask_own) {
     __shared__ int ok;
     const int i = blockIdx.x, src_rank = i / T;
-    if (src_rank == rank) {          // my own tokens are served in place, not through the exchange
-        if (threadIdx.x < K) valid[i * K + threadIdx.x] = 0;
-        return;
-    }
+    const bool masked = mask_own && src_rank == rank;   // my own tokens are served in place by the caller: their rows select nothing
     uint32_t *flag = reinterpret_cast<uint32_t *>(area + off_rflag) + i;
     if (threadIdx.x == 0) ok = wait_flag(flag, status, limit) ? 1 : 0;
     __syncthreads();
@@ -109,7 +105,7 @@ __global__ void __launch_bounds__(128) peer_receive_kernel(uint8_t *area, int ra
         const int k = threadIdx.x;
         ids[i * K + k] = reinterpret_cast<const int32_t *>(rec + row_bytes)[k];
         weights[i * K + k] = reinterpret_cast<const float *>(rec + row_bytes + 4 * K)[k];
-        valid[i * K + k] = rec[row_bytes + 8 * K + k];
+        valid[i * K + k] = masked ? (uint8_t)0 : rec[row_bytes + 8 * K + k];
     }
     __syncthreads();
     if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t *>(flag) = 0u;
@@ -266,7 +262,6 @@ extern "C" int finch_encode_ep_peer_dispatch(finch_ctx *ctx, finch_stream stream
     if (!ctx || !p || p->ctx != ctx || !h_post || !expert_ids || !weights) return FINCH_E_ARG;
     int rc = connected(p);
     if (rc) return rc;
-    if (p->world == 1) return FINCH_OK;
     const finch_config &c = ctx->cfg;
     const int elt = c.act_dtype == FINCH_BF16 ? 2 : 4, row_bytes = c.hidden * elt;
     if (row_bytes % 16) return finch_fail(ctx, FINCH_E_ARG, "activation rows must be multiples of 16 bytes");
@@ -280,14 +275,14 @@ extern "C" int finch_encode_ep_peer_dispatch(finch_ctx *ctx, finch_stream stream
 }
 
 extern "C" int finch_encode_ep_peer_receive(finch_ctx *ctx, finch_stream stream, finch_ep_peer *p, void *h_post, int32_t *expert_ids, float *weights,
-                                            uint8_t *valid) {
+                                            uint8_t *valid, int mask_own) {
     if (!ctx || !p || p->ctx != ctx || !h_post || !expert_ids || !weights || !valid) return FINCH_E_ARG;
     const finch_config &c = ctx->cfg;
     const int elt = c.act_dtype == FINCH_BF16 ? 2 : 4;
     cudaSetDevice(c.device);
     peer_receive_kernel<<<p->world * p->T, 128, 0, finch_pick_stream(ctx, stream)>>>(p->area, p->rank, p->T, c.hidden * elt, c.top_k,
                                                                                       rec_bytes_of(c.hidden, elt, c.top_k), p->off_rflag, (uint8_t *)h_post,
-                                                                                      expert_ids, weights, valid, ctx->dev_status, p->limit);
+                                                                                      expert_ids, weights, valid, ctx->dev_status, p->limit, mask_own);
     FINCH_CUDA_OK(ctx, cudaGetLastError());
     ctx->launches++;
     return FINCH_OK;

@@ -57,6 +57,7 @@ constexpr int TEAM = 4;                     // warps that split the K dimension 
 constexpr int MAXP = FINCH_MAX_PAIRS;
 constexpr int MAXM = 8;                     // pairs per expert group (<= tokens per call)
 constexpr int NW_MAX = 24;                  // consumer warps per CTA
+constexpr int MAX_CALLS = 16;               // batches of one multi-batch launch (one per expert-parallel rank)
 constexpr int REC_CAP = 24;                 // act records a CTA of the down kernel can hold
 constexpr int UB = 288;                     // bytes of one 128-value unit in one section of a 3-bit operand record
 constexpr int GB4 = 128;                    // bytes of one 64-value group in one section of a 4-bit operand record
@@ -94,7 +95,44 @@ struct MoeArgs {
     float *hidden_out;
     int gs_a, gs_b;      // CTAs at the end of the gate/up / down grid that take the shared expert's tiles
     int fault;           // finch_debug_fault: 1 = one warp of the gate/up kernel withholds its first fetch
+    // Several independent batches of B tokens in one launch sequence (n_calls > 1): batch c owns rows
+    // [c * B, (c + 1) * B) of h_post / ids / weights / valid and the CTAs [cta0[c], cta0[c + 1]) of the two big
+    // grids.  Only batch own_call has h_mid, the shared expert and hidden_out; the others write their routed
+    // sums to rows_out[c * B + t].
+    int n_calls, own_call;
+    int cta0[MAX_CALLS + 1];
+    float *rows_out;
 };
+
+// The view of batch c of a multi-batch launch: pointers moved to its rows, the shared expert and the residual
+// only for the caller's own batch.  vb / vg: the CTA's index and the CTA count inside the batch.
+__device__ __forceinline__ void select_call(MoeArgs &a, int c) {
+    const size_t P = (size_t)a.P, B = (size_t)a.B;
+    a.h_post = reinterpret_cast<const char *>(a.h_post) + c * B * a.hidden * (a.act_dtype == FINCH_BF16 ? 2 : 4);
+    a.ids += c * P;
+    a.weights += c * P;
+    if (a.valid) a.valid += c * P;
+    a.act += c * P * a.inter;
+    a.partial += c * (P + B) * a.hidden;
+    if (c != a.own_call) {
+        a.has_shared = 0;
+        a.gs_a = a.gs_b = 0;
+        a.h_mid = nullptr;
+        a.hidden_out = a.rows_out + c * B * a.hidden;
+    }
+}
+// a0: the kernel parameter (its table is indexed at run time, which a copy in registers could not be)
+__device__ __forceinline__ void pick_call(const MoeArgs &a0, MoeArgs &a, int &vb, int &vg) {
+    vb = blockIdx.x;
+    vg = gridDim.x;
+    if (a0.n_calls > 1) {
+        int c = 0;
+        while (c + 1 < a0.n_calls && (int)blockIdx.x >= a0.cta0[c + 1]) ++c;
+        vb = blockIdx.x - a0.cta0[c];
+        vg = a0.cta0[c + 1] - a0.cta0[c];
+        select_call(a, c);
+    }
+}
 
 // ---- operand records -------------------------------------------------------
 // record = one or two sections of B fragments (hi; hi + lo) followed by a header of floats:
@@ -767,11 +805,14 @@ __device__ __forceinline__ WarpJobA warp_job_a(bool routed, int units, int n_til
 
 // grid: one CTA per SM (persistent); block: nteam teams of TEAM warps.
 template <bool HILO, bool FP16S>
-__global__ void __launch_bounds__(NW_MAX * 32, 1) moe_gateup_kernel(const MoeArgs a) {
+__global__ void __launch_bounds__(NW_MAX * 32, 1) moe_gateup_kernel(const MoeArgs a0) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     const int nwarps = blockDim.x >> 5, nteam = nwarps / TEAM;
-    const SmemA L = smem_a_layout(a.hidden, a.inter, a.sh_inter, a.B, a.has_shared, HILO, nwarps);
+    const SmemA L = smem_a_layout(a0.hidden, a0.inter, a0.sh_inter, a0.B, a0.has_shared, HILO, nwarps);
+    MoeArgs a = a0;
+    int vb, vg;
+    pick_call(a0, a, vb, vg);
     const FinchTile T = finch_tile(a.hidden, a.inter);
     const FinchTile4 T4 = finch_tile4(a.hidden, a.sh_inter);
     GroupTab *tab = reinterpret_cast<GroupTab *>(smem + L.tab);
@@ -786,8 +827,8 @@ __global__ void __launch_bounds__(NW_MAX * 32, 1) moe_gateup_kernel(const MoeArg
     const unsigned tries = a.fault ? 4u : (1u << 13);
     const unsigned spins = a.fault ? 64u : (1u << 22);
     constexpr int PER_PASS = HILO ? 2 : 4;
-    const int Gr = gridDim.x - a.gs_a;
-    const bool routed = (int)blockIdx.x < Gr;
+    const int Gr = vg - a.gs_a;
+    const bool routed = vb < Gr;
     const uint32_t rec32 = finch_smem_u32(smem + L.rec), zero32 = finch_smem_u32(smem + L.zero), col32 = finch_smem_u32(col);
     const uint32_t stage32 = finch_smem_u32(smem + L.stage), stdelta = (uint32_t)(nwarps * L.stg);   // stage s of warp w at stage32 + w * stg + s * stdelta
     const int rowb = K * (HILO ? 4 : 2);
@@ -841,7 +882,7 @@ __global__ void __launch_bounds__(NW_MAX * 32, 1) moe_gateup_kernel(const MoeArg
     auto row_ptr = [&](int b) { return (const void *)((const uint8_t *)a.h_post + (size_t)b * rowb); };
     const bool one_round = a.B <= xs_rows;   // else: the records are built round by round before anything is fetched
     if (warp < 2) {
-        build_groups(a, tab, sm_ids, sm_rank, PER_PASS, routed ? col : nullptr, rec32, L.rstride, trange, routed ? nteam : 0, blockIdx.x * nteam, Gr * nteam, T.nTA);
+        build_groups(a, tab, sm_ids, sm_rank, PER_PASS, routed ? col : nullptr, rec32, L.rstride, trange, routed ? nteam : 0, vb * nteam, Gr * nteam, T.nTA);
         STAMP(2);
     } else if (one_round) {
         if (tid == 64) records_fetch_rows(a.B, 0, rowb, xs, xbar, row_ptr);
@@ -856,7 +897,7 @@ __global__ void __launch_bounds__(NW_MAX * 32, 1) moe_gateup_kernel(const MoeArg
     }
     __syncthreads();
     STAMP(13);
-    const WarpJobA J = warp_job_a(routed, units, T4.nTA, blockIdx.x, Gr, a.gs_a, nteam, warp, trange);
+    const WarpJobA J = warp_job_a(routed, units, T4.nTA, vb, Gr, a.gs_a, nteam, warp, trange);
     const bool withhold = a.fault == 1 && routed && J.j0 == 0 && warp % TEAM == 0;   // the warp that owns the first quarter of tile 0
     if (lane == 0 && J.nu > 0 && J.j0 < J.j1 && !withhold) fetch(J, J.j0, stage32 + (uint32_t)(warp * L.stg), full);
     if (one_round) {
@@ -1056,11 +1097,14 @@ __host__ __device__ inline SmemB smem_b_layout(int hidden, int inter, int sh_int
 
 // grid: one CTA per SM (persistent); block: nwarps warps, each takes whole tiles.
 template <bool FP16S>
-__global__ void __launch_bounds__(NW_MAX * 32, 1) moe_down_kernel(const MoeArgs a) {
+__global__ void __launch_bounds__(NW_MAX * 32, 1) moe_down_kernel(const MoeArgs a0) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
     const int nwarps = blockDim.x >> 5;
-    const SmemB L = smem_b_layout(a.hidden, a.inter, a.sh_inter, a.B, a.has_shared, nwarps);
+    const SmemB L = smem_b_layout(a0.hidden, a0.inter, a0.sh_inter, a0.B, a0.has_shared, nwarps);
+    MoeArgs a = a0;
+    int vb, vg;
+    pick_call(a0, a, vb, vg);
     const FinchTile T = finch_tile(a.hidden, a.inter);
     const FinchTile4 T4 = finch_tile4(a.hidden, a.sh_inter);
     GroupTab *tab = reinterpret_cast<GroupTab *>(smem + L.tab);
@@ -1071,8 +1115,8 @@ __global__ void __launch_bounds__(NW_MAX * 32, 1) moe_down_kernel(const MoeArgs 
     uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + L.bar) + 2 * NW_MAX;
     const int K = a.inter, Ks = a.sh_inter;
     const unsigned tries = a.fault ? 4u : (1u << 13);
-    const int Gr = gridDim.x - a.gs_b;
-    const bool routed = (int)blockIdx.x < Gr;
+    const int Gr = vg - a.gs_b;
+    const bool routed = vb < Gr;
 
     if (lane == 0) {
         finch_mbar_init(full, 1);
@@ -1096,8 +1140,8 @@ __global__ void __launch_bounds__(NW_MAX * 32, 1) moe_down_kernel(const MoeArgs 
     if (routed) {
         const int ng = tab->ng;
         const int total = tab->pre[ng] * T.nTB;
-        const int job0 = job_at(tab->pre, ng, T.nTB, (int)((unsigned)total * blockIdx.x / (unsigned)Gr));
-        const int job1 = job_at(tab->pre, ng, T.nTB, (int)((unsigned)total * (blockIdx.x + 1) / (unsigned)Gr));
+        const int job0 = job_at(tab->pre, ng, T.nTB, (int)((unsigned)total * vb / (unsigned)Gr));
+        const int job1 = job_at(tab->pre, ng, T.nTB, (int)((unsigned)total * (vb + 1) / (unsigned)Gr));
         auto fetch = [&](int gi, int tb, uint32_t dst, uint64_t *bar) {   // lane 0
             finch_mbar_expect_tx(bar, (unsigned)T.tileB);
             finch_bulk_g2s_a(dst, a.pool_base + (size_t)tab->slot[gi] * a.slot_bytes + T.b_base + (size_t)tb * T.tileB, (unsigned)T.tileB, bar);
@@ -1188,7 +1232,7 @@ __global__ void __launch_bounds__(NW_MAX * 32, 1) moe_down_kernel(const MoeArgs 
         // ---------------- shared expert: 4-bit tiles of 16 down rows ----------------
         const int nps = (a.B + 3) / 4;   // passes of a tile: four tokens (hi + lo columns) each
         const int n_tiles = T4.nTB, stride = a.gs_b * nwarps;
-        const int tile0 = (blockIdx.x - Gr) * nwarps + warp;
+        const int tile0 = (vb - Gr) * nwarps + warp;
         auto fetch = [&](int tile, uint32_t dst, uint64_t *bar) {   // lane 0
             finch_mbar_expect_tx(bar, (unsigned)T4.tileB);
             finch_bulk_g2s_a(dst, a.sh_tiles + T4.b_base + (size_t)tile * T4.tileB, (unsigned)T4.tileB, bar);
@@ -1237,10 +1281,12 @@ __global__ void __launch_bounds__(NW_MAX * 32, 1) moe_down_kernel(const MoeArgs 
 // ============================ combine =====================================
 // hidden = h_mid + sum_{k ascending, usable} w_k * out_k + sigmoid(score) * shared_out, the arithmetic of
 // moe_combine_residual (finchmoe/shaders.metal:2196-2231).  grid: (hidden / 256, B); block 256.
-__global__ void __launch_bounds__(256) moe_combine_kernel(const MoeArgs a) {
+__global__ void __launch_bounds__(256) moe_combine_kernel(const MoeArgs a0) {
     __shared__ int ok[8];
     __shared__ float wk[8];
-    const int b = blockIdx.y, row = blockIdx.x * 256 + threadIdx.x;
+    MoeArgs a = a0;
+    const int b = blockIdx.y % a0.B, row = blockIdx.x * 256 + threadIdx.x;   // grid.y = B * n_calls
+    if (a0.n_calls > 1) select_call(a, blockIdx.y / a0.B);
     grid_dep_launch();
     // Routing, router weights, gate scores and h_mid are inputs of the whole call: final since the gate/up
     // kernel (the first of the chain) passed its own wait, and this kernel only starts once the down kernel has
@@ -1341,14 +1387,17 @@ int set_attrs_once(finch_ctx *ctx) {
 
 }  // namespace
 
-extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finch_pool *pool, int layer, const void *h_post,
-                                       const int32_t *expert_ids, const float *weights, const uint8_t *valid,
-                                       const finch_shared *shared, const float *h_mid, float *hidden_out, int B) {
+// n_calls batches of B tokens each (rows [c * B, (c + 1) * B) of the inputs) in one sequence of three launches.
+// Batch own_call gets shared / h_mid and writes hidden_out; the others write their routed sums to rows_out.
+static int encode_decode_calls(finch_ctx *ctx, finch_stream stream, finch_pool *pool, int layer, const void *h_post, const int32_t *expert_ids,
+                               const float *weights, const uint8_t *valid, const finch_shared *shared, const float *h_mid, float *hidden_out, int B,
+                               int n_calls, int own_call, float *rows_out) {
     if (!ctx || !pool || !h_post || !expert_ids || !weights || !hidden_out) return FINCH_E_ARG;
     const finch_config &c = ctx->cfg;
     if (pool->ctx != ctx) return finch_fail(ctx, FINCH_E_ARG, "pool belongs to another context");
     if (layer < 0 || layer >= pool->n_layers) return finch_fail(ctx, FINCH_E_ARG, "layer %d out of range", layer);
-    if (B < 1 || B > c.max_tokens) return finch_fail(ctx, FINCH_E_ARG, "B=%d outside 1..max_tokens=%d", B, c.max_tokens);
+    if (B < 1 || (long long)B * n_calls > c.max_tokens)
+        return finch_fail(ctx, FINCH_E_ARG, "%d batch(es) of B=%d outside 1..max_tokens=%d", n_calls, B, c.max_tokens);
     if (B * c.top_k > FINCH_MAX_PAIRS || B > MAXM)
         return finch_fail(ctx, FINCH_E_UNSUPPORTED, "decode path takes at most %d tokens / %d (token, expert) pairs; use finch_encode_moe_prefill",
                           MAXM, FINCH_MAX_PAIRS);
@@ -1387,17 +1436,38 @@ extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finc
     a.h_mid = h_mid;
     a.hidden_out = hidden_out;
     a.fault = ctx->fault;
+    a.n_calls = n_calls;
+    a.own_call = n_calls > 1 ? own_call : 0;
+    a.rows_out = rows_out;
     if ((uintptr_t)h_post & 15) return finch_fail(ctx, FINCH_E_ARG, "h_post must be 16-byte aligned");
     const int hilo = c.act_dtype == FINCH_BF16 ? 0 : 1;
     const bool fp16s = c.scale_dtype == FINCH_FP16;
-    const int grid = ctx->sm_count;
+    int grid = ctx->sm_count;
+    const int sm_all = grid;
+    if (n_calls > 1) {
+        // CTAs per batch: the routed experts of a batch cost about the same everywhere (a token's K experts spread over
+        // the ranks); the caller's own batch also carries the shared expert, about three routed experts' worth of MMAs.
+        const double routed = std::max(1.0, (double)B * c.top_k / n_calls), own = routed + (shared ? 3.0 : 0.0);
+        const double total = routed * (n_calls - 1) + own;
+        double acc = 0.0;
+        a.cta0[0] = 0;
+        for (int q = 0; q < n_calls; q++) {
+            acc += q == own_call ? own : routed;
+            int e = (int)(sm_all * acc / total + 0.5);
+            if (e < a.cta0[q] + 2) e = a.cta0[q] + 2;      // a batch with the shared expert needs a routed and a shared CTA
+            a.cta0[q + 1] = e;
+        }
+        a.cta0[n_calls] = std::max(a.cta0[n_calls], sm_all);   // at most 16 batches: every one gets CTAs of the first wave
+        grid = a.cta0[own_call >= 0 && own_call < n_calls ? own_call + 1 : 1] - a.cta0[own_call >= 0 && own_call < n_calls ? own_call : 0];
+    }
     if (shared) {
         // CTAs that take the shared expert's tiles: its expected share of the MMAs of each kernel.  The routing is
         // not known on the host: the distinct experts of a call are estimated from the batch (a token's K experts
         // are distinct; tokens overlap more as the batch grows) and so are the passes of a popular expert's tiles.
         const FinchTile T = finch_tile(c.hidden, c.moe_inter);
         const FinchTile4 T4 = finch_tile4(c.hidden, a.sh_inter);
-        const double U = B == 1 ? c.top_k : std::max((double)c.top_k, a.P * (1.0 - 0.04 * (B - 1)));
+        const double U = n_calls > 1 ? std::max(1.0, (double)a.P / n_calls)
+                                     : (B == 1 ? c.top_k : std::max((double)c.top_k, a.P * (1.0 - 0.04 * (B - 1))));
         const int ppa = hilo ? 2 : 4;
         const double fa = 1.0 + (B > ppa ? 0.1 : 0.0) + (hilo && B > 2 ? 0.35 * (B - 2) / 6.0 : 0.0), fb = B > 2 ? 1.0 + 0.45 * (B - 2) / 6.0 : 1.0;
         const int npa = hilo ? (B + 3) / 4 : (B + 7) / 8, npb = (B + 3) / 4;
@@ -1455,13 +1525,27 @@ extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finc
                           : (fp16s ? (const void *)moe_gateup_kernel<false, true> : (const void *)moe_gateup_kernel<false, false>);
     const void *kb = fp16s ? (const void *)moe_down_kernel<true> : (const void *)moe_down_kernel<false>;
     if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[0], st));
-    FINCH_CUDA_OK(ctx, launch(ka, dim3(grid), nteam * TEAM * 32, LA.total));
+    const int grid_all = n_calls > 1 ? a.cta0[n_calls] : grid;
+    FINCH_CUDA_OK(ctx, launch(ka, dim3(grid_all), nteam * TEAM * 32, LA.total));
     if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[1], st));
-    FINCH_CUDA_OK(ctx, launch(kb, dim3(grid), nwb * 32, LB.total));
-    FINCH_CUDA_OK(ctx, launch((const void *)moe_combine_kernel, dim3((c.hidden + 255) / 256, B), 256, 0));
+    FINCH_CUDA_OK(ctx, launch(kb, dim3(grid_all), nwb * 32, LB.total));
+    FINCH_CUDA_OK(ctx, launch((const void *)moe_combine_kernel, dim3((c.hidden + 255) / 256, B * n_calls), 256, 0));
     if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[2], st));
     ctx->launches += 3;
     return FINCH_OK;
+}
+
+extern "C" int finch_encode_moe_decode(finch_ctx *ctx, finch_stream stream, finch_pool *pool, int layer, const void *h_post,
+                                       const int32_t *expert_ids, const float *weights, const uint8_t *valid,
+                                       const finch_shared *shared, const float *h_mid, float *hidden_out, int B) {
+    return encode_decode_calls(ctx, stream, pool, layer, h_post, expert_ids, weights, valid, shared, h_mid, hidden_out, B, 1, 0, nullptr);
+}
+
+extern "C" int finch_encode_moe_decode_multi(finch_ctx *ctx, finch_stream stream, finch_pool *pool, int layer, int n_batches, int B, const void *h_post,
+                                             const int32_t *expert_ids, const float *weights, const uint8_t *valid, int own_batch,
+                                             const finch_shared *shared, const float *h_mid, float *hidden_out, float *rows_out) {
+    if (n_batches < 1 || n_batches > MAX_CALLS || own_batch < 0 || own_batch >= n_batches || !rows_out) return FINCH_E_ARG;
+    return encode_decode_calls(ctx, stream, pool, layer, h_post, expert_ids, weights, valid, shared, h_mid, hidden_out, B, n_batches, own_batch, rows_out);
 }
 
 extern "C" int finch_profile_enable(finch_ctx *ctx, int on) {

@@ -156,8 +156,13 @@ def _ep_layer_static(backend, dist, group, layer, x, ids, weights, valid, shared
         # The ranks' own kernels move the records and the partial rows through each other's memory (NVLink), each
         # slot with its flag: no collective and no host step, the whole layer is launches on the backend's stream.
         backend.peer_dispatch(x, ids, weights, valid)
-        backend.home(layer, x, ids, weights, valid, shared, h_mid, out)          # while the peers' records arrive
-        part = backend.peer_local_moe(layer, T * world, (rank * T, T))
+        if backend.can_multi(T, world):
+            # one launch sequence serves every rank's batch of T rows, the rank's own among them (with h_mid and the
+            # shared expert): batch c = the tokens of rank c, of which only the experts held here are computed
+            part = backend.peer_local_multi(layer, T, world, rank, shared, h_mid, out)
+        else:
+            backend.home(layer, x, ids, weights, valid, shared, h_mid, out)      # while the peers' records arrive
+            part = backend.peer_local_moe(layer, T * world, (rank * T, T))
         backend.peer_return(part)
         backend.peer_combine(out)
         return out
@@ -273,6 +278,7 @@ class GpuBackend:
         self.rout = torch.empty((max_rows, self.hidden), dtype=torch.float32, device=dev)
         self.zero_valid = None
         self._static = {}
+        self.multi = True            # decode-sized batches of all ranks in one launch sequence (finch_encode_moe_decode_multi)
         self.peer = None             # a connected PeerExchange routes the fixed-capacity layer through peer memory
         self.stats = None            # a list makes ep_layer append (rows sent per rank, rows received per rank) per layer
         # Received rows select few local experts each.  More than one decode-sized batch of them goes through the
@@ -407,12 +413,28 @@ class GpuBackend:
         self.ctx.check(self.lib.finch_encode_ep_peer_dispatch(self.ctx.h, self._stream(), self.peer.h, x.data_ptr(), ids.data_ptr(), weights.data_ptr(),
                                                               valid.data_ptr() if valid is not None else None))
 
+    def peer_receive(self, mask_own: bool):
+        self.ctx.check(self.lib.finch_encode_ep_peer_receive(self.ctx.h, self._stream(), self.peer.h, self.rx.data_ptr(), self.rids.data_ptr(),
+                                                             self.rw.data_ptr(), self.rv.data_ptr(), 1 if mask_own else 0))
+
     def peer_local_moe(self, layer, n, skip):
         if n > self.max_rows:
             raise ValueError(f"{n} rows, backend sized for {self.max_rows}")
-        self.ctx.check(self.lib.finch_encode_ep_peer_receive(self.ctx.h, self._stream(), self.peer.h, self.rx.data_ptr(), self.rids.data_ptr(),
-                                                             self.rw.data_ptr(), self.rv.data_ptr()))
+        self.peer_receive(True)
         return self._moe_rows(layer, n, skip)
+
+    def can_multi(self, T, world):
+        """finch_encode_moe_decode_multi takes the layer: decode-sized batches, one per rank."""
+        c = self.ctx.cfg
+        return self.multi and T <= 8 and T * self.K <= 64 and world <= 16 and T * world <= min(c.max_tokens, self.max_rows)
+
+    def peer_local_multi(self, layer, T, world, rank, shared, h_mid, out):
+        self.peer_receive(False)
+        self.ctx.check(self.lib.finch_encode_moe_decode_multi(
+            self.ctx.h, self._stream(), self.pool.h, layer, world, T, self.rx.data_ptr(), self.rids.data_ptr(), self.rw.data_ptr(), self.rv.data_ptr(),
+            rank, C.byref(shared) if shared is not None else None, h_mid.data_ptr() if h_mid is not None else None, out.data_ptr(),
+            self.rout.data_ptr()))
+        return self.rout[:T * world]
 
     def peer_return(self, part):
         self.ctx.check(self.lib.finch_encode_ep_peer_return(self.ctx.h, self._stream(), self.peer.h, part.data_ptr()))

@@ -72,6 +72,7 @@ _PROTOS = {
     "finch_encode_batch_matvec": (_i, [_vp, _vp, _vp, _i, C.POINTER(WDesc), C.POINTER(_vp), _i, _i]),
     "finch_encode_route_topk": (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp, _i]),
     "finch_encode_moe_decode": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, C.POINTER(Shared), _vp, _vp, _i]),
+    "finch_encode_moe_decode_multi": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _i, C.POINTER(Shared), _vp, _vp, _vp]),
     "finch_encode_moe_prefill": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, C.POINTER(Shared), _vp, _vp, _i]),
     "finch_set_prefill_mode": (_i, [_vp, _i]),
     "finch_set_prefill_chunk": (_i, [_vp, _i]),
@@ -90,7 +91,7 @@ _PROTOS = {
     "finch_ep_peer_reset": (_i, [_vp]),
     "finch_ep_peer_destroy": (_i, [_vp]),
     "finch_encode_ep_peer_dispatch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
-    "finch_encode_ep_peer_receive": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "finch_encode_ep_peer_receive": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i]),
     "finch_encode_ep_peer_return": (_i, [_vp, _vp, _vp, _vp]),
     "finch_encode_ep_peer_combine": (_i, [_vp, _vp, _vp, _vp]),
     "finch_pool_fill_synthetic_range": (_i, [_vp, _i, _i, _i, _i, C.c_uint64]),

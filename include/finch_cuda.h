@@ -327,14 +327,28 @@ FINCH_API int finch_encode_ep_unpack(finch_ctx *ctx, finch_stream stream, const 
 /* hidden_out[t] += sum over destinations d in ascending order of back_rows[offs[d] + slot_of[t][d]]. */
 FINCH_API int finch_encode_ep_combine(finch_ctx *ctx, finch_stream stream, float *hidden_out, const float *back_rows,
                                       const int *slot_of, const int *offs, int T, int world);
+/* n_batches independent decode-sized batches of B tokens (B <= 8, B * top_k <= FINCH_MAX_PAIRS,
+ * n_batches <= 16, n_batches * B <= max_tokens) in one sequence of three launches: rows
+ * [c * B, (c + 1) * B) of h_post / expert_ids / weights / valid are batch c, and the SMs are divided
+ * among the batches.  Batch own_batch is finch_encode_moe_decode as it stands (h_mid, shared expert,
+ * result in hidden_out [B][hidden]); every other batch gets the weighted sum over its usable routed
+ * experts only, in rows_out[c * B + t] (row block own_batch of rows_out is not written).  This is the
+ * per-layer call of an expert-parallel rank for decode: batch c holds the tokens of rank c, most of
+ * whose experts are not in this rank's pool and are skipped. */
+FINCH_API int finch_encode_moe_decode_multi(finch_ctx *ctx, finch_stream stream, finch_pool *pool, int layer, int n_batches, int B,
+                                            const void *h_post, const int32_t *expert_ids, const float *weights,
+                                            const uint8_t *valid, int own_batch, const finch_shared *shared, const float *h_mid,
+                                            float *hidden_out, float *rows_out);
+
 /* ---- the fixed-capacity exchange over NVLink peer memory (decode-sized batches: every rank owns
  * tokens_per_rank tokens and sends each to every rank).  The ranks' kernels store records and partial
  * rows into each other's receive areas and wait on one flag per slot: no collective call and no host
  * step per layer, so a layer is a fixed sequence of launches that a CUDA graph can hold.  Setup, once:
  * every rank creates its area, exports a 64-byte handle, receives the other ranks' handles by whatever
  * channel the host has (the MPI / NCCL bootstrap, a file) and imports them.  Per layer, every rank, in
- * this order: dispatch -> (finch_encode_moe_decode on its own tokens) -> receive ->
- * finch_encode_moe_prefill on the world * tokens_per_rank received rows -> return -> combine.
+ * this order: dispatch -> receive -> finch_encode_moe_decode_multi on the world batches of received rows
+ * (or: finch_encode_moe_decode on its own tokens, receive with mask_own, finch_encode_moe_prefill on the
+ * received rows) -> return -> combine.
  * Every device-side wait is bounded: a flag that does not arrive records FINCH_E_TIMEOUT in the
  * device status word, the slot counts as empty and later waits no longer spin; the host then calls
  * finch_ep_peer_reset on every rank (after a barrier) or falls back to the all-to-all steps above. */
@@ -349,9 +363,11 @@ FINCH_API int finch_ep_peer_reset(finch_ep_peer *peer);                         
 FINCH_API int finch_ep_peer_destroy(finch_ep_peer *peer);
 FINCH_API int finch_encode_ep_peer_dispatch(finch_ctx *ctx, finch_stream stream, finch_ep_peer *peer, const void *h_post,
                                             const int32_t *expert_ids, const float *weights, const uint8_t *valid);
-/* Rows [world * tokens_per_rank] in source-rank order; the block of this rank's own tokens gets an all-zero mask. */
+/* Rows [world * tokens_per_rank] in source-rank order, this rank's own tokens among them (dispatch stores them into
+ * its own area too).  mask_own != 0: the block of the rank's own tokens gets an all-zero mask (the caller has served
+ * them in place); 0: it is an ordinary block, as finch_encode_moe_decode_multi wants it. */
 FINCH_API int finch_encode_ep_peer_receive(finch_ctx *ctx, finch_stream stream, finch_ep_peer *peer, void *h_post,
-                                           int32_t *expert_ids, float *weights, uint8_t *valid);
+                                           int32_t *expert_ids, float *weights, uint8_t *valid, int mask_own);
 /* rows: fp32 [world * tokens_per_rank][hidden], block s = the partial sums of rank s's tokens. */
 FINCH_API int finch_encode_ep_peer_return(finch_ctx *ctx, finch_stream stream, finch_ep_peer *peer, const float *rows);
 /* hidden_out[t] += the other ranks' partial rows of token t, in ascending rank order. */

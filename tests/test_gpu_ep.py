@@ -141,7 +141,8 @@ def _two_ranks_one_process(api, T=8):
     return blocks, sh, ranks
 
 
-def test_peer_exchange_two_ranks_in_one_process_match_oracle():
+@pytest.mark.parametrize("multi", [False, True])
+def test_peer_exchange_two_ranks_in_one_process_match_oracle(multi):
     """The exchange through peer memory (dispatch / receive / return / combine with one flag per slot), its two
     ranks run from one process on one GPU: each step of both ranks is launched before the step that waits for it, so
     no kernel ever waits for one that has not run.  Twice, so that the cleared flags are exercised."""
@@ -172,8 +173,12 @@ def test_peer_exchange_two_ranks_in_one_process_match_oracle():
             torch.cuda.synchronize()
             for r, (ctx, pool, be) in enumerate(ranks):
                 with be.stream_scope():
-                    be.home(0, *inputs[r][6:10], inputs[r][10], inputs[r][11], outs[r])
-                    part = be.peer_local_moe(0, 2 * T, (r * T, T))
+                    if multi:       # every rank's batch, the rank's own among them, in one launch sequence
+                        assert be.can_multi(T, 2)
+                        part = be.peer_local_multi(0, T, 2, r, inputs[r][10], inputs[r][11], outs[r])
+                    else:
+                        be.home(0, *inputs[r][6:10], inputs[r][10], inputs[r][11], outs[r])
+                        part = be.peer_local_moe(0, 2 * T, (r * T, T))
                     be.peer_return(part)
             torch.cuda.synchronize()
             for r, (ctx, pool, be) in enumerate(ranks):
@@ -186,7 +191,7 @@ def test_peer_exchange_two_ranks_in_one_process_match_oracle():
                                                   np.array([1 if (valid[t, k] and int(e) in blocks) else 0 for k, e in enumerate(ids[t])], np.uint8),
                                                   x[t], bits=3, scale_dtype=oracle.SCALE_BF16, hidden=H, inter=I, h_mid=h_mid[t], shared=sh,
                                                   shared_gate_score=float(score[t])) for t in range(T)])
-                assert_close(outs[r].cpu().numpy(), want, f"peer exchange, rank {r}, pass {rep}")
+                assert_close(outs[r].cpu().numpy(), want, f"peer exchange, rank {r}, pass {rep}, multi={multi}")
                 assert ctx.device_status() == 0
     finally:
         for ctx, pool, be in ranks:
@@ -208,8 +213,7 @@ def test_peer_receive_wait_runs_out_and_reports_timeout():
         be.peer.set_wait_limit(2000)
         be.rv.fill_(1)
         with be.stream_scope():
-            be.ctx.check(be.lib.finch_encode_ep_peer_receive(ctx.h, be._stream(), be.peer.h, be.rx.data_ptr(), be.rids.data_ptr(),
-                                                             be.rw.data_ptr(), be.rv.data_ptr()))
+            be.peer_receive(True)
         torch.cuda.synchronize()
         assert ctx.device_status() == L.E_TIMEOUT
         assert int(be.rv[:2 * T].sum().item()) == 0            # nothing arrived: every row is masked

@@ -648,3 +648,58 @@ def test_pool_put_between_decode_calls_with_fewer_slots_than_experts(api):
     finally:
         pool.destroy()
         ctx.destroy()
+
+
+@pytest.mark.parametrize("n_batches,B,own", [(2, 8, 1), (8, 8, 3), (4, 5, 0), (16, 2, 15)])
+def test_moe_decode_multi_equals_the_batches_one_by_one(api, n_batches, B, own):
+    """finch_encode_moe_decode_multi at full size (hidden 2048, inter 512, 256 experts, top-8): the pool holds the
+    experts of one expert-parallel rank (every n_batches-th block of them), so most pairs of every row are skipped.
+    Every batch must equal, bit for bit, what finch_encode_moe_decode gives for it alone (the own batch with h_mid
+    and the shared expert, the others routed sums only); the own batch is also held against the oracle."""
+    import torch
+    ctx = api.Context(max_tokens=n_batches * B, n_layers=1)
+    per = 256 // n_batches
+    pool = ctx.pool(n_layers=1, max_slots=per)
+    try:
+        rng = synth.rng_for(31, n_batches * 100 + B)
+        blocks = {}
+        for e in range(own * per, (own + 1) * per):        # this rank's contiguous block of experts
+            blocks[e] = synth.expert_block(rng, scale_dtype=L.FP16)
+            pool.put(0, e, blocks[e])
+        R = n_batches * B
+        perm = synth.zipf_popularity(rng, 256)
+        ids, w = synth.zipf_routing_shared(rng, R, perm, 8)
+        valid = (rng.random((R, 8)) > 0.05).astype(np.uint8)
+        x = synth.activations(rng, R, 2048)
+        sh = synth.shared_expert(rng, scale_dtype=L.FP16)
+        score = rng.normal(0, 1, size=B).astype(np.float32)
+        h_mid = synth.activations(rng, B, 2048)
+        d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        xd = d(x).to(torch.bfloat16)
+        idd, wd, vd, hd, sd = d(ids), d(w), d(valid), d(h_mid), d(score)
+        shd = ctx.make_shared(*[ctx.upload_tensor(t) for t in sh], gate_score=sd)
+        out = torch.zeros((B, 2048), dtype=torch.float32, device="cuda")
+        rows = torch.full((R, 2048), 7.0, dtype=torch.float32, device="cuda")
+        import ctypes as C
+        ctx.check(ctx.lib.finch_encode_moe_decode_multi(ctx.h, None, pool.h, 0, n_batches, B, xd.data_ptr(), idd.data_ptr(), wd.data_ptr(), vd.data_ptr(),
+                                                        own, C.byref(shd), hd.data_ptr(), out.data_ptr(), rows.data_ptr()))
+        ctx.sync()
+        torch.cuda.synchronize()
+        one = torch.empty((B, 2048), dtype=torch.float32, device="cuda")
+        for c in range(n_batches):
+            sl = slice(c * B, (c + 1) * B)
+            if c == own:
+                ctx.encode_moe_decode(pool, 0, xd[sl], idd[sl], wd[sl], vd[sl], shd, hd, one, B)
+            else:
+                ctx.encode_moe_decode(pool, 0, xd[sl], idd[sl], wd[sl], vd[sl], None, None, one, B)
+            ctx.sync()
+            got = out if c == own else rows[sl]
+            assert torch.equal(got, one), f"batch {c} differs from the single call"
+        assert torch.all(rows[own * B:(own + 1) * B] == 7.0)           # the own block of rows_out is left alone
+        sl = slice(own * B, (own + 1) * B)
+        want = _oracle_layer(blocks, ids[sl], w[sl], valid[sl], x[sl], dict(hidden=2048, inter=512, sd=L.FP16), shared=sh, score=score, h_mid=h_mid)
+        assert_close(out.cpu().numpy(), want, f"own batch of {n_batches} x {B}")
+        assert ctx.device_status() == 0
+    finally:
+        pool.destroy()
+        ctx.destroy()
