@@ -50,6 +50,12 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
     return v;
 }
 
+// Programmatic dependent launch: a kernel of the chain may be scheduled while its predecessor still runs.  Every
+// kernel here executes dep_wait() before it exits, so "my predecessor has completed" holds transitively along the
+// stream; a kernel that needs nothing its predecessor wrote does its work first and waits last.
+__device__ __forceinline__ void dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // One thread waits for a slot's flag.  False: it did not arrive (recorded), the slot is to be treated as empty.
 __device__ bool wait_flag(const uint32_t *flag, int *status, long long limit) {
     if (ld_acquire_sys(flag) == 1u) return true;
@@ -66,6 +72,8 @@ __device__ bool wait_flag(const uint32_t *flag, int *status, long long limit) {
 __global__ void __launch_bounds__(128) peer_dispatch_kernel(Areas areas, int rank, int T, const uint8_t *x, const int32_t *ids, const float *weights,
                                                             const uint8_t *valid, int row_bytes, int K, int rec_bytes, size_t off_rflag) {
     const int t = blockIdx.x, d = blockIdx.y;   // d == rank: my own area (the rank's tokens take the same route)
+    dep_wait();        // the activations are the work of what ran before
+    dep_launch();
     uint8_t *area = areas.p[d];
     uint8_t *rec = area + (size_t)(rank * T + t) * rec_bytes;
     const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)t * row_bytes);
@@ -91,10 +99,14 @@ __global__ void __launch_bounds__(128) peer_receive_kernel(uint8_t *area, int ra
     const int i = blockIdx.x, src_rank = i / T;
     const bool masked = mask_own && src_rank == rank;   // my own tokens are served in place by the caller: their rows select nothing
     uint32_t *flag = reinterpret_cast<uint32_t *>(area + off_rflag) + i;
+    dep_launch();
+    // The records are ordered by their flags, and the row arrays were last read by kernels that completed before the
+    // dispatch kernel passed its wait (which is before this grid could start): no wait for the predecessor up front.
     if (threadIdx.x == 0) ok = wait_flag(flag, status, limit) ? 1 : 0;
     __syncthreads();
     if (!ok) {
         if (threadIdx.x < K) valid[i * K + threadIdx.x] = 0;
+        dep_wait();
         return;
     }
     const uint8_t *rec = area + (size_t)i * rec_bytes;
@@ -109,11 +121,14 @@ __global__ void __launch_bounds__(128) peer_receive_kernel(uint8_t *area, int ra
     }
     __syncthreads();
     if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t *>(flag) = 0u;
+    dep_wait();
 }
 
 // grid (T, world), 256 threads: partial row of source s's token t -> rank s's area
 __global__ void __launch_bounds__(256) peer_return_kernel(Areas areas, int rank, int T, const float *rows, int hidden, size_t off_back, size_t off_bflag) {
     const int t = blockIdx.x, s = blockIdx.y;
+    dep_wait();        // the rows are the predecessor's output
+    dep_launch();
     if (s == rank) return;
     uint8_t *area = areas.p[s];
     const float4 *src = reinterpret_cast<const float4 *>(rows + (size_t)(s * T + t) * hidden);
@@ -132,6 +147,9 @@ __global__ void __launch_bounds__(256) peer_combine_kernel(uint8_t *area, int ra
     __shared__ int ok[MAXW];
     const int t = blockIdx.x;
     uint32_t *flags = reinterpret_cast<uint32_t *>(area + off_bflag);
+    dep_launch();
+    // hidden_out was written two kernels back; the return kernel in between passed its wait before this grid could
+    // start, so that writer has completed.  The peers' rows are ordered by their flags.
     if (threadIdx.x < world) {
         const int d = threadIdx.x;
         ok[d] = d != rank && wait_flag(flags + d * T + t, status, limit);
@@ -153,6 +171,21 @@ __global__ void __launch_bounds__(256) peer_combine_kernel(uint8_t *area, int ra
     }
     __syncthreads();
     if (threadIdx.x < world && ok[threadIdx.x]) *reinterpret_cast<volatile uint32_t *>(flags + threadIdx.x * T + t) = 0u;
+    dep_wait();
+}
+
+template <typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Args...), dim3 grid, int threads, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(threads);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 Areas areas_of(const finch_ep_peer *p) {
@@ -266,10 +299,8 @@ extern "C" int finch_encode_ep_peer_dispatch(finch_ctx *ctx, finch_stream stream
     const int elt = c.act_dtype == FINCH_BF16 ? 2 : 4, row_bytes = c.hidden * elt;
     if (row_bytes % 16) return finch_fail(ctx, FINCH_E_ARG, "activation rows must be multiples of 16 bytes");
     cudaSetDevice(c.device);
-    peer_dispatch_kernel<<<dim3(p->T, p->world), 128, 0, finch_pick_stream(ctx, stream)>>>(areas_of(p), p->rank, p->T, (const uint8_t *)h_post, expert_ids, weights,
-                                                                                            valid, row_bytes, c.top_k, rec_bytes_of(c.hidden, elt, c.top_k),
-                                                                                            p->off_rflag);
-    FINCH_CUDA_OK(ctx, cudaGetLastError());
+    FINCH_CUDA_OK(ctx, launch_pdl(peer_dispatch_kernel, dim3(p->T, p->world), 128, finch_pick_stream(ctx, stream), areas_of(p), p->rank, p->T,
+                                  (const uint8_t *)h_post, expert_ids, weights, valid, row_bytes, c.top_k, rec_bytes_of(c.hidden, elt, c.top_k), p->off_rflag));
     ctx->launches++;
     return FINCH_OK;
 }
@@ -280,10 +311,9 @@ extern "C" int finch_encode_ep_peer_receive(finch_ctx *ctx, finch_stream stream,
     const finch_config &c = ctx->cfg;
     const int elt = c.act_dtype == FINCH_BF16 ? 2 : 4;
     cudaSetDevice(c.device);
-    peer_receive_kernel<<<p->world * p->T, 128, 0, finch_pick_stream(ctx, stream)>>>(p->area, p->rank, p->T, c.hidden * elt, c.top_k,
-                                                                                      rec_bytes_of(c.hidden, elt, c.top_k), p->off_rflag, (uint8_t *)h_post,
-                                                                                      expert_ids, weights, valid, ctx->dev_status, p->limit, mask_own);
-    FINCH_CUDA_OK(ctx, cudaGetLastError());
+    FINCH_CUDA_OK(ctx, launch_pdl(peer_receive_kernel, dim3(p->world * p->T), 128, finch_pick_stream(ctx, stream), p->area, p->rank, p->T, c.hidden * elt,
+                                  c.top_k, rec_bytes_of(c.hidden, elt, c.top_k), p->off_rflag, (uint8_t *)h_post, expert_ids, weights, valid, ctx->dev_status,
+                                  p->limit, mask_own));
     ctx->launches++;
     return FINCH_OK;
 }
@@ -294,9 +324,8 @@ extern "C" int finch_encode_ep_peer_return(finch_ctx *ctx, finch_stream stream, 
     if (rc) return rc;
     if (p->world == 1) return FINCH_OK;
     cudaSetDevice(ctx->cfg.device);
-    peer_return_kernel<<<dim3(p->T, p->world), 256, 0, finch_pick_stream(ctx, stream)>>>(areas_of(p), p->rank, p->T, rows, ctx->cfg.hidden, p->off_back,
-                                                                                          p->off_bflag);
-    FINCH_CUDA_OK(ctx, cudaGetLastError());
+    FINCH_CUDA_OK(ctx, launch_pdl(peer_return_kernel, dim3(p->T, p->world), 256, finch_pick_stream(ctx, stream), areas_of(p), p->rank, p->T, rows,
+                                  ctx->cfg.hidden, p->off_back, p->off_bflag));
     ctx->launches++;
     return FINCH_OK;
 }
@@ -305,9 +334,8 @@ extern "C" int finch_encode_ep_peer_combine(finch_ctx *ctx, finch_stream stream,
     if (!ctx || !p || p->ctx != ctx || !hidden_out) return FINCH_E_ARG;
     if (p->world == 1) return FINCH_OK;
     cudaSetDevice(ctx->cfg.device);
-    peer_combine_kernel<<<p->T, 256, 0, finch_pick_stream(ctx, stream)>>>(p->area, p->rank, p->world, p->T, hidden_out, ctx->cfg.hidden, p->off_back,
-                                                                           p->off_bflag, ctx->dev_status, p->limit);
-    FINCH_CUDA_OK(ctx, cudaGetLastError());
+    FINCH_CUDA_OK(ctx, launch_pdl(peer_combine_kernel, dim3(p->T), 256, finch_pick_stream(ctx, stream), p->area, p->rank, p->world, p->T, hidden_out,
+                                  ctx->cfg.hidden, p->off_back, p->off_bflag, ctx->dev_status, p->limit));
     ctx->launches++;
     return FINCH_OK;
 }
