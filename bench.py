@@ -939,7 +939,31 @@ def aux_rooflines(stack, peaks, peak_kind, iters=8):
             ceil = min(peaks["bf16_tflops"], fl / b * peaks["hbm_gbs"] / 1e3)
             rows.append({"op": "dense_gemm_4bit_g64_tcgen05", "shape": list(shape), "T": T, "us": secs * 1e6, "tflops": fl / secs / 1e12,
                          "gbs": b / secs / 1e9, "ceiling_tflops": ceil, "frac_" + peak_kind: fl / secs / 1e12 / ceil})
-    # the output projection (lm_head tier): 248,320 rows of 2048, device-generated bytes
+    rows += lm_head_rows(stack, peaks, peak_kind, timed)
+    return rows
+
+
+def lm_head_rows(stack, peaks, peak_kind, timed=None, iters=8):
+    """The output projection (lm_head tier): 248,320 rows of 2048 in 8 and 4 bits, device-generated bytes, one
+    position.  The tensor is larger than L2 by itself, so nothing is flushed between the timed launches."""
+    import torch
+    ctx, L, st = stack.ctx, stack.L, stack.stream
+    rng = synth.rng_for(4, 0, 98)
+    if timed is None:
+        def timed(fn, do_flush=True):
+            fn()
+            torch.cuda.synchronize()
+            tot = 0.0
+            for _ in range(iters):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(st):
+                    e0.record(st)
+                    fn()
+                    e1.record(st)
+                torch.cuda.synchronize()
+                tot += e0.elapsed_time(e1)
+            return tot / iters * 1e-3
+    rows = []
     rows_out, in_dim = 248320, 2048
     for bits in (8, 4):
         Wd = torch.randint(0, 256, (rows_out, in_dim * bits // 8), dtype=torch.uint8, device="cuda")
@@ -951,7 +975,7 @@ def aux_rooflines(stack, peaks, peak_kind, iters=8):
         secs = timed(lambda: ctx.fast_batch_matvec(x, L.BF16, [w], [out], M=1, stream=st.cuda_stream), do_flush=False)
         b = Wd.numel() + Sd.numel() * 2 + Bd.numel() * 2 + in_dim * 2 + rows_out * 4
         rows.append({"op": f"lm_head_matvec_{bits}bit_g64", "shape": [rows_out, in_dim], "T": 1, "us": secs * 1e6, "gbs": b / secs / 1e9,
-                     "frac_hbm_" + peak_kind: b / secs / 1e9 / peaks["hbm_gbs"]})
+                     "bytes": int(b), "frac_hbm_" + peak_kind: b / secs / 1e9 / peaks["hbm_gbs"]})
         del Wd, Sd, Bd
     return rows
 
@@ -1000,7 +1024,8 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS, help="fewer layers = a small case for profiler captures")
     ap.add_argument("--no-graph", action="store_true", help="launch from the host every step instead of replaying CUDA graphs")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"], help="N > 1, decode: the ranks' own kernels over peer memory, or NCCL all-to-alls")
-    ap.add_argument("--only", default="", choices=["", "prefill", "decode"], help="just the 512-token chunk, or just the batch-8 decode steps, on --layers layers (profiler captures)")
+    ap.add_argument("--only", default="", choices=["", "prefill", "decode", "lmhead"],
+                    help="just the 512-token chunk, just the batch-8 decode steps (both on --layers layers), or just the output-projection matvecs (profiler captures)")
     args = ap.parse_args()
     LAYERS = args.layers
     if args.only == "prefill":
@@ -1015,6 +1040,10 @@ def main():
         secs, per_step = stack.time_steps(dev, xd, score, out, 8, args.steps, args.warmup, use_graph=not args.no_graph)
         print(json.dumps({"only": "decode", "layers": LAYERS, "ms_per_step": secs / args.steps * 1e3, "step_ms": spread(per_step),
                           "status": stack.ctx.device_status()}))
+    elif args.only == "lmhead":
+        stack = Stack(0, max_tokens=8, layers=1)
+        peaks, peak_kind = measured_peaks()
+        print(json.dumps({"only": "lmhead", "rows": lm_head_rows(stack, peaks, peak_kind, iters=max(1, args.steps)), "status": stack.ctx.device_status()}))
     elif args.impl == "reference":
         run_reference(args)
     else:
