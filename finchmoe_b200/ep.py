@@ -169,15 +169,19 @@ def _ep_layer_static(backend, dist, group, layer, x, ids, weights, valid, shared
     h = backend.static_plan(T, world, rank if direct else -1)
     rec, H, n = backend.record_bytes(), backend.hidden, T * world
     send_buf = backend.pack(h, x, ids, weights, valid, n)
+    multi = direct and hasattr(backend, "can_multi") and backend.can_multi(T, world)
     if world > 1:
         recv_buf = backend.empty_bytes(n * rec)
         work = dist.all_to_all_single(recv_buf, send_buf, group=group, async_op=True)    # equal splits: T records per peer
-        if direct:
+        if direct and not multi:
             backend.home(layer, x, ids, weights, valid, shared, h_mid, out)
         work.wait()
     else:
         recv_buf = send_buf
-    part = backend.local_moe(layer, recv_buf, n, (rank * T, T) if direct else None)   # fp32 [n, H], source-major
+    if multi:      # every rank's batch, the rank's own among them (h_mid, shared expert), in one launch sequence
+        part = backend.local_multi(layer, recv_buf, T, world, rank, shared, h_mid, out)
+    else:
+        part = backend.local_moe(layer, recv_buf, n, (rank * T, T) if direct else None)   # fp32 [n, H], source-major
     if world > 1:
         back = backend.empty_f32(n * H)
         dist.all_to_all_single(back, part.reshape(-1), group=group)
@@ -428,8 +432,16 @@ class GpuBackend:
         c = self.ctx.cfg
         return self.multi and T <= 8 and T * self.K <= 64 and world <= 16 and T * world <= min(c.max_tokens, self.max_rows)
 
+    def local_multi(self, layer, recv_buf, T, world, rank, shared, h_mid, out):
+        self.ctx.check(self.lib.finch_encode_ep_unpack(self.ctx.h, self._stream(), recv_buf.data_ptr(), T * world, self.rx.data_ptr(),
+                                                       self.rids.data_ptr(), self.rw.data_ptr(), self.rv.data_ptr()))
+        return self._multi_rows(layer, T, world, rank, shared, h_mid, out)
+
     def peer_local_multi(self, layer, T, world, rank, shared, h_mid, out):
         self.peer_receive(False)
+        return self._multi_rows(layer, T, world, rank, shared, h_mid, out)
+
+    def _multi_rows(self, layer, T, world, rank, shared, h_mid, out):
         self.ctx.check(self.lib.finch_encode_moe_decode_multi(
             self.ctx.h, self._stream(), self.pool.h, layer, world, T, self.rx.data_ptr(), self.rids.data_ptr(), self.rw.data_ptr(), self.rv.data_ptr(),
             rank, C.byref(shared) if shared is not None else None, h_mid.data_ptr() if h_mid is not None else None, out.data_ptr(),

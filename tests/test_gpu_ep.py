@@ -288,6 +288,23 @@ for rep in range(2):
 torch.cuda.synchronize()
 assert_close(args[-1].cpu().numpy(), want[:Ts], f"rank {rank} fixed capacity, graph replay")
 assert ctx.device_status() == 0
+# decode-sized batches (8 rows per rank): both ranks' batches in one launch sequence, over the all-to-alls
+a8 = (d(x[:8]), d(ids[:8]), d(w[:8]), d(valid[:8]), shd, d(h_mid[:8]), torch.zeros((8, H), dtype=torch.float32, device="cuda"))
+assert be.can_multi(8, world)
+ep.ep_layer_static(be, dist, None, 0, *a8)
+torch.cuda.synchronize()
+assert_close(a8[-1].cpu().numpy(), want[:8], f"rank {rank} multi-batch decode over NCCL")
+# ... and through peer memory
+px8 = ep.PeerExchange.connect(ctx, dist, None, 8)
+assert px8 is not None, "the ranks could not map each other's receive areas"
+be.peer = px8
+for rep in range(2):
+    a8[-1].zero_()
+    ep.ep_layer_static(be, dist, None, 0, *a8)
+torch.cuda.synchronize()
+assert_close(a8[-1].cpu().numpy(), want[:8], f"rank {rank} multi-batch decode over peer memory")
+assert ctx.device_status() == 0
+dist.barrier()
 # the same layer with the exchange through peer memory instead of the all-to-alls: from the host, then from a graph
 be.peer = ep.PeerExchange.connect(ctx, dist, None, Ts)
 assert be.peer is not None, "the ranks could not map each other's receive areas"
