@@ -36,6 +36,18 @@ extern "C" const char *finch_last_error(const finch_ctx *ctx) { return ctx ? ctx
 extern "C" size_t finch_expert_bytes(const finch_ctx *ctx) { return ctx ? ctx->expert_bytes : 0; }
 extern "C" uint64_t finch_launch_count(const finch_ctx *ctx) { return ctx ? ctx->launches : 0; }
 
+int finch_func_attr_once(finch_ctx *ctx, const void *func, int smem_bytes) {
+    static std::mutex mu;
+    static std::vector<std::pair<const void *, int>> done;
+    std::lock_guard<std::mutex> lk(mu);
+    const int dev = ctx->cfg.device;
+    for (const auto &d : done)
+        if (d.first == func && d.second == dev) return FINCH_OK;
+    if (smem_bytes > 48 * 1024) FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes));
+    done.push_back({func, dev});
+    return FINCH_OK;
+}
+
 extern "C" int finch_ctx_create(const finch_config *cfg, finch_ctx **out) {
     if (!cfg || !out) return FINCH_E_ARG;
     *out = nullptr;
@@ -97,6 +109,7 @@ extern "C" void finch_ctx_destroy(finch_ctx *ctx) {
     for (auto &e : ctx->shared_cache) cudaFree(e.tiles);
     cudaFree(ctx->stage_dev);
     cudaFree(ctx->pf_ws);
+    cudaFree(ctx->gq_ws);
     cudaFree(ctx->gguf_ws);
     cudaFree(ctx->logits);
     if (ctx->stage_host) cudaFreeHost(ctx->stage_host);

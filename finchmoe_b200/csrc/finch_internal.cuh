@@ -44,6 +44,8 @@ struct finch_ctx {
     float *logits = nullptr;        // [max_tokens][n_experts] router logits (finch_encode_router, allocated on first use)
     void *gguf_ws = nullptr;        // scratch of finch_encode_moe_gguf (allocated on first use)
     size_t gguf_ws_bytes = 0;
+    void *gq_ws = nullptr;          // activation planes of the GGUF many-position matvec (matvec_gguf_mma.cu)
+    size_t gq_ws_bytes = 0;
     int prefill_chunk = 0;          // finch_set_prefill_chunk: tokens per tensor-core pass, 0 = 512
     int prefill_mode = 0;           // finch_set_prefill_mode: 0 by chunk length, 1 sub-batches through decode, 2 tensor cores
     uint64_t launches = 0;
@@ -90,6 +92,9 @@ int finch_fail(finch_ctx *ctx, int code, const char *fmt, ...);
 static inline cudaStream_t finch_pick_stream(finch_ctx *ctx, finch_stream s) {
     return s ? (cudaStream_t)s : ctx->stream;
 }
+
+// Opt-in to more than 48 KB of dynamic shared memory: a per-device function attribute, set once per (function, device).
+int finch_func_attr_once(finch_ctx *ctx, const void *func, int smem_bytes);
 
 // Implemented in moe_decode.cu / moe_prefill.cu, used by the host-pointer entry point.
 int finch_validate_wdesc(finch_ctx *ctx, const finch_wdesc *w, const char *what);

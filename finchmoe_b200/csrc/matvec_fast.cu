@@ -367,17 +367,16 @@ __global__ void __launch_bounds__(FNT, 1) fast_matvec_kernel(FPack pack, const v
     }
 }
 
-bool g_fast_attr[10] = {false, false, false, false, false, false, false, false, false, false};
-
 template <int BITS>
 int launch_fast(finch_ctx *ctx, cudaStream_t st, const FPack &pack, const void *x, int x_dtype, int M, int K, int max_out, int slot) {
     const int Kp = (K + 1023) & ~1023;
     const size_t smem = ((size_t)M * Kp + (size_t)M * (Kp / 32) + (size_t)M * (Kp / 16)) * sizeof(float);
     const int one = M == 1;   // a single position gets its own instantiation (fewer registers, same code)
-    if (!g_fast_attr[2 * slot + one]) {
-        if (one) FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(fast_matvec_kernel<BITS, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        else FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(fast_matvec_kernel<BITS, FM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        g_fast_attr[2 * slot + one] = true;
+    {   // the shared-memory opt-in is a per-device attribute of each instantiation
+        const int rc = one ? finch_func_attr_once(ctx, (const void *)fast_matvec_kernel<BITS, 1>, 200 * 1024)
+                           : finch_func_attr_once(ctx, (const void *)fast_matvec_kernel<BITS, FM>, 200 * 1024);
+        if (rc) return rc;
+        (void)slot;
     }
     int ctas = (max_out + 31) / 32;   // 16 warps x 2 rows per sweep
     if (ctas > ctx->sm_count) ctas = ctx->sm_count;

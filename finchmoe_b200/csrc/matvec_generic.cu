@@ -10,6 +10,7 @@
 
 int finch_try_fast_matvec(finch_ctx *ctx, cudaStream_t st, const void *x, int x_dtype, const finch_wdesc *specs, float *const *outs, int n, int M);
 int finch_try_stream_matvec(finch_ctx *ctx, cudaStream_t st, const void *x, int x_dtype, const finch_wdesc *specs, float *const *outs, int n, int M);
+int finch_try_gguf_mma(finch_ctx *ctx, cudaStream_t st, const void *x, int x_dtype, const finch_wdesc *specs, float *const *outs, int n, int M);
 
 namespace {
 
@@ -354,6 +355,10 @@ extern "C" int finch_encode_batch_matvec(finch_ctx *ctx, finch_stream stream, co
     cudaSetDevice(ctx->cfg.device);
     {   // a large 4- or 8-bit tensor (lm_head, the big projections) at a few positions: the tensor-core streaming kernel (matvec_stream.cu)
         const int rc = finch_try_stream_matvec(ctx, finch_pick_stream(ctx, stream), x, x_dtype, specs, outs, n, M);
+        if (rc >= 0) return rc;
+    }
+    {   // 9 and more positions of Q4_K / Q6_K tensors: one pass over the weights on the tensor cores (matvec_gguf_mma.cu)
+        const int rc = finch_try_gguf_mma(ctx, finch_pick_stream(ctx, stream), x, x_dtype, specs, outs, n, M);
         if (rc >= 0) return rc;
     }
     {   // 1..8 positions of a 3-bit / 4-bit / Q4_K tensor: the streaming kernel (matvec_fast.cu)

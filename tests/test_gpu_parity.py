@@ -131,6 +131,46 @@ def test_large_affine_matvec_streaming_kernel_vs_oracle(ctx_small, bits, o, i, M
     assert_close(out.cpu().numpy(), want, f"streaming matvec bits={bits} [{o} x {i}] M={M}")
 
 
+@pytest.mark.parametrize("ty,bits", [(12, 10), (14, 11)])
+@pytest.mark.parametrize("o,i", [(72, 512), (1001, 2048), (8192, 2048)])
+@pytest.mark.parametrize("M", [9, 33, 64, 65, 90, 128, 130])
+@pytest.mark.parametrize("xdt", [L.F32, L.BF16])
+def test_gguf_many_positions_one_pass_vs_oracle(ctx_small, ty, bits, o, i, M, xdt):
+    """Q4_K / Q6_K at 9 and more positions: one pass over the weights on the tensor cores (codes as fp16 subnormals,
+    activations as fp16 planes scaled per position).  Row counts that are not multiples of 16, position counts around
+    the tile and pass boundaries (64 per pass with fp32 activations, 128 with bf16), two tensors sharing the
+    activations, and positions whose magnitudes differ by five orders."""
+    import torch
+    if o == 8192 and M not in (9, 90, 130):
+        pytest.skip("the large shape at three position counts")
+    rng = synth.rng_for(4, ty, o + M)
+    t = synth.gguf_tensor(rng, o, i, ty)
+    t2 = synth.gguf_tensor(rng, 40, i, ty)
+    x = synth.activations(rng, M, i)
+    x[1] *= 300.0
+    x[2] *= 1.0e-3
+    if xdt == L.F32:
+        x = (x * (1.0 + rng.normal(0, 1e-3, size=x.shape))).astype(np.float32)
+        xd = torch.from_numpy(x).cuda()
+    else:
+        x = synth.bf16_to_f32(synth.f32_to_bf16_rne(x))
+        xd = torch.from_numpy(synth.f32_to_bf16_rne(x)).cuda().view(torch.bfloat16)
+    out = torch.empty((M, o), dtype=torch.float32, device="cuda")
+    out2 = torch.empty((M, 40), dtype=torch.float32, device="cuda")
+    ctx_small.fast_batch_matvec(xd, xdt, [ctx_small.upload_tensor(t), ctx_small.upload_tensor(t2)], [out, out2], M=M)
+    ctx_small.sync()
+    rows = np.arange(M) if o * i * M <= 2 ** 27 else np.sort(rng.choice(M, size=8, replace=False))
+    rows = np.union1d(rows, [1, 2])
+    want = orc.matvec(t["W"], None, None, L.FP16, x[rows], o, i, 256, bits, orc.ACC_F64)
+    got = out.cpu().numpy()
+    assert np.all(np.isfinite(got))
+    for j, r in enumerate(rows):      # row by row: the positions have very different scales
+        assert_close(got[r], want[j], f"GGUF type {ty} [{o} x {i}] M={M} position {r}")
+    want2 = orc.matvec(t2["W"], None, None, L.FP16, x[rows], 40, i, 256, bits, orc.ACC_F64)
+    assert_close(out2.cpu().numpy()[rows], want2, f"second tensor, GGUF type {ty} M={M}", tight_rel=None)
+    assert ctx_small.device_status() == 0
+
+
 def test_lm_head_tier_row_slices_vs_oracle(ctx_small):
     """The lm_head / embedding tier (finchmoe/infer.m:5728-5815): 8-bit g64 [248,320 x 2048] at one position;
     three slices of rows against the oracle."""

@@ -109,3 +109,129 @@ def test_files_load_into_pool_and_device_buffer(tmp_path):
     finally:
         pool.destroy()
         ctx.destroy()
+
+
+# ------------------------------------------------------------------ GGUF container
+def _write_gguf(path, layers, NE, H, I, alignment=None, rng=None):
+    """A GGUF v3 file written by gguf-py's own writer (an independent implementation of the format): metadata of
+    every value kind the reader has to skip, the stacked expert tensors of `layers`, one dense Q6_K matrix and an
+    F32 vector between them.  Returns what was written."""
+    import gguf
+    rng = rng or synth.rng_for(15, 1)
+    w = gguf.GGUFWriter(path, "finchtest")
+    w.add_block_count(len(layers))
+    w.add_string("general.name", "synthetic")
+    w.add_float32("finchtest.rope_base", 1.0e6)
+    w.add_bool("finchtest.flag", True)
+    w.add_uint64("finchtest.big", 1 << 40)
+    w.add_array("tokenizer.ggml.tokens", ["a", "bc", "def", ""])
+    w.add_array("finchtest.ints", [1, 2, 3, 4, 5])
+    if alignment:
+        w.add_custom_alignment(alignment)
+    written = {}
+    Q = {12: gguf.GGMLQuantizationType.Q4_K, 14: gguf.GGMLQuantizationType.Q6_K}
+    norm = rng.normal(0, 1, size=H).astype(np.float32)
+    for l, types in layers.items():
+        w.add_tensor(f"blk.{l}.attn_norm.weight", norm)
+        for which, ty, (o, i) in (("gate", types[0], (I, H)), ("up", types[1], (I, H)), ("down", types[2], (H, I))):
+            ex = [synth.gguf_tensor(rng, o, i, ty) for _ in range(NE)]
+            slab = np.stack([e["W"] for e in ex])                      # [NE, out, row_bytes]
+            w.add_tensor(f"blk.{l}.ffn_{which}_exps.weight", slab, raw_dtype=Q[ty])
+            written[(l, which)] = ex
+    dense = synth.gguf_tensor(rng, 96, H, 14)
+    w.add_tensor("output.weight", dense["W"], raw_dtype=Q[14])
+    written["output.weight"] = dense
+    written["norm"] = norm
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    return written
+
+
+@pytest.mark.parametrize("alignment", [None, 64])
+def test_gguf_container_reader_finds_every_tensor_where_the_writer_put_it(tmp_path, alignment):
+    import gguf
+    path = str(tmp_path / "m.gguf")
+    NE, H, I = 5, 512, 256
+    written = _write_gguf(path, {0: (12, 12, 14), 3: (14, 12, 12)}, NE, H, I, alignment)
+    g = loaders.GgufFile(path)
+    assert g.version == 3 and g.alignment == (alignment or 32) and g.data_offset % g.alignment == 0
+    assert sorted(g.experts) == [0, 3]
+    # the same offsets as gguf-py's reader reports
+    rd = gguf.GGUFReader(path)
+    by_name = {t.name: t for t in rd.tensors}
+    for l in (0, 3):
+        for which, (o, i) in (("gate", (I, H)), ("up", (I, H)), ("down", (H, I))):
+            e = g.experts[l][which]
+            t = by_name[f"blk.{l}.ffn_{which}_exps.weight"]
+            assert e["offset"] == t.data_offset and e["n_experts"] == NE and e["in_dim"] == i and e["out_dim"] == o
+            assert e["type"] == int(t.tensor_type)
+            for x in range(NE):
+                assert np.array_equal(g.expert_slab(l, which, x), written[(l, which)][x]["W"].reshape(-1)), (l, which, x)
+    # ordinary tensors: listed under their GGUF names with the writer's bytes
+    assert np.array_equal(g.tensor_bytes("output.weight"), written["output.weight"]["W"].reshape(-1))
+    assert g.tensors["output.weight"]["dims"] == [H, 96] and g.tensors["output.weight"]["type"] == 14
+    assert np.array_equal(g.tensor_bytes("blk.3.attn_norm.weight").view(np.float32), written["norm"])
+    assert not any("_exps" in n for n in g.tensors)
+
+
+def test_gguf_container_reader_rejects_damaged_files(tmp_path):
+    path = str(tmp_path / "m.gguf")
+    _write_gguf(path, {0: (12, 12, 14)}, 2, 256, 256)
+    raw = open(path, "rb").read()
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"GGML" + raw[4:])
+    with pytest.raises(ValueError, match="not a GGUF"):
+        loaders.GgufFile(str(bad))
+    bad.write_bytes(raw[:4] + (9).to_bytes(4, "little") + raw[8:])
+    with pytest.raises(ValueError, match="version"):
+        loaders.GgufFile(str(bad))
+    bad.write_bytes(raw[:len(raw) // 2])                    # tensor data cut off
+    with pytest.raises(ValueError, match="ends at byte|truncated|overruns"):
+        loaders.GgufFile(str(bad))
+    bad.write_bytes(raw[:40])                               # cut inside the key/value block
+    with pytest.raises(ValueError, match="truncated|overruns"):
+        loaders.GgufFile(str(bad))
+
+
+@pytest.mark.gpu
+def test_gguf_file_experts_on_the_device_vs_oracle(tmp_path):
+    """A GGUF file's stacked expert tensors loaded by the container reader and run through finch_encode_moe_gguf,
+    and its dense Q6_K matrix through the matvec seam, against the oracle."""
+    import torch
+    from finchmoe_b200 import api
+    from oracle import oracle
+    from parity import assert_close
+    path = str(tmp_path / "m.gguf")
+    NE, H, I, K, B = 6, 512, 256, 4, 3
+    written = _write_gguf(path, {1: (12, 12, 14)}, NE, H, I)
+    g = loaders.GgufFile(path)
+    ctx = api.Context(hidden=H, n_experts=NE, top_k=K, moe_inter=I, shared_inter=256, n_layers=2, act_dtype=L.F32, max_tokens=4)
+    try:
+        ge = g.upload_experts(ctx, 1)
+        rng = synth.rng_for(15, 2)
+        x = rng.normal(0, 1, size=(B, H)).astype(np.float32)
+        ids = np.stack([rng.permutation(NE)[:K] for _ in range(B)]).astype(np.int32)
+        w = rng.random((B, K)).astype(np.float32)
+        w /= w.sum(axis=1, keepdims=True)
+        d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        out = torch.empty((B, H), dtype=torch.float32, device="cuda")
+        ctx.encode_moe_gguf(ge, d(x), d(ids), d(w), None, None, out, B)
+        ctx.sync()
+
+        def mv(t, v):
+            return oracle.matvec(t["W"], None, None, 1, v, t["out_dim"], t["in_dim"], 256, t["bits"])
+        want = np.zeros((B, H), np.float32)
+        for b in range(B):
+            for k in range(K):
+                e = int(ids[b, k])
+                act = oracle.swiglu(mv(written[(1, "gate")][e], x[b]), mv(written[(1, "up")][e], x[b]))
+                want[b] += w[b, k] * mv(written[(1, "down")][e], act)
+        assert_close(out.cpu().numpy(), want, "experts of a GGUF file")
+        wd = g.wdesc(ctx, "output.weight")
+        got = ctx.fast_dequant_matvec(wd, x)
+        assert_close(got, mv(written["output.weight"], x), "dense Q6_K matrix of a GGUF file")
+        assert ctx.device_status() == 0
+    finally:
+        ctx.destroy()
