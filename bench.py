@@ -940,6 +940,39 @@ def aux_rooflines(stack, peaks, peak_kind, iters=8):
             rows.append({"op": "dense_gemm_4bit_g64_tcgen05", "shape": list(shape), "T": T, "us": secs * 1e6, "tflops": fl / secs / 1e12,
                          "gbs": b / secs / 1e9, "ceiling_tflops": ceil, "frac_" + peak_kind: fl / secs / 1e12 / ceil})
     rows += lm_head_rows(stack, peaks, peak_kind, timed)
+    rows += gguf_expert_rows(stack, peaks, peak_kind, timed)
+    return rows
+
+
+def gguf_expert_rows(stack, peaks, peak_kind, timed):
+    """The GGUF expert MLP (Q4_K gate / up, Q6_K down: the Q4_K_M mix) of a 90-token prefill chunk and of one decode
+    token at the model's size, from stacked slabs of all 256 experts (device-generated codes, |N(0, 0.01)| block
+    scales).  bytes = the distinct selected experts' slabs."""
+    import torch
+    ctx, L, st = stack.ctx, stack.L, stack.stream
+    rng = synth.rng_for(4, 0, 97)
+
+    def slab(rows, cols, block, d_at, n_d):
+        nb = cols // 256
+        W = torch.randint(0, 256, (NEXP, rows, nb, block), dtype=torch.uint8, device="cuda")
+        d = (torch.randn((NEXP, rows, nb, n_d), device="cuda").abs() * 0.01).to(torch.float16)
+        W[..., d_at:d_at + 2 * n_d] = d.view(torch.uint8).reshape(NEXP, rows, nb, 2 * n_d)
+        return W
+    gate, up, down = slab(INTER, HIDDEN, 144, 0, 2), slab(INTER, HIDDEN, 144, 0, 2), slab(HIDDEN, INTER, 210, 208, 1)
+    ge = L.GgufExperts(gate.data_ptr(), up.data_ptr(), down.data_ptr(), gate[0].numel(), up[0].numel(), down[0].numel(), 10, 10, 11)
+    per_expert = gate[0].numel() + up[0].numel() + down[0].numel()
+    rows = []
+    perm = layer_popularity(0)
+    for T in (1, 90):
+        ids, w = synth.zipf_routing_shared(rng, T, perm, TOPK)
+        x = torch.from_numpy(synth.activations(rng, T, HIDDEN)).cuda().to(torch.bfloat16)
+        idd, wd = torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda()
+        out = torch.empty((T, HIDDEN), dtype=torch.float32, device="cuda")
+        secs = timed(lambda: ctx.encode_moe_gguf(ge, x, idd, wd, None, None, out, T, stream=st.cuda_stream))
+        b = len(set(ids.ravel().tolist())) * per_expert
+        rows.append({"op": "gguf_expert_mlp_q4k_q4k_q6k", "T": T, "distinct_experts": len(set(ids.ravel().tolist())), "us": secs * 1e6, "gbs": b / secs / 1e9,
+                     "path": "grouped by expert, one pass per expert" if T >= 9 else "token by token", "frac_hbm_" + peak_kind: b / secs / 1e9 / peaks["hbm_gbs"]})
+    del gate, up, down
     return rows
 
 

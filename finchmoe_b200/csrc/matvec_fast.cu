@@ -486,6 +486,9 @@ int launch_gguf(finch_ctx *ctx, cudaStream_t st, int type, const FPack &pack, co
 
 }  // namespace
 
+int finch_gguf_experts_grouped(finch_ctx *ctx, cudaStream_t st, const finch_gguf_experts *ex, const void *h_post, const int32_t *expert_ids, const float *weights,
+                               const uint8_t *valid, const float *h_mid, float *hidden_out, int B);
+
 extern "C" int finch_encode_moe_gguf(finch_ctx *ctx, finch_stream stream, const finch_gguf_experts *ex, const void *h_post, const int32_t *expert_ids,
                                      const float *weights, const uint8_t *valid, const float *h_mid, float *hidden_out, int B) {
     if (!ctx || !ex || !h_post || !expert_ids || !weights || !hidden_out || B < 1) return FINCH_E_ARG;
@@ -497,6 +500,10 @@ extern "C" int finch_encode_moe_gguf(finch_ctx *ctx, finch_stream stream, const 
     if (!ex->gate || !ex->up || !ex->down) return finch_fail(ctx, FINCH_E_ARG, "GGUF experts: null slab");
     cudaSetDevice(c.device);
     cudaStream_t st = finch_pick_stream(ctx, stream);
+    if (B >= 9) {   // a prefill chunk: pairs grouped by expert, every selected expert's rows read once (matvec_gguf_mma.cu)
+        const int rc = finch_gguf_experts_grouped(ctx, st, ex, h_post, expert_ids, weights, valid, h_mid, hidden_out, B);
+        if (rc >= 0) return rc;
+    }
     const size_t need = (size_t)K * (3 * I + H) * sizeof(float);
     if (ctx->gguf_ws_bytes < need) {
         cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;

@@ -291,7 +291,11 @@ FINCH_API int finch_encode_dense_gemm(finch_ctx *ctx, finch_stream stream, const
  * tensor starts at base + e * slab), types FINCH_BITS_Q4_K / FINCH_BITS_Q6_K.  hidden_out[b] = h_mid[b] (or 0) +
  * sum_k w_k * out_k over the experts whose output energy is finite and < 1e20, renormalised by the accepted
  * weight when that lies in (0, 0.99) -- the reference's guarded combine (infer.m:3334-3347).  No shared expert
- * here: the reference's GGUF path adds it in the caller.  The first call allocates scratch (outside capture). */
+ * here: the reference's GGUF path adds it in the caller.  The first call allocates scratch (outside capture).
+ * B <= 8 runs token by token; a chunk of B >= 9 tokens (prefill) sorts its (token, expert) pairs by expert and
+ * reads every selected expert's rows once for all the tokens that chose it (the reference's pool de-duplication,
+ * infer.m:12424-12532; fused_gate_up_swiglu_qk_pool_prefill / dequant_matvec_qk_pool_prefill,
+ * finchmoe/shaders.metal:3460-3517, 3641-3712), on the tensor cores. */
 typedef struct finch_gguf_experts {
     const void *gate, *up, *down;
     size_t gate_slab, up_slab, down_slab;
