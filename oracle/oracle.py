@@ -37,10 +37,12 @@ _REF_SO = os.path.join(_HERE, "_ref", "libfinch_ref.so")
 _ref_lib = None
 
 
-def build_ref(ref_root: str = "/root/reference") -> str | None:
+def build_ref(ref_root: str | None = None) -> str | None:
     """Compile the reference's own CPU math (``make ref``: its pure-C region, from a reference checkout)
     into ``oracle/_ref/``.  Returns the library's path, the path of an earlier build when the checkout is
     absent (the build travels with the tree), or None."""
+    # default: a checkout beside this repository (or wherever FINCH_REFERENCE points)
+    ref_root = ref_root or os.environ.get("FINCH_REFERENCE", os.path.normpath(os.path.join(_HERE, "..", "..", "reference")))
     src = os.path.join(ref_root, "finchmoe", "infer.m")
     if os.path.exists(src):
         subprocess.check_call(["make", "-C", _HERE, "-s", "ref", f"REF={ref_root}"])

@@ -378,7 +378,7 @@ def test_moe_skips_non_resident_and_poisoned_experts(api):
 
 @pytest.mark.parametrize("B", [1, 3, 5, 8])
 def test_moe_decode_full_size_vs_oracle(api, B):
-    """BASELINE shapes: hidden 2048, inter 512, 256 experts, top-8, fp16 scales, bf16 activations."""
+    """The model's shapes: hidden 2048, inter 512, 256 experts, top-8, fp16 scales, bf16 activations."""
     ctx = api.Context(max_tokens=8, n_layers=1)
     pool = ctx.pool(n_layers=1)
     try:
@@ -397,7 +397,7 @@ def test_moe_decode_full_size_vs_oracle(api, B):
         cfg = dict(hidden=2048, inter=512, sd=L.FP16)
         want = _oracle_layer(blocks, ids, w, None, x, cfg, shared=sh, score=score, h_mid=h_mid)
         assert_close(out, want, f"full-size B={B}")
-        # without residual/shared: the pure sum_k w_k * expert_k(x) of BASELINE config 1
+        # without residual/shared: the pure sum_k w_k * expert_k(x) of a single MoE layer
         out2 = ctx.moe_forward_host(pool, 0, x, ids, w)
         want2 = _oracle_layer(blocks, ids, w, None, x, cfg)
         assert_close(out2, want2, f"full-size routed only B={B}")
@@ -577,7 +577,7 @@ def test_residual_norm_vs_oracle(api, ad):
 
 @pytest.mark.parametrize("shape", ["all_same", "all_distinct", "one_hot_expert"])
 def test_moe_decode_extreme_routings_full_size(api, shape):
-    """Group sizes at their extremes, BASELINE shapes, batch 8: every token picks the same eight experts (eight groups of
+    """Group sizes at their extremes, the model's shapes, batch 8: every token picks the same eight experts (eight groups of
     eight pairs), all 64 pairs distinct (64 groups of one), and one expert shared by all tokens next to distinct ones."""
     B = 8
     ctx = api.Context(max_tokens=8, n_layers=1)
