@@ -1,23 +1,24 @@
 // The fixed-capacity exchange of the expert-parallel layer over NVLink peer memory: the ranks' own kernels
-// store records and partial rows straight into each other's receive areas, one release flag per slot, and
-// the receiving kernels wait for the flags.  No collective library call and no host step per layer, so a
-// decode layer is a fixed sequence of launches on one stream (and can sit in a CUDA graph).
+// store records and partial rows straight into each other's receive areas, every payload word beside the
+// sender's epoch, and the receiving kernels read word pairs until they carry the epoch they expect.  No
+// collective library call and no host step per layer, so a decode layer is a fixed sequence of launches on
+// one stream (and can sit in a CUDA graph).
 //
-//   dispatch   every token's record -> slot [my rank][t] of every rank's area (my own included), then its flag
-//   receive    wait for the world * T records addressed to me, spread them into the row arrays the MoE entry
-//              points take, clear their flags; on request the block of my own tokens is masked out
-//   return     the partial rows of source s's tokens -> slot [my rank][t] of rank s's area, then its flag
-//   combine    wait for every other rank's partial rows of my tokens, add them to the layer output in
-//              ascending rank order, clear their flags
+//   dispatch   every token's record -> slot [my rank][t] of every rank's area (my own included)
+//   receive    read the world * T records addressed to me as they arrive and spread them into the row arrays
+//              the MoE entry points take; on request the block of my own tokens is masked out
+//   return     the partial rows of source s's tokens -> slot [my rank][t] of rank s's area
+//   combine    read every other rank's partial rows of my tokens as they arrive, add them to the layer output
+//              in ascending rank order, and advance this rank's epoch
 //
-// Why one buffer and a 0/1 flag per slot are enough: a rank dispatches layer l + 1 only after its combine
-// of layer l, which waited for every peer's return of layer l, which each peer issued after its receive of
-// layer l had read and cleared the slots.  The same chain orders the partial-row slots.  All ranks must
-// therefore call the four steps in the same order the same number of times.
+// Why one buffer per slot is enough: a rank dispatches layer l + 1 only after its combine of layer l, which read
+// every peer's return of layer l, which each peer issued after its receive of layer l had read the slots.  The
+// same chain orders the partial-row slots.  All ranks must therefore call the four steps in the same order the
+// same number of times (that also keeps their epochs equal).
 //
-// Every wait is bounded: when a flag does not arrive within the limit the kernel records FINCH_E_TIMEOUT in
-// the device status word, treats the slot as empty and returns; once the status word is set no later wait
-// spins again.  Plain peer loads and stores only (no multicast objects).
+// Every wait is bounded: when a word pair does not arrive within the limit the kernel records FINCH_E_TIMEOUT
+// in the device status word, treats the slot as empty and goes on; once the status word is set no later wait
+// spins again.  Plain peer stores and local loads only (no multicast objects).
 // The reference runs on one device; this extends its per-layer path (finchmoe/infer.m:9597-9741).
 #include <cstring>
 
@@ -26,7 +27,8 @@
 struct finch_ep_peer {
     finch_ctx *ctx = nullptr;
     int rank = 0, world = 0, T = 0;
-    size_t bytes = 0, off_rflag = 0, off_back = 0, off_bflag = 0;
+    size_t bytes = 0, off_back = 0;      // the area: records [world * T] (each word beside its epoch), then partial rows likewise
+    uint32_t *sync = nullptr;            // this rank's own {epoch, ticket of the combine kernel}
     uint8_t *area = nullptr;             // this rank's receive area
     uint8_t *remote[16] = {};            // every rank's area as this process addresses it (remote[rank] == area)
     bool opened[16] = {};                // mapped through an IPC handle (to be closed)
@@ -43,142 +45,157 @@ struct Areas {
 __host__ __device__ inline int rec_bytes_of(int hidden, int elt, int K) { return (hidden * elt + 9 * K + 15) & ~15; }
 inline size_t up256(size_t n) { return (n + 255) & ~(size_t)255; }
 
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) { asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory"); }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 // Programmatic dependent launch: a kernel of the chain may be scheduled while its predecessor still runs.  Every
 // kernel here executes dep_wait() before it exits, so "my predecessor has completed" holds transitively along the
 // stream; a kernel that needs nothing its predecessor wrote does its work first and waits last.
 __device__ __forceinline__ void dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// One thread waits for a slot's flag.  False: it did not arrive (recorded), the slot is to be treated as empty.
-__device__ bool wait_flag(const uint32_t *flag, int *status, long long limit) {
-    if (ld_acquire_sys(flag) == 1u) return true;
-    if (*reinterpret_cast<volatile int *>(status) != 0) return false;   // an earlier wait already ran out: do not spin again
-    for (long long i = 0; i < limit; i++) {
-        __nanosleep(64);
-        if (ld_acquire_sys(flag) == 1u) return true;
+// ---- data and flag in the same word pair -------------------------------------------------------------
+// Every 16-byte store carries two payload words and, beside each, the sender's epoch: {w0, epoch, w1, epoch}.  An
+// aligned 8-byte half of it arrives whole, so a receiver that reads a pair with the epoch it expects has the
+// payload word that came with it: no fence and no separate flag round trip on the sending side, one NVLink
+// crossing per hop.  The epoch is a word in each rank's own memory that the combine kernel advances once per layer;
+// all ranks run the same sequence, so sender and receiver agree on it, and a slot's previous contents carry an
+// older epoch (zeroed memory: 0, which no epoch takes).
+__device__ __forceinline__ void ll_store(uint4 *p, uint32_t w0, uint32_t w1, uint32_t e) {
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(w0), "r"(e), "r"(w1), "r"(e) : "memory");
+}
+// False: the pair did not arrive within the limit (recorded in the status word).  Once the status word is set,
+// nothing spins again.
+__device__ __forceinline__ bool ll_load(const uint4 *p, uint32_t e, uint32_t &w0, uint32_t &w1, int *status, long long limit) {
+    for (long long i = 0;; i++) {
+        uint32_t a, b, c, d;
+        asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(a), "=r"(b), "=r"(c), "=r"(d) : "l"(p) : "memory");
+        if (b == e && d == e) {
+            w0 = a;
+            w1 = c;
+            return true;
+        }
+        if (i >= limit || (i == 0 && *reinterpret_cast<volatile int *>(status) != 0)) break;
+        __nanosleep(40);
     }
     atomicCAS(status, 0, FINCH_E_TIMEOUT);
+    w0 = w1 = 0u;
     return false;
 }
 
-// grid (T, world), 128 threads: record of token t -> rank d's area
+// grid (T, world), 128 threads: record of token t -> rank d's area (d == rank: my own; the rank's tokens take the same route)
 __global__ void __launch_bounds__(128) peer_dispatch_kernel(Areas areas, int rank, int T, const uint8_t *x, const int32_t *ids, const float *weights,
-                                                            const uint8_t *valid, int row_bytes, int K, int rec_bytes, size_t off_rflag) {
-    const int t = blockIdx.x, d = blockIdx.y;   // d == rank: my own area (the rank's tokens take the same route)
-    dep_wait();        // the activations are the work of what ran before
+                                                            const uint8_t *valid, int row_bytes, int K, int rec_bytes, const uint32_t *epoch) {
+    __shared__ __align__(16) uint32_t tail[32];      // ids, weights, mask bytes, padding: the part of the record after the row
+    const int t = blockIdx.x, d = blockIdx.y;
+    dep_wait();        // the activations are the work of what ran before (and the epoch that of the previous layer's combine)
+    const uint32_t e = *epoch;
     dep_launch();
-    uint8_t *area = areas.p[d];
-    uint8_t *rec = area + (size_t)(rank * T + t) * rec_bytes;
-    const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)t * row_bytes);
-    uint4 *dst = reinterpret_cast<uint4 *>(rec);
-    for (int j = threadIdx.x; j < row_bytes / 16; j += blockDim.x) dst[j] = src[j];
+    if (threadIdx.x < 32) tail[threadIdx.x] = 0u;
+    __syncthreads();
     if (threadIdx.x < K) {
         const int k = threadIdx.x;
-        reinterpret_cast<int32_t *>(rec + row_bytes)[k] = ids[t * K + k];
-        reinterpret_cast<float *>(rec + row_bytes + 4 * K)[k] = weights[t * K + k];
-        rec[row_bytes + 8 * K + k] = valid ? valid[t * K + k] : (uint8_t)1;
+        tail[k] = (uint32_t)ids[t * K + k];
+        tail[K + k] = __float_as_uint(weights[t * K + k]);
+        reinterpret_cast<uint8_t *>(tail + 2 * K)[k] = valid ? valid[t * K + k] : (uint8_t)1;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        st_release_sys(reinterpret_cast<uint32_t *>(area + off_rflag) + rank * T + t, 1u);
+    uint4 *dst = reinterpret_cast<uint4 *>(areas.p[d]) + (size_t)(rank * T + t) * (rec_bytes / 8);
+    const uint2 *row = reinterpret_cast<const uint2 *>(x + (size_t)t * row_bytes);
+    for (int q = threadIdx.x; q < rec_bytes / 8; q += blockDim.x) {
+        uint2 w;
+        if (q < row_bytes / 8) w = row[q];
+        else w = make_uint2(tail[2 * (q - row_bytes / 8)], tail[2 * (q - row_bytes / 8) + 1]);
+        ll_store(dst + q, w.x, w.y, e);
     }
 }
 
-// grid world * T, 128 threads: slot i = [source][t] of my area -> row i of the arrays
-__global__ void __launch_bounds__(128) peer_receive_kernel(uint8_t *area, int rank, int T, int row_bytes, int K, int rec_bytes, size_t off_rflag, uint8_t *x,
-                                                           int32_t *ids, float *weights, uint8_t *valid, int *status, long long limit, int mask_own) {
-    __shared__ int ok;
+// grid world * T, 128 threads, rec_bytes of dynamic shared memory: slot i = [source][t] of my area -> row i of the arrays
+__global__ void __launch_bounds__(128) peer_receive_kernel(const uint8_t *area, int rank, int T, int row_bytes, int K, int rec_bytes, uint8_t *x, int32_t *ids,
+                                                           float *weights, uint8_t *valid, int *status, long long limit, int mask_own, const uint32_t *epoch) {
+    extern __shared__ __align__(16) uint32_t srec[];
     const int i = blockIdx.x, src_rank = i / T;
     const bool masked = mask_own && src_rank == rank;   // my own tokens are served in place by the caller: their rows select nothing
-    uint32_t *flag = reinterpret_cast<uint32_t *>(area + off_rflag) + i;
+    const uint32_t e = *epoch;
     dep_launch();
-    // The records are ordered by their flags, and the row arrays were last read by kernels that completed before the
-    // dispatch kernel passed its wait (which is before this grid could start): no wait for the predecessor up front.
-    if (threadIdx.x == 0) ok = wait_flag(flag, status, limit) ? 1 : 0;
-    __syncthreads();
-    if (!ok) {
+    // The records are ordered by the epochs they carry, and the row arrays were last read by kernels that completed
+    // before the dispatch kernel passed its wait (which is before this grid could start): no wait up front.
+    const uint4 *src = reinterpret_cast<const uint4 *>(area) + (size_t)i * (rec_bytes / 8);
+    int bad = 0;
+    for (int q = threadIdx.x; q < rec_bytes / 8; q += blockDim.x) {
+        uint32_t w0, w1;
+        if (!ll_load(src + q, e, w0, w1, status, limit)) bad = 1;
+        srec[2 * q] = w0;
+        srec[2 * q + 1] = w1;
+    }
+    bad = __syncthreads_or(bad);
+    if (bad) {          // incomplete: the row selects nothing
         if (threadIdx.x < K) valid[i * K + threadIdx.x] = 0;
         dep_wait();
         return;
     }
-    const uint8_t *rec = area + (size_t)i * rec_bytes;
-    const uint4 *src = reinterpret_cast<const uint4 *>(rec);
+    const uint4 *s4 = reinterpret_cast<const uint4 *>(srec);
     uint4 *dst = reinterpret_cast<uint4 *>(x + (size_t)i * row_bytes);
-    for (int j = threadIdx.x; j < row_bytes / 16; j += blockDim.x) dst[j] = src[j];
+    for (int j = threadIdx.x; j < row_bytes / 16; j += blockDim.x) dst[j] = s4[j];
     if (threadIdx.x < K) {
         const int k = threadIdx.x;
-        ids[i * K + k] = reinterpret_cast<const int32_t *>(rec + row_bytes)[k];
-        weights[i * K + k] = reinterpret_cast<const float *>(rec + row_bytes + 4 * K)[k];
-        valid[i * K + k] = masked ? (uint8_t)0 : rec[row_bytes + 8 * K + k];
+        const uint32_t *tail = srec + row_bytes / 4;
+        ids[i * K + k] = (int32_t)tail[k];
+        weights[i * K + k] = __uint_as_float(tail[K + k]);
+        valid[i * K + k] = masked ? (uint8_t)0 : reinterpret_cast<const uint8_t *>(tail + 2 * K)[k];
     }
-    __syncthreads();
-    if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t *>(flag) = 0u;
     dep_wait();
 }
 
 // grid (T, world), 256 threads: partial row of source s's token t -> rank s's area
-__global__ void __launch_bounds__(256) peer_return_kernel(Areas areas, int rank, int T, const float *rows, int hidden, size_t off_back, size_t off_bflag) {
+__global__ void __launch_bounds__(256) peer_return_kernel(Areas areas, int rank, int T, const float *rows, int hidden, size_t off_back, const uint32_t *epoch) {
     const int t = blockIdx.x, s = blockIdx.y;
     dep_wait();        // the rows are the predecessor's output
+    const uint32_t e = *epoch;
     dep_launch();
     if (s == rank) return;
-    uint8_t *area = areas.p[s];
-    const float4 *src = reinterpret_cast<const float4 *>(rows + (size_t)(s * T + t) * hidden);
-    float4 *dst = reinterpret_cast<float4 *>(area + off_back) + (size_t)(rank * T + t) * (hidden / 4);
-    for (int j = threadIdx.x; j < hidden / 4; j += blockDim.x) dst[j] = src[j];
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        st_release_sys(reinterpret_cast<uint32_t *>(area + off_bflag) + rank * T + t, 1u);
+    const uint2 *src = reinterpret_cast<const uint2 *>(rows + (size_t)(s * T + t) * hidden);
+    uint4 *dst = reinterpret_cast<uint4 *>(areas.p[s] + off_back) + (size_t)(rank * T + t) * (hidden / 2);
+    for (int q = threadIdx.x; q < hidden / 2; q += blockDim.x) {
+        const uint2 w = src[q];
+        ll_store(dst + q, w.x, w.y, e);
     }
 }
 
-// grid T, 256 threads: hidden_out[t] += partial rows of ranks 0 .. world - 1 (not mine), ascending
-__global__ void __launch_bounds__(256) peer_combine_kernel(uint8_t *area, int rank, int world, int T, float *hidden_out, int hidden, size_t off_back,
-                                                           size_t off_bflag, int *status, long long limit) {
-    __shared__ int ok[MAXW];
+// grid T, 256 threads: hidden_out[t] += partial rows of ranks 0 .. world - 1 (not mine), ascending; the last CTA
+// to finish advances the epoch.
+__global__ void __launch_bounds__(256) peer_combine_kernel(const uint8_t *area, int rank, int world, int T, float *hidden_out, int hidden, size_t off_back,
+                                                           int *status, long long limit, uint32_t *epoch, unsigned *ticket) {
     const int t = blockIdx.x;
-    uint32_t *flags = reinterpret_cast<uint32_t *>(area + off_bflag);
+    const uint32_t e = *epoch;
     dep_launch();
     // hidden_out was written two kernels back; the return kernel in between passed its wait before this grid could
-    // start, so that writer has completed.  The peers' rows are ordered by their flags.
-    if (threadIdx.x < world) {
-        const int d = threadIdx.x;
-        ok[d] = d != rank && wait_flag(flags + d * T + t, status, limit);
-    }
-    __syncthreads();
-    const float4 *back = reinterpret_cast<const float4 *>(area + off_back);
-    float4 *out = reinterpret_cast<float4 *>(hidden_out + (size_t)t * hidden);
-    for (int j = threadIdx.x; j < hidden / 4; j += blockDim.x) {
-        float4 h = out[j];
+    // start, so that writer has completed.  The peers' rows are ordered by the epochs they carry.
+    const uint4 *back = reinterpret_cast<const uint4 *>(area + off_back);
+    float2 *out = reinterpret_cast<float2 *>(hidden_out + (size_t)t * hidden);
+    for (int q = threadIdx.x; q < hidden / 2; q += blockDim.x) {
+        float2 h = out[q];
         for (int d = 0; d < world; d++) {
-            if (!ok[d]) continue;
-            const float4 v = back[(size_t)(d * T + t) * (hidden / 4) + j];
-            h.x += v.x;
-            h.y += v.y;
-            h.z += v.z;
-            h.w += v.w;
+            if (d == rank) continue;
+            uint32_t w0, w1;
+            ll_load(back + (size_t)(d * T + t) * (hidden / 2) + q, e, w0, w1, status, limit);
+            h.x += __uint_as_float(w0);
+            h.y += __uint_as_float(w1);
         }
-        out[j] = h;
+        out[q] = h;
     }
-    __syncthreads();
-    if (threadIdx.x < world && ok[threadIdx.x]) *reinterpret_cast<volatile uint32_t *>(flags + threadIdx.x * T + t) = 0u;
     dep_wait();
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(ticket, 1u) == gridDim.x - 1) {
+        *ticket = 0u;
+        *epoch = e + 1u == 0u ? 1u : e + 1u;
+        __threadfence();
+    }
 }
 
 template <typename... Args>
-cudaError_t launch_pdl(void (*kernel)(Args...), dim3 grid, int threads, cudaStream_t st, Args... args) {
+cudaError_t launch_pdl(void (*kernel)(Args...), dim3 grid, int threads, size_t smem, cudaStream_t st, Args... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -215,16 +232,18 @@ extern "C" int finch_ep_peer_create(finch_ctx *ctx, int rank, int world, int tok
     p->T = tokens_per_rank;
     const int elt = c.act_dtype == FINCH_BF16 ? 2 : 4;
     const size_t slots = (size_t)world * tokens_per_rank;
-    p->off_rflag = up256(slots * rec_bytes_of(c.hidden, elt, c.top_k));
-    p->off_back = p->off_rflag + up256(slots * 4);
-    p->off_bflag = p->off_back + up256(slots * c.hidden * 4);
-    p->bytes = p->off_bflag + up256(slots * 4);
-    if (cudaMalloc(&p->area, p->bytes) != cudaSuccess) {
+    p->off_back = up256(slots * 2 * rec_bytes_of(c.hidden, elt, c.top_k));
+    p->bytes = p->off_back + up256(slots * 2 * c.hidden * 4);
+    if (cudaMalloc(&p->area, p->bytes) != cudaSuccess || cudaMalloc(&p->sync, 2 * sizeof(uint32_t)) != cudaSuccess) {
         cudaGetLastError();
+        cudaFree(p->area);
+        const size_t bytes = p->bytes;
         delete p;
-        return finch_fail(ctx, FINCH_E_NOMEM, "peer receive area (%zu bytes)", p->bytes);
+        return finch_fail(ctx, FINCH_E_NOMEM, "peer receive area (%zu bytes)", bytes);
     }
     cudaMemset(p->area, 0, p->bytes);
+    const uint32_t init[2] = {1u, 0u};          // epochs start at 1: zeroed slots match none
+    cudaMemcpy(p->sync, init, sizeof(init), cudaMemcpyHostToDevice);
     cudaDeviceSynchronize();
     p->remote[rank] = p->area;
     *out = p;
@@ -273,8 +292,9 @@ extern "C" int finch_ep_peer_reset(finch_ep_peer *p) {
     if (!p) return FINCH_E_ARG;
     cudaSetDevice(p->ctx->cfg.device);
     FINCH_CUDA_OK(p->ctx, cudaDeviceSynchronize());
-    FINCH_CUDA_OK(p->ctx, cudaMemset(p->area + p->off_rflag, 0, p->off_back - p->off_rflag));
-    FINCH_CUDA_OK(p->ctx, cudaMemset(p->area + p->off_bflag, 0, p->bytes - p->off_bflag));
+    FINCH_CUDA_OK(p->ctx, cudaMemset(p->area, 0, p->bytes));
+    const uint32_t init[2] = {1u, 0u};
+    FINCH_CUDA_OK(p->ctx, cudaMemcpy(p->sync, init, sizeof(init), cudaMemcpyHostToDevice));
     FINCH_CUDA_OK(p->ctx, cudaDeviceSynchronize());
     return FINCH_OK;
 }
@@ -286,6 +306,7 @@ extern "C" int finch_ep_peer_destroy(finch_ep_peer *p) {
     for (int r = 0; r < p->world; r++)
         if (p->opened[r]) cudaIpcCloseMemHandle(p->remote[r]);
     cudaFree(p->area);
+    cudaFree(p->sync);
     delete p;
     return FINCH_OK;
 }
@@ -299,8 +320,9 @@ extern "C" int finch_encode_ep_peer_dispatch(finch_ctx *ctx, finch_stream stream
     const int elt = c.act_dtype == FINCH_BF16 ? 2 : 4, row_bytes = c.hidden * elt;
     if (row_bytes % 16) return finch_fail(ctx, FINCH_E_ARG, "activation rows must be multiples of 16 bytes");
     cudaSetDevice(c.device);
-    FINCH_CUDA_OK(ctx, launch_pdl(peer_dispatch_kernel, dim3(p->T, p->world), 128, finch_pick_stream(ctx, stream), areas_of(p), p->rank, p->T,
-                                  (const uint8_t *)h_post, expert_ids, weights, valid, row_bytes, c.top_k, rec_bytes_of(c.hidden, elt, c.top_k), p->off_rflag));
+    FINCH_CUDA_OK(ctx, launch_pdl(peer_dispatch_kernel, dim3(p->T, p->world), 128, 0, finch_pick_stream(ctx, stream), areas_of(p), p->rank, p->T,
+                                  (const uint8_t *)h_post, expert_ids, weights, valid, row_bytes, c.top_k, rec_bytes_of(c.hidden, elt, c.top_k),
+                                  (const uint32_t *)p->sync));
     ctx->launches++;
     return FINCH_OK;
 }
@@ -311,9 +333,10 @@ extern "C" int finch_encode_ep_peer_receive(finch_ctx *ctx, finch_stream stream,
     const finch_config &c = ctx->cfg;
     const int elt = c.act_dtype == FINCH_BF16 ? 2 : 4;
     cudaSetDevice(c.device);
-    FINCH_CUDA_OK(ctx, launch_pdl(peer_receive_kernel, dim3(p->world * p->T), 128, finch_pick_stream(ctx, stream), p->area, p->rank, p->T, c.hidden * elt,
-                                  c.top_k, rec_bytes_of(c.hidden, elt, c.top_k), p->off_rflag, (uint8_t *)h_post, expert_ids, weights, valid, ctx->dev_status,
-                                  p->limit, mask_own));
+    const int rec = rec_bytes_of(c.hidden, elt, c.top_k);
+    FINCH_CUDA_OK(ctx, launch_pdl(peer_receive_kernel, dim3(p->world * p->T), 128, (size_t)rec, finch_pick_stream(ctx, stream), (const uint8_t *)p->area, p->rank,
+                                  p->T, c.hidden * elt, c.top_k, rec, (uint8_t *)h_post, expert_ids, weights, valid, ctx->dev_status, p->limit, mask_own,
+                                  (const uint32_t *)p->sync));
     ctx->launches++;
     return FINCH_OK;
 }
@@ -324,18 +347,18 @@ extern "C" int finch_encode_ep_peer_return(finch_ctx *ctx, finch_stream stream, 
     if (rc) return rc;
     if (p->world == 1) return FINCH_OK;
     cudaSetDevice(ctx->cfg.device);
-    FINCH_CUDA_OK(ctx, launch_pdl(peer_return_kernel, dim3(p->T, p->world), 256, finch_pick_stream(ctx, stream), areas_of(p), p->rank, p->T, rows,
-                                  ctx->cfg.hidden, p->off_back, p->off_bflag));
+    FINCH_CUDA_OK(ctx, launch_pdl(peer_return_kernel, dim3(p->T, p->world), 256, 0, finch_pick_stream(ctx, stream), areas_of(p), p->rank, p->T, rows,
+                                  ctx->cfg.hidden, p->off_back, (const uint32_t *)p->sync));
     ctx->launches++;
     return FINCH_OK;
 }
 
 extern "C" int finch_encode_ep_peer_combine(finch_ctx *ctx, finch_stream stream, finch_ep_peer *p, float *hidden_out) {
     if (!ctx || !p || p->ctx != ctx || !hidden_out) return FINCH_E_ARG;
-    if (p->world == 1) return FINCH_OK;
+    // with one rank there is nothing to add, but the kernel still closes the layer: it advances the epoch
     cudaSetDevice(ctx->cfg.device);
-    FINCH_CUDA_OK(ctx, launch_pdl(peer_combine_kernel, dim3(p->T), 256, finch_pick_stream(ctx, stream), p->area, p->rank, p->world, p->T, hidden_out,
-                                  ctx->cfg.hidden, p->off_back, p->off_bflag, ctx->dev_status, p->limit));
+    FINCH_CUDA_OK(ctx, launch_pdl(peer_combine_kernel, dim3(p->T), 256, 0, finch_pick_stream(ctx, stream), (const uint8_t *)p->area, p->rank, p->world, p->T,
+                                  hidden_out, ctx->cfg.hidden, p->off_back, ctx->dev_status, p->limit, p->sync, (unsigned *)(p->sync + 1)));
     ctx->launches++;
     return FINCH_OK;
 }

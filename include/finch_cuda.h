@@ -346,16 +346,20 @@ FINCH_API int finch_encode_moe_decode_multi(finch_ctx *ctx, finch_stream stream,
 
 /* ---- the fixed-capacity exchange over NVLink peer memory (decode-sized batches: every rank owns
  * tokens_per_rank tokens and sends each to every rank).  The ranks' kernels store records and partial
- * rows into each other's receive areas and wait on one flag per slot: no collective call and no host
- * step per layer, so a layer is a fixed sequence of launches that a CUDA graph can hold.  Setup, once:
+ * rows into each other's receive areas, every payload word beside the sender's epoch (a per-rank
+ * counter that combine advances once per layer), and the receiving kernels read until the words carry
+ * the epoch they expect: no fence, no collective call and no host step per layer, so a layer is a
+ * fixed sequence of launches that a CUDA graph can hold.  All ranks must issue the per-layer calls in
+ * the same order the same number of times (combine included, also with one rank).  Setup, once:
  * every rank creates its area, exports a 64-byte handle, receives the other ranks' handles by whatever
  * channel the host has (the MPI / NCCL bootstrap, a file) and imports them.  Per layer, every rank, in
  * this order: dispatch -> receive -> finch_encode_moe_decode_multi on the world batches of received rows
  * (or: finch_encode_moe_decode on its own tokens, receive with mask_own, finch_encode_moe_prefill on the
  * received rows) -> return -> combine.
- * Every device-side wait is bounded: a flag that does not arrive records FINCH_E_TIMEOUT in the
+ * Every device-side wait is bounded: words that do not arrive record FINCH_E_TIMEOUT in the
  * device status word, the slot counts as empty and later waits no longer spin; the host then calls
- * finch_ep_peer_reset on every rank (after a barrier) or falls back to the all-to-all steps above. */
+ * finch_ep_peer_reset on every rank (after a barrier: it clears the area and restarts the epoch) or
+ * falls back to the all-to-all steps above. */
 typedef struct finch_ep_peer finch_ep_peer;
 FINCH_API int finch_ep_peer_create(finch_ctx *ctx, int rank, int world, int tokens_per_rank, finch_ep_peer **out);
 FINCH_API int finch_ep_peer_export(finch_ep_peer *peer, void *handle64);                        /* this rank's area, for the others */
@@ -363,7 +367,7 @@ FINCH_API int finch_ep_peer_import(finch_ep_peer *peer, int src_rank, const void
 FINCH_API void *finch_ep_peer_area(finch_ep_peer *peer);                                        /* device pointer of this rank's area */
 FINCH_API int finch_ep_peer_attach(finch_ep_peer *peer, int src_rank, void *area);              /* an area of the same process */
 FINCH_API int finch_ep_peer_set_wait_limit(finch_ep_peer *peer, long long polls);               /* ~100 ns each; default 4,000,000 */
-FINCH_API int finch_ep_peer_reset(finch_ep_peer *peer);                                         /* waits for the device, clears all flags */
+FINCH_API int finch_ep_peer_reset(finch_ep_peer *peer);                                         /* waits for the device, clears the area, epoch = 1 */
 FINCH_API int finch_ep_peer_destroy(finch_ep_peer *peer);
 FINCH_API int finch_encode_ep_peer_dispatch(finch_ctx *ctx, finch_stream stream, finch_ep_peer *peer, const void *h_post,
                                             const int32_t *expert_ids, const float *weights, const uint8_t *valid);
