@@ -61,6 +61,11 @@ __device__ __forceinline__ void dep_launch() { asm volatile("griddepcontrol.laun
 __device__ __forceinline__ void ll_store(uint4 *p, uint32_t w0, uint32_t w1, uint32_t e) {
     asm volatile("st.volatile.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(w0), "r"(e), "r"(w1), "r"(e) : "memory");
 }
+__device__ __forceinline__ uint4 ll_peek(const uint4 *p) {
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
+    return v;
+}
 // False: the pair did not arrive within the limit (recorded in the status word).  Once the status word is set,
 // nothing spins again.
 __device__ __forceinline__ bool ll_load(const uint4 *p, uint32_t e, uint32_t &w0, uint32_t &w1, int *status, long long limit) {
@@ -119,7 +124,26 @@ __global__ void __launch_bounds__(128) peer_receive_kernel(const uint8_t *area, 
     // before the dispatch kernel passed its wait (which is before this grid could start): no wait up front.
     const uint4 *src = reinterpret_cast<const uint4 *>(area) + (size_t)i * (rec_bytes / 8);
     int bad = 0;
-    for (int q = threadIdx.x; q < rec_bytes / 8; q += blockDim.x) {
+    // a thread's word pairs are requested together; those that have not arrived yet are then waited for one by one
+    constexpr int RQ = 10;      // 128 threads x 10 pairs x 8 payload bytes covers a record of 10 KB
+    uint4 v[RQ];
+#pragma unroll
+    for (int r = 0; r < RQ; r++) {
+        const int q = threadIdx.x + r * 128;
+        if (q < rec_bytes / 8) v[r] = ll_peek(src + q);
+    }
+#pragma unroll
+    for (int r = 0; r < RQ; r++) {
+        const int q = threadIdx.x + r * 128;
+        if (q < rec_bytes / 8) {
+            uint32_t w0 = v[r].x, w1 = v[r].z;
+            if (v[r].y != e || v[r].w != e)
+                if (!ll_load(src + q, e, w0, w1, status, limit)) bad = 1;
+            srec[2 * q] = w0;
+            srec[2 * q + 1] = w1;
+        }
+    }
+    for (int q = threadIdx.x + RQ * 128; q < rec_bytes / 8; q += blockDim.x) {     // longer records: the plain loop
         uint32_t w0, w1;
         if (!ll_load(src + q, e, w0, w1, status, limit)) bad = 1;
         srec[2 * q] = w0;
@@ -159,31 +183,37 @@ __global__ void __launch_bounds__(256) peer_return_kernel(Areas areas, int rank,
     }
 }
 
-// grid T, 256 threads: hidden_out[t] += partial rows of ranks 0 .. world - 1 (not mine), ascending; the last CTA
-// to finish advances the epoch.
+// grid (T, hidden / 512), 256 threads, a thread per pair of outputs: hidden_out[t] += partial rows of ranks
+// 0 .. world - 1 (not mine), ascending; the last CTA to finish advances the epoch.
 __global__ void __launch_bounds__(256) peer_combine_kernel(const uint8_t *area, int rank, int world, int T, float *hidden_out, int hidden, size_t off_back,
                                                            int *status, long long limit, uint32_t *epoch, unsigned *ticket) {
-    const int t = blockIdx.x;
+    const int t = blockIdx.x, q = blockIdx.y * 256 + threadIdx.x;
     const uint32_t e = *epoch;
     dep_launch();
     // hidden_out was written two kernels back; the return kernel in between passed its wait before this grid could
     // start, so that writer has completed.  The peers' rows are ordered by the epochs they carry.
-    const uint4 *back = reinterpret_cast<const uint4 *>(area + off_back);
-    float2 *out = reinterpret_cast<float2 *>(hidden_out + (size_t)t * hidden);
-    for (int q = threadIdx.x; q < hidden / 2; q += blockDim.x) {
-        float2 h = out[q];
-        for (int d = 0; d < world; d++) {
-            if (d == rank) continue;
-            uint32_t w0, w1;
-            ll_load(back + (size_t)(d * T + t) * (hidden / 2) + q, e, w0, w1, status, limit);
-            h.x += __uint_as_float(w0);
-            h.y += __uint_as_float(w1);
-        }
-        out[q] = h;
+    if (q < hidden / 2) {
+        const uint4 *back = reinterpret_cast<const uint4 *>(area + off_back) + (size_t)t * (hidden / 2) + q;
+        const size_t dstride = (size_t)T * (hidden / 2);
+        uint4 v[MAXW];
+#pragma unroll
+        for (int d = 0; d < MAXW; d++)
+            if (d < world && d != rank) v[d] = ll_peek(back + d * dstride);      // all peers' words requested together
+        float2 *out = reinterpret_cast<float2 *>(hidden_out + (size_t)t * hidden) + q;
+        float2 h = *out;
+#pragma unroll
+        for (int d = 0; d < MAXW; d++)
+            if (d < world && d != rank) {
+                uint32_t w0 = v[d].x, w1 = v[d].z;
+                if (v[d].y != e || v[d].w != e) ll_load(back + d * dstride, e, w0, w1, status, limit);
+                h.x += __uint_as_float(w0);
+                h.y += __uint_as_float(w1);
+            }
+        *out = h;
     }
     dep_wait();
     __syncthreads();
-    if (threadIdx.x == 0 && atomicAdd(ticket, 1u) == gridDim.x - 1) {
+    if (threadIdx.x == 0 && atomicAdd(ticket, 1u) == gridDim.x * gridDim.y - 1) {
         *ticket = 0u;
         *epoch = e + 1u == 0u ? 1u : e + 1u;
         __threadfence();
@@ -357,7 +387,7 @@ extern "C" int finch_encode_ep_peer_combine(finch_ctx *ctx, finch_stream stream,
     if (!ctx || !p || p->ctx != ctx || !hidden_out) return FINCH_E_ARG;
     // with one rank there is nothing to add, but the kernel still closes the layer: it advances the epoch
     cudaSetDevice(ctx->cfg.device);
-    FINCH_CUDA_OK(ctx, launch_pdl(peer_combine_kernel, dim3(p->T), 256, 0, finch_pick_stream(ctx, stream), (const uint8_t *)p->area, p->rank, p->world, p->T,
+    FINCH_CUDA_OK(ctx, launch_pdl(peer_combine_kernel, dim3(p->T, (ctx->cfg.hidden / 2 + 255) / 256), 256, 0, finch_pick_stream(ctx, stream), (const uint8_t *)p->area, p->rank, p->world, p->T,
                                   hidden_out, ctx->cfg.hidden, p->off_back, ctx->dev_status, p->limit, p->sync, (unsigned *)(p->sync + 1)));
     ctx->launches++;
     return FINCH_OK;
