@@ -219,6 +219,14 @@ class Context:
         self.check(self.lib.finch_encode_moe_gguf(self.h, stream, C.byref(experts), _ptr(h_post), _ptr(ids), _ptr(weights), _ptr(valid),
                                                   _ptr(h_mid), _ptr(hidden_out), B))
 
+    def moe_forward_host_ptrs(self, pool: Pool, layer: int, h_post: int, ids: int, weights: int, valid: int | None, shared, gate_score: int | None,
+                              h_mid: int | None, hidden_out: int, T: int):
+        """finch_moe_forward_host on raw host addresses (arrays the caller keeps alive and contiguous): the call a C
+        host makes, without the per-call array conversions of moe_forward_host."""
+        rc = self.lib.finch_moe_forward_host(self.h, pool.h, layer, h_post, ids, weights, valid, shared, gate_score, h_mid, hidden_out, T)
+        if rc:
+            self.check(rc)
+
     def moe_forward_host(self, pool: Pool, layer: int, h_post: np.ndarray, ids: np.ndarray, weights: np.ndarray,
                          valid=None, shared: L.Shared | None = None, gate_score=None, h_mid=None) -> np.ndarray:
         """Host buffers in, host buffer out (one H2D, the kernels, one D2H, wait)."""

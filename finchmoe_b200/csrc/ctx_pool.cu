@@ -89,9 +89,10 @@ extern "C" int finch_ctx_create(const finch_config *cfg, finch_ctx **out) {
     bool ok = cudaMalloc(&ctx->act, pairs * c.moe_inter * sizeof(float)) == cudaSuccess &&
               cudaMalloc(&ctx->shared_act, (size_t)c.max_tokens * sh_inter * sizeof(float)) == cudaSuccess &&
               cudaMalloc(&ctx->partial, (pairs + c.max_tokens) * c.hidden * sizeof(float)) == cudaSuccess &&
-              cudaMalloc(&ctx->dev_status, sizeof(int)) == cudaSuccess;
+              cudaMalloc(&ctx->dev_status, sizeof(int)) == cudaSuccess && cudaMalloc(&ctx->hp_ticket, sizeof(unsigned)) == cudaSuccess;
     if (!ok) return bail(FINCH_E_NOMEM);
     cudaMemset(ctx->dev_status, 0, sizeof(int));
+    cudaMemset(ctx->hp_ticket, 0, sizeof(unsigned));
     cudaMemset(ctx->partial, 0, (pairs + c.max_tokens) * c.hidden * sizeof(float));
     if (cudaDeviceSynchronize() != cudaSuccess) return bail(FINCH_E_CUDA);
     *out = ctx;
@@ -106,6 +107,7 @@ extern "C" void finch_ctx_destroy(finch_ctx *ctx) {
     cudaFree(ctx->shared_act);
     cudaFree(ctx->partial);
     cudaFree(ctx->dev_status);
+    cudaFree(ctx->hp_ticket);
     for (auto &e : ctx->shared_cache) cudaFree(e.tiles);
     cudaFree(ctx->stage_dev);
     cudaFree(ctx->pf_ws);

@@ -27,6 +27,10 @@ struct finch_ctx {
     float *shared_act = nullptr;    // [max_tokens][shared_inter]
     float *partial = nullptr;       // [max_pairs + max_tokens][hidden] per-pair down outputs (+ shared rows)
     int *dev_status = nullptr;      // sticky device status word
+    unsigned *hp_ticket = nullptr;  // device word: CTAs of the combine kernel that have finished (host-pointer path)
+    unsigned *hp_done = nullptr;    // armed by finch_moe_forward_host for its next decode call: device address of the host's
+    int *hp_status = nullptr;       //   completion word and status word (mapped pinned memory), and the value to write
+    unsigned hp_seq = 0;
     int fault = 0;                  // finch_debug_fault: failure injected into the next decode calls
     bool no_pdl = false;            // FINCH_NO_PDL=1 in the environment: plain stream-ordered launches
     struct SharedPrepared {

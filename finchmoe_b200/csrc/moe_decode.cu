@@ -102,6 +102,11 @@ struct MoeArgs {
     int n_calls, own_call;
     int cta0[MAX_CALLS + 1];
     float *rows_out;
+    // host-pointer path: when host_done is set, the last CTA of the combine kernel copies the status word to
+    // host_status and then writes done_seq to host_done (both mapped pinned memory): the host waits on that word
+    unsigned *done_ticket, *host_done;
+    int *host_status;
+    unsigned done_seq;
 };
 
 // The view of batch c of a multi-batch launch: pointers moved to its rows, the shared expert and the residual
@@ -1301,13 +1306,24 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const MoeArgs a0) {
     const float sg = a.has_shared ? 1.0f / (1.0f + expf(-a.gate_score[b])) : 0.f;
     __syncthreads();
     grid_dep_wait();
-    if (!live) return;
-    float moe = 0.f;
-    for (int k = 0; k < a.K; k++)
-        if (ok[k]) moe = fmaf(wk[k], __ldcg(a.partial + (size_t)(b * a.K + k) * a.hidden + row), moe);
-    h += moe;
-    if (a.has_shared) h = fmaf(sg, __ldcg(a.partial + (size_t)(a.P + b) * a.hidden + row), h);
-    a.hidden_out[(size_t)b * a.hidden + row] = h;
+    if (live) {
+        float moe = 0.f;
+        for (int k = 0; k < a.K; k++)
+            if (ok[k]) moe = fmaf(wk[k], __ldcg(a.partial + (size_t)(b * a.K + k) * a.hidden + row), moe);
+        h += moe;
+        if (a.has_shared) h = fmaf(sg, __ldcg(a.partial + (size_t)(a.P + b) * a.hidden + row), h);
+        a.hidden_out[(size_t)b * a.hidden + row] = h;
+    }
+    if (a0.host_done) {   // launch-uniform
+        __threadfence_system();          // this thread's output is on its way to the host before the CTA reports
+        __syncthreads();
+        if (threadIdx.x == 0 && atomicAdd(a0.done_ticket, 1u) == gridDim.x * gridDim.y - 1) {
+            *a0.done_ticket = 0u;
+            *a0.host_status = *reinterpret_cast<volatile int *>(a0.status);
+            __threadfence_system();
+            *reinterpret_cast<volatile unsigned *>(a0.host_done) = a0.done_seq;
+        }
+    }
 }
 
 constexpr int SMEM_MAX = 227 * 1024;
@@ -1439,6 +1455,13 @@ static int encode_decode_calls(finch_ctx *ctx, finch_stream stream, finch_pool *
     a.n_calls = n_calls;
     a.own_call = n_calls > 1 ? own_call : 0;
     a.rows_out = rows_out;
+    if (ctx->hp_done && n_calls == 1) {      // armed by the host-pointer entry point for this one call
+        a.done_ticket = ctx->hp_ticket;
+        a.host_done = ctx->hp_done;
+        a.host_status = ctx->hp_status;
+        a.done_seq = ctx->hp_seq;
+    }
+    ctx->hp_done = nullptr;
     if ((uintptr_t)h_post & 15) return finch_fail(ctx, FINCH_E_ARG, "h_post must be 16-byte aligned");
     const int hilo = c.act_dtype == FINCH_BF16 ? 0 : 1;
     const bool fp16s = c.scale_dtype == FINCH_FP16;

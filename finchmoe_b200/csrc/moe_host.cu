@@ -2,6 +2,8 @@
 // into one pinned staging block, moves it to the device in one transfer, encodes
 // the decode or prefill path (decode-sized calls write their result rows straight
 // into the pinned block; larger ones copy them back) and waits.
+#include <chrono>
+
 #include "finch_internal.cuh"
 
 int finch_stage_reserve(finch_ctx *ctx, size_t bytes);
@@ -47,6 +49,17 @@ extern "C" int finch_moe_forward_host(finch_ctx *ctx, finch_pool *pool, int laye
         else cudaGetLastError();
     }
     FINCH_CUDA_OK(ctx, cudaMemcpyAsync(ds, hs, o_o, cudaMemcpyHostToDevice, ctx->stream));
+    // A decode-sized call whose result lands in the pinned block also reports there: the last CTA of the combine
+    // kernel writes the status word and then this call's sequence number, and the host waits on that word instead
+    // of on the stream (no copy operation for the status, no driver wake-up).
+    const bool flagged = out != ds;
+    volatile unsigned *done = reinterpret_cast<volatile unsigned *>(hs + o_st + 64);
+    if (flagged) {
+        ctx->hp_seq = ctx->hp_seq + 1 == 0 ? 1 : ctx->hp_seq + 1;
+        *done = 0u;                      // the block is reused: whatever lay here is not a completion
+        ctx->hp_done = reinterpret_cast<unsigned *>(out + o_st + 64);
+        ctx->hp_status = reinterpret_cast<int *>(out + o_st);
+    }
     finch_shared sh;
     if (shared) {
         sh = *shared;
@@ -56,11 +69,25 @@ extern "C" int finch_moe_forward_host(finch_ctx *ctx, finch_pool *pool, int laye
     rc = fn(ctx, ctx->stream, pool, layer, in + o_x, (const int32_t *)(in + o_id), (const float *)(in + o_w),
             valid ? (const uint8_t *)(in + o_v) : nullptr, shared ? &sh : nullptr, h_mid ? (const float *)(in + o_h) : nullptr,
             (float *)(out + o_o), T);
+    ctx->hp_done = nullptr;
     if (rc) return rc;
-    if (out == ds) FINCH_CUDA_OK(ctx, cudaMemcpyAsync(hs + o_o, ds + o_o, n_o, cudaMemcpyDeviceToHost, ctx->stream));
-    // the device status word rides along (a bounded wait that ran out leaves the output undefined)
-    FINCH_CUDA_OK(ctx, cudaMemcpyAsync(hs + o_st, ctx->dev_status, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
-    FINCH_CUDA_OK(ctx, cudaStreamSynchronize(ctx->stream));
+    bool waited = false;
+    if (flagged) {
+        const auto t0 = std::chrono::steady_clock::now();
+        for (unsigned spins = 0;; spins++) {
+            if (*done == ctx->hp_seq) {
+                waited = true;
+                break;
+            }
+            if ((spins & 0xfffu) == 0xfffu && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(2)) break;   // fall back to the stream
+        }
+    }
+    if (!waited) {
+        if (out == ds) FINCH_CUDA_OK(ctx, cudaMemcpyAsync(hs + o_o, ds + o_o, n_o, cudaMemcpyDeviceToHost, ctx->stream));
+        // the device status word rides along (a bounded wait that ran out leaves the output undefined)
+        FINCH_CUDA_OK(ctx, cudaMemcpyAsync(hs + o_st, ctx->dev_status, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+        FINCH_CUDA_OK(ctx, cudaStreamSynchronize(ctx->stream));
+    }
     memcpy(hidden_out, hs + o_o, n_o);
     const int dev_rc = *(const int *)(hs + o_st);
     if (dev_rc != FINCH_OK) return finch_fail(ctx, dev_rc, "device status %d after the MoE layer", dev_rc);
