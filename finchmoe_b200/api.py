@@ -195,7 +195,8 @@ class Context:
 
     # -- MoE layer
     def set_prefill_mode(self, mode: int):
-        """0: by chunk length, 1: sub-batches through the decode kernels, 2: tensor-core grouped GEMM."""
+        """0: by chunk length, 1: sub-batches through the decode kernels, 2: grouped dequant-GEMMs on tcgen05,
+        3: grouped mma.sync passes (one unpack per unit for up to 16 tokens of an expert)."""
         self.check(self.lib.finch_set_prefill_mode(self.h, mode))
         self.prefill_mode = mode
 

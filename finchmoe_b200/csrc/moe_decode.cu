@@ -1401,7 +1401,444 @@ int set_attrs_once(finch_ctx *ctx) {
     return FINCH_OK;
 }
 
+
+// =============== grouped 3-bit expert passes for prefill chunks (mma.sync) ================
+// The pairs of a chunk sorted by expert; an expert's tokens are served up to 16 (8 with two activation planes) at a
+// time by the unit loop of the decode kernels, with ONE unpack of a unit's codes for all its passes: 21 logic
+// operations per 32 codes whatever the number of tokens, against a dequantisation into shared-memory tiles that a
+// tensor-memory GEMM needs.  At the few tokens per expert of a prefill chunk (about 16 at 512 tokens, top-8 of 256)
+// this is the cheaper form; the tcgen05 GEMM takes over when experts see many tokens (expert-parallel ranks).
+struct G3Args {
+    const uint8_t *pool_base;
+    size_t slot_bytes;
+    const int32_t *slot_row;   // the layer's slot table [n_experts]
+    int hidden, inter;
+    const uint8_t *recs;       // operand records by position (global memory)
+    int rstride;
+    const int4 *items;         // (expert, first position, tokens, -)
+    const int *n_items;
+    const int *order;          // position -> pair index t * K + k
+    float *out;                // gate/up: act [position][inter]; down: [pair][hidden]
+    int *status;
+};
+
+// One CTA: positions = the usable pairs sorted by expert.  order[pos] = pair, src_tok[pos] = token.  Item lists for
+// the gate/up passes (ppa tokens per pass) and the down passes (ppb): an expert with at most pp / 2 pp tokens is one
+// item of list 0 / 1, a larger one chunks of 4 pp in list 2.  counts = {nA0, nA1, nA2, nB0, nB1, nB2, positions}.
+__global__ void __launch_bounds__(1024) g3_sort_kernel(const int32_t *ids, const uint8_t *valid, const int32_t *slot_row, int n_experts, int P, int Kx,
+                                                       int ppa, int ppb, int *order, int *src_tok, int4 *la0, int4 *la1, int4 *la2, int4 *lb0, int4 *lb1,
+                                                       int4 *lb2, int *counts) {
+    extern __shared__ int g3s[];
+    __shared__ int wsum[7][32];
+    int *cnt = g3s, *cur = g3s + n_experts;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    for (int e = tid; e < n_experts; e += 1024) cnt[e] = 0;
+    __syncthreads();
+    for (int p = tid; p < P; p += 1024) {
+        const int e = ids[p];
+        if ((valid && !valid[p]) || e < 0 || e >= n_experts || slot_row[e] < 0) continue;
+        atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    // Exclusive scans over the experts, 1024 at a time (carry between rounds): positions, and the number of items every
+    // expert adds to each of the six lists.
+    int carry[7] = {0, 0, 0, 0, 0, 0, 0};
+    for (int e0 = 0; e0 < n_experts; e0 += 1024) {
+        const int e = e0 + tid, c = e < n_experts ? cnt[e] : 0;
+        int v[7], inc[7];
+        v[0] = c;
+#pragma unroll
+        for (int side = 0; side < 2; side++) {
+            const int pp = side ? ppb : ppa;
+            v[1 + 3 * side] = c > 0 && c <= pp;
+            v[2 + 3 * side] = c > pp && c <= 2 * pp;
+            v[3 + 3 * side] = c > 2 * pp ? (c + 4 * pp - 1) / (4 * pp) : 0;
+        }
+#pragma unroll
+        for (int q = 0; q < 7; q++) {
+            inc[q] = v[q];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int u = __shfl_up_sync(0xffffffffu, inc[q], o);
+                if (lane >= o) inc[q] += u;
+            }
+            if (lane == 31) wsum[q][wid] = inc[q];
+        }
+        __syncthreads();
+        if (wid == 0) {
+#pragma unroll
+            for (int q = 0; q < 7; q++) {
+                const int w = wsum[q][lane];
+                int acc = w;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int u = __shfl_up_sync(0xffffffffu, acc, o);
+                    if (lane >= o) acc += u;
+                }
+                wsum[q][lane] = acc - w;
+            }
+        }
+        __syncthreads();
+        int ex[7];
+#pragma unroll
+        for (int q = 0; q < 7; q++) ex[q] = carry[q] + wsum[q][wid] + inc[q] - v[q];
+        if (e < n_experts) {
+            cur[e] = ex[0];
+            if (c > 0) {
+#pragma unroll
+                for (int side = 0; side < 2; side++) {
+                    const int pp = side ? ppb : ppa;
+                    int4 *l0 = side ? lb0 : la0, *l1 = side ? lb1 : la1, *l2 = side ? lb2 : la2;
+                    if (c <= pp) l0[ex[1 + 3 * side]] = make_int4(e, ex[0], c, 0);
+                    else if (c <= 2 * pp) l1[ex[2 + 3 * side]] = make_int4(e, ex[0], c, 0);
+                    else
+                        for (int o = 0, i = 0; o < c; o += 4 * pp, i++) l2[ex[3 + 3 * side] + i] = make_int4(e, ex[0] + o, c - o < 4 * pp ? c - o : 4 * pp, 0);
+                }
+            }
+        }
+        // totals of this round -> carry (every thread computes the same: last lane of last warp's inclusive value)
+        __syncthreads();
+        if (tid == 1023) {
+#pragma unroll
+            for (int q = 0; q < 7; q++) wsum[q][0] = ex[q] + v[q];
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < 7; q++) carry[q] = wsum[q][0];
+        __syncthreads();
+    }
+    if (tid == 0) {
+        for (int q = 0; q < 6; q++) counts[q] = carry[q + 1];
+        counts[6] = carry[0];
+    }
+    for (int p = tid; p < P; p += 1024) {
+        const int e = ids[p];
+        if ((valid && !valid[p]) || e < 0 || e >= n_experts || slot_row[e] < 0) continue;
+        const int pos = atomicAdd(&cur[e], 1);   // the order inside an expert's range is arbitrary: a pair's row depends on its own input only
+        order[pos] = p;
+        src_tok[pos] = p / Kx;
+    }
+}
+
+// One CTA of 128 threads per position: the operand record (B fragments of every unit, group sums, exponent) of row
+// src[pos] of x (identity: row pos), written to recs + pos * rstride.
+template <bool HILO, bool SRC_BF16>
+__global__ void __launch_bounds__(128) g3_records_kernel(const void *x, const int *src, int identity, const int *total, int K, uint8_t *recs, int rstride) {
+    extern __shared__ __align__(16) uint8_t g3row[];
+    __shared__ float wmax[4];
+    const int pos = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (pos >= *total) return;
+    const size_t row = identity ? (size_t)pos : (size_t)src[pos];
+    const int rowb = K * (SRC_BF16 ? 2 : 4);
+    const uint4 *g = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(x) + row * rowb);
+    for (int i = tid; i < rowb / 16; i += 128) reinterpret_cast<uint4 *>(g3row)[i] = g[i];
+    __syncthreads();
+    uint8_t *rec = recs + (size_t)pos * rstride;
+    const int secb = sec3_bytes(K), hdr_off = secb * (HILO ? 2 : 1);
+    float amax = 0.f;
+    for (int grp = warp; grp < K / 64; grp += 4) {       // a warp per group of 64: two values per lane
+        float v[2];
+        if (SRC_BF16) {
+            const uint32_t u = reinterpret_cast<const uint32_t *>(g3row)[grp * 32 + lane];
+            v[0] = __uint_as_float(u << 16);
+            v[1] = __uint_as_float(u & 0xffff0000u);
+        } else {
+            const float2 f = reinterpret_cast<const float2 *>(g3row)[grp * 32 + lane];
+            v[0] = f.x;
+            v[1] = f.y;
+        }
+        float s = v[0] + v[1];
+        amax = fmaxf(amax, fmaxf(fabsf(v[0]), fabsf(v[1])));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) reinterpret_cast<float *>(rec + hdr_off)[grp] = s;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) wmax[warp] = amax;
+    __syncthreads();
+    const float m = fmaxf(fmaxf(wmax[0], wmax[1]), fmaxf(wmax[2], wmax[3]));
+    int E = (int)(__float_as_uint(m) >> 23) + 1;
+    E = E < 30 ? 30 : (E > 230 ? 230 : E);
+    if (tid == 0) reinterpret_cast<float *>(rec + hdr_off)[K / 64] = __int_as_float(E);
+    for (int it = tid; it < (K / 128) * 4; it += 128) build_frag3_item<HILO, SRC_BF16>(g3row, it >> 2, it & 3, E, rec, secb);
+}
+
+// grid (tile splits, items), 256 threads = 8 warps, two CTAs per SM.  A warp takes whole tiles (16 fragment rows,
+// all of K); the item's records sit in shared memory; the packed units come straight from the pool by coalesced
+// loads (768 contiguous bytes per unit), two units ahead.
+template <bool HILO, bool FP16S, int NPASS, bool DOWN>
+__global__ void __launch_bounds__(256, 2) moe_group3_kernel(const G3Args a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int PP = HILO ? 2 : 4, NTOK = PP * NPASS;
+    if ((int)blockIdx.y >= *a.n_items) return;
+    const int4 item = a.items[blockIdx.y];
+    const int count = item.z;
+    const FinchTile T = finch_tile(a.hidden, a.inter);
+    const int K = DOWN ? a.inter : a.hidden, units = K / 128;
+    const int ntiles = DOWN ? T.nTB : T.nTA, tile_bytes = DOWN ? T.tileB : T.tileA;
+    const uint8_t *tiles = a.pool_base + (size_t)a.slot_row[item.x] * a.slot_bytes + (DOWN ? T.b_base : 0);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+    const int sec = sec3_bytes(K), hdr_off = sec * (HILO ? 2 : 1);
+    // records of the item's tokens
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(a.recs + (size_t)item.y * a.rstride);
+        uint4 *dst = reinterpret_cast<uint4 *>(smem);
+        const int n16 = count * a.rstride / 16;
+        for (int i = tid; i < n16; i += 256) dst[i] = __ldg(src + i);
+    }
+    __syncthreads();
+    const uint32_t rec32 = finch_smem_u32(smem);
+    const bool mine = (g & 1) == (t >> 1);
+    const int pos_b = HILO ? (g >> 2) : (g >> 1), pos_o = HILO ? (t >> 1) : t;
+    const uint32_t sec_b = HILO ? (uint32_t)(((g >> 1) & 1) * sec) : 0u;
+    // B operand of this lane per pass: the record section of its column's token, or nothing (zeros in registers) when
+    // the lane's k-slots belong to the other group of the unit or the column has no token.  Plain loads from shared
+    // memory (the records do not change after the barrier), so the compiler schedules them ahead of the MMAs.
+    const uint8_t *pb[NPASS];
+    uint32_t ph[NPASS];
+    bool live[NPASS], hasb[NPASS];
+#pragma unroll
+    for (int ps = 0; ps < NPASS; ps++) {
+        const int tb = ps * PP + pos_b, to = ps * PP + pos_o;
+        hasb[ps] = mine && tb < count;
+        pb[ps] = smem + (hasb[ps] ? tb * a.rstride + (int)sec_b : 0) + t * 16;
+        live[ps] = to < count;
+        ph[ps] = rec32 + (uint32_t)((live[ps] ? to : 0) * a.rstride + hdr_off);
+    }
+    struct Unit {
+        uint2 q0, q1, q2;
+        uint4 s;
+    };
+    for (int tile = blockIdx.x * 8 + warp; tile < ntiles; tile += gridDim.x * 8) {
+        const uint8_t *tp = tiles + (size_t)tile * tile_bytes;
+        auto load_unit = [&](int u, Unit &o) {
+            const uint2 *w = reinterpret_cast<const uint2 *>(tp + (size_t)u * 768 + lane * 24);
+            o.q0 = __ldg(w);
+            o.q1 = __ldg(w + 1);
+            o.q2 = __ldg(w + 2);
+            o.s = __ldg(reinterpret_cast<const uint4 *>(tp + (size_t)units * 768 + u * 128 + g * 16));
+        };
+        float run[NPASS][4];   // runA, runB, biasA, biasB of every pass
+#pragma unroll
+        for (int ps = 0; ps < NPASS; ps++) run[ps][0] = run[ps][1] = run[ps][2] = run[ps][3] = 0.f;
+        Unit nx0, nx1;
+        load_unit(0, nx0);
+        load_unit(units > 1 ? 1 : 0, nx1);
+#pragma unroll 1
+        for (int u = 0; u < units; u += 2) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                if (u + h >= units) break;
+                const Unit cu = h ? nx1 : nx0;
+                if (u + h + 2 < units) load_unit(u + h + 2, h ? nx1 : nx0);
+                const uint2 q0 = cu.q0, q1 = cu.q1, q2 = cu.q2;
+                const uint32_t av1 = __funnelshift_r(q0.x, q0.y, 8), av3 = __funnelshift_r(q0.y, q1.x, 8), av5 = q1.x >> 8;
+                const uint32_t bv1 = __funnelshift_r(q1.y, q2.x, 8), bv3 = __funnelshift_r(q2.x, q2.y, 8), bv5 = q2.y >> 8;
+                float sA0, sA1, sB0, sB1, bA0, bA1, bB0, bB1;
+                widen2<FP16S>(cu.s.x, sA0, sA1);
+                widen2<FP16S>(cu.s.y, sB0, sB1);
+                widen2<FP16S>(cu.s.z, bA0, bA1);
+                widen2<FP16S>(cu.s.w, bB0, bB1);
+                const int uo = (u + h) * UB;
+                // The nine MMAs of the unit, two at a time: their A fragments are extracted once and used by every pass,
+                // and the passes' accumulators are independent chains that keep the tensor pipe busy between them.
+                float acc[NPASS][4];
+#define FINCH_A3(j, r)                                                     \
+    r[0] = extract3_one<2 * (j)>(q0.x, av1, q0.y, av3, q1.x, av5);         \
+    r[1] = extract3_one<2 * (j)>(q1.y, bv1, q2.x, bv3, q2.y, bv5);         \
+    r[2] = extract3_one<2 * (j) + 1>(q0.x, av1, q0.y, av3, q1.x, av5);     \
+    r[3] = extract3_one<2 * (j) + 1>(q1.y, bv1, q2.x, bv3, q2.y, bv5);
+#define FINCH_PAIR3(jp)                                                                                   \
+    {                                                                                                     \
+        uint32_t A0[4], A1[4];                                                                            \
+        FINCH_A3(2 * (jp), A0) FINCH_A3(2 * (jp) + 1, A1)                                                 \
+        uint4 bb[NPASS];                                                                                  \
+        _Pragma("unroll") for (int ps = 0; ps < NPASS; ps++)                                              \
+            bb[ps] = hasb[ps] ? *reinterpret_cast<const uint4 *>(pb[ps] + uo + (jp) * 64) : make_uint4(0u, 0u, 0u, 0u); \
+        _Pragma("unroll") for (int ps = 0; ps < NPASS; ps++) {                                            \
+            if ((jp) == 0) mma16816_z(acc[ps], A0[0], A0[1], A0[2], A0[3], bb[ps].x, bb[ps].y);           \
+            else mma16816(acc[ps], A0[0], A0[1], A0[2], A0[3], bb[ps].x, bb[ps].y);                       \
+        }                                                                                                 \
+        _Pragma("unroll") for (int ps = 0; ps < NPASS; ps++) mma16816(acc[ps], A1[0], A1[1], A1[2], A1[3], bb[ps].z, bb[ps].w); \
+    }
+                FINCH_PAIR3(0) FINCH_PAIR3(1) FINCH_PAIR3(2) FINCH_PAIR3(3)
+                {
+                    uint32_t A8[4];
+                    FINCH_A3(8, A8)
+                    uint2 b8[NPASS];
+#pragma unroll
+                    for (int ps = 0; ps < NPASS; ps++)   // section + 256 + t * 8 (pb carries t * 16)
+                        b8[ps] = hasb[ps] ? *reinterpret_cast<const uint2 *>(pb[ps] + uo + 256 - t * 8) : make_uint2(0u, 0u);
+#pragma unroll
+                    for (int ps = 0; ps < NPASS; ps++) mma16816(acc[ps], A8[0], A8[1], A8[2], A8[3], b8[ps].x, b8[ps].y);
+                }
+#undef FINCH_PAIR3
+#undef FINCH_A3
+#pragma unroll
+                for (int ps = 0; ps < NPASS; ps++) {
+                    const uint2 xgb = lds64(ph[ps] + (uint32_t)((u + h) * 8));
+                    const float x0 = __uint_as_float(xgb.x), x1 = __uint_as_float(xgb.y);
+                    run[ps][0] = fmaf(sA1, acc[ps][1], fmaf(sA0, acc[ps][0], run[ps][0]));
+                    run[ps][1] = fmaf(sB1, acc[ps][3], fmaf(sB0, acc[ps][2], run[ps][1]));
+                    run[ps][2] = fmaf(bA1, x1, fmaf(bA0, x0, run[ps][2]));
+                    run[ps][3] = fmaf(bB1, x1, fmaf(bB0, x0, run[ps][3]));
+                }
+            }
+        }
+#pragma unroll
+        for (int ps = 0; ps < NPASS; ps++) {
+            float runA = run[ps][0], runB = run[ps][1];
+            if (HILO) {
+                const float oA = __shfl_xor_sync(0xffffffffu, runA, 1), oB = __shfl_xor_sync(0xffffffffu, runB, 1);
+                runA += oA * (1.0f / 2048.0f);
+                runB += oB * (1.0f / 2048.0f);
+            }
+            if (live[ps] && (!HILO || !(t & 1))) {
+                const float fac = pow2_biased(__float_as_int(lds32f(ph[ps] + (uint32_t)((K / 64) * 4))) + 17);
+                const float vA = fmaf(runA, fac, run[ps][2]), vB = fmaf(runB, fac, run[ps][3]);
+                const int pos = item.y + ps * PP + pos_o;
+                if (DOWN) {
+                    float *o = a.out + (size_t)a.order[pos] * a.hidden + 16 * tile + g;
+                    o[0] = vA;
+                    o[8] = vB;
+                } else {
+                    a.out[(size_t)pos * a.inter + 8 * tile + g] = __fdividef(vA, 1.0f + __expf(-vA)) * vB;
+                }
+            }
+        }
+    }
+}
+
+template <bool HILO, bool FP16S, bool DOWN>
+static cudaError_t g3_launch_lists(cudaStream_t st, G3Args a, int4 *const lists[3], const int *counts, const int bounds[3], int split, int rstride,
+                                   int K) {
+    constexpr int PP = HILO ? 2 : 4;
+    const int sec = sec3_bytes(K);
+    cudaError_t e;
+    a.items = lists[0];
+    a.n_items = counts;
+    moe_group3_kernel<HILO, FP16S, 1, DOWN><<<dim3(split, bounds[0]), 256, PP * 1 * rstride + sec, st>>>(a);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    a.items = lists[1];
+    a.n_items = counts + 1;
+    moe_group3_kernel<HILO, FP16S, 2, DOWN><<<dim3(split, bounds[1]), 256, PP * 2 * rstride + sec, st>>>(a);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    a.items = lists[2];
+    a.n_items = counts + 2;
+    moe_group3_kernel<HILO, FP16S, 4, DOWN><<<dim3(split, bounds[2]), 256, PP * 4 * rstride + sec, st>>>(a);
+    return cudaGetLastError();
+}
+
+template <bool HILO, bool FP16S, bool DOWN>
+static int g3_attrs(finch_ctx *ctx, int rstride, int K) {
+    constexpr int PP = HILO ? 2 : 4;
+    const int sec = sec3_bytes(K);
+    int rc;
+    if ((rc = finch_func_attr_once(ctx, (const void *)moe_group3_kernel<HILO, FP16S, 1, DOWN>, PP * 1 * rstride + sec))) return rc;
+    if ((rc = finch_func_attr_once(ctx, (const void *)moe_group3_kernel<HILO, FP16S, 2, DOWN>, PP * 2 * rstride + sec))) return rc;
+    return finch_func_attr_once(ctx, (const void *)moe_group3_kernel<HILO, FP16S, 4, DOWN>, PP * 4 * rstride + sec);
+}
+
 }  // namespace
+
+// ---- host side of the grouped 3-bit passes (called by finch_encode_moe_prefill) ----
+namespace {
+struct G3Plan {
+    int P, ppa, bound01, bound2a, bound2b, rs_a, rs_b;
+    size_t o_order, o_src, o_counts, o_la[3], o_lb[3], o_ra, o_rb, o_act, total;
+};
+G3Plan g3_plan(const finch_config &c, int T) {
+    G3Plan p{};
+    p.P = T * c.top_k;
+    const int hilo_a = c.act_dtype != FINCH_BF16;
+    p.ppa = hilo_a ? 2 : 4;
+    p.bound01 = c.n_experts < p.P ? c.n_experts : p.P;
+    p.bound2a = p.P / (4 * p.ppa) + p.bound01 + 1;
+    p.bound2b = p.P / 8 + p.bound01 + 1;
+    p.rs_a = rec3_bytes(c.hidden, hilo_a);
+    p.rs_b = rec3_bytes(c.moe_inter, 1);
+    size_t off = 0;
+    auto take = [&](size_t b) {
+        const size_t r = off;
+        off += (b + 255) & ~(size_t)255;
+        return r;
+    };
+    p.o_order = take((size_t)p.P * 4);
+    p.o_src = take((size_t)p.P * 4);
+    p.o_counts = take(64);
+    p.o_la[0] = take((size_t)p.bound01 * 16);
+    p.o_la[1] = take((size_t)p.bound01 * 16);
+    p.o_la[2] = take((size_t)p.bound2a * 16);
+    p.o_lb[0] = take((size_t)p.bound01 * 16);
+    p.o_lb[1] = take((size_t)p.bound01 * 16);
+    p.o_lb[2] = take((size_t)p.bound2b * 16);
+    p.o_ra = take((size_t)p.P * p.rs_a);
+    p.o_rb = take((size_t)p.P * p.rs_b);
+    p.o_act = take((size_t)p.P * c.moe_inter * 4);
+    p.total = off;
+    return p;
+}
+}  // namespace
+
+size_t finch_group3_ws_bytes(finch_ctx *ctx, int T) { return g3_plan(ctx->cfg, T).total; }
+
+// down_out[pair][hidden] = expert(pair) applied to its token's row, for every usable pair of the chunk (pairs that are
+// masked, out of range or not resident are left alone).  ws: finch_group3_ws_bytes(ctx, T) bytes of device memory.
+int finch_group3_prefill(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int layer, const void *x, const int32_t *ids, const uint8_t *valid, int T, void *ws,
+                         float *down_out) {
+    const finch_config &c = ctx->cfg;
+    if (c.n_experts > 4096) return finch_fail(ctx, FINCH_E_UNSUPPORTED, "the grouped prefill passes take at most 4096 experts");
+    const G3Plan p = g3_plan(c, T);
+    char *w = (char *)ws;
+    int *order = (int *)(w + p.o_order), *src_tok = (int *)(w + p.o_src), *counts = (int *)(w + p.o_counts);
+    int4 *la[3] = {(int4 *)(w + p.o_la[0]), (int4 *)(w + p.o_la[1]), (int4 *)(w + p.o_la[2])};
+    int4 *lb[3] = {(int4 *)(w + p.o_lb[0]), (int4 *)(w + p.o_lb[1]), (int4 *)(w + p.o_lb[2])};
+    uint8_t *recs_a = (uint8_t *)(w + p.o_ra), *recs_b = (uint8_t *)(w + p.o_rb);
+    float *act = (float *)(w + p.o_act);
+    const int32_t *slot_row = pool->slot_table_dev + (size_t)layer * pool->n_experts;
+    const bool hilo_a = c.act_dtype != FINCH_BF16, fp16s = c.scale_dtype == FINCH_FP16;
+    int rc;
+    if (hilo_a) rc = fp16s ? g3_attrs<true, true, false>(ctx, p.rs_a, c.hidden) : g3_attrs<true, false, false>(ctx, p.rs_a, c.hidden);
+    else rc = fp16s ? g3_attrs<false, true, false>(ctx, p.rs_a, c.hidden) : g3_attrs<false, false, false>(ctx, p.rs_a, c.hidden);
+    if (rc) return rc;
+    if ((rc = fp16s ? g3_attrs<true, true, true>(ctx, p.rs_b, c.moe_inter) : g3_attrs<true, false, true>(ctx, p.rs_b, c.moe_inter))) return rc;
+
+    g3_sort_kernel<<<1, 1024, 2 * c.n_experts * sizeof(int), st>>>(ids, valid, slot_row, c.n_experts, p.P, c.top_k, p.ppa, 2, order, src_tok, la[0], la[1], la[2],
+                                                                    lb[0], lb[1], lb[2], counts);
+    FINCH_CUDA_OK(ctx, cudaGetLastError());
+    if (hilo_a) g3_records_kernel<true, false><<<p.P, 128, c.hidden * 4, st>>>(x, src_tok, 0, counts + 6, c.hidden, recs_a, p.rs_a);
+    else g3_records_kernel<false, true><<<p.P, 128, c.hidden * 2, st>>>(x, src_tok, 0, counts + 6, c.hidden, recs_a, p.rs_a);
+    FINCH_CUDA_OK(ctx, cudaGetLastError());
+    G3Args a{};
+    a.pool_base = pool->base;
+    a.slot_bytes = pool->slot_bytes;
+    a.slot_row = slot_row;
+    a.hidden = c.hidden;
+    a.inter = c.moe_inter;
+    a.order = order;
+    a.status = ctx->dev_status;
+    a.recs = recs_a;
+    a.rstride = p.rs_a;
+    a.out = act;
+    const int bounds_a[3] = {p.bound01, p.bound01, p.bound2a}, bounds_b[3] = {p.bound01, p.bound01, p.bound2b};
+    cudaError_t e;
+    if (hilo_a) e = fp16s ? g3_launch_lists<true, true, false>(st, a, la, counts, bounds_a, 2, p.rs_a, c.hidden)
+                          : g3_launch_lists<true, false, false>(st, a, la, counts, bounds_a, 2, p.rs_a, c.hidden);
+    else e = fp16s ? g3_launch_lists<false, true, false>(st, a, la, counts, bounds_a, 2, p.rs_a, c.hidden)
+                   : g3_launch_lists<false, false, false>(st, a, la, counts, bounds_a, 2, p.rs_a, c.hidden);
+    FINCH_CUDA_OK(ctx, e);
+    g3_records_kernel<true, false><<<p.P, 128, c.moe_inter * 4, st>>>(act, src_tok, 1, counts + 6, c.moe_inter, recs_b, p.rs_b);
+    FINCH_CUDA_OK(ctx, cudaGetLastError());
+    a.recs = recs_b;
+    a.rstride = p.rs_b;
+    a.out = down_out;
+    e = fp16s ? g3_launch_lists<true, true, true>(st, a, lb, counts + 3, bounds_b, 4, p.rs_b, c.moe_inter)
+              : g3_launch_lists<true, false, true>(st, a, lb, counts + 3, bounds_b, 4, p.rs_b, c.moe_inter);
+    FINCH_CUDA_OK(ctx, e);
+    ctx->launches += 9;
+    return FINCH_OK;
+}
 
 // n_calls batches of B tokens each (rows [c * B, (c + 1) * B) of the inputs) in one sequence of three launches.
 // Batch own_call gets shared / h_mid and writes hidden_out; the others write their routed sums to rows_out.

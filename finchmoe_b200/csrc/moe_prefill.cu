@@ -21,6 +21,11 @@
 // to about 1e-5 of an output's scale; the parity tests hold it to the same bar as the decode path.
 #include "dqgemm_tc.cuh"
 
+// the grouped 3-bit passes on mma.sync (moe_decode.cu)
+size_t finch_group3_ws_bytes(finch_ctx *ctx, int T);
+int finch_group3_prefill(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int layer, const void *x, const int32_t *ids, const uint8_t *valid, int T, void *ws,
+                         float *down_out);
+
 namespace {
 
 constexpr int CHUNK = 512;   // default tokens per tensor-core pass: 4096 pairs (finch_set_prefill_chunk changes it)
@@ -237,8 +242,9 @@ int ensure_ws(finch_ctx *ctx, size_t bytes, cudaStream_t st) {
     return FINCH_OK;
 }
 
+// grouped: the routed experts go through the grouped mma.sync passes instead of the two tcgen05 GEMMs
 int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int layer, const void *h_post, const int32_t *ids,
-                     const float *weights, const uint8_t *valid, const finch_shared *shared, const float *h_mid, float *hidden_out, int T) {
+                     const float *weights, const uint8_t *valid, const finch_shared *shared, const float *h_mid, float *hidden_out, int T, bool grouped) {
     const finch_config &c = ctx->cfg;
     const int P = T * c.top_k, H = c.hidden, I = c.moe_inter, Is = shared ? shared->gate.out_dim : 0;
     const int32_t *slot_row = pool->slot_table_dev + (size_t)layer * pool->n_experts;
@@ -253,6 +259,7 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
     const int max_items = P / 16 + c.n_experts + 1;   // tiles of at least 16 tokens, plus one ragged tile per expert
     const size_t o_ia = take((size_t)max_items * sizeof(int2)), o_ib = take((size_t)max_items * sizeof(int2)), o_ni = take(2 * sizeof(int));
     const size_t o_xb = take((size_t)T * H * 2), o_xl = take((size_t)T * H * 2), o_sg = take((size_t)T * Is * 4), o_su = take((size_t)T * Is * 4), o_sact = take((size_t)T * Is * 4);
+    const size_t o_g3 = grouped ? take(finch_group3_ws_bytes(ctx, T)) : 0;
     int rc = ensure_ws(ctx, off, st);
     if (rc) return rc;
     char *ws = (char *)ctx->pf_ws;
@@ -265,6 +272,30 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
 
     // token tiles: as many tokens as still let two CTAs share an SM (an expert's tile is dequantised once per token tile)
     const bool x_lo_needed = c.act_dtype != FINCH_BF16;   // fp32 activations travel as two bf16 planes
+    if (grouped) {
+        const uint16_t *x = (const uint16_t *)h_post, *x_lo = nullptr;
+        if (x_lo_needed && shared) {
+            pf_to_bf16_kernel<<<148, 256, 0, st>>>((const float *)h_post, xb, xl, (size_t)T * H);
+            FINCH_CUDA_OK(ctx, cudaGetLastError());
+            x = xb;
+            x_lo = xl;
+            ctx->launches++;
+        }
+        if ((rc = finch_group3_prefill(ctx, st, pool, layer, h_post, ids, valid, T, ws + o_g3, down))) return rc;
+        if (shared) {
+            if ((rc = dense4_gemm(ctx, st, &shared->gate, x, x_lo, sg, T))) return rc;
+            if ((rc = dense4_gemm(ctx, st, &shared->up, x, x_lo, su, T))) return rc;
+            pf_swiglu_kernel<<<148, 256, 0, st>>>(sg, su, sact, sact_lo, (size_t)T * Is);
+            FINCH_CUDA_OK(ctx, cudaGetLastError());
+            if ((rc = dense4_gemm(ctx, st, &shared->down, sact, sact_lo, shared_out, T))) return rc;
+            ctx->launches++;
+        }
+        pf_combine_kernel<<<dim3((H + 255) / 256, T), 256, 0, st>>>(ids, valid, slot_row, c.n_experts, weights, c.top_k, down, shared ? shared_out : nullptr,
+                                                                    shared ? shared->gate_score : nullptr, h_mid, hidden_out, H);
+        FINCH_CUDA_OK(ctx, cudaGetLastError());
+        ctx->launches++;
+        return FINCH_OK;
+    }
     const int tn_a = tn_max_for(T < 64 ? T : (x_lo_needed ? 32 : 64)), tn_b = 32;
     // the grids of the two grouped GEMMs hold one CTA row per possible (expert, token tile): at most one ragged tile
     // per expert that is resident now, plus the full tiles
@@ -335,7 +366,7 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
 }  // namespace
 
 extern "C" int finch_set_prefill_mode(finch_ctx *ctx, int mode) {
-    if (!ctx || mode < 0 || mode > 2) return FINCH_E_ARG;
+    if (!ctx || mode < 0 || mode > 3) return FINCH_E_ARG;
     ctx->prefill_mode = mode;
     return FINCH_OK;
 }
@@ -353,7 +384,11 @@ extern "C" int finch_encode_moe_prefill(finch_ctx *ctx, finch_stream stream, fin
     if (!ctx || !pool || !h_post || !expert_ids || !weights || !hidden_out || T < 1) return FINCH_E_ARG;
     const finch_config &c = ctx->cfg;
     const size_t elt = c.act_dtype == FINCH_BF16 ? 2 : 4;
-    bool tc = ctx->prefill_mode == 2 || (ctx->prefill_mode == 0 && T >= TC_MIN_TOKENS);
+    bool tc = ctx->prefill_mode >= 2 || (ctx->prefill_mode == 0 && T >= TC_MIN_TOKENS);
+    // which kernels serve the routed experts of a tensor-core chunk: the grouped mma.sync passes (mode 3) unpack a
+    // unit once for up to 16 tokens and win while experts see few tokens; the tcgen05 GEMMs (mode 2) win when a tile
+    // of 64 tokens fills (the rows an expert-parallel rank receives).  By chunk length: the former.
+    const bool grouped = ctx->prefill_mode == 3 || ctx->prefill_mode == 0;
     // shapes the tensor-core kernels take: whole 128-row tiles, 128-value K blocks, a 3-bit pool
     if (c.expert_bits != 3 || c.hidden % 128 || c.moe_inter % 128 || c.top_k > 8 || c.n_experts > 1024) tc = false;
     if (tc && shared) {
@@ -382,7 +417,7 @@ extern "C" int finch_encode_moe_prefill(finch_ctx *ctx, finch_stream stream, fin
             const int rc = prefill_tc_chunk(ctx, st, pool, layer, (const char *)h_post + (size_t)t0 * c.hidden * elt,
                                             expert_ids + (size_t)t0 * c.top_k, weights + (size_t)t0 * c.top_k,
                                             valid ? valid + (size_t)t0 * c.top_k : nullptr, shared ? &sh : nullptr,
-                                            h_mid ? h_mid + (size_t)t0 * c.hidden : nullptr, hidden_out + (size_t)t0 * c.hidden, n);
+                                            h_mid ? h_mid + (size_t)t0 * c.hidden : nullptr, hidden_out + (size_t)t0 * c.hidden, n, grouped);
             if (rc) return rc;
         }
         return FINCH_OK;

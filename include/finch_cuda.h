@@ -266,9 +266,15 @@ FINCH_API int finch_debug_dequant(finch_ctx *ctx, const finch_wdesc *w, uint8_t 
 FINCH_API int finch_profile_enable(finch_ctx *ctx, int on);
 FINCH_API int finch_profile_read(finch_ctx *ctx, float *ms_gateup, float *ms_down_combine, int *n_calls);
 
-/* Path selection of finch_encode_moe_prefill: 0 = by chunk length (default),
- * 1 = always the sub-batch path (exact weights, fp32 activations), 2 = always
- * the tensor-core path.  The reference has one path only (per-position CMD3). */
+/* Path selection of finch_encode_moe_prefill: 0 = by chunk length (default:
+ * chunks of 128 tokens and more as mode 3, shorter ones as mode 1), 1 = always the
+ * sub-batch path through the decode kernels, 2 = the routed experts as two grouped
+ * dequant-GEMMs on tcgen05 (best when experts see 64 tokens and more, e.g. the rows
+ * an expert-parallel rank receives), 3 = the routed experts as grouped mma.sync
+ * passes that unpack a unit of codes once for up to 16 tokens of its expert (best at
+ * the few tokens per expert of an ordinary chunk).  In modes 2 and 3 the shared
+ * expert runs as dense tcgen05 GEMMs.  The reference has one path only
+ * (per-position CMD3). */
 FINCH_API int finch_set_prefill_mode(finch_ctx *ctx, int mode);
 
 /* Tokens per pass of the tensor-core path of finch_encode_moe_prefill (the

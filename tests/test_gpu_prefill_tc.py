@@ -51,7 +51,8 @@ def test_dense_4bit_gemm_vs_oracle(api, shape, M):
 
 
 @pytest.mark.parametrize("T,act_dtype", [(16, L.F32), (23, L.BF16), (64, L.F32), (200, L.BF16)])
-def test_prefill_tensor_core_small_vs_oracle(api, T, act_dtype):
+@pytest.mark.parametrize("mode", [2, 3])
+def test_prefill_tensor_core_small_vs_oracle(api, T, act_dtype, mode):
     cfg = dict(hidden=256, inter=128, sd=L.BF16)
     ctx = api.Context(hidden=256, n_experts=16, top_k=8, moe_inter=128, shared_inter=128, n_layers=1,
                       scale_dtype=L.BF16, act_dtype=act_dtype, max_tokens=256)
@@ -70,10 +71,10 @@ def test_prefill_tensor_core_small_vs_oracle(api, T, act_dtype):
         shd = ctx.make_shared(*[ctx.upload_tensor(t) for t in sh])
         score = rng.normal(0, 1, size=T).astype(np.float32)
         h_mid = rng.normal(0, 1, size=(T, 256)).astype(np.float32)
-        ctx.set_prefill_mode(2)
+        ctx.set_prefill_mode(mode)
         out = ctx.moe_forward_host(pool, 0, x, ids, w, valid=valid, shared=shd, gate_score=score, h_mid=h_mid)
         want = oracle_layer(blocks, ids, w, valid, x, cfg, shared=sh, score=score, h_mid=h_mid)
-        _report(f"tensor-core prefill T={T}", out, want)
+        _report(f"prefill mode {mode} T={T}", out, want)
         assert_close(out, want, f"tensor-core prefill T={T}")
         out2 = ctx.moe_forward_host(pool, 0, x, ids, w)
         want2 = oracle_layer(blocks, ids, w, None, x, cfg)
@@ -88,11 +89,12 @@ def test_prefill_tensor_core_small_vs_oracle(api, T, act_dtype):
         ctx.destroy()
 
 
-def test_prefill_tensor_core_full_size_vs_oracle(api):
+@pytest.mark.parametrize("mode", [2, 3])
+def test_prefill_tensor_core_full_size_vs_oracle(api, mode):
     """Hidden 2048, inter 512, 256 experts, top-8, Zipf routing, fp16 scales, bf16 activations: a 64-token chunk."""
     T = 64
     ctx = api.Context(max_tokens=64, n_layers=1, scale_dtype=L.FP16, act_dtype=L.BF16)
-    ctx.set_prefill_mode(2)
+    ctx.set_prefill_mode(mode)
     pool = ctx.pool(n_layers=1)
     try:
         rng = synth.rng_for(7, T)
@@ -121,7 +123,8 @@ def test_prefill_tensor_core_full_size_vs_oracle(api):
         ctx.destroy()
 
 
-def test_prefill_512_tokens_full_size_sampled_oracle_and_exact_path(api):
+@pytest.mark.parametrize("mode", [2, 3])
+def test_prefill_512_tokens_full_size_sampled_oracle_and_exact_path(api, mode):
     """The largest chunk (512 tokens, hidden 2048, 256 experts, Zipf top-8) through the tensor-core path: every row
     finite, 24 sampled rows against the oracle's exact arithmetic, and all rows against the sub-batch path."""
     T = 512
@@ -136,7 +139,7 @@ def test_prefill_512_tokens_full_size_sampled_oracle_and_exact_path(api):
         shd = ctx.make_shared(*[ctx.upload_tensor(t) for t in sh])
         score = rng.normal(0, 1, size=T).astype(np.float32)
         h_mid = synth.activations(rng, T, 2048)
-        ctx.set_prefill_mode(2)
+        ctx.set_prefill_mode(mode)
         out = ctx.moe_forward_host(pool, 0, x, ids, w, shared=shd, gate_score=score, h_mid=h_mid)
         assert np.all(np.isfinite(out))
         sample = rng.choice(T, size=24, replace=False)
