@@ -1622,16 +1622,18 @@ __global__ void __launch_bounds__(256, 2) moe_group3_kernel(const G3Args a) {
         float run[NPASS][4];   // runA, runB, biasA, biasB of every pass
 #pragma unroll
         for (int ps = 0; ps < NPASS; ps++) run[ps][0] = run[ps][1] = run[ps][2] = run[ps][3] = 0.f;
-        Unit nx0, nx1;
-        load_unit(0, nx0);
-        load_unit(units > 1 ? 1 : 0, nx1);
-#pragma unroll 1
-        for (int u = 0; u < units; u += 2) {
+        // packed units are requested PD units ahead of their use (more where few passes leave registers free)
+        constexpr int PD = NPASS == 4 ? 2 : 4;
+        Unit nx[PD];
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
+        for (int d = 0; d < PD; d++) load_unit(d < units ? d : 0, nx[d]);
+#pragma unroll 1
+        for (int u = 0; u < units; u += PD) {
+#pragma unroll
+            for (int h = 0; h < PD; h++) {
                 if (u + h >= units) break;
-                const Unit cu = h ? nx1 : nx0;
-                if (u + h + 2 < units) load_unit(u + h + 2, h ? nx1 : nx0);
+                const Unit cu = nx[h];
+                if (u + h + PD < units) load_unit(u + h + PD, nx[h]);
                 const uint2 q0 = cu.q0, q1 = cu.q1, q2 = cu.q2;
                 const uint32_t av1 = __funnelshift_r(q0.x, q0.y, 8), av3 = __funnelshift_r(q0.y, q1.x, 8), av5 = q1.x >> 8;
                 const uint32_t bv1 = __funnelshift_r(q1.y, q2.x, 8), bv3 = __funnelshift_r(q2.x, q2.y, 8), bv5 = q2.y >> 8;
@@ -1713,16 +1715,17 @@ __global__ void __launch_bounds__(256, 2) moe_group3_kernel(const G3Args a) {
 template <bool HILO, bool FP16S, bool DOWN>
 static cudaError_t g3_launch_lists(cudaStream_t st, G3Args a, int4 *const lists[3], const int *counts, const int bounds[3], int split, int rstride,
                                    int K) {
+    // split: CTAs per item of the largest class; items with fewer tokens do less per tile and get more CTAs each
     constexpr int PP = HILO ? 2 : 4;
     const int sec = sec3_bytes(K);
     cudaError_t e;
     a.items = lists[0];
     a.n_items = counts;
-    moe_group3_kernel<HILO, FP16S, 1, DOWN><<<dim3(split, bounds[0]), 256, PP * 1 * rstride + sec, st>>>(a);
+    moe_group3_kernel<HILO, FP16S, 1, DOWN><<<dim3(4 * split, bounds[0]), 256, PP * 1 * rstride + sec, st>>>(a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     a.items = lists[1];
     a.n_items = counts + 1;
-    moe_group3_kernel<HILO, FP16S, 2, DOWN><<<dim3(split, bounds[1]), 256, PP * 2 * rstride + sec, st>>>(a);
+    moe_group3_kernel<HILO, FP16S, 2, DOWN><<<dim3(2 * split, bounds[1]), 256, PP * 2 * rstride + sec, st>>>(a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     a.items = lists[2];
     a.n_items = counts + 2;

@@ -267,7 +267,7 @@ FINCH_API int finch_profile_enable(finch_ctx *ctx, int on);
 FINCH_API int finch_profile_read(finch_ctx *ctx, float *ms_gateup, float *ms_down_combine, int *n_calls);
 
 /* Path selection of finch_encode_moe_prefill: 0 = by chunk length (default:
- * chunks of 128 tokens and more as mode 3, shorter ones as mode 1), 1 = always the
+ * chunks of 80 tokens and more as mode 3, shorter ones as mode 1), 1 = always the
  * sub-batch path through the decode kernels, 2 = the routed experts as two grouped
  * dequant-GEMMs on tcgen05 (best when experts see 64 tokens and more, e.g. the rows
  * an expert-parallel rank receives), 3 = the routed experts as grouped mma.sync
