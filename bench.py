@@ -459,6 +459,7 @@ class EpBench:
         from finchmoe_b200 import ep
         self.torch, self.ep, self.stack, self.dist, self.rank, self.world, self.args = torch, ep, stack, dist, rank, world, args
         self.backend = ep.GpuBackend(stack.ctx, stack.pool, max(self.BATCH, PREFILL_CHUNK) * world)
+        self.backend.tc_mode = args.ep_prefill_mode
         self.score_val = 0.1
         self.graphs = None
         # decode: the exchange goes through the ranks' own kernels over peer memory unless told (or forced) otherwise
@@ -627,18 +628,27 @@ class EpBench:
         self.pf = (rs, ids, w, x, xd, score, shared)
         self.backend.stats = []
 
+        fixed = self.args.ep_prefill_exchange == "fixed" and self.world > 1
+        layer_fn = self.ep.ep_layer_static if fixed else self.ep.ep_layer
+        self.pf_layer = layer_fn
+
         def step(_):
             for l in range(LAYERS):
-                self.ep.ep_layer(self.backend, self.dist, None, l, xd, ids[l], w[l], None, shared[l], None, out[l & 1])
+                layer_fn(self.backend, self.dist, None, l, xd, ids[l], w[l], None, shared[l], None, out[l & 1])
         secs, per_step = self.timed(steps, warmup, step)
         stats, self.backend.stats = self.backend.stats, None
-        per_call = stats[-LAYERS:]                                       # the last step's layers
-        rows_sent = sum(sum(c for d, c in enumerate(cs) if d != self.rank) for cs, _ in per_call)
-        rows_recv = sum(sum(cr) for _, cr in per_call)
+        if fixed:       # every token to every rank
+            rows_sent, rows_recv = T * (self.world - 1) * LAYERS, T * self.world * LAYERS
+        else:
+            per_call = stats[-LAYERS:]                                   # the last step's layers
+            rows_sent = sum(sum(c for d, c in enumerate(cs) if d != self.rank) for cs, _ in per_call)
+            rows_recv = sum(sum(cr) for _, cr in per_call)
         rec = self.backend.record_bytes()
         pairs_local = sum(int(((r[0] // (NEXP // self.world)) == self.rank).sum()) for r in rs)   # of this rank's own tokens
         link = rows_sent * (rec + HIDDEN * 4)
-        return {"chunk_tokens_per_gpu": T, "tokens_per_step": T * self.world, "steps": steps, "ms_per_step": secs / steps * 1e3,
+        return {"exchange": "fixed capacity (every token to every rank: two all-to-alls with equal splits, no host synchronisation)" if fixed
+                else "planned (a token goes where it has an expert; row counts exchanged first, one host synchronisation per layer)",
+                "chunk_tokens_per_gpu": T, "tokens_per_step": T * self.world, "steps": steps, "ms_per_step": secs / steps * 1e3,
                 "step_ms": spread(per_step), "tokens_per_s": T * self.world * steps / secs,
                 "rows_received_per_gpu_per_step": self.gather_ints(rows_recv),
                 "rows_sent_per_gpu_per_step": self.gather_ints(rows_sent),
@@ -667,7 +677,7 @@ class EpBench:
             rs, pids, pw, x, xd, score, shared = self.pf
             T = PREFILL_CHUNK
             out = torch.empty((T, HIDDEN), device="cuda")
-            self.ep.ep_layer(self.backend, self.dist, None, 0, xd, pids[0], pw[0], None, shared[0], None, out)
+            self.pf_layer(self.backend, self.dist, None, 0, xd, pids[0], pw[0], None, shared[0], None, out)
             torch.cuda.synchronize()
             want_p = torch.empty_like(out)
             ctx.set_prefill_mode(1)            # the exact sub-batch path: the decode kernels, 8 tokens at a time
@@ -1070,6 +1080,10 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS, help="fewer layers = a small case for profiler captures")
     ap.add_argument("--no-graph", action="store_true", help="launch from the host every step instead of replaying CUDA graphs")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"], help="N > 1, decode: the ranks' own kernels over peer memory, or NCCL all-to-alls")
+    ap.add_argument("--ep-prefill-mode", type=int, default=2, choices=[2, 3],
+                    help="N > 1, prefill: the received rows through the tcgen05 grouped GEMMs (2) or the grouped mma.sync passes (3)")
+    ap.add_argument("--ep-prefill-exchange", default="fixed", choices=["fixed", "planned"],
+                    help="N > 1, prefill: every token to every rank with equal splits and no host step, or the planned exchange")
     ap.add_argument("--only", default="", choices=["", "prefill", "decode", "lmhead"],
                     help="just the 512-token chunk, just the batch-8 decode steps (both on --layers layers), or just the output-projection matvecs (profiler captures)")
     args = ap.parse_args()
