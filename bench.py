@@ -462,6 +462,7 @@ class EpBench:
         self.backend.tc_mode = args.ep_prefill_mode
         self.score_val = 0.1
         self.graphs = None
+        self.graphs_extra = None
         # decode: the exchange goes through the ranks' own kernels over peer memory unless told (or forced) otherwise
         self.exchange = "none (one rank)"
         if world > 1:
@@ -632,9 +633,40 @@ class EpBench:
         layer_fn = self.ep.ep_layer_static if fixed else self.ep.ep_layer
         self.pf_layer = layer_fn
 
-        def step(_):
+        def layers(in_scope):
             for l in range(LAYERS):
-                layer_fn(self.backend, self.dist, None, l, xd, ids[l], w[l], None, shared[l], None, out[l & 1])
+                if fixed:
+                    layer_fn(self.backend, self.dist, None, l, xd, ids[l], w[l], None, shared[l], None, out[l & 1], in_scope=in_scope)
+                else:
+                    layer_fn(self.backend, self.dist, None, l, xd, ids[l], w[l], None, shared[l], None, out[l & 1])
+
+        def eager(_):
+            if fixed:
+                with self.backend.stream_scope():
+                    layers(True)
+            else:
+                layers(False)
+        step, launch = eager, "launched from the host every step"
+        if fixed and not self.args.no_graph:
+            # the fixed-capacity layer has no host step: the chunk's 40 layers (kernels and all-to-alls) replay from one CUDA graph
+            g, ok = None, 1
+            try:
+                eager(0)                              # workspaces, attributes and communicators exist before capture
+                torch.cuda.synchronize()
+                self.barrier()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=self.backend.stream, capture_error_mode="thread_local"):
+                    layers(True)
+                torch.cuda.synchronize()
+            except Exception:
+                g, ok = None, 0
+                torch.cuda.synchronize()
+            flag = torch.tensor([ok], device="cuda")
+            self.dist.all_reduce(flag, op=self.dist.ReduceOp.MIN)
+            if int(flag.item()) == 1:
+                self.graphs_extra = g                 # released with the others, no other name holds it
+                step, launch = (lambda _: self.graphs_extra.replay()), "one CUDA graph per chunk (kernels and all-to-alls)"
+            del g
         secs, per_step = self.timed(steps, warmup, step)
         stats, self.backend.stats = self.backend.stats, None
         if fixed:       # every token to every rank
@@ -648,6 +680,7 @@ class EpBench:
         link = rows_sent * (rec + HIDDEN * 4)
         return {"exchange": "fixed capacity (every token to every rank: two all-to-alls with equal splits, no host synchronisation)" if fixed
                 else "planned (a token goes where it has an expert; row counts exchanged first, one host synchronisation per layer)",
+                "launch": launch,
                 "chunk_tokens_per_gpu": T, "tokens_per_step": T * self.world, "steps": steps, "ms_per_step": secs / steps * 1e3,
                 "step_ms": spread(per_step), "tokens_per_s": T * self.world * steps / secs,
                 "rows_received_per_gpu_per_step": self.gather_ints(rows_recv),
@@ -754,6 +787,7 @@ class EpBench:
 
     def release(self):
         self.graphs = None
+        self.graphs_extra = None
         gc.collect()
 
 
@@ -1080,8 +1114,8 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS, help="fewer layers = a small case for profiler captures")
     ap.add_argument("--no-graph", action="store_true", help="launch from the host every step instead of replaying CUDA graphs")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"], help="N > 1, decode: the ranks' own kernels over peer memory, or NCCL all-to-alls")
-    ap.add_argument("--ep-prefill-mode", type=int, default=2, choices=[2, 3],
-                    help="N > 1, prefill: the received rows through the tcgen05 grouped GEMMs (2) or the grouped mma.sync passes (3)")
+    ap.add_argument("--ep-prefill-mode", type=int, default=0, choices=[0, 2, 3],
+                    help="N > 1, prefill: the received rows through the tcgen05 grouped GEMMs (2), the grouped mma.sync passes (3), or by tokens per expert (0)")
     ap.add_argument("--ep-prefill-exchange", default="fixed", choices=["fixed", "planned"],
                     help="N > 1, prefill: every token to every rank with equal splits and no host step, or the planned exchange")
     ap.add_argument("--only", default="", choices=["", "prefill", "decode", "lmhead"],

@@ -289,7 +289,9 @@ class GpuBackend:
         # tensor-core path in passes of `tc_chunk` rows (one sort and one pair of grouped GEMMs per pass) instead of
         # one decode pass per 8 rows.
         self.tc_rows_min = 9
-        self.tc_mode = 2             # 2: tcgen05 grouped GEMMs (experts that see many tokens), 3: grouped mma.sync passes
+        # how the received rows' experts run: 2 = tcgen05 grouped GEMMs, 3 = grouped mma.sync passes, 0 = by the tokens an
+        # expert sees on average (rows * top_k / n_experts): the GEMMs from 64 up, where a 64-token tile fills
+        self.tc_mode = 0
         self.tc_chunk = min(ctx.cfg.max_tokens, max_rows, 4096)
 
         self.stream = torch.cuda.Stream(device=dev)   # kernels, copies and collectives of a layer are ordered on it
@@ -397,7 +399,8 @@ class GpuBackend:
         rows = sum(hi - lo for lo, hi in blocks)
         tc = rows >= self.tc_rows_min and step >= 16
         if tc:
-            self.ctx.check(self.lib.finch_set_prefill_mode(self.ctx.h, self.tc_mode))
+            mode = self.tc_mode or (2 if rows * self.K >= 64 * self.ctx.cfg.n_experts else 3)
+            self.ctx.check(self.lib.finch_set_prefill_mode(self.ctx.h, mode))
             self.ctx.check(self.lib.finch_set_prefill_chunk(self.ctx.h, min(self.tc_chunk, step)))
             if skip is not None:     # one pass over all rows; the block that is left out selects nothing
                 self.rv[skip[0]:skip[0] + skip[1]].zero_()
