@@ -72,6 +72,10 @@ extern "C" int finch_ctx_create(const finch_config *cfg, finch_ctx **out) {
     if (cudaGetDeviceProperties(&prop, c.device) != cudaSuccess) return bail(FINCH_E_CUDA);
     ctx->sm_count = prop.multiProcessorCount;
     if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) return bail(FINCH_E_CUDA);
+    if (cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->ev_join, cudaEventDisableTiming) != cudaSuccess)
+        return bail(FINCH_E_CUDA);
     const size_t gw = (size_t)c.moe_inter * c.hidden * 3 / 8, gs = (size_t)c.moe_inter * (c.hidden / 64) * 2;
     const size_t dw = gw, ds = (size_t)c.hidden * (c.moe_inter / 64) * 2;
     ctx->lay.gate_w = 0;
@@ -108,6 +112,9 @@ extern "C" void finch_ctx_destroy(finch_ctx *ctx) {
     cudaFree(ctx->partial);
     cudaFree(ctx->dev_status);
     cudaFree(ctx->hp_ticket);
+    if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
+    if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
+    if (ctx->side) cudaStreamDestroy(ctx->side);
     for (auto &e : ctx->shared_cache) cudaFree(e.tiles);
     cudaFree(ctx->stage_dev);
     cudaFree(ctx->pf_ws);

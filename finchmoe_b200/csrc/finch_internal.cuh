@@ -21,6 +21,8 @@
 struct finch_ctx {
     finch_config cfg{};
     cudaStream_t stream = nullptr;  // context-owned stream (used when the caller passes NULL)
+    cudaStream_t side = nullptr;    // second stream: the shared expert of a prefill chunk runs beside the routed experts
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     int sm_count = 0;
     // scratch shared by every call on this context (calls that overlap on the GPU race)
     float *act = nullptr;           // [max_pairs][moe_inter]   routed SwiGLU activations

@@ -281,15 +281,23 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
             x_lo = xl;
             ctx->launches++;
         }
-        if ((rc = finch_group3_prefill(ctx, st, pool, layer, h_post, ids, valid, T, ws + o_g3, down))) return rc;
+        // The shared expert (three small dense GEMMs, each bounded by the latency of its K loop) runs on a second stream
+        // beside the routed experts' passes and joins before the combine; both branches only read the inputs.
+        cudaStream_t ss = st;
         if (shared) {
-            if ((rc = dense4_gemm(ctx, st, &shared->gate, x, x_lo, sg, T))) return rc;
-            if ((rc = dense4_gemm(ctx, st, &shared->up, x, x_lo, su, T))) return rc;
-            pf_swiglu_kernel<<<148, 256, 0, st>>>(sg, su, sact, sact_lo, (size_t)T * Is);
+            ss = ctx->side;
+            FINCH_CUDA_OK(ctx, cudaEventRecord(ctx->ev_fork, st));
+            FINCH_CUDA_OK(ctx, cudaStreamWaitEvent(ss, ctx->ev_fork, 0));
+            if ((rc = dense4_gemm(ctx, ss, &shared->gate, x, x_lo, sg, T))) return rc;
+            if ((rc = dense4_gemm(ctx, ss, &shared->up, x, x_lo, su, T))) return rc;
+            pf_swiglu_kernel<<<148, 256, 0, ss>>>(sg, su, sact, sact_lo, (size_t)T * Is);
             FINCH_CUDA_OK(ctx, cudaGetLastError());
-            if ((rc = dense4_gemm(ctx, st, &shared->down, sact, sact_lo, shared_out, T))) return rc;
+            if ((rc = dense4_gemm(ctx, ss, &shared->down, sact, sact_lo, shared_out, T))) return rc;
+            FINCH_CUDA_OK(ctx, cudaEventRecord(ctx->ev_join, ss));
             ctx->launches++;
         }
+        if ((rc = finch_group3_prefill(ctx, st, pool, layer, h_post, ids, valid, T, ws + o_g3, down))) return rc;
+        if (shared) FINCH_CUDA_OK(ctx, cudaStreamWaitEvent(st, ctx->ev_join, 0));
         pf_combine_kernel<<<dim3((H + 255) / 256, T), 256, 0, st>>>(ids, valid, slot_row, c.n_experts, weights, c.top_k, down, shared ? shared_out : nullptr,
                                                                     shared ? shared->gate_score : nullptr, h_mid, hidden_out, H);
         FINCH_CUDA_OK(ctx, cudaGetLastError());
