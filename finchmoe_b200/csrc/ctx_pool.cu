@@ -72,7 +72,9 @@ extern "C" int finch_ctx_create(const finch_config *cfg, finch_ctx **out) {
     if (cudaGetDeviceProperties(&prop, c.device) != cudaSuccess) return bail(FINCH_E_CUDA);
     ctx->sm_count = prop.multiProcessorCount;
     if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) return bail(FINCH_E_CUDA);
-    if (cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking) != cudaSuccess ||
+    if (cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking) != cudaSuccess || cudaStreamCreateWithFlags(&ctx->side2, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->ev_fork2, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->ev_join2, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&ctx->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&ctx->ev_join, cudaEventDisableTiming) != cudaSuccess)
         return bail(FINCH_E_CUDA);
@@ -115,6 +117,9 @@ extern "C" void finch_ctx_destroy(finch_ctx *ctx) {
     if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
     if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
     if (ctx->side) cudaStreamDestroy(ctx->side);
+    if (ctx->ev_fork2) cudaEventDestroy(ctx->ev_fork2);
+    if (ctx->ev_join2) cudaEventDestroy(ctx->ev_join2);
+    if (ctx->side2) cudaStreamDestroy(ctx->side2);
     for (auto &e : ctx->shared_cache) cudaFree(e.tiles);
     cudaFree(ctx->stage_dev);
     cudaFree(ctx->pf_ws);

@@ -23,6 +23,8 @@ struct finch_ctx {
     cudaStream_t stream = nullptr;  // context-owned stream (used when the caller passes NULL)
     cudaStream_t side = nullptr;    // second stream: the shared expert of a prefill chunk runs beside the routed experts
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    cudaStream_t side2 = nullptr;   // third stream: the small item classes of the grouped prefill passes beside the large one
+    cudaEvent_t ev_fork2 = nullptr, ev_join2 = nullptr;
     int sm_count = 0;
     // scratch shared by every call on this context (calls that overlap on the GPU race)
     float *act = nullptr;           // [max_pairs][moe_inter]   routed SwiGLU activations

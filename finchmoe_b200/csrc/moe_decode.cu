@@ -1413,7 +1413,8 @@ struct G3Args {
     size_t slot_bytes;
     const int32_t *slot_row;   // the layer's slot table [n_experts]
     int hidden, inter;
-    const uint8_t *recs;       // operand records by position (global memory)
+    const uint8_t *recs;       // operand records (global memory): record rec_of[position], or record `position` when rec_of is NULL
+    const int *rec_of;
     int rstride;
     const int4 *items;         // (expert, first position, tokens, -)
     const int *n_items;
@@ -1527,7 +1528,7 @@ __global__ void __launch_bounds__(128) g3_records_kernel(const void *x, const in
     extern __shared__ __align__(16) uint8_t g3row[];
     __shared__ float wmax[4];
     const int pos = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (pos >= *total) return;
+    if (total && pos >= *total) return;      // total == NULL: every CTA of the grid has a row
     const size_t row = identity ? (size_t)pos : (size_t)src[pos];
     const int rowb = K * (SRC_BF16 ? 2 : 4);
     const uint4 *g = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(x) + row * rowb);
@@ -1582,10 +1583,17 @@ __global__ void __launch_bounds__(256, 2) moe_group3_kernel(const G3Args a) {
     const int sec = sec3_bytes(K), hdr_off = sec * (HILO ? 2 : 1);
     // records of the item's tokens
     {
-        const uint4 *src = reinterpret_cast<const uint4 *>(a.recs + (size_t)item.y * a.rstride);
+        const int per = a.rstride / 16;
         uint4 *dst = reinterpret_cast<uint4 *>(smem);
-        const int n16 = count * a.rstride / 16;
-        for (int i = tid; i < n16; i += 256) dst[i] = __ldg(src + i);
+        if (a.rec_of) {     // the tokens' records: one per token, shared by all the token's pairs
+            for (int q = 0; q < count; q++) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(a.recs + (size_t)a.rec_of[item.y + q] * a.rstride);
+                for (int i = tid; i < per; i += 256) dst[q * per + i] = __ldg(src + i);
+            }
+        } else {
+            const uint4 *src = reinterpret_cast<const uint4 *>(a.recs + (size_t)item.y * a.rstride);
+            for (int i = tid; i < count * per; i += 256) dst[i] = __ldg(src + i);
+        }
     }
     __syncthreads();
     const uint32_t rec32 = finch_smem_u32(smem);
@@ -1712,25 +1720,32 @@ __global__ void __launch_bounds__(256, 2) moe_group3_kernel(const G3Args a) {
     }
 }
 
+// The three item classes are independent: the two small ones (few tokens per item: little work per unit, bound by
+// load latency) run on a second stream beside the large one and join before whatever reads their output.
 template <bool HILO, bool FP16S, bool DOWN>
-static cudaError_t g3_launch_lists(cudaStream_t st, G3Args a, int4 *const lists[3], const int *counts, const int bounds[3], int split, int rstride,
-                                   int K) {
+static cudaError_t g3_launch_lists(finch_ctx *ctx, cudaStream_t st, G3Args a, int4 *const lists[3], const int *counts, const int bounds[3], int split,
+                                   int rstride, int K) {
     // split: CTAs per item of the largest class; items with fewer tokens do less per tile and get more CTAs each
     constexpr int PP = HILO ? 2 : 4;
     const int sec = sec3_bytes(K);
     cudaError_t e;
+    cudaStream_t s2 = ctx->side2;
+    if ((e = cudaEventRecord(ctx->ev_fork2, st)) != cudaSuccess) return e;
+    if ((e = cudaStreamWaitEvent(s2, ctx->ev_fork2, 0)) != cudaSuccess) return e;
     a.items = lists[0];
     a.n_items = counts;
-    moe_group3_kernel<HILO, FP16S, 1, DOWN><<<dim3(4 * split, bounds[0]), 256, PP * 1 * rstride + sec, st>>>(a);
+    moe_group3_kernel<HILO, FP16S, 1, DOWN><<<dim3(4 * split, bounds[0]), 256, PP * 1 * rstride + sec, s2>>>(a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     a.items = lists[1];
     a.n_items = counts + 1;
-    moe_group3_kernel<HILO, FP16S, 2, DOWN><<<dim3(2 * split, bounds[1]), 256, PP * 2 * rstride + sec, st>>>(a);
+    moe_group3_kernel<HILO, FP16S, 2, DOWN><<<dim3(2 * split, bounds[1]), 256, PP * 2 * rstride + sec, s2>>>(a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if ((e = cudaEventRecord(ctx->ev_join2, s2)) != cudaSuccess) return e;
     a.items = lists[2];
     a.n_items = counts + 2;
     moe_group3_kernel<HILO, FP16S, 4, DOWN><<<dim3(split, bounds[2]), 256, PP * 4 * rstride + sec, st>>>(a);
-    return cudaGetLastError();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    return cudaStreamWaitEvent(st, ctx->ev_join2, 0);
 }
 
 template <bool HILO, bool FP16S, bool DOWN>
@@ -1810,6 +1825,7 @@ int finch_group3_prefill(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int 
     g3_sort_kernel<<<1, 1024, 2 * c.n_experts * sizeof(int), st>>>(ids, valid, slot_row, c.n_experts, p.P, c.top_k, p.ppa, 2, order, src_tok, la[0], la[1], la[2],
                                                                     lb[0], lb[1], lb[2], counts);
     FINCH_CUDA_OK(ctx, cudaGetLastError());
+    // one operand record per position (a token's pairs each get a copy: the item kernels then read their records as one run)
     if (hilo_a) g3_records_kernel<true, false><<<p.P, 128, c.hidden * 4, st>>>(x, src_tok, 0, counts + 6, c.hidden, recs_a, p.rs_a);
     else g3_records_kernel<false, true><<<p.P, 128, c.hidden * 2, st>>>(x, src_tok, 0, counts + 6, c.hidden, recs_a, p.rs_a);
     FINCH_CUDA_OK(ctx, cudaGetLastError());
@@ -1822,22 +1838,24 @@ int finch_group3_prefill(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int 
     a.order = order;
     a.status = ctx->dev_status;
     a.recs = recs_a;
+    a.rec_of = nullptr;
     a.rstride = p.rs_a;
     a.out = act;
     const int bounds_a[3] = {p.bound01, p.bound01, p.bound2a}, bounds_b[3] = {p.bound01, p.bound01, p.bound2b};
     cudaError_t e;
-    if (hilo_a) e = fp16s ? g3_launch_lists<true, true, false>(st, a, la, counts, bounds_a, 2, p.rs_a, c.hidden)
-                          : g3_launch_lists<true, false, false>(st, a, la, counts, bounds_a, 2, p.rs_a, c.hidden);
-    else e = fp16s ? g3_launch_lists<false, true, false>(st, a, la, counts, bounds_a, 2, p.rs_a, c.hidden)
-                   : g3_launch_lists<false, false, false>(st, a, la, counts, bounds_a, 2, p.rs_a, c.hidden);
+    if (hilo_a) e = fp16s ? g3_launch_lists<true, true, false>(ctx, st, a, la, counts, bounds_a, 2, p.rs_a, c.hidden)
+                          : g3_launch_lists<true, false, false>(ctx, st, a, la, counts, bounds_a, 2, p.rs_a, c.hidden);
+    else e = fp16s ? g3_launch_lists<false, true, false>(ctx, st, a, la, counts, bounds_a, 2, p.rs_a, c.hidden)
+                   : g3_launch_lists<false, false, false>(ctx, st, a, la, counts, bounds_a, 2, p.rs_a, c.hidden);
     FINCH_CUDA_OK(ctx, e);
     g3_records_kernel<true, false><<<p.P, 128, c.moe_inter * 4, st>>>(act, src_tok, 1, counts + 6, c.moe_inter, recs_b, p.rs_b);
     FINCH_CUDA_OK(ctx, cudaGetLastError());
     a.recs = recs_b;
+    a.rec_of = nullptr;
     a.rstride = p.rs_b;
     a.out = down_out;
-    e = fp16s ? g3_launch_lists<true, true, true>(st, a, lb, counts + 3, bounds_b, 4, p.rs_b, c.moe_inter)
-              : g3_launch_lists<true, false, true>(st, a, lb, counts + 3, bounds_b, 4, p.rs_b, c.moe_inter);
+    e = fp16s ? g3_launch_lists<true, true, true>(ctx, st, a, lb, counts + 3, bounds_b, 4, p.rs_b, c.moe_inter)
+              : g3_launch_lists<true, false, true>(ctx, st, a, lb, counts + 3, bounds_b, 4, p.rs_b, c.moe_inter);
     FINCH_CUDA_OK(ctx, e);
     ctx->launches += 9;
     return FINCH_OK;
