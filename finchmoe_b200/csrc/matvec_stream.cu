@@ -258,12 +258,13 @@ int launch_stream(finch_ctx *ctx, cudaStream_t st, const StreamArgs &a, int smem
 }  // namespace
 
 // Returns FINCH_OK after launching, or -1 when the call is not one this kernel takes (the caller then tries the
-// other matvec kernels): one affine 4- or 8-bit g64 tensor of at least 4096 rows, K a multiple of 512 up to 8192,
+// other matvec kernels): one affine 4- or 8-bit g64 tensor of at least 32,768 rows (a CTA takes 128 rows: fewer rows
+// leave SMs without work, and the row-pair kernel of matvec_fast.cu is faster there), K a multiple of 512 up to 8192,
 // 16-byte aligned rows, up to four fp32 or eight bf16 positions per pass (more run as further passes).
 int finch_try_stream_matvec(finch_ctx *ctx, cudaStream_t st, const void *x, int x_dtype, const finch_wdesc *specs, float *const *outs, int n, int M) {
     if (n != 1) return -1;
     const finch_wdesc &w = specs[0];
-    if ((w.bits != 4 && w.bits != 8) || w.group_size != 64 || w.out_dim < 4096 || w.in_dim % 512 || w.in_dim > SMAXK) return -1;
+    if ((w.bits != 4 && w.bits != 8) || w.group_size != 64 || w.out_dim < 32768 || w.in_dim % 512 || w.in_dim > SMAXK) return -1;
     if (((uintptr_t)w.scales & 15) || ((uintptr_t)w.biases & 15)) return -1;
     if (((uintptr_t)w.W & 15) || ((size_t)w.in_dim * w.bits / 8) % 16) return -1;
     const bool hilo = x_dtype != FINCH_BF16;

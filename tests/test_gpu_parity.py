@@ -109,12 +109,13 @@ def test_gguf_matvec_benchmark_shapes_vs_oracle(ctx_small, ty, bits, o, i, T):
     assert_close(y[rows], want, f"GGUF type {ty} [{o} x {i}] T={T}")
 
 
-@pytest.mark.parametrize("bits,o,i", [(8, 4100, 2048), (4, 8192, 2048), (4, 4099, 4096), (8, 5000, 512)])
+@pytest.mark.parametrize("bits,o,i", [(8, 4100, 2048), (4, 8192, 2048), (4, 4099, 4096), (8, 5000, 512), (4, 33001, 512), (8, 32800, 1024)])
 @pytest.mark.parametrize("M", [1, 3, 9])
 @pytest.mark.parametrize("xdt", [L.F32, L.BF16])
 def test_large_affine_matvec_streaming_kernel_vs_oracle(ctx_small, bits, o, i, M, xdt):
-    """Large row-major 4- / 8-bit tensors (4096 rows and more) take the tensor-core streaming kernel, straight from
-    the reference tensor layout; row counts that are not multiples of 16, fp32 and bf16 activations, several passes."""
+    """Large row-major 4- / 8-bit tensors: from 32,768 rows the tensor-core streaming kernel, below that the row-pair
+    kernel, both straight from the reference tensor layout; row counts that are not multiples of 16, fp32 and bf16
+    activations, several passes."""
     import torch
     rng = synth.rng_for(4, bits, o + M)
     t = synth.affine_tensor(rng, o, i, bits, L.FP16 if (o + M) % 2 else L.BF16)
