@@ -1134,7 +1134,8 @@ __global__ void __launch_bounds__(NW_MAX * 32, 1) moe_down_kernel(const MoeArgs 
     // The routing is an input of the whole call, final since the gate/up kernel passed its own wait (this grid
     // is scheduled only after that): groups, ranges and the first weight pieces do not wait for the gate/up
     // kernel to finish.  Only the activations (its output) do.
-    if (routed && warp < 2) build_groups(a, tab, sm_ids, sm_rank, 2, nullptr, 0u, 0);
+    // (the two ends of this CTA's job range are worked out by two threads side by side, into sm_ids[0..1])
+    if (routed && warp < 2) build_groups(a, tab, sm_ids, sm_rank, 2, nullptr, 0u, 0, sm_ids, 1, vb, Gr, T.nTB);
     __syncthreads();
     STAMPB(1);
     const uint32_t st32 = finch_smem_u32(smem + L.stage + warp * L.stg), stdelta = (uint32_t)(nwarps * L.stg);
@@ -1144,9 +1145,7 @@ __global__ void __launch_bounds__(NW_MAX * 32, 1) moe_down_kernel(const MoeArgs 
 
     if (routed) {
         const int ng = tab->ng;
-        const int total = tab->pre[ng] * T.nTB;
-        const int job0 = job_at(tab->pre, ng, T.nTB, (int)((unsigned)total * vb / (unsigned)Gr));
-        const int job1 = job_at(tab->pre, ng, T.nTB, (int)((unsigned)total * (vb + 1) / (unsigned)Gr));
+        const int job0 = sm_ids[0], job1 = sm_ids[1];
         auto fetch = [&](int gi, int tb, uint32_t dst, uint64_t *bar) {   // lane 0
             finch_mbar_expect_tx(bar, (unsigned)T.tileB);
             finch_bulk_g2s_a(dst, a.pool_base + (size_t)tab->slot[gi] * a.slot_bytes + T.b_base + (size_t)tb * T.tileB, (unsigned)T.tileB, bar);
