@@ -1118,12 +1118,15 @@ def main():
                     help="N > 1, prefill: the received rows through the tcgen05 grouped GEMMs (2), the grouped mma.sync passes (3), or by tokens per expert (0)")
     ap.add_argument("--ep-prefill-exchange", default="fixed", choices=["fixed", "planned"],
                     help="N > 1, prefill: every token to every rank with equal splits and no host step, or the planned exchange")
+    ap.add_argument("--prefill-mode", type=int, default=0, choices=[0, 1, 2, 3, 4],
+                    help="with --only prefill: which kernels take the routed experts of a chunk (0: the library's choice)")
     ap.add_argument("--only", default="", choices=["", "prefill", "decode", "lmhead"],
                     help="just the 512-token chunk, just the batch-8 decode steps (both on --layers layers), or just the output-projection matvecs (profiler captures)")
     args = ap.parse_args()
     LAYERS = args.layers
     if args.only == "prefill":
         stack = Stack(0, max_tokens=PREFILL_CHUNK, layers=LAYERS)
+        stack.ctx.set_prefill_mode(args.prefill_mode)
         ps, uniq = stack.time_prefill(PREFILL_CHUNK, max(1, args.steps), max(1, args.warmup))
         print(json.dumps({"only": "prefill", "chunk": PREFILL_CHUNK, "layers": LAYERS, "ms_per_chunk": ps * 1e3, "tokens_per_s": PREFILL_CHUNK / ps,
                           "distinct_experts": uniq, "status": stack.ctx.device_status()}))

@@ -196,7 +196,8 @@ class Context:
     # -- MoE layer
     def set_prefill_mode(self, mode: int):
         """0: by chunk length, 1: sub-batches through the decode kernels, 2: grouped dequant-GEMMs on tcgen05,
-        3: grouped mma.sync passes (one unpack per unit for up to 16 tokens of an expert)."""
+        3: grouped mma.sync passes (one unpack per unit for up to 16 tokens of an expert),
+        4: grouped tcgen05 GEMMs whose A operand is the packed codes themselves (no dequantisation)."""
         self.check(self.lib.finch_set_prefill_mode(self.h, mode))
         self.prefill_mode = mode
 

@@ -55,7 +55,7 @@ struct finch_ctx {
     void *gq_ws = nullptr;          // activation planes of the GGUF many-position matvec (matvec_gguf_mma.cu)
     size_t gq_ws_bytes = 0;
     int prefill_chunk = 0;          // finch_set_prefill_chunk: tokens per tensor-core pass, 0 = 512
-    int prefill_mode = 0;           // finch_set_prefill_mode: 0 by chunk length, 1 sub-batches through decode, 2 tensor cores
+    int prefill_mode = 0;           // finch_set_prefill_mode: 0 by chunk length, 1 sub-batches through decode, 2 / 3 / 4 the tensor-core paths
     uint64_t launches = 0;
     // optional per-kernel timing of the MoE decode call (finch_profile_enable)
     bool profile = false;

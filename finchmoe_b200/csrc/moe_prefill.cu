@@ -20,6 +20,7 @@
 // accumulates in fp32, so it agrees with the reference's arithmetic (exact fp32 weights and activations)
 // to about 1e-5 of an output's scale; the parity tests hold it to the same bar as the decode path.
 #include "dqgemm_tc.cuh"
+#include "umma3.cuh"
 
 // the grouped 3-bit passes on mma.sync (moe_decode.cu)
 size_t finch_group3_ws_bytes(finch_ctx *ctx, int T);
@@ -242,9 +243,26 @@ int ensure_ws(finch_ctx *ctx, size_t bytes, cudaStream_t st) {
     return FINCH_OK;
 }
 
-// grouped: the routed experts go through the grouped mma.sync passes instead of the two tcgen05 GEMMs
+int umma_attr_once(finch_ctx *ctx) {
+    static std::mutex mu;
+    static std::vector<int> done;
+    std::lock_guard<std::mutex> lk(mu);
+    for (int d : done)
+        if (d == ctx->cfg.device) return FINCH_OK;
+    FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(umma3::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(umma3::gemm_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    done.push_back(ctx->cfg.device);
+    return FINCH_OK;
+}
+
+// Which kernels take the routed experts of a chunk.
+enum RoutedKind { ROUTED_DEQUANT = 0,   // two tcgen05 GEMMs over weights dequantised to bf16 planes (dqgemm_tc.cuh)
+                  ROUTED_GROUPED = 1,   // grouped mma.sync passes (moe_decode.cu)
+                  ROUTED_CODES = 2 };   // two tcgen05 GEMMs over the packed codes themselves (umma3.cuh)
+
 int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int layer, const void *h_post, const int32_t *ids,
-                     const float *weights, const uint8_t *valid, const finch_shared *shared, const float *h_mid, float *hidden_out, int T, bool grouped) {
+                     const float *weights, const uint8_t *valid, const finch_shared *shared, const float *h_mid, float *hidden_out, int T, int kind) {
+    const bool grouped = kind == ROUTED_GROUPED;
     const finch_config &c = ctx->cfg;
     const int P = T * c.top_k, H = c.hidden, I = c.moe_inter, Is = shared ? shared->gate.out_dim : 0;
     const int32_t *slot_row = pool->slot_table_dev + (size_t)layer * pool->n_experts;
@@ -260,6 +278,11 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
     const size_t o_ia = take((size_t)max_items * sizeof(int2)), o_ib = take((size_t)max_items * sizeof(int2)), o_ni = take(2 * sizeof(int));
     const size_t o_xb = take((size_t)T * H * 2), o_xl = take((size_t)T * H * 2), o_sg = take((size_t)T * Is * 4), o_su = take((size_t)T * Is * 4), o_sact = take((size_t)T * Is * 4);
     const size_t o_g3 = grouped ? take(finch_group3_ws_bytes(ctx, T)) : 0;
+    const bool codes = kind == ROUTED_CODES;
+    const int pl_a = c.act_dtype == FINCH_BF16 ? 1 : 2;   // activation columns per token of the gate/up GEMM (the down GEMM's fp32 input: 2)
+    const size_t o_ra = codes ? take((size_t)T * (H / 64) * pl_a * umma3::REC) : 0, o_xa = codes ? take((size_t)T * (H / 64) * 4) : 0,
+                 o_fa = codes ? take((size_t)T * 4) : 0, o_rb = codes ? take((size_t)P * (I / 64) * 2 * umma3::REC) : 0,
+                 o_xsb = codes ? take((size_t)P * (I / 64) * 4) : 0, o_fb = codes ? take((size_t)P * 4) : 0;
     int rc = ensure_ws(ctx, off, st);
     if (rc) return rc;
     char *ws = (char *)ctx->pf_ws;
@@ -297,6 +320,83 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
             ctx->launches++;
         }
         if ((rc = finch_group3_prefill(ctx, st, pool, layer, h_post, ids, valid, T, ws + o_g3, down))) return rc;
+        if (shared) FINCH_CUDA_OK(ctx, cudaStreamWaitEvent(st, ctx->ev_join, 0));
+        pf_combine_kernel<<<dim3((H + 255) / 256, T), 256, 0, st>>>(ids, valid, slot_row, c.n_experts, weights, c.top_k, down, shared ? shared_out : nullptr,
+                                                                    shared ? shared->gate_score : nullptr, h_mid, hidden_out, H);
+        FINCH_CUDA_OK(ctx, cudaGetLastError());
+        ctx->launches++;
+        return FINCH_OK;
+    }
+    if (codes) {
+        if ((rc = umma_attr_once(ctx))) return rc;
+        int resident = 0;
+        for (int e = 0; e < pool->n_experts; e++) resident += pool->slot_of[(size_t)layer * pool->n_experts + e] >= 0;
+        const int tn_ga = umma3::tokens_per_cta(pl_a), tn_dn = umma3::tokens_per_cta(2);
+        const int cap = P / tn_dn + resident + 1;
+        pf_sort_kernel<<<1, 1024, 4 * c.n_experts * sizeof(int), st>>>(ids, valid, slot_row, c.n_experts, P, seg, order, tn_ga, tn_dn, items_a, items_b,
+                                                                       n_items, cap, cap, ctx->dev_status);
+        FINCH_CUDA_OK(ctx, cudaGetLastError());
+        const uint16_t *x = (const uint16_t *)h_post, *x_lo = nullptr;
+        if (x_lo_needed && shared) {
+            pf_to_bf16_kernel<<<148, 256, 0, st>>>((const float *)h_post, xb, xl, (size_t)T * H);
+            FINCH_CUDA_OK(ctx, cudaGetLastError());
+            x = xb;
+            x_lo = xl;
+            ctx->launches++;
+        }
+        cudaStream_t ss = st;
+        if (shared) {   // the shared expert's dense GEMMs beside the routed experts, as in the grouped branch
+            ss = ctx->side;
+            FINCH_CUDA_OK(ctx, cudaEventRecord(ctx->ev_fork, st));
+            FINCH_CUDA_OK(ctx, cudaStreamWaitEvent(ss, ctx->ev_fork, 0));
+            if ((rc = dense4_gemm(ctx, ss, &shared->gate, x, x_lo, sg, T))) return rc;
+            if ((rc = dense4_gemm(ctx, ss, &shared->up, x, x_lo, su, T))) return rc;
+            pf_swiglu_kernel<<<148, 256, 0, ss>>>(sg, su, sact, sact_lo, (size_t)T * Is);
+            FINCH_CUDA_OK(ctx, cudaGetLastError());
+            if ((rc = dense4_gemm(ctx, ss, &shared->down, sact, sact_lo, shared_out, T))) return rc;
+            FINCH_CUDA_OK(ctx, cudaEventRecord(ctx->ev_join, ss));
+            ctx->launches++;
+        }
+        uint8_t *ra = (uint8_t *)(ws + o_ra), *rb = (uint8_t *)(ws + o_rb);
+        float *xa = (float *)(ws + o_xa), *fa = (float *)(ws + o_fa), *xsb = (float *)(ws + o_xsb), *fb = (float *)(ws + o_fb);
+        if (pl_a == 1) umma3::records_kernel<true, false><<<(T + 7) / 8, 256, 0, st>>>(h_post, T, H, ra, xa, fa);
+        else umma3::records_kernel<false, true><<<(T + 7) / 8, 256, 0, st>>>(h_post, T, H, ra, xa, fa);
+        FINCH_CUDA_OK(ctx, cudaGetLastError());
+        umma3::Args u{};
+        u.K = H;
+        u.planes = pl_a;
+        u.scale_dtype = c.scale_dtype;
+        u.pool_base = (const uint8_t *)pool->base;
+        u.slot_bytes = pool->slot_bytes;
+        u.slot_row = slot_row;
+        u.hidden = H;
+        u.inter = I;
+        u.seg = seg;
+        u.order = order;
+        u.items = items_a;
+        u.n_items = n_items;
+        u.top_k = c.top_k;
+        u.recs = ra;
+        u.xsum = xa;
+        u.fac = fa;
+        u.act_out = ctx->act;
+        u.status = ctx->dev_status;
+        umma3::gemm_kernel<<<dim3(I / 64, cap), dqgemm::NTB, umma3::smem_bytes(H, pl_a), st>>>(u);
+        FINCH_CUDA_OK(ctx, cudaGetLastError());
+        umma3::records_kernel<false, true><<<(P + 7) / 8, 256, 0, st>>>(ctx->act, P, I, rb, xsb, fb);
+        FINCH_CUDA_OK(ctx, cudaGetLastError());
+        u.down = 1;
+        u.K = I;
+        u.planes = 2;
+        u.items = items_b;
+        u.n_items = n_items + 1;
+        u.recs = rb;
+        u.xsum = xsb;
+        u.fac = fb;
+        u.out = down;
+        umma3::gemm_kernel<<<dim3(H / dqgemm::GM, cap), dqgemm::NTB, umma3::smem_bytes(I, 2), st>>>(u);
+        FINCH_CUDA_OK(ctx, cudaGetLastError());
+        ctx->launches += 5;
         if (shared) FINCH_CUDA_OK(ctx, cudaStreamWaitEvent(st, ctx->ev_join, 0));
         pf_combine_kernel<<<dim3((H + 255) / 256, T), 256, 0, st>>>(ids, valid, slot_row, c.n_experts, weights, c.top_k, down, shared ? shared_out : nullptr,
                                                                     shared ? shared->gate_score : nullptr, h_mid, hidden_out, H);
@@ -374,7 +474,7 @@ int prefill_tc_chunk(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int laye
 }  // namespace
 
 extern "C" int finch_set_prefill_mode(finch_ctx *ctx, int mode) {
-    if (!ctx || mode < 0 || mode > 3) return FINCH_E_ARG;
+    if (!ctx || mode < 0 || mode > 4) return FINCH_E_ARG;
     ctx->prefill_mode = mode;
     return FINCH_OK;
 }
@@ -396,7 +496,7 @@ extern "C" int finch_encode_moe_prefill(finch_ctx *ctx, finch_stream stream, fin
     // which kernels serve the routed experts of a tensor-core chunk: the grouped mma.sync passes (mode 3) unpack a
     // unit once for up to 16 tokens and win while experts see few tokens; the tcgen05 GEMMs (mode 2) win when a tile
     // of 64 tokens fills (the rows an expert-parallel rank receives).  By chunk length: the former.
-    const bool grouped = ctx->prefill_mode == 3 || ctx->prefill_mode == 0;
+    const int kind = ctx->prefill_mode == 4 ? ROUTED_CODES : (ctx->prefill_mode == 3 || ctx->prefill_mode == 0) ? ROUTED_GROUPED : ROUTED_DEQUANT;
     // shapes the tensor-core kernels take: whole 128-row tiles, 128-value K blocks, a 3-bit pool
     if (c.expert_bits != 3 || c.hidden % 128 || c.moe_inter % 128 || c.top_k > 8 || c.n_experts > 1024) tc = false;
     if (tc && shared) {
@@ -425,7 +525,7 @@ extern "C" int finch_encode_moe_prefill(finch_ctx *ctx, finch_stream stream, fin
             const int rc = prefill_tc_chunk(ctx, st, pool, layer, (const char *)h_post + (size_t)t0 * c.hidden * elt,
                                             expert_ids + (size_t)t0 * c.top_k, weights + (size_t)t0 * c.top_k,
                                             valid ? valid + (size_t)t0 * c.top_k : nullptr, shared ? &sh : nullptr,
-                                            h_mid ? h_mid + (size_t)t0 * c.hidden : nullptr, hidden_out + (size_t)t0 * c.hidden, n, grouped);
+                                            h_mid ? h_mid + (size_t)t0 * c.hidden : nullptr, hidden_out + (size_t)t0 * c.hidden, n, kind);
             if (rc) return rc;
         }
         return FINCH_OK;

@@ -272,9 +272,13 @@ FINCH_API int finch_profile_read(finch_ctx *ctx, float *ms_gateup, float *ms_dow
  * dequant-GEMMs on tcgen05 (best when experts see 64 tokens and more, e.g. the rows
  * an expert-parallel rank receives), 3 = the routed experts as grouped mma.sync
  * passes that unpack a unit of codes once for up to 16 tokens of its expert (best at
- * the few tokens per expert of an ordinary chunk).  In modes 2 and 3 the shared
- * expert runs as dense tcgen05 GEMMs.  The reference has one path only
- * (per-position CMD3). */
+ * the few tokens per expert of an ordinary chunk), 4 = the routed experts as two
+ * grouped tcgen05 GEMMs that take the packed codes themselves as the A operand (a
+ * masked code is an fp16 subnormal; nothing is dequantised, each scale group is
+ * accumulated in tensor memory and folded with its scale and bias by the warps that
+ * unpack the next one; measured level with modes 2 and 3, not chosen by mode 0).
+ * In modes 2, 3 and 4 the shared expert runs as dense tcgen05 GEMMs.  The reference
+ * has one path only (per-position CMD3). */
 FINCH_API int finch_set_prefill_mode(finch_ctx *ctx, int mode);
 
 /* Tokens per pass of the tensor-core path of finch_encode_moe_prefill (the

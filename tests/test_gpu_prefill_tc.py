@@ -51,7 +51,7 @@ def test_dense_4bit_gemm_vs_oracle(api, shape, M):
 
 
 @pytest.mark.parametrize("T,act_dtype", [(16, L.F32), (23, L.BF16), (64, L.F32), (200, L.BF16)])
-@pytest.mark.parametrize("mode", [2, 3])
+@pytest.mark.parametrize("mode", [2, 3, 4])
 def test_prefill_tensor_core_small_vs_oracle(api, T, act_dtype, mode):
     cfg = dict(hidden=256, inter=128, sd=L.BF16)
     ctx = api.Context(hidden=256, n_experts=16, top_k=8, moe_inter=128, shared_inter=128, n_layers=1,
@@ -89,7 +89,7 @@ def test_prefill_tensor_core_small_vs_oracle(api, T, act_dtype, mode):
         ctx.destroy()
 
 
-@pytest.mark.parametrize("mode", [2, 3])
+@pytest.mark.parametrize("mode", [2, 3, 4])
 def test_prefill_tensor_core_full_size_vs_oracle(api, mode):
     """Hidden 2048, inter 512, 256 experts, top-8, Zipf routing, fp16 scales, bf16 activations: a 64-token chunk."""
     T = 64
@@ -123,7 +123,7 @@ def test_prefill_tensor_core_full_size_vs_oracle(api, mode):
         ctx.destroy()
 
 
-@pytest.mark.parametrize("mode", [2, 3])
+@pytest.mark.parametrize("mode", [2, 3, 4])
 def test_prefill_512_tokens_full_size_sampled_oracle_and_exact_path(api, mode):
     """The largest chunk (512 tokens, hidden 2048, 256 experts, Zipf top-8) through the tensor-core path: every row
     finite, 24 sampled rows against the oracle's exact arithmetic, and all rows against the sub-batch path."""
