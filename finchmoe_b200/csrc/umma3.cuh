@@ -66,6 +66,27 @@ __device__ __forceinline__ uint64_t desc_plain(uint32_t addr, uint32_t lbo) {
 // fp16 x fp16 -> fp32, both operands K-major, M = 128, N = n
 __device__ __forceinline__ uint32_t idesc_f16(int n) { return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(GM >> 4) << 24); }
 
+// 16 consecutive fp32 columns of this thread's lane, without waiting for them: several loads go out before one tmem_ld_wait
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+                   "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                 : "r"(taddr)
+                 : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+// The loaded values are operands of the wait, so that nothing that uses them can be scheduled ahead of it.
+__device__ __forceinline__ void tmem_ld_wait(float (&a)[16], float (&b)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+f"(a[0]), "+f"(a[1]), "+f"(a[2]), "+f"(a[3]), "+f"(a[4]), "+f"(a[5]), "+f"(a[6]), "+f"(a[7]), "+f"(a[8]), "+f"(a[9]), "+f"(a[10]),
+                   "+f"(a[11]), "+f"(a[12]), "+f"(a[13]), "+f"(a[14]), "+f"(a[15]), "+f"(b[0]), "+f"(b[1]), "+f"(b[2]), "+f"(b[3]), "+f"(b[4]), "+f"(b[5]),
+                   "+f"(b[6]), "+f"(b[7]), "+f"(b[8]), "+f"(b[9]), "+f"(b[10]), "+f"(b[11]), "+f"(b[12]), "+f"(b[13]), "+f"(b[14]), "+f"(b[15])
+                 :
+                 : "memory");
+}
+
 __device__ __forceinline__ void cp_async4(uint32_t dst, const void *src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
 }
@@ -298,28 +319,36 @@ __global__ void __launch_bounds__(NTB, 2) gemm_kernel(const Args a) {
         bool ok = !*abort_flag && finch_mbar_wait(done + (g & 1), (g >> 1) & 1);
         if (!__all_sync(0xffffffffu, ok)) return false;
         tc_fence_after();
+        // the loads of the iteration go out together: with two columns per token the hi and the lo chunk (the thread's
+        // second chunk lies beyond 32 tokens then), with one column the thread's two chunks
+        const uint32_t tb = trow + (uint32_t)((g & 1) * TM_BUF);
+        const int c0 = ch * 16, c1 = planes == 2 ? tn + c0 : c0 + 32;
+        const bool use0 = c0 < tn, use1 = use0 && (planes == 2 || c1 < tn);
+        float v0[16], v1[16];
 #pragma unroll
-        for (int q = 0; q < 2; q++) {
-            const int c0 = (ch + 2 * q) * 16;
-            if (control || c0 >= tn) continue;
-            float v[16];
-            tmem_ld16(trow + (uint32_t)((g & 1) * TM_BUF + c0), v);
-            if (planes == 2) {
-                float v2[16];
-                tmem_ld16(trow + (uint32_t)((g & 1) * TM_BUF + tn + c0), v2);
-#pragma unroll
-                for (int j = 0; j < 16; j++) v[j] = fmaf(v2[j], 1.0f / 2048.0f, v[j]);
-            }
-            const float4 *xq = reinterpret_cast<const float4 *>(xs_p + g * TN + c0);
+        for (int j = 0; j < 16; j++) v0[j] = v1[j] = 0.f;
+        if (use0) tmem_ld16_issue(tb + (uint32_t)c0, v0);
+        if (use1) tmem_ld16_issue(tb + (uint32_t)c1, v1);
+        if (use0) tmem_ld_wait(v0, v1);
+        auto add = [&](float (&ac)[16], const float (&v)[16], int col0) {
+            const float4 *xq = reinterpret_cast<const float4 *>(xs_p + g * TN + col0);
 #pragma unroll
             for (int k = 0; k < 4; k++) {
                 const float4 x4 = xq[k];
-                acc[q][4 * k] = fmaf(b, x4.x, fmaf(s, v[4 * k], acc[q][4 * k]));
-                acc[q][4 * k + 1] = fmaf(b, x4.y, fmaf(s, v[4 * k + 1], acc[q][4 * k + 1]));
-                acc[q][4 * k + 2] = fmaf(b, x4.z, fmaf(s, v[4 * k + 2], acc[q][4 * k + 2]));
-                acc[q][4 * k + 3] = fmaf(b, x4.w, fmaf(s, v[4 * k + 3], acc[q][4 * k + 3]));
+                ac[4 * k] = fmaf(b, x4.x, fmaf(s, v[4 * k], ac[4 * k]));
+                ac[4 * k + 1] = fmaf(b, x4.y, fmaf(s, v[4 * k + 1], ac[4 * k + 1]));
+                ac[4 * k + 2] = fmaf(b, x4.z, fmaf(s, v[4 * k + 2], ac[4 * k + 2]));
+                ac[4 * k + 3] = fmaf(b, x4.w, fmaf(s, v[4 * k + 3], ac[4 * k + 3]));
             }
+        };
+        if (use0) {
+            if (planes == 2) {
+#pragma unroll
+                for (int j = 0; j < 16; j++) v0[j] = fmaf(v1[j], 1.0f / 2048.0f, v0[j]);
+            }
+            add(acc[0], v0, c0);
         }
+        if (use1 && planes == 1) add(acc[1], v1, c1);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(finch_smem_u32(tm_empty + (g & 1))) : "memory");
