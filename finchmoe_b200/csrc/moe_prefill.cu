@@ -2,23 +2,28 @@
 // finchmoe/infer.m:10704-11241) and the dense 4-bit projection GEMM
 // (gpu_encode_prefill_matvec, infer.m:3672).
 //
-// Two paths:
-//  * tensor-core path (chunks of 128 tokens and more, or on request): the (token, k) pairs are sorted by expert
-//    and two grouped dequant-GEMMs (dqgemm_tc.cuh) run on tcgen05:
-//    gate/up with SiLU(gate)*up in the epilogue (activation stored as two bf16 planes, value and
-//    remainder, about 16 bits together), then down -- both planes against the same weight tile -- into
-//    one fp32 row per pair; the shared expert is three dense 4-bit GEMMs; a last kernel applies the router weights
-//    in ascending k, the shared gate and the residual (moe_combine_residual_prefill,
+// Paths (finch_set_prefill_mode; by default chosen by chunk length):
+//  * tensor-core paths (chunks of 80 tokens and more, or on request): the (token, k) pairs are sorted by expert and
+//    the routed experts run as one of
+//      - grouped mma.sync passes (moe_decode.cu, the default): a unit of codes is unpacked once for up to 16
+//        tokens of its expert, same arithmetic as the decode kernels;
+//      - two grouped dequant-GEMMs on tcgen05 (dqgemm_tc.cuh): gate/up with SiLU(gate)*up in the epilogue
+//        (activation stored as two bf16 planes, value and remainder, about 16 bits together), then down -- both
+//        planes against the same weight tile -- into one fp32 row per pair;
+//      - two grouped tcgen05 GEMMs that take the packed codes themselves as the A operand (umma3.cuh);
+//    the shared expert is three dense 4-bit GEMMs (dqgemm_tc.cuh) on a second stream; a last kernel applies the
+//    router weights in ascending k, the shared gate and the residual (moe_combine_residual_prefill,
 //    finchmoe/shaders.metal:2764-2802).  Every selected expert is read from HBM once per chunk of 512.
 //  * sub-batch path (short chunks, or on request): groups of at most eight tokens go through the
 //    decode kernels (moe_decode.cu) -- the reference's own scheme, per-position dispatch of the decode
 //    kernels with expert de-duplication inside a group (infer.m:12424-12532).  Every output row is then
 //    bit-identical to the decode entry point's, the property the reference claims (README.md:25).
 //
-// The tensor-core path carries every operand as a bf16 value plus a bf16 remainder (16 significant bits:
+// The dequantising path carries every operand as a bf16 value plus a bf16 remainder (16 significant bits:
 // the dequantised weights, fp32 activations, SiLU(gate)*up; bf16 activations are exact as they are) and
 // accumulates in fp32, so it agrees with the reference's arithmetic (exact fp32 weights and activations)
-// to about 1e-5 of an output's scale; the parity tests hold it to the same bar as the decode path.
+// to about 1e-5 of an output's scale; the other two multiply exact operands.  The parity tests hold all of
+// them to the same bar as the decode path.
 #include "dqgemm_tc.cuh"
 #include "umma3.cuh"
 
