@@ -1,5 +1,6 @@
 // Host-pointer entry point of the MoE layer: packs the caller's CPU buffers
-// into one pinned staging block, moves it to the device in one transfer, encodes
+// into one pinned staging block, moves it to the device in one transfer (a kernel
+// that reads the block over the bus for decode-sized calls, a copy otherwise), encodes
 // the decode or prefill path (decode-sized calls write their result rows straight
 // into the pinned block; larger ones copy them back) and waits.
 #include <chrono>
@@ -9,6 +10,16 @@
 int finch_stage_reserve(finch_ctx *ctx, size_t bytes);
 
 static inline size_t up256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+// The inputs of a decode-sized call, read from the pinned block over the bus by a kernel instead of a copy
+// operation: a few tens of KB, one 16-byte word per thread.  It lets the kernels behind it start at once
+// (griddepcontrol.launch_dependents first), so the gate/up kernel's prologue runs while the words are in flight,
+// which a copy operation in the stream does not allow.
+__global__ void __launch_bounds__(256) host_stage_kernel(const uint4 *__restrict__ src, uint4 *__restrict__ dst, int n16) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n16) dst[i] = src[i];
+}
 
 extern "C" int finch_moe_forward_host(finch_ctx *ctx, finch_pool *pool, int layer, const void *h_post,
                                       const int32_t *expert_ids, const float *weights, const uint8_t *valid,
@@ -37,10 +48,12 @@ extern "C" int finch_moe_forward_host(finch_ctx *ctx, finch_pool *pool, int laye
     // The inputs cross the bus in one copy into device memory: every CTA of the gate/up kernel reads the
     // activations and the routing.  The result of a decode-sized call is a few tens of KB: the combine kernel
     // writes its rows straight into the pinned staging block, which saves the copy back and its stream
-    // dependency (it costs more than moving the bytes).  FINCH_HOST_PATH=0 forces a copy back as well.
+    // dependency (it costs more than moving the bytes), and a kernel fetches the inputs from the pinned block instead
+    // of a copy operation (measured: 61.2 against 62.7 us per layer).  FINCH_HOST_PATH=1 keeps the copy operation
+    // for the inputs, 0 forces a copy back as well.
     static const int host_path = [] {
         const char *e = getenv("FINCH_HOST_PATH");
-        return e ? atoi(e) : 1;
+        return e ? atoi(e) : 2;
     }();
     char *in = ds, *out = ds;
     if (small && host_path >= 1) {
@@ -48,7 +61,14 @@ extern "C" int finch_moe_forward_host(finch_ctx *ctx, finch_pool *pool, int laye
         if (cudaHostGetDevicePointer(&m, hs, 0) == cudaSuccess && m) out = (char *)m;
         else cudaGetLastError();
     }
-    FINCH_CUDA_OK(ctx, cudaMemcpyAsync(ds, hs, o_o, cudaMemcpyHostToDevice, ctx->stream));
+    if (out != ds && host_path >= 2) {
+        const int n16 = (int)(o_o / 16);
+        host_stage_kernel<<<(n16 + 255) / 256, 256, 0, ctx->stream>>>(reinterpret_cast<const uint4 *>(out), reinterpret_cast<uint4 *>(ds), n16);
+        FINCH_CUDA_OK(ctx, cudaGetLastError());
+        ctx->launches++;
+    } else {
+        FINCH_CUDA_OK(ctx, cudaMemcpyAsync(ds, hs, o_o, cudaMemcpyHostToDevice, ctx->stream));
+    }
     // A decode-sized call whose result lands in the pinned block also reports there: the last CTA of the combine
     // kernel writes the status word and then this call's sequence number, and the host waits on that word instead
     // of on the stream (no copy operation for the status, no driver wake-up).
