@@ -121,6 +121,8 @@ extern "C" void finch_ctx_destroy(finch_ctx *ctx) {
     if (ctx->ev_join2) cudaEventDestroy(ctx->ev_join2);
     if (ctx->side2) cudaStreamDestroy(ctx->side2);
     for (auto &e : ctx->shared_cache) cudaFree(e.tiles);
+    for (auto &g : ctx->host_graphs)
+        if (g.exec) cudaGraphExecDestroy(g.exec);
     cudaFree(ctx->stage_dev);
     cudaFree(ctx->pf_ws);
     cudaFree(ctx->gq_ws);
@@ -242,6 +244,14 @@ extern "C" void finch_pool_destroy(finch_pool *p) {
     if (!p) return;
     cudaSetDevice(p->ctx->cfg.device);
     cudaDeviceSynchronize();
+    // launch sequences captured for this pool carry its addresses
+    for (auto &g : p->ctx->host_graphs)
+        if (g.pool == p) {
+            if (g.exec) cudaGraphExecDestroy(g.exec);
+            g.exec = nullptr;
+            g.pool = nullptr;
+            g.seen = -1;
+        }
     cudaFree(p->base);
     cudaFree(p->slot_table_dev);
     delete p;

@@ -35,6 +35,22 @@ struct finch_ctx {
     unsigned *hp_done = nullptr;    // armed by finch_moe_forward_host for its next decode call: device address of the host's
     int *hp_status = nullptr;       //   completion word and status word (mapped pinned memory), and the value to write
     unsigned hp_seq = 0;
+    const unsigned *hp_seq_src = nullptr;   // device word the completion value is read from (staged with the inputs)
+    // finch_moe_forward_host: the launch sequence of a decode-sized call (input fetch, gate/up, down, combine), captured
+    // once per (pool, layer, T, which optional inputs, shared expert) and replayed with one graph launch.  All addresses
+    // in it are the staging blocks'; stage_gen changes when those are reallocated.
+    struct HostGraph {
+        finch_pool *pool;
+        int layer, T;
+        bool valid, h_mid, has_shared;
+        int fault;                  // finch_debug_fault is part of the kernels' parameters
+        finch_shared shared;
+        unsigned stage_gen;
+        int seen;                   // calls so far; the second one is captured; < 0: capture failed, stay with plain launches
+        cudaGraphExec_t exec;
+    };
+    std::vector<HostGraph> host_graphs;
+    unsigned stage_gen = 0;
     int fault = 0;                  // finch_debug_fault: failure injected into the next decode calls
     bool no_pdl = false;            // FINCH_NO_PDL=1 in the environment: plain stream-ordered launches
     struct SharedPrepared {

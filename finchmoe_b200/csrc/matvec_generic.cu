@@ -304,6 +304,7 @@ int ensure_stage(finch_ctx *ctx, size_t bytes) {
     if (ctx->stage_host) cudaFreeHost(ctx->stage_host);
     ctx->stage_dev = ctx->stage_host = nullptr;
     ctx->stage_bytes = 0;
+    ctx->stage_gen++;   // launch sequences captured on the old blocks are stale
     const size_t want = (bytes + (1u << 20) - 1) & ~(size_t)((1u << 20) - 1);
     if (cudaMalloc(&ctx->stage_dev, want) != cudaSuccess || cudaMallocHost(&ctx->stage_host, want) != cudaSuccess) {
         cudaGetLastError();

@@ -103,10 +103,11 @@ struct MoeArgs {
     int cta0[MAX_CALLS + 1];
     float *rows_out;
     // host-pointer path: when host_done is set, the last CTA of the combine kernel copies the status word to
-    // host_status and then writes done_seq to host_done (both mapped pinned memory): the host waits on that word
+    // host_status and then writes the word at done_seq_src (device memory, staged with the call's inputs, so that the
+    // launch sequence can be replayed from a graph) to host_done (both mapped pinned memory): the host waits on that word
     unsigned *done_ticket, *host_done;
     int *host_status;
-    unsigned done_seq;
+    const unsigned *done_seq_src;
 };
 
 // The view of batch c of a multi-batch launch: pointers moved to its rows, the shared expert and the residual
@@ -1320,7 +1321,7 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const MoeArgs a0) {
             *a0.done_ticket = 0u;
             *a0.host_status = *reinterpret_cast<volatile int *>(a0.status);
             __threadfence_system();
-            *reinterpret_cast<volatile unsigned *>(a0.host_done) = a0.done_seq;
+            *reinterpret_cast<volatile unsigned *>(a0.host_done) = *reinterpret_cast<const volatile unsigned *>(a0.done_seq_src);
         }
     }
 }
@@ -1916,7 +1917,7 @@ static int encode_decode_calls(finch_ctx *ctx, finch_stream stream, finch_pool *
         a.done_ticket = ctx->hp_ticket;
         a.host_done = ctx->hp_done;
         a.host_status = ctx->hp_status;
-        a.done_seq = ctx->hp_seq;
+        a.done_seq_src = ctx->hp_seq_src;
     }
     ctx->hp_done = nullptr;
     if ((uintptr_t)h_post & 15) return finch_fail(ctx, FINCH_E_ARG, "h_post must be 16-byte aligned");
