@@ -642,6 +642,7 @@ __device__ int job_at(const int *pre, int ng, int per_group, int target) {
 // sm_ids: MAXP + 2 ints, sm_rank: MAXP bytes of scratch.
 // bound (optional, nbound + 1 ints): boundaries of nbound cost-balanced contiguous ranges of the group-major tile list
 // (per_group tiles per group) for the teams first_team .. first_team + nbound - 1 of n_teams.
+template <bool ONE = false>   // ONE: the call has a single token (compiled into kernels of their own, the others carry none of it)
 __device__ void build_groups(const MoeArgs &a, GroupTab *T, int *sm_ids, unsigned char *sm_rank, int per_pass, uint32_t *col, uint32_t rec32,
                              int rstride, int *bound = nullptr, int nbound = 0, int first_team = 0, int n_teams = 1, int per_group = 1) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -654,6 +655,36 @@ __device__ void build_groups(const MoeArgs &a, GroupTab *T, int *sm_ids, unsigne
             slot = a.slot_row[e];
             if (slot >= 0) id = e;
         }
+    }
+    if (ONE) {
+        // One token: every usable pair is its own group (a token's experts are distinct; should two coincide, the expert
+        // is simply read twice).  No matching across the two warps, one barrier.
+        if (col)
+            for (int i = tid; i < MAXP * MAXM; i += 64) col[i] = 0u;
+        const unsigned fb1 = __ballot_sync(0xffffffffu, id >= 0);   // P <= 8: all pairs sit in warp 0
+        const int ng1 = __popc(fb1);
+        if (warp == 0) {
+            if (id >= 0) {
+                const int gi = __popc(fb1 & ((1u << lane) - 1u));
+                T->pairs[gi][0] = (unsigned char)tid;
+                T->m[gi] = 1;
+                T->slot[gi] = slot;
+            }
+            T->pre[lane] = lane < ng1 ? lane : ng1;      // one pass per group
+            T->pre[lane + 32] = ng1;
+            if (lane == 0) {
+                T->ng = ng1;
+                T->pre[64] = ng1;
+            }
+        }
+        named_sync(BAR_GROUPS, 64);
+        if (col && warp == 0 && id >= 0) col[__popc(fb1 & ((1u << lane) - 1u)) * MAXM] = rec32;   // after the zeroing above
+        if (bound && tid <= nbound) {
+            const int ng = T->ng;
+            const unsigned total = (unsigned)(T->pre[ng] * per_group);
+            bound[tid] = job_at(T->pre, ng, per_group, (int)(total * (unsigned)(first_team + tid) / (unsigned)n_teams));
+        }
+        return;
     }
     sm_ids[tid] = id;
     if (col)
@@ -810,7 +841,7 @@ __device__ __forceinline__ WarpJobA warp_job_a(bool routed, int units, int n_til
 }
 
 // grid: one CTA per SM (persistent); block: nteam teams of TEAM warps.
-template <bool HILO, bool FP16S>
+template <bool HILO, bool FP16S, bool ONE = false>
 __global__ void __launch_bounds__(NW_MAX * 32, 1) moe_gateup_kernel(const MoeArgs a0) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
@@ -888,7 +919,7 @@ __global__ void __launch_bounds__(NW_MAX * 32, 1) moe_gateup_kernel(const MoeArg
     auto row_ptr = [&](int b) { return (const void *)((const uint8_t *)a.h_post + (size_t)b * rowb); };
     const bool one_round = a.B <= xs_rows;   // else: the records are built round by round before anything is fetched
     if (warp < 2) {
-        build_groups(a, tab, sm_ids, sm_rank, PER_PASS, routed ? col : nullptr, rec32, L.rstride, trange, routed ? nteam : 0, vb * nteam, Gr * nteam, T.nTA);
+        build_groups<ONE>(a, tab, sm_ids, sm_rank, PER_PASS, routed ? col : nullptr, rec32, L.rstride, trange, routed ? nteam : 0, vb * nteam, Gr * nteam, T.nTA);
         STAMP(2);
     } else if (one_round) {
         if (tid == 64) records_fetch_rows(a.B, 0, rowb, xs, xbar, row_ptr);
@@ -1389,6 +1420,8 @@ int set_attrs_once(finch_ctx *ctx) {
         if (d == dev) return FINCH_OK;
     const void *big[] = {(const void *)moe_gateup_kernel<false, false>, (const void *)moe_gateup_kernel<false, true>,
                          (const void *)moe_gateup_kernel<true, false>,  (const void *)moe_gateup_kernel<true, true>,
+                         (const void *)moe_gateup_kernel<false, false, true>, (const void *)moe_gateup_kernel<false, true, true>,
+                         (const void *)moe_gateup_kernel<true, false, true>,  (const void *)moe_gateup_kernel<true, true, true>,
                          (const void *)moe_down_kernel<false>,          (const void *)moe_down_kernel<true>};
     for (const void *f : big) {
         FINCH_CUDA_OK(ctx, cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_MAX));
@@ -2004,6 +2037,9 @@ static int encode_decode_calls(finch_ctx *ctx, finch_stream stream, finch_pool *
     };
     const void *ka = hilo ? (fp16s ? (const void *)moe_gateup_kernel<true, true> : (const void *)moe_gateup_kernel<true, false>)
                           : (fp16s ? (const void *)moe_gateup_kernel<false, true> : (const void *)moe_gateup_kernel<false, false>);
+    if (B == 1)   // one token per batch: the grouping has nothing to match
+        ka = hilo ? (fp16s ? (const void *)moe_gateup_kernel<true, true, true> : (const void *)moe_gateup_kernel<true, false, true>)
+                  : (fp16s ? (const void *)moe_gateup_kernel<false, true, true> : (const void *)moe_gateup_kernel<false, false, true>);
     const void *kb = fp16s ? (const void *)moe_down_kernel<true> : (const void *)moe_down_kernel<false>;
     if (pe) FINCH_CUDA_OK(ctx, cudaEventRecord(pe[0], st));
     const int grid_all = n_calls > 1 ? a.cta0[n_calls] : grid;
