@@ -1067,6 +1067,24 @@ def lm_head_rows(stack, peaks, peak_kind, timed=None, iters=8):
         rows.append({"op": f"lm_head_matvec_{bits}bit_g64", "shape": [rows_out, in_dim], "T": 1, "us": secs * 1e6, "gbs": b / secs / 1e9,
                      "bytes": int(b), "frac_hbm_" + peak_kind: b / secs / 1e9 / peaks["hbm_gbs"]})
         del Wd, Sd, Bd
+    # the same projection as GGUF K-quants (the tier a GGUF model's output tensor uses): 256-value blocks, uniform bytes,
+    # block scales d (and dmin) = 0.003 as fp16
+    import numpy as _np
+    lo, hi = (int(v) for v in _np.array([0.003], _np.float16).view(_np.uint8))
+    for name, bs, bits, dpos in (("q6_k", 210, 11, (208,)), ("q4_k", 144, 10, (0, 2))):
+        nb = in_dim // 256
+        Wd = torch.randint(0, 256, (rows_out * nb, bs), dtype=torch.uint8, device="cuda")
+        for o in dpos:
+            Wd[:, o] = lo
+            Wd[:, o + 1] = hi
+        w = L.WDesc(Wd.data_ptr(), None, None, rows_out, in_dim, 256, bits, L.FP16)
+        x = torch.from_numpy(synth.activations(rng, 1, in_dim)).cuda().to(torch.bfloat16)
+        out = torch.empty((1, rows_out), dtype=torch.float32, device="cuda")
+        secs = timed(lambda: ctx.fast_batch_matvec(x, L.BF16, [w], [out], M=1, stream=st.cuda_stream), do_flush=False)
+        b = Wd.numel() + in_dim * 2 + rows_out * 4
+        rows.append({"op": f"lm_head_matvec_{name}", "shape": [rows_out, in_dim], "T": 1, "us": secs * 1e6, "gbs": b / secs / 1e9,
+                     "bytes": int(b), "frac_hbm_" + peak_kind: b / secs / 1e9 / peaks["hbm_gbs"]})
+        del Wd
     return rows
 
 
