@@ -9,7 +9,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 SO = os.path.join(PKG, "libfinchcuda.so")
-SOURCES = ["ctx_pool.cu", "matvec_generic.cu", "moe_decode.cu", "moe_prefill.cu", "moe_host.cu", "ep_exchange.cu", "ep_peer.cu", "matvec_fast.cu", "matvec_stream.cu", "matvec_gguf_mma.cu"]
+SOURCES = ["ctx_pool.cu", "matvec_generic.cu", "moe_decode.cu", "moe_prefill.cu", "moe_host.cu", "ep_exchange.cu", "ep_peer.cu", "matvec_fast.cu", "matvec_stream.cu", "matvec_gguf_mma.cu", "matvec_kq_stream.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
          "-Xcompiler", "-fPIC,-fvisibility=hidden", "-I", os.path.join(ROOT, "include"), "-I", CSRC]

@@ -10,6 +10,7 @@
 
 int finch_try_fast_matvec(finch_ctx *ctx, cudaStream_t st, const void *x, int x_dtype, const finch_wdesc *specs, float *const *outs, int n, int M);
 int finch_try_stream_matvec(finch_ctx *ctx, cudaStream_t st, const void *x, int x_dtype, const finch_wdesc *specs, float *const *outs, int n, int M);
+int finch_kq_stream_matvec(finch_ctx *ctx, cudaStream_t st, const finch_wdesc *w, const void *x, int x_dtype, float *out, int M);
 int finch_try_gguf_mma(finch_ctx *ctx, cudaStream_t st, const void *x, int x_dtype, const finch_wdesc *specs, float *const *outs, int n, int M);
 
 namespace {
@@ -356,6 +357,10 @@ extern "C" int finch_encode_batch_matvec(finch_ctx *ctx, finch_stream stream, co
     cudaSetDevice(ctx->cfg.device);
     {   // a large 4- or 8-bit tensor (lm_head, the big projections) at a few positions: the tensor-core streaming kernel (matvec_stream.cu)
         const int rc = finch_try_stream_matvec(ctx, finch_pick_stream(ctx, stream), x, x_dtype, specs, outs, n, M);
+        if (rc >= 0) return rc;
+    }
+    if (n == 1) {   // a large Q6_K tensor (a GGUF model's output projection) at one position: matvec_kq_stream.cu
+        const int rc = finch_kq_stream_matvec(ctx, finch_pick_stream(ctx, stream), &specs[0], x, x_dtype, outs[0], M);
         if (rc >= 0) return rc;
     }
     {   // 9 and more positions of Q4_K / Q6_K tensors: one pass over the weights on the tensor cores (matvec_gguf_mma.cu)

@@ -172,6 +172,34 @@ def test_gguf_many_positions_one_pass_vs_oracle(ctx_small, ty, bits, o, i, M, xd
     assert ctx_small.device_status() == 0
 
 
+@pytest.mark.parametrize("ty,bits", [(14, 11), (12, 10)])
+@pytest.mark.parametrize("o,i,xdt", [(248320, 2048, L.BF16), (33001, 512, L.F32), (40000, 1280, L.BF16)])
+def test_gguf_output_projection_tier_row_slices_vs_oracle(ctx_small, ty, bits, o, i, xdt):
+    """The lm_head tier of a GGUF model (finchmoe/infer.m:5728-5815): a Q6_K / Q4_K tensor with tens of thousands of
+    rows at one position takes the K-quant streaming kernel (odd row counts, an odd number of blocks per row, fp32 and
+    bf16 activations); slices of rows against the oracle."""
+    import torch
+    rng = synth.rng_for(4, ty, o + i)
+    base = synth.gguf_tensor(rng, 4096, i, ty)
+    reps = o // 4096 + 1
+    perm = rng.permutation(4096)
+    W = np.ascontiguousarray(np.concatenate([base["W"][np.roll(perm, r)] for r in range(reps)])[:o])
+    t = dict(base, W=W, out_dim=o)
+    x = synth.activations(rng, 1, i)
+    xd = torch.from_numpy(synth.f32_to_bf16_rne(x)).cuda().view(torch.bfloat16) if xdt == L.BF16 else torch.from_numpy(x).cuda()
+    out = torch.empty((1, o), dtype=torch.float32, device="cuda")
+    w = ctx_small.upload_tensor(t)
+    ctx_small.fast_batch_matvec(xd, xdt, [w], [out], M=1)
+    ctx_small.sync()
+    got = out.cpu().numpy()[0]
+    assert np.all(np.isfinite(got))
+    for r0 in (0, o // 2 + 17, o - 600):
+        sl = slice(r0, r0 + 600)
+        want = orc.matvec(W[sl], None, None, L.FP16, x[0], 600, i, 256, bits, orc.ACC_F64)
+        assert_close(got[sl], want, f"GGUF type {ty} output projection rows {r0}..")
+    assert ctx_small.device_status() == 0
+
+
 def test_lm_head_tier_row_slices_vs_oracle(ctx_small):
     """The lm_head / embedding tier (finchmoe/infer.m:5728-5815): 8-bit g64 [248,320 x 2048] at one position;
     three slices of rows against the oracle."""
