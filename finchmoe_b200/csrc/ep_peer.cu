@@ -7,7 +7,8 @@
 //   dispatch   every token's record -> slot [my rank][t] of every rank's area (my own included)
 //   receive    read the world * T records addressed to me as they arrive and spread them into the row arrays
 //              the MoE entry points take; on request the block of my own tokens is masked out
-//   return     the partial rows of source s's tokens -> slot [my rank][t] of rank s's area
+//   return     the partial rows of source s's tokens -> slot [my rank][t] of rank s's area (a kernel of its own, or
+//              the last kernel of the decode pass when the layer runs through finch_encode_ep_peer_decode)
 //   combine    read every other rank's partial rows of my tokens as they arrive, add them to the layer output
 //              in ascending rank order, and advance this rank's epoch
 //
@@ -190,15 +191,20 @@ __global__ void __launch_bounds__(256) peer_combine_kernel(const uint8_t *area, 
     const int t = blockIdx.x, q = blockIdx.y * 256 + threadIdx.x;
     const uint32_t e = *epoch;
     dep_launch();
-    // hidden_out was written two kernels back; the return kernel in between passed its wait before this grid could
-    // start, so that writer has completed.  The peers' rows are ordered by the epochs they carry.
-    if (q < hidden / 2) {
-        const uint4 *back = reinterpret_cast<const uint4 *>(area + off_back) + (size_t)t * (hidden / 2) + q;
-        const size_t dstride = (size_t)T * (hidden / 2);
-        uint4 v[MAXW];
+    // The peers' rows are ordered by the epochs they carry: they are requested before anything else.  hidden_out is
+    // the work of the kernel before this one (the decode pass that also returned the other ranks' rows): it is read
+    // only after the wait.
+    const bool mine = q < hidden / 2;
+    const uint4 *back = reinterpret_cast<const uint4 *>(area + off_back) + (size_t)t * (hidden / 2) + q;
+    const size_t dstride = (size_t)T * (hidden / 2);
+    uint4 v[MAXW];
+    if (mine) {
 #pragma unroll
         for (int d = 0; d < MAXW; d++)
             if (d < world && d != rank) v[d] = ll_peek(back + d * dstride);      // all peers' words requested together
+    }
+    dep_wait();
+    if (mine) {
         float2 *out = reinterpret_cast<float2 *>(hidden_out + (size_t)t * hidden) + q;
         float2 h = *out;
 #pragma unroll
@@ -211,7 +217,6 @@ __global__ void __launch_bounds__(256) peer_combine_kernel(const uint8_t *area, 
             }
         *out = h;
     }
-    dep_wait();
     __syncthreads();
     if (threadIdx.x == 0 && atomicAdd(ticket, 1u) == gridDim.x * gridDim.y - 1) {
         *ticket = 0u;
@@ -381,6 +386,26 @@ extern "C" int finch_encode_ep_peer_return(finch_ctx *ctx, finch_stream stream, 
                                   ctx->cfg.hidden, p->off_back, (const uint32_t *)p->sync));
     ctx->launches++;
     return FINCH_OK;
+}
+
+// One launch sequence for the whole layer on this rank: batch c = the T rows received from rank c (the receive step's
+// arrays), of which the experts held here are computed; the rank's own batch also gets h_mid and the shared expert and
+// lands in hidden_out, and the combine kernel of the decode path stores the other batches' rows straight into their
+// ranks' partial-row slots (the return step, without a kernel of its own).  Then: finch_encode_ep_peer_combine.
+extern "C" int finch_encode_ep_peer_decode(finch_ctx *ctx, finch_stream stream, finch_ep_peer *p, finch_pool *pool, int layer, const void *rows_x,
+                                           const int32_t *rows_ids, const float *rows_weights, const uint8_t *rows_valid, const finch_shared *shared,
+                                           const float *h_mid, float *hidden_out) {
+    if (!ctx || !p || p->ctx != ctx || !pool || !rows_x || !rows_ids || !rows_weights || !hidden_out) return FINCH_E_ARG;
+    int rc = connected(p);
+    if (rc) return rc;
+    finch_ret_info ret{};
+    for (int r = 0; r < p->world; r++) ret.area[r] = p->remote[r];
+    ret.off_back = p->off_back;
+    ret.rank = p->rank;
+    ret.T = p->T;
+    ret.epoch = p->sync;
+    return finch_encode_moe_decode_multi_ret(ctx, stream, pool, layer, p->world, p->T, rows_x, rows_ids, rows_weights, rows_valid, p->rank, shared, h_mid,
+                                             hidden_out, &ret);
 }
 
 extern "C" int finch_encode_ep_peer_combine(finch_ctx *ctx, finch_stream stream, finch_ep_peer *p, float *hidden_out) {

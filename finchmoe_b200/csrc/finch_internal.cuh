@@ -120,6 +120,20 @@ static inline cudaStream_t finch_pick_stream(finch_ctx *ctx, finch_stream s) {
 // Opt-in to more than 48 KB of dynamic shared memory: a per-device function attribute, set once per (function, device).
 int finch_func_attr_once(finch_ctx *ctx, const void *func, int smem_bytes);
 
+// Where the rows of the other batches of a multi-batch decode call go when the batches are the ranks of an
+// expert-parallel layer: straight into the partial-row slots of those ranks' receive areas (ep_peer.cu), every
+// pair of values beside the sender's epoch, instead of into a local array that a second kernel would send.
+struct finch_ret_info {
+    uint8_t *area[16];        // every rank's receive area as this process addresses it
+    size_t off_back;          // where the partial-row slots begin inside an area
+    int rank, T;              // this rank; tokens per rank (slot [rank][t] of the destination's area)
+    const uint32_t *epoch;    // this rank's epoch word
+};
+// finch_encode_moe_decode_multi with the rows of the other batches returned through `ret` (implemented in moe_decode.cu)
+int finch_encode_moe_decode_multi_ret(finch_ctx *ctx, finch_stream stream, finch_pool *pool, int layer, int n_batches, int B, const void *h_post,
+                                      const int32_t *expert_ids, const float *weights, const uint8_t *valid, int own_batch,
+                                      const finch_shared *shared, const float *h_mid, float *hidden_out, const finch_ret_info *ret);
+
 // Implemented in moe_decode.cu / moe_prefill.cu, used by the host-pointer entry point.
 int finch_validate_wdesc(finch_ctx *ctx, const finch_wdesc *w, const char *what);
 

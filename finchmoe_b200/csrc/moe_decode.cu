@@ -108,6 +108,8 @@ struct MoeArgs {
     unsigned *done_ticket, *host_done;
     int *host_status;
     const unsigned *done_seq_src;
+    // expert-parallel layer: the other batches' rows go to their ranks' receive areas (ret.epoch != NULL), see finch_ret_info
+    finch_ret_info ret;
 };
 
 // The view of batch c of a multi-batch launch: pointers moved to its rows, the shared expert and the residual
@@ -1321,8 +1323,8 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const MoeArgs a0) {
     __shared__ int ok[8];
     __shared__ float wk[8];
     MoeArgs a = a0;
-    const int b = blockIdx.y % a0.B, row = blockIdx.x * 256 + threadIdx.x;   // grid.y = B * n_calls
-    if (a0.n_calls > 1) select_call(a, blockIdx.y / a0.B);
+    const int b = blockIdx.y % a0.B, c = blockIdx.y / a0.B, row = blockIdx.x * 256 + threadIdx.x;   // grid.y = B * n_calls
+    if (a0.n_calls > 1) select_call(a, c);
     grid_dep_launch();
     // Routing, router weights, gate scores and h_mid are inputs of the whole call: final since the gate/up
     // kernel (the first of the chain) passed its own wait, and this kernel only starts once the down kernel has
@@ -1335,6 +1337,8 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const MoeArgs a0) {
     const bool live = row < a.hidden;
     float h = live && a.h_mid ? a.h_mid[(size_t)b * a.hidden + row] : 0.f;
     const float sg = a.has_shared ? 1.0f / (1.0f + expf(-a.gate_score[b])) : 0.f;
+    const bool away = a0.ret.epoch && c != a0.own_call;   // this batch's rows belong to another rank
+    const uint32_t e = away ? *reinterpret_cast<const volatile uint32_t *>(a0.ret.epoch) : 0u;
     __syncthreads();
     grid_dep_wait();
     if (live) {
@@ -1343,6 +1347,17 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const MoeArgs a0) {
             if (ok[k]) moe = fmaf(wk[k], __ldcg(a.partial + (size_t)(b * a.K + k) * a.hidden + row), moe);
         h += moe;
         if (a.has_shared) h = fmaf(sg, __ldcg(a.partial + (size_t)(a.P + b) * a.hidden + row), h);
+    }
+    if (away) {
+        // {h[row], epoch, h[row + 1], epoch} into slot [my rank][b] of rank c's area: the receiver takes a pair once it
+        // carries the epoch it expects (the word pairs of ep_peer.cu)
+        const float hn = __shfl_down_sync(0xffffffffu, h, 1);
+        if (live && !(row & 1)) {
+            uint4 *dst = reinterpret_cast<uint4 *>(a0.ret.area[c] + a0.ret.off_back) + (size_t)(a0.ret.rank * a0.ret.T + b) * (a.hidden / 2) + (row >> 1);
+            asm volatile("st.volatile.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(dst), "r"(__float_as_uint(h)), "r"(e), "r"(__float_as_uint(hn)), "r"(e)
+                         : "memory");
+        }
+    } else if (live) {
         a.hidden_out[(size_t)b * a.hidden + row] = h;
     }
     if (a0.host_done) {   // launch-uniform
@@ -1898,7 +1913,7 @@ int finch_group3_prefill(finch_ctx *ctx, cudaStream_t st, finch_pool *pool, int 
 // Batch own_call gets shared / h_mid and writes hidden_out; the others write their routed sums to rows_out.
 static int encode_decode_calls(finch_ctx *ctx, finch_stream stream, finch_pool *pool, int layer, const void *h_post, const int32_t *expert_ids,
                                const float *weights, const uint8_t *valid, const finch_shared *shared, const float *h_mid, float *hidden_out, int B,
-                               int n_calls, int own_call, float *rows_out) {
+                               int n_calls, int own_call, float *rows_out, const finch_ret_info *ret = nullptr) {
     if (!ctx || !pool || !h_post || !expert_ids || !weights || !hidden_out) return FINCH_E_ARG;
     const finch_config &c = ctx->cfg;
     if (pool->ctx != ctx) return finch_fail(ctx, FINCH_E_ARG, "pool belongs to another context");
@@ -1946,6 +1961,7 @@ static int encode_decode_calls(finch_ctx *ctx, finch_stream stream, finch_pool *
     a.n_calls = n_calls;
     a.own_call = n_calls > 1 ? own_call : 0;
     a.rows_out = rows_out;
+    if (ret) a.ret = *ret;
     if (ctx->hp_done && n_calls == 1) {      // armed by the host-pointer entry point for this one call
         a.done_ticket = ctx->hp_ticket;
         a.host_done = ctx->hp_done;
@@ -2063,6 +2079,14 @@ extern "C" int finch_encode_moe_decode_multi(finch_ctx *ctx, finch_stream stream
                                              const finch_shared *shared, const float *h_mid, float *hidden_out, float *rows_out) {
     if (n_batches < 1 || n_batches > MAX_CALLS || own_batch < 0 || own_batch >= n_batches || !rows_out) return FINCH_E_ARG;
     return encode_decode_calls(ctx, stream, pool, layer, h_post, expert_ids, weights, valid, shared, h_mid, hidden_out, B, n_batches, own_batch, rows_out);
+}
+
+int finch_encode_moe_decode_multi_ret(finch_ctx *ctx, finch_stream stream, finch_pool *pool, int layer, int n_batches, int B, const void *h_post,
+                                      const int32_t *expert_ids, const float *weights, const uint8_t *valid, int own_batch,
+                                      const finch_shared *shared, const float *h_mid, float *hidden_out, const finch_ret_info *ret) {
+    if (n_batches < 1 || n_batches > MAX_CALLS || own_batch < 0 || own_batch >= n_batches || !ret || !ret->epoch || ret->T != B) return FINCH_E_ARG;
+    if (ctx && ctx->cfg.hidden % 2) return FINCH_E_ARG;
+    return encode_decode_calls(ctx, stream, pool, layer, h_post, expert_ids, weights, valid, shared, h_mid, hidden_out, B, n_batches, own_batch, nullptr, ret);
 }
 
 extern "C" int finch_profile_enable(finch_ctx *ctx, int on) {

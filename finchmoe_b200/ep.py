@@ -156,6 +156,12 @@ def _ep_layer_static(backend, dist, group, layer, x, ids, weights, valid, shared
         # The ranks' own kernels move the records and the partial rows through each other's memory (NVLink), each
         # slot with its flag: no collective and no host step, the whole layer is launches on the backend's stream.
         backend.peer_dispatch(x, ids, weights, valid)
+        if backend.can_multi(T, world) and getattr(backend, "fuse_return", False):
+            # the same launch sequence, whose last kernel also stores the other ranks' rows into their areas: the
+            # return step without a kernel of its own
+            backend.peer_decode(layer, shared, h_mid, out)
+            backend.peer_combine(out)
+            return out
         if backend.can_multi(T, world):
             # one launch sequence serves every rank's batch of T rows, the rank's own among them (with h_mid and the
             # shared expert): batch c = the tokens of rank c, of which only the experts held here are computed
@@ -284,6 +290,7 @@ class GpuBackend:
         self._static = {}
         self.multi = True            # decode-sized batches of all ranks in one launch sequence (finch_encode_moe_decode_multi)
         self.peer = None             # a connected PeerExchange routes the fixed-capacity layer through peer memory
+        self.fuse_return = True      # ... and the decode pass's last kernel stores the other ranks' rows into their areas itself
         self.stats = None            # a list makes ep_layer append (rows sent per rank, rows received per rank) per layer
         # Received rows select few local experts each.  More than one decode-sized batch of them goes through the
         # tensor-core path in passes of `tc_chunk` rows (one sort and one pair of grouped GEMMs per pass) instead of
@@ -451,6 +458,14 @@ class GpuBackend:
             rank, C.byref(shared) if shared is not None else None, h_mid.data_ptr() if h_mid is not None else None, out.data_ptr(),
             self.rout.data_ptr()))
         return self.rout[:T * world]
+
+    def peer_decode(self, layer, shared, h_mid, out):
+        """receive + finch_encode_ep_peer_decode: the layer on this rank, the other ranks' rows stored into their areas
+        by the decode pass itself."""
+        self.peer_receive(False)
+        self.ctx.check(self.lib.finch_encode_ep_peer_decode(
+            self.ctx.h, self._stream(), self.peer.h, self.pool.h, layer, self.rx.data_ptr(), self.rids.data_ptr(), self.rw.data_ptr(),
+            self.rv.data_ptr(), C.byref(shared) if shared is not None else None, h_mid.data_ptr() if h_mid is not None else None, out.data_ptr()))
 
     def peer_return(self, part):
         self.ctx.check(self.lib.finch_encode_ep_peer_return(self.ctx.h, self._stream(), self.peer.h, part.data_ptr()))

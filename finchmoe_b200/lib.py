@@ -93,6 +93,7 @@ _PROTOS = {
     "finch_encode_ep_peer_dispatch": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "finch_encode_ep_peer_receive": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i]),
     "finch_encode_ep_peer_return": (_i, [_vp, _vp, _vp, _vp]),
+    "finch_encode_ep_peer_decode": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "finch_encode_ep_peer_combine": (_i, [_vp, _vp, _vp, _vp]),
     "finch_pool_fill_synthetic_range": (_i, [_vp, _i, _i, _i, _i, C.c_uint64]),
     "finch_encode_residual_norm": (_i, [_vp, _vp, _vp, _vp, _vp, C.c_float, _vp, _vp, _i]),

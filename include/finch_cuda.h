@@ -388,6 +388,14 @@ FINCH_API int finch_encode_ep_peer_receive(finch_ctx *ctx, finch_stream stream, 
                                            int32_t *expert_ids, float *weights, uint8_t *valid, int mask_own);
 /* rows: fp32 [world * tokens_per_rank][hidden], block s = the partial sums of rank s's tokens. */
 FINCH_API int finch_encode_ep_peer_return(finch_ctx *ctx, finch_stream stream, finch_ep_peer *peer, const float *rows);
+/* The layer on this rank in ONE launch sequence over the rows of finch_encode_ep_peer_receive (mask_own = 0): batch c =
+ * the tokens of rank c, served by the experts held here; the rank's own batch also gets h_mid and the shared expert and
+ * lands in hidden_out; the last kernel of the sequence stores the other batches' rows straight into their ranks' areas
+ * (the return step fused into the compute: no finch_encode_ep_peer_return, no local array of rows).  tokens_per_rank
+ * <= 8 and tokens_per_rank * top_k <= 64, as finch_encode_moe_decode_multi wants.  Then finch_encode_ep_peer_combine. */
+FINCH_API int finch_encode_ep_peer_decode(finch_ctx *ctx, finch_stream stream, finch_ep_peer *peer, finch_pool *pool, int layer, const void *rows_h_post,
+                                          const int32_t *rows_expert_ids, const float *rows_weights, const uint8_t *rows_valid,
+                                          const finch_shared *shared, const float *h_mid, float *hidden_out);
 /* hidden_out[t] += the other ranks' partial rows of token t, in ascending rank order. */
 FINCH_API int finch_encode_ep_peer_combine(finch_ctx *ctx, finch_stream stream, finch_ep_peer *peer, float *hidden_out);
 

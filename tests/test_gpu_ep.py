@@ -141,7 +141,7 @@ def _two_ranks_one_process(api, T=8):
     return blocks, sh, ranks
 
 
-@pytest.mark.parametrize("multi", [False, True])
+@pytest.mark.parametrize("multi", [False, True, "fused"])
 def test_peer_exchange_two_ranks_in_one_process_match_oracle(multi):
     """The exchange through peer memory (dispatch / receive / return / combine with one flag per slot), its two
     ranks run from one process on one GPU: each step of both ranks is launched before the step that waits for it, so
@@ -173,6 +173,10 @@ def test_peer_exchange_two_ranks_in_one_process_match_oracle(multi):
             torch.cuda.synchronize()
             for r, (ctx, pool, be) in enumerate(ranks):
                 with be.stream_scope():
+                    if multi == "fused":   # ... whose last kernel also stores the other rank's rows into its area
+                        assert be.can_multi(T, 2)
+                        be.peer_decode(0, inputs[r][10], inputs[r][11], outs[r])
+                        continue
                     if multi:       # every rank's batch, the rank's own among them, in one launch sequence
                         assert be.can_multi(T, 2)
                         part = be.peer_local_multi(0, T, 2, r, inputs[r][10], inputs[r][11], outs[r])
