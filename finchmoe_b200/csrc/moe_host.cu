@@ -131,17 +131,17 @@ extern "C" int finch_moe_forward_host(finch_ctx *ctx, finch_pool *pool, int laye
         ctx->launches += 4;
     } else if (hg && hg->seen == 1) {
         cudaGraph_t graph = nullptr;
-        FINCH_CUDA_OK(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
-        rc = encode();
-        const cudaError_t ce = cudaStreamEndCapture(ctx->stream, &graph);
         cudaGraphExec_t exec = nullptr;
-        if (rc == FINCH_OK && ce == cudaSuccess && graph && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess) {
-            hg->exec = exec;
-            hg->seen = 2;
-        } else {
-            cudaGetLastError();
-            hg->seen = -1;
+        hg->seen = -1;   // unless everything below works out
+        if (cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            rc = encode();
+            const cudaError_t ce = cudaStreamEndCapture(ctx->stream, &graph);
+            if (rc == FINCH_OK && ce == cudaSuccess && graph && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess) {
+                hg->exec = exec;
+                hg->seen = 2;
+            }
         }
+        if (!hg->exec) cudaGetLastError();
         if (graph) cudaGraphDestroy(graph);
         if (hg->exec) {
             FINCH_CUDA_OK(ctx, cudaGraphLaunch(hg->exec, ctx->stream));
