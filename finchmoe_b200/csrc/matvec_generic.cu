@@ -359,7 +359,7 @@ extern "C" int finch_encode_batch_matvec(finch_ctx *ctx, finch_stream stream, co
         const int rc = finch_try_stream_matvec(ctx, finch_pick_stream(ctx, stream), x, x_dtype, specs, outs, n, M);
         if (rc >= 0) return rc;
     }
-    if (n == 1) {   // a large Q6_K tensor (a GGUF model's output projection) at one position: matvec_kq_stream.cu
+    if (n == 1) {   // a large Q6_K / Q4_K tensor (a GGUF model's output projection) at one position: matvec_kq_stream.cu
         const int rc = finch_kq_stream_matvec(ctx, finch_pick_stream(ctx, stream), &specs[0], x, x_dtype, outs[0], M);
         if (rc >= 0) return rc;
     }

@@ -173,7 +173,7 @@ def test_gguf_many_positions_one_pass_vs_oracle(ctx_small, ty, bits, o, i, M, xd
 
 
 @pytest.mark.parametrize("ty,bits", [(14, 11), (12, 10)])
-@pytest.mark.parametrize("o,i,xdt", [(248320, 2048, L.BF16), (33001, 512, L.F32), (40000, 1280, L.BF16)])
+@pytest.mark.parametrize("o,i,xdt", [(248320, 2048, L.BF16), (33001, 512, L.F32), (40000, 1280, L.BF16), (33003, 1024, L.F32)])
 def test_gguf_output_projection_tier_row_slices_vs_oracle(ctx_small, ty, bits, o, i, xdt):
     """The lm_head tier of a GGUF model (finchmoe/infer.m:5728-5815): a Q6_K / Q4_K tensor with tens of thousands of
     rows at one position takes the K-quant streaming kernel (odd row counts, an odd number of blocks per row, fp32 and
