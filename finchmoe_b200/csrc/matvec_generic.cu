@@ -390,7 +390,10 @@ extern "C" int finch_matvec(finch_ctx *ctx, const finch_wdesc *w, const float *x
     float *outs[1] = {od};
     if ((rc = finch_encode_batch_matvec(ctx, ctx->stream, xd, FINCH_F32, w, outs, 1, M))) return rc;
     FINCH_CUDA_OK(ctx, cudaMemcpyAsync(out_host, od, ob, cudaMemcpyDeviceToHost, ctx->stream));
+    int dev_rc = FINCH_OK;   // the device status word rides along: a synchronous call reports what the device recorded
+    FINCH_CUDA_OK(ctx, cudaMemcpyAsync(&dev_rc, ctx->dev_status, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
     FINCH_CUDA_OK(ctx, cudaStreamSynchronize(ctx->stream));
+    if (dev_rc != FINCH_OK) return finch_fail(ctx, dev_rc, "device status %d after the matvec", dev_rc);
     return FINCH_OK;
 }
 
