@@ -105,10 +105,20 @@ extern "C" int finch_moe_forward_host(finch_ctx *ctx, finch_pool *pool, int laye
     // instead of four kernel launches.  FINCH_HOST_PATH=2 keeps the plain launches.
     finch_ctx::HostGraph *hg = nullptr;
     if (flagged && host_path >= 3 && !ctx->profile) {
-        finch_shared key{};
+        finch_shared key{};   // zero, padding included; filled field by field so that it stays comparable byte by byte
         if (shared) {
-            key = *shared;
-            key.gate_score = nullptr;
+            const finch_wdesc *from[3] = {&shared->gate, &shared->up, &shared->down};
+            finch_wdesc *to[3] = {&key.gate, &key.up, &key.down};
+            for (int i = 0; i < 3; i++) {
+                to[i]->W = from[i]->W;
+                to[i]->scales = from[i]->scales;
+                to[i]->biases = from[i]->biases;
+                to[i]->out_dim = from[i]->out_dim;
+                to[i]->in_dim = from[i]->in_dim;
+                to[i]->group_size = from[i]->group_size;
+                to[i]->bits = from[i]->bits;
+                to[i]->scale_dtype = from[i]->scale_dtype;
+            }
         }
         for (auto &g : ctx->host_graphs)
             if (g.pool == pool && g.layer == layer && g.T == T && g.valid == (valid != nullptr) && g.h_mid == (h_mid != nullptr) &&
@@ -117,7 +127,7 @@ extern "C" int finch_moe_forward_host(finch_ctx *ctx, finch_pool *pool, int laye
                 break;
             }
         if (!hg) {
-            if (ctx->host_graphs.size() >= 1024) {   // shapes that never repeat: start over rather than grow
+            if (ctx->host_graphs.size() >= 256) {   // shapes that never repeat: start over rather than grow
                 for (auto &g : ctx->host_graphs)
                     if (g.exec) cudaGraphExecDestroy(g.exec);
                 ctx->host_graphs.clear();
